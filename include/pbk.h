@@ -1,0 +1,104 @@
+/*
+ * pbk.h -- C ABI of the B200 (sm_100a) kernels for PseudoBrain's hot path.
+ *
+ * Everything here is plain C: device pointers, sizes, element strides, a dtype
+ * code per tensor and a cudaStream_t passed as void*. The library allocates no
+ * device memory: the caller owns every tensor, outputs and workspaces included
+ * (workspace sizes come from the *_workspace_size queries). Calls are
+ * stream-ordered, never synchronise the host, keep no pointer past the call and
+ * are re-entrant on different streams.
+ *
+ * Every entry point returns a pbk status (0 = PBK_OK, negative = error);
+ * pbk_status_string() names it. Arguments are validated on the host before any
+ * launch: a call that returns an error launched nothing.
+ *
+ * Layouts follow the reference (defnotean/pseudobrain):
+ *   q, k  [B, T, Hk, dk]    v, o  [B, T, Hv, dv]    g, beta  [B, T, Hv]
+ *   state [slots, Hv, dk, dv] fp32 (PBK_STATE_KV, the PyTorch core's [B,H,K,V])
+ *         or [slots, Hv, dv, dk] (PBK_STATE_VK, vLLM's state pool layout)
+ * Value head j reads key head j / (Hv / Hk), the repeat_interleave GQA map of
+ * pseudobrain/gated_deltanet.py:422-424; the kernels never materialise it.
+ */
+#ifndef PBK_H_
+#define PBK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PBK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define PBK_API __attribute__((visibility("default")))
+#else
+#define PBK_API
+#endif
+
+/* status codes */
+#define PBK_OK 0
+#define PBK_ERR_INVALID (-1)   /* null pointer or out-of-range argument */
+#define PBK_ERR_SHAPE (-2)     /* shape this build does not support */
+#define PBK_ERR_DTYPE (-3)     /* unsupported dtype code */
+#define PBK_ERR_ALIGN (-4)     /* pointer or stride not aligned for vector access */
+#define PBK_ERR_DEVICE (-5)    /* current device is not sm_100 */
+#define PBK_ERR_LAUNCH (-6)    /* the CUDA launch failed */
+#define PBK_ERR_TIMEOUT (-7)   /* a bounded device-side wait gave up */
+#define PBK_ERR_WORKSPACE (-8) /* workspace missing or too small */
+
+/* dtype codes */
+#define PBK_F32 0
+#define PBK_BF16 1
+
+/* state layouts */
+#define PBK_STATE_KV 0 /* [.., dk, dv]: pseudobrain/gated_deltanet.py:72-75 */
+#define PBK_STATE_VK 1 /* [.., dv, dk]: vLLM mamba state pool */
+
+/* A strided view of a [B, T, H, D] (or [B, T, H]) tensor whose last dimension is
+ * contiguous. Strides are in elements. */
+typedef struct pbk_view {
+  const void* data;
+  int64_t stride_b, stride_t, stride_h;
+  int32_t dtype;
+  int32_t pad_;
+} pbk_view;
+
+/* One gated delta rule problem (prefill or decode).
+ * h0 is the initial state [slots, Hv, ...] (NULL = zeros, prefill only); state
+ * receives the final state. For decode, state is updated in place (h0 must be
+ * NULL or equal to state). state_indices[b] picks the slot of sequence b
+ * (NULL = slot b); a negative index skips that sequence (vLLM's padding slot). */
+typedef struct pbk_gdn_desc {
+  int32_t batch, seqlen, hk, hv, dk, dv;
+  pbk_view q, k, v, g, beta;
+  pbk_view o;                 /* output; data is written */
+  const float* h0;
+  float* state;
+  int64_t state_slot_stride;  /* elements between slots; Hv*dk*dv when dense */
+  int32_t state_layout;       /* PBK_STATE_KV or PBK_STATE_VK */
+  int32_t pad_;
+  const int32_t* state_indices;
+  float scale;                /* the query scale, dk**-0.5 in the reference */
+  int32_t pad2_;
+} pbk_gdn_desc;
+
+PBK_API int pbk_abi_version(void);
+PBK_API const char* pbk_status_string(int status);
+/* PBK_OK when `device` is an sm_100 (B200-class) GPU. */
+PBK_API int pbk_device_check(int device);
+
+/* Gated delta rule over few tokens per sequence with the state held in registers:
+ * the recurrence of delta_rule_sequential, pseudobrain/gated_deltanet.py:93-107,
+ * and the decode step vLLM runs as fused_recurrent_gated_delta_rule
+ * (vllm/model_executor/layers/fla/ops/fused_recurrent.py). One read and one write
+ * of each fp32 state for any seqlen. Requires dk == dv == 128; q/k/v bf16 or fp32;
+ * g/beta bf16 or fp32; o bf16 or fp32. */
+PBK_API int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PBK_H_ */

@@ -1,0 +1,151 @@
+"""Quest page-bounded exact memory, restated in numpy. TEST INFRASTRUCTURE ONLY.
+
+Follows pseudobrain/exact_memory.py (flat, single-level mode: ``superblock=0``,
+``rerank=0``, ``neighbors=0``) and the exact attention of its caller
+pseudobrain/transplant.py:612-628. Layouts: keys/values [B,KV,N,D], page bounds
+[B,KV,P,D], queries [B,H,T,D] with H = KV * groups (head h reads key head
+h // groups).
+
+Scores are computed the way the reference's CPU path computes them: q cast to
+fp32, split into its positive and negative parts, two fp32 products against the
+page maxima and minima, then the maximum over the G*T query rows that share a key
+head (exact_memory.py:94-98,124-125). Page selection keeps the ``budget`` highest
+scores with ties going to the lowest page index (the tie rule of this build; the
+reference's ``torch.topk`` leaves it unspecified) and returns them in position
+order (exact_memory.py:135,144).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round fp32 to the nearest bf16 (ties to even) and return it as fp32."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 values that are exact bf16 -> their uint16 bit patterns."""
+    return (np.ascontiguousarray(x, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def bf16_from_bits(bits: np.ndarray) -> np.ndarray:
+    """uint16 bf16 bit patterns -> fp32."""
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def page_bounds(keys: np.ndarray, page: int) -> tuple[np.ndarray, np.ndarray]:
+    """Elementwise max and min of every page of ``page`` keys, exact_memory.py:43-50.
+
+    A trailing partial page is padded with its own last key, so its bounds are those
+    of the keys it holds."""
+    b, h, n, d = keys.shape
+    pad = (-n) % page
+    if pad:
+        keys = np.concatenate((keys, np.broadcast_to(keys[:, :, -1:], (b, h, pad, d))), axis=2)
+    blocks = keys.reshape(b, h, -1, page, d)
+    return blocks.max(axis=3), blocks.min(axis=3)
+
+
+class Archive:
+    """Evicted keys/values [B,KV,N,D] and per-page bounds [B,KV,P,D] (exact_memory.py:27-40)."""
+
+    def __init__(self, keys, values, kmax, kmin):
+        self.keys, self.values, self.kmax, self.kmin = keys, values, kmax, kmin
+
+    @property
+    def length(self) -> int:
+        return self.keys.shape[2]
+
+
+def archive_append(archive: Archive | None, keys, values, page: int) -> Archive | None:
+    """Append evicted keys/values and redo the bounds from the first incomplete page on,
+    exact_memory.py:66-85 (complete pages are final)."""
+    if keys.shape[2] == 0:
+        return archive
+    if archive is None:
+        kmax, kmin = page_bounds(keys, page)
+        return Archive(keys, values, kmax, kmin)
+    full = (archive.length // page) * page
+    new_k = np.concatenate((archive.keys, keys), axis=2)
+    new_v = np.concatenate((archive.values, values), axis=2)
+    tmax, tmin = page_bounds(new_k[:, :, full:], page)
+    kmax = np.concatenate((archive.kmax[:, :, : full // page], tmax), axis=2)
+    kmin = np.concatenate((archive.kmin[:, :, : full // page], tmin), axis=2)
+    return Archive(new_k, new_v, kmax, kmin)
+
+
+def page_scores(q: np.ndarray, kmax: np.ndarray, kmin: np.ndarray, groups: int) -> np.ndarray:
+    """Upper bound of every page's attention logit, max over the G*T query rows of a key
+    head: sum_d max(q_d, 0) kmax_d + min(q_d, 0) kmin_d (exact_memory.py:94-98,124-125).
+
+    q [B,H,T,D]; kmax, kmin [B,KV,P,D] (complete pages only) -> [B,KV,P] fp32."""
+    b, h, t, d = q.shape
+    kv = h // groups
+    qg = q.astype(np.float32).reshape(b, kv, groups * t, d)
+    pos, neg = np.maximum(qg, 0), np.minimum(qg, 0)
+    bound = pos @ kmax.astype(np.float32).swapaxes(-1, -2) + neg @ kmin.astype(np.float32).swapaxes(-1, -2)
+    return bound.max(axis=2).astype(np.float32)
+
+
+def select_pages(score: np.ndarray, budget: int) -> np.ndarray:
+    """The min(budget, P) highest-scoring pages of every row, ties to the lowest index,
+    returned in ascending page order (exact_memory.py:135,144). [..., P] -> [..., k] int64."""
+    p = score.shape[-1]
+    k = min(budget, p)
+    order = np.argsort(-score.astype(np.float64), axis=-1, kind="stable")[..., :k]
+    return np.sort(order, axis=-1).astype(np.int64)
+
+
+def retrieve(archive: Archive | None, q: np.ndarray, groups: int, page: int, budget: int):
+    """Flat Quest retrieval, exact_memory.py:88-152 with superblock=0, rerank=0,
+    neighbors=0: score complete pages, keep the top ``budget``, gather them in position
+    order and append the partial tail. Returns (keys, values, pages) or None."""
+    if archive is None or archive.length == 0:
+        return None
+    b, h, t, d = q.shape
+    kv = h // groups
+    full = archive.length // page
+    tail = archive.length - full * page
+    parts_k, parts_v = [], []
+    top = np.zeros((b, kv, 0), dtype=np.int64)
+    if full:
+        score = page_scores(q, archive.kmax[:, :, :full], archive.kmin[:, :, :full], groups)
+        top = select_pages(score, budget)
+        idx = (top[..., None] * page + np.arange(page)).reshape(b, kv, -1)
+        parts_k.append(np.take_along_axis(archive.keys, idx[..., None], axis=2))
+        parts_v.append(np.take_along_axis(archive.values, idx[..., None], axis=2))
+    if tail:
+        parts_k.append(archive.keys[:, :, full * page:])
+        parts_v.append(archive.values[:, :, full * page:])
+    return np.concatenate(parts_k, axis=2), np.concatenate(parts_v, axis=2), top
+
+
+def window_mask(qpos: np.ndarray, kpos: np.ndarray, window: int, sinks: int) -> np.ndarray:
+    """Causal sliding-window visibility of cached keys, transplant.py:621-622:
+    kpos <= qpos and (qpos - kpos < window or kpos < sinks). -> [T, S] bool."""
+    q_, k_ = qpos[:, None], kpos[None, :]
+    return (k_ <= q_) & (((q_ - k_) < window) | (k_ < sinks))
+
+
+def attend(q, rk, rv, wk, wv, qpos, kpos, window: int, sinks: int, groups: int) -> np.ndarray:
+    """Exact softmax attention over [retrieved ; window] keys, transplant.py:619-628.
+
+    q [B,H,T,D]; rk, rv [B,KV,R,D] (all visible); wk, wv [B,KV,S,D] with positions kpos [S];
+    queries at positions qpos [T]. Scale 1/sqrt(D) (SDPA's default). Computed in fp64,
+    returned as fp32 [B,H,T,D]."""
+    b, h, t, d = q.shape
+    mask = np.concatenate((np.ones((t, rk.shape[2]), dtype=bool),
+                           window_mask(qpos, kpos, window, sinks)), axis=1)
+    kk = np.concatenate((rk, wk), axis=2).astype(np.float64)
+    vv = np.concatenate((rv, wv), axis=2).astype(np.float64)
+    kk = np.repeat(kk, groups, axis=1)
+    vv = np.repeat(vv, groups, axis=1)
+    logits = (q.astype(np.float64) @ kk.swapaxes(-1, -2)) / np.sqrt(d)
+    logits = np.where(mask, logits, -np.inf)
+    logits -= logits.max(axis=-1, keepdims=True)
+    p = np.exp(logits)
+    p /= p.sum(axis=-1, keepdims=True)
+    return (p @ vv).astype(np.float32)

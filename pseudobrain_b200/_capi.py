@@ -1,0 +1,70 @@
+"""ctypes binding of libpbk.so (include/pbk.h).
+
+The library is the only compute path of this package: if it is missing or was
+built for another ABI, importing this module raises, and nothing falls back to
+PyTorch or to the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import build as _build
+
+PBK_ABI_VERSION = 1
+PBK_OK = 0
+PBK_ERR_TIMEOUT = -7
+PBK_F32, PBK_BF16 = 0, 1
+PBK_STATE_KV, PBK_STATE_VK = 0, 1
+
+
+class PbkView(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("stride_b", ctypes.c_int64), ("stride_t", ctypes.c_int64),
+                ("stride_h", ctypes.c_int64), ("dtype", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+
+
+class PbkGdnDesc(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hk", ctypes.c_int32),
+                ("hv", ctypes.c_int32), ("dk", ctypes.c_int32), ("dv", ctypes.c_int32),
+                ("q", PbkView), ("k", PbkView), ("v", PbkView), ("g", PbkView), ("beta", PbkView),
+                ("o", PbkView), ("h0", ctypes.c_void_p), ("state", ctypes.c_void_p),
+                ("state_slot_stride", ctypes.c_int64), ("state_layout", ctypes.c_int32),
+                ("pad_", ctypes.c_int32), ("state_indices", ctypes.c_void_p), ("scale", ctypes.c_float),
+                ("pad2_", ctypes.c_int32)]
+
+
+# name -> (restype, argtypes); every symbol include/pbk.h declares.
+SIGNATURES = {
+    "pbk_abi_version": (ctypes.c_int, []),
+    "pbk_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "pbk_device_check": (ctypes.c_int, [ctypes.c_int]),
+    "pbk_gdn_decode": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
+}
+
+
+def _load() -> ctypes.CDLL:
+    path = _build.LIB_PATH
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing: build it with `python -m pseudobrain_b200.build` "
+                          "(this package has no CPU or PyTorch fallback)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+    if lib.pbk_abi_version() != PBK_ABI_VERSION:
+        raise ImportError(f"{path} has ABI {lib.pbk_abi_version()}, expected {PBK_ABI_VERSION}: rebuild it")
+    return lib
+
+
+LIB = _load()
+
+
+class PbkError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {LIB.pbk_status_string(status).decode()} (status {status})")
+
+
+def check(status: int, what: str) -> None:
+    if status != PBK_OK:
+        raise PbkError(status, what)

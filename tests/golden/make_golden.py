@@ -1,0 +1,148 @@
+"""Generate the golden fixtures in tests/golden/ by running the REFERENCE implementation.
+
+Run once, in a container where defnotean/pseudobrain's source tree is available:
+
+    python tests/golden/make_golden.py /path/to/pseudobrain-checkout
+
+It imports the reference's own PyTorch functions (pseudobrain.gated_deltanet and
+pseudobrain.exact_memory) from that checkout, feeds them seeded inputs and stores
+inputs and outputs as .npz files next to this script. Nothing at test time imports
+the reference: the tests only read these files. bf16 tensors are stored as their
+uint16 bit patterns.
+
+Fixtures:
+  gdn_fp32.npz    delta_rule_chunked and delta_rule_sequential, fp32, ragged T=100
+                  (one full chunk of 64 and a partial one), GQA 1 key head / 2 value
+                  heads, nonzero initial state.
+  gdn_bf16.npz    delta_rule_chunked on bf16 q/k/v/beta (fp32 g and state), B=2, T=80.
+  gdn_decode.npz  delta_rule_sequential (the kernel select_kernel picks for T <= 4),
+                  T=3 tokens, bf16 inputs, fp32 state ~ N(0, 0.02).
+  quest.npz       archive_append + retrieve (flat mode, page 16, budget 4 pages) for a
+                  decode query (T=1) and a 3-token query, plus the exact attention over
+                  [retrieved ; window] as pseudobrain/transplant.py:619-628 computes it.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _bits(t):
+    import torch
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _gdn_inputs(gen, batch, length, hk, hv, dk, dv, dtype, state_std):
+    """Config-0 distributions: q,k ~ N(0,1) L2-normalised per head; v ~ N(0,1);
+    beta = sigmoid(N(0,1)); g = logsigmoid(N(2,1))."""
+    import torch
+    import torch.nn.functional as F
+    q = F.normalize(torch.randn(batch, length, hk, dk, generator=gen), dim=-1)
+    k = F.normalize(torch.randn(batch, length, hk, dk, generator=gen), dim=-1)
+    v = torch.randn(batch, length, hv, dv, generator=gen)
+    beta = torch.sigmoid(torch.randn(batch, length, hv, generator=gen))
+    g = F.logsigmoid(torch.randn(batch, length, hv, generator=gen) + 2.0)
+    h0 = torch.randn(batch, hv, dk, dv, generator=gen) * state_std
+    q, k, v, beta = (x.to(dtype) for x in (q, k, v, beta))
+    return q, k, v, g, beta, h0
+
+
+def _expand(x, hv):
+    return x.repeat_interleave(hv // x.shape[2], dim=2)
+
+
+def make_gdn(G):
+    import torch
+    dk = dv = 128
+    scale = dk ** -0.5
+
+    gen = torch.Generator().manual_seed(100)
+    q, k, v, g, beta, h0 = _gdn_inputs(gen, 1, 100, 1, 2, dk, dv, torch.float32, 0.02)
+    oc, sc = G.delta_rule_chunked(_expand(q, 2), _expand(k, 2), v, g, beta, scale, h0)
+    os_, ss = G.delta_rule_sequential(_expand(q, 2), _expand(k, 2), v, g, beta, scale, h0)
+    np.savez_compressed(os.path.join(HERE, "gdn_fp32.npz"), q=q.numpy(), k=k.numpy(), v=v.numpy(),
+                        g=g.numpy(), beta=beta.numpy(), h0=h0.numpy(), scale=np.float64(scale),
+                        o_chunked=oc.numpy(), s_chunked=sc.numpy(),
+                        o_sequential=os_.numpy(), s_sequential=ss.numpy())
+
+    gen = torch.Generator().manual_seed(101)
+    q, k, v, g, beta, h0 = _gdn_inputs(gen, 2, 80, 1, 2, dk, dv, torch.bfloat16, 0.0)
+    oc, sc = G.delta_rule_chunked(_expand(q, 2), _expand(k, 2), v, g, beta, scale, h0)
+    np.savez_compressed(os.path.join(HERE, "gdn_bf16.npz"), q=_bits(q), k=_bits(k), v=_bits(v),
+                        g=g.numpy(), beta=_bits(beta), h0=h0.numpy(), scale=np.float64(scale),
+                        o_chunked=oc.numpy(), s_chunked=sc.numpy())
+
+    gen = torch.Generator().manual_seed(102)
+    q, k, v, g, beta, h0 = _gdn_inputs(gen, 2, 3, 1, 2, dk, dv, torch.bfloat16, 0.02)
+    g = g.to(torch.bfloat16)
+    assert G.select_kernel("reference", False, 3, h0) == "sequential"
+    os_, ss = G.delta_rule_sequential(_expand(q, 2), _expand(k, 2), v, g, beta, scale, h0)
+    np.savez_compressed(os.path.join(HERE, "gdn_decode.npz"), q=_bits(q), k=_bits(k), v=_bits(v),
+                        g=_bits(g), beta=_bits(beta), h0=h0.numpy(), scale=np.float64(scale),
+                        o_sequential=os_.numpy(), s_sequential=ss.numpy())
+
+
+def make_quest(E):
+    import torch
+    import torch.nn.functional as F
+    page, budget, kv, groups, d = 16, 4, 2, 4, 128
+    E.EXACT_MEMORY.update(enabled=True, block_size=page, blocks=budget, decode_blocks=budget,
+                          superblock=0, rerank=0, decode_rerank=0, neighbors=0, keys_like_values=False)
+    gen = torch.Generator().manual_seed(103)
+    n_arch, n_win, window = 16 * page + 8, 24, 24
+    keys = torch.randn(1, kv, n_arch + n_win, d, generator=gen).to(torch.bfloat16)
+    values = torch.randn(1, kv, n_arch + n_win, d, generator=gen).to(torch.bfloat16)
+    # Two appends (the second completes the first's partial page), as eviction does.
+    arc = E.archive_append(None, keys[:, :, :100], values[:, :, :100])
+    arc = E.archive_append(arc, keys[:, :, 100:n_arch], values[:, :, 100:n_arch])
+    out = dict(keys=_bits(keys), values=_bits(values), kmax=_bits(arc.kmax), kmin=_bits(arc.kmin),
+               page=np.int64(page), budget=np.int64(budget), groups=np.int64(groups),
+               n_arch=np.int64(n_arch), window=np.int64(window))
+    wk, wv = keys[:, :, n_arch:], values[:, :, n_arch:]
+    kpos = torch.arange(n_arch, n_arch + n_win)
+    for name, t in (("t1", 1), ("t3", 3)):
+        q = torch.randn(1, kv * groups, t, d, generator=gen).to(torch.bfloat16)
+        arc.prompt_top = None
+        rk, rv = E.retrieve(arc, q, groups)
+        # Page indices: match each gathered page against the archive's pages.
+        full = n_arch // page
+        pages = arc.keys[:, :, : full * page].reshape(1, kv, full, page * d)
+        got = rk[:, :, : budget * page].reshape(1, kv, budget, page * d)
+        top = torch.stack([torch.stack([
+            torch.tensor([int(torch.nonzero((pages[0, h] == got[0, h, j]).all(-1))[0]) for j in range(budget)])
+            for h in range(kv)])])
+        # transplant.py:619-628: mask, GQA repeat, SDPA (run here in fp32).
+        qpos = torch.arange(n_arch + n_win - t, n_arch + n_win)
+        mask = (kpos[None, :] <= qpos[:, None]) & ((qpos[:, None] - kpos[None, :]) < window)
+        mask = torch.cat((torch.ones(t, rk.shape[2], dtype=torch.bool), mask), dim=1)
+        kk = torch.cat((rk, wk), dim=2).float().repeat_interleave(groups, dim=1)
+        vv = torch.cat((rv, wv), dim=2).float().repeat_interleave(groups, dim=1)
+        a = F.scaled_dot_product_attention(q.float(), kk, vv, attn_mask=mask)
+        out.update({f"{name}_q": _bits(q), f"{name}_top": top.numpy().astype(np.int64),
+                    f"{name}_rk": _bits(rk), f"{name}_rv": _bits(rv), f"{name}_out": a.numpy(),
+                    f"{name}_qpos": qpos.numpy().astype(np.int64)})
+    out["kpos"] = kpos.numpy().astype(np.int64)
+    np.savez_compressed(os.path.join(HERE, "quest.npz"), **out)
+
+
+def main(reference_root: str) -> None:
+    sys.path.insert(0, reference_root)
+    import torch
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    from pseudobrain import exact_memory as E
+    from pseudobrain import gated_deltanet as G
+    make_gdn(G)
+    make_quest(E)
+    for name in sorted(os.listdir(HERE)):
+        if name.endswith(".npz"):
+            print(name, os.path.getsize(os.path.join(HERE, name)), "bytes")
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <pseudobrain source checkout>")
+    main(sys.argv[1])

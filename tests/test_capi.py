@@ -1,0 +1,79 @@
+"""The C-ABI library loads on a CPU-only host and exports every function include/pbk.h
+declares; the ctypes structures match the header's layout. No compute calls."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from tests.conftest import ROOT
+
+HEADER_DIR = os.path.join(ROOT, "include")
+
+
+def _declared_functions() -> set[str]:
+    names = set()
+    for fn in os.listdir(HEADER_DIR):
+        if fn.endswith(".h"):
+            text = open(os.path.join(HEADER_DIR, fn)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names |= set(re.findall(r"^\s*(?:const\s+)?\w[\w\s\*]*?\b(pbk_\w+)\s*\(", text, flags=re.M))
+    return names
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from pseudobrain_b200 import build
+    build.build()
+    return ctypes.CDLL(build.LIB_PATH)
+
+
+def test_header_declares_entry_points():
+    names = _declared_functions()
+    assert {"pbk_abi_version", "pbk_status_string", "pbk_device_check", "pbk_gdn_decode"} <= names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in sorted(_declared_functions()) if not hasattr(lib, n)]
+    assert not missing, f"declared in include/ but not exported: {missing}"
+
+
+def test_ctypes_binding_covers_the_header(lib):
+    from pseudobrain_b200 import _capi
+    assert set(_capi.SIGNATURES) == _declared_functions()
+
+
+def test_abi_version_and_status_strings(lib):
+    from pseudobrain_b200 import _capi
+    assert _capi.LIB.pbk_abi_version() == _capi.PBK_ABI_VERSION
+    assert _capi.LIB.pbk_status_string(0) == b"ok"
+    assert _capi.LIB.pbk_status_string(-7) == b"device-side wait timed out"
+
+
+def test_descriptor_layout_matches_header():
+    """Offsets of the ctypes mirror equal the C struct's (checked by compiling a probe)."""
+    import subprocess
+    import tempfile
+    from pseudobrain_b200 import _capi
+    fields = ["batch", "q", "k", "v", "g", "beta", "o", "h0", "state", "state_slot_stride",
+              "state_layout", "state_indices", "scale"]
+    src = "#include <stdio.h>\n#include <stddef.h>\n#include \"pbk.h\"\nint main(void){\n"
+    src += "".join(f'printf("%zu\\n", offsetof(pbk_gdn_desc, {f}));\n' for f in fields)
+    src += 'printf("%zu\\n", sizeof(pbk_gdn_desc)); return 0; }\n'
+    with tempfile.TemporaryDirectory() as d:
+        c, exe = os.path.join(d, "p.c"), os.path.join(d, "p")
+        open(c, "w").write(src)
+        subprocess.run(["gcc", "-I", HEADER_DIR, c, "-o", exe], check=True)
+        got = [int(x) for x in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
+    want = [getattr(_capi.PbkGdnDesc, f).offset for f in fields] + [ctypes.sizeof(_capi.PbkGdnDesc)]
+    assert got == want
+
+
+def test_no_device_returns_error_without_launching(lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("host has a GPU")
+    from pseudobrain_b200 import _capi
+    assert _capi.LIB.pbk_device_check(0) == -5

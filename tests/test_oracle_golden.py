@@ -1,0 +1,112 @@
+"""Pin the CPU oracle against the reference's own outputs (tests/golden/*.npz).
+
+The fixtures were produced by tests/golden/make_golden.py from the reference's
+pseudobrain.gated_deltanet / pseudobrain.exact_memory functions. Both sides compute
+in fp32 with different summation orders, so float outputs agree to ~1e-6 relative;
+bounds, page indices and gathered keys must agree bit for bit.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import gdn as ogdn
+from oracle import quest as oq
+from tests.conftest import load_golden
+
+FP32_TOL = 1e-5
+
+
+def _f32(bits):
+    return oq.bf16_from_bits(bits)
+
+
+def test_gdn_fp32_chunked_and_sequential_match_reference():
+    f = load_golden("gdn_fp32.npz")
+    hv = f["v"].shape[2]
+    q, k = ogdn.expand_key_heads(f["q"], hv), ogdn.expand_key_heads(f["k"], hv)
+    args = (q, k, f["v"], f["g"], f["beta"], float(f["scale"]), f["h0"])
+    o, s = ogdn.delta_rule_chunked(*args)
+    assert ogdn.rel_err(o, f["o_chunked"]) < FP32_TOL
+    assert ogdn.rel_err(s, f["s_chunked"]) < FP32_TOL
+    o, s = ogdn.delta_rule_sequential(*args)
+    assert ogdn.rel_err(o, f["o_sequential"]) < FP32_TOL
+    assert ogdn.rel_err(s, f["s_sequential"]) < FP32_TOL
+    # The reference's two kernels agree with each other too (same recurrence).
+    assert ogdn.rel_err(f["o_chunked"], f["o_sequential"]) < FP32_TOL
+
+
+def test_gdn_bf16_inputs_chunked_matches_reference():
+    f = load_golden("gdn_bf16.npz")
+    hv = f["v"].shape[2]
+    q = ogdn.expand_key_heads(_f32(f["q"]), hv)
+    k = ogdn.expand_key_heads(_f32(f["k"]), hv)
+    o, s = ogdn.delta_rule_chunked(q, k, _f32(f["v"]), f["g"], _f32(f["beta"]), float(f["scale"]), f["h0"])
+    assert ogdn.rel_err(o, f["o_chunked"]) < FP32_TOL
+    assert ogdn.rel_err(s, f["s_chunked"]) < FP32_TOL
+
+
+def test_gdn_decode_sequential_matches_reference():
+    f = load_golden("gdn_decode.npz")
+    hv = f["v"].shape[2]
+    q = ogdn.expand_key_heads(_f32(f["q"]), hv)
+    k = ogdn.expand_key_heads(_f32(f["k"]), hv)
+    o, s = ogdn.delta_rule_sequential(q, k, _f32(f["v"]), _f32(f["g"]), _f32(f["beta"]),
+                                      float(f["scale"]), f["h0"])
+    assert ogdn.rel_err(o, f["o_sequential"]) < FP32_TOL
+    assert ogdn.rel_err(s, f["s_sequential"]) < FP32_TOL
+
+
+def test_gdn_fp64_oracle_agrees_with_fp32():
+    f = load_golden("gdn_fp32.npz")
+    hv = f["v"].shape[2]
+    q, k = ogdn.expand_key_heads(f["q"], hv), ogdn.expand_key_heads(f["k"], hv)
+    args64 = [x.astype(np.float64) for x in (q, k, f["v"], f["g"], f["beta"])]
+    o64, s64 = ogdn.delta_rule_sequential(*args64, float(f["scale"]), f["h0"].astype(np.float64))
+    assert ogdn.rel_err(f["o_chunked"], o64) < FP32_TOL
+    assert ogdn.rel_err(f["s_chunked"], s64) < FP32_TOL
+
+
+@pytest.fixture(scope="module")
+def quest():
+    f = load_golden("quest.npz")
+    page, n_arch = int(f["page"]), int(f["n_arch"])
+    keys, values = _f32(f["keys"]), _f32(f["values"])
+    arc = oq.archive_append(None, keys[:, :, :100], values[:, :, :100], page)
+    arc = oq.archive_append(arc, keys[:, :, 100:n_arch], values[:, :, 100:n_arch], page)
+    return f, arc, keys, values
+
+
+def test_quest_bounds_bit_exact(quest):
+    f, arc, _, _ = quest
+    assert np.array_equal(oq.bf16_bits(arc.kmax), f["kmax"])
+    assert np.array_equal(oq.bf16_bits(arc.kmin), f["kmin"])
+
+
+@pytest.mark.parametrize("case", ["t1", "t3"])
+def test_quest_retrieve_and_attend_match_reference(quest, case):
+    f, arc, keys, values = quest
+    page, budget, groups, window = (int(f[x]) for x in ("page", "budget", "groups", "window"))
+    n_arch = int(f["n_arch"])
+    q = _f32(f[f"{case}_q"])
+    rk, rv, top = oq.retrieve(arc, q, groups, page, budget)
+    assert np.array_equal(top, f[f"{case}_top"])
+    assert np.array_equal(oq.bf16_bits(rk), f[f"{case}_rk"])
+    assert np.array_equal(oq.bf16_bits(rv), f[f"{case}_rv"])
+    out = oq.attend(q, rk, rv, keys[:, :, n_arch:], values[:, :, n_arch:], f[f"{case}_qpos"],
+                    f["kpos"], window, 0, groups)
+    assert ogdn.rel_err(out, f[f"{case}_out"]) < FP32_TOL
+
+
+def test_select_pages_ties_go_to_lowest_index():
+    score = np.array([[3.0, 5.0, 5.0, 1.0, 5.0, 2.0]], dtype=np.float32)
+    assert oq.select_pages(score, 2).tolist() == [[1, 2]]
+    assert oq.select_pages(score, 4).tolist() == [[0, 1, 2, 4]]
+    assert oq.select_pages(score, 10).tolist() == [[0, 1, 2, 3, 4, 5]]
+
+
+def test_bf16_round_is_round_to_nearest_even():
+    import torch
+    x = np.random.default_rng(0).standard_normal(4096).astype(np.float32) * 37
+    ref = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    assert np.array_equal(oq.bf16_round(x), ref)
