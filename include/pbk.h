@@ -97,6 +97,14 @@ PBK_API int pbk_device_check(int device);
  * g/beta bf16 or fp32; o bf16 or fp32. */
 PBK_API int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream);
 
+/* Chunked gated delta rule (prefill): the chunkwise WY algorithm of
+ * delta_rule_chunked, pseudobrain/gated_deltanet.py:110-165 (chunk 64), reading h0
+ * (NULL = zeros) and writing the final state into `state` (h0 == state is allowed:
+ * in place) and every token's output into o. Sequence ends that are not a multiple
+ * of 64 are padded with identity steps as the reference does. Requires
+ * dk == dv == 128. */
+PBK_API int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

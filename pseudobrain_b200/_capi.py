@@ -39,6 +39,7 @@ SIGNATURES = {
     "pbk_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "pbk_device_check": (ctypes.c_int, [ctypes.c_int]),
     "pbk_gdn_decode": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
+    "pbk_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
 }
 
 

@@ -6,6 +6,7 @@
 
 namespace pbk {
 cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st);
+cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st);
 }
 
 namespace {
@@ -88,6 +89,15 @@ int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream) {
   if ((st = check_current_device()) != PBK_OK) return st;
   return pbk::launch_gdn_decode(*desc, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
                                                                                          : PBK_ERR_LAUNCH;
+}
+
+int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
+  int st = validate_gdn(desc);
+  if (st != PBK_OK) return st;
+  if (desc->batch == 0) return PBK_OK;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
+                                                                                               : PBK_ERR_LAUNCH;
 }
 
 }  // extern "C"

@@ -1,0 +1,116 @@
+"""GPU parity of the chunked prefill (pbk_gdn_prefill) against the oracle and the
+reference's golden outputs.
+
+fp32 inputs run the exact fp32 kernel: tolerance 1e-4 (BASELINE's fp32 bar). bf16
+inputs: 2e-2 norm-wise relative on o and on the final state (BASELINE's bf16 bar).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gdn as ogdn
+from oracle.quest import bf16_from_bits
+from tests.conftest import load_golden
+from tests.inputs import gdn_inputs, to_device
+
+pytestmark = pytest.mark.gpu
+TOL_FP32 = 1e-4
+TOL_BF16 = 2e-2
+
+
+def _oracle(inp):
+    hv = inp["v"].shape[2]
+    return ogdn.delta_rule_chunked(ogdn.expand_key_heads(inp["q"], hv), ogdn.expand_key_heads(inp["k"], hv),
+                                   inp["v"], inp["g"], inp["beta"], inp["scale"], inp["h0"])
+
+
+def test_prefill_fp32_matches_reference_golden(cuda_device):
+    from pseudobrain_b200 import gated_deltanet as G
+    f = load_golden("gdn_fp32.npz")
+    t = {n: torch.from_numpy(f[n]).to(cuda_device) for n in ("q", "k", "v", "g", "beta", "h0")}
+    o, s = G.delta_rule_chunked(t["q"], t["k"], t["v"], t["g"], t["beta"], float(f["scale"]), t["h0"])
+    assert ogdn.rel_err(o.cpu().numpy(), f["o_chunked"]) < TOL_FP32
+    assert ogdn.rel_err(s.cpu().numpy(), f["s_chunked"]) < TOL_FP32
+    # The reference's caller passes q, k already repeated to the value heads: same result.
+    qe, ke = (x.repeat_interleave(2, dim=2) for x in (t["q"], t["k"]))
+    o2, s2 = G.gated_delta_rule(qe, ke, t["v"], t["g"], t["beta"], float(f["scale"]), t["h0"], "chunked")
+    assert ogdn.rel_err(o2.cpu().numpy(), f["o_chunked"]) < TOL_FP32
+
+
+def test_prefill_bf16_matches_reference_golden(cuda_device):
+    from pseudobrain_b200 import gated_deltanet as G
+    f = load_golden("gdn_bf16.npz")
+    t = {n: torch.from_numpy(bf16_from_bits(f[n])).to(cuda_device, torch.bfloat16) for n in ("q", "k", "v", "beta")}
+    g = torch.from_numpy(f["g"]).to(cuda_device)
+    h0 = torch.from_numpy(f["h0"]).to(cuda_device)
+    o, s = G.delta_rule_chunked(t["q"], t["k"], t["v"], g, t["beta"], float(f["scale"]), h0)
+    assert ogdn.rel_err(o.cpu().numpy(), f["o_chunked"]) < TOL_BF16
+    assert ogdn.rel_err(s.cpu().numpy(), f["s_chunked"]) < TOL_BF16
+
+
+@pytest.mark.parametrize("batch,length,hk,hv,std", [
+    (1, 64, 1, 1, 0.0), (1, 2048, 4, 4, 0.0), (2, 200, 2, 4, 0.02), (3, 1, 1, 2, 0.02), (1, 129, 1, 8, 0.0)])
+def test_prefill_fp32_matches_oracle(cuda_device, batch, length, hk, hv, std):
+    """Includes BASELINE config 0 (B=1, T=2048, H=4) and ragged lengths."""
+    from pseudobrain_b200.gdn_prefill import gdn_prefill
+    inp = gdn_inputs(length + hv, batch, length, hk, hv, state_std=std)
+    d = to_device(inp, cuda_device)
+    o, s = gdn_prefill(d["q"], d["k"], d["v"], d["g"], d["beta"], inp["scale"], d["h0"])
+    ro, rs = _oracle(inp)
+    assert ogdn.rel_err(o.cpu().numpy(), ro) < TOL_FP32
+    assert ogdn.rel_err(s.cpu().numpy(), rs) < TOL_FP32
+
+
+@pytest.mark.parametrize("batch,length,hk,hv", [(1, 300, 1, 2), (2, 1024, 2, 4)])
+def test_prefill_bf16_matches_oracle(cuda_device, batch, length, hk, hv):
+    from pseudobrain_b200.gdn_prefill import gdn_prefill
+    inp = gdn_inputs(5 * length + hv, batch, length, hk, hv, bf16=True, state_std=0.02)
+    d = to_device(inp, cuda_device)
+    o, s = gdn_prefill(d["q"], d["k"], d["v"], d["g"], d["beta"], inp["scale"], d["h0"], torch.bfloat16)
+    ro, rs = _oracle(inp)
+    assert ogdn.rel_err(o.float().cpu().numpy(), ro) < TOL_BF16
+    assert ogdn.rel_err(s.cpu().numpy(), rs) < TOL_BF16
+
+
+def test_prefill_split_equals_whole(cuda_device):
+    """Chunked == full (gated_deltanet.py:26): two calls carrying the state equal one call."""
+    from pseudobrain_b200.gdn_prefill import gdn_prefill
+    inp = gdn_inputs(21, 2, 256, 1, 2, state_std=0.02)
+    d = to_device(inp, cuda_device)
+    args = [d[n] for n in ("q", "k", "v", "g", "beta")]
+    o, s = gdn_prefill(*args, inp["scale"], d["h0"])
+    o1, s1 = gdn_prefill(*(a[:, :128] for a in args), inp["scale"], d["h0"])
+    o2, s2 = gdn_prefill(*(a[:, 128:] for a in args), inp["scale"], s1)
+    assert torch.allclose(torch.cat((o1, o2), 1), o, rtol=0, atol=1e-5)
+    assert torch.allclose(s2, s, rtol=0, atol=1e-5)
+
+
+def test_prefill_and_decode_agree(cuda_device):
+    """Prefill of T tokens == T decode steps (two kernels, one recurrence)."""
+    from pseudobrain_b200 import gated_deltanet as G
+    from pseudobrain_b200.gdn_prefill import gdn_prefill
+    inp = gdn_inputs(22, 2, 70, 2, 4, state_std=0.02)
+    d = to_device(inp, cuda_device)
+    args = [d[n] for n in ("q", "k", "v", "g", "beta")]
+    o, s = gdn_prefill(*args, inp["scale"], d["h0"])
+    o2, s2 = G.delta_rule_sequential(*args, inp["scale"], d["h0"])
+    assert ogdn.rel_err(o.cpu().numpy(), o2.cpu().numpy()) < TOL_FP32
+    assert ogdn.rel_err(s.cpu().numpy(), s2.cpu().numpy()) < TOL_FP32
+
+
+def test_prefill_in_place_vk_layout_with_slots(cuda_device):
+    from pseudobrain_b200.gdn_prefill import gdn_prefill_
+    inp = gdn_inputs(23, 3, 100, 1, 2, state_std=0.02)
+    d = to_device(inp, cuda_device)
+    idx = torch.tensor([2, -1, 0], dtype=torch.int32, device=cuda_device)
+    pool = torch.zeros(4, 2, 128, 128, device=cuda_device)
+    pool[2], pool[0] = d["h0"][0].transpose(-1, -2), d["h0"][2].transpose(-1, -2)
+    o = torch.zeros(3, 100, 2, 128, device=cuda_device)
+    gdn_prefill_(d["q"], d["k"], d["v"], d["g"], d["beta"], pool, pool, o, inp["scale"], idx, 1)
+    ro, rs = _oracle(inp)
+    for b, slot in ((0, 2), (2, 0)):
+        assert ogdn.rel_err(pool[slot].transpose(-1, -2).cpu().numpy(), rs[b]) < TOL_FP32
+        assert ogdn.rel_err(o[b].cpu().numpy(), ro[b]) < TOL_FP32
+    assert torch.all(o[1] == 0) and torch.all(pool[1] == 0) and torch.all(pool[3] == 0)
