@@ -105,6 +105,76 @@ PBK_API int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream);
  * dk == dv == 128. */
 PBK_API int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Quest page-bounded exact memory (pseudobrain/exact_memory.py, flat mode).
+ *
+ * One archive of evicted keys/values [kv, n_arch, d] (bf16) with per-page key
+ * bounds [kv, n_arch / page, d] (bf16, elementwise max and min of each complete
+ * page), and nq independent query groups q [nq, t, h, d] (bf16): the t rows of a
+ * group share one page selection per key head, as the t queries of one call of
+ * the reference's retrieve() do (exact_memory.py:88-152). Query head j reads key
+ * head j / (h / kv).
+ * ------------------------------------------------------------------------ */
+typedef struct pbk_quest_desc {
+  int32_t nq, t, h, kv, d;  /* d must be 128 */
+  int32_t page;             /* tokens per page */
+  int32_t n_arch;           /* archived tokens; complete pages n_arch / page are scored, the rest is the tail */
+  int32_t budget;           /* pages kept per (group, key head): k = min(budget, n_arch / page) */
+  int32_t n_win;            /* window keys */
+  int32_t window, sinks;    /* window key visible to a query at qpos: kpos <= qpos and
+                               (qpos - kpos < window or kpos < sinks) (transplant.py:621-622) */
+  float scale;              /* softmax scale, d**-0.5 for SDPA's default */
+  const void* q;
+  int64_t q_stride_n, q_stride_t, q_stride_h;
+  const int32_t* qpos;      /* [nq, t] query positions */
+  const void* kmax;
+  const void* kmin;
+  int64_t bnd_stride_kv, bnd_stride_p;
+  const void* keys;
+  const void* values;
+  int64_t arc_stride_kv, arc_stride_n;
+  const void* win_keys;
+  const void* win_values;
+  int64_t win_stride_kv, win_stride_n;
+  const int32_t* kpos;      /* [n_win] positions of the window keys */
+  int32_t* pages;           /* [nq, kv, k] selected pages, ascending (written by select, read by attend) */
+  float* scores;            /* optional [nq, kv, n_arch / page] fp32 page scores (NULL: workspace) */
+  void* out;                /* [nq, t, h, d] attention output */
+  int64_t out_stride_n, out_stride_t, out_stride_h;
+  int32_t out_dtype;
+  int32_t pad_;
+} pbk_quest_desc;
+
+/* Bytes of caller-provided device workspace pbk_quest_select / pbk_quest_attend need
+ * for `desc` (0 when none; 256-byte aligned pointers). */
+PBK_API size_t pbk_quest_select_workspace(const pbk_quest_desc* desc);
+PBK_API size_t pbk_quest_attend_workspace(const pbk_quest_desc* desc);
+
+/* Page scores and top-k selection (exact_memory.py:94-98,124-125,135,144): for every
+ * group and key head, score page p as the maximum over the group's t * h/kv query rows
+ * of sum_d max(q_d kmax_pd, q_d kmin_pd) in fp32, keep the k highest (ties to the
+ * lowest page index) and write them to desc->pages in ascending order. */
+PBK_API int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Exact softmax attention of every query row over [selected pages ; partial tail ;
+ * window keys] with the window mask (pseudobrain/transplant.py:619-628), as a
+ * split-key pass plus a log-sum-exp combine. Gathers the pages itself. */
+PBK_API int pbk_quest_attend(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Copy `sel` pages per (group, key head) listed in desc->pages ([nq, kv, sel], any
+ * order, repeats allowed) and then the partial tail into out_keys / out_values
+ * [nq, kv, sel * page + tail, d] (bf16, contiguous): what retrieve() returns
+ * (exact_memory.py:145-151). */
+PBK_API int pbk_quest_gather(const pbk_quest_desc* desc, int32_t sel, void* out_keys, void* out_values, void* stream);
+
+/* Page bounds (exact_memory.py:43-50): kmax/kmin [kv, p, d] for pages
+ * first_page .. ceil(n / page) - 1 of keys [kv, n, d] (bf16); a trailing partial page
+ * takes the bounds of the keys it holds. Recomputing from the first incomplete page is
+ * archive_append's refresh (exact_memory.py:66-85). */
+PBK_API int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d, int32_t page,
+                             int64_t key_stride_kv, int64_t key_stride_n, void* kmax, void* kmin,
+                             int64_t bnd_stride_kv, int64_t bnd_stride_p, int32_t first_page, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,6 +33,27 @@ class PbkGdnDesc(ctypes.Structure):
                 ("pad2_", ctypes.c_int32)]
 
 
+class PbkQuestDesc(ctypes.Structure):
+    _fields_ = [("nq", ctypes.c_int32), ("t", ctypes.c_int32), ("h", ctypes.c_int32), ("kv", ctypes.c_int32),
+                ("d", ctypes.c_int32), ("page", ctypes.c_int32), ("n_arch", ctypes.c_int32),
+                ("budget", ctypes.c_int32), ("n_win", ctypes.c_int32), ("window", ctypes.c_int32),
+                ("sinks", ctypes.c_int32), ("scale", ctypes.c_float),
+                ("q", ctypes.c_void_p), ("q_stride_n", ctypes.c_int64), ("q_stride_t", ctypes.c_int64),
+                ("q_stride_h", ctypes.c_int64), ("qpos", ctypes.c_void_p),
+                ("kmax", ctypes.c_void_p), ("kmin", ctypes.c_void_p), ("bnd_stride_kv", ctypes.c_int64),
+                ("bnd_stride_p", ctypes.c_int64),
+                ("keys", ctypes.c_void_p), ("values", ctypes.c_void_p), ("arc_stride_kv", ctypes.c_int64),
+                ("arc_stride_n", ctypes.c_int64),
+                ("win_keys", ctypes.c_void_p), ("win_values", ctypes.c_void_p), ("win_stride_kv", ctypes.c_int64),
+                ("win_stride_n", ctypes.c_int64), ("kpos", ctypes.c_void_p),
+                ("pages", ctypes.c_void_p), ("scores", ctypes.c_void_p),
+                ("out", ctypes.c_void_p), ("out_stride_n", ctypes.c_int64), ("out_stride_t", ctypes.c_int64),
+                ("out_stride_h", ctypes.c_int64), ("out_dtype", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+
+
+_QD = ctypes.POINTER(PbkQuestDesc)
+_VP, _I32, _I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+
 # name -> (restype, argtypes); every symbol include/pbk.h declares.
 SIGNATURES = {
     "pbk_abi_version": (ctypes.c_int, []),
@@ -40,6 +61,12 @@ SIGNATURES = {
     "pbk_device_check": (ctypes.c_int, [ctypes.c_int]),
     "pbk_gdn_decode": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
     "pbk_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
+    "pbk_quest_select_workspace": (ctypes.c_size_t, [_QD]),
+    "pbk_quest_attend_workspace": (ctypes.c_size_t, [_QD]),
+    "pbk_quest_select": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
+    "pbk_quest_attend": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
+    "pbk_quest_gather": (ctypes.c_int, [_QD, _I32, _VP, _VP, _VP]),
+    "pbk_quest_bounds": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I64, _I64, _VP, _VP, _I64, _I64, _I32, _VP]),
 }
 
 

@@ -3,6 +3,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "quest.cuh"
 
 namespace pbk {
 cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st);
@@ -37,6 +38,49 @@ int validate_gdn(const pbk_gdn_desc* d) {
   if (d->state_slot_stride < (int64_t)d->hv * d->dk * d->dv) return PBK_ERR_INVALID;
   if (!aligned16(d->state) || (d->h0 && !aligned16(d->h0)) || (d->state_slot_stride & 3)) return PBK_ERR_ALIGN;
   if ((int64_t)d->batch * d->hv > INT32_MAX) return PBK_ERR_SHAPE;
+  return PBK_OK;
+}
+
+constexpr size_t kWsAlign = 256;
+size_t round_up(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
+bool aligned_elems(int64_t stride, int64_t elems) { return stride % elems == 0; }
+
+// Shapes, pointers and alignment shared by the Quest entry points. `need` selects
+// which tensors must be present: 1 select, 2 attend, 4 gather.
+int validate_quest(const pbk_quest_desc* d, int need) {
+  if (d == nullptr) return PBK_ERR_INVALID;
+  if (d->nq < 0 || d->t < 1 || d->kv < 1 || d->h < d->kv || d->page < 1 || d->n_arch < 0 || d->budget < 0 ||
+      d->n_win < 0)
+    return PBK_ERR_INVALID;
+  if (d->h % d->kv != 0) return PBK_ERR_SHAPE;
+  if (d->d != 128) return PBK_ERR_SHAPE;
+  const int64_t rows_per_head = (int64_t)d->nq * d->t * (d->h / d->kv);
+  if (rows_per_head * 128 * 4 > 220 * 1024) return PBK_ERR_SHAPE;  // query rows of one key head in shared memory
+  if (!d->q || !d->pages) return PBK_ERR_INVALID;
+  if (!aligned16(d->q) || !aligned_elems(d->q_stride_n, 8) || !aligned_elems(d->q_stride_t, 8) ||
+      !aligned_elems(d->q_stride_h, 8))
+    return PBK_ERR_ALIGN;
+  const int npages = d->n_arch / d->page;
+  if ((need & 1) && npages > 0) {
+    if (!d->kmax || !d->kmin) return PBK_ERR_INVALID;
+    if (!aligned16(d->kmax) || !aligned16(d->kmin) || !aligned_elems(d->bnd_stride_kv, 8) ||
+        !aligned_elems(d->bnd_stride_p, 8))
+      return PBK_ERR_ALIGN;
+  }
+  if (need & 6) {
+    if (d->n_arch > 0 && (!d->keys || !d->values)) return PBK_ERR_INVALID;
+    if (!aligned16(d->keys) || !aligned16(d->values) || !aligned_elems(d->arc_stride_kv, 8) ||
+        !aligned_elems(d->arc_stride_n, 8))
+      return PBK_ERR_ALIGN;
+  }
+  if (need & 2) {
+    if (d->n_win > 0 && (!d->win_keys || !d->win_values || !d->kpos)) return PBK_ERR_INVALID;
+    if (!aligned16(d->win_keys) || !aligned16(d->win_values) || !aligned_elems(d->win_stride_kv, 8) ||
+        !aligned_elems(d->win_stride_n, 8))
+      return PBK_ERR_ALIGN;
+    if (!d->qpos || !d->out) return PBK_ERR_INVALID;
+    if (d->out_dtype != PBK_F32 && d->out_dtype != PBK_BF16) return PBK_ERR_DTYPE;
+  }
   return PBK_OK;
 }
 
@@ -98,6 +142,72 @@ int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
   if ((st = check_current_device()) != PBK_OK) return st;
   return pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
                                                                                                : PBK_ERR_LAUNCH;
+}
+
+size_t pbk_quest_select_workspace(const pbk_quest_desc* desc) {
+  if (validate_quest(desc, 1) != PBK_OK) return 0;
+  return round_up(pbk::quest_score_bytes(*desc));
+}
+
+size_t pbk_quest_attend_workspace(const pbk_quest_desc* desc) {
+  if (validate_quest(desc, 2) != PBK_OK) return 0;
+  return round_up(pbk::quest_partial_bytes(*desc));
+}
+
+int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = validate_quest(desc, 1);
+  if (st != PBK_OK) return st;
+  const size_t need = pbk::quest_score_bytes(*desc);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return PBK_ERR_WORKSPACE;
+  if (desc->nq == 0) return PBK_OK;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  float* scores = desc->scores ? desc->scores : static_cast<float*>(workspace);
+  return pbk::launch_quest_select(*desc, scores, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
+                                                                                                   : PBK_ERR_LAUNCH;
+}
+
+int pbk_quest_attend(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = validate_quest(desc, 2);
+  if (st != PBK_OK) return st;
+  const size_t need = pbk::quest_partial_bytes(*desc);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return PBK_ERR_WORKSPACE;
+  if (desc->nq == 0) return PBK_OK;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return pbk::launch_quest_attend(*desc, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? PBK_OK
+             : PBK_ERR_LAUNCH;
+}
+
+int pbk_quest_gather(const pbk_quest_desc* desc, int32_t sel, void* out_keys, void* out_values, void* stream) {
+  int st = validate_quest(desc, 4);
+  if (st != PBK_OK) return st;
+  if (sel < 0 || (sel > 0 && desc->n_arch / desc->page == 0)) return PBK_ERR_INVALID;
+  if (!aligned16(out_keys) || !aligned16(out_values)) return PBK_ERR_ALIGN;
+  if (desc->nq == 0) return PBK_OK;
+  if (!out_keys || !out_values) return PBK_ERR_INVALID;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return pbk::launch_quest_gather(*desc, sel, out_keys, out_values, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? PBK_OK
+             : PBK_ERR_LAUNCH;
+}
+
+int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d, int32_t page, int64_t key_stride_kv,
+                     int64_t key_stride_n, void* kmax, void* kmin, int64_t bnd_stride_kv, int64_t bnd_stride_p,
+                     int32_t first_page, void* stream) {
+  if (kv < 1 || n < 0 || page < 1 || first_page < 0) return PBK_ERR_INVALID;
+  if (d != 128) return PBK_ERR_SHAPE;
+  if (n == 0 || first_page * (int64_t)page >= n) return PBK_OK;
+  if (!keys || !kmax || !kmin) return PBK_ERR_INVALID;
+  if (!aligned16(keys) || !aligned16(kmax) || !aligned16(kmin) || key_stride_n % 8 || key_stride_kv % 8 ||
+      bnd_stride_kv % 8 || bnd_stride_p % 8)
+    return PBK_ERR_ALIGN;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return pbk::launch_quest_bounds(keys, kv, n, page, key_stride_kv, key_stride_n, kmax, kmin, bnd_stride_kv,
+                                  bnd_stride_p, first_page, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? PBK_OK
+             : PBK_ERR_LAUNCH;
 }
 
 }  // extern "C"

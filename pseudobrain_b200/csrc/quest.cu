@@ -1,0 +1,452 @@
+// Quest page-bounded exact memory: page bounds, page scores, exact top-k page
+// selection, page gather and split-key exact attention (flat mode of
+// pseudobrain/exact_memory.py:43-152 and the attention of pseudobrain/transplant.py:612-628).
+#include <cfloat>
+
+#include "common.cuh"
+#include "quest.cuh"
+
+namespace pbk {
+namespace {
+
+constexpr int kD = 128;
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 raw, float* out) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(p[i]);
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Page bounds: one warp per (page, key head); lane l owns dims 4l..4l+3.
+// ---------------------------------------------------------------------------------
+__global__ void quest_bounds_kernel(const bf16* keys, int n, int page, int64_t ks_kv, int64_t ks_n, bf16* kmax,
+                                    bf16* kmin, int64_t bs_kv, int64_t bs_p, int first_page, int npages) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= npages) return;
+  const int p = first_page + warp, h = blockIdx.y;
+  const int t0 = p * page, t1 = min(t0 + page, n);
+  float mx[4], mn[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mx[i] = -FLT_MAX, mn[i] = FLT_MAX;
+  for (int t = t0; t < t1; ++t) {
+    const bf16* row = keys + h * ks_kv + (int64_t)t * ks_n + 4 * lane;
+    const uint2 raw = *reinterpret_cast<const uint2*>(row);
+    const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    const float2 a = __bfloat1622float2(pr[0]), b = __bfloat1622float2(pr[1]);
+    const float v[4] = {a.x, a.y, b.x, b.y};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mx[i] = fmaxf(mx[i], v[i]), mn[i] = fminf(mn[i], v[i]);
+  }
+  bf16* omx = kmax + h * bs_kv + (int64_t)p * bs_p + 4 * lane;
+  bf16* omn = kmin + h * bs_kv + (int64_t)p * bs_p + 4 * lane;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // max/min of bf16 values are bf16 values: exact
+    omx[i] = __float2bfloat16_rn(mx[i]);
+    omn[i] = __float2bfloat16_rn(mn[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Page scores. Thread = page; the group's query rows sit in shared memory as fp32.
+// score[n][kv][p] = max over rows r of group n of sum_d q_rd * (q_rd > 0 ? kmax_pd : kmin_pd)
+// (each product of two bf16 values is exact in fp32).
+// ---------------------------------------------------------------------------------
+constexpr int kScoreThreads = 128;
+constexpr int kRowBlock = 4;
+
+__global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_quest_desc d, int npages, float* scores) {
+  extern __shared__ __align__(16) float qs[];  // [rows of one key head][kD]
+  const int h = blockIdx.y, groups = d.h / d.kv, rows_per_group = d.t * groups;
+  const int rows = d.nq * rows_per_group;
+  for (int e = threadIdx.x; e < rows * kD; e += kScoreThreads) {
+    const int r = e / kD, dd = e % kD;
+    const int n = r / rows_per_group, rem = r % rows_per_group, ti = rem / groups, g = rem % groups;
+    const bf16* qp = reinterpret_cast<const bf16*>(d.q) + n * d.q_stride_n + ti * d.q_stride_t +
+                     (int64_t)(h * groups + g) * d.q_stride_h;
+    qs[e] = __bfloat162float(qp[dd]);
+  }
+  __syncthreads();
+  const int p = blockIdx.x * kScoreThreads + threadIdx.x;
+  if (p >= npages) return;
+  const bf16* bmax = reinterpret_cast<const bf16*>(d.kmax) + h * d.bnd_stride_kv + (int64_t)p * d.bnd_stride_p;
+  const bf16* bmin = reinterpret_cast<const bf16*>(d.kmin) + h * d.bnd_stride_kv + (int64_t)p * d.bnd_stride_p;
+  for (int n = 0; n < d.nq; ++n) {
+    float best = -INFINITY;
+    for (int r0 = 0; r0 < rows_per_group; r0 += kRowBlock) {
+      const int nr = min(kRowBlock, rows_per_group - r0);
+      const float* qb = qs + (n * rows_per_group + r0) * kD;
+      float acc[kRowBlock] = {0.f, 0.f, 0.f, 0.f};
+      for (int d0 = 0; d0 < kD; d0 += 8) {
+        float mx[8], mn[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmax + d0), mx);
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmin + d0), mn);
+#pragma unroll
+        for (int r = 0; r < kRowBlock; ++r) {
+          if (r < nr) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float qv = qb[r * kD + d0 + j];
+              acc[r] = fmaf(qv, qv > 0.f ? mx[j] : mn[j], acc[r]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kRowBlock; ++r)
+        if (r < nr) best = fmaxf(best, acc[r]);
+    }
+    scores[((int64_t)n * d.kv + h) * npages + p] = best;
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Exact top-k per row (one CTA per (group, key head)): radix select over the order-
+// preserving 32-bit keys of the fp32 scores, one 8-bit digit per pass, then one pass
+// that writes the selected page indices in ascending order (ties at the threshold go
+// to the lowest indices).
+// ---------------------------------------------------------------------------------
+constexpr int kTopkThreads = 1024;
+
+__device__ __forceinline__ uint32_t ordered_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int N>
+__device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
+  // scratch: >= N/32 + 1 ints
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < N / 32 ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < N / 32) scratch[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  const int base = warp > 0 ? scratch[warp - 1] : 0;
+  *total = scratch[N / 32 - 1];
+  __syncthreads();
+  return base + x - v;
+}
+
+__global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* scores, int npages, int k,
+                                                                  int32_t* pages) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh_prefix, sh_kk;
+  __shared__ int scan_scratch[kTopkThreads / 32 + 1];
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const float* s = scores + (int64_t)row * npages;
+  int32_t* out = pages + (int64_t)row * k;
+  uint32_t prefix = 0, mask = 0, kk = (uint32_t)k;
+  for (int digit = 3; digit >= 0; --digit) {
+    const int shift = digit * 8;
+    if (tid < 256) hist[tid] = 0;
+    __syncthreads();
+    for (int base = 0; base < npages; base += kTopkThreads) {
+      const int i = base + tid;
+      uint32_t bin = 0xFFFFFFFFu;
+      if (i < npages) {
+        const uint32_t u = ordered_key(s[i]);
+        if ((u & mask) == prefix) bin = (u >> shift) & 255u;
+      }
+      const uint32_t same = __match_any_sync(0xffffffffu, bin);
+      if (bin != 0xFFFFFFFFu && lane == __ffs(same) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(same));
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t above = 0;
+      int b = 255;
+      for (; b > 0; --b) {
+        if (above + hist[b] >= kk) break;
+        above += hist[b];
+      }
+      sh_prefix = prefix | ((uint32_t)b << shift);
+      sh_kk = kk - above;
+    }
+    __syncthreads();
+    prefix = sh_prefix;
+    kk = sh_kk;
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  // prefix is now the k-th largest key; kk of the elements equal to it are selected.
+  const int span = (npages + kTopkThreads - 1) / kTopkThreads;
+  const int lo = min(tid * span, npages), hi = min(lo + span, npages);
+  int n_gt = 0, n_eq = 0;
+  for (int i = lo; i < hi; ++i) {
+    const uint32_t u = ordered_key(s[i]);
+    n_gt += u > prefix;
+    n_eq += u == prefix;
+  }
+  int tot;
+  const int base_gt = block_exclusive_scan<kTopkThreads>(n_gt, scan_scratch, &tot);
+  const int base_eq = block_exclusive_scan<kTopkThreads>(n_eq, scan_scratch, &tot);
+  int pos = base_gt + min(base_eq, (int)kk), eq_seen = base_eq;
+  for (int i = lo; i < hi; ++i) {
+    const uint32_t u = ordered_key(s[i]);
+    if (u > prefix) {
+      out[pos++] = i;
+    } else if (u == prefix) {
+      if (eq_seen < (int)kk) out[pos++] = i;
+      ++eq_seen;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Gather of the selected pages + partial tail (what retrieve() returns).
+// ---------------------------------------------------------------------------------
+__global__ void quest_gather_kernel(const pbk_quest_desc d, int k, int tail, bf16* ok, bf16* ov) {
+  const int n = blockIdx.z, h = blockIdx.y;
+  const int rows = k * d.page + tail;
+  const int row = blockIdx.x * (blockDim.x / 16) + threadIdx.x / 16, part = threadIdx.x % 16;
+  if (row >= rows) return;
+  int src;
+  if (row < k * d.page) src = d.pages[((int64_t)n * d.kv + h) * k + row / d.page] * d.page + row % d.page;
+  else src = (d.n_arch / d.page) * d.page + (row - k * d.page);
+  const int64_t so = h * d.arc_stride_kv + (int64_t)src * d.arc_stride_n + part * 8;
+  const int64_t dst = (((int64_t)n * d.kv + h) * rows + row) * kD + part * 8;
+  *reinterpret_cast<uint4*>(ok + dst) = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(d.keys) + so);
+  *reinterpret_cast<uint4*>(ov + dst) = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(d.values) + so);
+}
+
+// ---------------------------------------------------------------------------------
+// Split-key exact attention. Virtual key j of a (group, key head):
+//   j <  k*page          : archive token pages[j / page] * page + j % page (visible)
+//   j <  k*page + tail   : archive tail token (visible)
+//   otherwise            : window key j - R (visible per the window mask)
+// CTA = (split of kSplitKeys virtual keys, group*kv + key head); 128 threads: two keys
+// per thread for the logits, one output dim per thread for P V. Partials (m, l, acc[d])
+// go to the workspace; quest_combine_kernel merges them.
+// ---------------------------------------------------------------------------------
+constexpr int kAttThreads = 128;
+constexpr int kSplitKeys = 256;
+constexpr int kAttRows = 4;  // query rows per pass
+
+__device__ __forceinline__ bool key_visible(int kp, int qp, int window, int sinks) {
+  return kp <= qp && ((qp - kp) < window || kp < sinks);
+}
+
+__global__ void __launch_bounds__(kAttThreads) quest_attend_kernel(const pbk_quest_desc d, int k, int tail, int splits,
+                                                                  float* part) {
+  __shared__ __align__(16) float qs[kAttRows][kD];
+  __shared__ float logit[kAttRows][kSplitKeys];
+  __shared__ int kidx[kSplitKeys];     // archive token, or -1 - window index
+  __shared__ float red[kAttRows][kAttThreads / 32];
+  __shared__ float sh_m[kAttRows], sh_l[kAttRows];
+  const int split = blockIdx.x, n = blockIdx.y / d.kv, h = blockIdx.y % d.kv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int groups = d.h / d.kv, rows = d.t * groups;
+  const int n_ret = k * d.page + tail, n_all = n_ret + d.n_win;
+  const int j0 = split * kSplitKeys, nkeys = min(kSplitKeys, n_all - j0);
+  const bf16* keys = reinterpret_cast<const bf16*>(d.keys);
+  const bf16* vals = reinterpret_cast<const bf16*>(d.values);
+  const bf16* wkeys = reinterpret_cast<const bf16*>(d.win_keys);
+  const bf16* wvals = reinterpret_cast<const bf16*>(d.win_values);
+  const float sl2 = d.scale * 1.4426950408889634f;  // softmax in base 2
+  for (int j = tid; j < kSplitKeys; j += kAttThreads) {
+    const int vj = j0 + j;
+    int idx = 0;
+    if (j < nkeys) {
+      if (vj < k * d.page) idx = d.pages[((int64_t)n * d.kv + h) * k + vj / d.page] * d.page + vj % d.page;
+      else if (vj < n_ret) idx = (d.n_arch / d.page) * d.page + (vj - k * d.page);
+      else idx = -1 - (vj - n_ret);
+    }
+    kidx[j] = idx;
+  }
+  for (int r0 = 0; r0 < rows; r0 += kAttRows) {
+    const int nr = min(kAttRows, rows - r0);
+    __syncthreads();
+    for (int e = tid; e < kAttRows * kD; e += kAttThreads) {
+      const int r = e / kD, dd = e % kD;
+      float v = 0.f;
+      if (r < nr) {
+        const int rr = r0 + r, ti = rr / groups, g = rr % groups;
+        v = __bfloat162float(reinterpret_cast<const bf16*>(d.q)[n * d.q_stride_n + ti * d.q_stride_t +
+                                                                 (int64_t)(h * groups + g) * d.q_stride_h + dd]);
+      }
+      qs[r][dd] = v;
+    }
+    __syncthreads();
+    // logits: thread handles keys tid and tid + 128
+    for (int j = tid; j < kSplitKeys; j += kAttThreads) {
+      float acc[kAttRows] = {0.f, 0.f, 0.f, 0.f};
+      const int idx = kidx[j];
+      if (j < nkeys) {
+        const bf16* kr = idx >= 0 ? keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
+                                  : wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+        for (int d0 = 0; d0 < kD; d0 += 8) {
+          float kv8[8];
+          bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + d0), kv8);
+#pragma unroll
+          for (int r = 0; r < kAttRows; ++r) {
+            const float4 qa = *reinterpret_cast<const float4*>(&qs[r][d0]);
+            const float4 qb = *reinterpret_cast<const float4*>(&qs[r][d0 + 4]);
+            acc[r] = fmaf(qa.x, kv8[0], acc[r]); acc[r] = fmaf(qa.y, kv8[1], acc[r]);
+            acc[r] = fmaf(qa.z, kv8[2], acc[r]); acc[r] = fmaf(qa.w, kv8[3], acc[r]);
+            acc[r] = fmaf(qb.x, kv8[4], acc[r]); acc[r] = fmaf(qb.y, kv8[5], acc[r]);
+            acc[r] = fmaf(qb.z, kv8[6], acc[r]); acc[r] = fmaf(qb.w, kv8[7], acc[r]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kAttRows; ++r) {
+        bool vis = j < nkeys && r < nr;
+        if (vis && idx < 0) {
+          const int rr = r0 + r, ti = rr / groups;
+          vis = key_visible(d.kpos[-1 - idx], d.qpos[n * d.t + ti], d.window, d.sinks);
+        }
+        logit[r][j] = vis ? acc[r] * sl2 : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // row max and sum over this split's keys
+    float m[kAttRows];
+#pragma unroll
+    for (int r = 0; r < kAttRows; ++r) {
+      float x = fmaxf(logit[r][tid], logit[r][tid + kAttThreads]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+      if (lane == 0) red[r][warp] = x;
+    }
+    __syncthreads();
+    if (tid < kAttRows) {
+      float x = red[tid][0];
+      for (int w = 1; w < kAttThreads / 32; ++w) x = fmaxf(x, red[tid][w]);
+      sh_m[tid] = x;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kAttRows; ++r) {
+      m[r] = sh_m[r];
+      float s = 0.f;
+      for (int j = tid; j < kSplitKeys; j += kAttThreads) {
+        const float p = m[r] == -INFINITY ? 0.f : exp2f(logit[r][j] - m[r]);
+        logit[r][j] = p;
+        s += p;
+      }
+      s = warp_sum(s);
+      if (lane == 0) red[r][warp] = s;
+    }
+    __syncthreads();
+    if (tid < kAttRows) {
+      float x = 0.f;
+      for (int w = 0; w < kAttThreads / 32; ++w) x += red[tid][w];
+      sh_l[tid] = x;
+    }
+    __syncthreads();
+    // P V: thread = output dim
+    float acc[kAttRows] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < nkeys; ++j) {
+      const int idx = kidx[j];
+      const bf16* vr = idx >= 0 ? vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
+                                : wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+      const float v = __bfloat162float(vr[tid]);
+#pragma unroll
+      for (int r = 0; r < kAttRows; ++r) acc[r] = fmaf(logit[r][j], v, acc[r]);
+    }
+    for (int r = 0; r < nr; ++r) {
+      const int rr = r0 + r, ti = rr / groups, g = rr % groups;
+      const int64_t row = (((int64_t)n * d.t + ti) * d.h + h * groups + g) * splits + split;
+      float* pp = part + row * (kD + 2);
+      pp[tid] = acc[r];
+      if (tid == 0) pp[kD] = sh_m[r], pp[kD + 1] = sh_l[r];
+    }
+  }
+}
+
+__global__ void quest_combine_kernel(const pbk_quest_desc d, int splits, const float* part) {
+  const int row = blockIdx.x;  // (n, ti, head)
+  const int head = row % d.h, ti = (row / d.h) % d.t, n = row / (d.h * d.t);
+  const float* pp = part + (int64_t)row * splits * (kD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, pp[s * (kD + 2) + kD]);
+  float L = 0.f, acc = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float ms = pp[s * (kD + 2) + kD];
+    const float w = ms == -INFINITY ? 0.f : exp2f(ms - M);
+    L = fmaf(pp[s * (kD + 2) + kD + 1], w, L);
+    acc = fmaf(pp[s * (kD + 2) + threadIdx.x], w, acc);
+  }
+  const float o = acc / L;
+  const int64_t off = n * d.out_stride_n + ti * d.out_stride_t + head * d.out_stride_h + threadIdx.x;
+  if (d.out_dtype == PBK_BF16) reinterpret_cast<bf16*>(d.out)[off] = __float2bfloat16_rn(o);
+  else reinterpret_cast<float*>(d.out)[off] = o;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------
+// Launch helpers (called from capi.cu after validation).
+// ---------------------------------------------------------------------------------
+int quest_k(const pbk_quest_desc& d) { return min(d.budget, d.n_arch / d.page); }
+int quest_splits(const pbk_quest_desc& d) {
+  const int n_all = quest_k(d) * d.page + (d.n_arch % d.page) + d.n_win;
+  return (n_all + kSplitKeys - 1) / kSplitKeys;
+}
+size_t quest_score_bytes(const pbk_quest_desc& d) {
+  return d.scores ? 0 : (size_t)d.nq * d.kv * (d.n_arch / d.page) * sizeof(float);
+}
+size_t quest_partial_bytes(const pbk_quest_desc& d) {
+  return (size_t)d.nq * d.t * d.h * quest_splits(d) * (kD + 2) * sizeof(float);
+}
+
+cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStream_t st) {
+  const int npages = d.n_arch / d.page, k = quest_k(d);
+  if (npages == 0 || k == 0) return cudaSuccess;
+  const int rows = d.nq * d.t * (d.h / d.kv);
+  const size_t smem = (size_t)rows * kD * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(quest_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  quest_score_kernel<<<dim3((npages + kScoreThreads - 1) / kScoreThreads, d.kv), kScoreThreads, smem, st>>>(
+      d, npages, scores);
+  quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, 0, st>>>(scores, npages, k, d.pages);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st) {
+  const int k = quest_k(d), tail = d.n_arch % d.page, splits = quest_splits(d);
+  if (splits == 0) return cudaSuccess;
+  quest_attend_kernel<<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part);
+  quest_combine_kernel<<<d.nq * d.t * d.h, kD, 0, st>>>(d, splits, part);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quest_gather(const pbk_quest_desc& d, int sel, void* ok, void* ov, cudaStream_t st) {
+  const int k = sel, tail = d.n_arch % d.page, rows = k * d.page + tail;
+  if (rows == 0) return cudaSuccess;
+  quest_gather_kernel<<<dim3((rows + 15) / 16, d.kv, d.nq), 256, 0, st>>>(d, k, tail, static_cast<bf16*>(ok),
+                                                                           static_cast<bf16*>(ov));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int page, int64_t ks_kv, int64_t ks_n, void* kmax,
+                                void* kmin, int64_t bs_kv, int64_t bs_p, int first_page, cudaStream_t st) {
+  const int npages = (n + page - 1) / page - first_page;
+  if (npages <= 0) return cudaSuccess;
+  quest_bounds_kernel<<<dim3((npages + 7) / 8, kv), 256, 0, st>>>(
+      static_cast<const bf16*>(keys), n, page, ks_kv, ks_n, static_cast<bf16*>(kmax), static_cast<bf16*>(kmin), bs_kv,
+      bs_p, first_page, npages);
+  return cudaGetLastError();
+}
+
+}  // namespace pbk

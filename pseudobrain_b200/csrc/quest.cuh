@@ -1,0 +1,19 @@
+// Launchers of the Quest kernels (quest.cu), called by the C ABI after validation.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#include "../../include/pbk.h"
+
+namespace pbk {
+int quest_k(const pbk_quest_desc& d);
+int quest_splits(const pbk_quest_desc& d);
+size_t quest_score_bytes(const pbk_quest_desc& d);
+size_t quest_partial_bytes(const pbk_quest_desc& d);
+cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStream_t st);
+cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st);
+cudaError_t launch_quest_gather(const pbk_quest_desc& d, int sel, void* ok, void* ov, cudaStream_t st);
+cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int page, int64_t ks_kv, int64_t ks_n, void* kmax,
+                                void* kmin, int64_t bs_kv, int64_t bs_p, int first_page, cudaStream_t st);
+}  // namespace pbk

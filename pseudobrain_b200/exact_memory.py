@@ -1,0 +1,284 @@
+"""Quest page-bounded exact memory on B200: drop-in for pseudobrain/exact_memory.py.
+
+Same names and meanings as the reference (pseudobrain/exact_memory.py:20-152):
+
+    EXACT_MEMORY                                  configuration dict
+    Archive(keys, values, kmax, kmin, ...)        evicted keys/values [B,KV,N,hd] + page bounds
+    archive_append(archive, keys, values)        -> Archive
+    retrieve(archive, q, groups)                 -> (keys, values) [B,KV,R,hd] or None
+
+plus the fused path of this build, which never materialises the gathered keys:
+
+    select_pages(...)     page scores + exact top-k   (pbk_quest_select)
+    attend_pages(...)     split-key exact attention over pages + tail + window (pbk_quest_attend)
+    retrieve_attend(...)  both, with the reference's mask (pseudobrain/transplant.py:612-628)
+
+Only the flat, single-level Quest mode runs here: ``superblock`` two-level selection
+and exact ``rerank`` raise NotImplementedError when the reference would take them.
+Keys are bf16 with head_dim 128; every call runs CUDA kernels from libpbk.so and
+there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _capi
+from ._capi import LIB, PbkQuestDesc, check
+
+EXACT_MEMORY = {"enabled": False, "blocks": 64, "block_size": 64, "decode_blocks": 64, "neighbors": 0, "rerank": 0,
+                "decode_rerank": 0, "superblock": 64, "keys_like_values": False}
+
+
+@dataclass
+class Archive:
+    """Evicted rotated keys/values [B,KV,N,hd] and per-page bounds [B,KV,pages,hd]
+    (reference: exact_memory.py:27-40)."""
+    keys: torch.Tensor
+    values: torch.Tensor
+    kmax: torch.Tensor
+    kmin: torch.Tensor
+    smax: torch.Tensor | None = None
+    smin: torch.Tensor | None = None
+    prompt_top: torch.Tensor | None = None
+
+    @property
+    def length(self) -> int:
+        return self.keys.shape[2]
+
+
+def _require(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what}: pseudobrain_b200 runs on CUDA only (no CPU fallback)")
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{what}: bf16 expected, got {t.dtype}")
+    if t.shape[-1] != 128 or t.stride(-1) != 1:
+        raise ValueError(f"{what}: head_dim must be 128 and contiguous")
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def page_bounds_(keys: torch.Tensor, page: int, kmax: torch.Tensor, kmin: torch.Tensor, first_page: int = 0) -> None:
+    """Write the bounds of pages first_page.. of keys [KV,N,hd] into kmax/kmin [KV,P,hd]
+    (reference: _bounds, exact_memory.py:43-50)."""
+    _require(keys, "keys")
+    kv, n, d = keys.shape
+    if kmax.shape != kmin.shape or kmax.shape[0] != kv or kmax.shape[1] < (n + page - 1) // page:
+        raise ValueError(f"bounds {tuple(kmax.shape)} too small for {n} keys in pages of {page}")
+    _require(kmax, "kmax")
+    _require(kmin, "kmin")
+    with torch.cuda.device(keys.device):
+        check(LIB.pbk_quest_bounds(keys.data_ptr(), kv, n, d, page, keys.stride(0), keys.stride(1), kmax.data_ptr(),
+                                   kmin.data_ptr(), kmax.stride(0), kmax.stride(1), first_page, _stream(keys)),
+              "pbk_quest_bounds")
+
+
+def page_bounds(keys: torch.Tensor, page: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(kmax, kmin) [B,KV,ceil(N/page),hd] of keys [B,KV,N,hd]."""
+    b, kv, n, d = keys.shape
+    p = (n + page - 1) // page
+    kmax = torch.empty(b, kv, p, d, dtype=keys.dtype, device=keys.device)
+    kmin = torch.empty_like(kmax)
+    for i in range(b):
+        page_bounds_(keys[i], page, kmax[i], kmin[i])
+    return kmax, kmin
+
+
+def archive_append(archive: Archive | None, keys: torch.Tensor, values: torch.Tensor) -> Archive | None:
+    """Append evicted keys/values and refresh the bounds from the first incomplete page
+    on (reference: exact_memory.py:66-85). Super-block bounds are not kept (flat mode)."""
+    if keys.shape[2] == 0:
+        return archive
+    page = EXACT_MEMORY["block_size"]
+    if EXACT_MEMORY["keys_like_values"]:
+        keys = keys.to(values.dtype)
+    if archive is None:
+        kmax, kmin = page_bounds(keys, page)
+        return Archive(keys, values, kmax, kmin)
+    full = archive.length // page
+    new_k = torch.cat((archive.keys, keys), dim=2)
+    new_v = torch.cat((archive.values, values), dim=2)
+    b, kv, n, d = new_k.shape
+    p = (n + page - 1) // page
+    kmax = torch.empty(b, kv, p, d, dtype=new_k.dtype, device=new_k.device)
+    kmin = torch.empty_like(kmax)
+    kmax[:, :, :full] = archive.kmax[:, :, :full]
+    kmin[:, :, :full] = archive.kmin[:, :, :full]
+    for i in range(b):
+        page_bounds_(new_k[i], page, kmax[i], kmin[i], first_page=full)
+    return Archive(new_k, new_v, kmax, kmin, None, None, archive.prompt_top)
+
+
+def _desc(q: torch.Tensor, page: int, n_arch: int, budget: int, *, kmax=None, kmin=None, keys=None, values=None,
+          pages=None, scores=None) -> PbkQuestDesc:
+    """q [nq, t, h, 128] bf16 (any strides with a contiguous last dim)."""
+    _require(q, "q")
+    nq, t, h, d = q.shape
+    kv = (kmax if kmax is not None else keys).shape[0]
+    desc = PbkQuestDesc(nq=nq, t=t, h=h, kv=kv, d=d, page=page, n_arch=n_arch, budget=budget,
+                        q=q.data_ptr(), q_stride_n=q.stride(0), q_stride_t=q.stride(1), q_stride_h=q.stride(2),
+                        pages=_ptr(pages), scores=_ptr(scores))
+    if kmax is not None:
+        desc.kmax, desc.kmin = kmax.data_ptr(), kmin.data_ptr()
+        desc.bnd_stride_kv, desc.bnd_stride_p = kmax.stride(0), kmax.stride(1)
+    if keys is not None:
+        desc.keys, desc.values = keys.data_ptr(), values.data_ptr()
+        desc.arc_stride_kv, desc.arc_stride_n = keys.stride(0), keys.stride(1)
+    return desc
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+
+
+def select_pages(q: torch.Tensor, kmax: torch.Tensor, kmin: torch.Tensor, n_arch: int, page: int, budget: int,
+                 scores: torch.Tensor | None = None) -> torch.Tensor:
+    """Top pages per (query group, key head): q [nq,t,h,128]; kmax/kmin [KV,P,128] bf16 over
+    the archive's n_arch tokens (complete pages n_arch // page are candidates). Returns int32
+    [nq, KV, min(budget, n_arch // page)], ascending; ties go to the lowest page. ``scores``
+    (fp32 [nq,KV,n_arch // page]) receives the page scores when given."""
+    _require(kmax, "kmax")
+    _require(kmin, "kmin")
+    nq = q.shape[0]
+    kv = kmax.shape[0]
+    k = min(budget, n_arch // page)
+    pages = torch.empty(nq, kv, k, dtype=torch.int32, device=q.device)
+    desc = _desc(q, page, n_arch, budget, kmax=kmax, kmin=kmin, pages=pages, scores=scores)
+    ws = _workspace(LIB.pbk_quest_select_workspace(desc), q.device)
+    with torch.cuda.device(q.device):
+        check(LIB.pbk_quest_select(desc, ws.data_ptr(), ws.numel(), _stream(q)), "pbk_quest_select")
+    return pages
+
+
+def attend_pages(q: torch.Tensor, qpos: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, n_arch: int,
+                 page: int, pages: torch.Tensor, win_keys: torch.Tensor, win_values: torch.Tensor,
+                 kpos: torch.Tensor, window: int, sinks: int = 0, scale: float | None = None,
+                 out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Exact attention of q [nq,t,h,128] (positions qpos [nq,t] int32) over, per key head,
+    the selected pages [nq,KV,k] of keys/values [KV,N,128], the archive's partial tail and
+    the window keys win_keys/win_values [KV,S,128] at positions kpos [S] int32 under the
+    reference's window mask. Returns [nq,t,h,128]."""
+    for t_, w in ((keys, "keys"), (values, "values"), (win_keys, "win_keys"), (win_values, "win_values")):
+        _require(t_, w)
+    nq, t, h, d = q.shape
+    out = torch.empty(nq, t, h, d, dtype=out_dtype, device=q.device)
+    desc = _desc(q, page, n_arch, pages.shape[-1], keys=keys, values=values, pages=pages)
+    desc.n_win, desc.window, desc.sinks = win_keys.shape[1], window, sinks
+    desc.scale = float(d ** -0.5 if scale is None else scale)
+    desc.qpos, desc.kpos = qpos.data_ptr(), kpos.data_ptr()
+    desc.win_keys, desc.win_values = win_keys.data_ptr(), win_values.data_ptr()
+    desc.win_stride_kv, desc.win_stride_n = win_keys.stride(0), win_keys.stride(1)
+    desc.out = out.data_ptr()
+    desc.out_stride_n, desc.out_stride_t, desc.out_stride_h = out.stride(0), out.stride(1), out.stride(2)
+    desc.out_dtype = _capi.PBK_BF16 if out_dtype == torch.bfloat16 else _capi.PBK_F32
+    if qpos.dtype != torch.int32 or kpos.dtype != torch.int32:
+        raise TypeError("qpos and kpos must be int32")
+    if pages.shape[:2] != (nq, keys.shape[0]) or pages.dtype != torch.int32 or not pages.is_contiguous():
+        raise ValueError("pages must be contiguous int32 [nq, KV, k]")
+    if pages.shape[-1] > n_arch // page:
+        raise ValueError("more selected pages than complete archive pages")
+    ws = _workspace(LIB.pbk_quest_attend_workspace(desc), q.device)
+    with torch.cuda.device(q.device):
+        check(LIB.pbk_quest_attend(desc, ws.data_ptr(), ws.numel(), _stream(q)), "pbk_quest_attend")
+    return out
+
+
+def gather_pages(keys: torch.Tensor, values: torch.Tensor, n_arch: int, page: int, pages: torch.Tensor,
+                 q: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Keys/values of `pages` [nq,KV,sel] followed by the partial tail: [nq,KV,sel*page+tail,128]."""
+    nq, kv, sel = pages.shape
+    if pages.dtype != torch.int32 or not pages.is_contiguous() or q.shape[0] != nq:
+        raise ValueError("pages must be contiguous int32 [nq, KV, sel] with nq query groups")
+    rows = sel * page + n_arch % page
+    ok = torch.empty(nq, kv, rows, keys.shape[-1], dtype=keys.dtype, device=keys.device)
+    ov = torch.empty_like(ok)
+    desc = _desc(q, page, n_arch, sel, keys=keys, values=values, pages=pages)
+    with torch.cuda.device(keys.device):
+        check(LIB.pbk_quest_gather(desc, sel, ok.data_ptr(), ov.data_ptr(), _stream(keys)), "pbk_quest_gather")
+    return ok, ov
+
+
+def _budget(t: int) -> tuple[int, bool]:
+    is_decode = t <= 64
+    budget = (EXACT_MEMORY["decode_blocks"] if (is_decode and EXACT_MEMORY["decode_blocks"])
+              else EXACT_MEMORY["blocks"])
+    return budget, is_decode
+
+
+def _check_flat(archive: Archive, full: int, k: int, is_decode: bool) -> None:
+    sblk = int(EXACT_MEMORY.get("superblock", 64) or 0)
+    rerank = int(EXACT_MEMORY.get("decode_rerank", 0) if is_decode else EXACT_MEMORY.get("rerank", 0))
+    if is_decode and rerank <= k and sblk > 1 and full > sblk * 16:
+        raise NotImplementedError("two-level super-block selection is not built; set EXACT_MEMORY['superblock']=0")
+    if rerank > k:
+        raise NotImplementedError("exact rerank is not built; set EXACT_MEMORY['rerank']=0")
+
+
+def retrieve(archive: Archive | None, q: torch.Tensor, groups: int) -> tuple[torch.Tensor, torch.Tensor] | None:
+    """Top pages per key head for query chunk q [B,H,T,hd]: (keys, values) [B,KV,R,hd] or None
+    (reference: exact_memory.py:88-152, flat mode; ``prompt_top`` and ``neighbors`` behave as
+    there)."""
+    if archive is None or archive.length == 0:
+        return None
+    page = EXACT_MEMORY["block_size"]
+    b, h, t, d = q.shape
+    full = archive.length // page
+    out_k, out_v = [], []
+    budget, is_decode = _budget(t)
+    k = min(budget, full)
+    if full:
+        _check_flat(archive, full, k, is_decode)
+    qs = q.to(torch.bfloat16)
+    tops = []
+    for i in range(b):
+        qi = qs[i].transpose(0, 1).unsqueeze(0)  # [1, T, H, hd] view
+        top = (select_pages(qi, archive.kmax[i], archive.kmin[i], archive.length, page, budget)[0]
+               if full else torch.empty(h // groups, 0, dtype=torch.int32, device=q.device))
+        tops.append(top)
+    top = torch.stack(tops).long()
+    if full:
+        if not is_decode:
+            archive.prompt_top = top
+        elif archive.prompt_top is not None:
+            top = torch.cat((archive.prompt_top.clamp(max=full - 1), top), dim=-1)
+        if EXACT_MEMORY["neighbors"]:
+            top = torch.cat([top] + [(top + j).clamp(max=full - 1) for j in range(1, EXACT_MEMORY["neighbors"] + 1)],
+                            dim=-1)
+        top = top.sort(-1).values
+    top32 = top.to(torch.int32).contiguous()
+    for i in range(b):
+        qi = qs[i].transpose(0, 1).unsqueeze(0)
+        ok, ov = gather_pages(archive.keys[i], archive.values[i], archive.length, page, top32[i:i + 1], qi)
+        out_k.append(ok[0])
+        out_v.append(ov[0])
+    return torch.stack(out_k), torch.stack(out_v)
+
+
+def retrieve_attend(archive: Archive, q: torch.Tensor, groups: int, win_keys: torch.Tensor,
+                    win_values: torch.Tensor, qpos: torch.Tensor, kpos: torch.Tensor, window: int,
+                    sinks: int = 0, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Fused retrieve + exact attention for one archive: q [1,H,T,hd] at positions qpos [T];
+    window cache win_keys/win_values [1,KV,S,hd] at positions kpos [S]. Equals
+    SDPA(q, [retrieve(archive, q) ; window], mask) of transplant.py:612-628 (decode budget,
+    flat mode, no prompt_top). Returns [1,H,T,hd]."""
+    page = EXACT_MEMORY["block_size"]
+    b, h, t, d = q.shape
+    if b != 1:
+        raise ValueError("retrieve_attend takes one archive (B=1)")
+    budget, is_decode = _budget(t)
+    full = archive.length // page
+    if full:
+        _check_flat(archive, full, min(budget, full), is_decode)
+    qi = q.to(torch.bfloat16)[0].transpose(0, 1).unsqueeze(0)
+    pages = select_pages(qi, archive.kmax[0], archive.kmin[0], archive.length, page, budget)
+    out = attend_pages(qi, qpos.to(torch.int32).view(1, t), archive.keys[0], archive.values[0], archive.length, page,
+                       pages, win_keys[0], win_values[0], kpos.to(torch.int32), window, sinks, out_dtype=out_dtype)
+    return out[0].transpose(0, 1).unsqueeze(0)
