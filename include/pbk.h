@@ -47,6 +47,7 @@ extern "C" {
 #define PBK_ERR_LAUNCH (-6)    /* the CUDA launch failed */
 #define PBK_ERR_TIMEOUT (-7)   /* a bounded device-side wait gave up */
 #define PBK_ERR_WORKSPACE (-8) /* workspace missing or too small */
+#define PBK_ERR_TOO_LARGE (-9) /* problem exceeds the fixed scratch of pbk_quest_select_noalloc */
 
 /* dtype codes */
 #define PBK_F32 0
@@ -155,6 +156,27 @@ PBK_API size_t pbk_quest_attend_workspace(const pbk_quest_desc* desc);
  * of sum_d max(q_d kmax_pd, q_d kmin_pd) in fp32, keep the k highest (ties to the
  * lowest page index) and write them to desc->pages in ascending order. */
 PBK_API int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Largest number of page scores (nq * kv * (n_arch / page)) pbk_quest_select_noalloc
+ * can hold: 4,194,304 fp32 = 16 MiB, enough for 8 query groups x 8 key heads over a
+ * 1M-token archive in 16-token pages. */
+#define PBK_QUEST_NOALLOC_MAX_SCORES 4194304
+
+/* pbk_quest_select for callers that cannot allocate device memory. This entry point has
+ * no counterpart in the reference. Some hosts own all device memory themselves (a serving
+ * engine that has reserved the free HBM for its KV cache, or a foreign-language caller
+ * with no handle on the framework's allocator): for them a workspace allocation fails or
+ * stalls the device. This variant takes no workspace: the page scores go to a fixed
+ * 16 MiB array that libpbk places in device memory (every GPU that loads the library
+ * holds it until the process exits), unless desc->scores is given, which is then used
+ * instead. It calls no allocator. Problems with more than PBK_QUEST_NOALLOC_MAX_SCORES
+ * scores return PBK_ERR_TOO_LARGE and launch nothing. The first call on a device looks up
+ * the array's device address (once per device, with that device current); make that
+ * first call before any stream capture. All calls share the one array: calls that overlap
+ * on the GPU (two streams at once) race on it, so serialise them. Nothing in the array
+ * needs to start at zero: each call overwrites every score it reads. Results equal
+ * pbk_quest_select's. */
+PBK_API int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream);
 
 /* Exact softmax attention of every query row over [selected pages ; partial tail ;
  * window keys] with the window mask (pseudobrain/transplant.py:619-628), as a

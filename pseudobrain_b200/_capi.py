@@ -14,6 +14,8 @@ from . import build as _build
 PBK_ABI_VERSION = 1
 PBK_OK = 0
 PBK_ERR_TIMEOUT = -7
+PBK_ERR_TOO_LARGE = -9
+PBK_QUEST_NOALLOC_MAX_SCORES = 4194304
 PBK_F32, PBK_BF16 = 0, 1
 PBK_STATE_KV, PBK_STATE_VK = 0, 1
 
@@ -64,6 +66,7 @@ SIGNATURES = {
     "pbk_quest_select_workspace": (ctypes.c_size_t, [_QD]),
     "pbk_quest_attend_workspace": (ctypes.c_size_t, [_QD]),
     "pbk_quest_select": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
+    "pbk_quest_select_noalloc": (ctypes.c_int, [_QD, _VP]),
     "pbk_quest_attend": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_gather": (ctypes.c_int, [_QD, _I32, _VP, _VP, _VP]),
     "pbk_quest_bounds": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I64, _I64, _VP, _VP, _I64, _I64, _I32, _VP]),

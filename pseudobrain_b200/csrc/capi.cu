@@ -101,6 +101,7 @@ const char* pbk_status_string(int status) {
     case PBK_ERR_LAUNCH: return "CUDA launch failed";
     case PBK_ERR_TIMEOUT: return "device-side wait timed out";
     case PBK_ERR_WORKSPACE: return "workspace missing or too small";
+    case PBK_ERR_TOO_LARGE: return "problem exceeds the fixed scratch of the no-allocation entry point";
     default: return "unknown status";
   }
 }
@@ -163,6 +164,17 @@ int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspa
   if ((st = check_current_device()) != PBK_OK) return st;
   float* scores = desc->scores ? desc->scores : static_cast<float*>(workspace);
   return pbk::launch_quest_select(*desc, scores, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
+                                                                                                   : PBK_ERR_LAUNCH;
+}
+
+int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream) {
+  int st = validate_quest(desc, 1);
+  if (st != PBK_OK) return st;
+  const int64_t nscores = (int64_t)desc->nq * desc->kv * (desc->n_arch / desc->page);
+  if (desc->scores == nullptr && nscores > PBK_QUEST_NOALLOC_MAX_SCORES) return PBK_ERR_TOO_LARGE;
+  if (desc->nq == 0) return PBK_OK;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return pbk::launch_quest_select_noalloc(*desc, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
                                                                                                    : PBK_ERR_LAUNCH;
 }
 

@@ -2,6 +2,7 @@
 // selection, page gather and split-key exact attention (flat mode of
 // pseudobrain/exact_memory.py:43-152 and the attention of pseudobrain/transplant.py:612-628).
 #include <cfloat>
+#include <mutex>
 
 #include "common.cuh"
 #include "quest.cuh"
@@ -421,6 +422,38 @@ cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStre
       d, npages, scores);
   quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, 0, st>>>(scores, npages, k, d.pages);
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------
+// Scratch of pbk_quest_select_noalloc: a fixed array in device memory, so the entry point
+// needs no allocation. Host code must not use the symbol's name as a device address; its
+// address is looked up once per device (that device current) with cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------------
+static __device__ __align__(256) float g_noalloc_scores[PBK_QUEST_NOALLOC_MAX_SCORES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st) {
+  float* scores = d.scores;
+  if (scores == nullptr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scores);
+      if (e != cudaSuccess) return e;
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    scores = g_noalloc_ptr[dev];
+  }
+  return launch_quest_select(d, scores, st);
 }
 
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st) {
