@@ -89,6 +89,11 @@ PBK_API int pbk_abi_version(void);
 PBK_API const char* pbk_status_string(int status);
 /* PBK_OK when `device` is an sm_100 (B200-class) GPU. */
 PBK_API int pbk_device_check(int device);
+/* Reads (and with clear != 0 resets) the current device's error word, which the
+ * tensor-core kernels set to a nonzero code when a bounded device-side wait gives up
+ * (the PBK_ERR_TIMEOUT condition; the code names the wait). Synchronises with the
+ * device: a diagnostic, not for hot paths. */
+PBK_API int pbk_device_error(int* code, int clear);
 
 /* Gated delta rule over few tokens per sequence with the state held in registers:
  * the recurrence of delta_rule_sequential, pseudobrain/gated_deltanet.py:93-107,

@@ -61,6 +61,7 @@ SIGNATURES = {
     "pbk_abi_version": (ctypes.c_int, []),
     "pbk_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "pbk_device_check": (ctypes.c_int, [ctypes.c_int]),
+    "pbk_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "pbk_gdn_decode": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
     "pbk_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
     "pbk_quest_select_workspace": (ctypes.c_size_t, [_QD]),
@@ -99,3 +100,11 @@ class PbkError(RuntimeError):
 def check(status: int, what: str) -> None:
     if status != PBK_OK:
         raise PbkError(status, what)
+
+
+def device_error(clear: bool = True) -> int:
+    """The current device's error word (nonzero: a tensor-core kernel's bounded wait gave
+    up; the code names the wait site). Synchronises with the device."""
+    code = ctypes.c_int(0)
+    check(LIB.pbk_device_error(ctypes.byref(code), int(clear)), "pbk_device_error")
+    return code.value

@@ -412,14 +412,20 @@ size_t quest_partial_bytes(const pbk_quest_desc& d) {
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStream_t st) {
   const int npages = d.n_arch / d.page, k = quest_k(d);
   if (npages == 0 || k == 0) return cudaSuccess;
-  const int rows = d.nq * d.t * (d.h / d.kv);
-  const size_t smem = (size_t)rows * kD * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(quest_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (quest_score_tc_supported(d)) {
+    // Up to 64 query rows per key head: tensor-core scores (tcgen05, TMA-fed).
+    cudaError_t e = launch_quest_score_tc(d, scores, st);
     if (e != cudaSuccess) return e;
+  } else {
+    const int rows = d.nq * d.t * (d.h / d.kv);
+    const size_t smem = (size_t)rows * kD * sizeof(float);
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(quest_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    quest_score_kernel<<<dim3((npages + kScoreThreads - 1) / kScoreThreads, d.kv), kScoreThreads, smem, st>>>(
+        d, npages, scores);
   }
-  quest_score_kernel<<<dim3((npages + kScoreThreads - 1) / kScoreThreads, d.kv), kScoreThreads, smem, st>>>(
-      d, npages, scores);
   quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, 0, st>>>(scores, npages, k, d.pages);
   return cudaGetLastError();
 }

@@ -12,6 +12,8 @@ int quest_splits(const pbk_quest_desc& d);
 size_t quest_score_bytes(const pbk_quest_desc& d);
 size_t quest_partial_bytes(const pbk_quest_desc& d);
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStream_t st);
+bool quest_score_tc_supported(const pbk_quest_desc& d);
+cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, cudaStream_t st);
 cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st);
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st);
 cudaError_t launch_quest_gather(const pbk_quest_desc& d, int sel, void* ok, void* ov, cudaStream_t st);

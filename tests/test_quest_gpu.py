@@ -122,6 +122,8 @@ def test_select_and_attend_match_oracle(cuda_device, kv, heads, n_arch, page, nq
     np.testing.assert_allclose(scores.cpu().numpy(), scores_ref, rtol=2e-6, atol=1e-4)
     for i, p in enumerate(planted):
         assert np.all((pages[i] == int(p)).any(-1).cpu().numpy())
+    from pseudobrain_b200._capi import device_error
+    assert device_error() == 0  # no bounded device-side wait gave up
     # attention over [pages ; tail ; window]
     qpos = (np.full((nq, t), n_arch + n_win - 1) - np.arange(t)[::-1][None]).astype(np.int32)
     kpos = np.arange(n_arch, n_arch + n_win, dtype=np.int32)
