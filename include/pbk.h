@@ -171,16 +171,16 @@ PBK_API int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t
  * no counterpart in the reference. Some hosts own all device memory themselves (a serving
  * engine that has reserved the free HBM for its KV cache, or a foreign-language caller
  * with no handle on the framework's allocator): for them a workspace allocation fails or
- * stalls the device. This variant takes no workspace: the page scores go to a fixed
- * 16 MiB array that libpbk places in device memory (every GPU that loads the library
- * holds it until the process exits), unless desc->scores is given, which is then used
- * instead. It calls no allocator. Problems with more than PBK_QUEST_NOALLOC_MAX_SCORES
- * scores return PBK_ERR_TOO_LARGE and launch nothing. The first call on a device looks up
- * the array's device address (once per device, with that device current); make that
- * first call before any stream capture. All calls share the one array: calls that overlap
- * on the GPU (two streams at once) race on it, so serialise them. Nothing in the array
- * needs to start at zero: each call overwrites every score it reads. Results equal
- * pbk_quest_select's. */
+ * stalls the device. This variant takes no workspace: the page scores and their per-32-
+ * page maxima go to a fixed 16.5 MiB array that libpbk places in device memory (every GPU
+ * that loads the library holds it until the process exits); when desc->scores is given,
+ * the scores go there instead. It calls no allocator. Problems with more than
+ * PBK_QUEST_NOALLOC_MAX_SCORES scores return PBK_ERR_TOO_LARGE and launch nothing. The
+ * first call on a device looks up the array's device address (once per device, with that
+ * device current); make that first call before any stream capture. All calls share the
+ * one array: calls that overlap on the GPU (two streams at once) race on it, so serialise
+ * them. Nothing in the array needs to start at zero: each call overwrites every value it
+ * reads. Results equal pbk_quest_select's. */
 PBK_API int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream);
 
 /* Exact softmax attention of every query row over [selected pages ; partial tail ;

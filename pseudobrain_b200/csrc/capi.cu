@@ -8,6 +8,8 @@
 namespace pbk {
 cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st);
+bool gdn_prefill_tc_supported(const pbk_gdn_desc& d);
+cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st);
 }
 
 namespace {
@@ -141,8 +143,12 @@ int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
   if (st != PBK_OK) return st;
   if (desc->batch == 0) return PBK_OK;
   if ((st = check_current_device()) != PBK_OK) return st;
-  return pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
-                                                                                               : PBK_ERR_LAUNCH;
+  // bf16 inputs: tensor-core kernel (bf16 operands, fp32 state and accumulation);
+  // fp32 inputs: the exact fp32 kernel.
+  const cudaError_t e = pbk::gdn_prefill_tc_supported(*desc)
+                            ? pbk::launch_gdn_prefill_tc(*desc, static_cast<cudaStream_t>(stream))
+                            : pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PBK_OK : PBK_ERR_LAUNCH;
 }
 
 size_t pbk_quest_select_workspace(const pbk_quest_desc* desc) {
@@ -162,9 +168,11 @@ int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspa
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return PBK_ERR_WORKSPACE;
   if (desc->nq == 0) return PBK_OK;
   if ((st = check_current_device()) != PBK_OK) return st;
-  float* scores = desc->scores ? desc->scores : static_cast<float*>(workspace);
-  return pbk::launch_quest_select(*desc, scores, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
-                                                                                                   : PBK_ERR_LAUNCH;
+  // workspace: the page scores (unless desc->scores keeps them), then the segment maxima
+  return pbk::launch_quest_select(*desc, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? PBK_OK
+             : PBK_ERR_LAUNCH;
 }
 
 int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream) {
@@ -172,6 +180,7 @@ int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream) {
   if (st != PBK_OK) return st;
   const int64_t nscores = (int64_t)desc->nq * desc->kv * (desc->n_arch / desc->page);
   if (desc->scores == nullptr && nscores > PBK_QUEST_NOALLOC_MAX_SCORES) return PBK_ERR_TOO_LARGE;
+  if (pbk::quest_select_floats(*desc) > pbk::kNoAllocFloats) return PBK_ERR_TOO_LARGE;
   if (desc->nq == 0) return PBK_OK;
   if ((st = check_current_device()) != PBK_OK) return st;
   return pbk::launch_quest_select_noalloc(*desc, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK

@@ -61,7 +61,8 @@ __global__ void quest_bounds_kernel(const bf16* keys, int n, int page, int64_t k
 constexpr int kScoreThreads = 128;
 constexpr int kRowBlock = 4;
 
-__global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_quest_desc d, int npages, float* scores) {
+__global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_quest_desc d, int npages, float* scores,
+                                                                   float* segmax, int nseg) {
   extern __shared__ __align__(16) float qs[];  // [rows of one key head][kD]
   const int h = blockIdx.y, groups = d.h / d.kv, rows_per_group = d.t * groups;
   const int rows = d.nq * rows_per_group;
@@ -74,9 +75,10 @@ __global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_qu
   }
   __syncthreads();
   const int p = blockIdx.x * kScoreThreads + threadIdx.x;
-  if (p >= npages) return;
-  const bf16* bmax = reinterpret_cast<const bf16*>(d.kmax) + h * d.bnd_stride_kv + (int64_t)p * d.bnd_stride_p;
-  const bf16* bmin = reinterpret_cast<const bf16*>(d.kmin) + h * d.bnd_stride_kv + (int64_t)p * d.bnd_stride_p;
+  const bool valid = p < npages;
+  const int pc = valid ? p : npages - 1;  // invalid lanes compute on a valid page, then drop it
+  const bf16* bmax = reinterpret_cast<const bf16*>(d.kmax) + h * d.bnd_stride_kv + (int64_t)pc * d.bnd_stride_p;
+  const bf16* bmin = reinterpret_cast<const bf16*>(d.kmin) + h * d.bnd_stride_kv + (int64_t)pc * d.bnd_stride_p;
   for (int n = 0; n < d.nq; ++n) {
     float best = -INFINITY;
     for (int r0 = 0; r0 < rows_per_group; r0 += kRowBlock) {
@@ -102,7 +104,13 @@ __global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_qu
       for (int r = 0; r < kRowBlock; ++r)
         if (r < nr) best = fmaxf(best, acc[r]);
     }
-    scores[((int64_t)n * d.kv + h) * npages + p] = best;
+    if (valid) scores[((int64_t)n * d.kv + h) * npages + p] = best;
+    if (segmax != nullptr) {  // max over this warp's 32 consecutive pages
+      float m = valid ? best : -INFINITY;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if ((threadIdx.x & 31) == 0 && (p >> 5) < nseg) segmax[((int64_t)n * d.kv + h) * nseg + (p >> 5)] = m;
+    }
   }
 }
 
@@ -113,6 +121,7 @@ __global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_qu
 // to the lowest indices).
 // ---------------------------------------------------------------------------------
 constexpr int kTopkThreads = 1024;
+constexpr int kSegMinPages = 1024;  // rows this long get segment maxima and the candidate path
 
 __device__ __forceinline__ uint32_t ordered_key(float f) {
   const uint32_t u = __float_as_uint(f);
@@ -147,52 +156,85 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* to
   return base + x - v;
 }
 
-__global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* scores, int npages, int k,
-                                                                  int32_t* pages) {
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t sh_prefix, sh_kk;
-  __shared__ int scan_scratch[kTopkThreads / 32 + 1];
-  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
-  const float* s = scores + (int64_t)row * npages;
-  int32_t* out = pages + (int64_t)row * k;
-  uint32_t prefix = 0, mask = 0, kk = (uint32_t)k;
+// Radix select over n keys key_of(i): the k-th largest key (`prefix` on return) and how
+// many elements equal to it belong to the top k (`kk`). Four 8-bit digits; warp-aggregated
+// shared-memory histograms; warp 0 finds each digit's bin with a suffix scan.
+struct SelectSmem {
+  uint32_t hist[256];
+  uint32_t prefix, kk;
+};
+
+template <typename KeyOf>
+__device__ __forceinline__ void radix_select(KeyOf key_of, int n, uint32_t k, SelectSmem& ss, uint32_t& prefix_out,
+                                             uint32_t& kk_out) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint32_t prefix = 0, mask = 0, kk = k;
   for (int digit = 3; digit >= 0; --digit) {
     const int shift = digit * 8;
-    if (tid < 256) hist[tid] = 0;
+    if (tid < 256) ss.hist[tid] = 0;
     __syncthreads();
-    for (int base = 0; base < npages; base += kTopkThreads) {
+    for (int base = 0; base < n; base += kTopkThreads) {
       const int i = base + tid;
       uint32_t bin = 0xFFFFFFFFu;
-      if (i < npages) {
-        const uint32_t u = ordered_key(s[i]);
+      if (i < n) {
+        const uint32_t u = key_of(i);
         if ((u & mask) == prefix) bin = (u >> shift) & 255u;
       }
       const uint32_t same = __match_any_sync(0xffffffffu, bin);
-      if (bin != 0xFFFFFFFFu && lane == __ffs(same) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(same));
+      if (bin != 0xFFFFFFFFu && lane == __ffs(same) - 1) atomicAdd(&ss.hist[bin], (uint32_t)__popc(same));
     }
     __syncthreads();
-    if (tid == 0) {
-      uint32_t above = 0;
-      int b = 255;
-      for (; b > 0; --b) {
-        if (above + hist[b] >= kk) break;
-        above += hist[b];
+    if (tid < 32) {
+      // lane l owns bins 255-8l down to 248-8l; suffix sums run from the top bin down
+      const int hi = 255 - 8 * lane;
+      uint32_t own = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) own += ss.hist[hi - j];
+      uint32_t incl = own;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
       }
-      sh_prefix = prefix | ((uint32_t)b << shift);
-      sh_kk = kk - above;
+      const uint32_t excl = incl - own;
+      if (lane == 0) {  // default, overwritten below whenever the count reaches kk
+        ss.prefix = prefix;
+        ss.kk = kk;
+      }
+      __syncwarp();
+      if (excl < kk && kk <= incl) {
+        uint32_t above = excl;
+        int b = hi;
+        for (int j = 0; j < 8; ++j, --b) {
+          if (above + ss.hist[b] >= kk) break;
+          above += ss.hist[b];
+        }
+        ss.prefix = prefix | ((uint32_t)b << shift);
+        ss.kk = kk - above;
+      }
     }
     __syncthreads();
-    prefix = sh_prefix;
-    kk = sh_kk;
+    prefix = ss.prefix;
+    kk = ss.kk;
     mask |= 255u << shift;
     __syncthreads();
   }
-  // prefix is now the k-th largest key; kk of the elements equal to it are selected.
-  const int span = (npages + kTopkThreads - 1) / kTopkThreads;
-  const int lo = min(tid * span, npages), hi = min(lo + span, npages);
+  prefix_out = prefix;
+  kk_out = kk;
+}
+
+// Write the top-k of n elements given in ascending index order (key_of(i), idx_of(i)) to
+// out[0..k) in that order: every thread owns a contiguous range; two block scans give each
+// selected element its rank. Elements equal to the threshold are taken lowest index first.
+template <typename KeyOf, typename IdxOf>
+__device__ __forceinline__ void collect_in_order(KeyOf key_of, IdxOf idx_of, int n, uint32_t prefix, uint32_t kk,
+                                                 int* scan_scratch, int32_t* out) {
+  const int tid = threadIdx.x;
+  const int span = (n + kTopkThreads - 1) / kTopkThreads;
+  const int lo = min(tid * span, n), hi = min(lo + span, n);
   int n_gt = 0, n_eq = 0;
   for (int i = lo; i < hi; ++i) {
-    const uint32_t u = ordered_key(s[i]);
+    const uint32_t u = key_of(i);
     n_gt += u > prefix;
     n_eq += u == prefix;
   }
@@ -201,14 +243,64 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
   const int base_eq = block_exclusive_scan<kTopkThreads>(n_eq, scan_scratch, &tot);
   int pos = base_gt + min(base_eq, (int)kk), eq_seen = base_eq;
   for (int i = lo; i < hi; ++i) {
-    const uint32_t u = ordered_key(s[i]);
+    const uint32_t u = key_of(i);
     if (u > prefix) {
-      out[pos++] = i;
+      out[pos++] = idx_of(i);
     } else if (u == prefix) {
-      if (eq_seen < (int)kk) out[pos++] = i;
+      if (eq_seen < (int)kk) out[pos++] = idx_of(i);
       ++eq_seen;
     }
   }
+}
+
+constexpr int kCandCap = 4096;  // candidates held in shared memory
+
+// One CTA per (group, key head) row of scores. With segment maxima (the max of every 32
+// consecutive pages), the k-th largest segment maximum tau bounds the k-th largest page
+// score from below (the top k segments hold k distinct pages scoring >= tau), so the top k
+// are among the pages scoring >= tau: one counting pass and one writing pass collect them
+// in index order into shared memory, and the exact selection runs there. When there are
+// too few segments or too many candidates, the selection runs over the whole row.
+__global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* scores, const float* segmax, int npages,
+                                                                  int nseg, int k, int32_t* pages) {
+  __shared__ SelectSmem ss;
+  __shared__ int scan_scratch[kTopkThreads / 32 + 1];
+  __shared__ uint32_t cand_key[kCandCap];
+  __shared__ int32_t cand_idx[kCandCap];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const float* s = scores + (int64_t)row * npages;
+  int32_t* out = pages + (int64_t)row * k;
+  uint32_t prefix, kk;
+  if (segmax != nullptr && nseg >= k) {
+    const float* sg = segmax + (int64_t)row * nseg;
+    uint32_t tau, unused;
+    radix_select([&](int i) { return ordered_key(sg[i]); }, nseg, (uint32_t)k, ss, tau, unused);
+    // count candidates (key >= tau) over contiguous per-thread ranges, then place them
+    const int span = (npages + kTopkThreads - 1) / kTopkThreads;
+    const int lo = min(tid * span, npages), hi = min(lo + span, npages);
+    int cnt = 0;
+    for (int i = lo; i < hi; ++i) cnt += ordered_key(s[i]) >= tau;
+    int total;
+    int pos = block_exclusive_scan<kTopkThreads>(cnt, scan_scratch, &total);
+    if (total <= kCandCap) {
+      for (int i = lo; i < hi; ++i) {
+        const uint32_t u = ordered_key(s[i]);
+        if (u >= tau) {
+          cand_key[pos] = u;
+          cand_idx[pos] = i;
+          ++pos;
+        }
+      }
+      __syncthreads();
+      radix_select([&](int i) { return cand_key[i]; }, total, (uint32_t)k, ss, prefix, kk);
+      collect_in_order([&](int i) { return cand_key[i]; }, [&](int i) { return cand_idx[i]; }, total, prefix, kk,
+                       scan_scratch, out);
+      return;
+    }
+  }
+  radix_select([&](int i) { return ordered_key(s[i]); }, npages, (uint32_t)k, ss, prefix, kk);
+  collect_in_order([&](int i) { return ordered_key(s[i]); }, [&](int i) { return i; }, npages, prefix, kk,
+                   scan_scratch, out);
 }
 
 // ---------------------------------------------------------------------------------
@@ -402,19 +494,31 @@ int quest_splits(const pbk_quest_desc& d) {
   const int n_all = quest_k(d) * d.page + (d.n_arch % d.page) + d.n_win;
   return (n_all + kSplitKeys - 1) / kSplitKeys;
 }
-size_t quest_score_bytes(const pbk_quest_desc& d) {
-  return d.scores ? 0 : (size_t)d.nq * d.kv * (d.n_arch / d.page) * sizeof(float);
+// Segment maxima are kept for rows of at least kSegMinPages pages (ceil(pages / 32) each).
+int quest_nseg(const pbk_quest_desc& d) {
+  const int npages = d.n_arch / d.page;
+  return npages >= kSegMinPages ? (npages + 31) / 32 : 0;
 }
+// Scratch of one select call, in floats: the scores (unless the caller keeps them in
+// desc.scores), then the segment maxima.
+size_t quest_select_floats(const pbk_quest_desc& d) {
+  const size_t rows = (size_t)d.nq * d.kv;
+  return (d.scores ? 0 : rows * (d.n_arch / d.page)) + rows * quest_nseg(d);
+}
+size_t quest_score_bytes(const pbk_quest_desc& d) { return quest_select_floats(d) * sizeof(float); }
 size_t quest_partial_bytes(const pbk_quest_desc& d) {
   return (size_t)d.nq * d.t * d.h * quest_splits(d) * (kD + 2) * sizeof(float);
 }
 
-cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStream_t st) {
+cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st) {
   const int npages = d.n_arch / d.page, k = quest_k(d);
   if (npages == 0 || k == 0) return cudaSuccess;
+  float* scores = d.scores ? d.scores : scratch;
+  const int nseg = quest_nseg(d);
+  float* segmax = nseg ? scratch + (d.scores ? 0 : (size_t)d.nq * d.kv * npages) : nullptr;
   if (quest_score_tc_supported(d)) {
     // Up to 64 query rows per key head: tensor-core scores (tcgen05, TMA-fed).
-    cudaError_t e = launch_quest_score_tc(d, scores, st);
+    cudaError_t e = launch_quest_score_tc(d, scores, segmax, nseg, st);
     if (e != cudaSuccess) return e;
   } else {
     const int rows = d.nq * d.t * (d.h / d.kv);
@@ -424,9 +528,9 @@ cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStre
       if (e != cudaSuccess) return e;
     }
     quest_score_kernel<<<dim3((npages + kScoreThreads - 1) / kScoreThreads, d.kv), kScoreThreads, smem, st>>>(
-        d, npages, scores);
+        d, npages, scores, segmax, nseg);
   }
-  quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, 0, st>>>(scores, npages, k, d.pages);
+  quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, 0, st>>>(scores, segmax, npages, nseg, k, d.pages);
   return cudaGetLastError();
 }
 
@@ -435,7 +539,7 @@ cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStre
 // needs no allocation. Host code must not use the symbol's name as a device address; its
 // address is looked up once per device (that device current) with cudaGetSymbolAddress.
 // ---------------------------------------------------------------------------------
-static __device__ __align__(256) float g_noalloc_scores[PBK_QUEST_NOALLOC_MAX_SCORES];
+static __device__ __align__(256) float g_noalloc_scores[kNoAllocFloats];
 
 namespace {
 constexpr int kMaxDevices = 64;
@@ -444,8 +548,8 @@ float* g_noalloc_ptr[kMaxDevices] = {};
 }  // namespace
 
 cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st) {
-  float* scores = d.scores;
-  if (scores == nullptr) {
+  float* scratch = nullptr;  // page scores (unless desc.scores is given) and segment maxima
+  {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -457,9 +561,9 @@ cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st
       if (e != cudaSuccess) return e;
       g_noalloc_ptr[dev] = static_cast<float*>(p);
     }
-    scores = g_noalloc_ptr[dev];
+    scratch = g_noalloc_ptr[dev];
   }
-  return launch_quest_select(d, scores, st);
+  return launch_quest_select(d, scratch, st);
 }
 
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st) {

@@ -10,10 +10,15 @@ namespace pbk {
 int quest_k(const pbk_quest_desc& d);
 int quest_splits(const pbk_quest_desc& d);
 size_t quest_score_bytes(const pbk_quest_desc& d);
+size_t quest_select_floats(const pbk_quest_desc& d);
+// Floats of the fixed scratch of pbk_quest_select_noalloc: the largest allowed score count
+// plus its segment maxima (rows of at least 1024 pages keep ceil(pages / 32) of them).
+constexpr size_t kNoAllocFloats = (size_t)PBK_QUEST_NOALLOC_MAX_SCORES + PBK_QUEST_NOALLOC_MAX_SCORES / 32 +
+                                  PBK_QUEST_NOALLOC_MAX_SCORES / 1024;
 size_t quest_partial_bytes(const pbk_quest_desc& d);
-cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scores, cudaStream_t st);
+cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st);
 bool quest_score_tc_supported(const pbk_quest_desc& d);
-cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, cudaStream_t st);
+cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float* segmax, int nseg, cudaStream_t st);
 cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st);
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st);
 cudaError_t launch_quest_gather(const pbk_quest_desc& d, int sel, void* ok, void* ov, cudaStream_t st);

@@ -46,6 +46,8 @@ struct ScoreArgs {
   const bf16* q;
   int64_t q_stride_n, q_stride_t, q_stride_h;
   float* scores;
+  float* segmax;  // max of every 32 consecutive pages per (group, key head), or null
+  int nseg;
   int* err;
   int nq, t, groups, kv, npages, rows, n_pad, tiles_per_kv, total_tiles;
 };
@@ -200,13 +202,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.acc_empty[acc]);
       const int p = p0 + quad * 32 + lane;
-      if (p < args.npages) {
-        for (int n = 0; n < args.nq; ++n) {
-          float best = -INFINITY;
+      const bool valid = p < args.npages;
+      for (int n = 0; n < args.nq; ++n) {
+        float best = -INFINITY;
 #pragma unroll
-          for (int r = 0; r < kMaxRows; ++r)
-            if (r >= n * rpg && r < (n + 1) * rpg) best = fmaxf(best, __uint_as_float(v[r]));
-          args.scores[((int64_t)n * args.kv + kvh) * args.npages + p] = best;
+        for (int r = 0; r < kMaxRows; ++r)
+          if (r >= n * rpg && r < (n + 1) * rpg) best = fmaxf(best, __uint_as_float(v[r]));
+        if (valid) args.scores[((int64_t)n * args.kv + kvh) * args.npages + p] = best;
+        if (args.segmax != nullptr) {  // this warp's 32 pages form one segment
+          float m = valid ? best : -INFINITY;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0 && (p >> 5) < args.nseg) args.segmax[((int64_t)n * args.kv + kvh) * args.nseg + (p >> 5)] = m;
         }
       }
     }
@@ -228,7 +235,7 @@ bool quest_score_tc_supported(const pbk_quest_desc& d) {
   return rows <= kMaxRows && d.n_arch / d.page > 0;
 }
 
-cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, cudaStream_t st) {
+cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float* segmax, int nseg, cudaStream_t st) {
   const int npages = d.n_arch / d.page;
   CUtensorMap tmax, tmin;
   const uint64_t dims[3] = {128, (uint64_t)npages, (uint64_t)d.kv};
@@ -243,6 +250,8 @@ cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, cudaSt
   a.q_stride_t = d.q_stride_t;
   a.q_stride_h = d.q_stride_h;
   a.scores = scores;
+  a.segmax = segmax;
+  a.nseg = nseg;
   a.err = device_error_word();
   a.nq = d.nq;
   a.t = d.t;

@@ -63,8 +63,10 @@ def test_prefill_fp32_matches_oracle(cuda_device, batch, length, hk, hv, std):
     assert ogdn.rel_err(s.cpu().numpy(), rs) < TOL_FP32
 
 
-@pytest.mark.parametrize("batch,length,hk,hv", [(1, 300, 1, 2), (2, 1024, 2, 4)])
+@pytest.mark.parametrize("batch,length,hk,hv", [(1, 300, 1, 2), (2, 1024, 2, 4), (1, 64, 1, 1), (3, 1, 1, 2),
+                                                (1, 130, 2, 2), (2, 4096, 1, 2)])
 def test_prefill_bf16_matches_oracle(cuda_device, batch, length, hk, hv):
+    """bf16 inputs run the tensor-core kernel (bf16 operands, fp32 state and accumulation)."""
     from pseudobrain_b200.gdn_prefill import gdn_prefill
     inp = gdn_inputs(5 * length + hv, batch, length, hk, hv, bf16=True, state_std=0.02)
     d = to_device(inp, cuda_device)
@@ -114,3 +116,78 @@ def test_prefill_in_place_vk_layout_with_slots(cuda_device):
         assert ogdn.rel_err(pool[slot].transpose(-1, -2).cpu().numpy(), rs[b]) < TOL_FP32
         assert ogdn.rel_err(o[b].cpu().numpy(), ro[b]) < TOL_FP32
     assert torch.all(o[1] == 0) and torch.all(pool[1] == 0) and torch.all(pool[3] == 0)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_prefill_tc_vk_layout_slots_in_place(cuda_device, out_dtype):
+    """Tensor-core kernel with vLLM's pool layout [slots,Hv,V,K], state_indices with a
+    padding slot, in-place state update."""
+    from pseudobrain_b200.gdn_prefill import gdn_prefill_
+    inp = gdn_inputs(31, 3, 200, 1, 2, bf16=True, state_std=0.02)
+    d = to_device(inp, cuda_device)
+    idx = torch.tensor([2, -1, 0], dtype=torch.int32, device=cuda_device)
+    pool = torch.zeros(4, 2, 128, 128, device=cuda_device)
+    pool[2], pool[0] = d["h0"][0].transpose(-1, -2), d["h0"][2].transpose(-1, -2)
+    o = torch.zeros(3, 200, 2, 128, device=cuda_device, dtype=out_dtype)
+    gdn_prefill_(d["q"], d["k"], d["v"], d["g"], d["beta"], pool, pool, o, inp["scale"], idx, 1)
+    ro, rs = _oracle(inp)
+    for b, slot in ((0, 2), (2, 0)):
+        assert ogdn.rel_err(pool[slot].transpose(-1, -2).cpu().numpy(), rs[b]) < TOL_BF16
+        assert ogdn.rel_err(o[b].float().cpu().numpy(), ro[b]) < TOL_BF16
+    assert torch.all(o[1] == 0) and torch.all(pool[1] == 0) and torch.all(pool[3] == 0)
+    from pseudobrain_b200._capi import device_error
+    assert device_error() == 0
+
+
+def test_prefill_tc_strided_packed_inputs(cuda_device):
+    """q, k, v as strided views into one packed [B, T, 2*Hk*128 + Hv*128] buffer (vLLM's
+    mixed_qkv layout): the tensor maps take the strides, no copies."""
+    from pseudobrain_b200.gdn_prefill import gdn_prefill
+    inp = gdn_inputs(32, 2, 333, 2, 4, bf16=True, state_std=0.02)
+    d = to_device(inp, cuda_device)
+    b, t = 2, 333
+    packed = torch.cat((d["q"].reshape(b, t, -1), d["k"].reshape(b, t, -1), d["v"].reshape(b, t, -1)), dim=-1)
+    q = packed[..., :256].view(b, t, 2, 128)
+    k = packed[..., 256:512].view(b, t, 2, 128)
+    v = packed[..., 512:].view(b, t, 4, 128)
+    assert not q.is_contiguous()
+    o, s = gdn_prefill(q, k, v, d["g"], d["beta"], inp["scale"], d["h0"])
+    ro, rs = _oracle(inp)
+    assert ogdn.rel_err(o.cpu().numpy(), ro) < TOL_BF16
+    assert ogdn.rel_err(s.cpu().numpy(), rs) < TOL_BF16
+
+
+def test_prefill_tc_split_equals_whole(cuda_device):
+    """Chunked == full on the tensor-core kernel: two calls carrying the state equal one."""
+    from pseudobrain_b200.gdn_prefill import gdn_prefill
+    inp = gdn_inputs(33, 2, 512, 1, 2, bf16=True, state_std=0.02)
+    d = to_device(inp, cuda_device)
+    args = [d[n] for n in ("q", "k", "v", "g", "beta")]
+    o, s = gdn_prefill(*args, inp["scale"], d["h0"])
+    o1, s1 = gdn_prefill(*(a[:, :192] for a in args), inp["scale"], d["h0"])
+    o2, s2 = gdn_prefill(*(a[:, 192:] for a in args), inp["scale"], s1)
+    assert ogdn.rel_err(torch.cat((o1, o2), 1).cpu().numpy(), o.cpu().numpy()) < TOL_BF16
+    assert ogdn.rel_err(s2.cpu().numpy(), s.cpu().numpy()) < TOL_BF16
+
+
+def test_prefill_config1_tc_matches_exact_kernel(cuda_device):
+    """BASELINE config 1 at full size (B=4, T=32768, 16 key / 32 value heads): the
+    tensor-core kernel against the exact fp32 kernel on the same bf16 inputs (fp32 copies),
+    plus the first 2048 tokens of one sequence against the oracle."""
+    from pseudobrain_b200.gdn_prefill import gdn_prefill
+    from pseudobrain_b200.synthetic import gdn_inputs as dev_inputs
+    x = dev_inputs(4, 32768, 16, 32, device=cuda_device, seed=1)
+    o, s = gdn_prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], x["scale"], None, torch.bfloat16)
+    o32, s32 = gdn_prefill(x["q"].float(), x["k"].float(), x["v"].float(), x["g"], x["beta"].float(), x["scale"],
+                           None)
+    for bb in range(4):
+        assert ogdn.rel_err(o[bb].float().cpu().numpy(), o32[bb].cpu().numpy()) < TOL_BF16
+        assert ogdn.rel_err(s[bb].cpu().numpy(), s32[bb].cpu().numpy()) < TOL_BF16
+    sl = slice(0, 2048)
+    q, k = (ogdn.expand_key_heads(x[n][1:2, sl].float().cpu().numpy(), 32) for n in ("q", "k"))
+    ro, _ = ogdn.delta_rule_chunked(q, k, x["v"][1:2, sl].float().cpu().numpy(), x["g"][1:2, sl].cpu().numpy(),
+                                    x["beta"][1:2, sl].float().cpu().numpy(), x["scale"],
+                                    np.zeros((1, 32, 128, 128), np.float32))
+    assert ogdn.rel_err(o[1:2, sl].float().cpu().numpy(), ro) < TOL_BF16
+    from pseudobrain_b200._capi import device_error
+    assert device_error() == 0
