@@ -7,23 +7,25 @@
 //   W = T diag(beta gamma) K,  U' = T diag(beta) V
 //   U = U' - W S;  O = diag(gamma scale) Q S + (scale Q K^T * D) U;  S <- gamma_C S + (diag(e) K)^T U
 // Every product is one M=128 tcgen05.mma chain with the value dim (or the stacked K|Q
-// rows) as M, so TMEM lane j of the CTA's 128 threads is "column j":
+// rows) as M, so TMEM lane j is "column j" for the warpgroup that reads it:
 //   [K;Q] K^T  -> TMEM D1 (lanes 0-63 K K^T rows, 64-127 Q K^T rows)       K = dk
 //   W^T  = K^T (T diag(beta gamma))^T -> TMEM D1        (A MN-major)      K = i
-//   U'^T = V^T (T diag(beta))^T       -> TMEM UP        (A MN-major)      K = i
+//   U'^T = V^T (T diag(beta))^T       -> TMEM UP[n&1]   (A MN-major)      K = i
 //   (WS)^T = S^T W^T -> TMEM WS;  (QS)^T = S^T Q^T -> TMEM QS               K = dk
 //   (UM)^T = U^T M^T -> TMEM UM;  S^T += U^T (diag(e) K) -> TMEM S           K = i
-// S^T (fp32, 128 TMEM columns) is loaded from h0 once, scaled by gamma_C through the
-// register file each chunk (which also writes its bf16 copy, the A operand of the S
-// products) and accumulated by the last MMA; it goes back to HBM once at the end.
 //
-// One CTA (128 threads, thread j <-> TMEM lane j) per (sequence, value head) chain walks
-// its chunks in order; thread 0 issues TMA loads and MMAs. The chunk-local preparation of
-// chunk n+1 (K K^T, the inverse, W, U') is interleaved with the tensor-core work of chunk
-// n. q/k/v arrive by 4-D TMA ([B,T,H,128] with any strides; rows past T are zero-filled,
-// the reference's identity padding); no multicast. Every mbarrier wait is bounded: on
-// timeout the kernel records an error code, waits (bounded) for its own loads and MMAs,
-// frees its TMEM and returns.
+// One CTA per (sequence, value head) chain, warp-specialised:
+//   warps 0-3 (serial): state step of chunk n -- S^T to bf16 and S^T *= gamma_C through
+//     the registers, then U = U' - WS, then the outputs; their thread 0 issues the S MMAs.
+//   warps 4-7 (prep): chunk n+1's scalars, K K^T, A and M, the inverse (16x16 diagonal
+//     blocks by substitution, off-diagonal blocks by tf32 mma.sync products), then W^T and
+//     U'^T; their thread 0 issues the prep MMAs.
+//   warp 8 (producer): TMA loads of K|Q and V (4-D maps over [B,T,H,128], any strides,
+//     rows past T zero-filled = the reference's identity padding; no multicast), and the
+//     TMEM allocation.
+// The roles meet on mbarriers; every wait is bounded: on timeout the kernel records an
+// error code, stops issuing, waits (bounded) for its own loads and MMAs, frees its TMEM
+// and returns.
 #include "common.cuh"
 #include "tc.cuh"
 #include "tma_host.h"
@@ -34,26 +36,27 @@ namespace {
 using bf16 = __nv_bfloat16;
 constexpr int C = 64;
 constexpr int D = 128;
-constexpr int NT = 128;
-constexpr int PA = C + 4;  // fp32 row stride of A: 16-byte rows, conflict-free float4 row writes
+constexpr int NT = 288;    // 2 warpgroups + producer warp
+constexpr int PA = C + 4;  // fp32 row stride of A (16-byte rows)
 
 // TMEM columns
-constexpr uint32_t kColS = 0, kColD1 = 128, kColUP = 192, kColWS = 256, kColQS = 320, kColUM = 384;
+constexpr uint32_t kColS = 0, kColD1 = 128, kColUP = 192, kColWS = 320, kColQS = 384, kColUM = 448;
 constexpr uint32_t kTmemCols = 512;
 
 struct __align__(1024) PrefillSmem {
   uint8_t kq[2][2][16384];   // [buf][dk atom][rows 0-63 K, 64-127 Q] x 64 bf16, SW128
   uint8_t v[2][8192];        // [dv atom][64 rows] x 64 bf16, SW128
   uint8_t st[2][16384];      // S^T bf16 [128 dv rows] x [dk atom] (A operand, K-major)
-  uint8_t wt[16384];         // W^T bf16 [128 dk rows x 64 t] (B operand, MN-major)
-  uint8_t m[2][8192];        // M bf16 [64 t x 64 i] (B operand, K-major)
-  uint8_t tb[8192];          // T diag(beta) bf16 [64 t x 64 i]
+  uint8_t wt[2][16384];      // [buf] W^T bf16 [128 dk rows x 64 t] (B, MN-major); also T scratch
+  uint8_t m[2][8192];        // [buf] M bf16 [64 t x 64 i] (B operand, K-major)
+  uint8_t tb[8192];          // T diag(beta) bf16 [64 t x 64 i]; also mma.sync scratch
   uint8_t tbg[8192];         // T diag(beta gamma) bf16 [64 t x 64 i]
-  uint8_t ut[16384];         // U^T bf16 [128 dv rows x 64 t] (A operand, K-major)
+  uint8_t ut[16384];         // U^T bf16 [128 dv rows x 64 t] (A operand); also output staging
   float a[C * PA];           // A fp32
-  float cum[2][C], cum2[2][C], gam[2][C], ee[2][C], beta[2][C];
-  uint64_t bar_kq[2], bar_v, bar_p1, bar_p3, bar_ws, bar_o, bar_s, bar_drain;
+  float cum[3][C], cum2[3][C], gam[3][C], ee[3][C], beta[3][C];
+  uint64_t bar_kq[2], bar_v, bar_p1, bar_p3, bar_ws, bar_s, prep_ready, drain_s, drain_p;
   uint32_t tmem_base;
+  volatile int abort;
 };
 
 struct PrefillArgs {
@@ -93,17 +96,74 @@ __device__ __forceinline__ void store_row_bf16(uint8_t* tile, int row, const flo
   }
 }
 
-// 64 TMEM columns of this thread's lane into v[64].
+// 64 TMEM columns of this thread's lane into v[64] (two loads in flight, one wait).
 __device__ __forceinline__ void tmem_row64(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  tc::tmem_ld_32x32(taddr, r);
+  uint32_t r0[32], r1[32];
+  tc::tmem_ld_32x32(taddr, r0);
+  tc::tmem_ld_32x32(taddr + 32, r1);
   tc::tmem_ld_wait();
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-  tc::tmem_ld_32x32(taddr + 32, r);
-  tc::tmem_ld_wait();
+  for (int i = 0; i < 32; ++i) {
+    v[i] = __uint_as_float(r0[i]);
+    v[32 + i] = __uint_as_float(r1[i]);
+  }
+}
+
+// Named barrier over one warpgroup (id 1: serial, 2: prep), and its AND-reduction.
+__device__ __forceinline__ void wg_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+__device__ __forceinline__ bool wg_and(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
+// fp32 T scratch (64 x 64) with an XOR swizzle that keeps the mma.sync fragment loads
+// conflict-free: element (r, c) at r * 64 + (c ^ ((r & 3) << 3)).
+__device__ __forceinline__ int tidx(int r, int c) { return r * 64 + (c ^ ((r & 3) << 3)); }
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+// acc (a 16x16 block as two m16n8 tiles) += X (16x16) * Y (16x16); x(r, c), y(r, c) read
+// the operands. Fragment layout of m16n8k8 tf32: groupID g = lane / 4, t = lane % 4.
+template <typename FX, typename FY>
+__device__ __forceinline__ void block_mma(float (&acc)[2][4], FX x, FY y, int lane) {
+  const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
+  for (int k0 = 0; k0 < 16; k0 += 8) {
+    const uint32_t a[4] = {to_tf32(x(g, k0 + t)), to_tf32(x(g + 8, k0 + t)), to_tf32(x(g, k0 + t + 4)),
+                           to_tf32(x(g + 8, k0 + t + 4))};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const uint32_t b[2] = {to_tf32(y(k0 + t, 8 * nt + g)), to_tf32(y(k0 + t + 4, 8 * nt + g))};
+      mma_tf32(acc[nt], a, b);
+    }
+  }
+}
+// Store acc (scaled by s) through st(r, c, value).
+template <typename FS>
+__device__ __forceinline__ void block_store(const float (&acc)[2][4], float s, FS st, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    st(g, 8 * nt + 2 * t, s * acc[nt][0]);
+    st(g, 8 * nt + 2 * t + 1, s * acc[nt][1]);
+    st(g + 8, 8 * nt + 2 * t, s * acc[nt][2]);
+    st(g + 8, 8 * nt + 2 * t + 1, s * acc[nt][3]);
+  }
 }
 
 template <typename TOut>
@@ -112,7 +172,7 @@ __global__ void __launch_bounds__(NT, 1)
                           const __grid_constant__ CUtensorMap tm_v, const PrefillArgs p) {
   extern __shared__ uint8_t smem_raw[];
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.x / p.hv, h = blockIdx.x % p.hv;
   const int hk = h / (p.hv / p.hk);
   int64_t slot = b;
@@ -129,15 +189,14 @@ __global__ void __launch_bounds__(NT, 1)
     tc::mbar_init(&sm.bar_p1, 1);
     tc::mbar_init(&sm.bar_p3, 1);
     tc::mbar_init(&sm.bar_ws, 1);
-    tc::mbar_init(&sm.bar_o, 1);
     tc::mbar_init(&sm.bar_s, 1);
-    tc::mbar_init(&sm.bar_drain, 1);
+    tc::mbar_init(&sm.prep_ready, 128);
+    tc::mbar_init(&sm.drain_s, 1);
+    tc::mbar_init(&sm.drain_p, 1);
+    sm.abort = 0;
     tc::fence_barrier_init();
-    tc::prefetch_tmap(&tm_q);
-    tc::prefetch_tmap(&tm_k);
-    tc::prefetch_tmap(&tm_v);
   }
-  if (warp == 0) {
+  if (warp == 8) {
     tc::tmem_alloc(&sm.tmem_base, kTmemCols);
     tc::tmem_relinquish();
   }
@@ -145,381 +204,428 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);  // this thread's TMEM lane (row tid)
-
-  // ------------------------------------------------------------ helpers
-  auto issue_kq = [&](int n) {
-    const int buf = n & 1;
-    tc::mbar_expect_tx(&sm.bar_kq[buf], 4 * 8192);
-    for (int a = 0; a < 2; ++a) {
-      tc::tma_load_4d(sm.kq[buf][a], &tm_k, &sm.bar_kq[buf], 64 * a, n * C, hk, b);
-      tc::tma_load_4d(sm.kq[buf][a] + 8192, &tm_q, &sm.bar_kq[buf], 64 * a, n * C, hk, b);
-    }
-  };
-  auto issue_v = [&](int n) {
-    tc::mbar_expect_tx(&sm.bar_v, 2 * 8192);
-    for (int a = 0; a < 2; ++a) tc::tma_load_4d(sm.v[a], &tm_v, &sm.bar_v, 64 * a, n * C, h, b);
-  };
-  // Chunk scalars: cumulative log decay, gamma, e, beta (identity steps past the end).
-  auto load_scalars = [&](int n) {
-    const int buf = n & 1;
-    if (tid < C) {
-      const int t = n * C + tid;
-      float gv = 0.f, bv = 0.f;
-      if (t < p.seqlen) {
-        gv = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
-        bv = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
-      }
-      float x = gv;  // inclusive scan over the 64 steps: warp scan, then carry
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, x, o);
-        if ((tid & 31) >= o) x += y;
-      }
-      sm.cum[buf][tid] = x;
-      sm.beta[buf][tid] = bv;
-    }
-    __syncthreads();
-    if (tid >= 32 && tid < C) sm.cum[buf][tid] += sm.cum[buf][31];
-    __syncthreads();
-    if (tid < C) {
-      const float c = sm.cum[buf][tid];
-      sm.gam[buf][tid] = expf(c);
-      sm.ee[buf][tid] = expf(sm.cum[buf][C - 1] - c);
-      sm.cum2[buf][tid] = c * 1.4426950408889634f;  // log2(e) c, for exp2 of differences
-    }
-  };
-
-  int failed = 0;
-  // Bounded wait by every thread; the outcome is made uniform across the CTA.
-  auto wait_all = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
-    const bool ok = tc::mbar_wait(bar, parity);
-    if (!__syncthreads_and(ok)) {
-      if (tid == 0 && p.err) atomicCAS(p.err, 0, 200 + site);
-      failed = 1;
-      return false;
-    }
-    tc::fence_after_sync();
-    return true;
-  };
-  // Last chunk whose K/Q (per buffer) and V load thread 0 issued, for a bounded drain on
-  // failure. Barrier parities follow from chunk indices: buffer n&1 holds the (n>>1)-th
-  // load of that buffer; V, P1 and P3 of chunk n are their barriers' n-th completions.
-  int last_kq[2] = {-1, -1}, last_v = -1;
+  const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // TMEM lane of row (tid % 128)
 
   const uint32_t i_kk = tc::idesc_bf16_f32(128, 64, false, false);   // A K-major, B K-major, N=64
   const uint32_t i_kmn = tc::idesc_bf16_f32(128, 64, false, true);   // A K-major, B MN-major, N=64
   const uint32_t i_mnk = tc::idesc_bf16_f32(128, 64, true, false);   // A MN-major, B K-major, N=64
   const uint32_t i_s = tc::idesc_bf16_f32(128, 128, false, true);    // S update, N=128
 
-  // Prep MMAs of chunk n (thread 0): [K;Q] K^T -> D1.
-  auto mma_p1 = [&](int n) {
-    const int buf = n & 1;
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint32_t base = tc::smem_u32(sm.kq[buf][kk >> 2]) + (kk & 3) * 32;
-      tc::mma_f16(tmem + kColD1, tc::sdesc_sw128(base, 16, 1024), tc::sdesc_sw128(base, 16, 1024), i_kk, kk != 0);
-    }
-    tc::mma_commit(&sm.bar_p1);
-  };
-  // W^T = K^T TBG^T -> D1;  U'^T = V^T TB^T -> UP.
-  auto mma_p3 = [&](int n) {
-    const int buf = n & 1;
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][0]) + kk * 2048, 16384, 1024);
-      const uint64_t bd = tc::sdesc_sw128(tc::smem_u32(sm.tbg) + kk * 32, 16, 1024);
-      tc::mma_f16(tmem + kColD1, ad, bd, i_mnk, kk != 0);
-    }
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.v[0]) + kk * 2048, 8192, 1024);
-      const uint64_t bd = tc::sdesc_sw128(tc::smem_u32(sm.tb) + kk * 32, 16, 1024);
-      tc::mma_f16(tmem + kColUP, ad, bd, i_mnk, kk != 0);
-    }
-    tc::mma_commit(&sm.bar_p3);
-  };
-
-  // P1 epilogue of chunk n: A (fp32) from K K^T rows, M (bf16) from Q K^T rows.
-  auto p1_epilogue = [&](int n) {
-    const int buf = n & 1;
-    float v[64];
-    tmem_row64(lane_addr + kColD1, v);
-    const float* c2 = sm.cum2[buf];
-    if (tid < C) {
-      const int t = tid;
-      const float bt = sm.beta[buf][t], ct = c2[t];
-#pragma unroll
-      for (int i = 0; i < C; i += 4) {
-        float4 w;
-        w.x = i + 0 < t ? bt * v[i + 0] * exp2f(ct - c2[i + 0]) : 0.f;
-        w.y = i + 1 < t ? bt * v[i + 1] * exp2f(ct - c2[i + 1]) : 0.f;
-        w.z = i + 2 < t ? bt * v[i + 2] * exp2f(ct - c2[i + 2]) : 0.f;
-        w.w = i + 3 < t ? bt * v[i + 3] * exp2f(ct - c2[i + 3]) : 0.f;
-        *reinterpret_cast<float4*>(&sm.a[t * PA + i]) = w;
-      }
-    } else {
-      const int t = tid - C;
-      const float ct = c2[t];
-#pragma unroll
-      for (int i = 0; i < C; ++i) v[i] = i <= t ? p.scale * v[i] * exp2f(ct - c2[i]) : 0.f;
-      store_row_bf16(sm.m[buf], t, v);
-    }
-  };
-
-  // T = (I + A)^-1 by forward substitution, one column of T per thread in registers
-  // (threads 0..63; rows of A are shared-memory broadcasts): x_i = -sum_{m<i} A_im x_m
-  // for i > col, x_col = 1, x_i = 0 above. Then TB = T diag(beta), TBG = T diag(beta gamma)
-  // as bf16 [t][i] tiles.
-  auto inverse = [&](int n) {
-    const int buf = n & 1;
-    if (tid < C) {
-      const int col = tid;
-      float x[C];
-#pragma unroll
-      for (int i = 0; i < C; ++i) {
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int m = 0; m + 3 < i; m += 4) {
-          const float4 a4 = *reinterpret_cast<const float4*>(&sm.a[i * PA + m]);
-          s0 = fmaf(a4.x, x[m], s0);
-          s1 = fmaf(a4.y, x[m + 1], s1);
-          s0 = fmaf(a4.z, x[m + 2], s0);
-          s1 = fmaf(a4.w, x[m + 3], s1);
+  if (warp == 8) {
+    // ================================================================ producer
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_q);
+      tc::prefetch_tmap(&tm_k);
+      tc::prefetch_tmap(&tm_v);
+      int last_kq[2] = {-1, -1}, last_v = -1;
+      for (int m = 0; m < nchunks && !sm.abort; ++m) {
+        // K|Q of chunk m reuse the buffer of chunk m-2: its state update must be done.
+        if (m >= 2 && !tc::mbar_wait(&sm.bar_s, (m - 2) & 1)) {
+          if (p.err) atomicCAS(p.err, 0, 301);
+          sm.abort = 1;
+          break;
         }
-#pragma unroll
-        for (int m = i & ~3; m < i; ++m) s0 = fmaf(sm.a[i * PA + m], x[m], s0);
-        x[i] = i < col ? 0.f : (i == col ? 1.f : -(s0 + s1));
+        const int buf = m & 1;
+        tc::mbar_expect_tx(&sm.bar_kq[buf], 4 * 8192);
+        for (int a = 0; a < 2; ++a) {
+          tc::tma_load_4d(sm.kq[buf][a], &tm_k, &sm.bar_kq[buf], 64 * a, m * C, hk, b);
+          tc::tma_load_4d(sm.kq[buf][a] + 8192, &tm_q, &sm.bar_kq[buf], 64 * a, m * C, hk, b);
+        }
+        last_kq[buf] = m;
+        // V of chunk m reuses the V buffer: the U' product of chunk m-1 must be done.
+        if (m >= 1 && !tc::mbar_wait(&sm.bar_p3, (m - 1) & 1)) {
+          if (p.err) atomicCAS(p.err, 0, 302);
+          sm.abort = 1;
+          break;
+        }
+        tc::mbar_expect_tx(&sm.bar_v, 2 * 8192);
+        for (int a = 0; a < 2; ++a) tc::tma_load_4d(sm.v[a], &tm_v, &sm.bar_v, 64 * a, m * C, h, b);
+        last_v = m;
       }
-      const float bc = sm.beta[buf][col], bgc = bc * sm.gam[buf][col];
-#pragma unroll
-      for (int t = 0; t < C; ++t) {
-        const uint32_t off = tc::sw128_offset(t, col);
-        *reinterpret_cast<bf16*>(sm.tb + off) = __float2bfloat16_rn(x[t] * bc);
-        *reinterpret_cast<bf16*>(sm.tbg + off) = __float2bfloat16_rn(x[t] * bgc);
-      }
+      // our loads in flight land before the CTA exits (bounded)
+      for (int bb = 0; bb < 2; ++bb)
+        if (last_kq[bb] >= 0) tc::mbar_wait(&sm.bar_kq[bb], (last_kq[bb] >> 1) & 1, 200000000ull);
+      if (last_v >= 0) tc::mbar_wait(&sm.bar_v, last_v & 1, 200000000ull);
     }
-  };
-
-  // W^T (TMEM D1, lane = dk) -> wt smem; then scale the chunk's K rows by e_i in place
-  // (the K operand of the state update).
-  auto w_epilogue = [&](int n) {
-    const int buf = n & 1;
-    float v[64];
-    tmem_row64(lane_addr + kColD1, v);
-    store_row_bf16(sm.wt, tid, v);
-    const int i = tid >> 1, a = tid & 1;
-    const float e = sm.ee[buf][i];
-    uint8_t* row = sm.kq[buf][a] + i * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 w = *reinterpret_cast<uint4*>(row + 16 * c);
-      __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = __bfloat1622float2(h2[j]);
-        h2[j] = __floats2bfloat162_rn(f.x * e, f.y * e);
+  } else if (warp >= 4) {
+    // ================================================================ prep warpgroup
+    const int pt = tid - 128, pw = warp - 4;  // thread / warp within the group
+    bool ok = true;
+    auto fail = [&](int site) {
+      if (pt == 0) {
+        if (p.err) atomicCAS(p.err, 0, 200 + site);
+        sm.abort = 1;
       }
-      *reinterpret_cast<uint4*>(row + 16 * c) = w;
-    }
-  };
-
-  // ------------------------------------------------------------ state in
-  {
-    const float* h0 = p.h0 != nullptr ? p.h0 + slot * p.slot_stride + (int64_t)h * D * D : nullptr;
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      uint32_t r[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float x = 0.f;
-        if (h0 != nullptr) x = p.layout == PBK_STATE_KV ? h0[(c0 + i) * D + tid] : h0[tid * D + c0 + i];
-        r[i] = __float_as_uint(x);
+      ok = false;
+    };
+    // bounded wait by every prep thread, outcome uniform across the group
+    auto pwait = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
+      const bool got = wg_and(2, tc::mbar_wait(bar, parity) && !sm.abort);
+      if (!got) fail(site);
+      tc::fence_after_sync();
+      return got;
+    };
+    // g and beta of the next chunk are loaded one chunk ahead (registers).
+    float g_next = 0.f, b_next = 0.f;
+    auto fetch_scalars = [&](int m) {
+      g_next = b_next = 0.f;
+      const int t = m * C + pt;
+      if (pt < C && m < nchunks && t < p.seqlen) {
+        g_next = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
+        b_next = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
       }
-      tc::tmem_st_32x32(lane_addr + kColS + c0, r);
-    }
-    tc::tmem_st_wait();
-  }
-
-  // ------------------------------------------------------------ prologue: prep of chunk 0
-  if (tid == 0) {
-    issue_kq(0);
-    last_kq[0] = 0;
-    if (nchunks > 1) { issue_kq(1); last_kq[1] = 1; }
-    issue_v(0);
-    last_v = 0;
-  }
-  load_scalars(0);
-  if (wait_all(&sm.bar_kq[0], 0, 1)) {
-    if (tid == 0) mma_p1(0);
-  }
-  if (!failed && wait_all(&sm.bar_p1, 0, 2)) {
-    p1_epilogue(0);
-    __syncthreads();
-    inverse(0);
-    tc::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (wait_all(&sm.bar_v, 0, 3)) {
-      if (tid == 0) mma_p3(0);
-      if (wait_all(&sm.bar_p3, 0, 4)) {
-        w_epilogue(0);
-        tc::fence_proxy_async_smem();
-        tc::fence_before_sync();
-        __syncthreads();
-        if (tid == 0 && nchunks > 1) { issue_v(1); last_v = 1; }
-      }
-    }
-  }
-
-  // ------------------------------------------------------------ chunk loop
-  TOut* out = reinterpret_cast<TOut*>(p.o) + b * p.o_sb + h * p.o_sh + tid;
-  for (int n = 0; n < nchunks && !failed; ++n) {
-    const int buf = n & 1;
-    const uint32_t par = n & 1;
-    const bool more = n + 1 < nchunks;
-    // (1) S^T -> bf16 A operand; S^T *= gamma_C in TMEM
-    {
-      const float gl = sm.gam[buf][C - 1];
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t r[32];
-        tc::tmem_ld_32x32(lane_addr + kColS + c0, r);
-        tc::tmem_ld_wait();
-        float f[32];
+    };
+    fetch_scalars(0);
+    for (int m = 0; m < nchunks && ok; ++m) {
+      const int buf = m & 1, sb = m % 3;
+      // ---- scalars: cumulative log decay, gamma, e, beta
+      {
+        float x = g_next;
+        const float bv = b_next;
+        if (pt < C) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]);
-        uint8_t* tile = sm.st[c0 >> 6];
+          for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+          }
+          sm.cum[sb][pt] = x;
+          sm.beta[sb][pt] = bv;
+        }
+        fetch_scalars(m + 1);
+        wg_sync(2);
+        if (pt >= 32 && pt < C) sm.cum[sb][pt] += sm.cum[sb][31];
+        wg_sync(2);
+        if (pt < C) {
+          const float c = sm.cum[sb][pt];
+          sm.gam[sb][pt] = expf(c);
+          sm.ee[sb][pt] = expf(sm.cum[sb][C - 1] - c);
+          sm.cum2[sb][pt] = c * 1.4426950408889634f;
+        }
+      }
+      // ---- [K;Q] K^T
+      if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
+      if (pt == 0) {
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t base = tc::smem_u32(sm.kq[buf][kk >> 2]) + (kk & 3) * 32;
+          tc::mma_f16(tmem + kColD1, tc::sdesc_sw128(base, 16, 1024), tc::sdesc_sw128(base, 16, 1024), i_kk,
+                      kk != 0);
+        }
+        tc::mma_commit(&sm.bar_p1);
+      }
+      if (!pwait(&sm.bar_p1, m & 1, 2)) break;
+      // ---- A (fp32) from K K^T rows (lanes 0-63), M (bf16) from Q K^T rows (lanes 64-127)
+      {
+        float v[64];
+        tmem_row64(lane_addr + kColD1, v);
+        const float* c2 = sm.cum2[sb];
+        if (pt < C) {
+          const int t = pt;
+          const float bt = sm.beta[sb][t], ct = c2[t];
+          const int lim = pw == 0 ? 32 : 64;  // rows 0-31 have no terms past column 31
+#pragma unroll
+          for (int i = 0; i < C; i += 4) {
+            float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < lim) {
+              w.x = i + 0 < t ? bt * v[i + 0] * exp2f(ct - c2[i + 0]) : 0.f;
+              w.y = i + 1 < t ? bt * v[i + 1] * exp2f(ct - c2[i + 1]) : 0.f;
+              w.z = i + 2 < t ? bt * v[i + 2] * exp2f(ct - c2[i + 2]) : 0.f;
+              w.w = i + 3 < t ? bt * v[i + 3] * exp2f(ct - c2[i + 3]) : 0.f;
+            }
+            *reinterpret_cast<float4*>(&sm.a[t * PA + i]) = w;
+          }
+        } else {
+          const int t = pt - C;
+          const float ct = c2[t];
+          const int lim = pw == 2 ? 32 : 64;
+#pragma unroll
+          for (int i = 0; i < C; ++i) v[i] = (i < lim && i <= t) ? p.scale * v[i] * exp2f(ct - c2[i]) : 0.f;
+          store_row_bf16(sm.m[buf], t, v);
+        }
+      }
+      tc::fence_before_sync();
+      wg_sync(2);
+      // ---- T = (I + A)^-1, blocked: diagonal 16x16 blocks by forward substitution
+      float* ts = reinterpret_cast<float*>(sm.wt[buf]);  // fp32 T scratch (free: W^T(m-2) consumed)
+      {
+        const int blk = pw, col = lane & 15, r0 = 16 * blk;
+        float x[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float s = 0.f;
+#pragma unroll
+          for (int mm = 0; mm + 3 < i; mm += 4) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&sm.a[(r0 + i) * PA + r0 + mm]);
+            s = fmaf(a4.x, x[mm], s);
+            s = fmaf(a4.y, x[mm + 1], s);
+            s = fmaf(a4.z, x[mm + 2], s);
+            s = fmaf(a4.w, x[mm + 3], s);
+          }
+#pragma unroll
+          for (int mm = i & ~3; mm < i; ++mm) s = fmaf(sm.a[(r0 + i) * PA + r0 + mm], x[mm], s);
+          x[i] = i < col ? 0.f : (i == col ? 1.f : -s);
+        }
+        if (lane < 16) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) ts[tidx(r0 + i, r0 + col)] = x[i];
+        }
+      }
+      wg_sync(2);
+      // off-diagonal blocks, by distance: T_ij = -T_ii (sum_{k=j}^{i-1} A_ik T_kj)
+      {
+        float* scr = reinterpret_cast<float*>(sm.tb) + pw * (16 * 24);  // per-warp 16x16 (stride 24)
+        auto at = [&](int bi, int bj) {
+          return [=, &sm](int r, int c) { return sm.a[(16 * bi + r) * PA + 16 * bj + c]; };
+        };
+        auto tt = [&](int bi, int bj) { return [=](int r, int c) { return ts[tidx(16 * bi + r, 16 * bj + c)]; }; };
+        for (int dist = 1; dist < 4; ++dist) {
+          if (pw < 4 - dist) {
+            const int j = pw, i = pw + dist;
+            float acc[2][4] = {};
+            for (int k = j; k < i; ++k) block_mma(acc, at(i, k), tt(k, j), lane);
+            block_store(acc, 1.f, [&](int r, int c, float x) { scr[r * 24 + c] = x; }, lane);
+            __syncwarp();
+            float acc2[2][4] = {};
+            block_mma(acc2, tt(i, i), [&](int r, int c) { return scr[r * 24 + c]; }, lane);
+            block_store(acc2, -1.f, [&](int r, int c, float x) { ts[tidx(16 * i + r, 16 * j + c)] = x; }, lane);
+          }
+          wg_sync(2);
+        }
+      }
+      // ---- TB = T diag(beta), TBG = T diag(beta gamma), bf16 rows (zero above the blocks)
+      {
+        const int t = pt >> 1, half = pt & 1;
+        float vb[32], vbg[32];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int i = 32 * half + jj;
+          const float x = (i >> 4) <= (t >> 4) ? ts[tidx(t, i)] * sm.beta[sb][i] : 0.f;
+          vb[jj] = x;
+          vbg[jj] = x * sm.gam[sb][i];
+        }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint4 w;
-          w.x = pack_bf16x2(f[8 * c + 0], f[8 * c + 1]);
-          w.y = pack_bf16x2(f[8 * c + 2], f[8 * c + 3]);
-          w.z = pack_bf16x2(f[8 * c + 4], f[8 * c + 5]);
-          w.w = pack_bf16x2(f[8 * c + 6], f[8 * c + 7]);
-          *reinterpret_cast<uint4*>(tile + tc::sw128_offset(tid, (c0 & 63) + 8 * c)) = w;
+          uint4 w1, w2;
+          w1.x = pack_bf16x2(vb[8 * c], vb[8 * c + 1]);
+          w1.y = pack_bf16x2(vb[8 * c + 2], vb[8 * c + 3]);
+          w1.z = pack_bf16x2(vb[8 * c + 4], vb[8 * c + 5]);
+          w1.w = pack_bf16x2(vb[8 * c + 6], vb[8 * c + 7]);
+          w2.x = pack_bf16x2(vbg[8 * c], vbg[8 * c + 1]);
+          w2.y = pack_bf16x2(vbg[8 * c + 2], vbg[8 * c + 3]);
+          w2.z = pack_bf16x2(vbg[8 * c + 4], vbg[8 * c + 5]);
+          w2.w = pack_bf16x2(vbg[8 * c + 6], vbg[8 * c + 7]);
+          const uint32_t off = tc::sw128_offset(t, 32 * half + 8 * c);
+          *reinterpret_cast<uint4*>(sm.tb + off) = w1;  // the tb scratch reads ended at the last barrier
+          *reinterpret_cast<uint4*>(sm.tbg + off) = w2;
         }
+      }
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      // ---- W^T = K^T TBG^T -> D1; U'^T = V^T TB^T -> UP[buf]
+      if (!pwait(&sm.bar_v, m & 1, 3)) break;
+      if (pt == 0) {
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][0]) + kk * 2048, 16384, 1024);
+          const uint64_t bd = tc::sdesc_sw128(tc::smem_u32(sm.tbg) + kk * 32, 16, 1024);
+          tc::mma_f16(tmem + kColD1, ad, bd, i_mnk, kk != 0);
+        }
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.v[0]) + kk * 2048, 8192, 1024);
+          const uint64_t bd = tc::sdesc_sw128(tc::smem_u32(sm.tb) + kk * 32, 16, 1024);
+          tc::mma_f16(tmem + kColUP + 64 * buf, ad, bd, i_mnk, kk != 0);
+        }
+        tc::mma_commit(&sm.bar_p3);
+      }
+      if (!pwait(&sm.bar_p3, m & 1, 4)) break;
+      // ---- W^T -> wt[buf] (bf16, MN-major rows); K rows scaled by e_i (state-update operand)
+      {
+        float v[64];
+        tmem_row64(lane_addr + kColD1, v);
+        store_row_bf16(sm.wt[buf], pt, v);
+        const int i = pt >> 1, a = pt & 1;
+        const float e = sm.ee[sb][i];
+        uint8_t* row = sm.kq[buf][a] + i * 128;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(f[i] * gl);
+        for (int c = 0; c < 8; ++c) {
+          uint4 w = *reinterpret_cast<uint4*>(row + 16 * c);
+          __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const float2 f = __bfloat1622float2(h2[jj]);
+            h2[jj] = __floats2bfloat162_rn(f.x * e, f.y * e);
+          }
+          *reinterpret_cast<uint4*>(row + 16 * c) = w;
+        }
+      }
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      // The serial group must have taken chunk m-1 (its first MMA commit) before chunk m is
+      // announced, so the two phases of prep_ready never alias.
+      if (m >= 1 && !pwait(&sm.bar_ws, (m - 1) & 1, 5)) break;
+      tc::mbar_arrive(&sm.prep_ready);
+    }
+    if (pt == 0) {  // every MMA this thread issued completes before TMEM is freed
+      tc::mma_commit(&sm.drain_p);
+      tc::mbar_wait(&sm.drain_p, 0, 200000000ull);
+    }
+  } else {
+    // ================================================================ serial warpgroup
+    bool ok = true;
+    auto fail = [&](int site) {
+      if (tid == 0) {
+        if (p.err) atomicCAS(p.err, 0, 250 + site);
+        sm.abort = 1;
+      }
+      ok = false;
+    };
+    auto swait = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
+      const bool got = wg_and(1, tc::mbar_wait(bar, parity) && !sm.abort);
+      if (!got) fail(site);
+      tc::fence_after_sync();
+      return got;
+    };
+    // state in: S^T in TMEM, row = this thread's value column
+    {
+      const float* h0 = p.h0 != nullptr ? p.h0 + slot * p.slot_stride + (int64_t)h * D * D : nullptr;
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = 0.f;
+          if (h0 != nullptr) x = p.layout == PBK_STATE_KV ? h0[(c0 + i) * D + tid] : h0[tid * D + c0 + i];
+          r[i] = __float_as_uint(x);
+        }
         tc::tmem_st_32x32(lane_addr + kColS + c0, r);
       }
       tc::tmem_st_wait();
     }
-    tc::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    // (2) WS^T = S^T W^T, QS^T = S^T Q^T
-    if (tid == 0) {
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
-        const uint64_t bw = tc::sdesc_sw128(tc::smem_u32(sm.wt) + kk * 2048, 16, 1024);
-        tc::mma_f16(tmem + kColWS, ad, bw, i_kmn, kk != 0);
-      }
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
-        const uint64_t bq = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][kk >> 2]) + 8192 + (kk & 3) * 32, 16, 1024);
-        tc::mma_f16(tmem + kColQS, ad, bq, i_kk, kk != 0);
-      }
-      tc::mma_commit(&sm.bar_ws);
-    }
-    // (3) prep of chunk n+1, part 1: scalars and [K;Q] K^T
-    if (more) {
-      load_scalars(n + 1);
-      if (!wait_all(&sm.bar_kq[buf ^ 1], ((n + 1) >> 1) & 1, 5)) break;
-      if (tid == 0) mma_p1(n + 1);
-    }
-    // (4) U = U' - WS  ->  U^T bf16
-    if (!wait_all(&sm.bar_ws, par, 6)) break;
-    {
-      float ws[64], up[64];
-      tmem_row64(lane_addr + kColWS, ws);
-      tmem_row64(lane_addr + kColUP, up);
+    // S step of chunk n: S^T -> bf16 operand tile; S^T *= gamma_C in TMEM. Then the
+    // S products of chunk n (thread 0).
+    auto state_step = [&](int n) {
+      const int buf = n & 1, sb = n % 3;
+      const float gl = sm.gam[sb][C - 1];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) up[i] -= ws[i];
-      store_row_bf16(sm.ut, tid, up);
-    }
-    tc::fence_proxy_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    // (5) UM^T = U^T M^T;  S^T += U^T (diag(e) K)
-    if (tid == 0) {
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.ut) + kk * 32, 16, 1024);
-        const uint64_t bm = tc::sdesc_sw128(tc::smem_u32(sm.m[buf]) + kk * 32, 16, 1024);
-        tc::mma_f16(tmem + kColUM, ad, bm, i_kk, kk != 0);
+      for (int c0 = 0; c0 < D; c0 += 64) {
+        float f[64];
+        tmem_row64(lane_addr + kColS + c0, f);
+        uint8_t* tile = sm.st[c0 >> 6];
+        store_row_bf16(tile, tid, f);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t r[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(f[32 * half + i] * gl);
+          tc::tmem_st_32x32(lane_addr + kColS + c0 + 32 * half, r);
+        }
       }
-      tc::mma_commit(&sm.bar_o);
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.ut) + kk * 32, 16, 1024);
-        const uint64_t bk = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][0]) + kk * 2048, 16384, 1024);
-        tc::mma_f16(tmem + kColS, ad, bk, i_s, 1);
-      }
-      tc::mma_commit(&sm.bar_s);
-    }
-    // (6)-(8) prep of chunk n+1: A, M, inverse, W^T and U'^T
-    if (more) {
-      if (!wait_all(&sm.bar_p1, (n + 1) & 1, 7)) break;
-      p1_epilogue(n + 1);
-      __syncthreads();
-      inverse(n + 1);
+      tc::tmem_st_wait();
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
-      __syncthreads();
-      if (!wait_all(&sm.bar_v, (n + 1) & 1, 8)) break;
-      if (tid == 0) mma_p3(n + 1);
-    }
-    // (9) O = gamma scale QS + UM
-    if (!wait_all(&sm.bar_o, par, 9)) break;
-    {
-      float qs[64], um[64];
-      tmem_row64(lane_addr + kColQS, qs);
-      tmem_row64(lane_addr + kColUM, um);
+      wg_sync(1);
+      if (tid == 0) {
+        tc::fence_after_sync();
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bw = tc::sdesc_sw128(tc::smem_u32(sm.wt[buf]) + kk * 2048, 16, 1024);
+          tc::mma_f16(tmem + kColWS, ad, bw, i_kmn, kk != 0);
+        }
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bq =
+              tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][kk >> 2]) + 8192 + (kk & 3) * 32, 16, 1024);
+          tc::mma_f16(tmem + kColQS, ad, bq, i_kk, kk != 0);
+        }
+        tc::mma_commit(&sm.bar_ws);
+      }
+    };
+    TOut* out = reinterpret_cast<TOut*>(p.o) + b * p.o_sb + h * p.o_sh;
+    if (swait(&sm.prep_ready, 0, 1)) state_step(0);
+    for (int n = 0; n < nchunks && ok; ++n) {
+      const int buf = n & 1, sb = n % 3;
+      // U = U' - WS -> U^T bf16; then UM^T = U^T M^T and S^T += U^T (diag(e) K)
+      if (!swait(&sm.bar_ws, n & 1, 2)) break;
+      {
+        float ws[64], up[64];
+        tmem_row64(lane_addr + kColWS, ws);
+        tmem_row64(lane_addr + kColUP + 64 * buf, up);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) up[i] -= ws[i];
+        store_row_bf16(sm.ut, tid, up);
+      }
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      wg_sync(1);
+      if (tid == 0) {
+        tc::fence_after_sync();
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.ut) + kk * 32, 16, 1024);
+          const uint64_t bm = tc::sdesc_sw128(tc::smem_u32(sm.m[buf]) + kk * 32, 16, 1024);
+          tc::mma_f16(tmem + kColUM, ad, bm, i_kk, kk != 0);
+        }
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.ut) + kk * 32, 16, 1024);
+          const uint64_t bk = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][0]) + kk * 2048, 16384, 1024);
+          tc::mma_f16(tmem + kColS, ad, bk, i_s, 1);
+        }
+        tc::mma_commit(&sm.bar_s);
+      }
+      if (!swait(&sm.bar_s, n & 1, 3)) break;
+      // O = gamma scale QS + UM (registers), then the next chunk's state step, then the
+      // stores of O through shared memory (ut is free: U products are done).
+      float o[64];
+      {
+        float um[64];
+        tmem_row64(lane_addr + kColQS, o);
+        tmem_row64(lane_addr + kColUM, um);
+        const float* gm = sm.gam[sb];
+#pragma unroll
+        for (int t = 0; t < 64; ++t) o[t] = fmaf(gm[t] * p.scale, o[t], um[t]);
+      }
+      tc::fence_before_sync();
+      if (n + 1 < nchunks) {
+        if (!swait(&sm.prep_ready, (n + 1) & 1, 4)) break;
+        state_step(n + 1);
+      }
       const int tmax = min(C, p.seqlen - n * C);
-      const float* gm = sm.gam[buf];
-      TOut* oc = out + (int64_t)(n * C) * p.o_st;
+      constexpr int kPer = 16 / sizeof(TOut);           // elements per 16-byte vector
+      constexpr int kRows = sizeof(TOut) == 2 ? 64 : 32;  // t rows staged per pass (16 KB)
 #pragma unroll
-      for (int t = 0; t < C; ++t)
-        if (t < tmax) oc[(int64_t)t * p.o_st] = from_f32<TOut>(fmaf(gm[t] * p.scale, qs[t], um[t]));
-    }
-    // (10) W^T of chunk n+1 -> smem; K(n+1) rows scaled by e; next V load
-    if (more) {
-      if (!wait_all(&sm.bar_p3, (n + 1) & 1, 10)) break;
-      w_epilogue(n + 1);
-      tc::fence_proxy_async_smem();
-      tc::fence_before_sync();
-      __syncthreads();
-      if (tid == 0 && n + 2 < nchunks) { issue_v(n + 2); last_v = n + 2; }
-    }
-    // (11) state update done: the chunk's K/Q buffer is free for chunk n+2
-    if (!wait_all(&sm.bar_s, par, 11)) break;
-    if (tid == 0 && n + 2 < nchunks) { issue_kq(n + 2); last_kq[buf] = n + 2; }
-  }
-
-  if (failed) {
-    // ------------------------------------------------------------ bounded drain
-    if (tid == 0) {
-      // Our loads land in the order of their barriers' phases: wait for the last of each.
-      for (int bb = 0; bb < 2; ++bb)
-        if (last_kq[bb] >= 0) tc::mbar_wait(&sm.bar_kq[bb], (last_kq[bb] >> 1) & 1, 200000000ull);
-      if (last_v >= 0) tc::mbar_wait(&sm.bar_v, last_v & 1, 200000000ull);
-      // One more commit tracks every MMA this thread issued.
-      tc::mma_commit(&sm.bar_drain);
-      tc::mbar_wait(&sm.bar_drain, 0, 200000000ull);
-    }
-  } else {
-    // ------------------------------------------------------------ state out
-    float* st = p.state + slot * p.slot_stride + (int64_t)h * D * D;
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      uint32_t r[32];
-      tc::tmem_ld_32x32(lane_addr + kColS + c0, r);
-      tc::tmem_ld_wait();
+      for (int t0 = 0; t0 < 64; t0 += kRows) {
+        TOut* stage = reinterpret_cast<TOut*>(sm.ut);  // [kRows][128]: row t, column = this thread
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (p.layout == PBK_STATE_KV) st[(c0 + i) * D + tid] = __uint_as_float(r[i]);
-        else st[tid * D + c0 + i] = __uint_as_float(r[i]);
+        for (int t = 0; t < kRows; ++t) stage[t * D + tid] = from_f32<TOut>(o[t0 + t]);
+        wg_sync(1);
+        constexpr int kVecs = kRows * D / kPer;
+        for (int vi = tid; vi < kVecs; vi += 128) {
+          const int t = vi / (D / kPer), c = (vi % (D / kPer)) * kPer;
+          if (t0 + t < tmax)
+            *reinterpret_cast<uint4*>(out + (int64_t)(n * C + t0 + t) * p.o_st + c) =
+                *reinterpret_cast<const uint4*>(stage + t * D + c);
+        }
+        wg_sync(1);
+      }
+    }
+    if (tid == 0) {  // every MMA this thread issued completes before TMEM is freed
+      tc::mma_commit(&sm.drain_s);
+      tc::mbar_wait(&sm.drain_s, 0, 200000000ull);
+    }
+    if (ok) {
+      // state out
+      float* st = p.state + slot * p.slot_stride + (int64_t)h * D * D;
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t r[32];
+        tc::tmem_ld_32x32(lane_addr + kColS + c0, r);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (p.layout == PBK_STATE_KV) st[(c0 + i) * D + tid] = __uint_as_float(r[i]);
+          else st[tid * D + c0 + i] = __uint_as_float(r[i]);
+        }
       }
     }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 8) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
@@ -541,8 +647,13 @@ bool gdn_prefill_tc_supported(const pbk_gdn_desc& d) {
     return (reinterpret_cast<uintptr_t>(v.data) & 15) == 0 && v.stride_t % 8 == 0 && v.stride_h % 8 == 0 &&
            v.stride_b % 8 == 0 && v.stride_t > 0 && v.stride_h > 0 && v.stride_b > 0;
   };
+  // the output is written with 16-byte vectors along the value dim
+  const bool out_ok = (reinterpret_cast<uintptr_t>(d.o.data) & 15) == 0 &&
+                      d.o.stride_t % (d.o.dtype == PBK_BF16 ? 8 : 4) == 0 &&
+                      d.o.stride_h % (d.o.dtype == PBK_BF16 ? 8 : 4) == 0 &&
+                      d.o.stride_b % (d.o.dtype == PBK_BF16 ? 8 : 4) == 0;
   return d.q.dtype == PBK_BF16 && d.dk == 128 && d.dv == 128 && d.seqlen > 0 && ok16(d.q) && ok16(d.k) &&
-         ok16(d.v);
+         ok16(d.v) && out_ok;
 }
 
 cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st) {

@@ -157,11 +157,14 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* to
 }
 
 // Radix select over n keys key_of(i): the k-th largest key (`prefix` on return) and how
-// many elements equal to it belong to the top k (`kk`). Four 8-bit digits; warp-aggregated
-// shared-memory histograms; warp 0 finds each digit's bin with a suffix scan.
+// many elements equal to it belong to the top k (`kk`). Three digits (11, 11, 10 bits),
+// warp-aggregated shared-memory histograms; warp 0 finds each digit's bin with a suffix
+// scan (lane l owns 64 consecutive bins, highest bins first).
+constexpr int kBins = 2048;
 struct SelectSmem {
-  uint32_t hist[256];
+  uint32_t hist[kBins];
   uint32_t prefix, kk;
+  int warp_tot[2][kTopkThreads / 32];
 };
 
 template <typename KeyOf>
@@ -169,27 +172,30 @@ __device__ __forceinline__ void radix_select(KeyOf key_of, int n, uint32_t k, Se
                                              uint32_t& kk_out) {
   const int tid = threadIdx.x, lane = tid & 31;
   uint32_t prefix = 0, mask = 0, kk = k;
-  for (int digit = 3; digit >= 0; --digit) {
-    const int shift = digit * 8;
-    if (tid < 256) ss.hist[tid] = 0;
+  const int shifts[3] = {21, 10, 0}, widths[3] = {11, 11, 10};
+#pragma unroll
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = shifts[pass];
+    const uint32_t dmask = (1u << widths[pass]) - 1u;
+    const int nb = 1 << widths[pass];
+    for (int i = tid; i < kBins; i += kTopkThreads) ss.hist[i] = 0;
     __syncthreads();
     for (int base = 0; base < n; base += kTopkThreads) {
       const int i = base + tid;
       uint32_t bin = 0xFFFFFFFFu;
       if (i < n) {
         const uint32_t u = key_of(i);
-        if ((u & mask) == prefix) bin = (u >> shift) & 255u;
+        if ((u & mask) == prefix) bin = (u >> shift) & dmask;
       }
       const uint32_t same = __match_any_sync(0xffffffffu, bin);
       if (bin != 0xFFFFFFFFu && lane == __ffs(same) - 1) atomicAdd(&ss.hist[bin], (uint32_t)__popc(same));
     }
     __syncthreads();
     if (tid < 32) {
-      // lane l owns bins 255-8l down to 248-8l; suffix sums run from the top bin down
-      const int hi = 255 - 8 * lane;
+      const int per = nb / 32;             // bins per lane
+      const int hi = nb - 1 - per * lane;  // this lane's highest bin
       uint32_t own = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) own += ss.hist[hi - j];
+      for (int j = 0; j < per; ++j) own += ss.hist[hi - j];
       uint32_t incl = own;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -205,7 +211,7 @@ __device__ __forceinline__ void radix_select(KeyOf key_of, int n, uint32_t k, Se
       if (excl < kk && kk <= incl) {
         uint32_t above = excl;
         int b = hi;
-        for (int j = 0; j < 8; ++j, --b) {
+        for (int j = 0; j < per - 1; ++j, --b) {
           if (above + ss.hist[b] >= kk) break;
           above += ss.hist[b];
         }
@@ -216,40 +222,66 @@ __device__ __forceinline__ void radix_select(KeyOf key_of, int n, uint32_t k, Se
     __syncthreads();
     prefix = ss.prefix;
     kk = ss.kk;
-    mask |= 255u << shift;
+    mask |= dmask << shift;
     __syncthreads();
   }
   prefix_out = prefix;
   kk_out = kk;
 }
 
+// Warp-contiguous ranges: warp w owns [w R, (w+1) R) of n elements, read 32 at a time
+// (coalesced); R = ceil(n / 32) rounded up to a multiple of 32.
+__device__ __forceinline__ int warp_range(int n) { return ((n + 31) / 32 + 31) / 32 * 32; }
+
+// Exclusive prefix over the 32 warps of per-warp totals a (and b); returns this warp's bases.
+__device__ __forceinline__ void warp_bases(int a, int b, SelectSmem& ss, int& base_a, int& base_b, int& tot_a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    ss.warp_tot[0][warp] = a;
+    ss.warp_tot[1][warp] = b;
+  }
+  __syncthreads();
+  int ea = 0, eb = 0, ta = 0;
+  for (int w = 0; w < kTopkThreads / 32; ++w) {  // 32 broadcast reads
+    const int x = ss.warp_tot[0][w], y = ss.warp_tot[1][w];
+    if (w < warp) ea += x, eb += y;
+    ta += x;
+  }
+  base_a = ea;
+  base_b = eb;
+  tot_a = ta;
+  __syncthreads();
+}
+
 // Write the top-k of n elements given in ascending index order (key_of(i), idx_of(i)) to
-// out[0..k) in that order: every thread owns a contiguous range; two block scans give each
-// selected element its rank. Elements equal to the threshold are taken lowest index first.
+// out[0..k) in that order: an element's output position is (#greater before it) +
+// min(#equal before it, kk), so ties at the threshold go to the lowest indices.
 template <typename KeyOf, typename IdxOf>
 __device__ __forceinline__ void collect_in_order(KeyOf key_of, IdxOf idx_of, int n, uint32_t prefix, uint32_t kk,
-                                                 int* scan_scratch, int32_t* out) {
-  const int tid = threadIdx.x;
-  const int span = (n + kTopkThreads - 1) / kTopkThreads;
-  const int lo = min(tid * span, n), hi = min(lo + span, n);
+                                                 SelectSmem& ss, int32_t* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  const int R = warp_range(n);
+  const int lo = min(warp * R, n), hi = min(lo + R, n);
   int n_gt = 0, n_eq = 0;
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t u = key_of(i);
-    n_gt += u > prefix;
-    n_eq += u == prefix;
+  for (int j = lo; j < hi; j += 32) {
+    const int i = j + lane;
+    const uint32_t u = i < hi ? key_of(i) : 0u;
+    n_gt += __popc(__ballot_sync(0xffffffffu, i < hi && u > prefix));
+    n_eq += __popc(__ballot_sync(0xffffffffu, i < hi && u == prefix));
   }
-  int tot;
-  const int base_gt = block_exclusive_scan<kTopkThreads>(n_gt, scan_scratch, &tot);
-  const int base_eq = block_exclusive_scan<kTopkThreads>(n_eq, scan_scratch, &tot);
-  int pos = base_gt + min(base_eq, (int)kk), eq_seen = base_eq;
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t u = key_of(i);
-    if (u > prefix) {
-      out[pos++] = idx_of(i);
-    } else if (u == prefix) {
-      if (eq_seen < (int)kk) out[pos++] = idx_of(i);
-      ++eq_seen;
-    }
+  int gt_before, eq_before, unused;
+  warp_bases(n_gt, n_eq, ss, gt_before, eq_before, unused);
+  for (int j = lo; j < hi; j += 32) {
+    const int i = j + lane;
+    const uint32_t u = i < hi ? key_of(i) : 0u;
+    const bool gt = i < hi && u > prefix, eq = i < hi && u == prefix;
+    const uint32_t bg = __ballot_sync(0xffffffffu, gt), be = __ballot_sync(0xffffffffu, eq);
+    const int g_rank = gt_before + __popc(bg & lt), e_rank = eq_before + __popc(be & lt);
+    if (gt) out[g_rank + min(e_rank, (int)kk)] = idx_of(i);
+    else if (eq && e_rank < (int)kk) out[g_rank + e_rank] = idx_of(i);
+    gt_before += __popc(bg);
+    eq_before += __popc(be);
   }
 }
 
@@ -264,10 +296,9 @@ constexpr int kCandCap = 4096;  // candidates held in shared memory
 __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* scores, const float* segmax, int npages,
                                                                   int nseg, int k, int32_t* pages) {
   __shared__ SelectSmem ss;
-  __shared__ int scan_scratch[kTopkThreads / 32 + 1];
   __shared__ uint32_t cand_key[kCandCap];
   __shared__ int32_t cand_idx[kCandCap];
-  const int row = blockIdx.x, tid = threadIdx.x;
+  const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* s = scores + (int64_t)row * npages;
   int32_t* out = pages + (int64_t)row * k;
   uint32_t prefix, kk;
@@ -275,32 +306,39 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
     const float* sg = segmax + (int64_t)row * nseg;
     uint32_t tau, unused;
     radix_select([&](int i) { return ordered_key(sg[i]); }, nseg, (uint32_t)k, ss, tau, unused);
-    // count candidates (key >= tau) over contiguous per-thread ranges, then place them
-    const int span = (npages + kTopkThreads - 1) / kTopkThreads;
-    const int lo = min(tid * span, npages), hi = min(lo + span, npages);
+    // count candidates (key >= tau) per warp-contiguous range, then place them in order
+    const uint32_t lt = (1u << lane) - 1u;
+    const int R = warp_range(npages);
+    const int lo = min(warp * R, npages), hi = min(lo + R, npages);
     int cnt = 0;
-    for (int i = lo; i < hi; ++i) cnt += ordered_key(s[i]) >= tau;
-    int total;
-    int pos = block_exclusive_scan<kTopkThreads>(cnt, scan_scratch, &total);
+    for (int j = lo; j < hi; j += 32) {
+      const int i = j + lane;
+      cnt += __popc(__ballot_sync(0xffffffffu, i < hi && ordered_key(s[min(i, npages - 1)]) >= tau));
+    }
+    int pos, zero, total;
+    warp_bases(cnt, 0, ss, pos, zero, total);
     if (total <= kCandCap) {
-      for (int i = lo; i < hi; ++i) {
-        const uint32_t u = ordered_key(s[i]);
-        if (u >= tau) {
-          cand_key[pos] = u;
-          cand_idx[pos] = i;
-          ++pos;
+      for (int j = lo; j < hi; j += 32) {
+        const int i = j + lane;
+        const uint32_t u = ordered_key(s[min(i, npages - 1)]);
+        const bool c = i < hi && u >= tau;
+        const uint32_t bc = __ballot_sync(0xffffffffu, c);
+        if (c) {
+          const int at = pos + __popc(bc & lt);
+          cand_key[at] = u;
+          cand_idx[at] = i;
         }
+        pos += __popc(bc);
       }
       __syncthreads();
       radix_select([&](int i) { return cand_key[i]; }, total, (uint32_t)k, ss, prefix, kk);
-      collect_in_order([&](int i) { return cand_key[i]; }, [&](int i) { return cand_idx[i]; }, total, prefix, kk,
-                       scan_scratch, out);
+      collect_in_order([&](int i) { return cand_key[i]; }, [&](int i) { return cand_idx[i]; }, total, prefix, kk, ss,
+                       out);
       return;
     }
   }
   radix_select([&](int i) { return ordered_key(s[i]); }, npages, (uint32_t)k, ss, prefix, kk);
-  collect_in_order([&](int i) { return ordered_key(s[i]); }, [&](int i) { return i; }, npages, prefix, kk,
-                   scan_scratch, out);
+  collect_in_order([&](int i) { return ordered_key(s[i]); }, [&](int i) { return i; }, npages, prefix, kk, ss, out);
 }
 
 // ---------------------------------------------------------------------------------

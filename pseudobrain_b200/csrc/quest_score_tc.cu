@@ -57,6 +57,37 @@ __device__ __forceinline__ void record_error(int* err, int site, ScoreSmem& sm) 
   sm.abort = 1;
 }
 
+// Page score of every query group (the max of its RPG consecutive rows, RPG = 0: any
+// rows-per-group at run time), stored for page p; and, per group, the max over this
+// warp's 32 pages as one segment maximum.
+template <int RPG>
+__device__ __forceinline__ void group_max_store(const uint32_t (&v)[kMaxRows], const ScoreArgs& args, int kvh, int p,
+                                                int lane) {
+  const bool valid = p < args.npages;
+  const int rpg = RPG > 0 ? RPG : args.t * args.groups;
+  constexpr int kGroups = RPG > 0 ? kMaxRows / RPG : kMaxRows;
+#pragma unroll
+  for (int n = 0; n < kGroups; ++n) {
+    if (n >= args.nq) break;  // uniform across the CTA
+    float best = -INFINITY;
+    if (RPG > 0) {
+#pragma unroll
+      for (int j = 0; j < (RPG > 0 ? RPG : 1); ++j) best = fmaxf(best, __uint_as_float(v[n * (RPG > 0 ? RPG : 1) + j]));
+    } else {
+#pragma unroll
+      for (int r = 0; r < kMaxRows; ++r)
+        if (r >= n * rpg && r < (n + 1) * rpg) best = fmaxf(best, __uint_as_float(v[r]));
+    }
+    if (valid) args.scores[((int64_t)n * args.kv + kvh) * args.npages + p] = best;
+    if (args.segmax != nullptr) {  // this warp's 32 pages form one segment
+      float m = valid ? best : -INFINITY;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0 && (p >> 5) < args.nseg) args.segmax[((int64_t)n * args.kv + kvh) * args.nseg + (p >> 5)] = m;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     quest_score_tc_kernel(const __grid_constant__ CUtensorMap tmap_max, const __grid_constant__ CUtensorMap tmap_min,
                           const ScoreArgs args) {
@@ -202,19 +233,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.acc_empty[acc]);
       const int p = p0 + quad * 32 + lane;
-      const bool valid = p < args.npages;
-      for (int n = 0; n < args.nq; ++n) {
-        float best = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < kMaxRows; ++r)
-          if (r >= n * rpg && r < (n + 1) * rpg) best = fmaxf(best, __uint_as_float(v[r]));
-        if (valid) args.scores[((int64_t)n * args.kv + kvh) * args.npages + p] = best;
-        if (args.segmax != nullptr) {  // this warp's 32 pages form one segment
-          float m = valid ? best : -INFINITY;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if (lane == 0 && (p >> 5) < args.nseg) args.segmax[((int64_t)n * args.kv + kvh) * args.nseg + (p >> 5)] = m;
-        }
+      switch (rpg) {  // rows per query group: compile-time for the common shapes
+        case 1: group_max_store<1>(v, args, kvh, p, lane); break;
+        case 2: group_max_store<2>(v, args, kvh, p, lane); break;
+        case 4: group_max_store<4>(v, args, kvh, p, lane); break;
+        case 8: group_max_store<8>(v, args, kvh, p, lane); break;
+        case 16: group_max_store<16>(v, args, kvh, p, lane); break;
+        case 32: group_max_store<32>(v, args, kvh, p, lane); break;
+        case 64: group_max_store<64>(v, args, kvh, p, lane); break;
+        default: group_max_store<0>(v, args, kvh, p, lane); break;
       }
     }
   }
