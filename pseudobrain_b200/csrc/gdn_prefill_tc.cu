@@ -169,7 +169,8 @@ __device__ __forceinline__ void block_store(const float (&acc)[2][4], float s, F
 template <typename TOut>
 __global__ void __launch_bounds__(NT, 1)
     gdn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                          const __grid_constant__ CUtensorMap tm_v, const PrefillArgs p) {
+                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                          const PrefillArgs p) {
   extern __shared__ uint8_t smem_raw[];
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(NT, 1)
       tc::prefetch_tmap(&tm_q);
       tc::prefetch_tmap(&tm_k);
       tc::prefetch_tmap(&tm_v);
+      tc::prefetch_tmap(&tm_o);
       int last_kq[2] = {-1, -1}, last_v = -1;
       for (int m = 0; m < nchunks && !sm.abort; ++m) {
         // K|Q of chunk m reuse the buffer of chunk m-2: its state update must be done.
@@ -265,43 +267,49 @@ __global__ void __launch_bounds__(NT, 1)
       tc::fence_after_sync();
       return got;
     };
-    // g and beta of the next chunk are loaded one chunk ahead (registers).
-    float g_next = 0.f, b_next = 0.f;
+    // g and beta of the next chunk are loaded one chunk ahead (registers of warp 4: lane
+    // l holds steps 2l and 2l+1).
+    float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
     auto fetch_scalars = [&](int m) {
-      g_next = b_next = 0.f;
-      const int t = m * C + pt;
-      if (pt < C && m < nchunks && t < p.seqlen) {
-        g_next = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
-        b_next = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
+      g0 = g1 = b0 = b1 = 0.f;
+      if (pw == 0 && m < nchunks) {
+        const int t = m * C + 2 * lane;
+        if (t < p.seqlen) {
+          g0 = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
+          b0 = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
+        }
+        if (t + 1 < p.seqlen) {
+          g1 = load_any(p.g, b * p.g_sb + (int64_t)(t + 1) * p.g_st + h * p.g_sh, p.g_dtype);
+          b1 = load_any(p.beta, b * p.b_sb + (int64_t)(t + 1) * p.b_st + h * p.b_sh, p.b_dtype);
+        }
       }
     };
     fetch_scalars(0);
     for (int m = 0; m < nchunks && ok; ++m) {
       const int buf = m & 1, sb = m % 3;
-      // ---- scalars: cumulative log decay, gamma, e, beta
-      {
-        float x = g_next;
-        const float bv = b_next;
-        if (pt < C) {
+      // ---- scalars: cumulative log decay c, gamma = e^c, e = e^(c_C - c), beta
+      if (pw == 0) {
+        constexpr float kLog2e = 1.4426950408889634f;
+        const float pair = g0 + g1;
+        float incl = pair;
 #pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, x, o);
-            if (lane >= o) x += y;
-          }
-          sm.cum[sb][pt] = x;
-          sm.beta[sb][pt] = bv;
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
         }
-        fetch_scalars(m + 1);
-        wg_sync(2);
-        if (pt >= 32 && pt < C) sm.cum[sb][pt] += sm.cum[sb][31];
-        wg_sync(2);
-        if (pt < C) {
-          const float c = sm.cum[sb][pt];
-          sm.gam[sb][pt] = expf(c);
-          sm.ee[sb][pt] = expf(sm.cum[sb][C - 1] - c);
-          sm.cum2[sb][pt] = c * 1.4426950408889634f;
-        }
+        const float c0 = incl - pair + g0, c1 = incl;
+        const float clast = __shfl_sync(0xffffffffu, incl, 31);
+        sm.cum2[sb][2 * lane] = c0 * kLog2e;
+        sm.cum2[sb][2 * lane + 1] = c1 * kLog2e;
+        sm.gam[sb][2 * lane] = exp2f(c0 * kLog2e);
+        sm.gam[sb][2 * lane + 1] = exp2f(c1 * kLog2e);
+        sm.ee[sb][2 * lane] = exp2f((clast - c0) * kLog2e);
+        sm.ee[sb][2 * lane + 1] = exp2f((clast - c1) * kLog2e);
+        sm.beta[sb][2 * lane] = b0;
+        sm.beta[sb][2 * lane + 1] = b1;
       }
+      fetch_scalars(m + 1);
+      wg_sync(2);
       // ---- [K;Q] K^T
       if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
       if (pt == 0) {
@@ -436,25 +444,11 @@ __global__ void __launch_bounds__(NT, 1)
         tc::mma_commit(&sm.bar_p3);
       }
       if (!pwait(&sm.bar_p3, m & 1, 4)) break;
-      // ---- W^T -> wt[buf] (bf16, MN-major rows); K rows scaled by e_i (state-update operand)
+      // ---- W^T -> wt[buf] (bf16, MN-major rows)
       {
         float v[64];
         tmem_row64(lane_addr + kColD1, v);
         store_row_bf16(sm.wt[buf], pt, v);
-        const int i = pt >> 1, a = pt & 1;
-        const float e = sm.ee[sb][i];
-        uint8_t* row = sm.kq[buf][a] + i * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 w = *reinterpret_cast<uint4*>(row + 16 * c);
-          __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const float2 f = __bfloat1622float2(h2[jj]);
-            h2[jj] = __floats2bfloat162_rn(f.x * e, f.y * e);
-          }
-          *reinterpret_cast<uint4*>(row + 16 * c) = w;
-        }
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
@@ -537,11 +531,11 @@ __global__ void __launch_bounds__(NT, 1)
         tc::mma_commit(&sm.bar_ws);
       }
     };
-    TOut* out = reinterpret_cast<TOut*>(p.o) + b * p.o_sb + h * p.o_sh;
     if (swait(&sm.prep_ready, 0, 1)) state_step(0);
     for (int n = 0; n < nchunks && ok; ++n) {
       const int buf = n & 1, sb = n % 3;
-      // U = U' - WS -> U^T bf16; then UM^T = U^T M^T and S^T += U^T (diag(e) K)
+      // U = U' - WS -> U^T bf16; then UM^T = U^T M^T and S^T += (U diag(e))^T K
+      if (tid == 0) tc::bulk_wait_read0();  // the output store of chunk n-1 has read ut
       if (!swait(&sm.bar_ws, n & 1, 2)) break;
       {
         float ws[64], up[64];
@@ -550,6 +544,12 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int i = 0; i < 64; ++i) up[i] -= ws[i];
         store_row_bf16(sm.ut, tid, up);
+        // U diag(e) -> st[0] (free: the S^T products of this chunk are done), the A
+        // operand of the state update
+        const float* ee = sm.ee[sb];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) up[i] *= ee[i];
+        store_row_bf16(sm.st[0], tid, up);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(NT, 1)
           tc::mma_f16(tmem + kColUM, ad, bm, i_kk, kk != 0);
         }
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.ut) + kk * 32, 16, 1024);
+          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[0]) + kk * 32, 16, 1024);
           const uint64_t bk = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][0]) + kk * 2048, 16384, 1024);
           tc::mma_f16(tmem + kColS, ad, bk, i_s, 1);
         }
@@ -585,25 +585,27 @@ __global__ void __launch_bounds__(NT, 1)
         if (!swait(&sm.prep_ready, (n + 1) & 1, 4)) break;
         state_step(n + 1);
       }
-      const int tmax = min(C, p.seqlen - n * C);
-      constexpr int kPer = 16 / sizeof(TOut);           // elements per 16-byte vector
-      constexpr int kRows = sizeof(TOut) == 2 ? 64 : 32;  // t rows staged per pass (16 KB)
+      // O through shared memory (ut, row-major [rows][128]) and a TMA store; rows past
+      // the sequence end fall outside the tensor and are not written.
+      constexpr int kRows = sizeof(TOut) == 2 ? 64 : 32;  // 16 KB per pass
+      TOut* stage = reinterpret_cast<TOut*>(sm.ut);
 #pragma unroll
       for (int t0 = 0; t0 < 64; t0 += kRows) {
-        TOut* stage = reinterpret_cast<TOut*>(sm.ut);  // [kRows][128]: row t, column = this thread
+        if (t0 > 0) {
+          if (tid == 0) tc::bulk_wait_read0();
+          wg_sync(1);
+        }
 #pragma unroll
         for (int t = 0; t < kRows; ++t) stage[t * D + tid] = from_f32<TOut>(o[t0 + t]);
+        tc::fence_proxy_async_smem();
         wg_sync(1);
-        constexpr int kVecs = kRows * D / kPer;
-        for (int vi = tid; vi < kVecs; vi += 128) {
-          const int t = vi / (D / kPer), c = (vi % (D / kPer)) * kPer;
-          if (t0 + t < tmax)
-            *reinterpret_cast<uint4*>(out + (int64_t)(n * C + t0 + t) * p.o_st + c) =
-                *reinterpret_cast<const uint4*>(stage + t * D + c);
+        if (tid == 0) {
+          tc::tma_store_4d(&tm_o, stage, 0, n * C + t0, h, b);
+          tc::bulk_commit();
         }
-        wg_sync(1);
       }
     }
+    if (tid == 0) tc::bulk_wait0();
     if (tid == 0) {  // every MMA this thread issued completes before TMEM is freed
       tc::mma_commit(&sm.drain_s);
       tc::mbar_wait(&sm.drain_s, 0, 200000000ull);
@@ -657,9 +659,18 @@ bool gdn_prefill_tc_supported(const pbk_gdn_desc& d) {
 }
 
 cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st) {
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   if (!make_map(&mq, d.q, d.hk, d) || !make_map(&mk, d.k, d.hk, d) || !make_map(&mv, d.v, d.hv, d))
     return cudaErrorInvalidValue;
+  {
+    const bool obf = d.o.dtype == PBK_BF16;
+    const uint64_t es = obf ? 2 : 4;
+    const uint64_t dims[4] = {128, (uint64_t)d.seqlen, (uint64_t)d.hv, (uint64_t)d.batch};
+    const uint64_t strides[3] = {(uint64_t)d.o.stride_t * es, (uint64_t)d.o.stride_h * es,
+                                 (uint64_t)d.o.stride_b * es};
+    const uint32_t box[4] = {128, obf ? 64u : 32u, 1, 1};
+    if (!make_tmap_plain(&mo, d.o.data, obf, 4, dims, strides, box)) return cudaErrorInvalidValue;
+  }
   PrefillArgs a;
   a.batch = d.batch;
   a.seqlen = d.seqlen;
@@ -691,12 +702,12 @@ cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(gdn_prefill_tc_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kSmemBytes);
     if (e != cudaSuccess) return e;
-    gdn_prefill_tc_kernel<bf16><<<grid, NT, kSmemBytes, st>>>(mq, mk, mv, a);
+    gdn_prefill_tc_kernel<bf16><<<grid, NT, kSmemBytes, st>>>(mq, mk, mv, mo, a);
   } else {
     cudaError_t e = cudaFuncSetAttribute(gdn_prefill_tc_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kSmemBytes);
     if (e != cudaSuccess) return e;
-    gdn_prefill_tc_kernel<float><<<grid, NT, kSmemBytes, st>>>(mq, mk, mv, a);
+    gdn_prefill_tc_kernel<float><<<grid, NT, kSmemBytes, st>>>(mq, mk, mv, mo, a);
   }
   return cudaGetLastError();
 }

@@ -15,6 +15,11 @@ namespace pbk {
 bool make_tmap_bf16_sw128(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                           const uint64_t* strides_bytes, const uint32_t* box);
 
+// Encode a tiled map without swizzle (bf16 when bf16, else fp32), e.g. for stores of
+// row-major tiles staged in shared memory.
+bool make_tmap_plain(CUtensorMap* map, const void* base, bool bf16, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes, const uint32_t* box);
+
 // Device address of this library's error word on the current device (looked up once
 // per device). Kernels write a nonzero code there when a bounded wait times out.
 int* device_error_word();
