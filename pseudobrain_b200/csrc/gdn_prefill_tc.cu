@@ -378,26 +378,44 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
       wg_sync(2);
-      // off-diagonal blocks, by distance: T_ij = -T_ii (sum_{k=j}^{i-1} A_ik T_kj)
+      // off-diagonal blocks: T_ij = -T_ii (sum_{k=j}^{i-1} A_ik T_kj), in three levels:
+      // the two 32x32 diagonal halves (T_10, T_32), then the lower-left 32x32 quarter as
+      // X = A_21 T_1 (four 16x16 blocks, one per warp) and T_21 = -T_2 X.
       {
-        float* scr = reinterpret_cast<float*>(sm.tb) + pw * (16 * 24);  // per-warp 16x16 (stride 24)
+        float* scr = reinterpret_cast<float*>(sm.tb);  // 4 x (16 x 24) fp32 scratch blocks
+        auto sread = [&](int w) { return [=](int r, int c) { return scr[w * 384 + r * 24 + c]; }; };
+        auto swrite = [&](int w) { return [=](int r, int c, float x) { scr[w * 384 + r * 24 + c] = x; }; };
         auto at = [&](int bi, int bj) {
           return [=, &sm](int r, int c) { return sm.a[(16 * bi + r) * PA + 16 * bj + c]; };
         };
         auto tt = [&](int bi, int bj) { return [=](int r, int c) { return ts[tidx(16 * bi + r, 16 * bj + c)]; }; };
-        for (int dist = 1; dist < 4; ++dist) {
-          if (pw < 4 - dist) {
-            const int j = pw, i = pw + dist;
-            float acc[2][4] = {};
-            for (int k = j; k < i; ++k) block_mma(acc, at(i, k), tt(k, j), lane);
-            block_store(acc, 1.f, [&](int r, int c, float x) { scr[r * 24 + c] = x; }, lane);
-            __syncwarp();
-            float acc2[2][4] = {};
-            block_mma(acc2, tt(i, i), [&](int r, int c) { return scr[r * 24 + c]; }, lane);
-            block_store(acc2, -1.f, [&](int r, int c, float x) { ts[tidx(16 * i + r, 16 * j + c)] = x; }, lane);
-          }
-          wg_sync(2);
+        auto twrite = [&](int bi, int bj) {
+          return [=](int r, int c, float x) { ts[tidx(16 * bi + r, 16 * bj + c)] = x; };
+        };
+        if (pw < 2) {  // T_10 (warp 0), T_32 (warp 1)
+          const int j = 2 * pw, i = j + 1;
+          float acc[2][4] = {};
+          block_mma(acc, at(i, j), tt(j, j), lane);
+          block_store(acc, 1.f, swrite(pw), lane);
+          __syncwarp();
+          float acc2[2][4] = {};
+          block_mma(acc2, tt(i, i), sread(pw), lane);
+          block_store(acc2, -1.f, twrite(i, j), lane);
         }
+        wg_sync(2);
+        const int r = 2 + (pw >> 1), c = pw & 1;
+        {  // X_rc = sum_{k=c}^{1} A_rk T_kc
+          float acc[2][4] = {};
+          for (int k = c; k < 2; ++k) block_mma(acc, at(r, k), tt(k, c), lane);
+          block_store(acc, 1.f, swrite(pw), lane);
+        }
+        wg_sync(2);
+        {  // T_rc = -sum_{k=2}^{r} T_rk X_kc
+          float acc[2][4] = {};
+          for (int k = 2; k <= r; ++k) block_mma(acc, tt(r, k), sread(2 * (k - 2) + c), lane);
+          block_store(acc, -1.f, twrite(r, c), lane);
+        }
+        wg_sync(2);
       }
       // ---- TB = T diag(beta), TBG = T diag(beta gamma), bf16 rows (zero above the blocks)
       {
