@@ -87,6 +87,9 @@ typedef struct pbk_gdn_desc {
 
 PBK_API int pbk_abi_version(void);
 PBK_API const char* pbk_status_string(int status);
+/* The CUDA error message behind the calling thread's last PBK_ERR_LAUNCH ("no error"
+ * when there was none). */
+PBK_API const char* pbk_last_launch_error(void);
 /* PBK_OK when `device` is an sm_100 (B200-class) GPU. */
 PBK_API int pbk_device_check(int device);
 /* Reads (and with clear != 0 resets) the current device's error word, which the

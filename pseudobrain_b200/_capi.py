@@ -60,6 +60,7 @@ _VP, _I32, _I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
 SIGNATURES = {
     "pbk_abi_version": (ctypes.c_int, []),
     "pbk_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "pbk_last_launch_error": (ctypes.c_char_p, []),
     "pbk_device_check": (ctypes.c_int, [ctypes.c_int]),
     "pbk_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "pbk_gdn_decode": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
@@ -94,7 +95,10 @@ LIB = _load()
 class PbkError(RuntimeError):
     def __init__(self, status: int, what: str):
         self.status = status
-        super().__init__(f"{what}: {LIB.pbk_status_string(status).decode()} (status {status})")
+        msg = f"{what}: {LIB.pbk_status_string(status).decode()} (status {status})"
+        if status == -6:
+            msg += f": {LIB.pbk_last_launch_error().decode()}"
+        super().__init__(msg)
 
 
 def check(status: int, what: str) -> None:

@@ -16,6 +16,15 @@ namespace {
 
 bool dtype_ok(int32_t dt) { return dt == PBK_F32 || dt == PBK_BF16; }
 
+// The CUDA error behind this thread's last PBK_ERR_LAUNCH (cudaSuccess if none).
+thread_local cudaError_t g_last_launch_error = cudaSuccess;
+
+int launch_status(cudaError_t e) {
+  if (e == cudaSuccess) return PBK_OK;
+  g_last_launch_error = e;
+  return PBK_ERR_LAUNCH;
+}
+
 // Compute capability 10.x, checked once per device and cached (immutable afterwards).
 int check_current_device() {
   int dev = 0;
@@ -92,6 +101,8 @@ extern "C" {
 
 int pbk_abi_version(void) { return PBK_ABI_VERSION; }
 
+const char* pbk_last_launch_error(void) { return cudaGetErrorString(g_last_launch_error); }
+
 const char* pbk_status_string(int status) {
   switch (status) {
     case PBK_OK: return "ok";
@@ -134,8 +145,7 @@ int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream) {
   }
   if (desc->batch == 0) return PBK_OK;  // seqlen 0 still copies h0 into state
   if ((st = check_current_device()) != PBK_OK) return st;
-  return pbk::launch_gdn_decode(*desc, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
-                                                                                         : PBK_ERR_LAUNCH;
+  return launch_status(pbk::launch_gdn_decode(*desc, static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
@@ -148,7 +158,7 @@ int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
   const cudaError_t e = pbk::gdn_prefill_tc_supported(*desc)
                             ? pbk::launch_gdn_prefill_tc(*desc, static_cast<cudaStream_t>(stream))
                             : pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? PBK_OK : PBK_ERR_LAUNCH;
+  return launch_status(e);
 }
 
 size_t pbk_quest_select_workspace(const pbk_quest_desc* desc) {
@@ -169,10 +179,7 @@ int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspa
   if (desc->nq == 0) return PBK_OK;
   if ((st = check_current_device()) != PBK_OK) return st;
   // workspace: the page scores (unless desc->scores keeps them), then the segment maxima
-  return pbk::launch_quest_select(*desc, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)) ==
-                 cudaSuccess
-             ? PBK_OK
-             : PBK_ERR_LAUNCH;
+  return launch_status(pbk::launch_quest_select(*desc, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream) {
@@ -183,8 +190,7 @@ int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream) {
   if (pbk::quest_select_floats(*desc) > pbk::kNoAllocFloats) return PBK_ERR_TOO_LARGE;
   if (desc->nq == 0) return PBK_OK;
   if ((st = check_current_device()) != PBK_OK) return st;
-  return pbk::launch_quest_select_noalloc(*desc, static_cast<cudaStream_t>(stream)) == cudaSuccess ? PBK_OK
-                                                                                                   : PBK_ERR_LAUNCH;
+  return launch_status(pbk::launch_quest_select_noalloc(*desc, static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_quest_attend(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
@@ -194,10 +200,7 @@ int pbk_quest_attend(const pbk_quest_desc* desc, void* workspace, size_t workspa
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return PBK_ERR_WORKSPACE;
   if (desc->nq == 0) return PBK_OK;
   if ((st = check_current_device()) != PBK_OK) return st;
-  return pbk::launch_quest_attend(*desc, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)) ==
-                 cudaSuccess
-             ? PBK_OK
-             : PBK_ERR_LAUNCH;
+  return launch_status(pbk::launch_quest_attend(*desc, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_quest_gather(const pbk_quest_desc* desc, int32_t sel, void* out_keys, void* out_values, void* stream) {
@@ -208,9 +211,7 @@ int pbk_quest_gather(const pbk_quest_desc* desc, int32_t sel, void* out_keys, vo
   if (desc->nq == 0) return PBK_OK;
   if (!out_keys || !out_values) return PBK_ERR_INVALID;
   if ((st = check_current_device()) != PBK_OK) return st;
-  return pbk::launch_quest_gather(*desc, sel, out_keys, out_values, static_cast<cudaStream_t>(stream)) == cudaSuccess
-             ? PBK_OK
-             : PBK_ERR_LAUNCH;
+  return launch_status(pbk::launch_quest_gather(*desc, sel, out_keys, out_values, static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d, int32_t page, int64_t key_stride_kv,
@@ -225,10 +226,8 @@ int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d, int32_t
     return PBK_ERR_ALIGN;
   int st = check_current_device();
   if (st != PBK_OK) return st;
-  return pbk::launch_quest_bounds(keys, kv, n, page, key_stride_kv, key_stride_n, kmax, kmin, bnd_stride_kv,
-                                  bnd_stride_p, first_page, static_cast<cudaStream_t>(stream)) == cudaSuccess
-             ? PBK_OK
-             : PBK_ERR_LAUNCH;
+  return launch_status(pbk::launch_quest_bounds(keys, kv, n, page, key_stride_kv, key_stride_n, kmax, kmin, bnd_stride_kv,
+                                  bnd_stride_p, first_page, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

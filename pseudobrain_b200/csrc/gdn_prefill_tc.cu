@@ -15,14 +15,14 @@
 //   (UM)^T = U^T M^T -> TMEM UM;  S^T += U^T (diag(e) K) -> TMEM S           K = i
 //
 // One CTA per (sequence, value head) chain, warp-specialised:
-//   warps 0-3 (serial): state step of chunk n -- S^T to bf16 and S^T *= gamma_C through
+//   warps 0-7 (serial): state step of chunk n -- S^T to bf16 and S^T *= gamma_C through
 //     the registers, then U = U' - WS, then the outputs; their thread 0 issues the S MMAs.
-//   warps 4-7 (prep): chunk n+1's scalars, K K^T, A and M, the inverse (16x16 diagonal
+//   warps 8-15 (prep): chunk n+1's scalars, K K^T, A and M, the inverse (16x16 diagonal
 //     blocks by substitution, off-diagonal blocks by tf32 mma.sync products), then W^T and
 //     U'^T; their thread 0 issues the prep MMAs.
-//   warp 8 (producer): TMA loads of K|Q and V (4-D maps over [B,T,H,128], any strides,
-//     rows past T zero-filled = the reference's identity padding; no multicast), and the
-//     TMEM allocation.
+// Warp w of a role reads TMEM lane quadrant w % 4 and half w / 4 of each row's columns.
+// K|Q and V arrive by TMA (4-D maps over [B,T,H,128], any strides; rows past T are
+// zero-filled, the reference's identity padding; no multicast), issued by the leaders.
 // The roles meet on mbarriers; every wait is bounded: on timeout the kernel records an
 // error code, stops issuing, waits (bounded) for its own loads and MMAs, frees its TMEM
 // and returns.
@@ -36,7 +36,9 @@ namespace {
 using bf16 = __nv_bfloat16;
 constexpr int C = 64;
 constexpr int D = 128;
-constexpr int NT = 288;    // 2 warpgroups + producer warp
+constexpr int kRoleWarps = 8;                 // warps per role (serial, prep)
+constexpr int kRoleThreads = 32 * kRoleWarps;
+constexpr int NT = 2 * kRoleThreads;          // serial role, prep role
 constexpr int PA = C + 4;  // fp32 row stride of A (16-byte rows)
 
 // TMEM columns
@@ -83,42 +85,41 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Write 64 fp32 values as one 128-byte bf16 row of a 128B-swizzled tile.
-__device__ __forceinline__ void store_row_bf16(uint8_t* tile, int row, const float* v) {
+// Named barrier over one role's threads (id 1: serial, 2: prep), and its AND-reduction.
+__device__ __forceinline__ void role_sync(int id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "n"(kRoleThreads) : "memory");
+}
+__device__ __forceinline__ bool role_and(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "n"(kRoleThreads)
+      : "memory");
+  return r != 0;
+}
+
+// 32 TMEM columns of this thread's lane into v[32].
+__device__ __forceinline__ void tmem_row32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  tc::tmem_ld_32x32(taddr, r);
+  tc::tmem_ld_wait();
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 fp32 values as bf16 into half `half` (elements 32 half .. 32 half + 31) of a 64-element
+// row of a 128B-swizzled tile.
+__device__ __forceinline__ void store_half_row_bf16(uint8_t* tile, int row, int half, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
     uint4 w;
     w.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
     w.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
     w.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
     w.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
-    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(row, 8 * c)) = w;
+    *reinterpret_cast<uint4*>(tile + tc::sw128_offset(row, 32 * half + 8 * c)) = w;
   }
-}
-
-// 64 TMEM columns of this thread's lane into v[64] (two loads in flight, one wait).
-__device__ __forceinline__ void tmem_row64(uint32_t taddr, float* v) {
-  uint32_t r0[32], r1[32];
-  tc::tmem_ld_32x32(taddr, r0);
-  tc::tmem_ld_32x32(taddr + 32, r1);
-  tc::tmem_ld_wait();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    v[i] = __uint_as_float(r0[i]);
-    v[32 + i] = __uint_as_float(r1[i]);
-  }
-}
-
-// Named barrier over one warpgroup (id 1: serial, 2: prep), and its AND-reduction.
-__device__ __forceinline__ void wg_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
-__device__ __forceinline__ bool wg_and(int id, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id)
-      : "memory");
-  return r != 0;
 }
 
 // fp32 T scratch (64 x 64) with an XOR swizzle that keeps the mma.sync fragment loads
@@ -137,33 +138,27 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
-// acc (a 16x16 block as two m16n8 tiles) += X (16x16) * Y (16x16); x(r, c), y(r, c) read
-// the operands. Fragment layout of m16n8k8 tf32: groupID g = lane / 4, t = lane % 4.
+// acc (the 16x8 n-tile nt of a 16x16 block) += X (16x16) * Y (16x16)[:, 8 nt ..]; x(r, c),
+// y(r, c) read the operands. m16n8k8 tf32 fragments: groupID g = lane / 4, t = lane % 4.
 template <typename FX, typename FY>
-__device__ __forceinline__ void block_mma(float (&acc)[2][4], FX x, FY y, int lane) {
+__device__ __forceinline__ void tile_mma(float (&acc)[4], FX x, FY y, int nt, int lane) {
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int k0 = 0; k0 < 16; k0 += 8) {
     const uint32_t a[4] = {to_tf32(x(g, k0 + t)), to_tf32(x(g + 8, k0 + t)), to_tf32(x(g, k0 + t + 4)),
                            to_tf32(x(g + 8, k0 + t + 4))};
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const uint32_t b[2] = {to_tf32(y(k0 + t, 8 * nt + g)), to_tf32(y(k0 + t + 4, 8 * nt + g))};
-      mma_tf32(acc[nt], a, b);
-    }
+    const uint32_t bb[2] = {to_tf32(y(k0 + t, 8 * nt + g)), to_tf32(y(k0 + t + 4, 8 * nt + g))};
+    mma_tf32(acc, a, bb);
   }
 }
-// Store acc (scaled by s) through st(r, c, value).
+// Store the n-tile (scaled by s) through st(r, c, value).
 template <typename FS>
-__device__ __forceinline__ void block_store(const float (&acc)[2][4], float s, FS st, int lane) {
+__device__ __forceinline__ void tile_store(const float (&acc)[4], float s, FS st, int nt, int lane) {
   const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    st(g, 8 * nt + 2 * t, s * acc[nt][0]);
-    st(g, 8 * nt + 2 * t + 1, s * acc[nt][1]);
-    st(g + 8, 8 * nt + 2 * t, s * acc[nt][2]);
-    st(g + 8, 8 * nt + 2 * t + 1, s * acc[nt][3]);
-  }
+  st(g, 8 * nt + 2 * t, s * acc[0]);
+  st(g, 8 * nt + 2 * t + 1, s * acc[1]);
+  st(g + 8, 8 * nt + 2 * t, s * acc[2]);
+  st(g + 8, 8 * nt + 2 * t + 1, s * acc[3]);
 }
 
 template <typename TOut>
@@ -191,13 +186,13 @@ __global__ void __launch_bounds__(NT, 1)
     tc::mbar_init(&sm.bar_p3, 1);
     tc::mbar_init(&sm.bar_ws, 1);
     tc::mbar_init(&sm.bar_s, 1);
-    tc::mbar_init(&sm.prep_ready, 128);
+    tc::mbar_init(&sm.prep_ready, kRoleThreads);
     tc::mbar_init(&sm.drain_s, 1);
     tc::mbar_init(&sm.drain_p, 1);
     sm.abort = 0;
     tc::fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == 0) {
     tc::tmem_alloc(&sm.tmem_base, kTmemCols);
     tc::tmem_relinquish();
   }
@@ -205,53 +200,45 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // TMEM lane of row (tid % 128)
+  // Role layout: warp w of a role reads TMEM lanes 32 (w % 4) .. + 31 (its operand rows)
+  // and owns half hf = w / 4 of each row's columns.
+  const int quad = warp & 3, hf = (warp >> 2) & 1;
+  const int row = 32 * quad + lane;
+  const uint32_t lane_addr = tmem + ((uint32_t)(32 * quad) << 16);
 
   const uint32_t i_kk = tc::idesc_bf16_f32(128, 64, false, false);   // A K-major, B K-major, N=64
   const uint32_t i_kmn = tc::idesc_bf16_f32(128, 64, false, true);   // A K-major, B MN-major, N=64
   const uint32_t i_mnk = tc::idesc_bf16_f32(128, 64, true, false);   // A MN-major, B K-major, N=64
   const uint32_t i_s = tc::idesc_bf16_f32(128, 128, false, true);    // S update, N=128
 
-  if (warp == 8) {
-    // ================================================================ producer
-    if (lane == 0) {
-      tc::prefetch_tmap(&tm_q);
-      tc::prefetch_tmap(&tm_k);
-      tc::prefetch_tmap(&tm_v);
-      tc::prefetch_tmap(&tm_o);
-      int last_kq[2] = {-1, -1}, last_v = -1;
-      for (int m = 0; m < nchunks && !sm.abort; ++m) {
-        // K|Q of chunk m reuse the buffer of chunk m-2: its state update must be done.
-        if (m >= 2 && !tc::mbar_wait(&sm.bar_s, (m - 2) & 1)) {
-          if (p.err) atomicCAS(p.err, 0, 301);
-          sm.abort = 1;
-          break;
-        }
-        const int buf = m & 1;
-        tc::mbar_expect_tx(&sm.bar_kq[buf], 4 * 8192);
-        for (int a = 0; a < 2; ++a) {
-          tc::tma_load_4d(sm.kq[buf][a], &tm_k, &sm.bar_kq[buf], 64 * a, m * C, hk, b);
-          tc::tma_load_4d(sm.kq[buf][a] + 8192, &tm_q, &sm.bar_kq[buf], 64 * a, m * C, hk, b);
-        }
-        last_kq[buf] = m;
-        // V of chunk m reuses the V buffer: the U' product of chunk m-1 must be done.
-        if (m >= 1 && !tc::mbar_wait(&sm.bar_p3, (m - 1) & 1)) {
-          if (p.err) atomicCAS(p.err, 0, 302);
-          sm.abort = 1;
-          break;
-        }
-        tc::mbar_expect_tx(&sm.bar_v, 2 * 8192);
-        for (int a = 0; a < 2; ++a) tc::tma_load_4d(sm.v[a], &tm_v, &sm.bar_v, 64 * a, m * C, h, b);
-        last_v = m;
-      }
-      // our loads in flight land before the CTA exits (bounded)
-      for (int bb = 0; bb < 2; ++bb)
-        if (last_kq[bb] >= 0) tc::mbar_wait(&sm.bar_kq[bb], (last_kq[bb] >> 1) & 1, 200000000ull);
-      if (last_v >= 0) tc::mbar_wait(&sm.bar_v, last_v & 1, 200000000ull);
+  // TMA loads (4-D maps over [B,T,H,128], rows past T zero-filled, no multicast). K|Q of
+  // chunk m go to buffer m&1 (issued by the serial leader once chunk m-2's state update is
+  // done), V to the single V buffer (issued by the prep leader once U' of chunk m-1 is done).
+  auto issue_kq = [&](int m) {
+    const int buf = m & 1;
+    tc::mbar_expect_tx(&sm.bar_kq[buf], 4 * 8192);
+    for (int a = 0; a < 2; ++a) {
+      tc::tma_load_4d(sm.kq[buf][a], &tm_k, &sm.bar_kq[buf], 64 * a, m * C, hk, b);
+      tc::tma_load_4d(sm.kq[buf][a] + 8192, &tm_q, &sm.bar_kq[buf], 64 * a, m * C, hk, b);
     }
-  } else if (warp >= 4) {
-    // ================================================================ prep warpgroup
-    const int pt = tid - 128, pw = warp - 4;  // thread / warp within the group
+  };
+  auto issue_v = [&](int m) {
+    tc::mbar_expect_tx(&sm.bar_v, 2 * 8192);
+    for (int a = 0; a < 2; ++a) tc::tma_load_4d(sm.v[a], &tm_v, &sm.bar_v, 64 * a, m * C, h, b);
+  };
+  if (tid == 0) {
+    tc::prefetch_tmap(&tm_q);
+    tc::prefetch_tmap(&tm_k);
+    tc::prefetch_tmap(&tm_v);
+    tc::prefetch_tmap(&tm_o);
+    issue_kq(0);
+    if (nchunks > 1) issue_kq(1);
+    issue_v(0);
+  }
+
+  if (warp >= kRoleWarps) {
+    // ================================================================ prep role
+    const int pt = tid - kRoleThreads, pw = warp - kRoleWarps;  // thread / warp within the role
     bool ok = true;
     auto fail = [&](int site) {
       if (pt == 0) {
@@ -260,15 +247,15 @@ __global__ void __launch_bounds__(NT, 1)
       }
       ok = false;
     };
-    // bounded wait by every prep thread, outcome uniform across the group
+    // bounded wait by every prep thread, outcome uniform across the role
     auto pwait = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
-      const bool got = wg_and(2, tc::mbar_wait(bar, parity) && !sm.abort);
+      const bool got = role_and(2, tc::mbar_wait(bar, parity) && !sm.abort);
       if (!got) fail(site);
       tc::fence_after_sync();
       return got;
     };
-    // g and beta of the next chunk are loaded one chunk ahead (registers of warp 4: lane
-    // l holds steps 2l and 2l+1).
+    // g and beta of the next chunk are loaded one chunk ahead (registers of the role's
+    // first warp: lane l holds steps 2l and 2l+1).
     float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
     auto fetch_scalars = [&](int m) {
       g0 = g1 = b0 = b1 = 0.f;
@@ -284,6 +271,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
     };
+    int last_v = 0;  // last V load issued (for the bounded drain)
     fetch_scalars(0);
     for (int m = 0; m < nchunks && ok; ++m) {
       const int buf = m & 1, sb = m % 3;
@@ -309,7 +297,6 @@ __global__ void __launch_bounds__(NT, 1)
         sm.beta[sb][2 * lane + 1] = b1;
       }
       fetch_scalars(m + 1);
-      wg_sync(2);
       // ---- [K;Q] K^T
       if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
       if (pt == 0) {
@@ -321,66 +308,61 @@ __global__ void __launch_bounds__(NT, 1)
         tc::mma_commit(&sm.bar_p1);
       }
       if (!pwait(&sm.bar_p1, m & 1, 2)) break;
-      // ---- A (fp32) from K K^T rows (lanes 0-63), M (bf16) from Q K^T rows (lanes 64-127)
+      // ---- A (fp32) from K K^T rows (lanes 0-63), M (bf16) from Q K^T rows (lanes 64-127);
+      // this thread: row `row`, columns 32 hf .. 32 hf + 31
       {
-        float v[64];
-        tmem_row64(lane_addr + kColD1, v);
         const float* c2 = sm.cum2[sb];
-        if (pt < C) {
-          const int t = pt;
+        const int t = row & 63, i0 = 32 * hf;
+        const bool zero = t < 32 && hf == 1;  // rows 0-31 have no terms past column 31
+        float v[32];
+        if (!zero) tmem_row32(lane_addr + kColD1 + i0, v);
+        if (row < C) {
           const float bt = sm.beta[sb][t], ct = c2[t];
-          const int lim = pw == 0 ? 32 : 64;  // rows 0-31 have no terms past column 31
 #pragma unroll
-          for (int i = 0; i < C; i += 4) {
+          for (int i = 0; i < 32; i += 4) {
             float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (i < lim) {
-              w.x = i + 0 < t ? bt * v[i + 0] * exp2f(ct - c2[i + 0]) : 0.f;
-              w.y = i + 1 < t ? bt * v[i + 1] * exp2f(ct - c2[i + 1]) : 0.f;
-              w.z = i + 2 < t ? bt * v[i + 2] * exp2f(ct - c2[i + 2]) : 0.f;
-              w.w = i + 3 < t ? bt * v[i + 3] * exp2f(ct - c2[i + 3]) : 0.f;
+            if (!zero) {
+              w.x = i0 + i + 0 < t ? bt * v[i + 0] * exp2f(ct - c2[i0 + i + 0]) : 0.f;
+              w.y = i0 + i + 1 < t ? bt * v[i + 1] * exp2f(ct - c2[i0 + i + 1]) : 0.f;
+              w.z = i0 + i + 2 < t ? bt * v[i + 2] * exp2f(ct - c2[i0 + i + 2]) : 0.f;
+              w.w = i0 + i + 3 < t ? bt * v[i + 3] * exp2f(ct - c2[i0 + i + 3]) : 0.f;
             }
-            *reinterpret_cast<float4*>(&sm.a[t * PA + i]) = w;
+            *reinterpret_cast<float4*>(&sm.a[t * PA + i0 + i]) = w;
           }
         } else {
-          const int t = pt - C;
           const float ct = c2[t];
-          const int lim = pw == 2 ? 32 : 64;
 #pragma unroll
-          for (int i = 0; i < C; ++i) v[i] = (i < lim && i <= t) ? p.scale * v[i] * exp2f(ct - c2[i]) : 0.f;
-          store_row_bf16(sm.m[buf], t, v);
+          for (int i = 0; i < 32; ++i) v[i] = (!zero && i0 + i <= t) ? p.scale * v[i] * exp2f(ct - c2[i0 + i]) : 0.f;
+          store_half_row_bf16(sm.m[buf], t, hf, v);
         }
       }
       tc::fence_before_sync();
-      wg_sync(2);
-      // ---- T = (I + A)^-1, blocked: diagonal 16x16 blocks by forward substitution
+      role_sync(2);
+      // ---- T = (I + A)^-1, blocked. Diagonal 16x16 blocks (warps 0-3 of the role, one block
+      // each, lane = column): right-looking substitution, v[r] accumulates sum_{m<r} A_rm x_m
+      // and becomes x_r when its turn comes (one FMA on the chain per step).
       float* ts = reinterpret_cast<float*>(sm.wt[buf]);  // fp32 T scratch (free: W^T(m-2) consumed)
-      {
-        const int blk = pw, col = lane & 15, r0 = 16 * blk;
-        float x[16];
+      if (pw < 4) {
+        const int col = lane & 15, r0 = 16 * pw;
+        float v[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float s = 0.f;
+        for (int r = 0; r < 16; ++r) v[r] = 0.f;
 #pragma unroll
-          for (int mm = 0; mm + 3 < i; mm += 4) {
-            const float4 a4 = *reinterpret_cast<const float4*>(&sm.a[(r0 + i) * PA + r0 + mm]);
-            s = fmaf(a4.x, x[mm], s);
-            s = fmaf(a4.y, x[mm + 1], s);
-            s = fmaf(a4.z, x[mm + 2], s);
-            s = fmaf(a4.w, x[mm + 3], s);
-          }
+        for (int mm = 0; mm < 16; ++mm) {
+          const float x = mm < col ? 0.f : (mm == col ? 1.f : -v[mm]);
+          v[mm] = x;
 #pragma unroll
-          for (int mm = i & ~3; mm < i; ++mm) s = fmaf(sm.a[(r0 + i) * PA + r0 + mm], x[mm], s);
-          x[i] = i < col ? 0.f : (i == col ? 1.f : -s);
+          for (int r = mm + 1; r < 16; ++r) v[r] = fmaf(sm.a[(r0 + r) * PA + r0 + mm], x, v[r]);
         }
         if (lane < 16) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) ts[tidx(r0 + i, r0 + col)] = x[i];
+          for (int r = 0; r < 16; ++r) ts[tidx(r0 + r, r0 + col)] = v[r];
         }
       }
-      wg_sync(2);
+      role_sync(2);
       // off-diagonal blocks: T_ij = -T_ii (sum_{k=j}^{i-1} A_ik T_kj), in three levels:
       // the two 32x32 diagonal halves (T_10, T_32), then the lower-left 32x32 quarter as
-      // X = A_21 T_1 (four 16x16 blocks, one per warp) and T_21 = -T_2 X.
+      // X = A_21 T_1 and T_21 = -T_2 X. Each warp computes one 16x8 tile (n-tile nt).
       {
         float* scr = reinterpret_cast<float*>(sm.tb);  // 4 x (16 x 24) fp32 scratch blocks
         auto sread = [&](int w) { return [=](int r, int c) { return scr[w * 384 + r * 24 + c]; }; };
@@ -392,44 +374,46 @@ __global__ void __launch_bounds__(NT, 1)
         auto twrite = [&](int bi, int bj) {
           return [=](int r, int c, float x) { ts[tidx(16 * bi + r, 16 * bj + c)] = x; };
         };
-        if (pw < 2) {  // T_10 (warp 0), T_32 (warp 1)
-          const int j = 2 * pw, i = j + 1;
-          float acc[2][4] = {};
-          block_mma(acc, at(i, j), tt(j, j), lane);
-          block_store(acc, 1.f, swrite(pw), lane);
+        const int blk = pw >> 1, nt = pw & 1;
+        if (blk < 2) {  // T_10 (warps 0-1), T_32 (warps 2-3)
+          const int j = 2 * blk, i = j + 1;
+          float acc[4] = {};
+          tile_mma(acc, at(i, j), tt(j, j), nt, lane);
+          tile_store(acc, 1.f, swrite(blk), nt, lane);
           __syncwarp();
-          float acc2[2][4] = {};
-          block_mma(acc2, tt(i, i), sread(pw), lane);
-          block_store(acc2, -1.f, twrite(i, j), lane);
+          float acc2[4] = {};
+          tile_mma(acc2, tt(i, i), sread(blk), nt, lane);
+          tile_store(acc2, -1.f, twrite(i, j), nt, lane);
         }
-        wg_sync(2);
-        const int r = 2 + (pw >> 1), c = pw & 1;
+        role_sync(2);
+        const int r = 2 + (blk >> 1), c = blk & 1;
         {  // X_rc = sum_{k=c}^{1} A_rk T_kc
-          float acc[2][4] = {};
-          for (int k = c; k < 2; ++k) block_mma(acc, at(r, k), tt(k, c), lane);
-          block_store(acc, 1.f, swrite(pw), lane);
+          float acc[4] = {};
+          for (int k = c; k < 2; ++k) tile_mma(acc, at(r, k), tt(k, c), nt, lane);
+          tile_store(acc, 1.f, swrite(blk), nt, lane);
         }
-        wg_sync(2);
+        role_sync(2);
         {  // T_rc = -sum_{k=2}^{r} T_rk X_kc
-          float acc[2][4] = {};
-          for (int k = 2; k <= r; ++k) block_mma(acc, tt(r, k), sread(2 * (k - 2) + c), lane);
-          block_store(acc, -1.f, twrite(r, c), lane);
+          float acc[4] = {};
+          for (int k = 2; k <= r; ++k) tile_mma(acc, tt(r, k), sread(2 * (k - 2) + c), nt, lane);
+          tile_store(acc, -1.f, twrite(r, c), nt, lane);
         }
-        wg_sync(2);
+        role_sync(2);
       }
-      // ---- TB = T diag(beta), TBG = T diag(beta gamma), bf16 rows (zero above the blocks)
+      // ---- TB = T diag(beta), TBG = T diag(beta gamma), bf16 (zero above the blocks);
+      // this thread: row t, columns 16 q .. 16 q + 15
       {
-        const int t = pt >> 1, half = pt & 1;
-        float vb[32], vbg[32];
+        const int t = pt >> 2, q = pt & 3;
+        float vb[16], vbg[16];
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int i = 32 * half + jj;
-          const float x = (i >> 4) <= (t >> 4) ? ts[tidx(t, i)] * sm.beta[sb][i] : 0.f;
+        for (int jj = 0; jj < 16; ++jj) {
+          const int i = 16 * q + jj;
+          const float x = q <= (t >> 4) ? ts[tidx(t, i)] * sm.beta[sb][i] : 0.f;
           vb[jj] = x;
           vbg[jj] = x * sm.gam[sb][i];
         }
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint4 w1, w2;
           w1.x = pack_bf16x2(vb[8 * c], vb[8 * c + 1]);
           w1.y = pack_bf16x2(vb[8 * c + 2], vb[8 * c + 3]);
@@ -439,7 +423,7 @@ __global__ void __launch_bounds__(NT, 1)
           w2.y = pack_bf16x2(vbg[8 * c + 2], vbg[8 * c + 3]);
           w2.z = pack_bf16x2(vbg[8 * c + 4], vbg[8 * c + 5]);
           w2.w = pack_bf16x2(vbg[8 * c + 6], vbg[8 * c + 7]);
-          const uint32_t off = tc::sw128_offset(t, 32 * half + 8 * c);
+          const uint32_t off = tc::sw128_offset(t, 16 * q + 8 * c);
           *reinterpret_cast<uint4*>(sm.tb + off) = w1;  // the tb scratch reads ended at the last barrier
           *reinterpret_cast<uint4*>(sm.tbg + off) = w2;
         }
@@ -462,25 +446,30 @@ __global__ void __launch_bounds__(NT, 1)
         tc::mma_commit(&sm.bar_p3);
       }
       if (!pwait(&sm.bar_p3, m & 1, 4)) break;
-      // ---- W^T -> wt[buf] (bf16, MN-major rows)
+      if (pt == 0 && m + 1 < nchunks) {
+        issue_v(m + 1);
+        last_v = m + 1;
+      }
+      // ---- W^T -> wt[buf] (bf16, MN-major rows): row = dk index, columns 32 hf ..
       {
-        float v[64];
-        tmem_row64(lane_addr + kColD1, v);
-        store_row_bf16(sm.wt[buf], pt, v);
+        float v[32];
+        tmem_row32(lane_addr + kColD1 + 32 * hf, v);
+        store_half_row_bf16(sm.wt[buf], row, hf, v);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
-      // The serial group must have taken chunk m-1 (its first MMA commit) before chunk m is
+      // The serial role must have taken chunk m-1 (its first MMA commit) before chunk m is
       // announced, so the two phases of prep_ready never alias.
       if (m >= 1 && !pwait(&sm.bar_ws, (m - 1) & 1, 5)) break;
       tc::mbar_arrive(&sm.prep_ready);
     }
-    if (pt == 0) {  // every MMA this thread issued completes before TMEM is freed
+    if (pt == 0) {  // our loads land and every MMA this thread issued completes before exit
+      tc::mbar_wait(&sm.bar_v, last_v & 1, 200000000ull);
       tc::mma_commit(&sm.drain_p);
       tc::mbar_wait(&sm.drain_p, 0, 200000000ull);
     }
   } else {
-    // ================================================================ serial warpgroup
+    // ================================================================ serial role
     bool ok = true;
     auto fail = [&](int site) {
       if (tid == 0) {
@@ -490,49 +479,46 @@ __global__ void __launch_bounds__(NT, 1)
       ok = false;
     };
     auto swait = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
-      const bool got = wg_and(1, tc::mbar_wait(bar, parity) && !sm.abort);
+      const bool got = role_and(1, tc::mbar_wait(bar, parity) && !sm.abort);
       if (!got) fail(site);
       tc::fence_after_sync();
       return got;
     };
-    // state in: S^T in TMEM, row = this thread's value column
+    const int j = row;  // this thread's value column (TMEM lane); state columns 64 hf .. + 63
+    // state in: S^T in TMEM
     {
       const float* h0 = p.h0 != nullptr ? p.h0 + slot * p.slot_stride + (int64_t)h * D * D : nullptr;
-      for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int c0 = 64 * hf; c0 < 64 * hf + 64; c0 += 32) {
         uint32_t r[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float x = 0.f;
-          if (h0 != nullptr) x = p.layout == PBK_STATE_KV ? h0[(c0 + i) * D + tid] : h0[tid * D + c0 + i];
+          if (h0 != nullptr) x = p.layout == PBK_STATE_KV ? h0[(c0 + i) * D + j] : h0[j * D + c0 + i];
           r[i] = __float_as_uint(x);
         }
         tc::tmem_st_32x32(lane_addr + kColS + c0, r);
       }
       tc::tmem_st_wait();
     }
-    // S step of chunk n: S^T -> bf16 operand tile; S^T *= gamma_C in TMEM. Then the
-    // S products of chunk n (thread 0).
+    // State step of chunk n: S^T -> bf16 operand tile (atom hf holds dk 64 hf ..); S^T *=
+    // gamma_C in TMEM. Then the S products of chunk n (thread 0).
     auto state_step = [&](int n) {
       const int buf = n & 1, sb = n % 3;
       const float gl = sm.gam[sb][C - 1];
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 64) {
-        float f[64];
-        tmem_row64(lane_addr + kColS + c0, f);
-        uint8_t* tile = sm.st[c0 >> 6];
-        store_row_bf16(tile, tid, f);
+      for (int c = 0; c < 2; ++c) {
+        float f[32];
+        tmem_row32(lane_addr + kColS + 64 * hf + 32 * c, f);
+        store_half_row_bf16(sm.st[hf], j, c, f);
+        uint32_t r[32];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t r[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(f[32 * half + i] * gl);
-          tc::tmem_st_32x32(lane_addr + kColS + c0 + 32 * half, r);
-        }
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(f[i] * gl);
+        tc::tmem_st_32x32(lane_addr + kColS + 64 * hf + 32 * c, r);
       }
       tc::tmem_st_wait();
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
-      wg_sync(1);
+      role_sync(1);
       if (tid == 0) {
         tc::fence_after_sync();
         for (int kk = 0; kk < 8; ++kk) {
@@ -549,29 +535,29 @@ __global__ void __launch_bounds__(NT, 1)
         tc::mma_commit(&sm.bar_ws);
       }
     };
+    int last_kq[2] = {0, nchunks > 1 ? 1 : -1};  // last K|Q load per buffer (for the drain)
     if (swait(&sm.prep_ready, 0, 1)) state_step(0);
     for (int n = 0; n < nchunks && ok; ++n) {
       const int buf = n & 1, sb = n % 3;
-      // U = U' - WS -> U^T bf16; then UM^T = U^T M^T and S^T += (U diag(e))^T K
+      // U = U' - WS -> U^T bf16 (ut) and U diag(e) (st[0], free: the S^T products are
+      // done); then UM^T = U^T M^T and S^T += (U diag(e))^T K. This thread: t = 32 hf ..
       if (tid == 0) tc::bulk_wait_read0();  // the output store of chunk n-1 has read ut
       if (!swait(&sm.bar_ws, n & 1, 2)) break;
       {
-        float ws[64], up[64];
-        tmem_row64(lane_addr + kColWS, ws);
-        tmem_row64(lane_addr + kColUP + 64 * buf, up);
+        float ws[32], up[32];
+        tmem_row32(lane_addr + kColWS + 32 * hf, ws);
+        tmem_row32(lane_addr + kColUP + 64 * buf + 32 * hf, up);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) up[i] -= ws[i];
-        store_row_bf16(sm.ut, tid, up);
-        // U diag(e) -> st[0] (free: the S^T products of this chunk are done), the A
-        // operand of the state update
-        const float* ee = sm.ee[sb];
+        for (int i = 0; i < 32; ++i) up[i] -= ws[i];
+        store_half_row_bf16(sm.ut, j, hf, up);
+        const float* ee = sm.ee[sb] + 32 * hf;
 #pragma unroll
-        for (int i = 0; i < 64; ++i) up[i] *= ee[i];
-        store_row_bf16(sm.st[0], tid, up);
+        for (int i = 0; i < 32; ++i) up[i] *= ee[i];
+        store_half_row_bf16(sm.st[0], j, hf, up);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
-      wg_sync(1);
+      role_sync(1);
       if (tid == 0) {
         tc::fence_after_sync();
         for (int kk = 0; kk < 4; ++kk) {
@@ -587,36 +573,42 @@ __global__ void __launch_bounds__(NT, 1)
         tc::mma_commit(&sm.bar_s);
       }
       if (!swait(&sm.bar_s, n & 1, 3)) break;
-      // O = gamma scale QS + UM (registers), then the next chunk's state step, then the
-      // stores of O through shared memory (ut is free: U products are done).
-      float o[64];
+      if (tid == 0 && n + 2 < nchunks) {  // chunk n's K|Q buffer is free for chunk n+2
+        issue_kq(n + 2);
+        last_kq[buf] = n + 2;
+      }
+      // O = gamma scale QS + UM (registers; t = 32 hf + i), then the next chunk's state
+      // step, then O through shared memory and a TMA store.
+      float o[32];
       {
-        float um[64];
-        tmem_row64(lane_addr + kColQS, o);
-        tmem_row64(lane_addr + kColUM, um);
-        const float* gm = sm.gam[sb];
+        float um[32];
+        tmem_row32(lane_addr + kColQS + 32 * hf, o);
+        tmem_row32(lane_addr + kColUM + 32 * hf, um);
+        const float* gm = sm.gam[sb] + 32 * hf;
 #pragma unroll
-        for (int t = 0; t < 64; ++t) o[t] = fmaf(gm[t] * p.scale, o[t], um[t]);
+        for (int t = 0; t < 32; ++t) o[t] = fmaf(gm[t] * p.scale, o[t], um[t]);
       }
       tc::fence_before_sync();
       if (n + 1 < nchunks) {
         if (!swait(&sm.prep_ready, (n + 1) & 1, 4)) break;
         state_step(n + 1);
       }
-      // O through shared memory (ut, row-major [rows][128]) and a TMA store; rows past
-      // the sequence end fall outside the tensor and are not written.
+      // staging in ut as row-major [rows][128]; rows past the sequence end fall outside
+      // the tensor and are not written by the store
       constexpr int kRows = sizeof(TOut) == 2 ? 64 : 32;  // 16 KB per pass
       TOut* stage = reinterpret_cast<TOut*>(sm.ut);
 #pragma unroll
       for (int t0 = 0; t0 < 64; t0 += kRows) {
         if (t0 > 0) {
           if (tid == 0) tc::bulk_wait_read0();
-          wg_sync(1);
+          role_sync(1);
         }
+        if (32 * hf >= t0 && 32 * hf < t0 + kRows) {
 #pragma unroll
-        for (int t = 0; t < kRows; ++t) stage[t * D + tid] = from_f32<TOut>(o[t0 + t]);
+          for (int t = 0; t < 32; ++t) stage[(32 * hf - t0 + t) * D + j] = from_f32<TOut>(o[t]);
+        }
         tc::fence_proxy_async_smem();
-        wg_sync(1);
+        role_sync(1);
         if (tid == 0) {
           tc::tma_store_4d(&tm_o, stage, 0, n * C + t0, h, b);
           tc::bulk_commit();
@@ -624,28 +616,30 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
     if (tid == 0) tc::bulk_wait0();
-    if (tid == 0) {  // every MMA this thread issued completes before TMEM is freed
+    if (tid == 0) {  // our loads land and every MMA this thread issued completes before exit
+      for (int bb = 0; bb < 2; ++bb)
+        if (last_kq[bb] >= 0) tc::mbar_wait(&sm.bar_kq[bb], (last_kq[bb] >> 1) & 1, 200000000ull);
       tc::mma_commit(&sm.drain_s);
       tc::mbar_wait(&sm.drain_s, 0, 200000000ull);
     }
     if (ok) {
-      // state out
+      // state out: columns 64 hf .. + 63 of row j of S^T
       float* st = p.state + slot * p.slot_stride + (int64_t)h * D * D;
-      for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int c0 = 64 * hf; c0 < 64 * hf + 64; c0 += 32) {
         uint32_t r[32];
         tc::tmem_ld_32x32(lane_addr + kColS + c0, r);
         tc::tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          if (p.layout == PBK_STATE_KV) st[(c0 + i) * D + tid] = __uint_as_float(r[i]);
-          else st[tid * D + c0 + i] = __uint_as_float(r[i]);
+          if (p.layout == PBK_STATE_KV) st[(c0 + i) * D + j] = __uint_as_float(r[i]);
+          else st[j * D + c0 + i] = __uint_as_float(r[i]);
         }
       }
     }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 0) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
