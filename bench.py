@@ -1,6 +1,7 @@
 """Benchmark of the PseudoBrain hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload all|prefill|decode|quest] [--size full|small]
 
 Headline (``value``): GDN chunked prefill of BASELINE config 1 (B=4, T=32768, 16 key /
 32 value heads, dk=dv=128, chunk 64, bf16 q/k/v/beta, fp32 g and state) in tok/s,
@@ -15,8 +16,9 @@ Multi-GPU (torchrun, one rank per GPU): weak scaling. Every rank runs its own sh
 exchange step, so there is no collective inside the timed region.
 
 ``--impl reference`` times the CPU restatement of the reference algorithm (oracle/,
-numpy, all host cores) on bounded samples of the same workloads and prints the same
-metric; under torchrun only rank 0 runs it.
+numpy, all host cores) on bounded samples of the same workload and prints the same
+metric; under torchrun only rank 0 runs it. ``--workload``/``--size small`` run one part
+on a reduced case, for profiler captures only (such a line is not a bench number).
 """
 from __future__ import annotations
 
@@ -32,9 +34,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GDN prefill tok/s & decode steps/s per B200; Quest q/s; % TC/HBM roofline"
-PREFILL = dict(batch=4, seqlen=32768, hk=16, hv=32, dk=128, dv=128, chunk=64)
-DECODE = dict(batch=256, hk=16, hv=32, dk=128, dv=128, steps_per_rep=1000)
-QUEST = dict(n_tokens=1 << 20, kv=8, heads=32, d=128, page=16, window=4096, nq=8, budget_tokens=4096)
+PREFILL = {"full": dict(batch=4, seqlen=32768), "small": dict(batch=1, seqlen=8192)}
+PREFILL_HEADS = dict(hk=16, hv=32, dk=128, dv=128, chunk=64)
+DECODE = {"full": dict(batch=256), "small": dict(batch=64)}
+DECODE_HEADS = dict(hk=16, hv=32, dk=128, dv=128)
+QUEST = {"full": dict(n_tokens=1 << 20), "small": dict(n_tokens=1 << 19)}
+QUEST_SHAPE = dict(kv=8, heads=32, d=128, page=16, window=4096, nq=8, budget_tokens=4096)
 
 
 def prefill_flops_per_token_head(c=64, d=128):
@@ -52,7 +57,8 @@ def peaks():
 
 
 def traffic(kernel_key):
-    """DRAM bytes per launch from the committed ncu summary (profiles/traffic.txt), or None."""
+    """DRAM bytes per launch of the bench workload from the committed ncu summary
+    (profiles/traffic.txt: `<kernel> <bytes per launch>` lines), or None."""
     path = os.path.join(ROOT, "profiles", "traffic.txt")
     if not os.path.exists(path):
         return None
@@ -109,131 +115,150 @@ class Clocks:
 # --------------------------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------------------------
-def run_ours(args, rank, world, local_rank):
-    import torch
-    import torch.distributed as dist
-    from pseudobrain_b200 import gated_deltanet as G
-    from pseudobrain_b200 import exact_memory as M
-    from pseudobrain_b200.gdn_prefill import gdn_prefill_
-    from pseudobrain_b200.synthetic import gdn_inputs, quest_inputs
+class Timer:
+    """Device time of K calls after W warm-ups, bracketed by barrier + synchronize on both
+    sides, CUDA events on the launching stream, max over ranks."""
 
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    pk = peaks()
+    def __init__(self, torch, dist, dev, world):
+        self.torch, self.dist, self.dev, self.world = torch, dist, dev, world
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
 
-    def max_over_ranks(x):
-        if world == 1:
+    def max_over_ranks(self, x):
+        if self.world == 1:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
-    def timed(fn, steps, warmup, events_stream=None):
-        """Device time of `steps` calls after `warmup`, bracketed by barrier + synchronize."""
+    def __call__(self, fn, steps, warmup):
+        torch = self.torch
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
-        barrier()
+        self.barrier()
         torch.cuda.synchronize()
+        s = torch.cuda.current_stream(self.dev)
         st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s = torch.cuda.current_stream(dev)
         st.record(s)
         for _ in range(steps):
             fn()
         en.record(s)
         torch.cuda.synchronize()
-        barrier()
-        return max_over_ranks(st.elapsed_time(en) / 1e3)
+        self.barrier()
+        return self.max_over_ranks(st.elapsed_time(en) / 1e3)
 
-    # ---------------- prefill (headline, config 1) ----------------
-    P = PREFILL
+
+def measure_prefill(args, timed, dev, rank, world, pk):
+    import torch
+    from pseudobrain_b200.gdn_prefill import gdn_prefill_
+    from pseudobrain_b200.synthetic import gdn_inputs
+    P = {**PREFILL[args.size], **PREFILL_HEADS}
     x = gdn_inputs(P["batch"], P["seqlen"], P["hk"], P["hv"], device=dev, seed=1 + 1000 * rank)
     state = torch.empty(P["batch"], P["hv"], P["dk"], P["dv"], device=dev)
     o = torch.empty(P["batch"], P["seqlen"], P["hv"], P["dv"], device=dev, dtype=torch.bfloat16)
 
-    def prefill_step():
+    def step():
         gdn_prefill_(x["q"], x["k"], x["v"], x["g"], x["beta"], None, state, o, x["scale"])
 
-    with Clocks(local_rank) as clk:
-        t_prefill = timed(prefill_step, args.steps, args.warmup)
+    t = timed(step, args.steps, args.warmup)
     tokens = P["batch"] * P["seqlen"]
-    value = world * tokens * args.steps / t_prefill
-    ms_per_step = t_prefill / args.steps * 1e3
+    per_step = t / args.steps
     flops = tokens * P["hv"] * prefill_flops_per_token_head(P["chunk"], P["dk"])
-    achieved_tf = flops / (t_prefill / args.steps) / 1e12
+    achieved = flops / per_step / 1e12
     algo_bytes = (2 * tokens * P["hk"] * P["dk"] * 2 + tokens * P["hv"] * P["dv"] * 2 * 2 + tokens * P["hv"] * 6
                   + 2 * P["batch"] * P["hv"] * P["dk"] * P["dv"] * 4)
-
     # e2e through the public API: pinned host inputs in, bf16 outputs back, every step
     host = {n: x[n].cpu().pin_memory() for n in ("q", "k", "v", "g", "beta")}
     dev_in = {n: torch.empty_like(x[n]) for n in host}
     host_o = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = host_o.numel() * host_o.element_size()
 
-    def prefill_e2e():
-        for n, t in host.items():
-            dev_in[n].copy_(t, non_blocking=True)
+    def e2e():
+        for n, tt in host.items():
+            dev_in[n].copy_(tt, non_blocking=True)
         gdn_prefill_(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], None, state, o, x["scale"])
         host_o.copy_(o, non_blocking=True)
 
     e2e_steps = max(3, args.steps // 2)
-    t_e2e = timed(prefill_e2e, e2e_steps, min(args.warmup, 3))
-    del x, dev_in, host, host_o, o, state
-    torch.cuda.empty_cache()
+    t_e2e = timed(e2e, e2e_steps, min(args.warmup, 3))
+    return {
+        "value": world * tokens * args.steps / t, "unit": "tok/s", "ms_per_step": per_step * 1e3,
+        "tokens": tokens,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["tc_sustained"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["tc_sustained"], "traffic": traffic("gdn_prefill_tc_kernel"),
+                     "peak_source": f"{pk['src']} bf16 sustained", "algorithmic_bytes": algo_bytes,
+                     "hbm_frac": algo_bytes / per_step / 1e9 / pk["hbm"]},
+        "e2e": {"value": world * tokens * e2e_steps / t_e2e, "unit": "tok/s",
+                "h2d_bytes_per_step": sum(tt.numel() * tt.element_size() for tt in host.values()),
+                "d2h_bytes_per_step": host_o.numel() * host_o.element_size()},
+        "gpu_launches": args.steps,
+    }
 
-    # ---------------- decode (config 2) ----------------
-    D = DECODE
+
+def measure_decode(args, timed, dev, rank, world, pk):
+    import torch
+    from pseudobrain_b200 import gated_deltanet as G
+    from pseudobrain_b200.synthetic import gdn_inputs
+    D = {**DECODE[args.size], **DECODE_HEADS}
     xd = gdn_inputs(D["batch"], 1, D["hk"], D["hv"], device=dev, seed=2 + 1000 * rank, g_dtype=torch.bfloat16,
                     state_std=0.02)
     od = torch.empty(D["batch"], 1, D["hv"], D["dv"], device=dev, dtype=torch.bfloat16)
 
-    def decode_step():
+    def step():
         G.gdn_recurrent_(xd["q"], xd["k"], xd["v"], xd["g"], xd["beta"], None, xd["h0"], od, xd["scale"])
 
-    dsteps = D["steps_per_rep"]
-    t_dec = timed(decode_step, dsteps, max(args.warmup, 10))
-    dec_value = world * dsteps / t_dec
-    dec_bytes = 2 * xd["h0"].numel() * 4 + sum(xd[n].numel() * xd[n].element_size() for n in ("q", "k", "v", "g", "beta")) \
-        + od.numel() * 2
-    hostd = {n: xd[n].cpu().pin_memory() for n in ("q", "k", "v", "g", "beta")}
-    devd = {n: torch.empty_like(xd[n]) for n in hostd}
-    host_od = torch.empty(od.shape, dtype=od.dtype, pin_memory=True)
+    nsteps = 1000 if args.size == "full" else 20  # config 2: 1000 sequential in-place steps
+    t = timed(step, nsteps, max(args.warmup, 10))
+    per_step = t / nsteps
+    nbytes = 2 * xd["h0"].numel() * 4 + sum(xd[n].numel() * xd[n].element_size()
+                                            for n in ("q", "k", "v", "g", "beta")) + od.numel() * 2
+    host = {n: xd[n].cpu().pin_memory() for n in ("q", "k", "v", "g", "beta")}
+    dev_in = {n: torch.empty_like(xd[n]) for n in host}
+    host_o = torch.empty(od.shape, dtype=od.dtype, pin_memory=True)
 
-    def decode_e2e():
-        for n, t in hostd.items():
-            devd[n].copy_(t, non_blocking=True)
-        G.gdn_recurrent_(devd["q"], devd["k"], devd["v"], devd["g"], devd["beta"], None, xd["h0"], od, xd["scale"])
-        host_od.copy_(od, non_blocking=True)
+    def e2e():
+        for n, tt in host.items():
+            dev_in[n].copy_(tt, non_blocking=True)
+        G.gdn_recurrent_(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], None, xd["h0"], od,
+                         xd["scale"])
+        host_o.copy_(od, non_blocking=True)
 
-    t_dec_e2e = timed(decode_e2e, 200, 10)
-    dec_h2d = sum(t.numel() * t.element_size() for t in hostd.values())
-    del xd, devd, hostd, od
-    torch.cuda.empty_cache()
+    t_e2e = timed(e2e, 200, 10)
+    return {
+        "metric": "GDN decode steps/s (config 2)", "value": world * nsteps / t, "unit": "steps/s",
+        "us_per_step": per_step * 1e6,
+        "roofline": {"bound": "hbm", "achieved": nbytes / per_step / 1e9, "peak": pk["hbm"], "unit": "GB/s",
+                     "frac": nbytes / per_step / 1e9 / pk["hbm"], "traffic": traffic("gdn_decode_kernel"),
+                     "algorithmic_bytes": nbytes},
+        "e2e": {"value": world * 200 / t_e2e, "unit": "steps/s",
+                "h2d_bytes_per_step": sum(tt.numel() * tt.element_size() for tt in host.values()),
+                "d2h_bytes_per_step": host_o.numel() * host_o.element_size()},
+        "gpu_launches": nsteps,
+    }
 
-    # ---------------- Quest (config 3) ----------------
-    Q = QUEST
-    xq = quest_inputs(device=dev, seed=3 + 1000 * rank, **{k: Q[k] for k in Q})
+
+def measure_quest(args, timed, dev, rank, world, pk):
+    import torch
+    from pseudobrain_b200 import exact_memory as M
+    from pseudobrain_b200.synthetic import quest_inputs
+    Q = {**QUEST[args.size], **QUEST_SHAPE}
+    xq = quest_inputs(device=dev, seed=3 + 1000 * rank, **Q)
     kv, npages = Q["kv"], xq["kmax"].shape[1]
-    ws_pages = torch.empty(Q["nq"], kv, xq["budget"], dtype=torch.int32, device=dev)
 
-    def quest_step():
+    def step():
         pages = M.select_pages(xq["q"], xq["kmax"], xq["kmin"], xq["n_arch"], xq["page"], xq["budget"])
         M.attend_pages(xq["q"], xq["qpos"], xq["keys"], xq["values"], xq["n_arch"], xq["page"], pages,
                        xq["win_keys"], xq["win_values"], xq["kpos"], xq["window"])
 
     qsteps = max(args.steps, 20)
-    t_q = timed(quest_step, qsteps, max(args.warmup, 3))
-    q_value = world * Q["nq"] * qsteps / t_q
+    t = timed(step, qsteps, max(args.warmup, 3))
+    per_step = t / qsteps
     bound_bytes = 2 * npages * kv * Q["d"] * 2
     page_bytes = xq["budget"] * Q["page"] * kv * Q["d"] * 2 * 2
     win_bytes = Q["window"] * kv * Q["d"] * 2 * 2
-    quest_bytes = bound_bytes + Q["nq"] * page_bytes + win_bytes
-    # score kernel alone
+    nbytes = bound_bytes + Q["nq"] * page_bytes + win_bytes
     scores = torch.empty(Q["nq"], kv, npages, device=dev)
     t_sel = timed(lambda: M.select_pages(xq["q"], xq["kmax"], xq["kmin"], xq["n_arch"], xq["page"], xq["budget"],
                                          scores=scores), qsteps, 3)
@@ -241,55 +266,67 @@ def run_ours(args, rank, world, local_rank):
     host_out = torch.empty(Q["nq"], 1, Q["heads"], Q["d"], pin_memory=True)
     dev_q = torch.empty_like(xq["q"])
 
-    def quest_e2e():
+    def e2e():
         dev_q.copy_(host_q, non_blocking=True)
         pages = M.select_pages(dev_q, xq["kmax"], xq["kmin"], xq["n_arch"], xq["page"], xq["budget"])
         out = M.attend_pages(dev_q, xq["qpos"], xq["keys"], xq["values"], xq["n_arch"], xq["page"], pages,
                              xq["win_keys"], xq["win_values"], xq["kpos"], xq["window"])
         host_out.copy_(out, non_blocking=True)
 
-    t_q_e2e = timed(quest_e2e, qsteps, 3)
-    del xq, scores
-    torch.cuda.empty_cache()
+    t_e2e = timed(e2e, qsteps, 3)
+    return {
+        "metric": "Quest q/s (config 3)", "value": world * Q["nq"] * qsteps / t, "unit": "q/s",
+        "us_per_batch": per_step * 1e6,
+        "roofline": {"bound": "hbm", "achieved": nbytes / per_step / 1e9, "peak": pk["hbm"], "unit": "GB/s",
+                     "frac": nbytes / per_step / 1e9 / pk["hbm"], "traffic": traffic("quest_score_tc_kernel"),
+                     "algorithmic_bytes": nbytes},
+        "select_gbps": bound_bytes / (t_sel / qsteps) / 1e9,
+        "e2e": {"value": world * Q["nq"] * qsteps / t_e2e, "unit": "q/s",
+                "h2d_bytes_per_step": host_q.numel() * 2, "d2h_bytes_per_step": host_out.numel() * 4},
+        "gpu_launches": 4 * qsteps,
+    }
 
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    pk = peaks()
+    timed = Timer(torch, dist, dev, world)
+    parts = {}
+    clk = Clocks(local_rank)
+    for name, fn in (("prefill", measure_prefill), ("decode", measure_decode), ("quest", measure_quest)):
+        if args.workload in ("all", name):
+            if name == "prefill":
+                with clk:
+                    parts[name] = fn(args, timed, dev, rank, world, pk)
+            else:
+                parts[name] = fn(args, timed, dev, rank, world, pk)
+            torch.cuda.empty_cache()
     if rank != 0:
         return None
-    tr = traffic("gdn_prefill")
+    head = parts.get("prefill") or next(iter(parts.values()))
+    ms = head.get("ms_per_step")
+    if ms is None:
+        ms = head.get("us_per_step", head.get("us_per_batch", 0.0)) / 1e3
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 inputs, fp32 state/accumulation", "data": "synthetic (seeded, BASELINE config distributions)",
-        "config": {"workload": "BASELINE config 1: GDN chunked prefill B=4 T=32768 Hk=16 Hv=32 dk=dv=128 chunk=64 per GPU",
-                   "global_batch": P["batch"] * world, "seq_len": P["seqlen"],
+        "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 inputs, fp32 state/accumulation", "data": "synthetic (seeded, BASELINE config distributions)",
+        "config": {"workload": ("BASELINE config 1: GDN chunked prefill B=4 T=32768 Hk=16 Hv=32 dk=dv=128 chunk=64 "
+                                "per GPU") if "prefill" in parts else f"{args.workload} part only",
+                   "size": args.size, "global_batch": PREFILL[args.size]["batch"] * world,
+                   "seq_len": PREFILL[args.size]["seqlen"],
                    "parallelism": f"(sequence x value-head) shards, {world} GPU(s), no collective",
-                   "l2": "inputs 1.6 GB per step, larger than L2 (126 MB)"},
-        "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": pk["tc_sustained"], "unit": "TFLOP/s",
-                     "frac": achieved_tf / pk["tc_sustained"], "traffic": tr,
-                     "peak_source": f"{pk['src']} bf16 sustained", "algorithmic_bytes": algo_bytes,
-                     "hbm_frac": algo_bytes / (t_prefill / args.steps) / 1e9 / pk["hbm"]},
-        "e2e": {"value": world * tokens * e2e_steps / t_e2e, "unit": "tok/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
+                   "l2": "inputs larger than L2 (126 MB) in every timed part"},
+        "roofline": head["roofline"], "e2e": head["e2e"], "gpu_launches": head["gpu_launches"],
         "clocks": clk.summary(),
-        "decode": {"metric": "GDN decode steps/s (config 2)", "value": dec_value, "unit": "steps/s",
-                   "us_per_step": t_dec / dsteps * 1e6,
-                   "roofline": {"bound": "hbm", "achieved": dec_bytes / (t_dec / dsteps) / 1e9, "peak": pk["hbm"],
-                                "unit": "GB/s", "frac": dec_bytes / (t_dec / dsteps) / 1e9 / pk["hbm"],
-                                "traffic": traffic("gdn_decode")},
-                   "e2e": {"value": world * 200 / t_dec_e2e, "unit": "steps/s", "h2d_bytes_per_step": dec_h2d,
-                           "d2h_bytes_per_step": host_od.numel() * 2},
-                   "gpu_launches": dsteps},
-        "quest": {"metric": "Quest q/s (config 3)", "value": q_value, "unit": "q/s",
-                  "us_per_batch": t_q / qsteps * 1e6,
-                  "roofline": {"bound": "hbm", "achieved": quest_bytes / (t_q / qsteps) / 1e9, "peak": pk["hbm"],
-                               "unit": "GB/s", "frac": quest_bytes / (t_q / qsteps) / 1e9 / pk["hbm"],
-                               "traffic": traffic("quest_score")},
-                  "select_gbps": bound_bytes / (t_sel / qsteps) / 1e9,
-                  "e2e": {"value": world * Q["nq"] * qsteps / t_q_e2e, "unit": "q/s",
-                          "h2d_bytes_per_step": host_q.numel() * 2, "d2h_bytes_per_step": host_out.numel() * 4},
-                  "gpu_launches": 4 * qsteps},
     }
-    if world == 1 and not args.no_cpu_baseline:
+    for name in ("decode", "quest"):
+        if name in parts and parts[name] is not head:
+            line[name] = parts[name]
+    if world == 1 and not args.no_cpu_baseline and "prefill" in parts:
         line["cpu_baseline"] = cpu_baseline(samples=1)
     return line
 
@@ -314,7 +351,7 @@ def cpu_baseline(samples=1):
     from oracle import gdn as ogdn
     cores = _cpu_threads()
     rng = np.random.default_rng(0)
-    t, hk, hv = 4096, PREFILL["hk"], PREFILL["hv"]
+    t, hk, hv = 4096, PREFILL_HEADS["hk"], PREFILL_HEADS["hv"]
 
     def unit(shape):
         a = rng.standard_normal(shape, dtype=np.float32)
@@ -358,6 +395,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=("all", "prefill", "decode", "quest"), default="all",
+                    help="run one part only (profiling); the JSON line then carries that part")
+    ap.add_argument("--size", choices=("full", "small"), default="full",
+                    help="small: a reduced case of the same kernels for ncu captures (not a bench number)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

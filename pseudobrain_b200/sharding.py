@@ -1,0 +1,79 @@
+"""(sequence x value-head) sharding of the gated delta rule over the GPUs of one node.
+
+The recurrence of every (sequence, value head) chain is independent
+(pseudobrain/gated_deltanet.py:110-165 runs each [b, h] on its own), so a rank can own any
+subset of chains with no exchange inside the recurrence. Two layouts:
+
+* batch shard: rank r owns sequences [r B/N, (r+1) B/N) with all heads -- its outputs are
+  already in the model's layout; nothing is exchanged (the weak-scaling bench).
+* head shard: every rank holds the same tokens and owns value heads
+  [r Hv/N, (r+1) Hv/N) with the key heads they read (Hv/N a multiple of the GQA ratio,
+  so no key head is split); one all-gather over the process group (NCCL over NVLink on a
+  node) restores the [B, T, Hv, V] outputs and [B, Hv, K, V] states.
+
+``prefill`` is the per-rank kernel: pseudobrain_b200.gdn_prefill.gdn_prefill by default.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def batch_shard(batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Sequences [b0, b1) of `rank` when `batch` sequences are split over `world` ranks."""
+    if batch % world:
+        raise ValueError(f"batch {batch} does not split over {world} ranks")
+    per = batch // world
+    return rank * per, (rank + 1) * per
+
+
+def head_shard(hv: int, hk: int, world: int, rank: int) -> tuple[int, int, int, int]:
+    """(v0, v1, k0, k1): the value heads of `rank` and the key heads they read."""
+    if hv % hk or hv % world:
+        raise ValueError(f"{hv} value heads do not split over {world} ranks")
+    ratio, per = hv // hk, hv // world
+    if per % ratio:
+        raise ValueError(f"{per} value heads per rank would split a key head shared by {ratio} value heads")
+    v0, v1 = rank * per, (rank + 1) * per
+    return v0, v1, v0 // ratio, v1 // ratio
+
+
+def gdn_prefill_head_sharded(q, k, v, g, beta, scale, h0=None, group=None, prefill=None):
+    """Chunked gated delta rule with the value heads split over the ranks of `group`.
+
+    Every rank passes the full q, k [B,T,Hk,K], v [B,T,Hv,V], g, beta [B,T,Hv] and h0
+    [B,Hv,K,V] (or None); each computes its own heads and the outputs are all-gathered.
+    Returns (o [B,T,Hv,V], final state [B,Hv,K,V]) on every rank."""
+    if prefill is None:
+        from .gdn_prefill import gdn_prefill as prefill
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    b, t, hk, _ = q.shape
+    hv = v.shape[2]
+    v0, v1, k0, k1 = head_shard(hv, hk, world, rank)
+    o_loc, s_loc = prefill(q[:, :, k0:k1], k[:, :, k0:k1], v[:, :, v0:v1], g[:, :, v0:v1], beta[:, :, v0:v1], scale,
+                           None if h0 is None else h0[:, v0:v1])
+    # rank blocks concatenated along dim 0 (the layout every backend accepts), then viewed
+    # as [N, ...]
+    o_all = torch.empty((world * o_loc.shape[0],) + tuple(o_loc.shape[1:]), dtype=o_loc.dtype, device=o_loc.device)
+    s_all = torch.empty((world * s_loc.shape[0],) + tuple(s_loc.shape[1:]), dtype=s_loc.dtype, device=s_loc.device)
+    dist.all_gather_into_tensor(o_all, o_loc.contiguous(), group=group)
+    dist.all_gather_into_tensor(s_all, s_loc.contiguous(), group=group)
+    o_all = o_all.view((world,) + tuple(o_loc.shape))
+    s_all = s_all.view((world,) + tuple(s_loc.shape))
+    # [N, B, T, Hv/N, V] -> [B, T, Hv, V];  [N, B, Hv/N, K, V] -> [B, Hv, K, V]
+    o = o_all.permute(1, 2, 0, 3, 4).reshape(b, t, hv, o_loc.shape[-1])
+    s = s_all.permute(1, 0, 2, 3, 4).reshape(b, hv, s_loc.shape[-2], s_loc.shape[-1])
+    return o, s
+
+
+def gdn_prefill_batch_sharded(q, k, v, g, beta, scale, h0=None, group=None, prefill=None):
+    """Chunked gated delta rule on this rank's sequences only (no exchange): returns the
+    (o, state) of sequences batch_shard(B, world, rank)."""
+    if prefill is None:
+        from .gdn_prefill import gdn_prefill as prefill
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    b0, b1 = batch_shard(q.shape[0], world, rank)
+    return prefill(q[b0:b1], k[b0:b1], v[b0:b1], g[b0:b1], beta[b0:b1], scale,
+                   None if h0 is None else h0[b0:b1])
