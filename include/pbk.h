@@ -205,6 +205,28 @@ PBK_API int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d,
                              int64_t key_stride_kv, int64_t key_stride_n, void* kmax, void* kmin,
                              int64_t bnd_stride_kv, int64_t bnd_stride_p, int32_t first_page, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Causal sliding-window attention with sinks (the hybrid model's attention branch,
+ * pseudobrain/transplant.py:417-436 causal_attention and its exact chunked form
+ * :346-362). Query t of head j sees key s of key head j / (h / kv) when
+ *   s <= t  and  (window <= 0  or  t - s < window  or  s < sinks),
+ * with softmax(scale * q.k) over the visible keys (scale = d**-0.5 for SDPA's
+ * default). window <= 0 is full causal attention.
+ * q, o [B, T, h, d] and k, v [B, T, kv, d] as strided views (the reference's
+ * [B, H, T, d] is the same tensor with other strides); q/k/v bf16, o bf16 or fp32.
+ * Requires d == 128, h a multiple of kv, 16-byte aligned pointers and strides.
+ * ------------------------------------------------------------------------ */
+typedef struct pbk_swa_desc {
+  int32_t batch, seqlen, h, kv, d;
+  int32_t window;  /* keys per query including itself; <= 0: unbounded */
+  int32_t sinks;   /* leading positions every query sees */
+  float scale;
+  pbk_view q, k, v;
+  pbk_view o;      /* output; data is written */
+} pbk_swa_desc;
+
+PBK_API int pbk_swa_prefill(const pbk_swa_desc* desc, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

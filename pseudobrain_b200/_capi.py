@@ -53,6 +53,12 @@ class PbkQuestDesc(ctypes.Structure):
                 ("out_stride_h", ctypes.c_int64), ("out_dtype", ctypes.c_int32), ("pad_", ctypes.c_int32)]
 
 
+class PbkSwaDesc(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("h", ctypes.c_int32), ("kv", ctypes.c_int32),
+                ("d", ctypes.c_int32), ("window", ctypes.c_int32), ("sinks", ctypes.c_int32), ("scale", ctypes.c_float),
+                ("q", PbkView), ("k", PbkView), ("v", PbkView), ("o", PbkView)]
+
+
 _QD = ctypes.POINTER(PbkQuestDesc)
 _VP, _I32, _I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
 
@@ -72,6 +78,7 @@ SIGNATURES = {
     "pbk_quest_attend": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_gather": (ctypes.c_int, [_QD, _I32, _VP, _VP, _VP]),
     "pbk_quest_bounds": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I64, _I64, _VP, _VP, _I64, _I64, _I32, _VP]),
+    "pbk_swa_prefill": (ctypes.c_int, [ctypes.POINTER(PbkSwaDesc), _VP]),
 }
 
 

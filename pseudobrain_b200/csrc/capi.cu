@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "quest.cuh"
+#include "swa.cuh"
 
 namespace pbk {
 cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st);
@@ -58,6 +59,26 @@ bool aligned_elems(int64_t stride, int64_t elems) { return stride % elems == 0; 
 
 // Shapes, pointers and alignment shared by the Quest entry points. `need` selects
 // which tensors must be present: 1 select, 2 attend, 4 gather.
+int validate_swa(const pbk_swa_desc* d) {
+  if (d == nullptr) return PBK_ERR_INVALID;
+  if (d->batch < 0 || d->seqlen < 0 || d->h < 1 || d->kv < 1 || d->sinks < 0 || !(d->scale > 0.f))
+    return PBK_ERR_INVALID;
+  if (d->h % d->kv != 0 || d->d != 128) return PBK_ERR_SHAPE;
+  if (d->q.dtype != PBK_BF16 || d->k.dtype != PBK_BF16 || d->v.dtype != PBK_BF16 || !dtype_ok(d->o.dtype))
+    return PBK_ERR_DTYPE;
+  if (d->batch == 0 || d->seqlen == 0) return PBK_OK;
+  const pbk_view* in[3] = {&d->q, &d->k, &d->v};
+  for (const pbk_view* v : in) {
+    if (v->data == nullptr) return PBK_ERR_INVALID;
+    if (v->stride_b <= 0 || v->stride_t <= 0 || v->stride_h <= 0) return PBK_ERR_INVALID;
+    if (!aligned16(v->data) || v->stride_b % 8 || v->stride_t % 8 || v->stride_h % 8) return PBK_ERR_ALIGN;
+  }
+  const int64_t ev = d->o.dtype == PBK_BF16 ? 8 : 4;  // elements per 16 bytes
+  if (d->o.data == nullptr) return PBK_ERR_INVALID;
+  if (!aligned16(d->o.data) || d->o.stride_b % ev || d->o.stride_t % ev || d->o.stride_h % ev) return PBK_ERR_ALIGN;
+  return PBK_OK;
+}
+
 int validate_quest(const pbk_quest_desc* d, int need) {
   if (d == nullptr) return PBK_ERR_INVALID;
   if (d->nq < 0 || d->t < 1 || d->kv < 1 || d->h < d->kv || d->page < 1 || d->n_arch < 0 || d->budget < 0 ||
@@ -228,6 +249,14 @@ int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d, int32_t
   if (st != PBK_OK) return st;
   return launch_status(pbk::launch_quest_bounds(keys, kv, n, page, key_stride_kv, key_stride_n, kmax, kmin, bnd_stride_kv,
                                   bnd_stride_p, first_page, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_swa_prefill(const pbk_swa_desc* desc, void* stream) {
+  int st = validate_swa(desc);
+  if (st != PBK_OK || desc->batch == 0 || desc->seqlen == 0) return st;
+  st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_swa_tc(*desc, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

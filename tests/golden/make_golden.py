@@ -17,6 +17,10 @@ Fixtures:
   gdn_bf16.npz    delta_rule_chunked on bf16 q/k/v/beta (fp32 g and state), B=2, T=80.
   gdn_decode.npz  delta_rule_sequential (the kernel select_kernel picks for T <= 4),
                   T=3 tokens, bf16 inputs, fp32 state ~ N(0, 0.02).
+  swa.npz         causal_attention (pseudobrain/transplant.py:417-436) on bf16-valued
+                  inputs (run in fp32), GQA 4 query / 2 key heads, d=128: a sliding window
+                  of 100 with 4 sinks over T=260 through the reference's query-chunked path
+                  (_chunked_window_attention, chunk forced to 128), and full causal T=200.
   quest.npz       archive_append + retrieve (flat mode, page 16, budget 4 pages) for a
                   decode query (T=1) and a 3-token query, plus the exact attention over
                   [retrieved ; window] as pseudobrain/transplant.py:619-628 computes it.
@@ -129,20 +133,45 @@ def make_quest(E):
     np.savez_compressed(os.path.join(HERE, "quest.npz"), **out)
 
 
+def make_swa(TR):
+    import torch
+    out = {}
+    gen = torch.Generator().manual_seed(104)
+    for name, t, window, sinks, chunk in (("win", 260, 100, 4, 128), ("full", 200, None, 0, 4096)):
+        q = torch.randn(1, 4, t, 128, generator=gen).to(torch.bfloat16)
+        k = torch.randn(1, 2, t, 128, generator=gen).to(torch.bfloat16)
+        v = torch.randn(1, 2, t, 128, generator=gen).to(torch.bfloat16)
+        saved = dict(TR.WINDOW_CHUNK)
+        TR.WINDOW_CHUNK["queries"] = chunk
+        try:
+            o = TR.causal_attention(q.float(), k.float(), v.float(), window=window, sinks=sinks)
+        finally:
+            TR.WINDOW_CHUNK.update(saved)
+        out.update({f"{name}_q": _bits(q), f"{name}_k": _bits(k), f"{name}_v": _bits(v), f"{name}_o": o.numpy(),
+                    f"{name}_window": np.int64(-1 if window is None else window), f"{name}_sinks": np.int64(sinks)})
+    np.savez_compressed(os.path.join(HERE, "swa.npz"), **out)
+
+
 def main(reference_root: str) -> None:
     sys.path.insert(0, reference_root)
     import torch
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     from pseudobrain import exact_memory as E
     from pseudobrain import gated_deltanet as G
+    from pseudobrain import transplant as TR
+    if len(sys.argv) > 2:  # regenerate only the named fixtures
+        for name in sys.argv[2:]:
+            {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR)}[name]()
+        return
     make_gdn(G)
     make_quest(E)
+    make_swa(TR)
     for name in sorted(os.listdir(HERE)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(HERE, name)), "bytes")
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <pseudobrain source checkout>")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <pseudobrain source checkout> [gdn|quest|swa ...]")
     main(sys.argv[1])

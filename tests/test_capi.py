@@ -52,22 +52,25 @@ def test_abi_version_and_status_strings(lib):
     assert _capi.LIB.pbk_status_string(-7) == b"device-side wait timed out"
 
 
-def test_descriptor_layout_matches_header():
-    """Offsets of the ctypes mirror equal the C struct's (checked by compiling a probe)."""
+@pytest.mark.parametrize("cname,pyname", [("pbk_gdn_desc", "PbkGdnDesc"), ("pbk_quest_desc", "PbkQuestDesc"),
+                                          ("pbk_swa_desc", "PbkSwaDesc"), ("pbk_view", "PbkView")])
+def test_descriptor_layout_matches_header(cname, pyname):
+    """Offsets of every field of the ctypes mirror equal the C struct's (checked by
+    compiling a probe against include/pbk.h)."""
     import subprocess
     import tempfile
     from pseudobrain_b200 import _capi
-    fields = ["batch", "q", "k", "v", "g", "beta", "o", "h0", "state", "state_slot_stride",
-              "state_layout", "state_indices", "scale"]
+    cls = getattr(_capi, pyname)
+    fields = [f for f, _ in cls._fields_]
     src = "#include <stdio.h>\n#include <stddef.h>\n#include \"pbk.h\"\nint main(void){\n"
-    src += "".join(f'printf("%zu\\n", offsetof(pbk_gdn_desc, {f}));\n' for f in fields)
-    src += 'printf("%zu\\n", sizeof(pbk_gdn_desc)); return 0; }\n'
+    src += "".join(f'printf("%zu\\n", offsetof({cname}, {f}));\n' for f in fields)
+    src += f'printf("%zu\\n", sizeof({cname})); return 0; }}\n'
     with tempfile.TemporaryDirectory() as d:
         c, exe = os.path.join(d, "p.c"), os.path.join(d, "p")
         open(c, "w").write(src)
         subprocess.run(["gcc", "-I", HEADER_DIR, c, "-o", exe], check=True)
         got = [int(x) for x in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
-    want = [getattr(_capi.PbkGdnDesc, f).offset for f in fields] + [ctypes.sizeof(_capi.PbkGdnDesc)]
+    want = [getattr(cls, f).offset for f in fields] + [ctypes.sizeof(cls)]
     assert got == want
 
 

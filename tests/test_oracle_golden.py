@@ -110,3 +110,20 @@ def test_bf16_round_is_round_to_nearest_even():
     x = np.random.default_rng(0).standard_normal(4096).astype(np.float32) * 37
     ref = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
     assert np.array_equal(oq.bf16_round(x), ref)
+
+
+@pytest.mark.parametrize("case", ["win", "full"])
+def test_window_attention_matches_reference(case):
+    """oracle/swa.py against transplant.causal_attention (window 100 + 4 sinks through the
+    reference's query-chunked path; full causal)."""
+    from oracle import swa as oswa
+    f = load_golden("swa.npz")
+    window = int(f[f"{case}_window"])
+    o = oswa.causal_attention(_f32(f[f"{case}_q"]), _f32(f[f"{case}_k"]), _f32(f[f"{case}_v"]),
+                              None if window < 0 else window, int(f[f"{case}_sinks"]))
+    assert ogdn.rel_err(o, f[f"{case}_o"]) < FP32_TOL
+    # the row-subset form used for long sequences agrees with the full one
+    part = oswa.causal_attention_at(_f32(f[f"{case}_q"]), _f32(f[f"{case}_k"]), _f32(f[f"{case}_v"]), [0, 130], 50,
+                                    None if window < 0 else window, int(f[f"{case}_sinks"]))
+    for s, x in part.items():
+        assert np.allclose(x, o[:, :, s:s + 50], rtol=0, atol=1e-12)
