@@ -7,8 +7,10 @@ Headline (``value``): GDN chunked prefill of BASELINE config 1 (B=4, T=32768, 16
 32 value heads, dk=dv=128, chunk 64, bf16 q/k/v/beta, fp32 g and state) in tok/s,
 inputs resident in HBM, device-timed with CUDA events, max over ranks. The same line
 carries the other two parts of the metric, each with its own roofline:
-``decode`` (config 2: B=256 decode step, 537 MB fp32 state, steps/s) and ``quest``
-(config 3: 8 queries over a 1M-token cache, q/s). ``e2e`` times the public API with
+``decode`` (config 2: B=256 decode step, 537 MB fp32 state, steps/s), ``quest``
+(config 3: 8 queries over a 1M-token cache, q/s) and ``hybrid`` (config 4: one GDN +
+sliding-window attention layer over a 1M-token sequence, heads split over the ranks with
+an NCCL all-gather of each branch's output; tok/s, strong scaling). ``e2e`` times the public API with
 pinned host inputs copied in and outputs copied back inside the timed region.
 
 Multi-GPU (torchrun, one rank per GPU): weak scaling. Every rank runs its own shard of
@@ -39,6 +41,8 @@ PREFILL_HEADS = dict(hk=16, hv=32, dk=128, dv=128, chunk=64)
 DECODE = {"full": dict(batch=256), "small": dict(batch=64)}
 DECODE_HEADS = dict(hk=16, hv=32, dk=128, dv=128)
 QUEST = {"full": dict(n_tokens=1 << 20), "small": dict(n_tokens=1 << 19)}
+HYBRID = {"full": dict(seqlen=1 << 20), "small": dict(seqlen=1 << 16)}
+HYBRID_HEADS = dict(hk=16, hv=32, heads=32, kv=8, d=128, window=4096)
 QUEST_SHAPE = dict(kv=8, heads=32, d=128, page=16, window=4096, nq=8, budget_tokens=4096)
 
 
@@ -287,6 +291,86 @@ def measure_quest(args, timed, dev, rank, world, pk):
     }
 
 
+def swa_pairs(t, window):
+    """Visible (query, key) pairs of a causal window over t tokens."""
+    w = min(window, t)
+    return t * w - w * (w - 1) // 2
+
+
+def measure_hybrid(args, timed, dev, rank, world, pk):
+    """one hybrid layer over a 1M-token sequence (B=1). The GDN branch
+    (16 key / 32 value heads) is split by value head over the ranks, and within a rank along
+    T (segments chained by the segment scan) so a few heads still fill the SMs; the
+    sliding-window attention branch (32 query / 8 key heads, window 4096) is split by key
+    head. Each branch's [T, heads/N * 128] output is all-gathered (NCCL) into a head-major
+    [N, T, heads/N * 128] buffer, the hidden-4096 layout the output projection reads.
+    Strong scaling: the job is one layer pass whatever N."""
+    import torch
+    import torch.distributed as dist
+    from pseudobrain_b200.gdn_prefill import auto_segments, gdn_prefill_segmented
+    from pseudobrain_b200.synthetic import gdn_inputs
+    from pseudobrain_b200.transplant import window_attention_
+    H = HYBRID_HEADS
+    t = HYBRID[args.size]["seqlen"]
+    if H["hv"] % world or H["kv"] % world:
+        return None
+    hv, hk, heads, kv = H["hv"] // world, H["hk"] // world, H["heads"] // world, H["kv"] // world
+    x = gdn_inputs(1, t, hk, hv, device=dev, seed=4 + 1000 * rank)
+    o_gdn = torch.empty(1, t, hv, H["d"], device=dev, dtype=torch.bfloat16)
+    gen = torch.Generator(device=dev).manual_seed(5 + 1000 * rank)
+    qa = torch.randn(1, t, heads, H["d"], device=dev, generator=gen).to(torch.bfloat16)
+    ka = torch.randn(1, t, kv, H["d"], device=dev, generator=gen).to(torch.bfloat16)
+    va = torch.randn(1, t, kv, H["d"], device=dev, generator=gen).to(torch.bfloat16)
+    o_swa = torch.empty_like(qa)
+    gath_gdn = torch.empty(world * t, hv * H["d"], device=dev, dtype=torch.bfloat16) if world > 1 else None
+    gath_swa = torch.empty(world * t, heads * H["d"], device=dev, dtype=torch.bfloat16) if world > 1 else None
+    segs = auto_segments(1, hv, t)
+
+    def gdn():
+        gdn_prefill_segmented(x["q"], x["k"], x["v"], x["g"], x["beta"], x["scale"], None, segments=segs, o=o_gdn)
+
+    def swa():
+        window_attention_(qa, ka, va, o_swa, H["window"], 0, H["d"] ** -0.5)
+
+    def gather():
+        if world > 1:
+            dist.all_gather_into_tensor(gath_gdn, o_gdn.view(t, -1))
+            dist.all_gather_into_tensor(gath_swa, o_swa.view(t, -1))
+
+    def step():
+        gdn()
+        swa()
+        gather()
+
+    steps = max(3, min(args.steps, 5))
+    t_step = timed(step, steps, 3) / steps
+    t_gdn = timed(gdn, 2, 1) / 2
+    t_swa = timed(swa, 2, 1) / 2
+    t_ag = timed(gather, 2, 1) / 2 if world > 1 else 0.0
+    gdn_flops = t * H["hv"] * prefill_flops_per_token_head(64, H["d"])
+    swa_flops = 4 * H["d"] * swa_pairs(t, H["window"]) * H["heads"]
+    per_gpu = (gdn_flops + swa_flops) / world
+    ag_bytes = (world - 1) * t * (hv + heads) * H["d"] * 2  # bf16 received per GPU
+    out = {
+        "metric": "hybrid layer tok/s (config 4)", "value": t / t_step, "unit": "tok/s",
+        "per_gpu": t / t_step / world, "scaling": "strong", "ms_per_step": t_step * 1e3,
+        "config": {"seqlen": t, "gdn_heads_per_gpu": hv, "gdn_segments": segs, "swa_q_heads_per_gpu": heads,
+                   "window": H["window"], "size": args.size},
+        "roofline": {"bound": "tensor", "achieved": per_gpu / t_step / 1e12, "peak": pk["tc_sustained"],
+                     "unit": "TFLOP/s", "frac": per_gpu / t_step / 1e12 / pk["tc_sustained"],
+                     "traffic": None, "peak_source": f"{pk['src']} bf16 sustained"},
+        "gdn": {"ms": t_gdn * 1e3, "tflops": gdn_flops / world / t_gdn / 1e12},
+        "swa": {"ms": t_swa * 1e3, "tflops": swa_flops / world / t_swa / 1e12,
+                "frac": swa_flops / world / t_swa / 1e12 / pk["tc_sustained"]},
+        "e2e": None,
+        "gpu_launches": steps * (5 + 1),
+    }
+    if world > 1:
+        out["all_gather"] = {"ms": t_ag * 1e3, "bytes_received_per_gpu": ag_bytes,
+                             "gbps": ag_bytes / t_ag / 1e9 if t_ag > 0 else None}
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -296,7 +380,8 @@ def run_ours(args, rank, world, local_rank):
     timed = Timer(torch, dist, dev, world)
     parts = {}
     clk = Clocks(local_rank)
-    for name, fn in (("prefill", measure_prefill), ("decode", measure_decode), ("quest", measure_quest)):
+    for name, fn in (("prefill", measure_prefill), ("decode", measure_decode), ("quest", measure_quest),
+                     ("hybrid", measure_hybrid)):
         if args.workload in ("all", name):
             if name == "prefill":
                 with clk:
@@ -323,8 +408,8 @@ def run_ours(args, rank, world, local_rank):
         "roofline": head["roofline"], "e2e": head["e2e"], "gpu_launches": head["gpu_launches"],
         "clocks": clk.summary(),
     }
-    for name in ("decode", "quest"):
-        if name in parts and parts[name] is not head:
+    for name in ("decode", "quest", "hybrid"):
+        if name in parts and parts[name] is not None and parts[name] is not head:
             line[name] = parts[name]
     if world == 1 and not args.no_cpu_baseline and "prefill" in parts:
         line["cpu_baseline"] = cpu_baseline(samples=1)
@@ -395,7 +480,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("all", "prefill", "decode", "quest"), default="all",
+    ap.add_argument("--workload", choices=("all", "prefill", "decode", "quest", "hybrid"), default="all",
                     help="run one part only (profiling); the JSON line then carries that part")
     ap.add_argument("--size", choices=("full", "small"), default="full",
                     help="small: a reduced case of the same kernels for ncu captures (not a bench number)")

@@ -111,8 +111,22 @@ PBK_API int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream);
  * (NULL = zeros) and writing the final state into `state` (h0 == state is allowed:
  * in place) and every token's output into o. Sequence ends that are not a multiple
  * of 64 are padded with identity steps as the reference does. Requires
- * dk == dv == 128. */
+ * dk == dv == 128. With bf16 q/k/v, o.data may be NULL: only the final state is
+ * computed (the segment runs of pbk_gdn_segment_scan). */
 PBK_API int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream);
+
+/* Segment scan for a prefill split along T into nseg segments of whole 64-token chunks
+ * (parallelism inside one long sequence; the reference runs a sequence's chunks in
+ * order, gated_deltanet.py:157-163). A segment's recurrence is affine in its initial
+ * state, S_out = A S_in + b: b is its final state from zeros and m = A + b its final
+ * state from the identity (two pbk_gdn_prefill runs of all segments at once, o = NULL).
+ * With b, m [batch, nseg - 1, hv, 128, 128] and h0 [batch, hv, 128, 128] (NULL =
+ * zeros), writes starts [batch, nseg, hv, 128, 128]:
+ *   starts[0] = h0,  starts[p + 1] = (m[p] - b[p]) starts[p] + b[p]   (fp32, exact);
+ * a third run from `starts` then gives every token's output and the final state.
+ * [K,V] state layout, dense, 16-byte aligned. */
+PBK_API int pbk_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int32_t batch,
+                                 int32_t nseg, int32_t hv, void* stream);
 
 /* ------------------------------------------------------------------------
  * Quest page-bounded exact memory (pseudobrain/exact_memory.py, flat mode).

@@ -11,6 +11,8 @@ cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st);
 bool gdn_prefill_tc_supported(const pbk_gdn_desc& d);
 cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st);
+cudaError_t launch_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int batch,
+                                    int nseg, int hv, cudaStream_t st);
 }
 
 namespace {
@@ -35,14 +37,15 @@ int check_current_device() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int validate_gdn(const pbk_gdn_desc* d) {
+// allow_null_o: prefill may run for its final state only (o.data == NULL).
+int validate_gdn(const pbk_gdn_desc* d, bool allow_null_o = false) {
   if (d == nullptr) return PBK_ERR_INVALID;
   if (d->batch < 0 || d->seqlen < 0 || d->hk < 1 || d->hv < 1) return PBK_ERR_INVALID;
   if (d->hv % d->hk != 0) return PBK_ERR_SHAPE;
   if (d->dk != 128 || d->dv != 128) return PBK_ERR_SHAPE;
   if (d->batch > 0) {
-    if (!d->q.data || !d->k.data || !d->v.data || !d->g.data || !d->beta.data || !d->o.data || !d->state)
-      return PBK_ERR_INVALID;
+    if (!d->q.data || !d->k.data || !d->v.data || !d->g.data || !d->beta.data || !d->state) return PBK_ERR_INVALID;
+    if (!d->o.data && !allow_null_o) return PBK_ERR_INVALID;
   }
   if (!dtype_ok(d->q.dtype) || d->k.dtype != d->q.dtype || d->v.dtype != d->q.dtype) return PBK_ERR_DTYPE;
   if (!dtype_ok(d->g.dtype) || !dtype_ok(d->beta.dtype) || !dtype_ok(d->o.dtype)) return PBK_ERR_DTYPE;
@@ -170,9 +173,11 @@ int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream) {
 }
 
 int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
-  int st = validate_gdn(desc);
+  int st = validate_gdn(desc, true);
   if (st != PBK_OK) return st;
   if (desc->batch == 0) return PBK_OK;
+  // state-only runs (no output) exist on the tensor-core path
+  if (desc->o.data == nullptr && !pbk::gdn_prefill_tc_supported(*desc)) return PBK_ERR_INVALID;
   if ((st = check_current_device()) != PBK_OK) return st;
   // bf16 inputs: tensor-core kernel (bf16 operands, fp32 state and accumulation);
   // fp32 inputs: the exact fp32 kernel.
@@ -180,6 +185,20 @@ int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
                             ? pbk::launch_gdn_prefill_tc(*desc, static_cast<cudaStream_t>(stream))
                             : pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream));
   return launch_status(e);
+}
+
+int pbk_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int32_t batch, int32_t nseg,
+                         int32_t hv, void* stream) {
+  if (batch < 0 || nseg < 1 || hv < 1) return PBK_ERR_INVALID;
+  if ((int64_t)batch * hv > INT32_MAX) return PBK_ERR_SHAPE;
+  if (batch == 0) return PBK_OK;
+  if (starts == nullptr || (nseg > 1 && (b == nullptr || m == nullptr))) return PBK_ERR_INVALID;
+  if (!aligned16(starts) || (b && !aligned16(b)) || (m && !aligned16(m)) || (h0 && !aligned16(h0)))
+    return PBK_ERR_ALIGN;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(
+      pbk::launch_gdn_segment_scan(b, m, h0, starts, batch, nseg, hv, static_cast<cudaStream_t>(stream)));
 }
 
 size_t pbk_quest_select_workspace(const pbk_quest_desc* desc) {

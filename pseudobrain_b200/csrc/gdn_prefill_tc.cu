@@ -26,6 +26,8 @@
 // The roles meet on mbarriers; every wait is bounded: on timeout the kernel records an
 // error code, stops issuing, waits (bounded) for its own loads and MMAs, frees its TMEM
 // and returns.
+#include <cstring>
+
 #include "common.cuh"
 #include "tc.cuh"
 #include "tma_host.h"
@@ -69,7 +71,7 @@ struct PrefillArgs {
   const void* beta;
   int64_t b_sb, b_st, b_sh;
   int b_dtype;
-  void* o;
+  void* o;  // NULL: final state only, no outputs written
   int64_t o_sb, o_st, o_sh;
   const float* h0;
   float* state;
@@ -230,7 +232,7 @@ __global__ void __launch_bounds__(NT, 1)
     tc::prefetch_tmap(&tm_q);
     tc::prefetch_tmap(&tm_k);
     tc::prefetch_tmap(&tm_v);
-    tc::prefetch_tmap(&tm_o);
+    if (p.o != nullptr) tc::prefetch_tmap(&tm_o);
     issue_kq(0);
     if (nchunks > 1) issue_kq(1);
     issue_v(0);
@@ -580,7 +582,7 @@ __global__ void __launch_bounds__(NT, 1)
       // O = gamma scale QS + UM (registers; t = 32 hf + i), then the next chunk's state
       // step, then O through shared memory and a TMA store.
       float o[32];
-      {
+      if (p.o != nullptr) {
         float um[32];
         tmem_row32(lane_addr + kColQS + 32 * hf, o);
         tmem_row32(lane_addr + kColUM + 32 * hf, um);
@@ -595,6 +597,7 @@ __global__ void __launch_bounds__(NT, 1)
       }
       // staging in ut as row-major [rows][128]; rows past the sequence end fall outside
       // the tensor and are not written by the store
+      if (p.o == nullptr) continue;
       constexpr int kRows = sizeof(TOut) == 2 ? 64 : 32;  // 16 KB per pass
       TOut* stage = reinterpret_cast<TOut*>(sm.ut);
 #pragma unroll
@@ -662,10 +665,11 @@ bool gdn_prefill_tc_supported(const pbk_gdn_desc& d) {
            v.stride_b % 8 == 0 && v.stride_t > 0 && v.stride_h > 0 && v.stride_b > 0;
   };
   // the output is written with 16-byte vectors along the value dim
-  const bool out_ok = (reinterpret_cast<uintptr_t>(d.o.data) & 15) == 0 &&
+  const bool out_ok = d.o.data == nullptr ||
+                      ((reinterpret_cast<uintptr_t>(d.o.data) & 15) == 0 &&
                       d.o.stride_t % (d.o.dtype == PBK_BF16 ? 8 : 4) == 0 &&
                       d.o.stride_h % (d.o.dtype == PBK_BF16 ? 8 : 4) == 0 &&
-                      d.o.stride_b % (d.o.dtype == PBK_BF16 ? 8 : 4) == 0;
+                      d.o.stride_b % (d.o.dtype == PBK_BF16 ? 8 : 4) == 0);
   return d.q.dtype == PBK_BF16 && d.dk == 128 && d.dv == 128 && d.seqlen > 0 && ok16(d.q) && ok16(d.k) &&
          ok16(d.v) && out_ok;
 }
@@ -674,7 +678,8 @@ cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st) {
   CUtensorMap mq, mk, mv, mo;
   if (!make_map(&mq, d.q, d.hk, d) || !make_map(&mk, d.k, d.hk, d) || !make_map(&mv, d.v, d.hv, d))
     return cudaErrorInvalidValue;
-  {
+  memset(&mo, 0, sizeof(mo));  // unused when only the final state is wanted
+  if (d.o.data != nullptr) {
     const bool obf = d.o.dtype == PBK_BF16;
     const uint64_t es = obf ? 2 : 4;
     const uint64_t dims[4] = {128, (uint64_t)d.seqlen, (uint64_t)d.hv, (uint64_t)d.batch};

@@ -67,12 +67,15 @@ def _desc(q, k, v, g, beta, o, h0, state, scale, state_indices, layout) -> PbkGd
                          f"q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)} g{tuple(g.shape)} beta{tuple(beta.shape)}")
     if state.dtype != torch.float32 or state.stride(-1) != 1:
         raise ValueError("state must be fp32 with a contiguous last dim")
-    if h0 is not None and (h0.dtype != torch.float32 or h0.stride() != state.stride()):
-        raise ValueError("h0 must be fp32 with the state's strides")
+    if h0 is not None and (h0.dtype != torch.float32 or h0.shape[1:] != state.shape[1:]
+                           or h0.stride()[1:] != state.stride()[1:]
+                           or (h0.shape[0] > 1 and h0.stride(0) != state.stride(0))):
+        raise ValueError("h0 must be fp32 with the state's strides")  # the kernels index both alike
     return PbkGdnDesc(
         batch=b, seqlen=t, hk=hk, hv=hv, dk=dk, dv=dv,
         q=view4(q, "q"), k=view4(k, "k"), v=view4(v, "v"), g=view3(g, "g"), beta=view3(beta, "beta"),
-        o=view4(o, "o"), h0=(h0.data_ptr() if h0 is not None else None), state=state.data_ptr(),
+        o=(view4(o, "o") if o is not None else PbkView(None, 0, 0, 0, _capi.PBK_BF16, 0)),
+        h0=(h0.data_ptr() if h0 is not None else None), state=state.data_ptr(),
         state_slot_stride=state.stride(0), state_layout=layout, pad_=0,
         state_indices=(state_indices.data_ptr() if state_indices is not None else None),
         scale=float(scale), pad2_=0)

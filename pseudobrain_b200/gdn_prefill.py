@@ -45,3 +45,102 @@ def gdn_prefill(q, k, v, g, beta, scale, h0=None, out_dtype: torch.dtype = torch
     o = torch.empty(b, t, hv, dv, dtype=out_dtype, device=q.device)
     gdn_prefill_(q, k, v, g, beta, h0, state, o, float(scale))
     return o, state
+
+
+# ------------------------------------------------------------------------------------------
+# Long sequences with few heads: split T into segments that run in parallel
+# ------------------------------------------------------------------------------------------
+@torch.library.custom_op("pbk::gdn_final_state", mutates_args=("state",))
+def gdn_final_state_(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                     h0: torch.Tensor | None, state: torch.Tensor, scale: float) -> None:
+    """The final state of the chunked recurrence only (no outputs written): bf16 q/k/v."""
+    dev = _check_cuda(q, k, v, g, beta, state)
+    d = _desc(q, k, v, g, beta, None, h0, state, scale, None, 0)
+    with torch.cuda.device(dev):
+        check(LIB.pbk_gdn_prefill(d, _stream(dev)), "pbk_gdn_prefill (state only)")
+
+
+@gdn_final_state_.register_fake
+def _(q, k, v, g, beta, h0, state, scale):
+    return None
+
+
+def segment_scan(b: torch.Tensor, m: torch.Tensor, h0: torch.Tensor | None, starts: torch.Tensor) -> None:
+    """starts[:, 0] = h0 (None: 0), starts[:, p+1] = (m[:, p] - b[:, p]) starts[:, p] + b[:, p];
+    b, m [B, nseg-1, Hv, 128, 128], starts [B, nseg, Hv, 128, 128], fp32 contiguous."""
+    batch, nseg, hv = starts.shape[:3]
+    for t in (b, m, h0, starts):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
+            raise ValueError("segment scan: fp32 contiguous tensors expected")
+    if b.shape != (batch, nseg - 1, hv, 128, 128) or m.shape != b.shape:
+        raise ValueError("segment scan: b and m must be [B, nseg - 1, Hv, 128, 128]")
+    dev = _check_cuda(b, m, starts)
+    with torch.cuda.device(dev):
+        check(LIB.pbk_gdn_segment_scan(b.data_ptr(), m.data_ptr(), None if h0 is None else h0.data_ptr(),
+                                       starts.data_ptr(), batch, nseg, hv, _stream(dev)), "pbk_gdn_segment_scan")
+
+
+def auto_segments(batch: int, hv: int, seqlen: int, sms: int | None = None) -> int:
+    """Segments per sequence so that batch x heads x segments CTAs fill the SMs once
+    (1 when the batch already does, or when segments would be under 16 chunks)."""
+    if sms is None:
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    chunks = -(-seqlen // 64)
+    want = sms // max(1, batch * hv)
+    return max(1, min(want, chunks // 16))
+
+
+def gdn_prefill_segmented(q, k, v, g, beta, scale, h0=None, segments: int | None = None,
+                          out_dtype: torch.dtype = torch.float32, o: torch.Tensor | None = None):
+    """delta_rule_chunked's (o, final state) with every sequence split into `segments`
+    pieces of whole 64-token chunks that run in parallel (bf16 q/k/v):
+
+    1. all full segments from zeros and from the identity (final states b and m only);
+    2. pbk_gdn_segment_scan chains them into each segment's true initial state;
+    3. all segments again from those states, writing the outputs and the final state.
+
+    The chunk boundaries are those of the unsplit sequence, so this is the reference's
+    arithmetic reassociated across segments (exact in real arithmetic)."""
+    _check_cuda(q, k, v, g, beta)
+    b, t, hk, dk = q.shape
+    hv, dv = v.shape[2], v.shape[3]
+    if segments is None:
+        segments = auto_segments(b, hv, t)
+    chunks = -(-t // 64)
+    seg_len = -(-chunks // max(1, segments)) * 64
+    nseg = -(-t // seg_len)
+    if o is None:
+        o = torch.empty(b, t, hv, dv, dtype=out_dtype, device=q.device)
+    if h0 is not None:
+        h0 = h0.float().contiguous()
+    final = torch.empty(b, hv, dk, dv, dtype=torch.float32, device=q.device)
+    if nseg == 1:
+        gdn_prefill_(q, k, v, g, beta, h0, final, o, float(scale))
+        return o, final
+    full = nseg - 1
+    cut = full * seg_len
+    for i in range(b):  # one sequence at a time: its full segments form a batch (a view)
+        def seg(x):
+            return x[i, :cut].unflatten(0, (full, seg_len))
+
+        qs, ks, vs, gs, bs = (seg(x) for x in (q, k, v, g, beta))
+        bst = torch.empty(full, hv, dk, dv, dtype=torch.float32, device=q.device)
+        mst = torch.empty_like(bst)
+        eye = torch.eye(dk, dtype=torch.float32, device=q.device).expand(full, hv, dk, dv).contiguous()
+        gdn_final_state_(qs, ks, vs, gs, bs, None, bst, float(scale))
+        gdn_final_state_(qs, ks, vs, gs, bs, eye, mst, float(scale))
+        starts = torch.empty(1, nseg, hv, dk, dv, dtype=torch.float32, device=q.device)
+        segment_scan(bst.unsqueeze(0), mst.unsqueeze(0), None if h0 is None else h0[i:i + 1], starts)
+        # the last (shorter) segment runs beside the full ones on a side stream, so the
+        # two launches share the SMs; `eye` receives the full segments' final states
+        # (not needed afterwards)
+        cur = torch.cuda.current_stream(q.device)
+        side = torch.cuda.Stream(q.device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            gdn_prefill_(q[i:i + 1, cut:], k[i:i + 1, cut:], v[i:i + 1, cut:], g[i:i + 1, cut:],
+                         beta[i:i + 1, cut:], starts[:, full], final[i:i + 1], o[i:i + 1, cut:], float(scale))
+        starts.record_stream(side)
+        gdn_prefill_(qs, ks, vs, gs, bs, starts[0, :full], eye, seg(o), float(scale))
+        cur.wait_stream(side)
+    return o, final

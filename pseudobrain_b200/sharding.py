@@ -77,3 +77,28 @@ def gdn_prefill_batch_sharded(q, k, v, g, beta, scale, h0=None, group=None, pref
     b0, b1 = batch_shard(q.shape[0], world, rank)
     return prefill(q[b0:b1], k[b0:b1], v[b0:b1], g[b0:b1], beta[b0:b1], scale,
                    None if h0 is None else h0[b0:b1])
+
+
+def causal_attention_head_sharded(q, k, v, window=None, sinks=0, group=None, attention=None):
+    """Sliding-window attention (transplant.py:417-436 semantics) with the key heads split
+    over the ranks of `group`: rank r computes key heads [r KV/N, (r+1) KV/N) and the query
+    heads that read them, then one all-gather restores [B,H,T,hd] on every rank.
+
+    q [B,H,T,hd], k/v [B,KV,T,hd] (the full tensors on every rank). ``attention`` is the
+    per-rank function, pseudobrain_b200.transplant.causal_attention by default."""
+    if attention is None:
+        from .transplant import causal_attention as attention
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    b, h, t, d = q.shape
+    kvh = k.shape[1]
+    if kvh % world:
+        raise ValueError(f"{kvh} key heads do not split over {world} ranks")
+    per = kvh // world
+    groups = h // kvh
+    k0, k1 = rank * per, (rank + 1) * per
+    o_loc = attention(q[:, k0 * groups:k1 * groups], k[:, k0:k1], v[:, k0:k1], window, sinks)
+    o_all = torch.empty((world * b,) + tuple(o_loc.shape[1:]), dtype=o_loc.dtype, device=o_loc.device)
+    dist.all_gather_into_tensor(o_all, o_loc.contiguous(), group=group)
+    # [N, B, H/N, T, hd] -> [B, H, T, hd]
+    return o_all.view((world,) + tuple(o_loc.shape)).transpose(0, 1).reshape(b, h, t, d)

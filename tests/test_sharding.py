@@ -37,6 +37,17 @@ def _inputs():
     return {n: torch.from_numpy(inp[n]) for n in ("q", "k", "v", "g", "beta", "h0")}, inp["scale"]
 
 
+def _oracle_attention(q, k, v, window, sinks):
+    from oracle import swa as oswa
+    return torch.from_numpy(oswa.causal_attention(q.numpy(), k.numpy(), v.numpy(), window, sinks)).float()
+
+
+def _attn_inputs():
+    g = torch.Generator().manual_seed(12)
+    return (torch.randn(1, 8, 150, 128, generator=g), torch.randn(1, 4, 150, 128, generator=g),
+            torch.randn(1, 4, 150, 128, generator=g))
+
+
 def _worker(rank, world, port, mode, outdir):
     import sys
     sys.path.insert(0, ROOT)
@@ -44,6 +55,11 @@ def _worker(rank, world, port, mode, outdir):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from pseudobrain_b200 import sharding
+        if mode == "attention":
+            q, k, v = _attn_inputs()
+            o = sharding.causal_attention_head_sharded(q, k, v, 50, 3, attention=_oracle_attention)
+            torch.save({"o": o}, os.path.join(outdir, f"{mode}_{rank}.pt"))
+            return
         x, scale = _inputs()
         fn = sharding.gdn_prefill_head_sharded if mode == "head" else sharding.gdn_prefill_batch_sharded
         o, s = fn(x["q"], x["k"], x["v"], x["g"], x["beta"], scale, x["h0"], prefill=_oracle_prefill)
@@ -64,6 +80,17 @@ def test_sharded_prefill_equals_unsharded(tmp_path, mode):
             assert torch.equal(got["o"], o_ref) and torch.equal(got["s"], s_ref)
         else:  # each rank has its own sequences
             assert torch.equal(got["o"], o_ref[rank:rank + 1]) and torch.equal(got["s"], s_ref[rank:rank + 1])
+
+
+def test_head_sharded_window_attention_equals_unsharded(tmp_path):
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), "attention", str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    q, k, v = _attn_inputs()
+    want = _oracle_attention(q, k, v, 50, 3)
+    for rank in range(world):
+        got = torch.load(os.path.join(tmp_path, f"attention_{rank}.pt"))["o"]
+        assert torch.equal(got, want)
 
 
 def test_shard_maps():
