@@ -141,8 +141,17 @@ def gated_delta_rule(q, k, v, g, beta, scale, h0, kernel: str = "chunked"):
 
 
 def delta_rule_chunked(q, k, v, g, beta, scale, h0, chunk: int | None = None):
-    """Chunkwise WY recurrence (reference: gated_deltanet.py:110-165) on CUDA."""
-    from .gdn_prefill import gdn_prefill
+    """Chunkwise WY recurrence (reference: gated_deltanet.py:110-165) on CUDA.
+
+    When the (sequence x value head) chains are too few to fill the GPU and the sequences
+    are long (bf16 inputs, at least 4 segments of 16+ chunks per sequence), the sequences
+    are split along T (gdn_prefill_segmented): three passes over the tokens, spread over
+    all SMs instead of one pass on a few."""
+    from .gdn_prefill import auto_segments, gdn_prefill, gdn_prefill_segmented
     if chunk not in (None, CHUNK):
         raise ValueError(f"the CUDA chunked kernel uses chunk={CHUNK}")
+    if q.dtype == torch.bfloat16 and q.is_cuda:
+        segs = auto_segments(q.shape[0], v.shape[2], q.shape[1])
+        if segs >= 4:
+            return gdn_prefill_segmented(q, k, v, g, beta, scale, h0, segments=segs)
     return gdn_prefill(q, k, v, g, beta, scale, h0)
