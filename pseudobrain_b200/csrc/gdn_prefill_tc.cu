@@ -58,7 +58,10 @@ struct __align__(1024) PrefillSmem {
   uint8_t ut[16384];         // U^T bf16 [128 dv rows x 64 t] (A operand); also output staging
   float a[C * PA];           // A fp32
   float cum[3][C], cum2[3][C], gam[3][C], ee[3][C], beta[3][C];
-  uint64_t bar_kq[2], bar_v, bar_p1, bar_p3, bar_ws, bar_s, prep_ready, drain_s, drain_p;
+  float da[3][C], db[3][C];  // exp2(c_t - c_ref), exp2(c_ref - c_i): the decay in factored form
+  float gs[4][C], bs[4][C];  // raw g and beta, staged 3 chunks ahead by a serial warp
+  int factored[3];           // the chunk's decay span allows the factored form
+  uint64_t bar_kq[2], bar_v, bar_p1, bar_p3, bar_ws, bar_s, prep_ready, drain_s, drain_p, scal[4];
   uint32_t tmem_base;
   volatile int abort;
 };
@@ -191,6 +194,7 @@ __global__ void __launch_bounds__(NT, 1)
     tc::mbar_init(&sm.prep_ready, kRoleThreads);
     tc::mbar_init(&sm.drain_s, 1);
     tc::mbar_init(&sm.drain_p, 1);
+    for (int i = 0; i < 4; ++i) tc::mbar_init(&sm.scal[i], 1);
     sm.abort = 0;
     tc::fence_barrier_init();
   }
@@ -256,30 +260,19 @@ __global__ void __launch_bounds__(NT, 1)
       tc::fence_after_sync();
       return got;
     };
-    // g and beta of the next chunk are loaded one chunk ahead (registers of the role's
-    // first warp: lane l holds steps 2l and 2l+1).
-    float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
-    auto fetch_scalars = [&](int m) {
-      g0 = g1 = b0 = b1 = 0.f;
-      if (pw == 0 && m < nchunks) {
-        const int t = m * C + 2 * lane;
-        if (t < p.seqlen) {
-          g0 = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
-          b0 = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
-        }
-        if (t + 1 < p.seqlen) {
-          g1 = load_any(p.g, b * p.g_sb + (int64_t)(t + 1) * p.g_st + h * p.g_sh, p.g_dtype);
-          b1 = load_any(p.beta, b * p.b_sb + (int64_t)(t + 1) * p.b_st + h * p.b_sh, p.b_dtype);
-        }
-      }
-    };
     int last_v = 0;  // last V load issued (for the bounded drain)
-    fetch_scalars(0);
     for (int m = 0; m < nchunks && ok; ++m) {
       const int buf = m & 1, sb = m % 3;
       // ---- scalars: cumulative log decay c, gamma = e^c, e = e^(c_C - c), beta
       if (pw == 0) {
         constexpr float kLog2e = 1.4426950408889634f;
+        // g and beta of chunk m, staged in shared memory by a serial warp
+        if (!tc::mbar_wait(&sm.scal[m & 3], (m >> 2) & 1)) {
+          if (p.err) atomicCAS(p.err, 0, 210);
+          sm.abort = 1;
+        }
+        const float g0 = sm.gs[m & 3][2 * lane], g1 = sm.gs[m & 3][2 * lane + 1];
+        const float b0 = sm.bs[m & 3][2 * lane], b1 = sm.bs[m & 3][2 * lane + 1];
         const float pair = g0 + g1;
         float incl = pair;
 #pragma unroll
@@ -297,8 +290,22 @@ __global__ void __launch_bounds__(NT, 1)
         sm.ee[sb][2 * lane + 1] = exp2f((clast - c1) * kLog2e);
         sm.beta[sb][2 * lane] = b0;
         sm.beta[sb][2 * lane + 1] = b1;
+        // decay factors exp2(c_t - c_i) = da_t db_i about c_ref = c_31, exact enough while
+        // the chunk's log2 decay spans less than 60 (no factor leaves fp32's normal range)
+        const float l0 = c0 * kLog2e, l1 = c1 * kLog2e;
+        const float ref = __shfl_sync(0xffffffffu, l1, 15);
+        float hi = fmaxf(l0, l1), lo = fminf(l0, l1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+          lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        }
+        sm.da[sb][2 * lane] = exp2f(l0 - ref);
+        sm.da[sb][2 * lane + 1] = exp2f(l1 - ref);
+        sm.db[sb][2 * lane] = exp2f(ref - l0);
+        sm.db[sb][2 * lane + 1] = exp2f(ref - l1);
+        if (lane == 0) sm.factored[sb] = (hi - lo) < 60.f;
       }
-      fetch_scalars(m + 1);
       // ---- [K;Q] K^T
       if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
       if (pt == 0) {
@@ -318,23 +325,35 @@ __global__ void __launch_bounds__(NT, 1)
         const bool zero = t < 32 && hf == 1;  // rows 0-31 have no terms past column 31
         float v[32];
         if (!zero) tmem_row32(lane_addr + kColD1 + i0, v);
+        // decay D_ti = exp2(c_t - c_i) for i <= t: factored (one multiply) or direct
+        if (!zero) {
+          const float ct = c2[t];
+          if (sm.factored[sb]) {
+            const float dt = sm.da[sb][t];
+            const float* dbi = sm.db[sb] + i0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= dt * dbi[i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] *= i0 + i <= t ? exp2f(ct - c2[i0 + i]) : 0.f;
+          }
+        }
         if (row < C) {
-          const float bt = sm.beta[sb][t], ct = c2[t];
+          const float bt = sm.beta[sb][t];
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
             if (!zero) {
-              w.x = i0 + i + 0 < t ? bt * v[i + 0] * exp2f(ct - c2[i0 + i + 0]) : 0.f;
-              w.y = i0 + i + 1 < t ? bt * v[i + 1] * exp2f(ct - c2[i0 + i + 1]) : 0.f;
-              w.z = i0 + i + 2 < t ? bt * v[i + 2] * exp2f(ct - c2[i0 + i + 2]) : 0.f;
-              w.w = i0 + i + 3 < t ? bt * v[i + 3] * exp2f(ct - c2[i0 + i + 3]) : 0.f;
+              w.x = i0 + i + 0 < t ? bt * v[i + 0] : 0.f;
+              w.y = i0 + i + 1 < t ? bt * v[i + 1] : 0.f;
+              w.z = i0 + i + 2 < t ? bt * v[i + 2] : 0.f;
+              w.w = i0 + i + 3 < t ? bt * v[i + 3] : 0.f;
             }
             *reinterpret_cast<float4*>(&sm.a[t * PA + i0 + i]) = w;
           }
         } else {
-          const float ct = c2[t];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = (!zero && i0 + i <= t) ? p.scale * v[i] * exp2f(ct - c2[i0 + i]) : 0.f;
+          for (int i = 0; i < 32; ++i) v[i] = (!zero && i0 + i <= t) ? p.scale * v[i] : 0.f;
           store_half_row_bf16(sm.m[buf], t, hf, v);
         }
       }
@@ -538,6 +557,31 @@ __global__ void __launch_bounds__(NT, 1)
       }
     };
     int last_kq[2] = {0, nchunks > 1 ? 1 : -1};  // last K|Q load per buffer (for the drain)
+    // g and beta of chunk m into slot m & 3 (the role's last warp; lane l: steps 2l, 2l+1).
+    // Slot m & 3 last held chunk m - 4, which the prep role scanned before announcing
+    // chunk m - 3, so the slot is free once the serial role has taken chunk m - 3.
+    auto stage_scalars = [&](int m) {
+      if (warp != kRoleWarps - 1 || m >= nchunks) return;
+      const int t = m * C + 2 * lane;
+      float x[4] = {0.f, 0.f, 0.f, 0.f};
+      if (t < p.seqlen) {
+        x[0] = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
+        x[2] = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
+      }
+      if (t + 1 < p.seqlen) {
+        x[1] = load_any(p.g, b * p.g_sb + (int64_t)(t + 1) * p.g_st + h * p.g_sh, p.g_dtype);
+        x[3] = load_any(p.beta, b * p.b_sb + (int64_t)(t + 1) * p.b_st + h * p.b_sh, p.b_dtype);
+      }
+      sm.gs[m & 3][2 * lane] = x[0];
+      sm.gs[m & 3][2 * lane + 1] = x[1];
+      sm.bs[m & 3][2 * lane] = x[2];
+      sm.bs[m & 3][2 * lane + 1] = x[3];
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&sm.scal[m & 3]);
+    };
+    stage_scalars(0);
+    stage_scalars(1);
+    stage_scalars(2);
     if (swait(&sm.prep_ready, 0, 1)) state_step(0);
     for (int n = 0; n < nchunks && ok; ++n) {
       const int buf = n & 1, sb = n % 3;
@@ -591,6 +635,7 @@ __global__ void __launch_bounds__(NT, 1)
         for (int t = 0; t < 32; ++t) o[t] = fmaf(gm[t] * p.scale, o[t], um[t]);
       }
       tc::fence_before_sync();
+      stage_scalars(n + 3);  // chunk n took the prep role's announcement of chunk n
       if (n + 1 < nchunks) {
         if (!swait(&sm.prep_ready, (n + 1) & 1, 4)) break;
         state_step(n + 1);
