@@ -263,6 +263,16 @@ __global__ void __launch_bounds__(NT, 1)
     int last_v = 0;  // last V load issued (for the bounded drain)
     for (int m = 0; m < nchunks && ok; ++m) {
       const int buf = m & 1, sb = m % 3;
+      // ---- [K;Q] K^T first: the scalar scan below runs under the MMA
+      if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
+      if (pt == 0) {
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t base = tc::smem_u32(sm.kq[buf][kk >> 2]) + (kk & 3) * 32;
+          tc::mma_f16(tmem + kColD1, tc::sdesc_sw128(base, 16, 1024), tc::sdesc_sw128(base, 16, 1024), i_kk,
+                      kk != 0);
+        }
+        tc::mma_commit(&sm.bar_p1);
+      }
       // ---- scalars: cumulative log decay c, gamma = e^c, e = e^(c_C - c), beta
       if (pw == 0) {
         constexpr float kLog2e = 1.4426950408889634f;
@@ -305,16 +315,6 @@ __global__ void __launch_bounds__(NT, 1)
         sm.db[sb][2 * lane] = exp2f(ref - l0);
         sm.db[sb][2 * lane + 1] = exp2f(ref - l1);
         if (lane == 0) sm.factored[sb] = (hi - lo) < 60.f;
-      }
-      // ---- [K;Q] K^T
-      if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
-      if (pt == 0) {
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t base = tc::smem_u32(sm.kq[buf][kk >> 2]) + (kk & 3) * 32;
-          tc::mma_f16(tmem + kColD1, tc::sdesc_sw128(base, 16, 1024), tc::sdesc_sw128(base, 16, 1024), i_kk,
-                      kk != 0);
-        }
-        tc::mma_commit(&sm.bar_p1);
       }
       if (!pwait(&sm.bar_p1, m & 1, 2)) break;
       // ---- A (fp32) from K K^T rows (lanes 0-63), M (bf16) from Q K^T rows (lanes 64-127);
@@ -523,20 +523,31 @@ __global__ void __launch_bounds__(NT, 1)
     }
     // State step of chunk n: S^T -> bf16 operand tile (atom hf holds dk 64 hf ..); S^T *=
     // gamma_C in TMEM. Then the S products of chunk n (thread 0).
+    // The state decays lazily: S^T = big_g * (TMEM S) with big_g the product of the chunk
+    // decays since the last renormalisation; chunk n's update adds K^T U diag(e) / big_g, and
+    // TMEM is rescaled only when big_g would fall below 2^-100 (fp32 keeps the ratio exact).
+    float big_g = 1.f, inv_next = 1.f;
     auto state_step = [&](int n) {
       const int buf = n & 1, sb = n % 3;
-      const float gl = sm.gam[sb][C - 1];
+      const float gnext = big_g * sm.gam[sb][C - 1];
+      const bool renorm = gnext < 0x1p-100f;  // identical in every thread of the role
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         float f[32];
         tmem_row32(lane_addr + kColS + 64 * hf + 32 * c, f);
-        store_half_row_bf16(sm.st[hf], j, c, f);
-        uint32_t r[32];
+        if (renorm) {
+          uint32_t r[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(f[i] * gl);
-        tc::tmem_st_32x32(lane_addr + kColS + 64 * hf + 32 * c, r);
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(f[i] * gnext);
+          tc::tmem_st_32x32(lane_addr + kColS + 64 * hf + 32 * c, r);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) f[i] *= big_g;
+        store_half_row_bf16(sm.st[hf], j, c, f);
       }
-      tc::tmem_st_wait();
+      if (renorm) tc::tmem_st_wait();
+      big_g = renorm ? 1.f : gnext;
+      inv_next = 1.f / big_g;
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       role_sync(1);
@@ -598,7 +609,7 @@ __global__ void __launch_bounds__(NT, 1)
         store_half_row_bf16(sm.ut, j, hf, up);
         const float* ee = sm.ee[sb] + 32 * hf;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) up[i] *= ee[i];
+        for (int i = 0; i < 32; ++i) up[i] *= ee[i] * inv_next;
         store_half_row_bf16(sm.st[0], j, hf, up);
       }
       tc::fence_proxy_async_smem();
@@ -679,8 +690,8 @@ __global__ void __launch_bounds__(NT, 1)
         tc::tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          if (p.layout == PBK_STATE_KV) st[(c0 + i) * D + j] = __uint_as_float(r[i]);
-          else st[j * D + c0 + i] = __uint_as_float(r[i]);
+          if (p.layout == PBK_STATE_KV) st[(c0 + i) * D + j] = __uint_as_float(r[i]) * big_g;
+          else st[j * D + c0 + i] = __uint_as_float(r[i]) * big_g;
         }
       }
     }
