@@ -363,11 +363,14 @@ __global__ void quest_gather_kernel(const pbk_quest_desc d, int k, int tail, bf1
 //   j <  k*page          : archive token pages[j / page] * page + j % page (visible)
 //   j <  k*page + tail   : archive tail token (visible)
 //   otherwise            : window key j - R (visible per the window mask)
-// CTA = (split of kSplitKeys virtual keys, group*kv + key head); 128 threads: two keys
-// per thread for the logits, one output dim per thread for P V. Partials (m, l, acc[d])
-// go to the workspace; quest_combine_kernel merges them.
+// CTA = (split of kSplitKeys virtual keys, group*kv + key head), 256 threads. Logits: one
+// key per thread (its 256-byte row in 16-byte loads). P V: warp w takes keys 32w..32w+31,
+// lane l dims 4l..4l+3, so each V row is one coalesced 256-byte warp load; the eight warps'
+// partial sums meet in shared memory. Partials (m, l, acc[d]) go to the workspace;
+// quest_combine_kernel merges them.
 // ---------------------------------------------------------------------------------
-constexpr int kAttThreads = 128;
+constexpr int kAttThreads = 256;
+constexpr int kAttWarps = kAttThreads / 32;
 constexpr int kSplitKeys = 256;
 constexpr int kAttRows = 4;  // query rows per pass
 
@@ -375,13 +378,14 @@ __device__ __forceinline__ bool key_visible(int kp, int qp, int window, int sink
   return kp <= qp && ((qp - kp) < window || kp < sinks);
 }
 
-__global__ void __launch_bounds__(kAttThreads) quest_attend_kernel(const pbk_quest_desc d, int k, int tail, int splits,
+__global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_quest_desc d, int k, int tail, int splits,
                                                                   float* part) {
   __shared__ __align__(16) float qs[kAttRows][kD];
-  __shared__ float logit[kAttRows][kSplitKeys];
+  __shared__ float prob[kAttRows][kSplitKeys];
   __shared__ int kidx[kSplitKeys];     // archive token, or -1 - window index
-  __shared__ float red[kAttRows][kAttThreads / 32];
+  __shared__ float red[kAttRows][kAttWarps];
   __shared__ float sh_m[kAttRows], sh_l[kAttRows];
+  __shared__ __align__(16) float accs[kAttWarps][kAttRows][kD];
   const int split = blockIdx.x, n = blockIdx.y / d.kv, h = blockIdx.y % d.kv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int groups = d.h / d.kv, rows = d.t * groups;
@@ -392,15 +396,15 @@ __global__ void __launch_bounds__(kAttThreads) quest_attend_kernel(const pbk_que
   const bf16* wkeys = reinterpret_cast<const bf16*>(d.win_keys);
   const bf16* wvals = reinterpret_cast<const bf16*>(d.win_values);
   const float sl2 = d.scale * 1.4426950408889634f;  // softmax in base 2
-  for (int j = tid; j < kSplitKeys; j += kAttThreads) {
-    const int vj = j0 + j;
+  {
+    const int vj = j0 + tid;
     int idx = 0;
-    if (j < nkeys) {
+    if (tid < nkeys) {
       if (vj < k * d.page) idx = d.pages[((int64_t)n * d.kv + h) * k + vj / d.page] * d.page + vj % d.page;
       else if (vj < n_ret) idx = (d.n_arch / d.page) * d.page + (vj - k * d.page);
       else idx = -1 - (vj - n_ret);
     }
-    kidx[j] = idx;
+    kidx[tid] = idx;
   }
   for (int r0 = 0; r0 < rows; r0 += kAttRows) {
     const int nr = min(kAttRows, rows - r0);
@@ -416,20 +420,25 @@ __global__ void __launch_bounds__(kAttThreads) quest_attend_kernel(const pbk_que
       qs[r][dd] = v;
     }
     __syncthreads();
-    // logits: thread handles keys tid and tid + 128
-    for (int j = tid; j < kSplitKeys; j += kAttThreads) {
+    // logits of key `tid`
+    float lg[kAttRows];
+    {
       float acc[kAttRows] = {0.f, 0.f, 0.f, 0.f};
-      const int idx = kidx[j];
-      if (j < nkeys) {
+      const int idx = kidx[tid];
+      if (tid < nkeys) {
         const bf16* kr = idx >= 0 ? keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
                                   : wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
-        for (int d0 = 0; d0 < kD; d0 += 8) {
+        uint4 raw[kD / 8];
+#pragma unroll
+        for (int c = 0; c < kD / 8; ++c) raw[c] = *reinterpret_cast<const uint4*>(kr + 8 * c);
+#pragma unroll
+        for (int c = 0; c < kD / 8; ++c) {
           float kv8[8];
-          bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + d0), kv8);
+          bf16x8_to_f32(raw[c], kv8);
 #pragma unroll
           for (int r = 0; r < kAttRows; ++r) {
-            const float4 qa = *reinterpret_cast<const float4*>(&qs[r][d0]);
-            const float4 qb = *reinterpret_cast<const float4*>(&qs[r][d0 + 4]);
+            const float4 qa = *reinterpret_cast<const float4*>(&qs[r][8 * c]);
+            const float4 qb = *reinterpret_cast<const float4*>(&qs[r][8 * c + 4]);
             acc[r] = fmaf(qa.x, kv8[0], acc[r]); acc[r] = fmaf(qa.y, kv8[1], acc[r]);
             acc[r] = fmaf(qa.z, kv8[2], acc[r]); acc[r] = fmaf(qa.w, kv8[3], acc[r]);
             acc[r] = fmaf(qb.x, kv8[4], acc[r]); acc[r] = fmaf(qb.y, kv8[5], acc[r]);
@@ -439,20 +448,18 @@ __global__ void __launch_bounds__(kAttThreads) quest_attend_kernel(const pbk_que
       }
 #pragma unroll
       for (int r = 0; r < kAttRows; ++r) {
-        bool vis = j < nkeys && r < nr;
+        bool vis = tid < nkeys && r < nr;
         if (vis && idx < 0) {
           const int rr = r0 + r, ti = rr / groups;
           vis = key_visible(d.kpos[-1 - idx], d.qpos[n * d.t + ti], d.window, d.sinks);
         }
-        logit[r][j] = vis ? acc[r] * sl2 : -INFINITY;
+        lg[r] = vis ? acc[r] * sl2 : -INFINITY;
       }
     }
-    __syncthreads();
-    // row max and sum over this split's keys
-    float m[kAttRows];
+    // row max over the split
 #pragma unroll
     for (int r = 0; r < kAttRows; ++r) {
-      float x = fmaxf(logit[r][tid], logit[r][tid + kAttThreads]);
+      float x = lg[r];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
       if (lane == 0) red[r][warp] = x;
@@ -460,45 +467,57 @@ __global__ void __launch_bounds__(kAttThreads) quest_attend_kernel(const pbk_que
     __syncthreads();
     if (tid < kAttRows) {
       float x = red[tid][0];
-      for (int w = 1; w < kAttThreads / 32; ++w) x = fmaxf(x, red[tid][w]);
+      for (int w = 1; w < kAttWarps; ++w) x = fmaxf(x, red[tid][w]);
       sh_m[tid] = x;
     }
     __syncthreads();
 #pragma unroll
     for (int r = 0; r < kAttRows; ++r) {
-      m[r] = sh_m[r];
-      float s = 0.f;
-      for (int j = tid; j < kSplitKeys; j += kAttThreads) {
-        const float p = m[r] == -INFINITY ? 0.f : exp2f(logit[r][j] - m[r]);
-        logit[r][j] = p;
-        s += p;
-      }
-      s = warp_sum(s);
+      const float m = sh_m[r];
+      const float p = m == -INFINITY ? 0.f : exp2f(lg[r] - m);
+      prob[r][tid] = p;
+      const float s = warp_sum(p);
       if (lane == 0) red[r][warp] = s;
     }
     __syncthreads();
     if (tid < kAttRows) {
       float x = 0.f;
-      for (int w = 0; w < kAttThreads / 32; ++w) x += red[tid][w];
+      for (int w = 0; w < kAttWarps; ++w) x += red[tid][w];
       sh_l[tid] = x;
     }
-    __syncthreads();
-    // P V: thread = output dim
-    float acc[kAttRows] = {0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < nkeys; ++j) {
+    // P V: warp keys 32 warp .., lane dims 4 lane ..
+    float acc[kAttRows][4] = {};
+    const int kend = min(32 * warp + 32, nkeys);
+    for (int j = 32 * warp; j < kend; ++j) {
       const int idx = kidx[j];
       const bf16* vr = idx >= 0 ? vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
                                 : wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
-      const float v = __bfloat162float(vr[tid]);
+      const uint2 raw = *reinterpret_cast<const uint2*>(vr + 4 * lane);
+      const float v0 = __uint_as_float(raw.x << 16), v1 = __uint_as_float(raw.x & 0xffff0000u);
+      const float v2 = __uint_as_float(raw.y << 16), v3 = __uint_as_float(raw.y & 0xffff0000u);
 #pragma unroll
-      for (int r = 0; r < kAttRows; ++r) acc[r] = fmaf(logit[r][j], v, acc[r]);
+      for (int r = 0; r < kAttRows; ++r) {
+        const float pr = prob[r][j];
+        acc[r][0] = fmaf(pr, v0, acc[r][0]);
+        acc[r][1] = fmaf(pr, v1, acc[r][1]);
+        acc[r][2] = fmaf(pr, v2, acc[r][2]);
+        acc[r][3] = fmaf(pr, v3, acc[r][3]);
+      }
     }
-    for (int r = 0; r < nr; ++r) {
+#pragma unroll
+    for (int r = 0; r < kAttRows; ++r)
+      *reinterpret_cast<float4*>(&accs[warp][r][4 * lane]) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    __syncthreads();
+    for (int e = tid; e < nr * kD; e += kAttThreads) {
+      const int r = e / kD, dd = e % kD;
+      float x = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAttWarps; ++w) x += accs[w][r][dd];
       const int rr = r0 + r, ti = rr / groups, g = rr % groups;
       const int64_t row = (((int64_t)n * d.t + ti) * d.h + h * groups + g) * splits + split;
       float* pp = part + row * (kD + 2);
-      pp[tid] = acc[r];
-      if (tid == 0) pp[kD] = sh_m[r], pp[kD + 1] = sh_l[r];
+      pp[dd] = x;
+      if (dd == 0) pp[kD] = sh_m[r], pp[kD + 1] = sh_l[r];
     }
   }
 }
