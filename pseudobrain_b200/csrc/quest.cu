@@ -286,55 +286,107 @@ __device__ __forceinline__ void collect_in_order(KeyOf key_of, IdxOf idx_of, int
 }
 
 constexpr int kCandCap = 4096;  // candidates held in shared memory
+constexpr int kSegCap = 4096;   // segment maxima held in shared memory (131072 pages)
+constexpr int kSegRegs = 16;    // candidate segments a warp keeps in registers per pass
+
+struct TopkSmem {
+  SelectSmem ss;
+  uint32_t seg_key[kSegCap];  // ordered keys of the row's segment maxima
+  int32_t cseg[kSegCap];      // candidate segments, ascending
+  uint32_t cand_key[kCandCap];
+  int32_t cand_idx[kCandCap];
+};
 
 // One CTA per (group, key head) row of scores. With segment maxima (the max of every 32
 // consecutive pages), the k-th largest segment maximum tau bounds the k-th largest page
 // score from below (the top k segments hold k distinct pages scoring >= tau), so the top k
-// are among the pages scoring >= tau: one counting pass and one writing pass collect them
-// in index order into shared memory, and the exact selection runs there. When there are
-// too few segments or too many candidates, the selection runs over the whole row.
+// are among the pages scoring >= tau, all inside segments whose maximum is >= tau. Those
+// segments are listed in index order, only their pages are read (one warp-wide load per
+// segment, in registers), the pages scoring >= tau are placed in index order into shared
+// memory, and the exact selection runs there. When there are too few segments, too many
+// segments or too many candidates, the selection runs over the whole row.
 __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* scores, const float* segmax, int npages,
                                                                   int nseg, int k, int32_t* pages) {
-  __shared__ SelectSmem ss;
-  __shared__ uint32_t cand_key[kCandCap];
-  __shared__ int32_t cand_idx[kCandCap];
+  extern __shared__ __align__(16) uint8_t topk_raw[];
+  TopkSmem& ts = *reinterpret_cast<TopkSmem*>(topk_raw);
+  SelectSmem& ss = ts.ss;
   const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* s = scores + (int64_t)row * npages;
   int32_t* out = pages + (int64_t)row * k;
+  const uint32_t lt = (1u << lane) - 1u;
   uint32_t prefix, kk;
-  if (segmax != nullptr && nseg >= k) {
+  if (segmax != nullptr && nseg >= k && nseg <= kSegCap) {
     const float* sg = segmax + (int64_t)row * nseg;
+    for (int i = threadIdx.x; i < nseg; i += kTopkThreads) ts.seg_key[i] = ordered_key(sg[i]);
+    __syncthreads();
     uint32_t tau, unused;
-    radix_select([&](int i) { return ordered_key(sg[i]); }, nseg, (uint32_t)k, ss, tau, unused);
-    // count candidates (key >= tau) per warp-contiguous range, then place them in order
-    const uint32_t lt = (1u << lane) - 1u;
-    const int R = warp_range(npages);
-    const int lo = min(warp * R, npages), hi = min(lo + R, npages);
-    int cnt = 0;
-    for (int j = lo; j < hi; j += 32) {
-      const int i = j + lane;
-      cnt += __popc(__ballot_sync(0xffffffffu, i < hi && ordered_key(s[min(i, npages - 1)]) >= tau));
-    }
-    int pos, zero, total;
-    warp_bases(cnt, 0, ss, pos, zero, total);
-    if (total <= kCandCap) {
+    radix_select([&](int i) { return ts.seg_key[i]; }, nseg, (uint32_t)k, ss, tau, unused);
+    // candidate segments (key >= tau) in index order
+    {
+      const int R = warp_range(nseg);
+      const int lo = min(warp * R, nseg), hi = min(lo + R, nseg);
+      int cnt = 0;
       for (int j = lo; j < hi; j += 32) {
         const int i = j + lane;
-        const uint32_t u = ordered_key(s[min(i, npages - 1)]);
-        const bool c = i < hi && u >= tau;
+        cnt += __popc(__ballot_sync(0xffffffffu, i < hi && ts.seg_key[i] >= tau));
+      }
+      int pos, zero, total;
+      warp_bases(cnt, 0, ss, pos, zero, total);
+      for (int j = lo; j < hi; j += 32) {
+        const int i = j + lane;
+        const bool c = i < hi && ts.seg_key[i] >= tau;
         const uint32_t bc = __ballot_sync(0xffffffffu, c);
-        if (c) {
-          const int at = pos + __popc(bc & lt);
-          cand_key[at] = u;
-          cand_idx[at] = i;
-        }
+        if (c) ts.cseg[pos + __popc(bc & lt)] = i;
         pos += __popc(bc);
       }
       __syncthreads();
-      radix_select([&](int i) { return cand_key[i]; }, total, (uint32_t)k, ss, prefix, kk);
-      collect_in_order([&](int i) { return cand_key[i]; }, [&](int i) { return cand_idx[i]; }, total, prefix, kk, ss,
-                       out);
-      return;
+      // pages of the candidate segments: warp w takes candidate segments [w P, (w+1) P),
+      // lane = page within the segment
+      const int nc = total, P = (nc + 31) / 32;
+      const int c0 = min(warp * P, nc), c1 = min(c0 + P, nc);
+      int pcnt = 0;
+      for (int b0 = c0; b0 < c1; b0 += kSegRegs) {
+        float x[kSegRegs];
+#pragma unroll
+        for (int u = 0; u < kSegRegs; ++u) {
+          const int page = b0 + u < c1 ? ts.cseg[b0 + u] * 32 + lane : npages;
+          x[u] = page < npages ? s[page] : -INFINITY;
+        }
+#pragma unroll
+        for (int u = 0; u < kSegRegs; ++u)
+          pcnt += __popc(__ballot_sync(0xffffffffu, b0 + u < c1 && ordered_key(x[u]) >= tau &&
+                                                        ts.cseg[min(b0 + u, c1 - 1)] * 32 + lane < npages));
+      }
+      int ppos, pzero, ptotal;
+      warp_bases(pcnt, 0, ss, ppos, pzero, ptotal);
+      if (ptotal <= kCandCap) {
+        for (int b0 = c0; b0 < c1; b0 += kSegRegs) {
+          float x[kSegRegs];
+#pragma unroll
+          for (int u = 0; u < kSegRegs; ++u) {
+            const int page = b0 + u < c1 ? ts.cseg[b0 + u] * 32 + lane : npages;
+            x[u] = page < npages ? s[page] : -INFINITY;
+          }
+#pragma unroll
+          for (int u = 0; u < kSegRegs; ++u) {
+            const int page = b0 + u < c1 ? ts.cseg[b0 + u] * 32 + lane : npages;
+            const uint32_t key = ordered_key(x[u]);
+            const bool c = page < npages && key >= tau;
+            const uint32_t bc = __ballot_sync(0xffffffffu, c);
+            if (c) {
+              const int at = ppos + __popc(bc & lt);
+              ts.cand_key[at] = key;
+              ts.cand_idx[at] = page;
+            }
+            ppos += __popc(bc);
+          }
+        }
+        __syncthreads();
+        radix_select([&](int i) { return ts.cand_key[i]; }, ptotal, (uint32_t)k, ss, prefix, kk);
+        collect_in_order([&](int i) { return ts.cand_key[i]; }, [&](int i) { return ts.cand_idx[i]; }, ptotal,
+                         prefix, kk, ss, out);
+        return;
+      }
     }
   }
   radix_select([&](int i) { return ordered_key(s[i]); }, npages, (uint32_t)k, ss, prefix, kk);
@@ -379,18 +431,21 @@ __device__ __forceinline__ bool key_visible(int kp, int qp, int window, int sink
 }
 
 __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_quest_desc d, int k, int tail, int splits,
-                                                                  float* part) {
+                                                                  float* part, int split0) {
   __shared__ __align__(16) float qs[kAttRows][kD];
   __shared__ float prob[kAttRows][kSplitKeys];
   __shared__ int kidx[kSplitKeys];     // archive token, or -1 - window index
   __shared__ float red[kAttRows][kAttWarps];
   __shared__ float sh_m[kAttRows], sh_l[kAttRows];
   __shared__ __align__(16) float accs[kAttWarps][kAttRows][kD];
-  const int split = blockIdx.x, n = blockIdx.y / d.kv, h = blockIdx.y % d.kv;
+  const int split = split0 + blockIdx.x, n = blockIdx.y / d.kv, h = blockIdx.y % d.kv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int groups = d.h / d.kv, rows = d.t * groups;
-  const int n_ret = k * d.page + tail, n_all = n_ret + d.n_win;
-  const int j0 = split * kSplitKeys, nkeys = min(kSplitKeys, n_all - j0);
+  // splits [0, sr) hold the retrieved keys, splits [sr, splits) the window keys
+  const int n_ret = k * d.page + tail, sr = (n_ret + kSplitKeys - 1) / kSplitKeys;
+  const bool win_split = split >= sr;
+  const int j0 = win_split ? (split - sr) * kSplitKeys : split * kSplitKeys;
+  const int nkeys = min(kSplitKeys, (win_split ? d.n_win : n_ret) - j0);
   const bf16* keys = reinterpret_cast<const bf16*>(d.keys);
   const bf16* vals = reinterpret_cast<const bf16*>(d.values);
   const bf16* wkeys = reinterpret_cast<const bf16*>(d.win_keys);
@@ -400,9 +455,9 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
     const int vj = j0 + tid;
     int idx = 0;
     if (tid < nkeys) {
-      if (vj < k * d.page) idx = d.pages[((int64_t)n * d.kv + h) * k + vj / d.page] * d.page + vj % d.page;
-      else if (vj < n_ret) idx = (d.n_arch / d.page) * d.page + (vj - k * d.page);
-      else idx = -1 - (vj - n_ret);
+      if (win_split) idx = -1 - vj;
+      else if (vj < k * d.page) idx = d.pages[((int64_t)n * d.kv + h) * k + vj / d.page] * d.page + vj % d.page;
+      else idx = (d.n_arch / d.page) * d.page + (vj - k * d.page);
     }
     kidx[tid] = idx;
   }
@@ -487,21 +542,31 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
     }
     // P V: warp keys 32 warp .., lane dims 4 lane ..
     float acc[kAttRows][4] = {};
-    const int kend = min(32 * warp + 32, nkeys);
-    for (int j = 32 * warp; j < kend; ++j) {
-      const int idx = kidx[j];
-      const bf16* vr = idx >= 0 ? vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
-                                : wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
-      const uint2 raw = *reinterpret_cast<const uint2*>(vr + 4 * lane);
-      const float v0 = __uint_as_float(raw.x << 16), v1 = __uint_as_float(raw.x & 0xffff0000u);
-      const float v2 = __uint_as_float(raw.y << 16), v3 = __uint_as_float(raw.y & 0xffff0000u);
+    const int jb = 32 * warp, kn = min(32, nkeys - jb);
+    {  // all 32 value rows of the warp in flight at once
+      uint2 raw[32];
 #pragma unroll
-      for (int r = 0; r < kAttRows; ++r) {
-        const float pr = prob[r][j];
-        acc[r][0] = fmaf(pr, v0, acc[r][0]);
-        acc[r][1] = fmaf(pr, v1, acc[r][1]);
-        acc[r][2] = fmaf(pr, v2, acc[r][2]);
-        acc[r][3] = fmaf(pr, v3, acc[r][3]);
+      for (int u = 0; u < 32; ++u) {
+        raw[u] = make_uint2(0u, 0u);
+        if (u < kn) {
+          const int idx = kidx[jb + u];
+          const bf16* vr = idx >= 0 ? vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
+                                    : wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+          raw[u] = *reinterpret_cast<const uint2*>(vr + 4 * lane);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const float v0 = __uint_as_float(raw[u].x << 16), v1 = __uint_as_float(raw[u].x & 0xffff0000u);
+        const float v2 = __uint_as_float(raw[u].y << 16), v3 = __uint_as_float(raw[u].y & 0xffff0000u);
+#pragma unroll
+        for (int r = 0; r < kAttRows; ++r) {
+          const float pr = u < kn ? prob[r][jb + u] : 0.f;
+          acc[r][0] = fmaf(pr, v0, acc[r][0]);
+          acc[r][1] = fmaf(pr, v1, acc[r][1]);
+          acc[r][2] = fmaf(pr, v2, acc[r][2]);
+          acc[r][3] = fmaf(pr, v3, acc[r][3]);
+        }
       }
     }
 #pragma unroll
@@ -547,10 +612,11 @@ __global__ void quest_combine_kernel(const pbk_quest_desc d, int splits, const f
 // Launch helpers (called from capi.cu after validation).
 // ---------------------------------------------------------------------------------
 int quest_k(const pbk_quest_desc& d) { return min(d.budget, d.n_arch / d.page); }
-int quest_splits(const pbk_quest_desc& d) {
-  const int n_all = quest_k(d) * d.page + (d.n_arch % d.page) + d.n_win;
-  return (n_all + kSplitKeys - 1) / kSplitKeys;
+// Splits of the retrieved keys (pages and tail) and of the window keys.
+int quest_ret_splits(const pbk_quest_desc& d) {
+  return (quest_k(d) * d.page + (d.n_arch % d.page) + kSplitKeys - 1) / kSplitKeys;
 }
+int quest_splits(const pbk_quest_desc& d) { return quest_ret_splits(d) + (d.n_win + kSplitKeys - 1) / kSplitKeys; }
 // Segment maxima are kept for rows of at least kSegMinPages pages (ceil(pages / 32) each).
 int quest_nseg(const pbk_quest_desc& d) {
   const int npages = d.n_arch / d.page;
@@ -587,7 +653,12 @@ cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStr
     quest_score_kernel<<<dim3((npages + kScoreThreads - 1) / kScoreThreads, d.kv), kScoreThreads, smem, st>>>(
         d, npages, scores, segmax, nseg);
   }
-  quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, 0, st>>>(scores, segmax, npages, nseg, k, d.pages);
+  {
+    cudaError_t e = cudaFuncSetAttribute(quest_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(TopkSmem));
+    if (e != cudaSuccess) return e;
+  }
+  quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, sizeof(TopkSmem), st>>>(scores, segmax, npages, nseg, k, d.pages);
   return cudaGetLastError();
 }
 
@@ -626,7 +697,7 @@ cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st) {
   const int k = quest_k(d), tail = d.n_arch % d.page, splits = quest_splits(d);
   if (splits == 0) return cudaSuccess;
-  quest_attend_kernel<<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part);
+  quest_attend_kernel<<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0);
   quest_combine_kernel<<<d.nq * d.t * d.h, kD, 0, st>>>(d, splits, part);
   return cudaGetLastError();
 }
