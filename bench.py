@@ -337,10 +337,13 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
             dist.all_gather_into_tensor(gath_gdn, o_gdn.view(t, -1))
             dist.all_gather_into_tensor(gath_swa, o_swa.view(t, -1))
 
-    def step():
+    def step():  # the GDN branch's all-gather runs under the attention branch
         gdn()
+        w = dist.all_gather_into_tensor(gath_gdn, o_gdn.view(t, -1), async_op=True) if world > 1 else None
         swa()
-        gather()
+        if world > 1:
+            dist.all_gather_into_tensor(gath_swa, o_swa.view(t, -1))
+            w.wait()
 
     steps = max(3, min(args.steps, 5))
     t_step = timed(step, steps, 3) / steps

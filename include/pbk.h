@@ -205,6 +205,27 @@ PBK_API int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream);
  * split-key pass plus a log-sum-exp combine. Gathers the pages itself. */
 PBK_API int pbk_quest_attend(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
+/* pbk_quest_attend with n_sink always-visible keys placed before the selected pages:
+ * rows 0 .. n_sink-1 of sink_keys / sink_values (bf16, element strides sink_stride_kv per
+ * key head and sink_stride_n per row). This is the key set of the serving path's
+ * piece_attention (pb27_vllm/memory.py:1311-1490): the sink positions, the retrieved
+ * blocks, the partial block before the window and the masked window. Workspace bytes from
+ * pbk_quest_attend_sinks_workspace(desc, n_sink). */
+PBK_API size_t pbk_quest_attend_sinks_workspace(const pbk_quest_desc* desc, int32_t n_sink);
+PBK_API int pbk_quest_attend_sinks(const pbk_quest_desc* desc, const void* sink_keys, const void* sink_values,
+                                   int32_t n_sink, int64_t sink_stride_kv, int64_t sink_stride_n, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* Exact rerank (pb27_vllm/memory.py:854-872): for c candidate pages per (group, key head),
+ * cand [nq, kv, c] int32 ascending, the exact score max over the head's query rows
+ * and the page's tokens of q.k (fp32 on bf16 keys); the best
+ * k = min(desc->budget, c) candidates, ties to the lowest page, go to desc->pages
+ * [nq, kv, k] ascending. Uses desc->q, keys (arc strides), page; workspace bytes from
+ * pbk_quest_rerank_workspace(desc, c). */
+PBK_API size_t pbk_quest_rerank_workspace(const pbk_quest_desc* desc, int32_t c);
+PBK_API int pbk_quest_rerank(const pbk_quest_desc* desc, const int32_t* cand, int32_t c, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* Copy `sel` pages per (group, key head) listed in desc->pages ([nq, kv, sel], any
  * order, repeats allowed) and then the partial tail into out_keys / out_values
  * [nq, kv, sel * page + tail, d] (bf16, contiguous): what retrieve() returns

@@ -77,6 +77,10 @@ SIGNATURES = {
     "pbk_quest_select": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_select_noalloc": (ctypes.c_int, [_QD, _VP]),
     "pbk_quest_attend": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
+    "pbk_quest_attend_sinks_workspace": (ctypes.c_size_t, [_QD, _I32]),
+    "pbk_quest_attend_sinks": (ctypes.c_int, [_QD, _VP, _VP, _I32, _I64, _I64, _VP, ctypes.c_size_t, _VP]),
+    "pbk_quest_rerank_workspace": (ctypes.c_size_t, [_QD, _I32]),
+    "pbk_quest_rerank": (ctypes.c_int, [_QD, _VP, _I32, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_gather": (ctypes.c_int, [_QD, _I32, _VP, _VP, _VP]),
     "pbk_quest_bounds": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I64, _I64, _VP, _VP, _I64, _I64, _I32, _VP]),
     "pbk_swa_prefill": (ctypes.c_int, [ctypes.POINTER(PbkSwaDesc), _VP]),

@@ -60,8 +60,6 @@ constexpr size_t kWsAlign = 256;
 size_t round_up(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
 bool aligned_elems(int64_t stride, int64_t elems) { return stride % elems == 0; }
 
-// Shapes, pointers and alignment shared by the Quest entry points. `need` selects
-// which tensors must be present: 1 select, 2 attend, 4 gather.
 int validate_swa(const pbk_swa_desc* d) {
   if (d == nullptr) return PBK_ERR_INVALID;
   if (d->batch < 0 || d->seqlen < 0 || d->h < 1 || d->kv < 1 || d->sinks < 0 || !(d->scale > 0.f))
@@ -82,6 +80,8 @@ int validate_swa(const pbk_swa_desc* d) {
   return PBK_OK;
 }
 
+// Shapes, pointers and alignment shared by the Quest entry points. `need` selects
+// which tensors must be present: 1 select, 2 attend, 4 gather.
 int validate_quest(const pbk_quest_desc* d, int need) {
   if (d == nullptr) return PBK_ERR_INVALID;
   if (d->nq < 0 || d->t < 1 || d->kv < 1 || d->h < d->kv || d->page < 1 || d->n_arch < 0 || d->budget < 0 ||
@@ -208,7 +208,17 @@ size_t pbk_quest_select_workspace(const pbk_quest_desc* desc) {
 
 size_t pbk_quest_attend_workspace(const pbk_quest_desc* desc) {
   if (validate_quest(desc, 2) != PBK_OK) return 0;
-  return round_up(pbk::quest_partial_bytes(*desc));
+  return round_up(pbk::quest_partial_bytes(*desc, 0));
+}
+
+size_t pbk_quest_attend_sinks_workspace(const pbk_quest_desc* desc, int32_t n_sink) {
+  if (validate_quest(desc, 2) != PBK_OK || n_sink < 0) return 0;
+  return round_up(pbk::quest_partial_bytes(*desc, n_sink));
+}
+
+size_t pbk_quest_rerank_workspace(const pbk_quest_desc* desc, int32_t c) {
+  if (desc == nullptr || c < 1 || desc->nq < 0 || desc->kv < 1) return 0;
+  return round_up((size_t)desc->nq * desc->kv * c * sizeof(float));
 }
 
 int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
@@ -233,14 +243,54 @@ int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream) {
   return launch_status(pbk::launch_quest_select_noalloc(*desc, static_cast<cudaStream_t>(stream)));
 }
 
-int pbk_quest_attend(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+int pbk_quest_attend_sinks(const pbk_quest_desc* desc, const void* sink_keys, const void* sink_values, int32_t n_sink,
+                           int64_t sink_stride_kv, int64_t sink_stride_n, void* workspace, size_t workspace_bytes,
+                           void* stream) {
   int st = validate_quest(desc, 2);
   if (st != PBK_OK) return st;
-  const size_t need = pbk::quest_partial_bytes(*desc);
+  if (n_sink < 0) return PBK_ERR_INVALID;
+  if (n_sink > 0) {
+    if (!sink_keys || !sink_values) return PBK_ERR_INVALID;
+    if (!aligned16(sink_keys) || !aligned16(sink_values) || !aligned_elems(sink_stride_kv, 8) ||
+        !aligned_elems(sink_stride_n, 8))
+      return PBK_ERR_ALIGN;
+  }
+  const size_t need = pbk::quest_partial_bytes(*desc, n_sink);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return PBK_ERR_WORKSPACE;
   if (desc->nq == 0) return PBK_OK;
   if ((st = check_current_device()) != PBK_OK) return st;
-  return launch_status(pbk::launch_quest_attend(*desc, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
+  pbk::SinkKeys sk;
+  sk.k = static_cast<const __nv_bfloat16*>(sink_keys);
+  sk.v = static_cast<const __nv_bfloat16*>(sink_values);
+  sk.s_kv = sink_stride_kv;
+  sk.s_n = sink_stride_n;
+  sk.n = n_sink;
+  return launch_status(
+      pbk::launch_quest_attend(*desc, static_cast<float*>(workspace), sk, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_quest_attend(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  return pbk_quest_attend_sinks(desc, nullptr, nullptr, 0, 0, 0, workspace, workspace_bytes, stream);
+}
+
+int pbk_quest_rerank(const pbk_quest_desc* desc, const int32_t* cand, int32_t c, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (desc == nullptr || cand == nullptr || c < 1) return PBK_ERR_INVALID;
+  if (desc->nq < 0 || desc->t < 1 || desc->kv < 1 || desc->h % desc->kv != 0 || desc->page < 1 || desc->budget < 1)
+    return PBK_ERR_INVALID;
+  if (desc->d != 128) return PBK_ERR_SHAPE;
+  if (!desc->q || !desc->keys || !desc->pages) return PBK_ERR_INVALID;
+  if (!aligned16(desc->q) || !aligned_elems(desc->q_stride_n, 8) || !aligned_elems(desc->q_stride_t, 8) ||
+      !aligned_elems(desc->q_stride_h, 8) || !aligned16(desc->keys) || !aligned_elems(desc->arc_stride_kv, 8) ||
+      !aligned_elems(desc->arc_stride_n, 8))
+    return PBK_ERR_ALIGN;
+  const size_t need = (size_t)desc->nq * desc->kv * c * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return PBK_ERR_WORKSPACE;
+  if (desc->nq == 0) return PBK_OK;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(
+      pbk::launch_quest_rerank(*desc, cand, c, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_quest_gather(const pbk_quest_desc* desc, int32_t sel, void* out_keys, void* out_values, void* stream) {

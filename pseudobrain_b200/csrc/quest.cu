@@ -425,13 +425,14 @@ constexpr int kAttThreads = 256;
 constexpr int kAttWarps = kAttThreads / 32;
 constexpr int kSplitKeys = 256;
 constexpr int kAttRows = 4;  // query rows per pass
+constexpr int kSinkTag = -(1 << 30);  // kidx encoding of always-visible leading keys: kSinkTag - i
 
 __device__ __forceinline__ bool key_visible(int kp, int qp, int window, int sinks) {
   return kp <= qp && ((qp - kp) < window || kp < sinks);
 }
 
 __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_quest_desc d, int k, int tail, int splits,
-                                                                  float* part, int split0) {
+                                                                     float* part, int split0, const SinkKeys sk) {
   __shared__ __align__(16) float qs[kAttRows][kD];
   __shared__ float prob[kAttRows][kSplitKeys];
   __shared__ int kidx[kSplitKeys];     // archive token, or -1 - window index
@@ -441,8 +442,9 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
   const int split = split0 + blockIdx.x, n = blockIdx.y / d.kv, h = blockIdx.y % d.kv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int groups = d.h / d.kv, rows = d.t * groups;
-  // splits [0, sr) hold the retrieved keys, splits [sr, splits) the window keys
-  const int n_ret = k * d.page + tail, sr = (n_ret + kSplitKeys - 1) / kSplitKeys;
+  // splits [0, sr) hold the retrieved keys (leading keys, pages, tail), splits [sr, splits)
+  // the window keys
+  const int n_ret = sk.n + k * d.page + tail, sr = (n_ret + kSplitKeys - 1) / kSplitKeys;
   const bool win_split = split >= sr;
   const int j0 = win_split ? (split - sr) * kSplitKeys : split * kSplitKeys;
   const int nkeys = min(kSplitKeys, (win_split ? d.n_win : n_ret) - j0);
@@ -456,8 +458,13 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
     int idx = 0;
     if (tid < nkeys) {
       if (win_split) idx = -1 - vj;
-      else if (vj < k * d.page) idx = d.pages[((int64_t)n * d.kv + h) * k + vj / d.page] * d.page + vj % d.page;
-      else idx = (d.n_arch / d.page) * d.page + (vj - k * d.page);
+      else if (vj < sk.n) idx = kSinkTag - vj;
+      else if (vj - sk.n < k * d.page) {
+        const int r = vj - sk.n;
+        idx = d.pages[((int64_t)n * d.kv + h) * k + r / d.page] * d.page + r % d.page;
+      } else {
+        idx = (d.n_arch / d.page) * d.page + (vj - sk.n - k * d.page);
+      }
     }
     kidx[tid] = idx;
   }
@@ -481,8 +488,9 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
       float acc[kAttRows] = {0.f, 0.f, 0.f, 0.f};
       const int idx = kidx[tid];
       if (tid < nkeys) {
-        const bf16* kr = idx >= 0 ? keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
-                                  : wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+        const bf16* kr = idx >= 0         ? keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
+                         : idx > kSinkTag ? wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n
+                                          : sk.k + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
         uint4 raw[kD / 8];
 #pragma unroll
         for (int c = 0; c < kD / 8; ++c) raw[c] = *reinterpret_cast<const uint4*>(kr + 8 * c);
@@ -504,7 +512,7 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
 #pragma unroll
       for (int r = 0; r < kAttRows; ++r) {
         bool vis = tid < nkeys && r < nr;
-        if (vis && idx < 0) {
+        if (vis && idx < 0 && idx > kSinkTag) {
           const int rr = r0 + r, ti = rr / groups;
           vis = key_visible(d.kpos[-1 - idx], d.qpos[n * d.t + ti], d.window, d.sinks);
         }
@@ -550,8 +558,9 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
         raw[u] = make_uint2(0u, 0u);
         if (u < kn) {
           const int idx = kidx[jb + u];
-          const bf16* vr = idx >= 0 ? vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
-                                    : wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+          const bf16* vr = idx >= 0         ? vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
+                           : idx > kSinkTag ? wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n
+                                            : sk.v + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
           raw[u] = *reinterpret_cast<const uint2*>(vr + 4 * lane);
         }
       }
@@ -609,14 +618,74 @@ __global__ void quest_combine_kernel(const pbk_quest_desc d, int splits, const f
 }  // namespace
 
 // ---------------------------------------------------------------------------------
+// Exact rerank (pb27_vllm/memory.py:854-872): the score of candidate page c is the max
+// over the key head's query rows and the page's tokens of q.k in fp32. CTA = (8
+// candidates, group*kv + key head), warp = one candidate page, lane = tokens lane,
+// lane + 32, ...; the query rows sit in shared memory.
+// ---------------------------------------------------------------------------------
+constexpr int kRerankRows = 64;  // query rows in shared memory per pass
+__global__ void __launch_bounds__(256) quest_rerank_kernel(const pbk_quest_desc d, const int32_t* cand, int c,
+                                                           float* exact) {
+  __shared__ __align__(16) float qs[kRerankRows][kD];
+  const int n = blockIdx.y / d.kv, h = blockIdx.y % d.kv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = d.h / d.kv, rows = d.t * groups;
+  const int ci = blockIdx.x * 8 + warp;
+  const int page = ci < c ? cand[((int64_t)n * d.kv + h) * c + ci] : 0;
+  const bf16* base = reinterpret_cast<const bf16*>(d.keys) + h * d.arc_stride_kv;
+  float best = -INFINITY;
+  for (int r0 = 0; r0 < rows; r0 += kRerankRows) {
+    const int nr = min(kRerankRows, rows - r0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < nr * kD; e += blockDim.x) {
+      const int r = e / kD, dd = e % kD, ti = (r0 + r) / groups, g = (r0 + r) % groups;
+      qs[r][dd] = __bfloat162float(reinterpret_cast<const bf16*>(d.q)[n * d.q_stride_n + ti * d.q_stride_t +
+                                                                        (int64_t)(h * groups + g) * d.q_stride_h + dd]);
+    }
+    __syncthreads();
+    if (ci >= c) continue;
+    for (int s = lane; s < d.page; s += 32) {
+      const bf16* kr = base + ((int64_t)page * d.page + s) * d.arc_stride_n;
+      float kf[kD];
+#pragma unroll
+      for (int c8 = 0; c8 < kD / 8; ++c8) bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + 8 * c8), kf + 8 * c8);
+      for (int r = 0; r < nr; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int dd = 0; dd < kD; dd += 4) {
+          const float4 qa = *reinterpret_cast<const float4*>(&qs[r][dd]);
+          acc = fmaf(qa.x, kf[dd], acc);
+          acc = fmaf(qa.y, kf[dd + 1], acc);
+          acc = fmaf(qa.z, kf[dd + 2], acc);
+          acc = fmaf(qa.w, kf[dd + 3], acc);
+        }
+        best = fmaxf(best, acc);
+      }
+    }
+  }
+  if (ci >= c) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
+  if (lane == 0) exact[((int64_t)n * d.kv + h) * c + ci] = best;
+}
+
+// pages[i] = cand[row][pages[i]]: the selected candidate positions become page indices.
+__global__ void quest_map_kernel(const int32_t* cand, int c, int k, int nrows, int32_t* pages) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nrows * k) return;
+  pages[i] = cand[(int64_t)(i / k) * c + pages[i]];
+}
+
+// ---------------------------------------------------------------------------------
 // Launch helpers (called from capi.cu after validation).
 // ---------------------------------------------------------------------------------
 int quest_k(const pbk_quest_desc& d) { return min(d.budget, d.n_arch / d.page); }
 // Splits of the retrieved keys (pages and tail) and of the window keys.
-int quest_ret_splits(const pbk_quest_desc& d) {
-  return (quest_k(d) * d.page + (d.n_arch % d.page) + kSplitKeys - 1) / kSplitKeys;
+int quest_ret_splits(const pbk_quest_desc& d, int n_sink) {
+  return (n_sink + quest_k(d) * d.page + (d.n_arch % d.page) + kSplitKeys - 1) / kSplitKeys;
 }
-int quest_splits(const pbk_quest_desc& d) { return quest_ret_splits(d) + (d.n_win + kSplitKeys - 1) / kSplitKeys; }
+int quest_splits(const pbk_quest_desc& d, int n_sink) {
+  return quest_ret_splits(d, n_sink) + (d.n_win + kSplitKeys - 1) / kSplitKeys;
+}
 // Segment maxima are kept for rows of at least kSegMinPages pages (ceil(pages / 32) each).
 int quest_nseg(const pbk_quest_desc& d) {
   const int npages = d.n_arch / d.page;
@@ -629,8 +698,8 @@ size_t quest_select_floats(const pbk_quest_desc& d) {
   return (d.scores ? 0 : rows * (d.n_arch / d.page)) + rows * quest_nseg(d);
 }
 size_t quest_score_bytes(const pbk_quest_desc& d) { return quest_select_floats(d) * sizeof(float); }
-size_t quest_partial_bytes(const pbk_quest_desc& d) {
-  return (size_t)d.nq * d.t * d.h * quest_splits(d) * (kD + 2) * sizeof(float);
+size_t quest_partial_bytes(const pbk_quest_desc& d, int n_sink) {
+  return (size_t)d.nq * d.t * d.h * quest_splits(d, n_sink) * (kD + 2) * sizeof(float);
 }
 
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st) {
@@ -694,11 +763,23 @@ cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st
   return launch_quest_select(d, scratch, st);
 }
 
-cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st) {
-  const int k = quest_k(d), tail = d.n_arch % d.page, splits = quest_splits(d);
+cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, cudaStream_t st) {
+  const int k = quest_k(d), tail = d.n_arch % d.page, splits = quest_splits(d, sk.n);
   if (splits == 0) return cudaSuccess;
-  quest_attend_kernel<<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0);
+  quest_attend_kernel<<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
   quest_combine_kernel<<<d.nq * d.t * d.h, kD, 0, st>>>(d, splits, part);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quest_rerank(const pbk_quest_desc& d, const int32_t* cand, int c, float* exact, cudaStream_t st) {
+  const int k = min(d.budget, c), nrows = d.nq * d.kv;
+  if (k <= 0) return cudaSuccess;
+  quest_rerank_kernel<<<dim3((c + 7) / 8, nrows), 256, 0, st>>>(d, cand, c, exact);
+  cudaError_t e = cudaFuncSetAttribute(quest_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(TopkSmem));
+  if (e != cudaSuccess) return e;
+  quest_topk_kernel<<<nrows, kTopkThreads, sizeof(TopkSmem), st>>>(exact, nullptr, c, 0, k, d.pages);
+  quest_map_kernel<<<(nrows * k + 255) / 256, 256, 0, st>>>(cand, c, k, nrows, d.pages);
   return cudaGetLastError();
 }
 

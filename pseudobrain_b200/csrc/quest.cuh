@@ -1,26 +1,38 @@
 // Launchers of the Quest kernels (quest.cu), called by the C ABI after validation.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
 #include "../../include/pbk.h"
 
 namespace pbk {
+// Always-visible keys placed before the retrieved pages (the serving path's sink
+// positions): n rows of k / v at element strides s_kv (key head) and s_n (row).
+struct SinkKeys {
+  const __nv_bfloat16* k = nullptr;
+  const __nv_bfloat16* v = nullptr;
+  int64_t s_kv = 0, s_n = 0;
+  int n = 0;
+};
 int quest_k(const pbk_quest_desc& d);
-int quest_splits(const pbk_quest_desc& d);
+int quest_splits(const pbk_quest_desc& d, int n_sink);
 size_t quest_score_bytes(const pbk_quest_desc& d);
 size_t quest_select_floats(const pbk_quest_desc& d);
 // Floats of the fixed scratch of pbk_quest_select_noalloc: the largest allowed score count
 // plus its segment maxima (rows of at least 1024 pages keep ceil(pages / 32) of them).
 constexpr size_t kNoAllocFloats = (size_t)PBK_QUEST_NOALLOC_MAX_SCORES + PBK_QUEST_NOALLOC_MAX_SCORES / 32 +
                                   PBK_QUEST_NOALLOC_MAX_SCORES / 1024;
-size_t quest_partial_bytes(const pbk_quest_desc& d);
+size_t quest_partial_bytes(const pbk_quest_desc& d, int n_sink);
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st);
 bool quest_score_tc_supported(const pbk_quest_desc& d);
 cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float* segmax, int nseg, cudaStream_t st);
 cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st);
-cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, cudaStream_t st);
+cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, cudaStream_t st);
+// Exact rescoring of c candidate pages [nq, kv, c] (ascending) and selection of the best
+// k = min(budget, c) into desc.pages, ascending; `exact` holds nq * kv * c floats.
+cudaError_t launch_quest_rerank(const pbk_quest_desc& d, const int32_t* cand, int c, float* exact, cudaStream_t st);
 cudaError_t launch_quest_gather(const pbk_quest_desc& d, int sel, void* ok, void* ov, cudaStream_t st);
 cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int page, int64_t ks_kv, int64_t ks_n, void* kmax,
                                 void* kmin, int64_t bs_kv, int64_t bs_p, int first_page, cudaStream_t st);

@@ -158,18 +158,11 @@ def select_pages(q: torch.Tensor, kmax: torch.Tensor, kmin: torch.Tensor, n_arch
     return pages
 
 
-def attend_pages(q: torch.Tensor, qpos: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, n_arch: int,
-                 page: int, pages: torch.Tensor, win_keys: torch.Tensor, win_values: torch.Tensor,
-                 kpos: torch.Tensor, window: int, sinks: int = 0, scale: float | None = None,
-                 out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
-    """Exact attention of q [nq,t,h,128] (positions qpos [nq,t] int32) over, per key head,
-    the selected pages [nq,KV,k] of keys/values [KV,N,128], the archive's partial tail and
-    the window keys win_keys/win_values [KV,S,128] at positions kpos [S] int32 under the
-    reference's window mask. Returns [nq,t,h,128]."""
+def _attend_desc(q, qpos, keys, values, n_arch, page, pages, win_keys, win_values, kpos, window, sinks, scale, out):
+    """Descriptor of an attention call (see attend_pages); `out` [nq,t,h,128] receives it."""
     for t_, w in ((keys, "keys"), (values, "values"), (win_keys, "win_keys"), (win_values, "win_values")):
         _require(t_, w)
     nq, t, h, d = q.shape
-    out = torch.empty(nq, t, h, d, dtype=out_dtype, device=q.device)
     desc = _desc(q, page, n_arch, pages.shape[-1], keys=keys, values=values, pages=pages)
     desc.n_win, desc.window, desc.sinks = win_keys.shape[1], window, sinks
     desc.scale = float(d ** -0.5 if scale is None else scale)
@@ -178,13 +171,28 @@ def attend_pages(q: torch.Tensor, qpos: torch.Tensor, keys: torch.Tensor, values
     desc.win_stride_kv, desc.win_stride_n = win_keys.stride(0), win_keys.stride(1)
     desc.out = out.data_ptr()
     desc.out_stride_n, desc.out_stride_t, desc.out_stride_h = out.stride(0), out.stride(1), out.stride(2)
-    desc.out_dtype = _capi.PBK_BF16 if out_dtype == torch.bfloat16 else _capi.PBK_F32
+    desc.out_dtype = _capi.PBK_BF16 if out.dtype == torch.bfloat16 else _capi.PBK_F32
     if qpos.dtype != torch.int32 or kpos.dtype != torch.int32:
         raise TypeError("qpos and kpos must be int32")
     if pages.shape[:2] != (nq, keys.shape[0]) or pages.dtype != torch.int32 or not pages.is_contiguous():
         raise ValueError("pages must be contiguous int32 [nq, KV, k]")
     if pages.shape[-1] > n_arch // page:
         raise ValueError("more selected pages than complete archive pages")
+    return desc
+
+
+def attend_pages(q: torch.Tensor, qpos: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, n_arch: int,
+                 page: int, pages: torch.Tensor, win_keys: torch.Tensor, win_values: torch.Tensor,
+                 kpos: torch.Tensor, window: int, sinks: int = 0, scale: float | None = None,
+                 out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Exact attention of q [nq,t,h,128] (positions qpos [nq,t] int32) over, per key head,
+    the selected pages [nq,KV,k] of keys/values [KV,N,128], the archive's partial tail and
+    the window keys win_keys/win_values [KV,S,128] at positions kpos [S] int32 under the
+    reference's window mask. Returns [nq,t,h,128]."""
+    nq, t, h, d = q.shape
+    out = torch.empty(nq, t, h, d, dtype=out_dtype, device=q.device)
+    desc = _attend_desc(q, qpos, keys, values, n_arch, page, pages, win_keys, win_values, kpos, window, sinks,
+                        scale, out)
     ws = _workspace(LIB.pbk_quest_attend_workspace(desc), q.device)
     with torch.cuda.device(q.device):
         check(LIB.pbk_quest_attend(desc, ws.data_ptr(), ws.numel(), _stream(q)), "pbk_quest_attend")

@@ -21,6 +21,11 @@ Fixtures:
                   inputs (run in fp32), GQA 4 query / 2 key heads, d=128: a sliding window
                   of 100 with 4 sinks over T=260 through the reference's query-chunked path
                   (_chunked_window_attention, chunk forced to 128), and full causal T=200.
+  serving.npz     the serving twins of pb27_vllm/memory.py: retrieve_blocks (flat bound scores,
+                  exact rerank of the candidates, and the flat path without rerank) and
+                  piece_attention (sinks + retrieved blocks + partial tail + masked window,
+                  the SDPA branch) over an Archive of 2 key heads, 64-token blocks after the 4
+                  sink positions, for a decode piece (T=1) and a 3-token piece.
   quest.npz       archive_append + retrieve (flat mode, page 16, budget 4 pages) for a
                   decode query (T=1) and a 3-token query, plus the exact attention over
                   [retrieved ; window] as pseudobrain/transplant.py:619-628 computes it.
@@ -152,6 +157,37 @@ def make_swa(TR):
     np.savez_compressed(os.path.join(HERE, "swa.npz"), **out)
 
 
+def make_serving(MEM):
+    import torch
+    kv, groups, d, block = 2, 3, 128, 64
+    MEM.MEMORY.update(blocks=4, decode_blocks=4, rerank=12, block_size=block, neighbors=0, window=256)
+    cap = MEM.ORIGIN + 40 * block + 20
+    gen = torch.Generator().manual_seed(105)
+    keys = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    values = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    n_blk = cap // block
+    arc = MEM.Archive(keys, values, torch.empty(kv, n_blk, d), torch.empty(kv, n_blk, d))
+    arc.size = arc.prompt_len = cap
+    arc.dirty_lo, arc.dirty_hi = 0, n_blk - 1
+    arc.refresh_bounds(block)
+    out = dict(keys=_bits(keys.to(torch.bfloat16)), values=_bits(values.to(torch.bfloat16)),
+               kmax=_bits(arc.kmax.to(torch.bfloat16)), kmin=_bits(arc.kmin.to(torch.bfloat16)),
+               origin=np.int64(MEM.ORIGIN), sinks=np.int64(MEM.SINKS), block=np.int64(block),
+               window=np.int64(256), groups=np.int64(groups), budget=np.int64(4), rerank_pool=np.int64(12))
+    for name, t, rerank in (("t1", 1, True), ("t3", 3, True), ("flat", 1, False)):
+        q = torch.randn(t, kv * groups, d, generator=gen).to(torch.bfloat16).float()
+        q_pos = torch.arange(cap - t, cap)
+        q_min, q_max = int(q_pos[0]), int(q_pos[-1])
+        window = 256
+        limit = q_min - window + 1
+        top = MEM.retrieve_blocks(arc, q, groups, limit, rerank)
+        o = MEM.piece_attention(arc, q, q_pos, top, groups, window, d ** -0.5, None, q_min=q_min, q_max=q_max)
+        out.update({f"{name}_q": _bits(q.to(torch.bfloat16)), f"{name}_pos": q_pos.numpy().astype(np.int64),
+                    f"{name}_limit": np.int64(limit), f"{name}_rerank": np.int64(rerank),
+                    f"{name}_top": top.numpy().astype(np.int64), f"{name}_out": o.float().numpy()})
+    np.savez_compressed(os.path.join(HERE, "serving.npz"), **out)
+
+
 def main(reference_root: str) -> None:
     sys.path.insert(0, reference_root)
     import torch
@@ -159,13 +195,13 @@ def main(reference_root: str) -> None:
     from pseudobrain import exact_memory as E
     from pseudobrain import gated_deltanet as G
     from pseudobrain import transplant as TR
-    if len(sys.argv) > 2:  # regenerate only the named fixtures
-        for name in sys.argv[2:]:
-            {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR)}[name]()
-        return
-    make_gdn(G)
-    make_quest(E)
-    make_swa(TR)
+    sys.path.insert(0, os.path.join(reference_root, "serving", "pb27_vllm"))
+    os.environ.setdefault("PB27_MEMORY_OFFLOAD", "")
+    import pb27_vllm.memory as MEM
+    makers = {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR),
+              "serving": lambda: make_serving(MEM)}
+    for name in (sys.argv[2:] if len(sys.argv) > 2 else makers):  # all, or only the named fixtures
+        makers[name]()
     for name in sorted(os.listdir(HERE)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(HERE, name)), "bytes")

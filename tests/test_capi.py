@@ -80,3 +80,10 @@ def test_no_device_returns_error_without_launching(lib):
         pytest.skip("host has a GPU")
     from pseudobrain_b200 import _capi
     assert _capi.LIB.pbk_device_check(0) == -5
+
+
+def test_every_module_imports(lib):
+    """The Python mirrors import on a host without a GPU (they fail only when called)."""
+    import importlib
+    for m in ("gated_deltanet", "gdn_prefill", "exact_memory", "transplant", "serving", "sharding", "synthetic"):
+        importlib.import_module(f"pseudobrain_b200.{m}")

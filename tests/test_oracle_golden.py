@@ -127,3 +127,21 @@ def test_window_attention_matches_reference(case):
                                     None if window < 0 else window, int(f[f"{case}_sinks"]))
     for s, x in part.items():
         assert np.allclose(x, o[:, :, s:s + 50], rtol=0, atol=1e-12)
+
+
+@pytest.mark.parametrize("case", ["t1", "t3", "flat"])
+def test_serving_twins_match_reference(case):
+    """oracle/serving.py against pb27_vllm/memory.py's retrieve_blocks and piece_attention."""
+    from oracle import serving as osv
+    f = load_golden("serving.npz")
+    keys, values = _f32(f["keys"]), _f32(f["values"])
+    kmax, kmin = _f32(f["kmax"]), _f32(f["kmin"])
+    q = _f32(f[f"{case}_q"])
+    mem = dict(blocks=int(f["budget"]), decode_blocks=int(f["budget"]), rerank=int(f["rerank_pool"]),
+               block_size=int(f["block"]), window=int(f["window"]))
+    top = osv.retrieve_blocks(keys, kmax, kmin, q, int(f["groups"]), int(f[f"{case}_limit"]),
+                              bool(f[f"{case}_rerank"]), mem, keys.shape[1])
+    assert np.array_equal(top, f[f"{case}_top"])
+    o = osv.piece_attention(keys, values, q, f[f"{case}_pos"], top, int(f["groups"]), int(f["window"]),
+                            q.shape[-1] ** -0.5, int(f["block"]))
+    assert ogdn.rel_err(o, f[f"{case}_out"]) < FP32_TOL
