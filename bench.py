@@ -291,6 +291,47 @@ def measure_quest(args, timed, dev, rank, world, pk):
     }
 
 
+def measure_serving(args, timed, dev, rank, world, pk):
+    """The serving twins (pb27_vllm/memory.py retrieve_blocks with exact rerank +
+    piece_attention) for one decode token of a PB-27-shaped layer (24 query / 4 key heads,
+    head dim 128 here), a 262144-token archive in 64-token blocks, window 16384 and the
+    reference's defaults: 512 candidates reranked exactly, 256 blocks kept."""
+    import types
+    import torch
+    from pseudobrain_b200 import serving as S
+    kv, heads, d, block, window = 4, 24, 128, 64, 16384
+    cap = 262144 if args.size == "full" else 65536
+    gen = torch.Generator(device=dev).manual_seed(6 + 1000 * rank)
+    keys = torch.randn(kv, cap, d, device=dev, generator=gen).to(torch.bfloat16)
+    values = torch.randn(kv, cap, d, device=dev, generator=gen).to(torch.bfloat16)
+    n_blk = cap // block
+    arc = types.SimpleNamespace(keys=keys, values=values, kmax=torch.empty(kv, n_blk, d, dtype=torch.bfloat16, device=dev),
+                                kmin=torch.empty(kv, n_blk, d, dtype=torch.bfloat16, device=dev), size=cap,
+                                prompt_len=cap, hole_lo=0, hole_hi=0, smax=None, dirty_lo=0, dirty_hi=n_blk - 1)
+    q = torch.randn(1, heads, d, device=dev, generator=gen).to(torch.bfloat16)
+    q_pos = torch.tensor([cap - 1], device=dev)
+    limit = cap - window
+
+    def step():
+        top = S.retrieve_blocks(arc, q, heads // kv, limit, True)
+        S.piece_attention(arc, q, q_pos, top, heads // kv, window, d ** -0.5, q_min=cap - 1, q_max=cap - 1)
+
+    steps = max(args.steps, 20)
+    t = timed(step, steps, max(args.warmup, 3)) / steps
+    full = (limit - S.ORIGIN) // block
+    k = S.budget_for(full, True, cap, limit)
+    c = min(max(S.MEMORY["rerank"], 2 * k), full)
+    nbytes = (2 * full * kv * d * 2 + c * block * kv * d * 2 + k * block * kv * d * 2 * 2
+              + (window + S.SINKS) * kv * d * 2 * 2)
+    return {"metric": "serving decode piece (retrieve_blocks + rerank + piece_attention) per s", "value": world / t,
+            "unit": "pieces/s", "us_per_piece": t * 1e6,
+            "config": {"archive_tokens": cap, "kv_heads": kv, "q_heads": heads, "head_dim": d, "block": block,
+                       "window": window, "rerank_candidates": c, "blocks_kept": k},
+            "roofline": {"bound": "hbm", "achieved": nbytes / t / 1e9, "peak": pk["hbm"], "unit": "GB/s",
+                         "frac": nbytes / t / 1e9 / pk["hbm"], "traffic": None, "algorithmic_bytes": nbytes},
+            "gpu_launches": 8 * steps}
+
+
 def swa_pairs(t, window):
     """Visible (query, key) pairs of a causal window over t tokens."""
     w = min(window, t)
@@ -384,7 +425,7 @@ def run_ours(args, rank, world, local_rank):
     parts = {}
     clk = Clocks(local_rank)
     for name, fn in (("prefill", measure_prefill), ("decode", measure_decode), ("quest", measure_quest),
-                     ("hybrid", measure_hybrid)):
+                     ("hybrid", measure_hybrid), ("serving", measure_serving)):
         if args.workload in ("all", name):
             if name == "prefill":
                 with clk:
@@ -411,7 +452,7 @@ def run_ours(args, rank, world, local_rank):
         "roofline": head["roofline"], "e2e": head["e2e"], "gpu_launches": head["gpu_launches"],
         "clocks": clk.summary(),
     }
-    for name in ("decode", "quest", "hybrid"):
+    for name in ("decode", "quest", "hybrid", "serving"):
         if name in parts and parts[name] is not None and parts[name] is not head:
             line[name] = parts[name]
     if world == 1 and not args.no_cpu_baseline and "prefill" in parts:
@@ -483,7 +524,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("all", "prefill", "decode", "quest", "hybrid"), default="all",
+    ap.add_argument("--workload", choices=("all", "prefill", "decode", "quest", "hybrid", "serving"), default="all",
                     help="run one part only (profiling); the JSON line then carries that part")
     ap.add_argument("--size", choices=("full", "small"), default="full",
                     help="small: a reduced case of the same kernels for ncu captures (not a bench number)")
