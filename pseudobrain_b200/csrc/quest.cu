@@ -424,13 +424,15 @@ __global__ void quest_gather_kernel(const pbk_quest_desc d, int k, int tail, bf1
 constexpr int kAttThreads = 256;
 constexpr int kAttWarps = kAttThreads / 32;
 constexpr int kSplitKeys = 256;
-constexpr int kAttRows = 4;  // query rows per pass
+// query rows per pass: 4, or 8 when a key head has more than 4 query rows (the serving
+// layout's 6), so that every key and value row is read once per CTA
 constexpr int kSinkTag = -(1 << 30);  // kidx encoding of always-visible leading keys: kSinkTag - i
 
 __device__ __forceinline__ bool key_visible(int kp, int qp, int window, int sinks) {
   return kp <= qp && ((qp - kp) < window || kp < sinks);
 }
 
+template <int kAttRows>
 __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_quest_desc d, int k, int tail, int splits,
                                                                      float* part, int split0, const SinkKeys sk) {
   __shared__ __align__(16) float qs[kAttRows][kD];
@@ -485,7 +487,7 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
     // logits of key `tid`
     float lg[kAttRows];
     {
-      float acc[kAttRows] = {0.f, 0.f, 0.f, 0.f};
+      float acc[kAttRows] = {};
       const int idx = kidx[tid];
       if (tid < nkeys) {
         const bf16* kr = idx >= 0         ? keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
@@ -596,21 +598,46 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
   }
 }
 
+// One CTA (128 threads) per output row: the split weights exp2(m_s - M) in shared memory
+// (max and sum over the splits in parallel), then thread = output dim over all splits with
+// independent loads.
 __global__ void quest_combine_kernel(const pbk_quest_desc d, int splits, const float* part) {
+  extern __shared__ float w[];  // [splits]
+  __shared__ float red[kD / 32];
   const int row = blockIdx.x;  // (n, ti, head)
   const int head = row % d.h, ti = (row / d.h) % d.t, n = row / (d.h * d.t);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* pp = part + (int64_t)row * splits * (kD + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, pp[s * (kD + 2) + kD]);
-  float L = 0.f, acc = 0.f;
-  for (int s = 0; s < splits; ++s) {
+  float m = -INFINITY;
+  for (int s = tid; s < splits; s += kD) m = fmaxf(m, pp[s * (kD + 2) + kD]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float l = 0.f;
+  for (int s = tid; s < splits; s += kD) {
     const float ms = pp[s * (kD + 2) + kD];
-    const float w = ms == -INFINITY ? 0.f : exp2f(ms - M);
-    L = fmaf(pp[s * (kD + 2) + kD + 1], w, L);
-    acc = fmaf(pp[s * (kD + 2) + threadIdx.x], w, acc);
+    const float ws = ms == -INFINITY ? 0.f : exp2f(ms - M);
+    w[s] = ws;
+    l = fmaf(pp[s * (kD + 2) + kD + 1], ws, l);
   }
-  const float o = acc / L;
-  const int64_t off = n * d.out_stride_n + ti * d.out_stride_t + head * d.out_stride_h + threadIdx.x;
+  l = warp_sum(l);
+  if (lane == 0) red[warp] = l;
+  __syncthreads();
+  const float L = (red[0] + red[1]) + (red[2] + red[3]);
+  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  int s = 0;
+  for (; s + 4 <= splits; s += 4) {
+    acc0 = fmaf(pp[s * (kD + 2) + tid], w[s], acc0);
+    acc1 = fmaf(pp[(s + 1) * (kD + 2) + tid], w[s + 1], acc1);
+    acc2 = fmaf(pp[(s + 2) * (kD + 2) + tid], w[s + 2], acc2);
+    acc3 = fmaf(pp[(s + 3) * (kD + 2) + tid], w[s + 3], acc3);
+  }
+  for (; s < splits; ++s) acc0 = fmaf(pp[s * (kD + 2) + tid], w[s], acc0);
+  const float o = ((acc0 + acc1) + (acc2 + acc3)) / L;
+  const int64_t off = n * d.out_stride_n + ti * d.out_stride_t + head * d.out_stride_h + tid;
   if (d.out_dtype == PBK_BF16) reinterpret_cast<bf16*>(d.out)[off] = __float2bfloat16_rn(o);
   else reinterpret_cast<float*>(d.out)[off] = o;
 }
@@ -766,8 +793,16 @@ cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, cudaStream_t st) {
   const int k = quest_k(d), tail = d.n_arch % d.page, splits = quest_splits(d, sk.n);
   if (splits == 0) return cudaSuccess;
-  quest_attend_kernel<<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
-  quest_combine_kernel<<<d.nq * d.t * d.h, kD, 0, st>>>(d, splits, part);
+  if (d.t * (d.h / d.kv) > 4)
+    quest_attend_kernel<8><<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
+  else
+    quest_attend_kernel<4><<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
+  const int wbytes = splits * (int)sizeof(float);
+  if (wbytes > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(quest_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, wbytes);
+    if (e != cudaSuccess) return e;
+  }
+  quest_combine_kernel<<<d.nq * d.t * d.h, kD, wbytes, st>>>(d, splits, part);
   return cudaGetLastError();
 }
 
