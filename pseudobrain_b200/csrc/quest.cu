@@ -793,10 +793,14 @@ cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, cudaStream_t st) {
   const int k = quest_k(d), tail = d.n_arch % d.page, splits = quest_splits(d, sk.n);
   if (splits == 0) return cudaSuccess;
-  if (d.t * (d.h / d.kv) > 4)
+  if (quest_attend_mma_supported(d)) {
+    cudaError_t e = launch_quest_attend_mma(d, k, tail, splits, part, sk, st);
+    if (e != cudaSuccess) return e;
+  } else if (d.t * (d.h / d.kv) > 4) {
     quest_attend_kernel<8><<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
-  else
+  } else {
     quest_attend_kernel<4><<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
+  }
   const int wbytes = splits * (int)sizeof(float);
   if (wbytes > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(quest_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, wbytes);

@@ -4,7 +4,9 @@ the reference's golden outputs.
 Page bounds, page indices and gathered keys must be bit-exact. Scores: both sides sum
 exact bf16 x bf16 products in fp32 (orders differ), so selections agree exactly on
 these seeded inputs; every test also checks that the selection boundary is not a
-near-tie. Attention output: fp32 accumulation over bf16 inputs, 1e-4 relative
+near-tie. Attention output: bf16 tensor-core products with fp32 accumulation and the
+probabilities rounded to bf16 for the P V product (as flash attention does), ATT_TOL = 5e-3
+relative (BASELINE's bar for bf16 inputs is 2e-2)
 (fp32 output) or 1e-2 (bf16 output rounding).
 """
 from __future__ import annotations
@@ -18,6 +20,7 @@ from oracle import quest as oq
 from tests.conftest import load_golden
 
 pytestmark = pytest.mark.gpu
+ATT_TOL = 5e-3
 
 
 def _bf16(x, dev):
@@ -55,7 +58,7 @@ def test_golden_archive_retrieve_and_attention(cuda_device, quest_cfg):
         qpos = torch.from_numpy(f[f"{case}_qpos"]).to(cuda_device)
         kpos = torch.from_numpy(f["kpos"]).to(cuda_device)
         out = M.retrieve_attend(arc, q, groups, wk, wv, qpos, kpos, window)
-        assert ogdn.rel_err(out.cpu().numpy(), f[f"{case}_out"]) < 1e-4
+        assert ogdn.rel_err(out.cpu().numpy(), f[f"{case}_out"]) < ATT_TOL
 
 
 def _random_problem(seed, kv, heads, n_arch, n_win, page, nq, t, dev, plant=True):
@@ -135,7 +138,7 @@ def test_select_and_attend_match_oracle(cuda_device, kv, heads, n_arch, page, nq
         rk, rv, top = oq.retrieve(arc, q[i].transpose(1, 0, 2)[None], groups, page, budget)
         ref = oq.attend(q[i].transpose(1, 0, 2)[None], rk, rv, keys[None, :, n_arch:], values[None, :, n_arch:],
                         qpos[i], kpos, window, 0, groups)[0].transpose(1, 0, 2)
-        assert ogdn.rel_err(out[i].cpu().numpy(), ref) < 1e-4
+        assert ogdn.rel_err(out[i].cpu().numpy(), ref) < ATT_TOL
         # and the gather (retrieve's return value) is bit-exact
         gk, gv = M.gather_pages(dk, dvv, n_arch, page, pages[i:i + 1].contiguous(), dq[i:i + 1])
         assert np.array_equal(gk[0].float().cpu().numpy(), rk[0])
@@ -190,7 +193,7 @@ def test_config3_full_size(cuda_device):
         ref = oq.attend(q[i].transpose(1, 0, 2)[None], rk, rv, x["win_keys"].float().cpu().numpy()[None],
                         x["win_values"].float().cpu().numpy()[None], x["qpos"][i].cpu().numpy(),
                         x["kpos"].cpu().numpy(), x["window"], 0, 4)[0].transpose(1, 0, 2)
-        assert ogdn.rel_err(out[i].cpu().numpy(), ref) < 1e-4
+        assert ogdn.rel_err(out[i].cpu().numpy(), ref) < ATT_TOL
 
 
 def test_quest_rejects_bad_arguments(cuda_device):
