@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload all|prefill|decode|quest] [--size full|small]
 
-Headline (``value``): GDN chunked prefill of BASELINE config 1 (B=4, T=32768, 16 key /
+Headline (``value``): GDN chunked prefill of benchmark config 1 (B=4, T=32768, 16 key /
 32 value heads, dk=dv=128, chunk 64, bf16 q/k/v/beta, fp32 g and state) in tok/s,
 inputs resident in HBM, device-timed with CUDA events, max over ranks. The same line
 carries the other two parts of the metric, each with its own roofline:
@@ -364,7 +364,7 @@ def swa_pairs(t, window):
 
 
 def measure_hybrid(args, timed, dev, rank, world, pk):
-    """one hybrid layer over a 1M-token sequence (B=1). The GDN branch
+    """benchmark config 4: one hybrid layer over a 1M-token sequence (B=1). The GDN branch
     (16 key / 32 value heads) is split by value head over the ranks, and within a rank along
     T (segments chained by the segment scan) so a few heads still fill the SMs; the
     sliding-window attention branch (32 query / 8 key heads, window 4096) is split by key
@@ -467,8 +467,8 @@ def run_ours(args, rank, world, local_rank):
     line = {
         "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16 inputs, fp32 state/accumulation", "data": "synthetic (seeded, BASELINE config distributions)",
-        "config": {"workload": ("BASELINE config 1: GDN chunked prefill B=4 T=32768 Hk=16 Hv=32 dk=dv=128 chunk=64 "
+        "dtype": "bf16 inputs, fp32 state/accumulation", "data": "synthetic (seeded, benchmark config distributions)",
+        "config": {"workload": ("benchmark config 1: GDN chunked prefill B=4 T=32768 Hk=16 Hv=32 dk=dv=128 chunk=64 "
                                 "per GPU") if "prefill" in parts else f"{args.workload} part only",
                    "size": args.size, "global_batch": PREFILL[args.size]["batch"] * world,
                    "seq_len": PREFILL[args.size]["seqlen"],
@@ -535,9 +535,9 @@ def run_reference(args, rank):
     value = statistics.median(vals)
     return {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(vals),
             "warmup": 1, "ms_per_step": 4096 / value * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config distributions)",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, benchmark config distributions)",
             "impl": "reference",
-            "config": {"workload": "BASELINE config 1 prefill, bounded CPU sample B=1 T=4096 Hv=32 per step"},
+            "config": {"workload": "benchmark config 1 prefill, bounded CPU sample B=1 T=4096 Hv=32 per step"},
             "cpu_baseline": {**base, "value": value},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 

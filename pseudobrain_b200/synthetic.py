@@ -1,4 +1,4 @@
-"""Seeded synthetic inputs of the BASELINE configurations, generated on the device.
+"""Seeded synthetic inputs of the benchmark configurations, generated on the device.
 
 No public dataset is involved: every configuration is defined by shapes and value
 distributions (config 0 distributions: q, k ~ N(0,1) L2-normalised per head; v ~ N(0,1);
@@ -28,7 +28,7 @@ def gdn_inputs(batch: int, length: int, hk: int, hv: int, *, device, seed: int, 
 def quest_inputs(*, device, seed: int = 3, n_tokens: int = 1 << 20, kv: int = 8, heads: int = 32, d: int = 128,
                  page: int = 16, window: int = 4096, nq: int = 8, budget_tokens: int = 4096,
                  planted_scale: float = 45.0) -> dict:
-    """a bf16 KV cache of n_tokens (K, V ~ N(0,1)); the last `window`
+    """benchmark config 3: a bf16 KV cache of n_tokens (K, V ~ N(0,1)); the last `window`
     positions are the window, the rest is the archive with precomputed page bounds. nq
     single-token queries q ~ N(0,1) at position n_tokens - 1. For query i one seeded archive
     page p_i holds, in every key head g, 16 copies of bf16(planted_scale * unit mean of the

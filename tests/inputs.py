@@ -1,6 +1,6 @@
 """Seeded synthetic inputs shared by the parity tests (numpy, deterministic on any host).
 
-Distributions follow BASELINE config 0: q, k ~ N(0,1) then L2-normalised per head;
+Distributions follow benchmark config 0: q, k ~ N(0,1) then L2-normalised per head;
 v ~ N(0,1); beta = sigmoid(N(0,1)); g = logsigmoid(N(2,1)); the state ~ N(0, state_std).
 bf16 tensors are generated in fp32 and rounded, so the oracle sees exactly the
 values the kernel reads.

@@ -97,7 +97,7 @@ def test_multi_token_call_equals_token_by_token(cuda_device):
 
 
 def test_decode_config2_full_size_one_step(cuda_device):
-    """BASELINE config 2 shape (B=256, 16 key / 32 value heads, 537 MB state), one step."""
+    """benchmark config 2 shape (B=256, 16 key / 32 value heads, 537 MB state), one step."""
     from pseudobrain_b200 import gated_deltanet as G
     inp = gdn_inputs(2, 256, 1, 16, 32, bf16=True, g_bf16=True, state_std=0.02)
     d = to_device(inp, cuda_device)

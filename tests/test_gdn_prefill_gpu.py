@@ -1,8 +1,8 @@
 """GPU parity of the chunked prefill (pbk_gdn_prefill) against the oracle and the
 reference's golden outputs.
 
-fp32 inputs run the exact fp32 kernel: tolerance 1e-4 (BASELINE's fp32 bar). bf16
-inputs: 2e-2 norm-wise relative on o and on the final state (BASELINE's bf16 bar).
+fp32 inputs run the exact fp32 kernel: tolerance 1e-4 (the fp32 tolerance). bf16
+inputs: 2e-2 norm-wise relative on o and on the final state (the bf16 tolerance).
 """
 from __future__ import annotations
 
@@ -53,7 +53,7 @@ def test_prefill_bf16_matches_reference_golden(cuda_device):
 @pytest.mark.parametrize("batch,length,hk,hv,std", [
     (1, 64, 1, 1, 0.0), (1, 2048, 4, 4, 0.0), (2, 200, 2, 4, 0.02), (3, 1, 1, 2, 0.02), (1, 129, 1, 8, 0.0)])
 def test_prefill_fp32_matches_oracle(cuda_device, batch, length, hk, hv, std):
-    """Includes BASELINE config 0 (B=1, T=2048, H=4) and ragged lengths."""
+    """Includes benchmark config 0 (B=1, T=2048, H=4) and ragged lengths."""
     from pseudobrain_b200.gdn_prefill import gdn_prefill
     inp = gdn_inputs(length + hv, batch, length, hk, hv, state_std=std)
     d = to_device(inp, cuda_device)
@@ -171,7 +171,7 @@ def test_prefill_tc_split_equals_whole(cuda_device):
 
 
 def test_prefill_config1_tc_matches_exact_kernel(cuda_device):
-    """BASELINE config 1 at full size (B=4, T=32768, 16 key / 32 value heads): the
+    """benchmark config 1 at full size (B=4, T=32768, 16 key / 32 value heads): the
     tensor-core kernel against the exact fp32 kernel on the same bf16 inputs (fp32 copies),
     plus the first 2048 tokens of one sequence against the oracle."""
     from pseudobrain_b200.gdn_prefill import gdn_prefill

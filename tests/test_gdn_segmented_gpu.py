@@ -79,7 +79,7 @@ def test_segmented_matches_oracle(cuda_device, batch, length, hk, hv, segments):
 
 
 def test_segmented_long_sequence(cuda_device):
-    """BASELINE config-4 GDN shape per GPU of 8 (4 value heads, 2 key heads), shortened to
+    """benchmark config-4 GDN shape per GPU of 8 (4 value heads, 2 key heads), shortened to
     T = 65536 + 100: automatic segment count, against the unsplit kernel."""
     from pseudobrain_b200 import _capi
     from pseudobrain_b200.gdn_prefill import auto_segments, gdn_prefill, gdn_prefill_segmented

@@ -6,7 +6,7 @@ exact bf16 x bf16 products in fp32 (orders differ), so selections agree exactly 
 these seeded inputs; every test also checks that the selection boundary is not a
 near-tie. Attention output: bf16 tensor-core products with fp32 accumulation and the
 probabilities rounded to bf16 for the P V product (as flash attention does), ATT_TOL = 5e-3
-relative (BASELINE's bar for bf16 inputs is 2e-2)
+relative (the bar for bf16 inputs is 2e-2)
 (fp32 output) or 1e-2 (bf16 output rounding).
 """
 from __future__ import annotations
@@ -169,7 +169,7 @@ def test_ties_go_to_lowest_page(cuda_device):
 
 
 def test_config3_full_size(cuda_device):
-    """1M-token cache, 8 queries, 32/8 heads, page 16, 256-page budget,
+    """benchmark config 3: 1M-token cache, 8 queries, 32/8 heads, page 16, 256-page budget,
     4096 window. Exact page sets vs the oracle's scores on the same bounds, planted pages
     present, and attention within tolerance for two of the queries."""
     from pseudobrain_b200 import exact_memory as M

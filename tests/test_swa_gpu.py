@@ -1,7 +1,7 @@
 """GPU parity of the sliding-window attention kernel (pbk_swa_prefill) against the
 reference's golden outputs and the oracle (oracle/swa.py).
 
-bf16 inputs, fp32 accumulation: 2e-2 norm-wise relative (BASELINE's bf16 bar) on every
+bf16 inputs, fp32 accumulation: 2e-2 norm-wise relative (the bf16 tolerance) on every
 case, per head. A window of one key is exact (each query copies its own value row).
 """
 from __future__ import annotations
@@ -104,7 +104,7 @@ def test_strided_views_of_packed_projections(cuda_device):
 
 
 def test_long_sequence_sampled_rows(cuda_device):
-    """BASELINE config-4 branch shape per GPU (4 query heads on one key head, window 4096)
+    """benchmark config-4 branch shape per GPU (4 query heads on one key head, window 4096)
     at T=65536: query runs at the start, across tile boundaries and at the end against the
     oracle's row-subset form."""
     from pseudobrain_b200.transplant import causal_attention
