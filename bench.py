@@ -197,7 +197,7 @@ def measure_prefill(args, timed, dev, rank, world, pk):
         "e2e": {"value": world * tokens * e2e_steps / t_e2e, "unit": "tok/s",
                 "h2d_bytes_per_step": sum(tt.numel() * tt.element_size() for tt in host.values()),
                 "d2h_bytes_per_step": host_o.numel() * host_o.element_size()},
-        "gpu_launches": args.steps,
+        "gpu_launches": 2 * args.steps,  # chunk solve + recurrence
     }
 
 
@@ -432,7 +432,7 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         "swa": {"ms": t_swa * 1e3, "tflops": swa_flops / world / t_swa / 1e12,
                 "frac": swa_flops / world / t_swa / 1e12 / pk["tc_sustained"]},
         "e2e": None,
-        "gpu_launches": steps * (5 + 1),
+        "gpu_launches": steps * (4 * 2 + 1 + 1),  # 4 prefill runs (solve + recurrence), scan, attention
     }
     if world > 1:
         out["all_gather"] = {"ms": t_ag * 1e3, "bytes_received_per_gpu": ag_bytes,

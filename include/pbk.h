@@ -115,6 +115,17 @@ PBK_API int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream);
  * computed (the segment runs of pbk_gdn_segment_scan). */
 PBK_API int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream);
 
+/* pbk_gdn_prefill with the chunk solve split out: on the tensor-core path (bf16 q/k/v) a
+ * first kernel solves every chunk of every (sequence, value head) at once -- the
+ * state-independent T = (I + A)^-1 of gated_deltanet.py:131-140 and its products with
+ * diag(beta) and diag(beta gamma), 16 KB per chunk -- into `workspace`, and the recurrence
+ * kernel copies them in instead of solving in line. Same results as pbk_gdn_prefill (the
+ * same arithmetic). workspace: at least pbk_gdn_prefill_workspace(desc) bytes, 16-byte
+ * aligned, private to the call until it completes on `stream`. Off the tensor-core path
+ * (fp32 inputs) the workspace is unused and may be NULL. */
+PBK_API size_t pbk_gdn_prefill_workspace(const pbk_gdn_desc* desc);
+PBK_API int pbk_gdn_prefill_ws(const pbk_gdn_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Segment scan for a prefill split along T into nseg segments of whole 64-token chunks
  * (parallelism inside one long sequence; the reference runs a sequence's chunks in
  * order, gated_deltanet.py:157-163). A segment's recurrence is affine in its initial

@@ -10,7 +10,8 @@ namespace pbk {
 cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st);
 bool gdn_prefill_tc_supported(const pbk_gdn_desc& d);
-cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st);
+size_t gdn_prefill_tc_workspace(const pbk_gdn_desc& d);
+cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, cudaStream_t st);
 cudaError_t launch_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int batch,
                                     int nseg, int hv, cudaStream_t st);
 }
@@ -182,9 +183,29 @@ int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
   // bf16 inputs: tensor-core kernel (bf16 operands, fp32 state and accumulation);
   // fp32 inputs: the exact fp32 kernel.
   const cudaError_t e = pbk::gdn_prefill_tc_supported(*desc)
-                            ? pbk::launch_gdn_prefill_tc(*desc, static_cast<cudaStream_t>(stream))
+                            ? pbk::launch_gdn_prefill_tc(*desc, nullptr, static_cast<cudaStream_t>(stream))
                             : pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream));
   return launch_status(e);
+}
+
+size_t pbk_gdn_prefill_workspace(const pbk_gdn_desc* desc) {
+  if (validate_gdn(desc, true) != PBK_OK || !pbk::gdn_prefill_tc_supported(*desc)) return 0;
+  return pbk::gdn_prefill_tc_workspace(*desc);
+}
+
+int pbk_gdn_prefill_ws(const pbk_gdn_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = validate_gdn(desc, true);
+  if (st != PBK_OK) return st;
+  if (desc->batch == 0) return PBK_OK;
+  if (!pbk::gdn_prefill_tc_supported(*desc)) {  // no workspace use off the tensor-core path
+    if (desc->o.data == nullptr) return PBK_ERR_INVALID;
+    if ((st = check_current_device()) != PBK_OK) return st;
+    return launch_status(pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream)));
+  }
+  if (workspace == nullptr || workspace_bytes < pbk::gdn_prefill_tc_workspace(*desc)) return PBK_ERR_INVALID;
+  if (!aligned16(workspace)) return PBK_ERR_ALIGN;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_prefill_tc(*desc, workspace, static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int32_t batch, int32_t nseg,

@@ -61,7 +61,7 @@ struct __align__(1024) PrefillSmem {
   float da[3][C], db[3][C];  // exp2(c_t - c_ref), exp2(c_ref - c_i): the decay in factored form
   float gs[4][C], bs[4][C];  // raw g and beta, staged 3 chunks ahead by a serial warp
   int factored[3];           // the chunk's decay span allows the factored form
-  uint64_t bar_kq[2], bar_v, bar_p1, bar_p3, bar_ws, bar_s, prep_ready, drain_s, drain_p, scal[4];
+  uint64_t bar_kq[2], bar_v, bar_tb, bar_p1, bar_p3, bar_ws, bar_s, prep_ready, drain_s, drain_p, scal[4];
   uint32_t tmem_base;
   volatile int abort;
 };
@@ -83,6 +83,7 @@ struct PrefillArgs {
   const int32_t* state_indices;
   float scale;
   int* err;
+  const uint8_t* solve;  // TB | TBG of every (sequence, chunk, value head), or NULL: solved here
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -166,7 +167,364 @@ __device__ __forceinline__ void tile_store(const float (&acc)[4], float s, FS st
   st(g + 8, 8 * nt + 2 * t + 1, s * acc[3]);
 }
 
-template <typename TOut>
+
+// T = (I + A)^-1 for the strictly lower 64 x 64 fp32 A (row stride PA) into the fp32
+// scratch ts (tidx layout), by 8 warps (w = 0..7) that meet at sync(); scr holds 4 x (16 x
+// 24) fp32 blocks. Diagonal 16x16 blocks (warps 0-3, one block each, lane = column) by
+// right-looking substitution: v[r] accumulates sum_{m<r} A_rm x_m and becomes x_r when its
+// turn comes (one FMA on the chain per step). Off-diagonal blocks T_ij = -T_ii (sum_{k=j}^{i-1}
+// A_ik T_kj) in three levels: the two 32x32 diagonal halves (T_10, T_32), then the lower-left
+// 32x32 quarter as X = A_21 T_1 and T_21 = -T_2 X; each warp computes one 16x8 tile (n-tile
+// nt) with tf32 mma.sync. Ends with a sync().
+template <typename Sync>
+__device__ __forceinline__ void invert_unit_lower(const float* a, float* ts, float* scr, int w, int lane, Sync sync) {
+  if (w < 4) {
+    const int col = lane & 15, r0 = 16 * w;
+    float v[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) v[r] = 0.f;
+#pragma unroll
+    for (int mm = 0; mm < 16; ++mm) {
+      const float x = mm < col ? 0.f : (mm == col ? 1.f : -v[mm]);
+      v[mm] = x;
+#pragma unroll
+      for (int r = mm + 1; r < 16; ++r) v[r] = fmaf(a[(r0 + r) * PA + r0 + mm], x, v[r]);
+    }
+    if (lane < 16) {
+#pragma unroll
+      for (int r = 0; r < 16; ++r) ts[tidx(r0 + r, r0 + col)] = v[r];
+    }
+  }
+  sync();
+  auto sread = [&](int b) { return [=](int r, int c) { return scr[b * 384 + r * 24 + c]; }; };
+  auto swrite = [&](int b) { return [=](int r, int c, float x) { scr[b * 384 + r * 24 + c] = x; }; };
+  auto at = [&](int bi, int bj) { return [=](int r, int c) { return a[(16 * bi + r) * PA + 16 * bj + c]; }; };
+  auto tt = [&](int bi, int bj) { return [=](int r, int c) { return ts[tidx(16 * bi + r, 16 * bj + c)]; }; };
+  auto twrite = [&](int bi, int bj) {
+    return [=](int r, int c, float x) { ts[tidx(16 * bi + r, 16 * bj + c)] = x; };
+  };
+  const int blk = w >> 1, nt = w & 1;
+  if (blk < 2) {  // T_10 (warps 0-1), T_32 (warps 2-3)
+    const int j = 2 * blk, i = j + 1;
+    float acc[4] = {};
+    tile_mma(acc, at(i, j), tt(j, j), nt, lane);
+    tile_store(acc, 1.f, swrite(blk), nt, lane);
+    __syncwarp();
+    float acc2[4] = {};
+    tile_mma(acc2, tt(i, i), sread(blk), nt, lane);
+    tile_store(acc2, -1.f, twrite(i, j), nt, lane);
+  }
+  sync();
+  const int r = 2 + (blk >> 1), c = blk & 1;
+  {  // X_rc = sum_{k=c}^{1} A_rk T_kc
+    float acc[4] = {};
+    for (int k = c; k < 2; ++k) tile_mma(acc, at(r, k), tt(k, c), nt, lane);
+    tile_store(acc, 1.f, swrite(blk), nt, lane);
+  }
+  sync();
+  {  // T_rc = -sum_{k=2}^{r} T_rk X_kc
+    float acc[4] = {};
+    for (int k = 2; k <= r; ++k) tile_mma(acc, tt(r, k), sread(2 * (k - 2) + c), nt, lane);
+    tile_store(acc, -1.f, twrite(r, c), nt, lane);
+  }
+  sync();
+}
+
+// TB = T diag(beta), TBG = T diag(beta gamma) as bf16 128B-swizzled [64 t x 64 i] tiles
+// (zero above the diagonal blocks); this thread: row t, columns 16 q .. 16 q + 15. The
+// destinations may be shared or global memory (the same byte image either way).
+__device__ __forceinline__ void store_tb_tbg(const float* ts, const float* beta, const float* gam, int t, int q,
+                                             uint8_t* tb, uint8_t* tbg) {
+  float vb[16], vbg[16];
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    const int i = 16 * q + jj;
+    const float x = q <= (t >> 4) ? ts[tidx(t, i)] * beta[i] : 0.f;
+    vb[jj] = x;
+    vbg[jj] = x * gam[i];
+  }
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint4 w1, w2;
+    w1.x = pack_bf16x2(vb[8 * c], vb[8 * c + 1]);
+    w1.y = pack_bf16x2(vb[8 * c + 2], vb[8 * c + 3]);
+    w1.z = pack_bf16x2(vb[8 * c + 4], vb[8 * c + 5]);
+    w1.w = pack_bf16x2(vb[8 * c + 6], vb[8 * c + 7]);
+    w2.x = pack_bf16x2(vbg[8 * c], vbg[8 * c + 1]);
+    w2.y = pack_bf16x2(vbg[8 * c + 2], vbg[8 * c + 3]);
+    w2.z = pack_bf16x2(vbg[8 * c + 4], vbg[8 * c + 5]);
+    w2.w = pack_bf16x2(vbg[8 * c + 6], vbg[8 * c + 7]);
+    const uint32_t off = tc::sw128_offset(t, 16 * q + 8 * c);
+    *reinterpret_cast<uint4*>(tb + off) = w1;
+    *reinterpret_cast<uint4*>(tbg + off) = w2;
+  }
+}
+
+// ------------------------------------------------------------------ chunk solve kernel
+// The state-independent part of every chunk, for all chunks of all (sequence, value head)
+// chains at once: one CTA (4 warps) per (chunk, value head, sequence) computes the chunk's
+// cumulative decay, A = strict_lower(beta_t K K^T * D) (K K^T by bf16 mma.sync, fp32
+// accumulate) in 16x16 blocks, T = (I + A)^-1 (diagonal blocks by substitution in fp32, the
+// off-diagonal blocks by tf32 mma.sync products in three levels, the same arithmetic as the
+// in-kernel solve), and writes TB and TBG (16 KB: the two bf16 tiles in the byte image the
+// prefill kernel's MMAs read) to workspace slot (sequence, chunk, head). The prefill kernel
+// then only copies them in.
+constexpr int kSolveThreads = 128;
+constexpr uint32_t kSolveBytes = 2 * 8192;  // TB | TBG per (sequence, chunk, value head)
+
+// 16x16 fp32 blocks (1 KB): element (r, c) at r * 16 + (c ^ bsw(r)). The swizzle keeps both
+// mma.sync tf32 operand patterns (A: rows g, columns t; B: rows t, columns g) free of bank
+// conflicts and 4-column groups contiguous (float4 row reads).
+__device__ __forceinline__ int bsw(int r) { return (((r >> 1) & 1) << 3) | (((r >> 2) & 1) << 2); }
+__device__ __forceinline__ int bidx(int r, int c) { return r * 16 + (c ^ bsw(r)); }
+// Off-diagonal block (i > j) number: (1,0) 0, (2,0) 1, (2,1) 2, (3,0) 3, (3,1) 4, (3,2) 5.
+__host__ __device__ constexpr int oidx(int i, int j) { return i * (i - 1) / 2 + j; }
+
+struct SolveSmem {
+  union {
+    uint8_t k[C * 256];  // K rows of the chunk, 16-byte chunk c of row r at (c ^ (r & 7))
+    struct {             // after K K^T:
+      float t[10][256];  // T blocks: diagonal b at b, off-diagonal (i, j) at 4 + oidx(i, j)
+      float x[4][256];   // X_20, X_21, X_30, X_31 (level 1 scratch in x[0], x[1])
+    } w;
+  };
+  float at[4][16][16];  // diagonal blocks of A, transposed: at[b][m][r] = A[16b + r][16b + m]
+  float ao[6][256];     // off-diagonal blocks of A
+  float c2[C], gam[C], beta[C];
+};
+
+struct SolveArgs {
+  const bf16* k;
+  int64_t k_sb, k_st, k_sh;
+  const void* g;
+  int64_t g_sb, g_st, g_sh;
+  int g_dtype;
+  const void* beta;
+  int64_t b_sb, b_st, b_sh;
+  int b_dtype;
+  int seqlen, hk, hv;
+  uint8_t* ws;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArgs p) {
+  extern __shared__ __align__(16) uint8_t solve_raw[];
+  SolveSmem& sm = *reinterpret_cast<SolveSmem*>(solve_raw);
+  const int m = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int hkh = h / (p.hv / p.hk);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // K rows (zero past the sequence end, the reference's padding)
+  for (int c = tid; c < C * 16; c += kSolveThreads) {
+    const int r = c >> 4, ch = c & 15, t = m * C + r;
+    const uint32_t dst = tc::smem_u32(sm.k) + r * 256 + ((ch ^ (r & 7)) << 4);
+    if (t < p.seqlen) {
+      const bf16* src = p.k + b * p.k_sb + (int64_t)t * p.k_st + hkh * p.k_sh + 8 * ch;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    } else {
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0u) : "memory");
+    }
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // cumulative log2 decay and gamma (warp 0; lane l: steps 2l, 2l + 1; zero past the end)
+  if (warp == 0) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    const int t = m * C + 2 * lane;
+    float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
+    if (t < p.seqlen) {
+      g0 = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
+      b0 = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
+    }
+    if (t + 1 < p.seqlen) {
+      g1 = load_any(p.g, b * p.g_sb + (int64_t)(t + 1) * p.g_st + h * p.g_sh, p.g_dtype);
+      b1 = load_any(p.beta, b * p.b_sb + (int64_t)(t + 1) * p.b_st + h * p.b_sh, p.b_dtype);
+    }
+    const float pair = g0 + g1;
+    float incl = pair;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const float c0 = (incl - pair + g0) * kLog2e, c1 = incl * kLog2e;
+    sm.c2[2 * lane] = c0;
+    sm.c2[2 * lane + 1] = c1;
+    sm.gam[2 * lane] = exp2f(c0);
+    sm.gam[2 * lane + 1] = exp2f(c1);
+    sm.beta[2 * lane] = b0;
+    sm.beta[2 * lane + 1] = b1;
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const int g = lane >> 2, t4 = lane & 3, mi = lane >> 3;
+  // ---- K K^T on the 10 lower 16x16 blocks (rb, cb), cb <= rb, numbered row by row; warp w
+  // takes blocks w, w + 4, w + 8. Epilogue: A = beta_t K K^T exp2(c_t - c_i) below the
+  // diagonal, zero on and above it; diagonal blocks stored transposed (substitution), the
+  // others in the block layout (mma operands).
+  {
+    auto rb_of = [](int j) { return j >= 6 ? 3 : (j >= 3 ? 2 : (j >= 1 ? 1 : 0)); };
+    auto cb_of = [&](int j) { return j - rb_of(j) * (rb_of(j) + 1) / 2; };
+    const uint32_t kb = tc::smem_u32(sm.k);
+    float acc[3][2][4];
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) acc[q][nt][0] = acc[q][nt][1] = acc[q][nt][2] = acc[q][nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {  // k-steps of 16 dims
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const int j = warp + 4 * q;
+        if (j >= 10) continue;
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        {  // A: rows 16 rb + (0..7 | 8..15), dims 16 kk + (0..7 | 8..15)
+          const int r = 16 * rb_of(j) + (mi & 1) * 8 + (lane & 7), ch = 2 * kk + (mi >> 1);
+          ldsm_x4(kb + r * 256 + ((ch ^ (r & 7)) << 4), a0, a1, a2, a3);
+        }
+        {  // B (n = K rows 16 cb ..): (rows 0-7, dims lo | hi) for n-tile 0, rows 8-15 for n-tile 1
+          const int r = 16 * cb_of(j) + (mi >> 1) * 8 + (lane & 7), ch = 2 * kk + (mi & 1);
+          ldsm_x4(kb + r * 256 + ((ch ^ (r & 7)) << 4), b0, b1, b2, b3);
+        }
+        mma_bf16_16816(acc[q][0], a0, a1, a2, a3, b0, b1);
+        mma_bf16_16816(acc[q][1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const int j = warp + 4 * q;
+      if (j >= 10) continue;
+      const int rb = rb_of(j), cb = cb_of(j);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = g + 8 * (e >> 1), c = 8 * nt + 2 * t4 + (e & 1);
+          const int t = 16 * rb + r, i = 16 * cb + c;
+          const float a = i < t ? sm.beta[t] * acc[q][nt][e] * exp2f(sm.c2[t] - sm.c2[i]) : 0.f;
+          if (rb == cb) sm.at[rb][c][r] = a;
+          else sm.ao[oidx(rb, cb)][bidx(r, c)] = a;
+        }
+    }
+  }
+  __syncthreads();  // K is dead: its space holds the T and X blocks from here
+  auto rd = [](const float* blk) { return [=](int r, int c) { return blk[bidx(r, c)]; }; };
+  auto wr = [](float* blk) { return [=](int r, int c, float x) { blk[bidx(r, c)] = x; }; };
+  // ---- diagonal blocks T_bb (warps 0-1, lane = column c of block 2 w + lane / 16):
+  // right-looking substitution, v[r] accumulates sum_{m<r} A_rm x_m and becomes x_r when its
+  // turn comes
+  if (warp < 2) {
+    const int bb = 2 * warp + (lane >> 4), c = lane & 15;
+    float v[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) v[r] = 0.f;
+#pragma unroll
+    for (int mm = 0; mm < 16; ++mm) {
+      const float x = mm < c ? 0.f : (mm == c ? 1.f : -v[mm]);
+      v[mm] = x;
+      const float4* col = reinterpret_cast<const float4*>(sm.at[bb][mm]);
+#pragma unroll
+      for (int q4 = (mm + 1) / 4; q4 < 4; ++q4) {
+        const float4 a4 = col[q4];
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (4 * q4 + e > mm) v[4 * q4 + e] = fmaf(av[e], x, v[4 * q4 + e]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) sm.w.t[bb][bidx(r, c)] = v[r];
+  }
+  __syncthreads();
+  // ---- off-diagonal blocks, T_ij = -T_ii (sum_{k=j}^{i-1} A_ik T_kj): warp = (block, n-tile)
+  {  // level 1: T_10 (warps 0-1), T_32 (warps 2-3) via Y = A_ij T_jj
+    const int blk = warp >> 1, nt = warp & 1, i = 2 * blk + 1, j = 2 * blk;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma(acc, rd(sm.ao[oidx(i, j)]), rd(sm.w.t[j]), nt, lane);
+    tile_store(acc, 1.f, wr(sm.w.x[blk]), nt, lane);
+    __syncwarp();
+    float acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    tile_mma(acc2, rd(sm.w.t[i]), rd(sm.w.x[blk]), nt, lane);
+    tile_store(acc2, -1.f, wr(sm.w.t[4 + oidx(i, j)]), nt, lane);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {  // level 2: X_rc = sum_{k=c}^{1} A_rk T_kc, r = 2, 3; c = 0, 1
+    const int u = warp + 4 * q, xb = u >> 1, nt = u & 1, r = 2 + (xb >> 1), c = xb & 1;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = c; k < 2; ++k)
+      tile_mma(acc, rd(sm.ao[oidx(r, k)]), rd(k == c ? sm.w.t[k] : sm.w.t[4 + oidx(1, 0)]), nt, lane);
+    tile_store(acc, 1.f, wr(sm.w.x[xb]), nt, lane);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {  // level 3: T_rc = -sum_{k=2}^{r} T_rk X_kc
+    const int u = warp + 4 * q, xb = u >> 1, nt = u & 1, r = 2 + (xb >> 1), c = xb & 1;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 2; k <= r; ++k)
+      tile_mma(acc, rd(k == r ? sm.w.t[r] : sm.w.t[4 + oidx(3, 2)]), rd(sm.w.x[2 * (k - 2) + c]), nt, lane);
+    tile_store(acc, -1.f, wr(sm.w.t[4 + oidx(r, c)]), nt, lane);
+  }
+  __syncthreads();
+  // ---- TB = T diag(beta), TBG = T diag(beta gamma) as bf16 128B-swizzled [64 t x 64 i]
+  // tiles (zero above the diagonal blocks) into the workspace; thread: row t, columns
+  // 32 hh .. 32 hh + 31
+  {
+    uint8_t* dst = p.ws + ((((int64_t)b * gridDim.x + m) * p.hv + h) * kSolveBytes);
+    const int t = tid >> 1, hh = tid & 1, rb = t >> 4, rl = t & 15;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int cb = 2 * hh + cc;
+      float v[16];
+      if (cb <= rb) {
+        const float* blk = cb == rb ? sm.w.t[rb] : sm.w.t[4 + oidx(rb, cb)];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 x = *reinterpret_cast<const float4*>(blk + rl * 16 + ((4 * q4) ^ bsw(rl)));
+          v[4 * q4] = x.x, v[4 * q4 + 1] = x.y, v[4 * q4 + 2] = x.z, v[4 * q4 + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float vb[8], vbg[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = 16 * cb + 8 * u + e;
+          vb[e] = v[8 * u + e] * sm.beta[i];
+          vbg[e] = vb[e] * sm.gam[i];
+        }
+        uint4 w1, w2;
+        w1.x = pack_bf16x2(vb[0], vb[1]);
+        w1.y = pack_bf16x2(vb[2], vb[3]);
+        w1.z = pack_bf16x2(vb[4], vb[5]);
+        w1.w = pack_bf16x2(vb[6], vb[7]);
+        w2.x = pack_bf16x2(vbg[0], vbg[1]);
+        w2.y = pack_bf16x2(vbg[2], vbg[3]);
+        w2.z = pack_bf16x2(vbg[4], vbg[5]);
+        w2.w = pack_bf16x2(vbg[6], vbg[7]);
+        const uint32_t off = tc::sw128_offset(t, 16 * cb + 8 * u);
+        *reinterpret_cast<uint4*>(dst + off) = w1;
+        *reinterpret_cast<uint4*>(dst + 8192 + off) = w2;
+      }
+    }
+  }
+}
+
+template <typename TOut, bool kOffload>
 __global__ void __launch_bounds__(NT, 1)
     gdn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -187,6 +545,7 @@ __global__ void __launch_bounds__(NT, 1)
     tc::mbar_init(&sm.bar_kq[0], 1);
     tc::mbar_init(&sm.bar_kq[1], 1);
     tc::mbar_init(&sm.bar_v, 1);
+    tc::mbar_init(&sm.bar_tb, 1);
     tc::mbar_init(&sm.bar_p1, 1);
     tc::mbar_init(&sm.bar_p3, 1);
     tc::mbar_init(&sm.bar_ws, 1);
@@ -232,6 +591,12 @@ __global__ void __launch_bounds__(NT, 1)
     tc::mbar_expect_tx(&sm.bar_v, 2 * 8192);
     for (int a = 0; a < 2; ++a) tc::tma_load_4d(sm.v[a], &tm_v, &sm.bar_v, 64 * a, m * C, h, b);
   };
+  // With the solve offloaded: chunk m's TB | TBG (16 KB, contiguous in sm.tb, sm.tbg) by one
+  // bulk copy, issued by the prep leader once chunk m-1's U' and W^T products are done.
+  auto issue_tb = [&](int m) {
+    tc::mbar_expect_tx(&sm.bar_tb, kSolveBytes);
+    tc::bulk_load(sm.tb, p.solve + (((int64_t)b * nchunks + m) * p.hv + h) * kSolveBytes, kSolveBytes, &sm.bar_tb);
+  };
   if (tid == 0) {
     tc::prefetch_tmap(&tm_q);
     tc::prefetch_tmap(&tm_k);
@@ -240,6 +605,7 @@ __global__ void __launch_bounds__(NT, 1)
     issue_kq(0);
     if (nchunks > 1) issue_kq(1);
     issue_v(0);
+    if (kOffload) issue_tb(0);
   }
 
   if (warp >= kRoleWarps) {
@@ -318,8 +684,9 @@ __global__ void __launch_bounds__(NT, 1)
       }
       if (!pwait(&sm.bar_p1, m & 1, 2)) break;
       // ---- A (fp32) from K K^T rows (lanes 0-63), M (bf16) from Q K^T rows (lanes 64-127);
-      // this thread: row `row`, columns 32 hf .. 32 hf + 31
-      {
+      // this thread: row `row`, columns 32 hf .. 32 hf + 31. With the solve offloaded only
+      // M is needed (warp-uniform: warps of quadrants 0-1 hold the K K^T rows).
+      if (!kOffload || row >= C) {
         const float* c2 = sm.cum2[sb];
         const int t = row & 63, i0 = 32 * hf;
         const bool zero = t < 32 && hf == 1;  // rows 0-31 have no terms past column 31
@@ -357,101 +724,19 @@ __global__ void __launch_bounds__(NT, 1)
           store_half_row_bf16(sm.m[buf], t, hf, v);
         }
       }
-      tc::fence_before_sync();
-      role_sync(2);
-      // ---- T = (I + A)^-1, blocked. Diagonal 16x16 blocks (warps 0-3 of the role, one block
-      // each, lane = column): right-looking substitution, v[r] accumulates sum_{m<r} A_rm x_m
-      // and becomes x_r when its turn comes (one FMA on the chain per step).
-      float* ts = reinterpret_cast<float*>(sm.wt[buf]);  // fp32 T scratch (free: W^T(m-2) consumed)
-      if (pw < 4) {
-        const int col = lane & 15, r0 = 16 * pw;
-        float v[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] = 0.f;
-#pragma unroll
-        for (int mm = 0; mm < 16; ++mm) {
-          const float x = mm < col ? 0.f : (mm == col ? 1.f : -v[mm]);
-          v[mm] = x;
-#pragma unroll
-          for (int r = mm + 1; r < 16; ++r) v[r] = fmaf(sm.a[(r0 + r) * PA + r0 + mm], x, v[r]);
-        }
-        if (lane < 16) {
-#pragma unroll
-          for (int r = 0; r < 16; ++r) ts[tidx(r0 + r, r0 + col)] = v[r];
-        }
-      }
-      role_sync(2);
-      // off-diagonal blocks: T_ij = -T_ii (sum_{k=j}^{i-1} A_ik T_kj), in three levels:
-      // the two 32x32 diagonal halves (T_10, T_32), then the lower-left 32x32 quarter as
-      // X = A_21 T_1 and T_21 = -T_2 X. Each warp computes one 16x8 tile (n-tile nt).
-      {
-        float* scr = reinterpret_cast<float*>(sm.tb);  // 4 x (16 x 24) fp32 scratch blocks
-        auto sread = [&](int w) { return [=](int r, int c) { return scr[w * 384 + r * 24 + c]; }; };
-        auto swrite = [&](int w) { return [=](int r, int c, float x) { scr[w * 384 + r * 24 + c] = x; }; };
-        auto at = [&](int bi, int bj) {
-          return [=, &sm](int r, int c) { return sm.a[(16 * bi + r) * PA + 16 * bj + c]; };
-        };
-        auto tt = [&](int bi, int bj) { return [=](int r, int c) { return ts[tidx(16 * bi + r, 16 * bj + c)]; }; };
-        auto twrite = [&](int bi, int bj) {
-          return [=](int r, int c, float x) { ts[tidx(16 * bi + r, 16 * bj + c)] = x; };
-        };
-        const int blk = pw >> 1, nt = pw & 1;
-        if (blk < 2) {  // T_10 (warps 0-1), T_32 (warps 2-3)
-          const int j = 2 * blk, i = j + 1;
-          float acc[4] = {};
-          tile_mma(acc, at(i, j), tt(j, j), nt, lane);
-          tile_store(acc, 1.f, swrite(blk), nt, lane);
-          __syncwarp();
-          float acc2[4] = {};
-          tile_mma(acc2, tt(i, i), sread(blk), nt, lane);
-          tile_store(acc2, -1.f, twrite(i, j), nt, lane);
-        }
+      if constexpr (!kOffload) {
+        tc::fence_before_sync();
         role_sync(2);
-        const int r = 2 + (blk >> 1), c = blk & 1;
-        {  // X_rc = sum_{k=c}^{1} A_rk T_kc
-          float acc[4] = {};
-          for (int k = c; k < 2; ++k) tile_mma(acc, at(r, k), tt(k, c), nt, lane);
-          tile_store(acc, 1.f, swrite(blk), nt, lane);
-        }
-        role_sync(2);
-        {  // T_rc = -sum_{k=2}^{r} T_rk X_kc
-          float acc[4] = {};
-          for (int k = 2; k <= r; ++k) tile_mma(acc, tt(r, k), sread(2 * (k - 2) + c), nt, lane);
-          tile_store(acc, -1.f, twrite(r, c), nt, lane);
-        }
-        role_sync(2);
-      }
-      // ---- TB = T diag(beta), TBG = T diag(beta gamma), bf16 (zero above the blocks);
-      // this thread: row t, columns 16 q .. 16 q + 15
-      {
-        const int t = pt >> 2, q = pt & 3;
-        float vb[16], vbg[16];
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int i = 16 * q + jj;
-          const float x = q <= (t >> 4) ? ts[tidx(t, i)] * sm.beta[sb][i] : 0.f;
-          vb[jj] = x;
-          vbg[jj] = x * sm.gam[sb][i];
-        }
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint4 w1, w2;
-          w1.x = pack_bf16x2(vb[8 * c], vb[8 * c + 1]);
-          w1.y = pack_bf16x2(vb[8 * c + 2], vb[8 * c + 3]);
-          w1.z = pack_bf16x2(vb[8 * c + 4], vb[8 * c + 5]);
-          w1.w = pack_bf16x2(vb[8 * c + 6], vb[8 * c + 7]);
-          w2.x = pack_bf16x2(vbg[8 * c], vbg[8 * c + 1]);
-          w2.y = pack_bf16x2(vbg[8 * c + 2], vbg[8 * c + 3]);
-          w2.z = pack_bf16x2(vbg[8 * c + 4], vbg[8 * c + 5]);
-          w2.w = pack_bf16x2(vbg[8 * c + 6], vbg[8 * c + 7]);
-          const uint32_t off = tc::sw128_offset(t, 16 * q + 8 * c);
-          *reinterpret_cast<uint4*>(sm.tb + off) = w1;  // the tb scratch reads ended at the last barrier
-          *reinterpret_cast<uint4*>(sm.tbg + off) = w2;
-        }
+        // ---- T = (I + A)^-1 into the fp32 scratch (free: W^T(m-2) consumed), then TB, TBG
+        float* ts = reinterpret_cast<float*>(sm.wt[buf]);
+        invert_unit_lower(sm.a, ts, reinterpret_cast<float*>(sm.tb), pw, lane, [] { role_sync(2); });
+        // the tb scratch reads ended at the inverse's last barrier
+        store_tb_tbg(ts, sm.beta[sb], sm.gam[sb], pt >> 2, pt & 3, sm.tb, sm.tbg);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       // ---- W^T = K^T TBG^T -> D1; U'^T = V^T TB^T -> UP[buf]
+      if (kOffload && !pwait(&sm.bar_tb, m & 1, 6)) break;
       if (!pwait(&sm.bar_v, m & 1, 3)) break;
       if (pt == 0) {
         for (int kk = 0; kk < 4; ++kk) {
@@ -469,6 +754,7 @@ __global__ void __launch_bounds__(NT, 1)
       if (!pwait(&sm.bar_p3, m & 1, 4)) break;
       if (pt == 0 && m + 1 < nchunks) {
         issue_v(m + 1);
+        if (kOffload) issue_tb(m + 1);
         last_v = m + 1;
       }
       // ---- W^T -> wt[buf] (bf16, MN-major rows): row = dk index, columns 32 hf ..
@@ -486,6 +772,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     if (pt == 0) {  // our loads land and every MMA this thread issued completes before exit
       tc::mbar_wait(&sm.bar_v, last_v & 1, 200000000ull);
+      if (kOffload) tc::mbar_wait(&sm.bar_tb, last_v & 1, 200000000ull);
       tc::mma_commit(&sm.drain_p);
       tc::mbar_wait(&sm.drain_p, 0, 200000000ull);
     }
@@ -730,7 +1017,13 @@ bool gdn_prefill_tc_supported(const pbk_gdn_desc& d) {
          ok16(d.v) && out_ok;
 }
 
-cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st) {
+size_t gdn_prefill_tc_workspace(const pbk_gdn_desc& d) {
+  return (size_t)d.batch * ((d.seqlen + C - 1) / C) * d.hv * kSolveBytes;
+}
+
+// solve_ws: gdn_prefill_tc_workspace(d) bytes (16-byte aligned) for the offloaded chunk
+// solve, or NULL to solve each chunk inside the prefill kernel.
+cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, cudaStream_t st) {
   CUtensorMap mq, mk, mv, mo;
   if (!make_map(&mq, d.q, d.hk, d) || !make_map(&mk, d.k, d.hk, d) || !make_map(&mv, d.v, d.hv, d))
     return cudaErrorInvalidValue;
@@ -770,19 +1063,43 @@ cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, cudaStream_t st) {
   a.state_indices = d.state_indices;
   a.scale = d.scale;
   a.err = device_error_word();
-  const dim3 grid((unsigned)((int64_t)d.batch * d.hv));
-  if (d.o.dtype == PBK_BF16) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_prefill_tc_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBytes);
+  a.solve = static_cast<const uint8_t*>(solve_ws);
+  if (solve_ws != nullptr) {
+    SolveArgs sa;
+    sa.k = static_cast<const bf16*>(d.k.data);
+    sa.k_sb = d.k.stride_b;
+    sa.k_st = d.k.stride_t;
+    sa.k_sh = d.k.stride_h;
+    sa.g = d.g.data;
+    sa.g_sb = d.g.stride_b;
+    sa.g_st = d.g.stride_t;
+    sa.g_sh = d.g.stride_h;
+    sa.g_dtype = d.g.dtype;
+    sa.beta = d.beta.data;
+    sa.b_sb = d.beta.stride_b;
+    sa.b_st = d.beta.stride_t;
+    sa.b_sh = d.beta.stride_h;
+    sa.b_dtype = d.beta.dtype;
+    sa.seqlen = d.seqlen;
+    sa.hk = d.hk;
+    sa.hv = d.hv;
+    sa.ws = static_cast<uint8_t*>(solve_ws);
+    cudaError_t e = cudaFuncSetAttribute(gdn_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(SolveSmem));
     if (e != cudaSuccess) return e;
-    gdn_prefill_tc_kernel<bf16><<<grid, NT, kSmemBytes, st>>>(mq, mk, mv, mo, a);
-  } else {
-    cudaError_t e = cudaFuncSetAttribute(gdn_prefill_tc_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBytes);
-    if (e != cudaSuccess) return e;
-    gdn_prefill_tc_kernel<float><<<grid, NT, kSmemBytes, st>>>(mq, mk, mv, mo, a);
+    const dim3 sgrid((unsigned)((d.seqlen + C - 1) / C), (unsigned)d.hv, (unsigned)d.batch);
+    gdn_solve_kernel<<<sgrid, kSolveThreads, sizeof(SolveSmem), st>>>(sa);
   }
-  return cudaGetLastError();
+  const dim3 grid((unsigned)((int64_t)d.batch * d.hv));
+  auto go = [&](auto kernel) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    kernel<<<grid, NT, kSmemBytes, st>>>(mq, mk, mv, mo, a);
+    return cudaGetLastError();
+  };
+  if (d.o.dtype == PBK_BF16)
+    return solve_ws ? go(gdn_prefill_tc_kernel<bf16, true>) : go(gdn_prefill_tc_kernel<bf16, false>);
+  return solve_ws ? go(gdn_prefill_tc_kernel<float, true>) : go(gdn_prefill_tc_kernel<float, false>);
 }
 
 }  // namespace pbk

@@ -158,8 +158,8 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* to
 
 // Radix select over n keys key_of(i): the k-th largest key (`prefix` on return) and how
 // many elements equal to it belong to the top k (`kk`). Three digits (11, 11, 10 bits),
-// warp-aggregated shared-memory histograms; warp 0 finds each digit's bin with a suffix
-// scan (lane l owns 64 consecutive bins, highest bins first).
+// warp-aggregated shared-memory histograms; each digit's bin comes from a block-wide scan
+// of the bin counts (thread t owns 2 or 1 consecutive bins, highest bins first).
 constexpr int kBins = 2048;
 struct SelectSmem {
   uint32_t hist[kBins];
@@ -190,34 +190,28 @@ __device__ __forceinline__ void radix_select(KeyOf key_of, int n, uint32_t k, Se
       const uint32_t same = __match_any_sync(0xffffffffu, bin);
       if (bin != 0xFFFFFFFFu && lane == __ffs(same) - 1) atomicAdd(&ss.hist[bin], (uint32_t)__popc(same));
     }
+    if (tid == 0) {  // default, overwritten below whenever the count reaches kk
+      ss.prefix = prefix;
+      ss.kk = kk;
+    }
     __syncthreads();
-    if (tid < 32) {
-      const int per = nb / 32;             // bins per lane
-      const int hi = nb - 1 - per * lane;  // this lane's highest bin
-      uint32_t own = 0;
-      for (int j = 0; j < per; ++j) own += ss.hist[hi - j];
-      uint32_t incl = own;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
+    // thread tid owns the `per` bins from hi = nb - 1 - per * tid down (highest bins first):
+    // a block-wide scan of the per-thread counts finds the bin holding the kk-th largest key
+    const int per = nb / kTopkThreads;
+    const int hi = nb - 1 - per * tid;
+    int own = 0;
+    for (int j = 0; j < per; ++j) own += (int)ss.hist[hi - j];
+    int total;
+    const uint32_t excl = (uint32_t)block_exclusive_scan<kTopkThreads>(own, ss.warp_tot[0], &total);
+    if (excl < kk && kk <= excl + (uint32_t)own) {
+      uint32_t above = excl;
+      int b = hi;
+      for (int j = 0; j < per - 1; ++j, --b) {
+        if (above + ss.hist[b] >= kk) break;
+        above += ss.hist[b];
       }
-      const uint32_t excl = incl - own;
-      if (lane == 0) {  // default, overwritten below whenever the count reaches kk
-        ss.prefix = prefix;
-        ss.kk = kk;
-      }
-      __syncwarp();
-      if (excl < kk && kk <= incl) {
-        uint32_t above = excl;
-        int b = hi;
-        for (int j = 0; j < per - 1; ++j, --b) {
-          if (above + ss.hist[b] >= kk) break;
-          above += ss.hist[b];
-        }
-        ss.prefix = prefix | ((uint32_t)b << shift);
-        ss.kk = kk - above;
-      }
+      ss.prefix = prefix | ((uint32_t)b << shift);
+      ss.kk = kk - above;
     }
     __syncthreads();
     prefix = ss.prefix;
@@ -598,18 +592,20 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
   }
 }
 
-// One CTA (128 threads) per output row: the split weights exp2(m_s - M) in shared memory
-// (max and sum over the splits in parallel), then thread = output dim over all splits with
-// independent loads.
-__global__ void quest_combine_kernel(const pbk_quest_desc d, int splits, const float* part) {
+// One CTA (128 threads) per (output row, 32 output dims): the split weights exp2(m_s - M)
+// in shared memory (max and sum over the splits in parallel), then each warp sums a quarter
+// of the splits for the 32 dims (lane = dim, eight independent loads in flight) and the
+// four partial sums meet in shared memory.
+__global__ void __launch_bounds__(128) quest_combine_kernel(const pbk_quest_desc d, int splits, const float* part) {
   extern __shared__ float w[];  // [splits]
-  __shared__ float red[kD / 32];
-  const int row = blockIdx.x;  // (n, ti, head)
+  __shared__ float red[4];
+  __shared__ float accs[4][32];
+  const int row = blockIdx.x;  // (n, ti, head); blockIdx.y: dims 32 y .. 32 y + 31
   const int head = row % d.h, ti = (row / d.h) % d.t, n = row / (d.h * d.t);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* pp = part + (int64_t)row * splits * (kD + 2);
   float m = -INFINITY;
-  for (int s = tid; s < splits; s += kD) m = fmaxf(m, pp[s * (kD + 2) + kD]);
+  for (int s = tid; s < splits; s += 128) m = fmaxf(m, pp[s * (kD + 2) + kD]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
@@ -617,7 +613,7 @@ __global__ void quest_combine_kernel(const pbk_quest_desc d, int splits, const f
   const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   __syncthreads();
   float l = 0.f;
-  for (int s = tid; s < splits; s += kD) {
+  for (int s = tid; s < splits; s += 128) {
     const float ms = pp[s * (kD + 2) + kD];
     const float ws = ms == -INFINITY ? 0.f : exp2f(ms - M);
     w[s] = ws;
@@ -627,19 +623,26 @@ __global__ void quest_combine_kernel(const pbk_quest_desc d, int splits, const f
   if (lane == 0) red[warp] = l;
   __syncthreads();
   const float L = (red[0] + red[1]) + (red[2] + red[3]);
-  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-  int s = 0;
-  for (; s + 4 <= splits; s += 4) {
-    acc0 = fmaf(pp[s * (kD + 2) + tid], w[s], acc0);
-    acc1 = fmaf(pp[(s + 1) * (kD + 2) + tid], w[s + 1], acc1);
-    acc2 = fmaf(pp[(s + 2) * (kD + 2) + tid], w[s + 2], acc2);
-    acc3 = fmaf(pp[(s + 3) * (kD + 2) + tid], w[s + 3], acc3);
+  // warp w sums splits w, w + 4, ..., eight loads in flight per lane; lane = one dim
+  const float* pd = pp + 32 * blockIdx.y + lane;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int s = warp;
+  for (; s + 28 < splits; s += 32) {
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] = pd[(s + 4 * u) * (kD + 2)];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc[u] = fmaf(x[u], w[s + 4 * u], acc[u]);
   }
-  for (; s < splits; ++s) acc0 = fmaf(pp[s * (kD + 2) + tid], w[s], acc0);
-  const float o = ((acc0 + acc1) + (acc2 + acc3)) / L;
-  const int64_t off = n * d.out_stride_n + ti * d.out_stride_t + head * d.out_stride_h + tid;
-  if (d.out_dtype == PBK_BF16) reinterpret_cast<bf16*>(d.out)[off] = __float2bfloat16_rn(o);
-  else reinterpret_cast<float*>(d.out)[off] = o;
+  for (; s < splits; s += 4) acc[0] = fmaf(pd[s * (kD + 2)], w[s], acc[0]);
+  accs[warp][lane] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+  __syncthreads();
+  if (warp == 0) {
+    const float o = ((accs[0][lane] + accs[1][lane]) + (accs[2][lane] + accs[3][lane])) / L;
+    const int64_t off = n * d.out_stride_n + ti * d.out_stride_t + head * d.out_stride_h + 32 * blockIdx.y + lane;
+    if (d.out_dtype == PBK_BF16) reinterpret_cast<bf16*>(d.out)[off] = __float2bfloat16_rn(o);
+    else reinterpret_cast<float*>(d.out)[off] = o;
+  }
 }
 
 }  // namespace
@@ -791,10 +794,11 @@ cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st
 }
 
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, cudaStream_t st) {
-  const int k = quest_k(d), tail = d.n_arch % d.page, splits = quest_splits(d, sk.n);
+  const int k = quest_k(d), tail = d.n_arch % d.page;
+  int splits = quest_splits(d, sk.n);
   if (splits == 0) return cudaSuccess;
   if (quest_attend_mma_supported(d)) {
-    cudaError_t e = launch_quest_attend_mma(d, k, tail, splits, part, sk, st);
+    cudaError_t e = launch_quest_attend_mma(d, k, tail, part, sk, &splits, st);
     if (e != cudaSuccess) return e;
   } else if (d.t * (d.h / d.kv) > 4) {
     quest_attend_kernel<8><<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
@@ -806,7 +810,7 @@ cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const Sink
     cudaError_t e = cudaFuncSetAttribute(quest_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, wbytes);
     if (e != cudaSuccess) return e;
   }
-  quest_combine_kernel<<<d.nq * d.t * d.h, kD, wbytes, st>>>(d, splits, part);
+  quest_combine_kernel<<<dim3(d.nq * d.t * d.h, kD / 32), 128, wbytes, st>>>(d, splits, part);
   return cudaGetLastError();
 }
 

@@ -2,13 +2,16 @@
 // fp32 accumulate): the same virtual keys, masks and workspace partials as the SIMT
 // quest_attend_kernel in quest.cu, for up to 16 query rows per key head.
 //
-// A warp owns one split of 256 virtual keys and walks it in sub-tiles of 32: the keys' and
-// values' rows are staged in the warp's shared memory with cp.async (16-byte chunks, XOR
-// swizzled so ldmatrix reads are conflict-free), S = Q K^T comes from ldmatrix'ed K and Q
-// fragments held in registers, the online softmax (base 2, rows g and g + 8 of the warp's
-// 16-row tile) rescales the running O, and O += P V reuses S's accumulator layout as the P
-// operand with V read by ldmatrix.trans. The warp writes (m, l, O) for its split; the
-// combine kernel merges the splits.
+// A warp owns one split of S virtual keys (S a multiple of 16 in [256, 512], chosen per
+// launch so that the grid fills one wave of resident blocks where it can) and walks it in
+// tiles of 16 keys through a two-stage ring: while the math runs on tile s, the cp.async
+// copies of tile s + 1 are in flight (16-byte chunks, XOR swizzled so ldmatrix reads are
+// conflict-free; window keys' positions ride along as 4-byte copies). The split's key
+// indices are resolved once, before the first copy. S = Q K^T comes from ldmatrix'ed K and
+// Q fragments held in registers, the online softmax (base 2, rows g and g + 8 of the warp's
+// 16-row tile) rescales the running O only when a row maximum rose, and O += P V reuses
+// S's accumulator layout as the P operand with V read by ldmatrix.trans. The warp writes
+// (m, l, O) for its split; the combine kernel merges the splits.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -19,17 +22,19 @@ namespace {
 
 using bf16 = __nv_bfloat16;
 constexpr int kD = 128;
-constexpr int kSplit = 256;   // virtual keys per warp (= the SIMT kernel's split)
-constexpr int kSub = 32;      // keys per sub-tile
+constexpr int kMinSplit = 256;  // = the SIMT kernel's split: the workspace holds its count
+constexpr int kMaxSplit = 512;
+constexpr int kTile = 16;       // keys per stage
+constexpr int kStages = 2;
 constexpr int kWarps = 4;
 constexpr int kSinkTag = -(1 << 30);  // same key encoding as quest.cu
 constexpr int kRowBytes = kD * 2;     // 256 bytes per key row
 
 struct WarpSmem {
-  uint8_t k[kSub * kRowBytes];  // 8 KB, row r at r * 256, 16-byte chunk c at (c ^ (r & 7))
-  uint8_t v[kSub * kRowBytes];
-  int kidx[kSub];
-  int kpos[kSub];  // window keys' positions (for the mask)
+  uint8_t k[kStages][kTile * kRowBytes];  // 4 KB a stage, row r at r * 256, chunk c at (c ^ (r & 7))
+  uint8_t v[kStages][kTile * kRowBytes];
+  int kpos[kStages][kTile];  // window keys' positions (for the mask)
+  int kidx[kMaxSplit];       // the split's key indices (encoding as in quest.cu)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -38,7 +43,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -69,19 +78,32 @@ __device__ __forceinline__ bool visible(int kp, int qp, int window, int sinks) {
   return kp <= qp && ((qp - kp) < window || kp < sinks);
 }
 
-__global__ void __launch_bounds__(32 * kWarps) quest_attend_mma_kernel(const pbk_quest_desc d, int k, int tail,
-                                                                       int splits, float* part, SinkKeys sk) {
+// Key index of virtual key vj of key head h of query n (vj < the part's length).
+__device__ __forceinline__ int key_index(const pbk_quest_desc& d, int k, const SinkKeys& sk, bool win, int vj, int n,
+                                         int h) {
+  if (win) return -1 - vj;
+  if (vj < sk.n) return kSinkTag - vj;
+  const int r = vj - sk.n;
+  if (r < k * d.page) return d.pages[((int64_t)n * d.kv + h) * k + r / d.page] * d.page + r % d.page;
+  return (d.n_arch / d.page) * d.page + (r - k * d.page);
+}
+
+__global__ void __launch_bounds__(32 * kWarps, 3)
+    quest_attend_mma_kernel(const pbk_quest_desc d, int k, int tail, int split_keys, int sr, int splits, float* part,
+                            SinkKeys sk) {
   extern __shared__ __align__(16) uint8_t attn_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpSmem& ws = reinterpret_cast<WarpSmem*>(attn_raw)[warp];
-  const int split = blockIdx.x * kWarps + warp, n = blockIdx.y / d.kv, h = blockIdx.y % d.kv;
-  if (split >= splits) return;
+  const int task = blockIdx.x * kWarps + warp;
+  if (task >= d.nq * d.kv * splits) return;
+  const int split = task % splits, n = task / splits / d.kv, h = task / splits % d.kv;
   const int g = lane >> 2, t = lane & 3;
   const int groups = d.h / d.kv, rows = d.t * groups;
-  const int n_ret = sk.n + k * d.page + tail, sr = (n_ret + kSplit - 1) / kSplit;
+  const int n_ret = sk.n + k * d.page + tail;
   const bool win_split = split >= sr;
-  const int j0 = win_split ? (split - sr) * kSplit : split * kSplit;
-  const int nkeys = min(kSplit, (win_split ? d.n_win : n_ret) - j0);
+  const int j0 = win_split ? (split - sr) * split_keys : split * split_keys;
+  const int nkeys = min(split_keys, (win_split ? d.n_win : n_ret) - j0);
+  const int ntiles = (nkeys + kTile - 1) / kTile;
   const bf16* keys = reinterpret_cast<const bf16*>(d.keys);
   const bf16* vals = reinterpret_cast<const bf16*>(d.values);
   const bf16* wkeys = reinterpret_cast<const bf16*>(d.win_keys);
@@ -89,8 +111,53 @@ __global__ void __launch_bounds__(32 * kWarps) quest_attend_mma_kernel(const pbk
   const bf16* q = reinterpret_cast<const bf16*>(d.q);
   const float sl2 = d.scale * 1.4426950408889634f;
 
+  // the split's key indices; keys past the split (up to the tile edge) are INT32_MIN: masked,
+  // rows zero
+  for (int i = lane; i < ntiles * kTile; i += 32)
+    ws.kidx[i] = i < nkeys ? key_index(d, k, sk, win_split, j0 + i, n, h) : INT32_MIN;
+  __syncwarp();
+
+  // tile s into stage b: 16 key and 16 value rows of 16 chunks (8 of each per lane), and the
+  // window keys' positions; rows past the split are zeroed (their probabilities are 0, and
+  // 0 * (stale bits) could be NaN). One cp.async group per tile.
+  auto issue = [&](int s, int b) {
+#pragma unroll
+    for (int it = 0; it < kTile * 16 / 32; ++it) {
+      const int c = it * 32 + lane, r = c >> 4, ch = c & 15;
+      const int idx = ws.kidx[s * kTile + r];
+      const uint32_t ko = smem_u32(ws.k[b]) + sw_off(r, ch), vo = smem_u32(ws.v[b]) + sw_off(r, ch);
+      if (idx == INT32_MIN) {
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(ko), "r"(0u) : "memory");
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vo), "r"(0u) : "memory");
+        continue;
+      }
+      const bf16 *kr, *vr;
+      if (idx >= 0) {
+        kr = keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n;
+        vr = vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n;
+      } else if (idx > kSinkTag) {
+        kr = wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+        vr = wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+      } else {
+        kr = sk.k + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
+        vr = sk.v + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
+      }
+      cp_async16(ko, kr + 8 * ch);
+      cp_async16(vo, vr + 8 * ch);
+    }
+    if (lane < kTile) {
+      const int idx = ws.kidx[s * kTile + lane];
+      if (idx < 0 && idx > kSinkTag) cp_async4(smem_u32(&ws.kpos[b][lane]), d.kpos + (-1 - idx));
+      else ws.kpos[b][lane] = 0;
+    }
+    cp_async_commit();
+  };
+
   // Q fragments (rows g and g + 8 of the 16-row tile; rows past `rows` are zero): for k-step
   // kk, a0 = (g, 16kk + 2t..), a1 = (g + 8, ..), a2 = (g, 16kk + 8 + 2t..), a3 = (g + 8, ..)
+  issue(0, 0);
+  if (ntiles > 1) issue(1, 1);
+  else cp_async_commit();
   uint32_t qa[8][4];
   int qpos_r[2];
 #pragma unroll
@@ -112,81 +179,39 @@ __global__ void __launch_bounds__(32 * kWarps) quest_attend_mma_kernel(const pbk
   for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
-  for (int s0 = 0; s0 < nkeys; s0 += kSub) {
-    // key index of this sub-tile's key `lane`
-    {
-      const int vj = j0 + s0 + lane;
-      int idx = 0;
-      if (s0 + lane < nkeys) {
-        if (win_split) idx = -1 - vj;
-        else if (vj < sk.n) idx = kSinkTag - vj;
-        else if (vj - sk.n < k * d.page) {
-          const int r = vj - sk.n;
-          idx = d.pages[((int64_t)n * d.kv + h) * k + r / d.page] * d.page + r % d.page;
-        } else {
-          idx = (d.n_arch / d.page) * d.page + (vj - sk.n - k * d.page);
-        }
-      } else {
-        idx = INT32_MIN;  // past the split's keys: masked, rows zero
-      }
-      ws.kidx[lane] = idx;
-      ws.kpos[lane] = (idx < 0 && idx > kSinkTag) ? d.kpos[-1 - idx] : 0;
-    }
+  for (int s = 0; s < ntiles; ++s) {
+    const int b = s & 1;
+    cp_async_wait_prev();  // tile s's group is complete (only tile s + 1's may be pending)
     __syncwarp();
-    // stage the 32 key and value rows (16 chunks each); rows past the split are zeroed (their
-    // probabilities are 0, and 0 * (stale bits) could be NaN)
-#pragma unroll 4
-    for (int it = 0; it < kSub * 16 / 32; ++it) {
-      const int c = it * 32 + lane, r = c >> 4, ch = c & 15;
-      const int idx = ws.kidx[r];
-      if (idx == INT32_MIN) {
-        *reinterpret_cast<uint4*>(ws.k + sw_off(r, ch)) = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(ws.v + sw_off(r, ch)) = make_uint4(0u, 0u, 0u, 0u);
-        continue;
-      }
-      const bf16 *kr, *vr;
-      if (idx >= 0) {
-        kr = keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n;
-        vr = vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n;
-      } else if (idx > kSinkTag) {
-        kr = wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
-        vr = wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
-      } else {
-        kr = sk.k + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
-        vr = sk.v + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
-      }
-      cp_async16(smem_u32(ws.k) + sw_off(r, ch), kr + 8 * ch);
-      cp_async16(smem_u32(ws.v) + sw_off(r, ch), vr + 8 * ch);
-    }
-    cp_async_wait_all();
-    __syncwarp();
-
-    // S = Q K^T for the sub-tile's 4 n-tiles of 8 keys
-    float sc[4][4];
+    const uint32_t kb = smem_u32(ws.k[b]), vb = smem_u32(ws.v[b]);
+    // S = Q K^T for the tile's 2 n-tiles of 8 keys; even and odd k-steps accumulate apart
+    // (two independent chains per n-tile)
+    float sc[2][4], sc2[2][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[j][e] = sc2[j][e] = 0.f;
 #pragma unroll
       for (int kq = 0; kq < 4; ++kq) {  // two k-steps (32 dims) per ldmatrix.x4
         // matrices: (keys 8j.., dims 32kq + 0..7 | 8..15 | 16..23 | 24..31); lane -> row
         const int mi = lane >> 3, row = 8 * j + (lane & 7);
         uint32_t b0, b1, b2, b3;
-        ldsm_x4(smem_u32(ws.k) + sw_off(row, 4 * kq + mi), b0, b1, b2, b3);
+        ldsm_x4(kb + sw_off(row, 4 * kq + mi), b0, b1, b2, b3);
         mma_bf16(sc[j], qa[2 * kq][0], qa[2 * kq][1], qa[2 * kq][2], qa[2 * kq][3], b0, b1);
-        mma_bf16(sc[j], qa[2 * kq + 1][0], qa[2 * kq + 1][1], qa[2 * kq + 1][2], qa[2 * kq + 1][3], b2, b3);
+        mma_bf16(sc2[j], qa[2 * kq + 1][0], qa[2 * kq + 1][1], qa[2 * kq + 1][2], qa[2 * kq + 1][3], b2, b3);
       }
     }
     // mask, scale (base 2), online softmax per row (g: elements 0,1; g + 8: elements 2,3)
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int key = 8 * j + 2 * t + (e & 1), hr = e >> 1;
-        const int idx = ws.kidx[key];
+        const int idx = ws.kidx[s * kTile + key];
         bool vis = idx != INT32_MIN;
-        if (vis && idx < 0 && idx > kSinkTag) vis = visible(ws.kpos[key], qpos_r[hr], d.window, d.sinks);
-        const float x = vis ? sc[j][e] * sl2 : -INFINITY;
+        if (vis && idx < 0 && idx > kSinkTag) vis = visible(ws.kpos[b][key], qpos_r[hr], d.window, d.sinks);
+        const float x = vis ? (sc[j][e] + sc2[j][e]) * sl2 : -INFINITY;
         sc[j][e] = x;
         mx[hr] = fmaxf(mx[hr], x);
       }
@@ -199,10 +224,10 @@ __global__ void __launch_bounds__(32 * kWarps) quest_attend_mma_kernel(const pbk
       fac[hr] = m_run[hr] == -INFINITY ? 0.f : exp2f(m_run[hr] - m_new);
       m_run[hr] = m_new;
     }
-    uint32_t pa[2][4];  // P as A fragments for the two 16-key k-steps
+    uint32_t pa[4];  // P as the A fragment of the tile's one 16-key k-step
     float ls[2] = {0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 2; ++j) {
       float p[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -210,33 +235,34 @@ __global__ void __launch_bounds__(32 * kWarps) quest_attend_mma_kernel(const pbk
         p[e] = m == -INFINITY ? 0.f : exp2f(sc[j][e] - m);
         ls[e >> 1] += p[e];
       }
-      // n-tile j covers keys 8j..: k-step j / 2, low (j even) or high (j odd) half
-      pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16(p[0], p[1]);
-      pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16(p[2], p[3]);
+      // n-tile j covers keys 8j..: the low (j = 0) or high (j = 1) half of the k-step
+      pa[j * 2 + 0] = pack_bf16(p[0], p[1]);
+      pa[j * 2 + 1] = pack_bf16(p[2], p[3]);
     }
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) l_run[hr] = l_run[hr] * fac[hr] + ls[hr];
+    if (__any_sync(0xffffffffu, fac[0] != 1.f || fac[1] != 1.f)) {
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      o[nt][0] *= fac[0];
-      o[nt][1] *= fac[0];
-      o[nt][2] *= fac[1];
-      o[nt][3] *= fac[1];
-    }
-    // O += P V: k-step kv2 (keys 16 kv2..), n-tile pairs (dims 16 dp..)
-#pragma unroll
-    for (int kv2 = 0; kv2 < 2; ++kv2) {
-#pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        // matrices: (keys 16kv2 + 0..7, dims 16dp..+7), (keys +8..15, same), (keys 0..7, dims +8..15), (8..15, +8..)
-        const int mi = lane >> 3, row = 16 * kv2 + (mi & 1) * 8 + (lane & 7), ch = 2 * dp + (mi >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(ws.v) + sw_off(row, ch), b0, b1, b2, b3);
-        mma_bf16(o[2 * dp], pa[kv2][0], pa[kv2][1], pa[kv2][2], pa[kv2][3], b0, b1);
-        mma_bf16(o[2 * dp + 1], pa[kv2][0], pa[kv2][1], pa[kv2][2], pa[kv2][3], b2, b3);
+      for (int nt = 0; nt < 16; ++nt) {
+        o[nt][0] *= fac[0];
+        o[nt][1] *= fac[0];
+        o[nt][2] *= fac[1];
+        o[nt][3] *= fac[1];
       }
     }
-    __syncwarp();  // the smem tiles are rewritten by the next sub-tile
+    // O += P V: n-tile pairs (dims 16 dp..)
+#pragma unroll
+    for (int dp = 0; dp < 8; ++dp) {
+      // matrices: (keys 0..7, dims 16dp..+7), (keys 8..15, same), (keys 0..7, dims +8..15), (8..15, +8..)
+      const int mi = lane >> 3, row = (mi & 1) * 8 + (lane & 7), ch = 2 * dp + (mi >> 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vb + sw_off(row, ch), b0, b1, b2, b3);
+      mma_bf16(o[2 * dp], pa[0], pa[1], pa[2], pa[3], b0, b1);
+      mma_bf16(o[2 * dp + 1], pa[0], pa[1], pa[2], pa[3], b2, b3);
+    }
+    __syncwarp();  // stage b is rewritten by tile s + 2
+    if (s + 2 < ntiles) issue(s + 2, b);
+    else cp_async_commit();  // an empty group keeps "all but the newest" meaning tile s + 1
   }
   // row sums over the 4 lanes of a row, then the partials of rows g and g + 8
 #pragma unroll
@@ -262,13 +288,47 @@ __global__ void __launch_bounds__(32 * kWarps) quest_attend_mma_kernel(const pbk
 
 bool quest_attend_mma_supported(const pbk_quest_desc& d) { return d.t * (d.h / d.kv) <= 16; }
 
-cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, int splits, float* part,
-                                    const SinkKeys& sk, cudaStream_t st) {
+// Split length S in [256, 512] (a multiple of 16) that minimises waves x S, the launch's
+// length in key tiles: with `slots` resident blocks, the fewest waves, then the shortest
+// splits. Returns the number of splits per (query, key head) through *splits_out.
+static int choose_split(const pbk_quest_desc& d, int n_ret, int slots, int* splits_out, int* sr_out) {
+  int best = kMinSplit, best_cost = INT32_MAX;
+  const int64_t pairs = (int64_t)d.nq * d.kv;
+  for (int sl = kMinSplit; sl <= kMaxSplit; sl += kTile) {
+    const int sp = (n_ret + sl - 1) / sl + (d.n_win + sl - 1) / sl;
+    const int64_t blocks = (pairs * sp + kWarps - 1) / kWarps;
+    const int64_t waves = (blocks + slots - 1) / slots;
+    const int64_t cost = waves * sl;
+    if (cost < best_cost) best_cost = (int)cost, best = sl;
+  }
+  *sr_out = (n_ret + best - 1) / best;
+  *splits_out = *sr_out + (d.n_win + best - 1) / best;
+  return best;
+}
+
+cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, float* part, const SinkKeys& sk,
+                                    int* splits_out, cudaStream_t st) {
   const size_t smem = sizeof(WarpSmem) * kWarps;
   cudaError_t e = cudaFuncSetAttribute(quest_attend_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  quest_attend_mma_kernel<<<dim3((splits + kWarps - 1) / kWarps, d.nq * d.kv), 32 * kWarps, smem, st>>>(
-      d, k, tail, splits, part, sk);
+  static int slots[64] = {0};  // resident blocks per device (SMs x blocks per SM)
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 64 && slots[dev] == 0) {
+    int sms = 0, per_sm = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quest_attend_mma_kernel, 32 * kWarps, smem)) !=
+        cudaSuccess)
+      return e;
+    slots[dev] = sms * (per_sm > 0 ? per_sm : 1);
+  }
+  const int n_ret = sk.n + k * d.page + tail;
+  int splits = 0, sr = 0;
+  const int sl = choose_split(d, n_ret, dev < 64 ? slots[dev] : 148, &splits, &sr);
+  *splits_out = splits;
+  if (splits == 0) return cudaSuccess;
+  const int64_t blocks = ((int64_t)d.nq * d.kv * splits + kWarps - 1) / kWarps;
+  quest_attend_mma_kernel<<<(unsigned)blocks, 32 * kWarps, smem, st>>>(d, k, tail, sl, sr, splits, part, sk);
   return cudaGetLastError();
 }
 

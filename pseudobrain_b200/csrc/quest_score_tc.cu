@@ -11,8 +11,9 @@
 // Persistent CTAs, each owning a contiguous range of (key head, page tile) items:
 //   warp 0: TMA producer (3-stage ring of 64 KB stages, 128B swizzle, no multicast)
 //   warp 1: TMEM allocation and the MMA issuer (M=128 pages, N=R rounded to 16, K=256)
-//   warps 2-5: build B when the key head changes, read D from TMEM (double-buffered),
-//              reduce per group and store the scores.
+//   warps 2-9: two epilogue warpgroups, one per TMEM accumulator buffer (even / odd
+//              tiles): read D from TMEM, reduce per query group and store the scores; the
+//              group that meets a key head's first tile builds B for it.
 // Every mbarrier wait is bounded: on timeout the kernel records an error code in the
 // library's device error word and winds down (waiting, bounded, for its own loads and
 // MMAs), frees its TMEM and returns.
@@ -31,7 +32,7 @@ constexpr int kMaxRows = 64;                    // query rows per key head = MMA
 constexpr int kAtomBytes = kTileP * 128;        // [128 rows x 64 bf16] swizzled atom
 constexpr int kStageBytes = 4 * kAtomBytes;     // kmax d0-63 | kmax d64-127 | kmin d0-63 | kmin d64-127
 constexpr int kBAtomBytes = kMaxRows * 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kTmemCols = 2 * kMaxRows;         // two accumulator buffers
 
 struct __align__(1024) ScoreSmem {
@@ -57,6 +58,15 @@ __device__ __forceinline__ void record_error(int* err, int site, ScoreSmem& sm) 
   sm.abort = 1;
 }
 
+// Order-preserving map of fp32 to uint32 (and back), for integer warp reductions.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float order_key_inv(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 // Page score of every query group (the max of its RPG consecutive rows, RPG = 0: any
 // rows-per-group at run time), stored for page p; and, per group, the max over this
 // warp's 32 pages as one segment maximum.
@@ -79,11 +89,10 @@ __device__ __forceinline__ void group_max_store(const uint32_t (&v)[kMaxRows], c
         if (r >= n * rpg && r < (n + 1) * rpg) best = fmaxf(best, __uint_as_float(v[r]));
     }
     if (valid) args.scores[((int64_t)n * args.kv + kvh) * args.npages + p] = best;
-    if (args.segmax != nullptr) {  // this warp's 32 pages form one segment
-      float m = valid ? best : -INFINITY;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0 && (p >> 5) < args.nseg) args.segmax[((int64_t)n * args.kv + kvh) * args.nseg + (p >> 5)] = m;
+    if (args.segmax != nullptr) {  // this warp's 32 pages form one segment: one warp max
+      const uint32_t m = __reduce_max_sync(0xffffffffu, order_key(valid ? best : -INFINITY));
+      if (lane == 0 && (p >> 5) < args.nseg)
+        args.segmax[((int64_t)n * args.kv + kvh) * args.nseg + (p >> 5)] = order_key_inv(m);
     }
   }
 }
@@ -106,9 +115,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&sm.acc_full[b], 1);
-      tc::mbar_init(&sm.acc_empty[b], 4);  // one arrival per epilogue warp
+      tc::mbar_init(&sm.acc_empty[b], 4);  // one arrival per warp of the buffer's epilogue group
     }
-    tc::mbar_init(&sm.b_ready, 128);       // every epilogue thread, after its B writes
+    tc::mbar_init(&sm.b_ready, 128);       // every thread of the building group, after its B writes
     sm.abort = 0;
     tc::fence_barrier_init();
     tc::prefetch_tmap(&tmap_max);
@@ -182,17 +191,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         record_error(args.err, 6, sm);
     }
   } else {
-    // ---------------- epilogue: warps 2..5 ----------------
+    // ---------------- epilogue: warps 2..9, group eg takes tiles i = eg, eg + 2, ... ----------------
     const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
-    const int etid = threadIdx.x - 64;
+    const int eg = (warp - 2) >> 2, etid = (threadIdx.x - 64) & 127;
     const int rpg = args.t * args.groups;
-    int cur_kv = -1;
-    for (int i = 0; i < ntiles; ++i) {
+    for (int i = eg; i < ntiles; i += 2) {
       if (__any_sync(0xffffffffu, sm.abort)) break;  // warp-uniform exit
       const int tile = t_begin + i, kvh = tile / args.tiles_per_kv, p0 = (tile % args.tiles_per_kv) * kTileP;
-      if (kvh != cur_kv) {
-        // B = [max(q,0) | min(q,0)] for this key head's rows; the MMAs that read the old
-        // B completed before this warp consumed the previous tile's accumulator.
+      if (i == 0 || (tile - 1) / args.tiles_per_kv != kvh) {
+        // B = [max(q,0) | min(q,0)] for this key head's rows, once the MMAs that read the
+        // old B completed: the last of them is tile i-1's (the other group's buffer; its
+        // next phase needs this B, so the phase cannot move on before the wait).
+        if (i > 0) {
+          const bool ok = tc::mbar_wait(&sm.acc_full[(i - 1) & 1], ((i - 1) >> 1) & 1);
+          if (!__all_sync(0xffffffffu, ok)) {
+            record_error(args.err, 8, sm);
+            break;
+          }
+        }
         for (int e = etid; e < args.rows * 16; e += 128) {
           const int r = e >> 4, c = e & 15;  // 16-byte chunk c of row r (8 dims)
           const int n = r / rpg, rem = r % rpg, ti = rem / args.groups, g = rem % args.groups;
@@ -215,7 +231,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc::fence_proxy_async_smem();
         tc::mbar_arrive(&sm.b_ready);
-        cur_kv = kvh;
       }
       const int acc = i & 1;
       const bool ok = tc::mbar_wait(&sm.acc_full[acc], (i >> 1) & 1);

@@ -25,7 +25,19 @@ def gdn_prefill_(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Ten
         raise TypeError("state_indices must be int32")
     d = _desc(q, k, v, g, beta, o, h0, state, scale, state_indices, layout)
     with torch.cuda.device(dev):
-        check(LIB.pbk_gdn_prefill(d, _stream(dev)), "pbk_gdn_prefill")
+        _run(d, dev, "pbk_gdn_prefill")
+
+
+def _run(d, dev: torch.device, what: str) -> None:
+    """pbk_gdn_prefill_ws with a stream-ordered workspace from the caching allocator (the
+    chunk solve runs for all chunks at once first) where the tensor-core path takes the
+    call; pbk_gdn_prefill otherwise."""
+    n = LIB.pbk_gdn_prefill_workspace(d)
+    if n == 0:
+        check(LIB.pbk_gdn_prefill(d, _stream(dev)), what)
+        return
+    ws = torch.empty(n, dtype=torch.uint8, device=dev)
+    check(LIB.pbk_gdn_prefill_ws(d, ws.data_ptr(), n, _stream(dev)), what)
 
 
 @gdn_prefill_.register_fake
@@ -57,7 +69,7 @@ def gdn_final_state_(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch
     dev = _check_cuda(q, k, v, g, beta, state)
     d = _desc(q, k, v, g, beta, None, h0, state, scale, None, 0)
     with torch.cuda.device(dev):
-        check(LIB.pbk_gdn_prefill(d, _stream(dev)), "pbk_gdn_prefill (state only)")
+        _run(d, dev, "pbk_gdn_prefill (state only)")
 
 
 @gdn_final_state_.register_fake

@@ -191,3 +191,35 @@ def test_prefill_config1_tc_matches_exact_kernel(cuda_device):
     assert ogdn.rel_err(o[1:2, sl].float().cpu().numpy(), ro) < TOL_BF16
     from pseudobrain_b200._capi import device_error
     assert device_error() == 0
+
+
+@pytest.mark.parametrize("batch,length,hk,hv", [(1, 300, 1, 2), (2, 1000, 2, 4), (1, 64, 1, 1), (3, 1, 1, 2)])
+def test_prefill_tc_offloaded_solve_matches_inline_solve(cuda_device, batch, length, hk, hv):
+    """pbk_gdn_prefill_ws (chunk solve for all chunks first, copied in by the recurrence) and
+    pbk_gdn_prefill (solve inside the recurrence kernel) agree, and both match the oracle."""
+    from pseudobrain_b200._capi import LIB, PbkError, check, device_error
+    from pseudobrain_b200.gated_deltanet import _desc, _stream
+    inp = gdn_inputs(7 * length + hv, batch, length, hk, hv, bf16=True, state_std=0.02)
+    d = to_device(inp, cuda_device)
+    outs = []
+    for ws in (False, True):
+        o = torch.empty(batch, length, hv, 128, device=cuda_device)
+        s = torch.empty(batch, hv, 128, 128, device=cuda_device)
+        desc = _desc(d["q"], d["k"], d["v"], d["g"], d["beta"], o, d["h0"], s, inp["scale"], None, 0)
+        if ws:
+            n = LIB.pbk_gdn_prefill_workspace(desc)
+            assert n == batch * ((length + 63) // 64) * hv * 16384
+            buf = torch.empty(n + 16, dtype=torch.uint8, device=cuda_device)
+            with pytest.raises(PbkError):  # too small
+                check(LIB.pbk_gdn_prefill_ws(desc, buf.data_ptr(), n - 16, _stream(cuda_device)), "ws")
+            with pytest.raises(PbkError):  # not 16-byte aligned
+                check(LIB.pbk_gdn_prefill_ws(desc, buf.data_ptr() + 8, n, _stream(cuda_device)), "ws")
+            check(LIB.pbk_gdn_prefill_ws(desc, buf.data_ptr(), n, _stream(cuda_device)), "ws")
+        else:
+            check(LIB.pbk_gdn_prefill(desc, _stream(cuda_device)), "inline")
+        outs.append((o.cpu().numpy(), s.cpu().numpy()))
+    ro, rs = _oracle(inp)
+    for o, s in outs:
+        assert ogdn.rel_err(o, ro) < TOL_BF16 and ogdn.rel_err(s, rs) < TOL_BF16
+    assert ogdn.rel_err(outs[1][0], outs[0][0]) < 1e-2 and ogdn.rel_err(outs[1][1], outs[0][1]) < 1e-2
+    assert device_error() == 0
