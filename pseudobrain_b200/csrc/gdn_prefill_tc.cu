@@ -114,6 +114,16 @@ __device__ __forceinline__ void tmem_row32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 TMEM columns at each of two addresses of this thread's lane, one wait for both.
+__device__ __forceinline__ void tmem_row32x2(uint32_t ta, float* va, uint32_t tb, float* vb) {
+  uint32_t ra[32], rb[32];
+  tc::tmem_ld_32x32(ta, ra);
+  tc::tmem_ld_32x32(tb, rb);
+  tc::tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) va[i] = __uint_as_float(ra[i]), vb[i] = __uint_as_float(rb[i]);
+}
+
 // 32 fp32 values as bf16 into half `half` (elements 32 half .. 32 half + 31) of a 64-element
 // row of a 128B-swizzled tile.
 __device__ __forceinline__ void store_half_row_bf16(uint8_t* tile, int row, int half, const float* v) {
@@ -629,6 +639,16 @@ __global__ void __launch_bounds__(NT, 1)
     int last_v = 0;  // last V load issued (for the bounded drain)
     for (int m = 0; m < nchunks && ok; ++m) {
       const int buf = m & 1, sb = m % 3;
+      // K|Q, V (and TB | TBG) of chunk m + 2 into L2 now: their loads into shared memory wait
+      // for buffers that free up one chunk later, and then hit L2
+      if (pt == 0 && m + 2 < nchunks) {
+        for (int a = 0; a < 2; ++a) {
+          tc::tma_prefetch_4d(&tm_k, 64 * a, (m + 2) * C, hk, b);
+          tc::tma_prefetch_4d(&tm_q, 64 * a, (m + 2) * C, hk, b);
+          tc::tma_prefetch_4d(&tm_v, 64 * a, (m + 2) * C, h, b);
+        }
+        if (kOffload) tc::bulk_prefetch_l2(p.solve + (((int64_t)b * nchunks + m + 2) * p.hv + h) * kSolveBytes, kSolveBytes);
+      }
       // ---- [K;Q] K^T first: the scalar scan below runs under the MMA
       if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
       if (pt == 0) {
@@ -845,41 +865,55 @@ __global__ void __launch_bounds__(NT, 1)
           const uint64_t bw = tc::sdesc_sw128(tc::smem_u32(sm.wt[buf]) + kk * 2048, 16, 1024);
           tc::mma_f16(tmem + kColWS, ad, bw, i_kmn, kk != 0);
         }
+        // With U diag(e) in its own buffer (offloaded solve) the U epilogue waits for WS
+        // only; QS completes before the chunk's S update commits (commits track every earlier
+        // MMA of the issuing thread).
+        if (kOffload) tc::mma_commit(&sm.bar_ws);
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
           const uint64_t bq =
               tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][kk >> 2]) + 8192 + (kk & 3) * 32, 16, 1024);
           tc::mma_f16(tmem + kColQS, ad, bq, i_kk, kk != 0);
         }
-        tc::mma_commit(&sm.bar_ws);
+        if (!kOffload) tc::mma_commit(&sm.bar_ws);
       }
     };
     int last_kq[2] = {0, nchunks > 1 ? 1 : -1};  // last K|Q load per buffer (for the drain)
     // g and beta of chunk m into slot m & 3 (the role's last warp; lane l: steps 2l, 2l+1).
     // Slot m & 3 last held chunk m - 4, which the prep role scanned before announcing
-    // chunk m - 3, so the slot is free once the serial role has taken chunk m - 3.
+    // chunk m - 3, so the slot is free once the serial role has taken chunk m - 3. The loads
+    // run one call ahead: a call stores the values loaded by the previous call (chunk m) and
+    // issues the loads of chunk m + 1, so the warp never waits on them before a role barrier.
+    float pend[4] = {0.f, 0.f, 0.f, 0.f};
+    auto load_scalars = [&](int m) {
+      const int t = m * C + 2 * lane;
+      pend[0] = pend[1] = pend[2] = pend[3] = 0.f;
+      if (m < nchunks && t < p.seqlen) {
+        pend[0] = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
+        pend[2] = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
+      }
+      if (m < nchunks && t + 1 < p.seqlen) {
+        pend[1] = load_any(p.g, b * p.g_sb + (int64_t)(t + 1) * p.g_st + h * p.g_sh, p.g_dtype);
+        pend[3] = load_any(p.beta, b * p.b_sb + (int64_t)(t + 1) * p.b_st + h * p.b_sh, p.b_dtype);
+      }
+    };
     auto stage_scalars = [&](int m) {
       if (warp != kRoleWarps - 1 || m >= nchunks) return;
-      const int t = m * C + 2 * lane;
-      float x[4] = {0.f, 0.f, 0.f, 0.f};
-      if (t < p.seqlen) {
-        x[0] = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
-        x[2] = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
-      }
-      if (t + 1 < p.seqlen) {
-        x[1] = load_any(p.g, b * p.g_sb + (int64_t)(t + 1) * p.g_st + h * p.g_sh, p.g_dtype);
-        x[3] = load_any(p.beta, b * p.b_sb + (int64_t)(t + 1) * p.b_st + h * p.b_sh, p.b_dtype);
-      }
-      sm.gs[m & 3][2 * lane] = x[0];
-      sm.gs[m & 3][2 * lane + 1] = x[1];
-      sm.bs[m & 3][2 * lane] = x[2];
-      sm.bs[m & 3][2 * lane + 1] = x[3];
+      sm.gs[m & 3][2 * lane] = pend[0];
+      sm.gs[m & 3][2 * lane + 1] = pend[1];
+      sm.bs[m & 3][2 * lane] = pend[2];
+      sm.bs[m & 3][2 * lane + 1] = pend[3];
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.scal[m & 3]);
+      load_scalars(m + 1);
     };
+    if (warp == kRoleWarps - 1) load_scalars(0);
     stage_scalars(0);
     stage_scalars(1);
     stage_scalars(2);
+    // U diag(e), the A operand of the state update: its own tile when the solve is offloaded
+    // (the unused A scratch), else st[0] once the S^T products are done
+    uint8_t* const ue = kOffload ? reinterpret_cast<uint8_t*>(sm.a) : sm.st[0];
     if (swait(&sm.prep_ready, 0, 1)) state_step(0);
     for (int n = 0; n < nchunks && ok; ++n) {
       const int buf = n & 1, sb = n % 3;
@@ -889,15 +923,14 @@ __global__ void __launch_bounds__(NT, 1)
       if (!swait(&sm.bar_ws, n & 1, 2)) break;
       {
         float ws[32], up[32];
-        tmem_row32(lane_addr + kColWS + 32 * hf, ws);
-        tmem_row32(lane_addr + kColUP + 64 * buf + 32 * hf, up);
+        tmem_row32x2(lane_addr + kColWS + 32 * hf, ws, lane_addr + kColUP + 64 * buf + 32 * hf, up);
 #pragma unroll
         for (int i = 0; i < 32; ++i) up[i] -= ws[i];
         store_half_row_bf16(sm.ut, j, hf, up);
         const float* ee = sm.ee[sb] + 32 * hf;
 #pragma unroll
         for (int i = 0; i < 32; ++i) up[i] *= ee[i] * inv_next;
-        store_half_row_bf16(sm.st[0], j, hf, up);
+        store_half_row_bf16(ue, j, hf, up);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
@@ -910,7 +943,7 @@ __global__ void __launch_bounds__(NT, 1)
           tc::mma_f16(tmem + kColUM, ad, bm, i_kk, kk != 0);
         }
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[0]) + kk * 32, 16, 1024);
+          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(ue) + kk * 32, 16, 1024);
           const uint64_t bk = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][0]) + kk * 2048, 16384, 1024);
           tc::mma_f16(tmem + kColS, ad, bk, i_s, 1);
         }
@@ -926,8 +959,7 @@ __global__ void __launch_bounds__(NT, 1)
       float o[32];
       if (p.o != nullptr) {
         float um[32];
-        tmem_row32(lane_addr + kColQS + 32 * hf, o);
-        tmem_row32(lane_addr + kColUM + 32 * hf, um);
+        tmem_row32x2(lane_addr + kColQS + 32 * hf, o, lane_addr + kColUM + 32 * hf, um);
         const float* gm = sm.gam[sb] + 32 * hf;
 #pragma unroll
         for (int t = 0; t < 32; ++t) o[t] = fmaf(gm[t] * p.scale, o[t], um[t]);
@@ -992,6 +1024,8 @@ __global__ void __launch_bounds__(NT, 1)
 }
 
 constexpr size_t kSmemBytes = sizeof(PrefillSmem) + 1024;
+static_assert(offsetof(PrefillSmem, a) % 1024 == 0 && sizeof(PrefillSmem::a) >= 16384,
+              "the A scratch doubles as the U diag(e) operand tile (SW128, 1024-byte aligned)");
 
 bool make_map(CUtensorMap* m, const pbk_view& v, int heads, const pbk_gdn_desc& d) {
   const uint64_t dims[4] = {128, (uint64_t)d.seqlen, (uint64_t)heads, (uint64_t)d.batch};

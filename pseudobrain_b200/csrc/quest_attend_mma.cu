@@ -88,6 +88,47 @@ __device__ __forceinline__ int key_index(const pbk_quest_desc& d, int k, const S
   return (d.n_arch / d.page) * d.page + (r - k * d.page);
 }
 
+// Tile s of the warp's split into stage b: 16 key and 16 value rows of 16 chunks (8 of each
+// per lane), and the window keys' positions; rows past the split are zeroed (their
+// probabilities are 0, and 0 * (stale bits) could be NaN). One cp.async group per tile.
+__device__ __forceinline__ void stage_tile(WarpSmem& ws, int s, int b, int lane, const pbk_quest_desc& d,
+                                           const SinkKeys& sk, int h) {
+  const bf16* keys = reinterpret_cast<const bf16*>(d.keys);
+  const bf16* vals = reinterpret_cast<const bf16*>(d.values);
+  const bf16* wkeys = reinterpret_cast<const bf16*>(d.win_keys);
+  const bf16* wvals = reinterpret_cast<const bf16*>(d.win_values);
+#pragma unroll
+  for (int it = 0; it < kTile * 16 / 32; ++it) {
+    const int c = it * 32 + lane, r = c >> 4, ch = c & 15;
+    const int idx = ws.kidx[s * kTile + r];
+    const uint32_t ko = smem_u32(ws.k[b]) + sw_off(r, ch), vo = smem_u32(ws.v[b]) + sw_off(r, ch);
+    if (idx == INT32_MIN) {
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(ko), "r"(0u) : "memory");
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vo), "r"(0u) : "memory");
+      continue;
+    }
+    const bf16 *kr, *vr;
+    if (idx >= 0) {
+      kr = keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n;
+      vr = vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n;
+    } else if (idx > kSinkTag) {
+      kr = wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+      vr = wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
+    } else {
+      kr = sk.k + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
+      vr = sk.v + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
+    }
+    cp_async16(ko, kr + 8 * ch);
+    cp_async16(vo, vr + 8 * ch);
+  }
+  if (lane < kTile) {
+    const int idx = ws.kidx[s * kTile + lane];
+    if (idx < 0 && idx > kSinkTag) cp_async4(smem_u32(&ws.kpos[b][lane]), d.kpos + (-1 - idx));
+    else ws.kpos[b][lane] = 0;
+  }
+  cp_async_commit();
+}
+
 __global__ void __launch_bounds__(32 * kWarps, 3)
     quest_attend_mma_kernel(const pbk_quest_desc d, int k, int tail, int split_keys, int sr, int splits, float* part,
                             SinkKeys sk) {
@@ -104,10 +145,6 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
   const int j0 = win_split ? (split - sr) * split_keys : split * split_keys;
   const int nkeys = min(split_keys, (win_split ? d.n_win : n_ret) - j0);
   const int ntiles = (nkeys + kTile - 1) / kTile;
-  const bf16* keys = reinterpret_cast<const bf16*>(d.keys);
-  const bf16* vals = reinterpret_cast<const bf16*>(d.values);
-  const bf16* wkeys = reinterpret_cast<const bf16*>(d.win_keys);
-  const bf16* wvals = reinterpret_cast<const bf16*>(d.win_values);
   const bf16* q = reinterpret_cast<const bf16*>(d.q);
   const float sl2 = d.scale * 1.4426950408889634f;
 
@@ -117,41 +154,7 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
     ws.kidx[i] = i < nkeys ? key_index(d, k, sk, win_split, j0 + i, n, h) : INT32_MIN;
   __syncwarp();
 
-  // tile s into stage b: 16 key and 16 value rows of 16 chunks (8 of each per lane), and the
-  // window keys' positions; rows past the split are zeroed (their probabilities are 0, and
-  // 0 * (stale bits) could be NaN). One cp.async group per tile.
-  auto issue = [&](int s, int b) {
-#pragma unroll
-    for (int it = 0; it < kTile * 16 / 32; ++it) {
-      const int c = it * 32 + lane, r = c >> 4, ch = c & 15;
-      const int idx = ws.kidx[s * kTile + r];
-      const uint32_t ko = smem_u32(ws.k[b]) + sw_off(r, ch), vo = smem_u32(ws.v[b]) + sw_off(r, ch);
-      if (idx == INT32_MIN) {
-        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(ko), "r"(0u) : "memory");
-        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vo), "r"(0u) : "memory");
-        continue;
-      }
-      const bf16 *kr, *vr;
-      if (idx >= 0) {
-        kr = keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n;
-        vr = vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n;
-      } else if (idx > kSinkTag) {
-        kr = wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
-        vr = wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n;
-      } else {
-        kr = sk.k + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
-        vr = sk.v + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
-      }
-      cp_async16(ko, kr + 8 * ch);
-      cp_async16(vo, vr + 8 * ch);
-    }
-    if (lane < kTile) {
-      const int idx = ws.kidx[s * kTile + lane];
-      if (idx < 0 && idx > kSinkTag) cp_async4(smem_u32(&ws.kpos[b][lane]), d.kpos + (-1 - idx));
-      else ws.kpos[b][lane] = 0;
-    }
-    cp_async_commit();
-  };
+  auto issue = [&](int s, int b) { stage_tile(ws, s, b, lane, d, sk, h); };
 
   // Q fragments (rows g and g + 8 of the 16-row tile; rows past `rows` are zero): for k-step
   // kk, a0 = (g, 16kk + 2t..), a1 = (g + 8, ..), a2 = (g, 16kk + 8 + 2t..), a3 = (g + 8, ..)
@@ -284,6 +287,179 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
   }
 }
 
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+
+// Up to 8 query rows per task: the keys are the MMA's M dimension. S^T = K Q^T (m16n8k16: A = a
+// 16-key tile by ldmatrix, B = Q^T fragments in registers, 8 rows as N), the online softmax
+// runs per row over the key lanes, P^T goes from the accumulator layout to the B layout of
+// the next product with two movmatrix transposes, and O^T += V^T P^T (A = V^T by
+// ldmatrix.trans, 8 m-tiles of 16 dims). Half the MMAs of the 16-row kernel for these
+// shapes, and a quarter of its O registers. A window task serves every query of a
+// group of qpg = 8 / rows-per-query queries at once: the window keys are the same for all
+// queries of a key head (only the mask differs), so they are staged once per group.
+__global__ void __launch_bounds__(32 * kWarps, 3)
+    quest_attend_n8_kernel(const pbk_quest_desc d, int k, int tail, int split_keys, int sr, int sw, int qpg,
+                           float* part, SinkKeys sk) {
+  extern __shared__ __align__(16) uint8_t attn_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WarpSmem& ws = reinterpret_cast<WarpSmem*>(attn_raw)[warp];
+  const int task = blockIdx.x * kWarps + warp;
+  const int ret_tasks = d.nq * d.kv * sr, ngroups = (d.nq + qpg - 1) / qpg;
+  if (task >= ret_tasks + ngroups * d.kv * sw) return;
+  const bool win_split = task >= ret_tasks;
+  int n0, h, split, nqt;  // first query, key head, split index, queries in the task
+  if (!win_split) {
+    split = task % sr;
+    n0 = task / sr / d.kv;
+    h = task / sr % d.kv;
+    nqt = 1;
+  } else {
+    const int wt = task - ret_tasks;
+    split = sr + wt % sw;
+    n0 = wt / sw / d.kv * qpg;
+    h = wt / sw % d.kv;
+    nqt = min(qpg, d.nq - n0);
+  }
+  const int g = lane >> 2, t = lane & 3;
+  const int groups = d.h / d.kv, rpq = d.t * groups, rows = nqt * rpq;
+  const int n_ret = sk.n + k * d.page + tail;
+  const int j0 = (win_split ? split - sr : split) * split_keys;
+  const int nkeys = min(split_keys, (win_split ? d.n_win : n_ret) - j0);
+  const int ntiles = (nkeys + kTile - 1) / kTile;
+  const bf16* q = reinterpret_cast<const bf16*>(d.q);
+  const float sl2 = d.scale * 1.4426950408889634f;
+
+  for (int i = lane; i < ntiles * kTile; i += 32)
+    ws.kidx[i] = i < nkeys ? key_index(d, k, sk, win_split, j0 + i, n0, h) : INT32_MIN;
+  __syncwarp();
+  auto issue = [&](int s, int b) { stage_tile(ws, s, b, lane, d, sk, h); };
+  issue(0, 0);
+  if (ntiles > 1) issue(1, 1);
+  else cp_async_commit();
+
+  // row r of the task: query n0 + r / rpq, token (r % rpq) / groups, head h groups + r % groups
+  auto row_q = [&](int r) {
+    const int n = n0 + r / rpq, rem = r % rpq;
+    return q + n * d.q_stride_n + (rem / groups) * d.q_stride_t + (int64_t)(h * groups + rem % groups) * d.q_stride_h;
+  };
+  auto row_pos = [&](int r) { return d.qpos[(n0 + r / rpq) * d.t + (r % rpq) / groups]; };
+  // Q^T fragments (B: k = dims, n = row g): b0 = Q[g][16kk + 2t..], b1 = Q[g][16kk + 8 + 2t..]
+  uint32_t qb[8][2];
+  {
+    const bool ok = g < rows;
+    const bf16* qr = ok ? row_q(g) : q;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      qb[kk][0] = ok ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 2 * t) : 0u;
+      qb[kk][1] = ok ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 8 + 2 * t) : 0u;
+    }
+  }
+  int qp[2];  // positions of this lane's rows 2t, 2t + 1
+#pragma unroll
+  for (int e = 0; e < 2; ++e) qp[e] = 2 * t + e < rows ? row_pos(2 * t + e) : 0;
+
+  float o[8][4];  // O^T: dims 16 mt + g (+ 8) x rows 2t, 2t + 1
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // rows 2t, 2t + 1 (lane partial l)
+
+  for (int s = 0; s < ntiles; ++s) {
+    const int b = s & 1;
+    cp_async_wait_prev();
+    __syncwarp();
+    const uint32_t kb = smem_u32(ws.k[b]), vb = smem_u32(ws.v[b]);
+    // S^T = K Q^T: keys g, g + 8 (c0/c1 and c2/c3) x rows 2t, 2t + 1; even and odd k-steps apart
+    float sc[4] = {0.f, 0.f, 0.f, 0.f}, sc2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      // matrices: (keys 0-7, dims 16kk..+7), (keys 8-15, same), (keys 0-7, +8..15), (keys 8-15, +8..15)
+      const int mi = lane >> 3, row = (mi & 1) * 8 + (lane & 7);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(kb + sw_off(row, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
+      if (kk & 1) mma_bf16(sc2, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      else mma_bf16(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+    }
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int key = g + 8 * (e >> 1), r = e & 1;
+      const int idx = ws.kidx[s * kTile + key];
+      bool vis = idx != INT32_MIN;
+      if (vis && idx < 0 && idx > kSinkTag) vis = visible(ws.kpos[b][key], qp[r], d.window, d.sinks);
+      const float x = vis ? (sc[e] + sc2[e]) * sl2 : -INFINITY;
+      sc[e] = x;
+      mx[r] = fmaxf(mx[r], x);
+    }
+    float fac[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {  // max over the 8 key lanes (g) of each row
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 4));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 8));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 16));
+      const float m_new = fmaxf(m_run[r], mx[r]);
+      fac[r] = m_run[r] == -INFINITY ? 0.f : exp2f(m_run[r] - m_new);
+      m_run[r] = m_new;
+    }
+    float p[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float m = m_run[e & 1];
+      p[e] = m == -INFINITY ? 0.f : exp2f(sc[e] - m);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) l_run[r] = l_run[r] * fac[r] + (p[r] + p[2 + r]);
+    if (__any_sync(0xffffffffu, fac[0] != 1.f || fac[1] != 1.f)) {
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= fac[0];
+        o[mt][1] *= fac[1];
+        o[mt][2] *= fac[0];
+        o[mt][3] *= fac[1];
+      }
+    }
+    // P^T (keys x rows) in the accumulator layout -> B fragments (k = keys 2t.., n = row g)
+    const uint32_t pb0 = movmatrix_t(pack_bf16(p[0], p[1])), pb1 = movmatrix_t(pack_bf16(p[2], p[3]));
+    // O^T += V^T P^T: A = V^T (dims 16 mt .. x keys) by ldmatrix.trans of the V rows
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      // matrices: (keys 0-7, dims 16mt..+7), (keys 0-7, +8..15), (keys 8-15, ..+7), (keys 8-15, +8..15)
+      const int mi = lane >> 3, row = (mi >> 1) * 8 + (lane & 7), ch = 2 * mt + (mi & 1);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vb + sw_off(row, ch), a0, a1, a2, a3);
+      mma_bf16(o[mt], a0, a1, a2, a3, pb0, pb1);
+    }
+    __syncwarp();  // stage b is rewritten by tile s + 2
+    if (s + 2 < ntiles) issue(s + 2, b);
+    else cp_async_commit();
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {  // row sums over the 8 key lanes
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 4);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 8);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 16);
+  }
+  const int splits = sr + sw;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int r = 2 * t + e;
+    if (r >= rows) continue;
+    const int n = n0 + r / rpq, rem = r % rpq, ti = rem / groups, gg = rem % groups;
+    const int64_t prow = (((int64_t)n * d.t + ti) * d.h + h * groups + gg) * splits + split;
+    float* pp = part + prow * (kD + 2);
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      pp[16 * mt + g] = o[mt][e];
+      pp[16 * mt + 8 + g] = o[mt][2 + e];
+    }
+    if (g == 0) pp[kD] = m_run[e], pp[kD + 1] = l_run[e];
+  }
+}
+
 }  // namespace
 
 bool quest_attend_mma_supported(const pbk_quest_desc& d) { return d.t * (d.h / d.kv) <= 16; }
@@ -291,44 +467,55 @@ bool quest_attend_mma_supported(const pbk_quest_desc& d) { return d.t * (d.h / d
 // Split length S in [256, 512] (a multiple of 16) that minimises waves x S, the launch's
 // length in key tiles: with `slots` resident blocks, the fewest waves, then the shortest
 // splits. Returns the number of splits per (query, key head) through *splits_out.
-static int choose_split(const pbk_quest_desc& d, int n_ret, int slots, int* splits_out, int* sr_out) {
-  int best = kMinSplit, best_cost = INT32_MAX;
-  const int64_t pairs = (int64_t)d.nq * d.kv;
-  for (int sl = kMinSplit; sl <= kMaxSplit; sl += kTile) {
-    const int sp = (n_ret + sl - 1) / sl + (d.n_win + sl - 1) / sl;
-    const int64_t blocks = (pairs * sp + kWarps - 1) / kWarps;
-    const int64_t waves = (blocks + slots - 1) / slots;
-    const int64_t cost = waves * sl;
-    if (cost < best_cost) best_cost = (int)cost, best = sl;
+static int slots_for(const void* kernel, size_t smem, cudaError_t* err) {
+  static int slots[2][64] = {};  // resident blocks per device (SMs x blocks per SM), per kernel
+  const int which = kernel == (const void*)quest_attend_n8_kernel ? 1 : 0;
+  int dev = 0;
+  if ((*err = cudaGetDevice(&dev)) != cudaSuccess) return 0;
+  if (dev >= 64) return 148;
+  if (slots[which][dev] == 0) {
+    int sms = 0, per_sm = 0;
+    if ((*err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return 0;
+    if ((*err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32 * kWarps, smem)) != cudaSuccess)
+      return 0;
+    slots[which][dev] = sms * (per_sm > 0 ? per_sm : 1);
   }
-  *sr_out = (n_ret + best - 1) / best;
-  *splits_out = *sr_out + (d.n_win + best - 1) / best;
-  return best;
+  return slots[which][dev];
 }
 
 cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, float* part, const SinkKeys& sk,
                                     int* splits_out, cudaStream_t st) {
   const size_t smem = sizeof(WarpSmem) * kWarps;
-  cudaError_t e = cudaFuncSetAttribute(quest_attend_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int rpq = d.t * (d.h / d.kv);
+  const bool n8 = rpq <= 8;
+  const void* kernel = n8 ? (const void*)quest_attend_n8_kernel : (const void*)quest_attend_mma_kernel;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  static int slots[64] = {0};  // resident blocks per device (SMs x blocks per SM)
-  int dev = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  if (dev < 64 && slots[dev] == 0) {
-    int sms = 0, per_sm = 0;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quest_attend_mma_kernel, 32 * kWarps, smem)) !=
-        cudaSuccess)
-      return e;
-    slots[dev] = sms * (per_sm > 0 ? per_sm : 1);
-  }
+  const int slots = slots_for(kernel, smem, &e);
+  if (e != cudaSuccess) return e;
+  // Split length S in [256, 512] (a multiple of 16) that minimises waves x S, the launch's
+  // length in key tiles: with `slots` resident blocks, the fewest waves, then the shortest
+  // splits. The 8-row kernel's window tasks serve qpg queries each.
   const int n_ret = sk.n + k * d.page + tail;
-  int splits = 0, sr = 0;
-  const int sl = choose_split(d, n_ret, dev < 64 ? slots[dev] : 148, &splits, &sr);
-  *splits_out = splits;
-  if (splits == 0) return cudaSuccess;
-  const int64_t blocks = ((int64_t)d.nq * d.kv * splits + kWarps - 1) / kWarps;
-  quest_attend_mma_kernel<<<(unsigned)blocks, 32 * kWarps, smem, st>>>(d, k, tail, sl, sr, splits, part, sk);
+  const int qpg = n8 ? 8 / rpq : 1;
+  const int64_t pairs = (int64_t)d.nq * d.kv, wpairs = (int64_t)((d.nq + qpg - 1) / qpg) * d.kv;
+  int best = kMinSplit;
+  int64_t best_cost = INT64_MAX;
+  for (int sl = kMinSplit; sl <= kMaxSplit; sl += kTile) {
+    const int64_t tasks = pairs * ((n_ret + sl - 1) / sl) + wpairs * ((d.n_win + sl - 1) / sl);
+    const int64_t blocks = (tasks + kWarps - 1) / kWarps;
+    const int64_t cost = (blocks + slots - 1) / slots * sl;
+    if (cost < best_cost) best_cost = cost, best = sl;
+  }
+  const int sr = (n_ret + best - 1) / best, sw = (d.n_win + best - 1) / best;
+  *splits_out = sr + sw;
+  if (sr + sw == 0) return cudaSuccess;
+  const int64_t tasks = pairs * sr + wpairs * sw;
+  const unsigned blocks = (unsigned)((tasks + kWarps - 1) / kWarps);
+  if (n8)
+    quest_attend_n8_kernel<<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sw, qpg, part, sk);
+  else
+    quest_attend_mma_kernel<<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sr + sw, part, sk);
   return cudaGetLastError();
 }
 
