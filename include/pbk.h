@@ -117,9 +117,9 @@ PBK_API int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream);
 
 /* pbk_gdn_prefill with the chunk solve split out: on the tensor-core path (bf16 q/k/v) a
  * first kernel solves every chunk of every (sequence, value head) at once -- the
- * state-independent T = (I + A)^-1 of gated_deltanet.py:131-140 and its products with
- * diag(beta) and diag(beta gamma), 16 KB per chunk -- into `workspace`, and the recurrence
- * kernel copies them in instead of solving in line. Same results as pbk_gdn_prefill (the
+ * state-independent T = (I + A)^-1 of gated_deltanet.py:131-140, its products with
+ * diag(beta) and diag(beta gamma) and the chunk's decay scalars, 17,936 bytes per chunk --
+ * into `workspace`, and the recurrence kernel copies them in instead of solving in line. Same results as pbk_gdn_prefill (the
  * same arithmetic). workspace: at least pbk_gdn_prefill_workspace(desc) bytes, 16-byte
  * aligned, private to the call until it completes on `stream`. Off the tensor-core path
  * (fp32 inputs) the workspace is unused and may be NULL. */

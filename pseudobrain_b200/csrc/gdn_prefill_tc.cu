@@ -47,6 +47,16 @@ constexpr int PA = C + 4;  // fp32 row stride of A (16-byte rows)
 constexpr uint32_t kColS = 0, kColD1 = 128, kColUP = 192, kColWS = 320, kColQS = 384, kColUM = 448;
 constexpr uint32_t kTmemCols = 512;
 
+// A chunk's decay scalars (log2 units): cumulative decay c2, gamma = exp2(c2), e =
+// exp2(c2_last - c2), the factored decay da = exp2(c2 - c2_31), db = exp2(c2_31 - c2) and
+// whether the chunk's span (< 60) allows it, and beta. The solve kernel writes one per chunk
+// after TB | TBG, and the recurrence copies it in with them.
+struct ChunkScalars {
+  float cum2[C], gam[C], ee[C], da[C], db[C], beta[C];
+  int factored;
+  int pad_[3];
+};
+
 struct __align__(1024) PrefillSmem {
   uint8_t kq[2][2][16384];   // [buf][dk atom][rows 0-63 K, 64-127 Q] x 64 bf16, SW128
   uint8_t v[2][8192];        // [dv atom][64 rows] x 64 bf16, SW128
@@ -57,10 +67,8 @@ struct __align__(1024) PrefillSmem {
   uint8_t tbg[8192];         // T diag(beta gamma) bf16 [64 t x 64 i]
   uint8_t ut[16384];         // U^T bf16 [128 dv rows x 64 t] (A operand); also output staging
   float a[C * PA];           // A fp32
-  float cum[3][C], cum2[3][C], gam[3][C], ee[3][C], beta[3][C];
-  float da[3][C], db[3][C];  // exp2(c_t - c_ref), exp2(c_ref - c_i): the decay in factored form
-  float gs[4][C], bs[4][C];  // raw g and beta, staged 3 chunks ahead by a serial warp
-  int factored[3];           // the chunk's decay span allows the factored form
+  ChunkScalars cs[4];        // chunk m's scalars in slot m & 3
+  float gs[4][C], bs[4][C];  // raw g and beta, staged 3 chunks ahead by a serial warp (in-line solve)
   uint64_t bar_kq[2], bar_v, bar_tb, bar_p1, bar_p3, bar_ws, bar_s, prep_ready, drain_s, drain_p, scal[4];
   uint32_t tmem_base;
   volatile int abort;
@@ -280,7 +288,9 @@ __device__ __forceinline__ void store_tb_tbg(const float* ts, const float* beta,
 // prefill kernel's MMAs read) to workspace slot (sequence, chunk, head). The prefill kernel
 // then only copies them in.
 constexpr int kSolveThreads = 128;
-constexpr uint32_t kSolveBytes = 2 * 8192;  // TB | TBG per (sequence, chunk, value head)
+// TB | TBG | ChunkScalars per (sequence, chunk, value head)
+constexpr uint32_t kSolveBytes = 2 * 8192 + sizeof(ChunkScalars);
+static_assert(sizeof(ChunkScalars) % 16 == 0, "bulk copies move multiples of 16 bytes");
 
 // 16x16 fp32 blocks (1 KB): element (r, c) at r * 16 + (c ^ bsw(r)). The swizzle keeps both
 // mma.sync tf32 operand patterns (A: rows g, columns t; B: rows t, columns g) free of bank
@@ -369,12 +379,31 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
       if (lane >= o) incl += y;
     }
     const float c0 = (incl - pair + g0) * kLog2e, c1 = incl * kLog2e;
+    const float ga0 = exp2f(c0), ga1 = exp2f(c1);
     sm.c2[2 * lane] = c0;
     sm.c2[2 * lane + 1] = c1;
-    sm.gam[2 * lane] = exp2f(c0);
-    sm.gam[2 * lane + 1] = exp2f(c1);
+    sm.gam[2 * lane] = ga0;
+    sm.gam[2 * lane + 1] = ga1;
     sm.beta[2 * lane] = b0;
     sm.beta[2 * lane + 1] = b1;
+    // the chunk's scalar record for the recurrence kernel (after TB | TBG): e = exp2(c_last -
+    // c), and the factored decay about c_ref = c_31 while the log2 span stays below 60
+    ChunkScalars* rec = reinterpret_cast<ChunkScalars*>(
+        p.ws + (((int64_t)b * gridDim.x + m) * p.hv + h) * kSolveBytes + 2 * 8192);
+    const float clast = __shfl_sync(0xffffffffu, c1, 31), ref = __shfl_sync(0xffffffffu, c1, 15);
+    float hi = fmaxf(c0, c1), lo = fminf(c0, c1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    }
+    *reinterpret_cast<float2*>(&rec->cum2[2 * lane]) = make_float2(c0, c1);
+    *reinterpret_cast<float2*>(&rec->gam[2 * lane]) = make_float2(ga0, ga1);
+    *reinterpret_cast<float2*>(&rec->ee[2 * lane]) = make_float2(exp2f(clast - c0), exp2f(clast - c1));
+    *reinterpret_cast<float2*>(&rec->da[2 * lane]) = make_float2(exp2f(c0 - ref), exp2f(c1 - ref));
+    *reinterpret_cast<float2*>(&rec->db[2 * lane]) = make_float2(exp2f(ref - c0), exp2f(ref - c1));
+    *reinterpret_cast<float2*>(&rec->beta[2 * lane]) = make_float2(b0, b1);
+    if (lane == 0) rec->factored = (hi - lo) < 60.f;
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
@@ -601,11 +630,14 @@ __global__ void __launch_bounds__(NT, 1)
     tc::mbar_expect_tx(&sm.bar_v, 2 * 8192);
     for (int a = 0; a < 2; ++a) tc::tma_load_4d(sm.v[a], &tm_v, &sm.bar_v, 64 * a, m * C, h, b);
   };
-  // With the solve offloaded: chunk m's TB | TBG (16 KB, contiguous in sm.tb, sm.tbg) by one
-  // bulk copy, issued by the prep leader once chunk m-1's U' and W^T products are done.
+  // With the solve offloaded: chunk m's TB | TBG (16 KB, contiguous in sm.tb, sm.tbg) and its
+  // scalars (slot m & 3, last read for chunk m-4) by bulk copies, issued by the prep leader
+  // once chunk m-1's U' and W^T products are done.
   auto issue_tb = [&](int m) {
+    const uint8_t* src = p.solve + (((int64_t)b * nchunks + m) * p.hv + h) * kSolveBytes;
     tc::mbar_expect_tx(&sm.bar_tb, kSolveBytes);
-    tc::bulk_load(sm.tb, p.solve + (((int64_t)b * nchunks + m) * p.hv + h) * kSolveBytes, kSolveBytes, &sm.bar_tb);
+    tc::bulk_load(sm.tb, src, 2 * 8192, &sm.bar_tb);
+    tc::bulk_load(&sm.cs[m & 3], src + 2 * 8192, sizeof(ChunkScalars), &sm.bar_tb);
   };
   if (tid == 0) {
     tc::prefetch_tmap(&tm_q);
@@ -638,7 +670,7 @@ __global__ void __launch_bounds__(NT, 1)
     };
     int last_v = 0;  // last V load issued (for the bounded drain)
     for (int m = 0; m < nchunks && ok; ++m) {
-      const int buf = m & 1, sb = m % 3;
+      const int buf = m & 1, sb = m & 3;
       // K|Q, V (and TB | TBG) of chunk m + 2 into L2 now: their loads into shared memory wait
       // for buffers that free up one chunk later, and then hit L2
       if (pt == 0 && m + 2 < nchunks) {
@@ -659,8 +691,10 @@ __global__ void __launch_bounds__(NT, 1)
         }
         tc::mma_commit(&sm.bar_p1);
       }
+      // the copied-in TB | TBG and scalars of chunk m (offloaded solve)
+      if (kOffload && !pwait(&sm.bar_tb, m & 1, 6)) break;
       // ---- scalars: cumulative log decay c, gamma = e^c, e = e^(c_C - c), beta
-      if (pw == 0) {
+      if (!kOffload && pw == 0) {
         constexpr float kLog2e = 1.4426950408889634f;
         // g and beta of chunk m, staged in shared memory by a serial warp
         if (!tc::mbar_wait(&sm.scal[m & 3], (m >> 2) & 1)) {
@@ -678,14 +712,14 @@ __global__ void __launch_bounds__(NT, 1)
         }
         const float c0 = incl - pair + g0, c1 = incl;
         const float clast = __shfl_sync(0xffffffffu, incl, 31);
-        sm.cum2[sb][2 * lane] = c0 * kLog2e;
-        sm.cum2[sb][2 * lane + 1] = c1 * kLog2e;
-        sm.gam[sb][2 * lane] = exp2f(c0 * kLog2e);
-        sm.gam[sb][2 * lane + 1] = exp2f(c1 * kLog2e);
-        sm.ee[sb][2 * lane] = exp2f((clast - c0) * kLog2e);
-        sm.ee[sb][2 * lane + 1] = exp2f((clast - c1) * kLog2e);
-        sm.beta[sb][2 * lane] = b0;
-        sm.beta[sb][2 * lane + 1] = b1;
+        sm.cs[sb].cum2[2 * lane] = c0 * kLog2e;
+        sm.cs[sb].cum2[2 * lane + 1] = c1 * kLog2e;
+        sm.cs[sb].gam[2 * lane] = exp2f(c0 * kLog2e);
+        sm.cs[sb].gam[2 * lane + 1] = exp2f(c1 * kLog2e);
+        sm.cs[sb].ee[2 * lane] = exp2f((clast - c0) * kLog2e);
+        sm.cs[sb].ee[2 * lane + 1] = exp2f((clast - c1) * kLog2e);
+        sm.cs[sb].beta[2 * lane] = b0;
+        sm.cs[sb].beta[2 * lane + 1] = b1;
         // decay factors exp2(c_t - c_i) = da_t db_i about c_ref = c_31, exact enough while
         // the chunk's log2 decay spans less than 60 (no factor leaves fp32's normal range)
         const float l0 = c0 * kLog2e, l1 = c1 * kLog2e;
@@ -696,18 +730,18 @@ __global__ void __launch_bounds__(NT, 1)
           hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
           lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
         }
-        sm.da[sb][2 * lane] = exp2f(l0 - ref);
-        sm.da[sb][2 * lane + 1] = exp2f(l1 - ref);
-        sm.db[sb][2 * lane] = exp2f(ref - l0);
-        sm.db[sb][2 * lane + 1] = exp2f(ref - l1);
-        if (lane == 0) sm.factored[sb] = (hi - lo) < 60.f;
+        sm.cs[sb].da[2 * lane] = exp2f(l0 - ref);
+        sm.cs[sb].da[2 * lane + 1] = exp2f(l1 - ref);
+        sm.cs[sb].db[2 * lane] = exp2f(ref - l0);
+        sm.cs[sb].db[2 * lane + 1] = exp2f(ref - l1);
+        if (lane == 0) sm.cs[sb].factored = (hi - lo) < 60.f;
       }
       if (!pwait(&sm.bar_p1, m & 1, 2)) break;
       // ---- A (fp32) from K K^T rows (lanes 0-63), M (bf16) from Q K^T rows (lanes 64-127);
       // this thread: row `row`, columns 32 hf .. 32 hf + 31. With the solve offloaded only
       // M is needed (warp-uniform: warps of quadrants 0-1 hold the K K^T rows).
       if (!kOffload || row >= C) {
-        const float* c2 = sm.cum2[sb];
+        const float* c2 = sm.cs[sb].cum2;
         const int t = row & 63, i0 = 32 * hf;
         const bool zero = t < 32 && hf == 1;  // rows 0-31 have no terms past column 31
         float v[32];
@@ -715,9 +749,9 @@ __global__ void __launch_bounds__(NT, 1)
         // decay D_ti = exp2(c_t - c_i) for i <= t: factored (one multiply) or direct
         if (!zero) {
           const float ct = c2[t];
-          if (sm.factored[sb]) {
-            const float dt = sm.da[sb][t];
-            const float* dbi = sm.db[sb] + i0;
+          if (sm.cs[sb].factored) {
+            const float dt = sm.cs[sb].da[t];
+            const float* dbi = sm.cs[sb].db + i0;
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] *= dt * dbi[i];
           } else {
@@ -726,7 +760,7 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
         if (row < C) {
-          const float bt = sm.beta[sb][t];
+          const float bt = sm.cs[sb].beta[t];
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -751,12 +785,11 @@ __global__ void __launch_bounds__(NT, 1)
         float* ts = reinterpret_cast<float*>(sm.wt[buf]);
         invert_unit_lower(sm.a, ts, reinterpret_cast<float*>(sm.tb), pw, lane, [] { role_sync(2); });
         // the tb scratch reads ended at the inverse's last barrier
-        store_tb_tbg(ts, sm.beta[sb], sm.gam[sb], pt >> 2, pt & 3, sm.tb, sm.tbg);
+        store_tb_tbg(ts, sm.cs[sb].beta, sm.cs[sb].gam, pt >> 2, pt & 3, sm.tb, sm.tbg);
       }
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       // ---- W^T = K^T TBG^T -> D1; U'^T = V^T TB^T -> UP[buf]
-      if (kOffload && !pwait(&sm.bar_tb, m & 1, 6)) break;
       if (!pwait(&sm.bar_v, m & 1, 3)) break;
       if (pt == 0) {
         for (int kk = 0; kk < 4; ++kk) {
@@ -835,8 +868,8 @@ __global__ void __launch_bounds__(NT, 1)
     // TMEM is rescaled only when big_g would fall below 2^-100 (fp32 keeps the ratio exact).
     float big_g = 1.f, inv_next = 1.f;
     auto state_step = [&](int n) {
-      const int buf = n & 1, sb = n % 3;
-      const float gnext = big_g * sm.gam[sb][C - 1];
+      const int buf = n & 1, sb = n & 3;
+      const float gnext = big_g * sm.cs[sb].gam[C - 1];
       const bool renorm = gnext < 0x1p-100f;  // identical in every thread of the role
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -898,7 +931,7 @@ __global__ void __launch_bounds__(NT, 1)
       }
     };
     auto stage_scalars = [&](int m) {
-      if (warp != kRoleWarps - 1 || m >= nchunks) return;
+      if (kOffload || warp != kRoleWarps - 1 || m >= nchunks) return;
       sm.gs[m & 3][2 * lane] = pend[0];
       sm.gs[m & 3][2 * lane + 1] = pend[1];
       sm.bs[m & 3][2 * lane] = pend[2];
@@ -907,7 +940,7 @@ __global__ void __launch_bounds__(NT, 1)
       if (lane == 0) tc::mbar_arrive(&sm.scal[m & 3]);
       load_scalars(m + 1);
     };
-    if (warp == kRoleWarps - 1) load_scalars(0);
+    if (!kOffload && warp == kRoleWarps - 1) load_scalars(0);
     stage_scalars(0);
     stage_scalars(1);
     stage_scalars(2);
@@ -916,7 +949,7 @@ __global__ void __launch_bounds__(NT, 1)
     uint8_t* const ue = kOffload ? reinterpret_cast<uint8_t*>(sm.a) : sm.st[0];
     if (swait(&sm.prep_ready, 0, 1)) state_step(0);
     for (int n = 0; n < nchunks && ok; ++n) {
-      const int buf = n & 1, sb = n % 3;
+      const int buf = n & 1, sb = n & 3;
       // U = U' - WS -> U^T bf16 (ut) and U diag(e) (st[0], free: the S^T products are
       // done); then UM^T = U^T M^T and S^T += (U diag(e))^T K. This thread: t = 32 hf ..
       if (tid == 0) tc::bulk_wait_read0();  // the output store of chunk n-1 has read ut
@@ -927,7 +960,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) up[i] -= ws[i];
         store_half_row_bf16(sm.ut, j, hf, up);
-        const float* ee = sm.ee[sb] + 32 * hf;
+        const float* ee = sm.cs[sb].ee + 32 * hf;
 #pragma unroll
         for (int i = 0; i < 32; ++i) up[i] *= ee[i] * inv_next;
         store_half_row_bf16(ue, j, hf, up);
@@ -960,7 +993,7 @@ __global__ void __launch_bounds__(NT, 1)
       if (p.o != nullptr) {
         float um[32];
         tmem_row32x2(lane_addr + kColQS + 32 * hf, o, lane_addr + kColUM + 32 * hf, um);
-        const float* gm = sm.gam[sb] + 32 * hf;
+        const float* gm = sm.cs[sb].gam + 32 * hf;
 #pragma unroll
         for (int t = 0; t < 32; ++t) o[t] = fmaf(gm[t] * p.scale, o[t], um[t]);
       }

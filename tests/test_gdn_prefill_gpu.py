@@ -208,7 +208,7 @@ def test_prefill_tc_offloaded_solve_matches_inline_solve(cuda_device, batch, len
         desc = _desc(d["q"], d["k"], d["v"], d["g"], d["beta"], o, d["h0"], s, inp["scale"], None, 0)
         if ws:
             n = LIB.pbk_gdn_prefill_workspace(desc)
-            assert n == batch * ((length + 63) // 64) * hv * 16384
+            assert n == batch * ((length + 63) // 64) * hv * (16384 + 1552)  # TB | TBG | scalars
             buf = torch.empty(n + 16, dtype=torch.uint8, device=cuda_device)
             with pytest.raises(PbkError):  # too small
                 check(LIB.pbk_gdn_prefill_ws(desc, buf.data_ptr(), n - 16, _stream(cuda_device)), "ws")
