@@ -867,6 +867,17 @@ __global__ void __launch_bounds__(NT, 1)
     // decays since the last renormalisation; chunk n's update adds K^T U diag(e) / big_g, and
     // TMEM is rescaled only when big_g would fall below 2^-100 (fp32 keeps the ratio exact).
     float big_g = 1.f, inv_next = 1.f;
+    // (QS)^T = S^T Q^T of chunk n (thread 0): the state's bf16 copy in st, Q in chunk n's K|Q.
+    // Its TMEM columns must have been read for chunk n-1, and st stays unchanged until the
+    // chunk's S update commits (which covers QS: commits track every earlier MMA).
+    auto issue_qs = [&](int n) {
+      const int buf = n & 1;
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
+        const uint64_t bq = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][kk >> 2]) + 8192 + (kk & 3) * 32, 16, 1024);
+        tc::mma_f16(tmem + kColQS, ad, bq, i_kk, kk != 0);
+      }
+    };
     auto state_step = [&](int n) {
       const int buf = n & 1, sb = n & 3;
       const float gnext = big_g * sm.cs[sb].gam[C - 1];
@@ -898,17 +909,10 @@ __global__ void __launch_bounds__(NT, 1)
           const uint64_t bw = tc::sdesc_sw128(tc::smem_u32(sm.wt[buf]) + kk * 2048, 16, 1024);
           tc::mma_f16(tmem + kColWS, ad, bw, i_kmn, kk != 0);
         }
-        // With U diag(e) in its own buffer (offloaded solve) the U epilogue waits for WS
-        // only; QS completes before the chunk's S update commits (commits track every earlier
-        // MMA of the issuing thread).
-        if (kOffload) tc::mma_commit(&sm.bar_ws);
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bq =
-              tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][kk >> 2]) + 8192 + (kk & 3) * 32, 16, 1024);
-          tc::mma_f16(tmem + kColQS, ad, bq, i_kk, kk != 0);
-        }
-        if (!kOffload) tc::mma_commit(&sm.bar_ws);
+        // With U diag(e) in its own buffer (offloaded solve) QS leaves the critical path: it
+        // is issued once the previous chunk's outputs have been read (issue_qs below).
+        if (!kOffload) issue_qs(n);
+        tc::mma_commit(&sm.bar_ws);
       }
     };
     int last_kq[2] = {0, nchunks > 1 ? 1 : -1};  // last K|Q load per buffer (for the drain)
@@ -947,7 +951,10 @@ __global__ void __launch_bounds__(NT, 1)
     // U diag(e), the A operand of the state update: its own tile when the solve is offloaded
     // (the unused A scratch), else st[0] once the S^T products are done
     uint8_t* const ue = kOffload ? reinterpret_cast<uint8_t*>(sm.a) : sm.st[0];
-    if (swait(&sm.prep_ready, 0, 1)) state_step(0);
+    if (swait(&sm.prep_ready, 0, 1)) {
+      state_step(0);
+      if (kOffload && p.o != nullptr && tid == 0) issue_qs(0);
+    }
     for (int n = 0; n < nchunks && ok; ++n) {
       const int buf = n & 1, sb = n & 3;
       // U = U' - WS -> U^T bf16 (ut) and U diag(e) (st[0], free: the S^T products are
@@ -987,16 +994,18 @@ __global__ void __launch_bounds__(NT, 1)
         issue_kq(n + 2);
         last_kq[buf] = n + 2;
       }
-      // O = gamma scale QS + UM (registers; t = 32 hf + i), then the next chunk's state
-      // step, then O through shared memory and a TMA store.
+      // O = gamma scale QS + UM (registers; t = 32 hf + i) and the next chunk's state step;
+      // then O through shared memory and a TMA store. With the solve offloaded the state step
+      // comes first, so that O's reads and store run while WS of chunk n+1 executes.
       float o[32];
-      if (p.o != nullptr) {
+      auto compute_o = [&]() {
         float um[32];
         tmem_row32x2(lane_addr + kColQS + 32 * hf, o, lane_addr + kColUM + 32 * hf, um);
         const float* gm = sm.cs[sb].gam + 32 * hf;
 #pragma unroll
         for (int t = 0; t < 32; ++t) o[t] = fmaf(gm[t] * p.scale, o[t], um[t]);
-      }
+      };
+      if (!kOffload && p.o != nullptr) compute_o();
       tc::fence_before_sync();
       stage_scalars(n + 3);  // chunk n took the prep role's announcement of chunk n
       if (n + 1 < nchunks) {
@@ -1006,6 +1015,7 @@ __global__ void __launch_bounds__(NT, 1)
       // staging in ut as row-major [rows][128]; rows past the sequence end fall outside
       // the tensor and are not written by the store
       if (p.o == nullptr) continue;
+      if (kOffload) compute_o();
       constexpr int kRows = sizeof(TOut) == 2 ? 64 : 32;  // 16 KB per pass
       TOut* stage = reinterpret_cast<TOut*>(sm.ut);
 #pragma unroll
@@ -1019,10 +1029,15 @@ __global__ void __launch_bounds__(NT, 1)
           for (int t = 0; t < 32; ++t) stage[(32 * hf - t0 + t) * D + j] = from_f32<TOut>(o[t]);
         }
         tc::fence_proxy_async_smem();
+        tc::fence_before_sync();  // every thread's TMEM reads of QS, UM precede QS(n+1)
         role_sync(1);
         if (tid == 0) {
           tc::tma_store_4d(&tm_o, stage, 0, n * C + t0, h, b);
           tc::bulk_commit();
+          if (kOffload && t0 == 0 && n + 1 < nchunks) {
+            tc::fence_after_sync();
+            issue_qs(n + 1);
+          }
         }
       }
     }
