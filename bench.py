@@ -432,7 +432,7 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         "swa": {"ms": t_swa * 1e3, "tflops": swa_flops / world / t_swa / 1e12,
                 "frac": swa_flops / world / t_swa / 1e12 / pk["tc_sustained"]},
         "e2e": None,
-        "gpu_launches": steps * (4 * 2 + 1 + 1),  # 4 prefill runs (solve + recurrence), scan, attention
+        "gpu_launches": steps * (1 + 4 + 1 + 1),  # one chunk solve, 4 recurrence runs, scan, attention
     }
     if world > 1:
         out["all_gather"] = {"ms": t_ag * 1e3, "bytes_received_per_gpu": ag_bytes,

@@ -126,6 +126,17 @@ PBK_API int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream);
 PBK_API size_t pbk_gdn_prefill_workspace(const pbk_gdn_desc* desc);
 PBK_API int pbk_gdn_prefill_ws(const pbk_gdn_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The two halves of pbk_gdn_prefill_ws, tensor-core path only (PBK_ERR_INVALID otherwise):
+ * pbk_gdn_chunk_solve writes the workspace from k, g and beta; pbk_gdn_prefill_solved runs
+ * the recurrence from a workspace holding the solve of the same chunks. Slot (b, chunk, h)
+ * sits at ((b * nchunks + chunk) * hv + h) * 17,936 bytes, so the solve of one long sequence
+ * also serves runs over segments of it (whole chunks, viewed as a batch of segments; a
+ * later segment starts at its first chunk's slot): the sequence-split prefill solves once
+ * and runs the recurrence three times. */
+PBK_API int pbk_gdn_chunk_solve(const pbk_gdn_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+PBK_API int pbk_gdn_prefill_solved(const pbk_gdn_desc* desc, const void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
 /* Segment scan for a prefill split along T into nseg segments of whole 64-token chunks
  * (parallelism inside one long sequence; the reference runs a sequence's chunks in
  * order, gated_deltanet.py:157-163). A segment's recurrence is affine in its initial

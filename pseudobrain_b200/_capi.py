@@ -73,6 +73,8 @@ SIGNATURES = {
     "pbk_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
     "pbk_gdn_prefill_workspace": (ctypes.c_size_t, [ctypes.POINTER(PbkGdnDesc)]),
     "pbk_gdn_prefill_ws": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),
+    "pbk_gdn_chunk_solve": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),
+    "pbk_gdn_prefill_solved": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),
     "pbk_gdn_segment_scan": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I32, _I32, _I32, _VP]),
     "pbk_quest_select_workspace": (ctypes.c_size_t, [_QD]),
     "pbk_quest_attend_workspace": (ctypes.c_size_t, [_QD]),

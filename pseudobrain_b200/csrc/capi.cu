@@ -11,7 +11,8 @@ cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st);
 bool gdn_prefill_tc_supported(const pbk_gdn_desc& d);
 size_t gdn_prefill_tc_workspace(const pbk_gdn_desc& d);
-cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, cudaStream_t st);
+cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t st);
+cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, bool solved, cudaStream_t st);
 cudaError_t launch_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int batch,
                                     int nseg, int hv, cudaStream_t st);
 }
@@ -183,7 +184,7 @@ int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {
   // bf16 inputs: tensor-core kernel (bf16 operands, fp32 state and accumulation);
   // fp32 inputs: the exact fp32 kernel.
   const cudaError_t e = pbk::gdn_prefill_tc_supported(*desc)
-                            ? pbk::launch_gdn_prefill_tc(*desc, nullptr, static_cast<cudaStream_t>(stream))
+                            ? pbk::launch_gdn_prefill_tc(*desc, nullptr, false, static_cast<cudaStream_t>(stream))
                             : pbk::launch_gdn_prefill_simt(*desc, static_cast<cudaStream_t>(stream));
   return launch_status(e);
 }
@@ -205,7 +206,32 @@ int pbk_gdn_prefill_ws(const pbk_gdn_desc* desc, void* workspace, size_t workspa
   if (workspace == nullptr || workspace_bytes < pbk::gdn_prefill_tc_workspace(*desc)) return PBK_ERR_INVALID;
   if (!aligned16(workspace)) return PBK_ERR_ALIGN;
   if ((st = check_current_device()) != PBK_OK) return st;
-  return launch_status(pbk::launch_gdn_prefill_tc(*desc, workspace, static_cast<cudaStream_t>(stream)));
+  return launch_status(pbk::launch_gdn_prefill_tc(*desc, workspace, false, static_cast<cudaStream_t>(stream)));
+}
+
+// The two halves of pbk_gdn_prefill_ws (tensor-core path only).
+static int check_solve_ws(const pbk_gdn_desc* desc, const void* workspace, size_t workspace_bytes) {
+  int st = validate_gdn(desc, true);
+  if (st != PBK_OK) return st;
+  if (!pbk::gdn_prefill_tc_supported(*desc)) return PBK_ERR_INVALID;
+  if (workspace == nullptr || workspace_bytes < pbk::gdn_prefill_tc_workspace(*desc)) return PBK_ERR_INVALID;
+  if (!aligned16(workspace)) return PBK_ERR_ALIGN;
+  return check_current_device();
+}
+
+int pbk_gdn_chunk_solve(const pbk_gdn_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  if (desc != nullptr && desc->batch == 0) return PBK_OK;
+  const int st = check_solve_ws(desc, workspace, workspace_bytes);
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_chunk_solve(*desc, workspace, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_gdn_prefill_solved(const pbk_gdn_desc* desc, const void* workspace, size_t workspace_bytes, void* stream) {
+  if (desc != nullptr && desc->batch == 0) return PBK_OK;
+  const int st = check_solve_ws(desc, workspace, workspace_bytes);
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_prefill_tc(*desc, const_cast<void*>(workspace), true,
+                                                  static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int32_t batch, int32_t nseg,

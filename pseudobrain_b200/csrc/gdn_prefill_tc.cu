@@ -1103,9 +1103,40 @@ size_t gdn_prefill_tc_workspace(const pbk_gdn_desc& d) {
   return (size_t)d.batch * ((d.seqlen + C - 1) / C) * d.hv * kSolveBytes;
 }
 
-// solve_ws: gdn_prefill_tc_workspace(d) bytes (16-byte aligned) for the offloaded chunk
-// solve, or NULL to solve each chunk inside the prefill kernel.
-cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, cudaStream_t st) {
+// The chunk solve of every (sequence, chunk, value head) of d into ws
+// (gdn_prefill_tc_workspace(d) bytes, 16-byte aligned).
+cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t st) {
+  SolveArgs sa;
+  sa.k = static_cast<const bf16*>(d.k.data);
+  sa.k_sb = d.k.stride_b;
+  sa.k_st = d.k.stride_t;
+  sa.k_sh = d.k.stride_h;
+  sa.g = d.g.data;
+  sa.g_sb = d.g.stride_b;
+  sa.g_st = d.g.stride_t;
+  sa.g_sh = d.g.stride_h;
+  sa.g_dtype = d.g.dtype;
+  sa.beta = d.beta.data;
+  sa.b_sb = d.beta.stride_b;
+  sa.b_st = d.beta.stride_t;
+  sa.b_sh = d.beta.stride_h;
+  sa.b_dtype = d.beta.dtype;
+  sa.seqlen = d.seqlen;
+  sa.hk = d.hk;
+  sa.hv = d.hv;
+  sa.ws = static_cast<uint8_t*>(ws);
+  cudaError_t e =
+      cudaFuncSetAttribute(gdn_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SolveSmem));
+  if (e != cudaSuccess) return e;
+  const dim3 sgrid((unsigned)((d.seqlen + C - 1) / C), (unsigned)d.hv, (unsigned)d.batch);
+  gdn_solve_kernel<<<sgrid, kSolveThreads, sizeof(SolveSmem), st>>>(sa);
+  return cudaGetLastError();
+}
+
+// solve_ws: gdn_prefill_tc_workspace(d) bytes (16-byte aligned) holding the chunk solve of d
+// (launch_gdn_chunk_solve) when `solved`, filled here first otherwise; NULL to solve each
+// chunk inside the prefill kernel.
+cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, bool solved, cudaStream_t st) {
   CUtensorMap mq, mk, mv, mo;
   if (!make_map(&mq, d.q, d.hk, d) || !make_map(&mk, d.k, d.hk, d) || !make_map(&mv, d.v, d.hv, d))
     return cudaErrorInvalidValue;
@@ -1146,31 +1177,9 @@ cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, cudaStr
   a.scale = d.scale;
   a.err = device_error_word();
   a.solve = static_cast<const uint8_t*>(solve_ws);
-  if (solve_ws != nullptr) {
-    SolveArgs sa;
-    sa.k = static_cast<const bf16*>(d.k.data);
-    sa.k_sb = d.k.stride_b;
-    sa.k_st = d.k.stride_t;
-    sa.k_sh = d.k.stride_h;
-    sa.g = d.g.data;
-    sa.g_sb = d.g.stride_b;
-    sa.g_st = d.g.stride_t;
-    sa.g_sh = d.g.stride_h;
-    sa.g_dtype = d.g.dtype;
-    sa.beta = d.beta.data;
-    sa.b_sb = d.beta.stride_b;
-    sa.b_st = d.beta.stride_t;
-    sa.b_sh = d.beta.stride_h;
-    sa.b_dtype = d.beta.dtype;
-    sa.seqlen = d.seqlen;
-    sa.hk = d.hk;
-    sa.hv = d.hv;
-    sa.ws = static_cast<uint8_t*>(solve_ws);
-    cudaError_t e = cudaFuncSetAttribute(gdn_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sizeof(SolveSmem));
+  if (solve_ws != nullptr && !solved) {
+    cudaError_t e = launch_gdn_chunk_solve(d, solve_ws, st);
     if (e != cudaSuccess) return e;
-    const dim3 sgrid((unsigned)((d.seqlen + C - 1) / C), (unsigned)d.hv, (unsigned)d.batch);
-    gdn_solve_kernel<<<sgrid, kSolveThreads, sizeof(SolveSmem), st>>>(sa);
   }
   const dim3 grid((unsigned)((int64_t)d.batch * d.hv));
   auto go = [&](auto kernel) {

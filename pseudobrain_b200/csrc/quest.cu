@@ -167,14 +167,17 @@ struct SelectSmem {
   int warp_tot[2][kTopkThreads / 32];
 };
 
+// With passes = 2 only the top 22 bits are resolved: `prefix` (low 10 bits zero) is then a
+// lower bound of the k-th largest key, tight to 2^-13 relative for finite scores.
 template <typename KeyOf>
 __device__ __forceinline__ void radix_select(KeyOf key_of, int n, uint32_t k, SelectSmem& ss, uint32_t& prefix_out,
-                                             uint32_t& kk_out) {
+                                             uint32_t& kk_out, int passes = 3) {
   const int tid = threadIdx.x, lane = tid & 31;
   uint32_t prefix = 0, mask = 0, kk = k;
   const int shifts[3] = {21, 10, 0}, widths[3] = {11, 11, 10};
 #pragma unroll
   for (int pass = 0; pass < 3; ++pass) {
+    if (pass >= passes) break;
     const int shift = shifts[pass];
     const uint32_t dmask = (1u << widths[pass]) - 1u;
     const int nb = 1 << widths[pass];
@@ -292,9 +295,10 @@ struct TopkSmem {
 };
 
 // One CTA per (group, key head) row of scores. With segment maxima (the max of every 32
-// consecutive pages), the k-th largest segment maximum tau bounds the k-th largest page
-// score from below (the top k segments hold k distinct pages scoring >= tau), so the top k
-// are among the pages scoring >= tau, all inside segments whose maximum is >= tau. Those
+// consecutive pages), the k-th largest segment maximum bounds the k-th largest page score
+// from below (the top k segments hold k distinct pages scoring at least that), and so does
+// any tau below it (here: its top 22 bits), so the top k are among the pages scoring >= tau,
+// all inside segments whose maximum is >= tau. Those
 // segments are listed in index order, only their pages are read (one warp-wide load per
 // segment, in registers), the pages scoring >= tau are placed in index order into shared
 // memory, and the exact selection runs there. When there are too few segments, too many
@@ -313,8 +317,10 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
     const float* sg = segmax + (int64_t)row * nseg;
     for (int i = threadIdx.x; i < nseg; i += kTopkThreads) ts.seg_key[i] = ordered_key(sg[i]);
     __syncthreads();
+    // tau: a lower bound of the k-th largest segment maximum (two digits: any bound at or
+    // below it keeps every top-k page among the candidates, the exact select comes later)
     uint32_t tau, unused;
-    radix_select([&](int i) { return ts.seg_key[i]; }, nseg, (uint32_t)k, ss, tau, unused);
+    radix_select([&](int i) { return ts.seg_key[i]; }, nseg, (uint32_t)k, ss, tau, unused, 2);
     // candidate segments (key >= tau) in index order
     {
       const int R = warp_range(nseg);
