@@ -52,6 +52,12 @@ def prefill_flops_per_token_head(c=64, d=128):
     return 5 * 2 * c * d + 3 * 2 * d * d + 2 * c * c / 3
 
 
+def solve_flops_per_token_head(c=64, d=128):
+    """The chunk solve kernel's share: K K^T and the triangular inverse; the recurrence
+    kernel does the other 4 C x C x d and 3 d x d products."""
+    return 2 * c * d + 2 * c * c / 3
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -157,7 +163,7 @@ class Timer:
 
 def measure_prefill(args, timed, dev, rank, world, pk):
     import torch
-    from pseudobrain_b200.gdn_prefill import gdn_prefill_
+    from pseudobrain_b200.gdn_prefill import chunk_solve, gdn_prefill_, prefill_solved
     from pseudobrain_b200.synthetic import gdn_inputs
     P = {**PREFILL[args.size], **PREFILL_HEADS}
     x = gdn_inputs(P["batch"], P["seqlen"], P["hk"], P["hv"], device=dev, seed=1 + 1000 * rank)
@@ -171,9 +177,29 @@ def measure_prefill(args, timed, dev, rank, world, pk):
     tokens = P["batch"] * P["seqlen"]
     per_step = t / args.steps
     flops = tokens * P["hv"] * prefill_flops_per_token_head(P["chunk"], P["dk"])
-    achieved = flops / per_step / 1e12
+    solve_flops = tokens * P["hv"] * solve_flops_per_token_head(P["chunk"], P["dk"])
     algo_bytes = (2 * tokens * P["hk"] * P["dk"] * 2 + tokens * P["hv"] * P["dv"] * 2 * 2 + tokens * P["hv"] * 6
                   + 2 * P["batch"] * P["hv"] * P["dk"] * P["dv"] * 4)
+    # the step's two kernels timed apart (CUDA events on the launching stream around each
+    # launch, summed over K steps): the roofline is the recurrence kernel's, the dominant one
+    ws = chunk_solve(x["q"], x["k"], x["v"], x["g"], x["beta"], state, x["scale"])
+    cur = torch.cuda.current_stream(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    for _ in range(args.warmup):
+        chunk_solve(x["q"], x["k"], x["v"], x["g"], x["beta"], state, x["scale"], ws)
+        prefill_solved(x["q"], x["k"], x["v"], x["g"], x["beta"], None, state, o, x["scale"], ws)
+    torch.cuda.synchronize()
+    for e in evs:
+        e[0].record(cur)
+        chunk_solve(x["q"], x["k"], x["v"], x["g"], x["beta"], state, x["scale"], ws)
+        e[1].record(cur)
+        prefill_solved(x["q"], x["k"], x["v"], x["g"], x["beta"], None, state, o, x["scale"], ws)
+        e[2].record(cur)
+    torch.cuda.synchronize()
+    t_solve = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps / 1e3
+    t_rec = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps / 1e3
+    del ws
+    achieved = (flops - solve_flops) / t_rec / 1e12
     # e2e through the public API: pinned host inputs in, bf16 outputs back, every step
     host = {n: x[n].cpu().pin_memory() for n in ("q", "k", "v", "g", "beta")}
     dev_in = {n: torch.empty_like(x[n]) for n in host}
@@ -190,10 +216,15 @@ def measure_prefill(args, timed, dev, rank, world, pk):
     return {
         "value": world * tokens * args.steps / t, "unit": "tok/s", "ms_per_step": per_step * 1e3,
         "tokens": tokens,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["tc_sustained"], "unit": "TFLOP/s",
-                     "frac": achieved / pk["tc_sustained"], "traffic": traffic("gdn_prefill_tc_kernel"),
-                     "peak_source": f"{pk['src']} bf16 sustained", "algorithmic_bytes": algo_bytes,
-                     "hbm_frac": algo_bytes / per_step / 1e9 / pk["hbm"]},
+        "roofline": {"bound": "tensor", "kernel": "gdn_prefill_tc_kernel", "achieved": achieved,
+                     "peak": pk["tc_sustained"], "unit": "TFLOP/s", "frac": achieved / pk["tc_sustained"],
+                     "traffic": traffic("gdn_prefill_tc_kernel"), "peak_source": f"{pk['src']} bf16 sustained",
+                     "algorithmic_flops": flops - solve_flops, "ms": t_rec * 1e3},
+        "kernels": {"gdn_solve_kernel": {"ms": t_solve * 1e3, "tflops": solve_flops / t_solve / 1e12,
+                                         "traffic": traffic("gdn_solve_kernel")},
+                    "gdn_prefill_tc_kernel": {"ms": t_rec * 1e3, "tflops": (flops - solve_flops) / t_rec / 1e12}},
+        "step": {"tflops": flops / per_step / 1e12, "frac": flops / per_step / 1e12 / pk["tc_sustained"],
+                 "algorithmic_bytes": algo_bytes, "hbm_frac": algo_bytes / per_step / 1e9 / pk["hbm"]},
         "e2e": {"value": world * tokens * e2e_steps / t_e2e, "unit": "tok/s",
                 "h2d_bytes_per_step": sum(tt.numel() * tt.element_size() for tt in host.values()),
                 "d2h_bytes_per_step": host_o.numel() * host_o.element_size()},

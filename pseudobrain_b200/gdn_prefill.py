@@ -102,19 +102,23 @@ def auto_segments(batch: int, hv: int, seqlen: int, sms: int | None = None) -> i
     return max(1, min(want, chunks // 16))
 
 
-def _chunk_solve(q, k, v, g, beta, state, scale) -> torch.Tensor:
-    """pbk_gdn_chunk_solve of the (bf16) inputs into a new workspace."""
+def chunk_solve(q, k, v, g, beta, state, scale, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """pbk_gdn_chunk_solve of the (bf16) inputs into ws (a new workspace when None); `state`
+    only shapes the call."""
     dev = q.device
     d = _desc(q, k, v, g, beta, None, None, state, scale, None, 0)
     n = LIB.pbk_gdn_prefill_workspace(d)
     if n == 0:
         raise ValueError("the chunk solve runs on the bf16 tensor-core path only")
-    ws = torch.empty(n, dtype=torch.uint8, device=dev)
+    if ws is None:
+        ws = torch.empty(n, dtype=torch.uint8, device=dev)
+    elif ws.numel() < n:
+        raise ValueError("workspace too small")
     check(LIB.pbk_gdn_chunk_solve(d, ws.data_ptr(), n, _stream(dev)), "pbk_gdn_chunk_solve")
     return ws
 
 
-def _prefill_solved(q, k, v, g, beta, h0, state, o, scale, ws: torch.Tensor, offset: int) -> None:
+def prefill_solved(q, k, v, g, beta, h0, state, o, scale, ws: torch.Tensor, offset: int = 0) -> None:
     """pbk_gdn_prefill_solved from the solve slots starting `offset` bytes into ws."""
     dev = q.device
     d = _desc(q, k, v, g, beta, o, h0, state, scale, None, 0)
@@ -159,15 +163,15 @@ def gdn_prefill_segmented(q, k, v, g, beta, scale, h0=None, segments: int | None
 
         # one chunk solve of the whole sequence serves all three runs: slot (segment p,
         # chunk c) of the segment batch is slot (0, p * seg_chunks + c) of the sequence
-        ws = _chunk_solve(q[i:i + 1], k[i:i + 1], v[i:i + 1], g[i:i + 1], beta[i:i + 1], final[i:i + 1],
+        ws = chunk_solve(q[i:i + 1], k[i:i + 1], v[i:i + 1], g[i:i + 1], beta[i:i + 1], final[i:i + 1],
                           float(scale))
         slot = ws.numel() // (chunks * hv)
         qs, ks, vs, gs, bs = (seg(x) for x in (q, k, v, g, beta))
         bst = torch.empty(full, hv, dk, dv, dtype=torch.float32, device=q.device)
         mst = torch.empty_like(bst)
         eye = torch.eye(dk, dtype=torch.float32, device=q.device).expand(full, hv, dk, dv).contiguous()
-        _prefill_solved(qs, ks, vs, gs, bs, None, bst, None, float(scale), ws, 0)
-        _prefill_solved(qs, ks, vs, gs, bs, eye, mst, None, float(scale), ws, 0)
+        prefill_solved(qs, ks, vs, gs, bs, None, bst, None, float(scale), ws, 0)
+        prefill_solved(qs, ks, vs, gs, bs, eye, mst, None, float(scale), ws, 0)
         starts = torch.empty(1, nseg, hv, dk, dv, dtype=torch.float32, device=q.device)
         segment_scan(bst.unsqueeze(0), mst.unsqueeze(0), None if h0 is None else h0[i:i + 1], starts)
         # the last (shorter) segment runs beside the full ones on a side stream, so the
@@ -177,11 +181,11 @@ def gdn_prefill_segmented(q, k, v, g, beta, scale, h0=None, segments: int | None
         side = torch.cuda.Stream(q.device)
         side.wait_stream(cur)
         with torch.cuda.stream(side):
-            _prefill_solved(q[i:i + 1, cut:], k[i:i + 1, cut:], v[i:i + 1, cut:], g[i:i + 1, cut:],
+            prefill_solved(q[i:i + 1, cut:], k[i:i + 1, cut:], v[i:i + 1, cut:], g[i:i + 1, cut:],
                             beta[i:i + 1, cut:], starts[:, full], final[i:i + 1], o[i:i + 1, cut:], float(scale),
                             ws, (cut // 64) * hv * slot)
         starts.record_stream(side)
         ws.record_stream(side)
-        _prefill_solved(qs, ks, vs, gs, bs, starts[0, :full], eye, seg(o), float(scale), ws, 0)
+        prefill_solved(qs, ks, vs, gs, bs, starts[0, :full], eye, seg(o), float(scale), ws, 0)
         cur.wait_stream(side)
     return o, final
