@@ -85,6 +85,38 @@ typedef struct pbk_gdn_desc {
   int32_t pad2_;
 } pbk_gdn_desc;
 
+/* Layer pieces around the recurrence (vLLM's adapter path: causal_conv1d, fused gating,
+ * q/k L2 norm in the producer, gated RMSNorm on the output). Channel views use stride_h as
+ * the channel stride; [B, T, H, 128] views have a contiguous last dim. */
+typedef struct pbk_conv_desc {
+  int32_t batch, seqlen, hk, hv;
+  int32_t width;    /* convolution taps, 1..8 (4 in Qwen3-Next); ignored when weight is NULL */
+  int32_t l2mode;   /* q/k normalisation: 0 none, 1 'max' (x / max(|x|, eps)), 2 'hf' (x rsqrt(|x|^2 + eps)) */
+  float eps;        /* the normalisation eps (1e-6 in the reference) */
+  int32_t pad_;
+  pbk_view x;        /* [B, T, (2 hk + hv) 128] inputs q | k | v channels */
+  pbk_view tail;     /* [B, width - 1, channels] the inputs before x; data NULL: zeros */
+  pbk_view new_tail; /* [B, width - 1, channels] written with the last width - 1 inputs; NULL: skipped */
+  const float* weight; /* [channels, width] fp32 contiguous (weight[:, width-1] multiplies x_t); NULL: SiLU only */
+  pbk_view q, k, v;  /* [B, T, hk | hk | hv, 128] outputs */
+} pbk_conv_desc;
+
+typedef struct pbk_gating_desc {
+  int32_t batch, seqlen, hv, pad_;
+  pbk_view decay;      /* [B, T, 2 hv]: a | b */
+  const float* a_log;  /* [hv] */
+  const float* dt_bias; /* [hv] */
+  pbk_view g, beta;    /* [B, T, hv] outputs */
+} pbk_gating_desc;
+
+typedef struct pbk_out_norm_desc {
+  int32_t batch, seqlen, hv, weight_dtype;
+  float eps;          /* 1e-5 in the reference */
+  int32_t pad_;
+  pbk_view o, gate, out; /* [B, T, hv, 128] each */
+  const void* weight;    /* [128] */
+} pbk_out_norm_desc;
+
 PBK_API int pbk_abi_version(void);
 PBK_API const char* pbk_status_string(int status);
 /* The CUDA error message behind the calling thread's last PBK_ERR_LAUNCH ("no error"
@@ -133,6 +165,30 @@ PBK_API int pbk_gdn_prefill_ws(const pbk_gdn_desc* desc, void* workspace, size_t
  * also serves runs over segments of it (whole chunks, viewed as a batch of segments; a
  * later segment starts at its first chunk's slot): the sequence-split prefill solves once
  * and runs the recurrence three times. */
+/* Packed varlen prefill (vLLM's chunked-prefill batch; tensor-core path, bf16 q/k/v): desc
+ * describes [1, T, H, 128] tensors (batch 1, seqlen = T total rows). Sequence s is rows
+ * cu_seqlens[s] .. cu_seqlens[s+1] of them (cu_seqlens: num_seqs + 1 ascending int32 on the
+ * device, 16-byte aligned), starts from h0 slot state_indices[s] (or s when state_indices is
+ * NULL; a negative index skips the sequence) and ends in that slot of `state`; its outputs go
+ * to its rows of o. Each sequence is the reference's delta_rule_chunked on its own
+ * (gated_deltanet.py:110-165, chunks counted from the sequence's first row). Workspace:
+ * pbk_gdn_prefill_varlen_workspace(desc, num_seqs) bytes, 16-byte aligned, private to the
+ * call until it completes on `stream`. */
+PBK_API size_t pbk_gdn_prefill_varlen_workspace(const pbk_gdn_desc* desc, int32_t num_seqs);
+PBK_API int pbk_gdn_prefill_varlen(const pbk_gdn_desc* desc, const int32_t* cu_seqlens, int32_t num_seqs,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Causal depthwise convolution + SiLU over the q | k | v channels with a carried tail
+ * (short_convolution, gated_deltanet.py:314-338), q and k L2-normalised per 128-channel head
+ * (l2_normalize, :59-70); fp32 arithmetic, outputs in their views' dtypes. new_tail must not
+ * overlap tail. */
+PBK_API int pbk_gdn_conv_norm(const pbk_conv_desc* desc, void* stream);
+/* g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (gated_deltanet.py:427-429). */
+PBK_API int pbk_gdn_gating(const pbk_gating_desc* desc, void* stream);
+/* out = o rsqrt(mean(o^2) + eps) weight SiLU(gate) per 128-wide head row
+ * (gated_deltanet.py:439-440). */
+PBK_API int pbk_gdn_out_norm(const pbk_out_norm_desc* desc, void* stream);
+
 PBK_API int pbk_gdn_chunk_solve(const pbk_gdn_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 PBK_API int pbk_gdn_prefill_solved(const pbk_gdn_desc* desc, const void* workspace, size_t workspace_bytes,
                                    void* stream);

@@ -25,6 +25,25 @@ class PbkView(ctypes.Structure):
                 ("stride_h", ctypes.c_int64), ("dtype", ctypes.c_int32), ("pad_", ctypes.c_int32)]
 
 
+class PbkConvDesc(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hk", ctypes.c_int32), ("hv", ctypes.c_int32),
+                ("width", ctypes.c_int32), ("l2mode", ctypes.c_int32), ("eps", ctypes.c_float), ("pad_", ctypes.c_int32),
+                ("x", PbkView), ("tail", PbkView), ("new_tail", PbkView), ("weight", ctypes.c_void_p),
+                ("q", PbkView), ("k", PbkView), ("v", PbkView)]
+
+
+class PbkGatingDesc(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hv", ctypes.c_int32), ("pad_", ctypes.c_int32),
+                ("decay", PbkView), ("a_log", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p),
+                ("g", PbkView), ("beta", PbkView)]
+
+
+class PbkOutNormDesc(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hv", ctypes.c_int32),
+                ("weight_dtype", ctypes.c_int32), ("eps", ctypes.c_float), ("pad_", ctypes.c_int32),
+                ("o", PbkView), ("gate", PbkView), ("out", PbkView), ("weight", ctypes.c_void_p)]
+
+
 class PbkGdnDesc(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hk", ctypes.c_int32),
                 ("hv", ctypes.c_int32), ("dk", ctypes.c_int32), ("dv", ctypes.c_int32),
@@ -74,6 +93,11 @@ SIGNATURES = {
     "pbk_gdn_prefill_workspace": (ctypes.c_size_t, [ctypes.POINTER(PbkGdnDesc)]),
     "pbk_gdn_prefill_ws": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),
     "pbk_gdn_chunk_solve": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),
+    "pbk_gdn_conv_norm": (ctypes.c_int, [ctypes.POINTER(PbkConvDesc), _VP]),
+    "pbk_gdn_gating": (ctypes.c_int, [ctypes.POINTER(PbkGatingDesc), _VP]),
+    "pbk_gdn_out_norm": (ctypes.c_int, [ctypes.POINTER(PbkOutNormDesc), _VP]),
+    "pbk_gdn_prefill_varlen_workspace": (ctypes.c_size_t, [ctypes.POINTER(PbkGdnDesc), _I32]),
+    "pbk_gdn_prefill_varlen": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, _I32, _VP, ctypes.c_size_t, _VP]),
     "pbk_gdn_prefill_solved": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),
     "pbk_gdn_segment_scan": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I32, _I32, _I32, _VP]),
     "pbk_quest_select_workspace": (ctypes.c_size_t, [_QD]),

@@ -12,6 +12,13 @@ cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st);
 bool gdn_prefill_tc_supported(const pbk_gdn_desc& d);
 size_t gdn_prefill_tc_workspace(const pbk_gdn_desc& d);
 cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t st);
+size_t gdn_prefill_varlen_workspace(const pbk_gdn_desc& d, int num_seqs);
+cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st);
+cudaError_t launch_gdn_gating(const pbk_gating_desc& d, cudaStream_t st);
+cudaError_t launch_gdn_out_norm(const pbk_out_norm_desc& d, cudaStream_t st);
+bool gdn_conv_width_ok(int width);
+cudaError_t launch_gdn_prefill_varlen(const pbk_gdn_desc& d, const int32_t* cu_seqlens, int num_seqs, void* ws,
+                                      cudaStream_t st);
 cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, bool solved, cudaStream_t st);
 cudaError_t launch_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int batch,
                                     int nseg, int hv, cudaStream_t st);
@@ -224,6 +231,71 @@ int pbk_gdn_chunk_solve(const pbk_gdn_desc* desc, void* workspace, size_t worksp
   const int st = check_solve_ws(desc, workspace, workspace_bytes);
   if (st != PBK_OK) return st;
   return launch_status(pbk::launch_gdn_chunk_solve(*desc, workspace, static_cast<cudaStream_t>(stream)));
+}
+
+// ---- layer pieces around the recurrence
+static bool view_ok(const pbk_view& v) { return v.data != nullptr && dtype_ok(v.dtype); }
+
+int pbk_gdn_conv_norm(const pbk_conv_desc* d, void* stream) {
+  if (d == nullptr || d->batch < 0 || d->seqlen < 0 || d->hk < 1 || d->hv < 1) return PBK_ERR_INVALID;
+  if (d->weight != nullptr && !pbk::gdn_conv_width_ok(d->width)) return PBK_ERR_SHAPE;
+  if (d->l2mode < 0 || d->l2mode > 2 || !(d->eps >= 0.f)) return PBK_ERR_INVALID;
+  if (d->batch == 0 || d->seqlen == 0) return PBK_OK;
+  if (!view_ok(d->x) || !view_ok(d->q) || !view_ok(d->k) || !view_ok(d->v)) return PBK_ERR_INVALID;
+  if (d->tail.data != nullptr && !dtype_ok(d->tail.dtype)) return PBK_ERR_DTYPE;
+  if (d->new_tail.data != nullptr && (!dtype_ok(d->new_tail.dtype) || d->new_tail.data == d->tail.data))
+    return PBK_ERR_INVALID;
+  if (d->batch > 65535 || 2 * d->hk + d->hv > 65535) return PBK_ERR_SHAPE;  // grid y, z
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_conv_norm(*d, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_gdn_gating(const pbk_gating_desc* d, void* stream) {
+  if (d == nullptr || d->batch < 0 || d->seqlen < 0 || d->hv < 1) return PBK_ERR_INVALID;
+  if (d->batch == 0 || d->seqlen == 0) return PBK_OK;
+  if (!view_ok(d->decay) || !view_ok(d->g) || !view_ok(d->beta) || !d->a_log || !d->dt_bias) return PBK_ERR_INVALID;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_gating(*d, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_gdn_out_norm(const pbk_out_norm_desc* d, void* stream) {
+  if (d == nullptr || d->batch < 0 || d->seqlen < 0 || d->hv < 1 || !(d->eps >= 0.f)) return PBK_ERR_INVALID;
+  if (d->batch == 0 || d->seqlen == 0) return PBK_OK;
+  if (!view_ok(d->o) || !view_ok(d->gate) || !view_ok(d->out) || !d->weight || !dtype_ok(d->weight_dtype))
+    return PBK_ERR_INVALID;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_out_norm(*d, static_cast<cudaStream_t>(stream)));
+}
+
+// Packed varlen prefill (tensor-core path): desc describes [1, T, H, 128] tensors.
+static int check_varlen(const pbk_gdn_desc* desc, const int32_t* cu_seqlens, int32_t num_seqs) {
+  const int st = validate_gdn(desc, true);
+  if (st != PBK_OK) return st;
+  if (desc->batch != 1 || num_seqs < 0 || (num_seqs > 0 && cu_seqlens == nullptr)) return PBK_ERR_INVALID;
+  if ((int64_t)num_seqs * desc->hv > INT32_MAX) return PBK_ERR_SHAPE;
+  if (!pbk::gdn_prefill_tc_supported(*desc)) return PBK_ERR_INVALID;
+  return PBK_OK;
+}
+
+size_t pbk_gdn_prefill_varlen_workspace(const pbk_gdn_desc* desc, int32_t num_seqs) {
+  if (check_varlen(desc, nullptr, 0) != PBK_OK || num_seqs < 0) return 0;
+  return round_up(pbk::gdn_prefill_varlen_workspace(*desc, num_seqs));
+}
+
+int pbk_gdn_prefill_varlen(const pbk_gdn_desc* desc, const int32_t* cu_seqlens, int32_t num_seqs, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  int st = check_varlen(desc, cu_seqlens, num_seqs);
+  if (st != PBK_OK) return st;
+  if (num_seqs == 0 || desc->seqlen == 0) return PBK_OK;
+  if (workspace == nullptr || workspace_bytes < pbk::gdn_prefill_varlen_workspace(*desc, num_seqs))
+    return PBK_ERR_INVALID;
+  if (!aligned16(workspace) || !aligned16(cu_seqlens)) return PBK_ERR_ALIGN;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_prefill_varlen(*desc, cu_seqlens, num_seqs, workspace,
+                                                      static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_gdn_prefill_solved(const pbk_gdn_desc* desc, const void* workspace, size_t workspace_bytes, void* stream) {

@@ -1,0 +1,156 @@
+// The Gated DeltaNet layer's elementwise stages around the recurrence, as vLLM's adapter
+// runs them (causal_conv1d, fused gating, in-kernel q/k L2 norm, gated RMSNorm):
+//   conv + norm: y = SiLU(causal depthwise conv of x over time, carried tail) per channel
+//     (short_convolution, pseudobrain/gated_deltanet.py:314-338), split into q | k | v heads
+//     of 128 channels, q and k L2-normalised per head (l2_normalize, :59-70, 'max' or 'hf'),
+//     and the new tail (the last width-1 inputs);
+//   gating: g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (:427-429);
+//   output norm: o * rsqrt(mean(o^2) + eps) * weight * SiLU(gate) (:439-440).
+// All arithmetic in fp32. Memory-bound: each reads and writes its tensors once.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace pbk {
+namespace {
+
+constexpr int kHd = 128;    // channels per head
+constexpr int kTile = 32;   // tokens per CTA of the conv + norm kernel
+constexpr int kMaxWidth = 8;
+
+__device__ __forceinline__ float silu(float y) { return y / (1.f + expf(-y)); }
+// Store into an output view (pbk_view carries its pointer as const void*).
+__device__ __forceinline__ void store_any(const void* p, int64_t i, int dtype, float x) {
+  if (dtype == PBK_BF16) const_cast<__nv_bfloat16*>(reinterpret_cast<const __nv_bfloat16*>(p))[i] = __float2bfloat16_rn(x);
+  else const_cast<float*>(reinterpret_cast<const float*>(p))[i] = x;
+}
+
+// CTA = (token tile, head of the q | k | v channel layout, sequence); thread = channel.
+__global__ void __launch_bounds__(kHd) gdn_conv_norm_kernel(const pbk_conv_desc d) {
+  __shared__ float ys[kTile][kHd + 1];
+  const int tile = blockIdx.x, hd = blockIdx.y, b = blockIdx.z, c = threadIdx.x;
+  const int ch = hd * kHd + c, K = d.weight != nullptr ? d.width : 1, t0 = tile * kTile;
+  const int nt = min(kTile, d.seqlen - t0);
+  auto x_at = [&](int t) -> float {  // input of step t; t < 0 reads the carried tail
+    if (t >= 0) return load_any(d.x.data, b * d.x.stride_b + (int64_t)t * d.x.stride_t + ch * d.x.stride_h, d.x.dtype);
+    const int j = K - 1 + t;  // tail row
+    if (j < 0 || d.tail.data == nullptr) return 0.f;
+    return load_any(d.tail.data, b * d.tail.stride_b + (int64_t)j * d.tail.stride_t + ch * d.tail.stride_h, d.tail.dtype);
+  };
+  // right-aligned taps: win[i] = x_{t - (kMaxWidth - 1 - i)} for the step t being computed,
+  // w[i] its weight (weight[ch][K - kMaxWidth + i]; zero left of the K taps)
+  float w[kMaxWidth], win[kMaxWidth];
+#pragma unroll
+  for (int i = 0; i < kMaxWidth; ++i) {
+    const int j = i - (kMaxWidth - K);
+    w[i] = (d.weight != nullptr && j >= 0) ? d.weight[(int64_t)ch * K + j] : 0.f;
+    win[i] = (i < kMaxWidth - 1 && j >= 0) ? x_at(t0 - (kMaxWidth - 1 - i)) : 0.f;
+  }
+  for (int i = 0; i < nt; ++i) {
+    win[kMaxWidth - 1] = x_at(t0 + i);
+    float y = 0.f;
+#pragma unroll
+    for (int u = 0; u < kMaxWidth; ++u) y = fmaf(w[u], win[u], y);
+    ys[i][c] = silu(d.weight != nullptr ? y : win[kMaxWidth - 1]);
+#pragma unroll
+    for (int u = 0; u < kMaxWidth - 1; ++u) win[u] = win[u + 1];
+  }
+  // the new tail: inputs T-K+1 .. T-1, written by the tile holding step T-1
+  if (d.new_tail.data != nullptr && t0 + nt == d.seqlen) {
+    for (int j = 0; j < K - 1; ++j)
+      store_any(d.new_tail.data, b * d.new_tail.stride_b + (int64_t)j * d.new_tail.stride_t + ch * d.new_tail.stride_h,
+                d.new_tail.dtype, x_at(d.seqlen - K + 1 + j));
+  }
+  __syncthreads();
+  // rows: q heads 0 .. hk-1, k heads hk .. 2hk-1 (normalised), v heads after them
+  const bool is_q = hd < d.hk, is_k = !is_q && hd < 2 * d.hk;
+  const pbk_view& out = is_q ? d.q : (is_k ? d.k : d.v);
+  const int oh = is_q ? hd : (is_k ? hd - d.hk : hd - 2 * d.hk);
+  const int warp = c >> 5, lane = c & 31;
+  for (int i = warp; i < nt; i += kHd / 32) {
+    float v[4], ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      v[u] = ys[i][lane + 32 * u];
+      ss = fmaf(v[u], v[u], ss);
+    }
+    float scale = 1.f;
+    if ((is_q || is_k) && d.l2mode != 0) {
+      ss = warp_sum(ss);
+      // 'max': x / max(||x||, eps) (F.normalize); 'hf': x * rsqrt(sum x^2 + eps)
+      scale = d.l2mode == 1 ? 1.f / fmaxf(sqrtf(ss), d.eps) : rsqrtf(ss + d.eps);
+    }
+    const int64_t base = b * out.stride_b + (int64_t)(t0 + i) * out.stride_t + (int64_t)oh * out.stride_h;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) store_any(out.data, base + lane + 32 * u, out.dtype, v[u] * scale);
+  }
+}
+
+__global__ void gdn_gating_kernel(const pbk_gating_desc d) {
+  const int64_t n = (int64_t)d.batch * d.seqlen * d.hv;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int h = (int)(e % d.hv), t = (int)((e / d.hv) % d.seqlen), b = (int)(e / ((int64_t)d.hv * d.seqlen));
+    const int64_t ab = b * d.decay.stride_b + (int64_t)t * d.decay.stride_t;
+    const float a = load_any(d.decay.data, ab + (int64_t)h * d.decay.stride_h, d.decay.dtype);
+    const float bb = load_any(d.decay.data, ab + (int64_t)(d.hv + h) * d.decay.stride_h, d.decay.dtype);
+    const float x = a + d.dt_bias[h];
+    const float sp = x > 20.f ? x : log1pf(expf(x));  // softplus, threshold 20 as F.softplus
+    const float gv = -expf(d.a_log[h]) * sp;
+    const float be = 1.f / (1.f + expf(-bb));
+    store_any(d.g.data, b * d.g.stride_b + (int64_t)t * d.g.stride_t + (int64_t)h * d.g.stride_h, d.g.dtype, gv);
+    store_any(d.beta.data, b * d.beta.stride_b + (int64_t)t * d.beta.stride_t + (int64_t)h * d.beta.stride_h,
+              d.beta.dtype, be);
+  }
+}
+
+// One warp per (sequence, token, value head) row of 128.
+__global__ void __launch_bounds__(256) gdn_out_norm_kernel(const pbk_out_norm_desc d) {
+  const int64_t rows = (int64_t)d.batch * d.seqlen * d.hv;
+  const int64_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int h = (int)(r % d.hv), t = (int)((r / d.hv) % d.seqlen), b = (int)(r / ((int64_t)d.hv * d.seqlen));
+  const int64_t ob = b * d.o.stride_b + (int64_t)t * d.o.stride_t + (int64_t)h * d.o.stride_h;
+  const int64_t gb = b * d.gate.stride_b + (int64_t)t * d.gate.stride_t + (int64_t)h * d.gate.stride_h;
+  const int64_t yb = b * d.out.stride_b + (int64_t)t * d.out.stride_t + (int64_t)h * d.out.stride_h;
+  float v[4], ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    v[u] = load_any(d.o.data, ob + lane + 32 * u, d.o.dtype);
+    ss = fmaf(v[u], v[u], ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / kHd + d.eps);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int i = lane + 32 * u;
+    const float gt = load_any(d.gate.data, gb + i, d.gate.dtype);
+    const float wt = load_any(d.weight, i, d.weight_dtype);
+    store_any(d.out.data, yb + i, d.out.dtype, v[u] * inv * wt * silu(gt));
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st) {
+  const dim3 grid((unsigned)((d.seqlen + kTile - 1) / kTile), (unsigned)(2 * d.hk + d.hv), (unsigned)d.batch);
+  gdn_conv_norm_kernel<<<grid, kHd, 0, st>>>(d);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_gating(const pbk_gating_desc& d, cudaStream_t st) {
+  const int64_t n = (int64_t)d.batch * d.seqlen * d.hv;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  gdn_gating_kernel<<<blocks, 256, 0, st>>>(d);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_out_norm(const pbk_out_norm_desc& d, cudaStream_t st) {
+  const int64_t rows = (int64_t)d.batch * d.seqlen * d.hv;
+  gdn_out_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(d);
+  return cudaGetLastError();
+}
+
+bool gdn_conv_width_ok(int width) { return width >= 1 && width <= kMaxWidth; }
+
+}  // namespace pbk

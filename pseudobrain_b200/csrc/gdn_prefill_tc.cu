@@ -92,6 +92,11 @@ struct PrefillArgs {
   float scale;
   int* err;
   const uint8_t* solve;  // TB | TBG of every (sequence, chunk, value head), or NULL: solved here
+  // varlen (packed [1, T, H, 128]): sequence s = rows cu_seqlens[s] .. cu_seqlens[s+1],
+  // its chunks at solve slots chunk_off[s] ..; NULL: dense [B, T, H, 128]
+  const int32_t* cu_seqlens;
+  const int32_t* chunk_off;
+  int solve_slots;  // chunk slots of the varlen workspace (bound on cbase + nchunks)
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -324,7 +329,31 @@ struct SolveArgs {
   int b_dtype;
   int seqlen, hk, hv;
   uint8_t* ws;
+  // varlen (packed [1, T, H, 128] inputs): sequence s spans rows cu_seqlens[s] ..
+  // cu_seqlens[s+1], its chunks take workspace slots chunk_off[s] .. chunk_off[s+1]; NULL: dense
+  const int32_t* cu_seqlens;
+  const int32_t* chunk_off;
+  int num_seqs;
 };
+
+// Rows [t0, t0 + len) of packed sequence s, clamped into [0, T] (offsets out of order or out of
+// range read nothing outside the tensors; they are caller errors).
+__device__ __forceinline__ void seq_rows(const int32_t* cu_seqlens, int s, int T, int& t0, int& len) {
+  t0 = min(max(cu_seqlens[s], 0), T);
+  len = min(max(cu_seqlens[s + 1], t0), T) - t0;
+}
+
+// Sequence of global chunk c (chunk_off ascending, num_seqs + 1 entries): the last s with
+// chunk_off[s] <= c.
+__device__ __forceinline__ int seq_of_chunk(const int32_t* chunk_off, int num_seqs, int c) {
+  int lo = 0, hi = num_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (chunk_off[mid] <= c) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -340,18 +369,68 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// chunk_off[s] = sum over s' < s of ceil(len_s' / C) for s = 0 .. num_seqs (one 1024-thread
+// block: each thread sums a run of sequences, then a block scan).
+__global__ void __launch_bounds__(1024) gdn_chunk_offsets_kernel(const int32_t* cu_seqlens, int num_seqs, int T,
+                                                                  int32_t* chunk_off) {
+  __shared__ int warp_tot[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (num_seqs + 1023) / 1024, s0 = min(num_seqs, tid * per), s1 = min(num_seqs, s0 + per);
+  int own = 0;
+  int t0, len;
+  for (int s = s0; s < s1; ++s) {
+    seq_rows(cu_seqlens, s, T, t0, len);
+    own += (len + C - 1) / C;
+  }
+  int x = own;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_tot[lane] = w;
+  }
+  __syncthreads();
+  int run = (warp > 0 ? warp_tot[warp - 1] : 0) + x - own;  // chunks before sequence s0
+  for (int s = s0; s < s1; ++s) {
+    chunk_off[s] = run;
+    seq_rows(cu_seqlens, s, T, t0, len);
+    run += (len + C - 1) / C;
+  }
+  if (tid == 1023) chunk_off[num_seqs] = warp_tot[31];
+}
+
 __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArgs p) {
   extern __shared__ __align__(16) uint8_t solve_raw[];
   SolveSmem& sm = *reinterpret_cast<SolveSmem*>(solve_raw);
-  const int m = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int h = blockIdx.y, b = blockIdx.z;
+  // this CTA's chunk m of a sequence at rows t0 .. t0 + len, workspace slot `cslot`
+  int m = blockIdx.x, t0 = 0, len = p.seqlen;
+  int64_t cslot = (int64_t)b * gridDim.x + m;
+  if (p.cu_seqlens != nullptr) {
+    if (m >= p.chunk_off[p.num_seqs]) return;  // the grid covers an upper bound of the chunks
+    const int s = seq_of_chunk(p.chunk_off, p.num_seqs, m);
+    seq_rows(p.cu_seqlens, s, p.seqlen, t0, len);
+    cslot = m;
+    m -= p.chunk_off[s];
+  }
   const int hkh = h / (p.hv / p.hk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // K rows (zero past the sequence end, the reference's padding)
   for (int c = tid; c < C * 16; c += kSolveThreads) {
     const int r = c >> 4, ch = c & 15, t = m * C + r;
     const uint32_t dst = tc::smem_u32(sm.k) + r * 256 + ((ch ^ (r & 7)) << 4);
-    if (t < p.seqlen) {
-      const bf16* src = p.k + b * p.k_sb + (int64_t)t * p.k_st + hkh * p.k_sh + 8 * ch;
+    if (t < len) {
+      const bf16* src = p.k + b * p.k_sb + (int64_t)(t0 + t) * p.k_st + hkh * p.k_sh + 8 * ch;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
     } else {
       asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0u) : "memory");
@@ -362,14 +441,15 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
   if (warp == 0) {
     constexpr float kLog2e = 1.4426950408889634f;
     const int t = m * C + 2 * lane;
+    const int64_t tg = t0 + t;  // row in the (packed) tensor
     float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
-    if (t < p.seqlen) {
-      g0 = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
-      b0 = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
+    if (t < len) {
+      g0 = load_any(p.g, b * p.g_sb + tg * p.g_st + h * p.g_sh, p.g_dtype);
+      b0 = load_any(p.beta, b * p.b_sb + tg * p.b_st + h * p.b_sh, p.b_dtype);
     }
-    if (t + 1 < p.seqlen) {
-      g1 = load_any(p.g, b * p.g_sb + (int64_t)(t + 1) * p.g_st + h * p.g_sh, p.g_dtype);
-      b1 = load_any(p.beta, b * p.b_sb + (int64_t)(t + 1) * p.b_st + h * p.b_sh, p.b_dtype);
+    if (t + 1 < len) {
+      g1 = load_any(p.g, b * p.g_sb + (tg + 1) * p.g_st + h * p.g_sh, p.g_dtype);
+      b1 = load_any(p.beta, b * p.b_sb + (tg + 1) * p.b_st + h * p.b_sh, p.b_dtype);
     }
     const float pair = g0 + g1;
     float incl = pair;
@@ -388,8 +468,7 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
     sm.beta[2 * lane + 1] = b1;
     // the chunk's scalar record for the recurrence kernel (after TB | TBG): e = exp2(c_last -
     // c), and the factored decay about c_ref = c_31 while the log2 span stays below 60
-    ChunkScalars* rec = reinterpret_cast<ChunkScalars*>(
-        p.ws + (((int64_t)b * gridDim.x + m) * p.hv + h) * kSolveBytes + 2 * 8192);
+    ChunkScalars* rec = reinterpret_cast<ChunkScalars*>(p.ws + (cslot * p.hv + h) * kSolveBytes + 2 * 8192);
     const float clast = __shfl_sync(0xffffffffu, c1, 31), ref = __shfl_sync(0xffffffffu, c1, 15);
     float hi = fmaxf(c0, c1), lo = fminf(c0, c1);
 #pragma unroll
@@ -520,7 +599,7 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
   // tiles (zero above the diagonal blocks) into the workspace; thread: row t, columns
   // 32 hh .. 32 hh + 31
   {
-    uint8_t* dst = p.ws + ((((int64_t)b * gridDim.x + m) * p.hv + h) * kSolveBytes);
+    uint8_t* dst = p.ws + (cslot * p.hv + h) * kSolveBytes;
     const int t = tid >> 1, hh = tid & 1, rb = t >> 4, rl = t & 15;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
@@ -571,14 +650,32 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int b = blockIdx.x / p.hv, h = blockIdx.x % p.hv;
+  // sequence `seq` of this CTA: rows t0 .. t0 + len of tensor batch b (b = 0 when packed),
+  // its chunks at solve slots cbase ..
+  const int seq = blockIdx.x / p.hv, h = blockIdx.x % p.hv;
+  const bool varlen = p.cu_seqlens != nullptr;
+  const int b = varlen ? 0 : seq;
+  int t0 = 0, len = p.seqlen;
+  if (varlen) seq_rows(p.cu_seqlens, seq, p.seqlen, t0, len);
   const int hk = h / (p.hv / p.hk);
-  int64_t slot = b;
+  int64_t slot = seq;
   if (p.state_indices != nullptr) {
-    slot = p.state_indices[b];
+    slot = p.state_indices[seq];
     if (slot < 0) return;  // padding slot (uniform for the CTA)
   }
-  const int nchunks = (p.seqlen + C - 1) / C;
+  const int nchunks = (len + C - 1) / C;
+  const int64_t cbase = varlen ? (p.chunk_off != nullptr ? p.chunk_off[seq] : 0) : (int64_t)b * nchunks;
+  if (varlen && cbase + nchunks > p.solve_slots) {  // offsets inconsistent with the workspace sizing
+    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, 270);
+    return;
+  }
+  if (nchunks == 0) {  // an empty packed sequence: the final state is the initial one
+    float* st = p.state + slot * p.slot_stride + (int64_t)h * D * D;
+    const float* h0 = p.h0 != nullptr ? p.h0 + slot * p.slot_stride + (int64_t)h * D * D : nullptr;
+    if (h0 != st)
+      for (int i = threadIdx.x; i < D * D; i += NT) st[i] = h0 != nullptr ? h0[i] : 0.f;
+    return;
+  }
 
   if (tid == 0) {
     tc::mbar_init(&sm.bar_kq[0], 1);
@@ -622,19 +719,19 @@ __global__ void __launch_bounds__(NT, 1)
     const int buf = m & 1;
     tc::mbar_expect_tx(&sm.bar_kq[buf], 4 * 8192);
     for (int a = 0; a < 2; ++a) {
-      tc::tma_load_4d(sm.kq[buf][a], &tm_k, &sm.bar_kq[buf], 64 * a, m * C, hk, b);
-      tc::tma_load_4d(sm.kq[buf][a] + 8192, &tm_q, &sm.bar_kq[buf], 64 * a, m * C, hk, b);
+      tc::tma_load_4d(sm.kq[buf][a], &tm_k, &sm.bar_kq[buf], 64 * a, t0 + m * C, hk, b);
+      tc::tma_load_4d(sm.kq[buf][a] + 8192, &tm_q, &sm.bar_kq[buf], 64 * a, t0 + m * C, hk, b);
     }
   };
   auto issue_v = [&](int m) {
     tc::mbar_expect_tx(&sm.bar_v, 2 * 8192);
-    for (int a = 0; a < 2; ++a) tc::tma_load_4d(sm.v[a], &tm_v, &sm.bar_v, 64 * a, m * C, h, b);
+    for (int a = 0; a < 2; ++a) tc::tma_load_4d(sm.v[a], &tm_v, &sm.bar_v, 64 * a, t0 + m * C, h, b);
   };
   // With the solve offloaded: chunk m's TB | TBG (16 KB, contiguous in sm.tb, sm.tbg) and its
   // scalars (slot m & 3, last read for chunk m-4) by bulk copies, issued by the prep leader
   // once chunk m-1's U' and W^T products are done.
   auto issue_tb = [&](int m) {
-    const uint8_t* src = p.solve + (((int64_t)b * nchunks + m) * p.hv + h) * kSolveBytes;
+    const uint8_t* src = p.solve + ((cbase + m) * p.hv + h) * kSolveBytes;
     tc::mbar_expect_tx(&sm.bar_tb, kSolveBytes);
     tc::bulk_load(sm.tb, src, 2 * 8192, &sm.bar_tb);
     tc::bulk_load(&sm.cs[m & 3], src + 2 * 8192, sizeof(ChunkScalars), &sm.bar_tb);
@@ -675,11 +772,11 @@ __global__ void __launch_bounds__(NT, 1)
       // for buffers that free up one chunk later, and then hit L2
       if (pt == 0 && m + 2 < nchunks) {
         for (int a = 0; a < 2; ++a) {
-          tc::tma_prefetch_4d(&tm_k, 64 * a, (m + 2) * C, hk, b);
-          tc::tma_prefetch_4d(&tm_q, 64 * a, (m + 2) * C, hk, b);
-          tc::tma_prefetch_4d(&tm_v, 64 * a, (m + 2) * C, h, b);
+          tc::tma_prefetch_4d(&tm_k, 64 * a, t0 + (m + 2) * C, hk, b);
+          tc::tma_prefetch_4d(&tm_q, 64 * a, t0 + (m + 2) * C, hk, b);
+          tc::tma_prefetch_4d(&tm_v, 64 * a, t0 + (m + 2) * C, h, b);
         }
-        if (kOffload) tc::bulk_prefetch_l2(p.solve + (((int64_t)b * nchunks + m + 2) * p.hv + h) * kSolveBytes, kSolveBytes);
+        if (kOffload) tc::bulk_prefetch_l2(p.solve + ((cbase + m + 2) * p.hv + h) * kSolveBytes, kSolveBytes);
       }
       // ---- [K;Q] K^T first: the scalar scan below runs under the MMA
       if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
@@ -924,14 +1021,15 @@ __global__ void __launch_bounds__(NT, 1)
     float pend[4] = {0.f, 0.f, 0.f, 0.f};
     auto load_scalars = [&](int m) {
       const int t = m * C + 2 * lane;
+      const int64_t tg = t0 + t;
       pend[0] = pend[1] = pend[2] = pend[3] = 0.f;
-      if (m < nchunks && t < p.seqlen) {
-        pend[0] = load_any(p.g, b * p.g_sb + (int64_t)t * p.g_st + h * p.g_sh, p.g_dtype);
-        pend[2] = load_any(p.beta, b * p.b_sb + (int64_t)t * p.b_st + h * p.b_sh, p.b_dtype);
+      if (m < nchunks && t < len) {
+        pend[0] = load_any(p.g, b * p.g_sb + tg * p.g_st + h * p.g_sh, p.g_dtype);
+        pend[2] = load_any(p.beta, b * p.b_sb + tg * p.b_st + h * p.b_sh, p.b_dtype);
       }
-      if (m < nchunks && t + 1 < p.seqlen) {
-        pend[1] = load_any(p.g, b * p.g_sb + (int64_t)(t + 1) * p.g_st + h * p.g_sh, p.g_dtype);
-        pend[3] = load_any(p.beta, b * p.b_sb + (int64_t)(t + 1) * p.b_st + h * p.b_sh, p.b_dtype);
+      if (m < nchunks && t + 1 < len) {
+        pend[1] = load_any(p.g, b * p.g_sb + (tg + 1) * p.g_st + h * p.g_sh, p.g_dtype);
+        pend[3] = load_any(p.beta, b * p.b_sb + (tg + 1) * p.b_st + h * p.b_sh, p.b_dtype);
       }
     };
     auto stage_scalars = [&](int m) {
@@ -1013,28 +1111,42 @@ __global__ void __launch_bounds__(NT, 1)
         state_step(n + 1);
       }
       // staging in ut as row-major [rows][128]; rows past the sequence end fall outside
-      // the tensor and are not written by the store
+      // the tensor and are not written by the TMA store. A packed sequence's last, partial
+      // chunk is copied out row by row instead (its next rows belong to the next sequence).
       if (p.o == nullptr) continue;
       if (kOffload) compute_o();
       constexpr int kRows = sizeof(TOut) == 2 ? 64 : 32;  // 16 KB per pass
       TOut* stage = reinterpret_cast<TOut*>(sm.ut);
+      const bool partial = varlen && n * C + C > len;
 #pragma unroll
-      for (int t0 = 0; t0 < 64; t0 += kRows) {
-        if (t0 > 0) {
+      for (int r0 = 0; r0 < 64; r0 += kRows) {
+        if (r0 > 0) {
           if (tid == 0) tc::bulk_wait_read0();
           role_sync(1);
         }
-        if (32 * hf >= t0 && 32 * hf < t0 + kRows) {
+        if (32 * hf >= r0 && 32 * hf < r0 + kRows) {
 #pragma unroll
-          for (int t = 0; t < 32; ++t) stage[(32 * hf - t0 + t) * D + j] = from_f32<TOut>(o[t]);
+          for (int t = 0; t < 32; ++t) stage[(32 * hf - r0 + t) * D + j] = from_f32<TOut>(o[t]);
         }
         tc::fence_proxy_async_smem();
         tc::fence_before_sync();  // every thread's TMEM reads of QS, UM precede QS(n+1)
         role_sync(1);
+        if (partial) {
+          constexpr int kVec = 16 / (int)sizeof(TOut), kRowVecs = D / kVec;
+          const int valid = min(kRows, len - n * C - r0);
+          TOut* out = static_cast<TOut*>(p.o);
+          for (int e = tid; e < valid * kRowVecs; e += kRoleThreads) {
+            const int r = e / kRowVecs, c = (e % kRowVecs) * kVec;
+            const int64_t off = (int64_t)b * p.o_sb + (int64_t)(t0 + n * C + r0 + r) * p.o_st + (int64_t)h * p.o_sh + c;
+            *reinterpret_cast<uint4*>(out + off) = *reinterpret_cast<const uint4*>(stage + r * D + c);
+          }
+        }
         if (tid == 0) {
-          tc::tma_store_4d(&tm_o, stage, 0, n * C + t0, h, b);
-          tc::bulk_commit();
-          if (kOffload && t0 == 0 && n + 1 < nchunks) {
+          if (!partial) {
+            tc::tma_store_4d(&tm_o, stage, 0, t0 + n * C + r0, h, b);
+            tc::bulk_commit();
+          }
+          if (kOffload && r0 == 0 && n + 1 < nchunks) {
             tc::fence_after_sync();
             issue_qs(n + 1);
           }
@@ -1082,6 +1194,38 @@ bool make_map(CUtensorMap* m, const pbk_view& v, int heads, const pbk_gdn_desc& 
   return make_tmap_bf16_sw128(m, v.data, 4, dims, strides, box);
 }
 
+void fill_args(PrefillArgs& a, const pbk_gdn_desc& d) {
+  a.batch = d.batch;
+  a.seqlen = d.seqlen;
+  a.hk = d.hk;
+  a.hv = d.hv;
+  a.g = d.g.data;
+  a.g_sb = d.g.stride_b;
+  a.g_st = d.g.stride_t;
+  a.g_sh = d.g.stride_h;
+  a.g_dtype = d.g.dtype;
+  a.beta = d.beta.data;
+  a.b_sb = d.beta.stride_b;
+  a.b_st = d.beta.stride_t;
+  a.b_sh = d.beta.stride_h;
+  a.b_dtype = d.beta.dtype;
+  a.o = const_cast<void*>(d.o.data);
+  a.o_sb = d.o.stride_b;
+  a.o_st = d.o.stride_t;
+  a.o_sh = d.o.stride_h;
+  a.h0 = d.h0;
+  a.state = d.state;
+  a.slot_stride = d.state_slot_stride;
+  a.layout = d.state_layout;
+  a.state_indices = d.state_indices;
+  a.scale = d.scale;
+  a.err = device_error_word();
+  a.solve = nullptr;
+  a.cu_seqlens = nullptr;
+  a.chunk_off = nullptr;
+  a.solve_slots = 0;
+}
+
 }  // namespace
 
 bool gdn_prefill_tc_supported(const pbk_gdn_desc& d) {
@@ -1125,6 +1269,9 @@ cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t
   sa.hk = d.hk;
   sa.hv = d.hv;
   sa.ws = static_cast<uint8_t*>(ws);
+  sa.cu_seqlens = nullptr;
+  sa.chunk_off = nullptr;
+  sa.num_seqs = 0;
   cudaError_t e =
       cudaFuncSetAttribute(gdn_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SolveSmem));
   if (e != cudaSuccess) return e;
@@ -1151,31 +1298,7 @@ cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, bool so
     if (!make_tmap_plain(&mo, d.o.data, obf, 4, dims, strides, box)) return cudaErrorInvalidValue;
   }
   PrefillArgs a;
-  a.batch = d.batch;
-  a.seqlen = d.seqlen;
-  a.hk = d.hk;
-  a.hv = d.hv;
-  a.g = d.g.data;
-  a.g_sb = d.g.stride_b;
-  a.g_st = d.g.stride_t;
-  a.g_sh = d.g.stride_h;
-  a.g_dtype = d.g.dtype;
-  a.beta = d.beta.data;
-  a.b_sb = d.beta.stride_b;
-  a.b_st = d.beta.stride_t;
-  a.b_sh = d.beta.stride_h;
-  a.b_dtype = d.beta.dtype;
-  a.o = const_cast<void*>(d.o.data);
-  a.o_sb = d.o.stride_b;
-  a.o_st = d.o.stride_t;
-  a.o_sh = d.o.stride_h;
-  a.h0 = d.h0;
-  a.state = d.state;
-  a.slot_stride = d.state_slot_stride;
-  a.layout = d.state_layout;
-  a.state_indices = d.state_indices;
-  a.scale = d.scale;
-  a.err = device_error_word();
+  fill_args(a, d);
   a.solve = static_cast<const uint8_t*>(solve_ws);
   if (solve_ws != nullptr && !solved) {
     cudaError_t e = launch_gdn_chunk_solve(d, solve_ws, st);
@@ -1191,6 +1314,81 @@ cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, bool so
   if (d.o.dtype == PBK_BF16)
     return solve_ws ? go(gdn_prefill_tc_kernel<bf16, true>) : go(gdn_prefill_tc_kernel<bf16, false>);
   return solve_ws ? go(gdn_prefill_tc_kernel<float, true>) : go(gdn_prefill_tc_kernel<float, false>);
+}
+
+// Packed varlen prefill: d describes [1, T, H, 128] tensors (batch 1, seqlen = T), sequence s
+// = rows cu_seqlens[s] .. cu_seqlens[s+1] (device array, ascending, cu_seqlens[0] = 0 is not
+// required), its state at slot state_indices[s] (or s). Workspace: the solve slots of at most
+// ceil(T / C) + num_seqs chunks, then the chunk offsets.
+size_t gdn_prefill_varlen_workspace(const pbk_gdn_desc& d, int num_seqs) {
+  const size_t slots = (size_t)((d.seqlen + C - 1) / C + num_seqs) * d.hv * kSolveBytes;
+  return slots + ((size_t)(num_seqs + 1) * sizeof(int32_t) + 15) / 16 * 16;
+}
+
+cudaError_t launch_gdn_prefill_varlen(const pbk_gdn_desc& d, const int32_t* cu_seqlens, int num_seqs, void* ws,
+                                      cudaStream_t st) {
+  const int max_chunks = (d.seqlen + C - 1) / C + num_seqs;
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  int32_t* chunk_off = reinterpret_cast<int32_t*>(wsb + (size_t)max_chunks * d.hv * kSolveBytes);
+  gdn_chunk_offsets_kernel<<<1, 1024, 0, st>>>(cu_seqlens, num_seqs, d.seqlen, chunk_off);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  SolveArgs sa;
+  sa.k = static_cast<const bf16*>(d.k.data);
+  sa.k_sb = d.k.stride_b;
+  sa.k_st = d.k.stride_t;
+  sa.k_sh = d.k.stride_h;
+  sa.g = d.g.data;
+  sa.g_sb = d.g.stride_b;
+  sa.g_st = d.g.stride_t;
+  sa.g_sh = d.g.stride_h;
+  sa.g_dtype = d.g.dtype;
+  sa.beta = d.beta.data;
+  sa.b_sb = d.beta.stride_b;
+  sa.b_st = d.beta.stride_t;
+  sa.b_sh = d.beta.stride_h;
+  sa.b_dtype = d.beta.dtype;
+  sa.seqlen = d.seqlen;
+  sa.hk = d.hk;
+  sa.hv = d.hv;
+  sa.ws = wsb;
+  sa.cu_seqlens = cu_seqlens;
+  sa.chunk_off = chunk_off;
+  sa.num_seqs = num_seqs;
+  if ((e = cudaFuncSetAttribute(gdn_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(SolveSmem))) != cudaSuccess)
+    return e;
+  gdn_solve_kernel<<<dim3((unsigned)max_chunks, (unsigned)d.hv, 1), kSolveThreads, sizeof(SolveSmem), st>>>(sa);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // the recurrence: one CTA per (sequence, value head) over the packed tensors
+  pbk_gdn_desc dv = d;
+  dv.batch = num_seqs;  // CTAs and state slots per sequence; the tensors stay [1, T, H, 128]
+  CUtensorMap mq, mk, mv, mo;
+  if (!make_map(&mq, d.q, d.hk, d) || !make_map(&mk, d.k, d.hk, d) || !make_map(&mv, d.v, d.hv, d))
+    return cudaErrorInvalidValue;
+  memset(&mo, 0, sizeof(mo));
+  if (d.o.data != nullptr) {
+    const bool obf = d.o.dtype == PBK_BF16;
+    const uint64_t es = obf ? 2 : 4;
+    const uint64_t dims[4] = {128, (uint64_t)d.seqlen, (uint64_t)d.hv, 1};
+    const uint64_t strides[3] = {(uint64_t)d.o.stride_t * es, (uint64_t)d.o.stride_h * es, (uint64_t)d.o.stride_b * es};
+    const uint32_t box[4] = {128, obf ? 64u : 32u, 1, 1};
+    if (!make_tmap_plain(&mo, d.o.data, obf, 4, dims, strides, box)) return cudaErrorInvalidValue;
+  }
+  PrefillArgs a;
+  fill_args(a, dv);
+  a.solve = wsb;
+  a.cu_seqlens = cu_seqlens;
+  a.chunk_off = chunk_off;
+  a.solve_slots = max_chunks;
+  const dim3 grid((unsigned)((int64_t)num_seqs * d.hv));
+  auto go = [&](auto kernel) {
+    cudaError_t e2 = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e2 != cudaSuccess) return e2;
+    kernel<<<grid, NT, kSmemBytes, st>>>(mq, mk, mv, mo, a);
+    return cudaGetLastError();
+  };
+  return d.o.dtype == PBK_BF16 ? go(gdn_prefill_tc_kernel<bf16, true>) : go(gdn_prefill_tc_kernel<float, true>);
 }
 
 }  // namespace pbk

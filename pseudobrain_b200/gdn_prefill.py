@@ -189,3 +189,39 @@ def gdn_prefill_segmented(q, k, v, g, beta, scale, h0=None, segments: int | None
         prefill_solved(qs, ks, vs, gs, bs, starts[0, :full], eye, seg(o), float(scale), ws, 0)
         cur.wait_stream(side)
     return o, final
+
+
+# ------------------------------------------------------------------------------------------
+# Packed varlen prefill (vLLM's chunked-prefill batch: cu_seqlens over [1, T, H, 128])
+# ------------------------------------------------------------------------------------------
+@torch.library.custom_op("pbk::gdn_prefill_varlen", mutates_args=("state", "o"))
+def gdn_prefill_varlen_(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                        h0: torch.Tensor | None, state: torch.Tensor, o: torch.Tensor, scale: float,
+                        cu_seqlens: torch.Tensor, state_indices: torch.Tensor | None = None,
+                        layout: int = 0) -> None:
+    """delta_rule_chunked on each packed sequence: q, k [1, T, Hk, 128], v [1, T, Hv, 128]
+    bf16, g, beta [1, T, Hv]; sequence s is rows cu_seqlens[s] .. cu_seqlens[s+1] (int32 on
+    the device). Reads h0 (None: zeros; h0 may be ``state``: in place) and writes the final
+    state of sequence s into slot state_indices[s] (or s) of ``state`` ([slots, Hv, K, V],
+    layout 0, or [slots, Hv, V, K], layout 1) and its outputs into its rows of o [1, T, Hv, 128]."""
+    dev = _check_cuda(q, k, v, g, beta, state, o, cu_seqlens)
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.dim() != 1 or not cu_seqlens.is_contiguous():
+        raise TypeError("cu_seqlens must be a contiguous int32 vector")
+    if state_indices is not None and state_indices.dtype != torch.int32:
+        raise TypeError("state_indices must be int32")
+    if q.shape[0] != 1:
+        raise ValueError("packed inputs have batch 1")
+    num_seqs = cu_seqlens.numel() - 1
+    d = _desc(q, k, v, g, beta, o, h0, state, scale, state_indices, layout)
+    with torch.cuda.device(dev):
+        n = LIB.pbk_gdn_prefill_varlen_workspace(d, num_seqs)
+        if n == 0:
+            raise ValueError("varlen prefill runs on the bf16 tensor-core path (bf16 q/k/v, 16-byte strides)")
+        ws = torch.empty(n, dtype=torch.uint8, device=dev)
+        check(LIB.pbk_gdn_prefill_varlen(d, cu_seqlens.data_ptr(), num_seqs, ws.data_ptr(), n, _stream(dev)),
+              "pbk_gdn_prefill_varlen")
+
+
+@gdn_prefill_varlen_.register_fake
+def _(q, k, v, g, beta, h0, state, o, scale, cu_seqlens, state_indices=None, layout=0):
+    return None
