@@ -128,3 +128,59 @@ def rel_err(x: np.ndarray, ref: np.ndarray) -> float:
     ref = np.asarray(ref, dtype=np.float64)
     den = np.linalg.norm(ref)
     return float(np.linalg.norm(x - ref) / (den if den > 0 else 1.0))
+
+
+# ------------------------------------------------------------------------------------------
+# The layer pieces around the recurrence (GatedDeltaNetLayer.forward, gated_deltanet.py:411-440)
+# ------------------------------------------------------------------------------------------
+L2_EPS = 1e-6    # gated_deltanet.py:55
+NORM_EPS = 1e-5  # gated_deltanet.py:72
+
+
+def short_convolution(x, tail, weight):
+    """Causal depthwise convolution over time with a carried input tail, then SiLU
+    (gated_deltanet.py:314-338). x [B,T,C]; tail [B,K-1,C]; weight [C,K] (weight[:, -1]
+    multiplies the current input) or None. fp32. Returns (y [B,T,C], new tail [B,K-1,C])."""
+    x = x.astype(np.float32)
+    if weight is None:
+        return x / (1.0 + np.exp(-x)), tail
+    size = weight.shape[1]
+    length = x.shape[1]
+    ext = np.concatenate((tail.astype(np.float32), x), axis=1) if size > 1 else x
+    new_tail = ext[:, ext.shape[1] - (size - 1):] if size > 1 else tail
+    w = weight.astype(np.float32)
+    y = ext[:, :length] * w[:, 0]
+    for j in range(1, size):
+        y = y + ext[:, j:j + length] * w[:, j]
+    return (y / (1.0 + np.exp(-y))).astype(np.float32), new_tail
+
+
+def l2_normalize(x, mode="max", eps=L2_EPS):
+    """q/k normalisation over the last dim (gated_deltanet.py:59-70): 'max' is
+    x / max(||x||, eps) (F.normalize), 'hf' is x * rsqrt(sum x^2 + eps), in fp32."""
+    xf = x.astype(np.float32)
+    ss = np.sum(xf * xf, axis=-1, keepdims=True)
+    if mode == "max":
+        return xf / np.maximum(np.sqrt(ss), eps)
+    if mode == "hf":
+        return xf / np.sqrt(ss + eps)
+    raise ValueError(mode)
+
+
+def gating(a, b, a_log, dt_bias):
+    """g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (gated_deltanet.py:427-429);
+    softplus with F.softplus's threshold of 20. fp32."""
+    x = a.astype(np.float32) + dt_bias.astype(np.float32)
+    sp = np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0))))
+    g = -np.exp(a_log.astype(np.float32)) * sp
+    beta = 1.0 / (1.0 + np.exp(-b.astype(np.float32)))
+    return g.astype(np.float32), beta.astype(np.float32)
+
+
+def gated_out_norm(o, gate, weight, eps=NORM_EPS):
+    """o * rsqrt(mean(o^2) + eps) * weight * SiLU(gate) over the value dim
+    (gated_deltanet.py:439-440). o, gate [B,T,H,V]; weight [V]. fp32."""
+    o = o.astype(np.float32)
+    gt = gate.astype(np.float32)
+    y = o / np.sqrt(np.mean(o * o, axis=-1, keepdims=True) + eps)
+    return (y * weight.astype(np.float32) * (gt / (1.0 + np.exp(-gt)))).astype(np.float32)

@@ -26,6 +26,9 @@ Fixtures:
                   piece_attention (sinks + retrieved blocks + partial tail + masked window,
                   the SDPA branch) over an Archive of 2 key heads, 64-token blocks after the 4
                   sink positions, for a decode piece (T=1) and a 3-token piece.
+  gdn_io.npz      the layer pieces around the recurrence: short_convolution with a carried
+                  tail (width 4), l2_normalize in both modes, the gating and gated output
+                  norm expressions of GatedDeltaNetLayer.forward.
   quest.npz       archive_append + retrieve (flat mode, page 16, budget 4 pages) for a
                   decode query (T=1) and a 3-token query, plus the exact attention over
                   [retrieved ; window] as pseudobrain/transplant.py:619-628 computes it.
@@ -188,6 +191,48 @@ def make_serving(MEM):
     np.savez_compressed(os.path.join(HERE, "serving.npz"), **out)
 
 
+def make_gdn_io(G):
+    """The layer pieces around the recurrence: short_convolution (with a carried tail) and
+    l2_normalize (both modes) are the reference's functions; gating and the gated output
+    norm are GatedDeltaNetLayer.forward's expressions (gated_deltanet.py:427-429, 439-440),
+    evaluated with the reference's torch ops."""
+    import torch
+    import torch.nn.functional as F
+    gen = torch.Generator().manual_seed(77)
+    b, t, hk, hv, d, width = 2, 70, 1, 2, 128, 4
+    ch = (2 * hk + hv) * d
+    x = torch.randn(b, t, ch, generator=gen)
+    tail = torch.randn(b, width - 1, ch, generator=gen)
+    weight = torch.randn(ch, width, generator=gen) * 0.5
+    y, new_tail = G.short_convolution(x, tail, weight)
+    q, k, v = y.split((hk * d, hk * d, hv * d), dim=-1)
+    out = {"x": x.numpy(), "tail": tail.numpy(), "weight": weight.numpy(), "y": y.numpy(),
+           "new_tail": new_tail.numpy()}
+    for mode in ("max", "hf"):
+        out[f"q_{mode}"] = G.l2_normalize(q.reshape(b, t, hk, d), mode).numpy()
+        out[f"k_{mode}"] = G.l2_normalize(k.reshape(b, t, hk, d), mode).numpy()
+    out["v"] = v.reshape(b, t, hv, d).numpy()
+    small = torch.zeros(1, 1, d)
+    small[..., 0] = 1e-4  # the modes differ for small vectors
+    out["small_max"], out["small_hf"] = G.l2_normalize(small, "max").numpy(), G.l2_normalize(small, "hf").numpy()
+    decay = torch.randn(b, t, 2 * hv, generator=gen) * 3.0
+    decay[0, 0, 0] = 25.0  # past softplus's threshold
+    a_log = torch.randn(hv, generator=gen)
+    dt_bias = torch.randn(hv, generator=gen)
+    a, bb = decay.chunk(2, dim=-1)
+    g = -a_log.exp() * F.softplus(a + dt_bias)
+    beta = torch.sigmoid(bb)
+    out.update({"decay": decay.numpy(), "a_log": a_log.numpy(), "dt_bias": dt_bias.numpy(), "g": g.numpy(),
+                "beta": beta.numpy()})
+    o = torch.randn(b, t, hv, d, generator=gen)
+    gate = torch.randn(b, t, hv * d, generator=gen)
+    o_norm = torch.randn(d, generator=gen) * 0.3 + 1.0
+    on = o * torch.rsqrt(o.square().mean(-1, keepdim=True) + G.NORM_EPS)
+    on = on * o_norm * F.silu(gate.view(b, t, hv, d))
+    out.update({"o": o.numpy(), "gate": gate.numpy(), "o_norm": o_norm.numpy(), "out": on.numpy()})
+    np.savez_compressed(os.path.join(HERE, "gdn_io.npz"), **out)
+
+
 def main(reference_root: str) -> None:
     sys.path.insert(0, reference_root)
     import torch
@@ -199,7 +244,7 @@ def main(reference_root: str) -> None:
     os.environ.setdefault("PB27_MEMORY_OFFLOAD", "")
     import pb27_vllm.memory as MEM
     makers = {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR),
-              "serving": lambda: make_serving(MEM)}
+              "serving": lambda: make_serving(MEM), "gdn_io": lambda: make_gdn_io(G)}
     for name in (sys.argv[2:] if len(sys.argv) > 2 else makers):  # all, or only the named fixtures
         makers[name]()
     for name in sorted(os.listdir(HERE)):

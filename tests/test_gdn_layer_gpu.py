@@ -1,0 +1,112 @@
+"""GPU parity of the layer pieces around the recurrence (pbk_gdn_conv_norm, pbk_gdn_gating,
+pbk_gdn_out_norm) against the reference's outputs (tests/golden/gdn_io.npz) and the oracle.
+fp32 outputs: 1e-5 norm-wise relative (fp32 arithmetic in another order); bf16 outputs: the
+bf16 rounding bound 4e-3."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gdn as ogdn
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(x, dev, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev, dtype)
+
+
+@pytest.mark.parametrize("mode", ["max", "hf"])
+@pytest.mark.parametrize("out_dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 4e-3)])
+def test_conv_norm_matches_reference(cuda_device, mode, out_dtype, tol):
+    from pseudobrain_b200.gdn_layer import conv_qkv
+    f = load_golden("gdn_io.npz")
+    x, tail, w = (_t(f[n], cuda_device) for n in ("x", "tail", "weight"))
+    new_tail = torch.empty_like(tail)
+    q, k, v = conv_qkv(x, tail, w, 1, 2, mode, new_tail, out_dtype)
+    assert ogdn.rel_err(q.float().cpu().numpy(), f[f"q_{mode}"]) < tol
+    assert ogdn.rel_err(k.float().cpu().numpy(), f[f"k_{mode}"]) < tol
+    assert ogdn.rel_err(v.float().cpu().numpy(), f["v"]) < tol
+    assert np.array_equal(new_tail.cpu().numpy(), f["new_tail"])
+
+
+def test_conv_short_sequences_and_no_weight(cuda_device):
+    """T shorter than the taps (the new tail mixes old tail and inputs), T across several
+    token tiles, and SiLU only (no convolution); no normalisation."""
+    from pseudobrain_b200.gdn_layer import conv_qkv
+    rng = np.random.default_rng(4)
+    for t in (1, 2, 33, 97):
+        x = rng.standard_normal((2, t, 512)).astype(np.float32)
+        tail = rng.standard_normal((2, 3, 512)).astype(np.float32)
+        w = (0.5 * rng.standard_normal((512, 4))).astype(np.float32)
+        new_tail = torch.empty(2, 3, 512, device=cuda_device)
+        q, k, v = conv_qkv(_t(x, cuda_device), _t(tail, cuda_device), _t(w, cuda_device), 1, 2, None, new_tail,
+                           torch.float32)
+        y, nt = ogdn.short_convolution(x, tail, w)
+        got = torch.cat((q.flatten(2), k.flatten(2), v.flatten(2)), -1).cpu().numpy()
+        assert ogdn.rel_err(got, y) < 1e-5, t
+        assert np.array_equal(new_tail.cpu().numpy(), nt), t
+    x = rng.standard_normal((1, 5, 512)).astype(np.float32)
+    q, k, v = conv_qkv(_t(x, cuda_device), None, None, 1, 2, None, None, torch.float32)
+    got = torch.cat((q.flatten(2), k.flatten(2), v.flatten(2)), -1).cpu().numpy()
+    assert ogdn.rel_err(got, ogdn.short_convolution(x, None, None)[0]) < 1e-5
+
+
+def test_gating_matches_reference(cuda_device):
+    from pseudobrain_b200.gdn_layer import gdn_gating
+    f = load_golden("gdn_io.npz")
+    g, beta = gdn_gating(_t(f["decay"], cuda_device), _t(f["a_log"], cuda_device), _t(f["dt_bias"], cuda_device))
+    assert ogdn.rel_err(g.cpu().numpy(), f["g"]) < 1e-5
+    assert ogdn.rel_err(beta.cpu().numpy(), f["beta"]) < 1e-5
+
+
+@pytest.mark.parametrize("in_dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 4e-3)])
+def test_out_norm_matches_reference(cuda_device, in_dtype, tol):
+    from pseudobrain_b200.gdn_layer import gated_out_norm
+    f = load_golden("gdn_io.npz")
+    o = _t(f["o"], cuda_device, in_dtype)
+    gate = _t(f["gate"], cuda_device, in_dtype)
+    out = gated_out_norm(o, gate, _t(f["o_norm"], cuda_device), out_dtype=torch.float32)
+    want = f["out"] if in_dtype == torch.float32 else ogdn.gated_out_norm(
+        o.float().cpu().numpy(), gate.float().cpu().numpy().reshape(o.shape), f["o_norm"])
+    assert ogdn.rel_err(out.cpu().numpy(), want) < tol
+
+
+def test_layer_core_matches_oracle_composition(cuda_device):
+    """conv + norm + gating + recurrence (chunked prefill, then a 1-token decode carrying
+    state and tail) + gated output norm, against the oracle's pieces composed the way
+    GatedDeltaNetLayer.forward composes them (gated_deltanet.py:411-440)."""
+    from pseudobrain_b200.gdn_layer import gated_deltanet_core
+    rng = np.random.default_rng(6)
+    b, hk, hv, c = 1, 1, 2, 512
+    w = (0.3 * rng.standard_normal((c, 4))).astype(np.float32)
+    a_log = rng.standard_normal(hv).astype(np.float32) * 0.5
+    dt_bias = rng.standard_normal(hv).astype(np.float32)
+    o_norm = (1.0 + 0.2 * rng.standard_normal(128)).astype(np.float32)
+    tail = np.zeros((b, 3, c), np.float32)
+    state = np.zeros((b, hv, 128, 128), np.float32)
+    d_tail, d_state = _t(tail, cuda_device), _t(state, cuda_device)
+    for t in (150, 1):
+        qkv = rng.standard_normal((b, t, c)).astype(np.float32)
+        gate = rng.standard_normal((b, t, hv * 128)).astype(np.float32)
+        decay = rng.standard_normal((b, t, 2 * hv)).astype(np.float32)
+        out, d_state, d_tail = gated_deltanet_core(_t(qkv, cuda_device), _t(gate, cuda_device), _t(decay, cuda_device),
+                                                   d_tail, _t(w, cuda_device), _t(a_log, cuda_device),
+                                                   _t(dt_bias, cuda_device), _t(o_norm, cuda_device), d_state, hk, hv)
+        y, tail = ogdn.short_convolution(qkv, tail, w)
+        q = ogdn.l2_normalize(y[..., :128].reshape(b, t, hk, 128))
+        k = ogdn.l2_normalize(y[..., 128:256].reshape(b, t, hk, 128))
+        v = y[..., 256:].reshape(b, t, hv, 128)
+        from oracle.quest import bf16_round
+        q, k, v = (bf16_round(x.astype(np.float32)) for x in (q, k, v))  # the kernels read bf16 q/k/v
+        g, beta = ogdn.gating(decay[..., :hv], decay[..., hv:], a_log, dt_bias)
+        beta = bf16_round(beta)
+        qe, ke = ogdn.expand_key_heads(q, hv), ogdn.expand_key_heads(k, hv)
+        fn = ogdn.delta_rule_sequential if t <= 4 else ogdn.delta_rule_chunked
+        o, state = fn(qe, ke, v, g, beta, 128 ** -0.5, state)
+        want = ogdn.gated_out_norm(o, gate.reshape(b, t, hv, 128), o_norm)
+        assert ogdn.rel_err(out.cpu().numpy(), want) < 2e-2, t
+        assert ogdn.rel_err(d_state.cpu().numpy(), state) < 2e-2, t
+        assert np.allclose(d_tail.cpu().numpy(), tail), t

@@ -145,3 +145,26 @@ def test_serving_twins_match_reference(case):
     o = osv.piece_attention(keys, values, q, f[f"{case}_pos"], top, int(f["groups"]), int(f["window"]),
                             q.shape[-1] ** -0.5, int(f["block"]))
     assert ogdn.rel_err(o, f[f"{case}_out"]) < FP32_TOL
+
+
+def test_gdn_layer_pieces_match_reference():
+    """short_convolution, l2_normalize (both modes), gating and the gated output norm of the
+    oracle against the reference's outputs."""
+    f = load_golden("gdn_io.npz")
+    y, new_tail = ogdn.short_convolution(f["x"], f["tail"], f["weight"])
+    assert ogdn.rel_err(y, f["y"]) < 1e-5
+    assert np.array_equal(new_tail, f["new_tail"])
+    b, t = f["x"].shape[:2]
+    d = 128
+    for mode in ("max", "hf"):
+        assert ogdn.rel_err(ogdn.l2_normalize(y[..., :d].reshape(b, t, 1, d), mode), f[f"q_{mode}"]) < 1e-5
+        assert ogdn.rel_err(ogdn.l2_normalize(y[..., d:2 * d].reshape(b, t, 1, d), mode), f[f"k_{mode}"]) < 1e-5
+    small = np.zeros((1, 1, d), np.float32)
+    small[..., 0] = 1e-4
+    assert np.allclose(ogdn.l2_normalize(small, "max"), f["small_max"])
+    assert np.allclose(ogdn.l2_normalize(small, "hf"), f["small_hf"])
+    hv = f["a_log"].shape[0]
+    g, beta = ogdn.gating(f["decay"][..., :hv], f["decay"][..., hv:], f["a_log"], f["dt_bias"])
+    assert ogdn.rel_err(g, f["g"]) < 1e-6 and ogdn.rel_err(beta, f["beta"]) < 1e-6
+    out = ogdn.gated_out_norm(f["o"], f["gate"].reshape(f["o"].shape), f["o_norm"])
+    assert ogdn.rel_err(out, f["out"]) < 1e-5
