@@ -256,6 +256,11 @@ PBK_API size_t pbk_quest_attend_workspace(const pbk_quest_desc* desc);
  * of sum_d max(q_d kmax_pd, q_d kmin_pd) in fp32, keep the k highest (ties to the
  * lowest page index) and write them to desc->pages in ascending order. */
 PBK_API int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
+/* pbk_quest_select in parts (bit mask): 1 the page scores and segment maxima into the
+ * workspace, 2 the top-k selection from them (3: both). A caller overlaps other work with
+ * the top-k by launching the parts apart, in order, with the same workspace. */
+PBK_API int pbk_quest_select_parts(const pbk_quest_desc* desc, int32_t parts, void* workspace, size_t workspace_bytes,
+                                   void* stream);
 
 /* Largest number of page scores (nq * kv * (n_arch / page)) pbk_quest_select_noalloc
  * can hold: 4,194,304 fp32 = 16 MiB, enough for 8 query groups x 8 key heads over a
@@ -293,6 +298,13 @@ PBK_API size_t pbk_quest_attend_sinks_workspace(const pbk_quest_desc* desc, int3
 PBK_API int pbk_quest_attend_sinks(const pbk_quest_desc* desc, const void* sink_keys, const void* sink_values,
                                    int32_t n_sink, int64_t sink_stride_kv, int64_t sink_stride_n, void* workspace,
                                    size_t workspace_bytes, void* stream);
+/* pbk_quest_attend_sinks in parts (bit mask): 1 the partials of the retrieved keys (sinks,
+ * pages, tail), 2 the partials of the window keys, 4 their combination into out (7: all).
+ * The window part does not read desc.pages, so it may run while the selection's top-k is
+ * still computing them; the combine runs after both, with the same workspace. */
+PBK_API int pbk_quest_attend_parts(const pbk_quest_desc* desc, const void* sink_keys, const void* sink_values,
+                                   int32_t n_sink, int64_t sink_stride_kv, int64_t sink_stride_n, int32_t parts,
+                                   void* workspace, size_t workspace_bytes, void* stream);
 
 /* Exact rerank (pb27_vllm/memory.py:854-872): for c candidate pages per (group, key head),
  * cand [nq, kv, c] int32 ascending, the exact score max over the head's query rows

@@ -104,6 +104,8 @@ SIGNATURES = {
     "pbk_quest_attend_workspace": (ctypes.c_size_t, [_QD]),
     "pbk_quest_select": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_select_noalloc": (ctypes.c_int, [_QD, _VP]),
+    "pbk_quest_select_parts": (ctypes.c_int, [_QD, _I32, _VP, ctypes.c_size_t, _VP]),
+    "pbk_quest_attend_parts": (ctypes.c_int, [_QD, _VP, _VP, _I32, _I64, _I64, _I32, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_attend": (ctypes.c_int, [_QD, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_attend_sinks_workspace": (ctypes.c_size_t, [_QD, _I32]),
     "pbk_quest_attend_sinks": (ctypes.c_int, [_QD, _VP, _VP, _I32, _I64, _I64, _VP, ctypes.c_size_t, _VP]),

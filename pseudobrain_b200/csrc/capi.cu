@@ -340,15 +340,22 @@ size_t pbk_quest_rerank_workspace(const pbk_quest_desc* desc, int32_t c) {
   return round_up((size_t)desc->nq * desc->kv * c * sizeof(float));
 }
 
-int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
-  int st = validate_quest(desc, 1);
+int pbk_quest_select_parts(const pbk_quest_desc* desc, int32_t parts, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  int st = validate_quest(desc, 1);  // the full select descriptor for either part
   if (st != PBK_OK) return st;
+  if (parts < 1 || parts > 3) return PBK_ERR_INVALID;
   const size_t need = pbk::quest_score_bytes(*desc);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return PBK_ERR_WORKSPACE;
   if (desc->nq == 0) return PBK_OK;
   if ((st = check_current_device()) != PBK_OK) return st;
   // workspace: the page scores (unless desc->scores keeps them), then the segment maxima
-  return launch_status(pbk::launch_quest_select(*desc, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
+  return launch_status(pbk::launch_quest_select_parts(*desc, static_cast<float*>(workspace), parts,
+                                                      static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {
+  return pbk_quest_select_parts(desc, 3, workspace, workspace_bytes, stream);
 }
 
 int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream) {
@@ -365,9 +372,16 @@ int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream) {
 int pbk_quest_attend_sinks(const pbk_quest_desc* desc, const void* sink_keys, const void* sink_values, int32_t n_sink,
                            int64_t sink_stride_kv, int64_t sink_stride_n, void* workspace, size_t workspace_bytes,
                            void* stream) {
+  return pbk_quest_attend_parts(desc, sink_keys, sink_values, n_sink, sink_stride_kv, sink_stride_n, 7, workspace,
+                                workspace_bytes, stream);
+}
+
+int pbk_quest_attend_parts(const pbk_quest_desc* desc, const void* sink_keys, const void* sink_values, int32_t n_sink,
+                           int64_t sink_stride_kv, int64_t sink_stride_n, int32_t parts, void* workspace,
+                           size_t workspace_bytes, void* stream) {
   int st = validate_quest(desc, 2);
   if (st != PBK_OK) return st;
-  if (n_sink < 0) return PBK_ERR_INVALID;
+  if (n_sink < 0 || parts < 1 || parts > 7) return PBK_ERR_INVALID;
   if (n_sink > 0) {
     if (!sink_keys || !sink_values) return PBK_ERR_INVALID;
     if (!aligned16(sink_keys) || !aligned16(sink_values) || !aligned_elems(sink_stride_kv, 8) ||
@@ -385,7 +399,7 @@ int pbk_quest_attend_sinks(const pbk_quest_desc* desc, const void* sink_keys, co
   sk.s_n = sink_stride_n;
   sk.n = n_sink;
   return launch_status(
-      pbk::launch_quest_attend(*desc, static_cast<float*>(workspace), sk, static_cast<cudaStream_t>(stream)));
+      pbk::launch_quest_attend(*desc, static_cast<float*>(workspace), sk, parts, static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_quest_attend(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream) {

@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_qu
 // to the lowest indices).
 // ---------------------------------------------------------------------------------
 constexpr int kTopkThreads = 1024;
+constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kSegMinPages = 1024;  // rows this long get segment maxima and the candidate path
 
 __device__ __forceinline__ uint32_t ordered_key(float f) {
@@ -164,7 +165,7 @@ constexpr int kBins = 2048;
 struct SelectSmem {
   uint32_t hist[kBins];
   uint32_t prefix, kk;
-  int warp_tot[2][kTopkThreads / 32];
+  int warp_tot[2][kTopkWarps];
 };
 
 // With passes = 2 only the top 22 bits are resolved: `prefix` (low 10 bits zero) is then a
@@ -227,8 +228,8 @@ __device__ __forceinline__ void radix_select(KeyOf key_of, int n, uint32_t k, Se
 }
 
 // Warp-contiguous ranges: warp w owns [w R, (w+1) R) of n elements, read 32 at a time
-// (coalesced); R = ceil(n / 32) rounded up to a multiple of 32.
-__device__ __forceinline__ int warp_range(int n) { return ((n + 31) / 32 + 31) / 32 * 32; }
+// (coalesced); R = ceil(n / warps) rounded up to a multiple of 32.
+__device__ __forceinline__ int warp_range(int n) { return ((n + kTopkWarps - 1) / kTopkWarps + 31) / 32 * 32; }
 
 // Exclusive prefix over the 32 warps of per-warp totals a (and b); returns this warp's bases.
 __device__ __forceinline__ void warp_bases(int a, int b, SelectSmem& ss, int& base_a, int& base_b, int& tot_a) {
@@ -239,7 +240,7 @@ __device__ __forceinline__ void warp_bases(int a, int b, SelectSmem& ss, int& ba
   }
   __syncthreads();
   int ea = 0, eb = 0, ta = 0;
-  for (int w = 0; w < kTopkThreads / 32; ++w) {  // 32 broadcast reads
+  for (int w = 0; w < kTopkWarps; ++w) {  // one broadcast read per warp
     const int x = ss.warp_tot[0][w], y = ss.warp_tot[1][w];
     if (w < warp) ea += x, eb += y;
     ta += x;
@@ -342,7 +343,7 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
       __syncthreads();
       // pages of the candidate segments: warp w takes candidate segments [w P, (w+1) P),
       // lane = page within the segment
-      const int nc = total, P = (nc + 31) / 32;
+      const int nc = total, P = (nc + kTopkWarps - 1) / kTopkWarps;
       const int c0 = min(warp * P, nc), c1 = min(c0 + P, nc);
       int pcnt = 0;
       for (int b0 = c0; b0 < c1; b0 += kSegRegs) {
@@ -739,12 +740,19 @@ size_t quest_partial_bytes(const pbk_quest_desc& d, int n_sink) {
 }
 
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st) {
+  return launch_quest_select_parts(d, scratch, 3, st);
+}
+
+// parts (bit mask): 1 the page scores (and segment maxima) into the workspace, 2 the top-k
+// selection from them.
+cudaError_t launch_quest_select_parts(const pbk_quest_desc& d, float* scratch, int parts, cudaStream_t st) {
   const int npages = d.n_arch / d.page, k = quest_k(d);
   if (npages == 0 || k == 0) return cudaSuccess;
   float* scores = d.scores ? d.scores : scratch;
   const int nseg = quest_nseg(d);
   float* segmax = nseg ? scratch + (d.scores ? 0 : (size_t)d.nq * d.kv * npages) : nullptr;
-  if (quest_score_tc_supported(d)) {
+  if (!(parts & 1)) {
+  } else if (quest_score_tc_supported(d)) {
     // Up to 64 query rows per key head: tensor-core scores (tcgen05, TMA-fed).
     cudaError_t e = launch_quest_score_tc(d, scores, segmax, nseg, st);
     if (e != cudaSuccess) return e;
@@ -758,6 +766,7 @@ cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStr
     quest_score_kernel<<<dim3((npages + kScoreThreads - 1) / kScoreThreads, d.kv), kScoreThreads, smem, st>>>(
         d, npages, scores, segmax, nseg);
   }
+  if (!(parts & 2)) return cudaGetLastError();
   {
     cudaError_t e = cudaFuncSetAttribute(quest_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(TopkSmem));
@@ -799,18 +808,25 @@ cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st
   return launch_quest_select(d, scratch, st);
 }
 
-cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, cudaStream_t st) {
+cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, int parts, cudaStream_t st) {
   const int k = quest_k(d), tail = d.n_arch % d.page;
   int splits = quest_splits(d, sk.n);
   if (splits == 0) return cudaSuccess;
   if (quest_attend_mma_supported(d)) {
-    cudaError_t e = launch_quest_attend_mma(d, k, tail, part, sk, &splits, st);
+    cudaError_t e = launch_quest_attend_mma(d, k, tail, part, sk, parts & 3, &splits, st);
     if (e != cudaSuccess) return e;
-  } else if (d.t * (d.h / d.kv) > 4) {
-    quest_attend_kernel<8><<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
-  } else {
-    quest_attend_kernel<4><<<dim3(splits, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, 0, sk);
+  } else if (parts & 3) {
+    // SIMT kernel: splits [0, sr) retrieved, [sr, splits) window
+    const int sr = quest_ret_splits(d, sk.n);
+    const int s0 = (parts & 1) ? 0 : sr, s1 = (parts & 2) ? splits : sr;
+    if (s1 > s0) {
+      if (d.t * (d.h / d.kv) > 4)
+        quest_attend_kernel<8><<<dim3(s1 - s0, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
+      else
+        quest_attend_kernel<4><<<dim3(s1 - s0, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
+    }
   }
+  if (!(parts & 4)) return cudaGetLastError();
   const int wbytes = splits * (int)sizeof(float);
   if (wbytes > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(quest_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, wbytes);

@@ -26,16 +26,19 @@ constexpr size_t kNoAllocFloats = (size_t)PBK_QUEST_NOALLOC_MAX_SCORES + PBK_QUE
                                   PBK_QUEST_NOALLOC_MAX_SCORES / 1024;
 size_t quest_partial_bytes(const pbk_quest_desc& d, int n_sink);
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st);
+cudaError_t launch_quest_select_parts(const pbk_quest_desc& d, float* scratch, int parts, cudaStream_t st);
 bool quest_score_tc_supported(const pbk_quest_desc& d);
 cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float* segmax, int nseg, cudaStream_t st);
 cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st);
-cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, cudaStream_t st);
+// parts (bit mask): 1 the retrieved splits, 2 the window splits, 4 the combine (all: 7).
+cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, int parts, cudaStream_t st);
 // Tensor-core split attention (quest_attend_mma.cu): up to 16 query rows per key head.
 bool quest_attend_mma_supported(const pbk_quest_desc& d);
 // It picks its own split length (>= the SIMT kernel's, so the workspace sized by
 // quest_partial_bytes holds its partials) and returns the splits per (query, key head).
+// parts: 1 the retrieved splits, 2 the window splits (both: 3).
 cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, float* part, const SinkKeys& sk,
-                                    int* splits, cudaStream_t st);
+                                    int parts, int* splits, cudaStream_t st);
 // Exact rescoring of c candidate pages [nq, kv, c] (ascending) and selection of the best
 // k = min(budget, c) into desc.pages, ascending; `exact` holds nq * kv * c floats.
 cudaError_t launch_quest_rerank(const pbk_quest_desc& d, const int32_t* cand, int c, float* exact, cudaStream_t st);

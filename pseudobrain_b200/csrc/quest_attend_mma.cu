@@ -131,13 +131,23 @@ __device__ __forceinline__ void stage_tile(WarpSmem& ws, int s, int b, int lane,
 
 __global__ void __launch_bounds__(32 * kWarps, 3)
     quest_attend_mma_kernel(const pbk_quest_desc d, int k, int tail, int split_keys, int sr, int splits, float* part,
-                            SinkKeys sk) {
+                            SinkKeys sk, int task0, int task_end) {
   extern __shared__ __align__(16) uint8_t attn_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpSmem& ws = reinterpret_cast<WarpSmem*>(attn_raw)[warp];
-  const int task = blockIdx.x * kWarps + warp;
-  if (task >= d.nq * d.kv * splits) return;
-  const int split = task % splits, n = task / splits / d.kv, h = task / splits % d.kv;
+  // tasks: the retrieved splits of every (query, key head), then their window splits
+  const int task = task0 + blockIdx.x * kWarps + warp;
+  if (task >= task_end) return;
+  const int ret_tasks = d.nq * d.kv * sr, sw = splits - sr;
+  int split, pair;
+  if (task < ret_tasks) {
+    split = task % sr;
+    pair = task / sr;
+  } else {
+    split = sr + (task - ret_tasks) % sw;
+    pair = (task - ret_tasks) / sw;
+  }
+  const int n = pair / d.kv, h = pair % d.kv;
   const int g = lane >> 2, t = lane & 3;
   const int groups = d.h / d.kv, rows = d.t * groups;
   const int n_ret = sk.n + k * d.page + tail;
@@ -304,13 +314,13 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
 // queries of a key head (only the mask differs), so they are staged once per group.
 __global__ void __launch_bounds__(32 * kWarps, 3)
     quest_attend_n8_kernel(const pbk_quest_desc d, int k, int tail, int split_keys, int sr, int sw, int qpg,
-                           float* part, SinkKeys sk) {
+                           float* part, SinkKeys sk, int task0, int task_end) {
   extern __shared__ __align__(16) uint8_t attn_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpSmem& ws = reinterpret_cast<WarpSmem*>(attn_raw)[warp];
-  const int task = blockIdx.x * kWarps + warp;
-  const int ret_tasks = d.nq * d.kv * sr, ngroups = (d.nq + qpg - 1) / qpg;
-  if (task >= ret_tasks + ngroups * d.kv * sw) return;
+  const int task = task0 + blockIdx.x * kWarps + warp;
+  const int ret_tasks = d.nq * d.kv * sr;
+  if (task >= task_end) return;
   const bool win_split = task >= ret_tasks;
   int n0, h, split, nqt;  // first query, key head, split index, queries in the task
   if (!win_split) {
@@ -484,7 +494,7 @@ static int slots_for(const void* kernel, size_t smem, cudaError_t* err) {
 }
 
 cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, float* part, const SinkKeys& sk,
-                                    int* splits_out, cudaStream_t st) {
+                                    int parts, int* splits_out, cudaStream_t st) {
   const size_t smem = sizeof(WarpSmem) * kWarps;
   const int rpq = d.t * (d.h / d.kv);
   const bool n8 = rpq <= 8;
@@ -495,7 +505,8 @@ cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, fl
   if (e != cudaSuccess) return e;
   // Split length S in [256, 512] (a multiple of 16) that minimises waves x S, the launch's
   // length in key tiles: with `slots` resident blocks, the fewest waves, then the shortest
-  // splits. The 8-row kernel's window tasks serve qpg queries each.
+  // splits. The 8-row kernel's window tasks serve qpg queries each. A function of d only, so
+  // launches of the retrieved and the window tasks apart agree on it.
   const int n_ret = sk.n + k * d.page + tail;
   const int qpg = n8 ? 8 / rpq : 1;
   const int64_t pairs = (int64_t)d.nq * d.kv, wpairs = (int64_t)((d.nq + qpg - 1) / qpg) * d.kv;
@@ -509,13 +520,15 @@ cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, fl
   }
   const int sr = (n_ret + best - 1) / best, sw = (d.n_win + best - 1) / best;
   *splits_out = sr + sw;
-  if (sr + sw == 0) return cudaSuccess;
-  const int64_t tasks = pairs * sr + wpairs * sw;
-  const unsigned blocks = (unsigned)((tasks + kWarps - 1) / kWarps);
+  const int ret_tasks = (int)(pairs * sr), all_tasks = (int)(pairs * sr + wpairs * sw);
+  const int task0 = (parts & 1) ? 0 : ret_tasks, task_end = (parts & 2) ? all_tasks : ret_tasks;
+  if (task_end <= task0) return cudaSuccess;
+  const unsigned blocks = (unsigned)((task_end - task0 + kWarps - 1) / kWarps);
   if (n8)
-    quest_attend_n8_kernel<<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sw, qpg, part, sk);
+    quest_attend_n8_kernel<<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sw, qpg, part, sk, task0, task_end);
   else
-    quest_attend_mma_kernel<<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sr + sw, part, sk);
+    quest_attend_mma_kernel<<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sr + sw, part, sk, task0,
+                                                               task_end);
   return cudaGetLastError();
 }
 

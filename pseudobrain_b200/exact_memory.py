@@ -9,9 +9,12 @@ Same names and meanings as the reference (pseudobrain/exact_memory.py:20-152):
 
 plus the fused path of this build, which never materialises the gathered keys:
 
-    select_pages(...)     page scores + exact top-k   (pbk_quest_select)
-    attend_pages(...)     split-key exact attention over pages + tail + window (pbk_quest_attend)
-    retrieve_attend(...)  both, with the reference's mask (pseudobrain/transplant.py:612-628)
+    select_pages(...)         page scores + exact top-k   (pbk_quest_select)
+    attend_pages(...)         split-key exact attention over pages + tail + window (pbk_quest_attend)
+    select_attend_pages(...)  both, the window half overlapped with the top-k
+                              (pbk_quest_select_parts, pbk_quest_attend_parts)
+    retrieve_attend(...)      the same for one Archive, with the reference's mask
+                              (pseudobrain/transplant.py:612-628)
 
 Only the flat, single-level Quest mode runs here: ``superblock`` two-level selection
 and exact ``rerank`` raise NotImplementedError when the reference would take them.
@@ -199,6 +202,64 @@ def attend_pages(q: torch.Tensor, qpos: torch.Tensor, keys: torch.Tensor, values
     return out
 
 
+_SIDE: dict[int, torch.cuda.Stream] = {}
+
+
+def _side_stream(dev: torch.device) -> torch.cuda.Stream:
+    """One auxiliary high-priority stream per device (made on the first call, outside any
+    graph capture): the block scheduler dispatches its blocks before the default-priority
+    stream's."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx not in _SIDE:
+        _SIDE[idx] = torch.cuda.Stream(dev, priority=-1)
+    return _SIDE[idx]
+
+
+def select_attend_pages(q: torch.Tensor, qpos: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                        kmax: torch.Tensor, kmin: torch.Tensor, n_arch: int, page: int, budget: int,
+                        win_keys: torch.Tensor, win_values: torch.Tensor, kpos: torch.Tensor, window: int,
+                        sinks: int = 0, scale: float | None = None, out_dtype: torch.dtype = torch.float32):
+    """select_pages followed by attend_pages (same arguments and results: (pages, out)), with
+    the window half of the attention overlapped with the top-k selection: the page scores
+    first, then on a side stream the window keys' partials while the top-k runs, then the
+    selected pages' partials and the combine (pbk_quest_select_parts, pbk_quest_attend_parts).
+    The window half needs no selected page, and the top-k occupies one SM per (query, key head)
+    row, leaving the others idle. Graph capturable (fork and join through the side stream)."""
+    _require(kmax, "kmax")
+    _require(kmin, "kmin")
+    dev = q.device
+    nq, t, h, d = q.shape
+    kv = kmax.shape[0]
+    k = min(budget, n_arch // page)
+    pages = torch.empty(nq, kv, k, dtype=torch.int32, device=dev)
+    out = torch.empty(nq, t, h, d, dtype=out_dtype, device=dev)
+    sdesc = _desc(q, page, n_arch, budget, kmax=kmax, kmin=kmin, pages=pages)
+    adesc = _attend_desc(q, qpos, keys, values, n_arch, page, pages, win_keys, win_values, kpos, window, sinks,
+                         scale, out)
+    sws = _workspace(LIB.pbk_quest_select_workspace(sdesc), dev)
+    aws = _workspace(LIB.pbk_quest_attend_workspace(adesc), dev)
+    side = _side_stream(dev)
+    with torch.cuda.device(dev):
+        cur = torch.cuda.current_stream(dev)
+        check(LIB.pbk_quest_select_parts(sdesc, 1, sws.data_ptr(), sws.numel(), cur.cuda_stream),
+              "pbk_quest_select_parts (scores)")
+        # the top-k and the pages' attention on the high-priority side stream (the top-k's
+        # blocks are dispatched first), the window's attention beside them on this stream
+        side.wait_stream(cur)  # after the persistent score kernel, which holds every SM
+        check(LIB.pbk_quest_select_parts(sdesc, 2, sws.data_ptr(), sws.numel(), side.cuda_stream),
+              "pbk_quest_select_parts (top-k)")
+        check(LIB.pbk_quest_attend_parts(adesc, None, None, 0, 0, 0, 1, aws.data_ptr(), aws.numel(), side.cuda_stream),
+              "pbk_quest_attend_parts (pages)")
+        check(LIB.pbk_quest_attend_parts(adesc, None, None, 0, 0, 0, 2, aws.data_ptr(), aws.numel(), cur.cuda_stream),
+              "pbk_quest_attend_parts (window)")
+        cur.wait_stream(side)
+        check(LIB.pbk_quest_attend_parts(adesc, None, None, 0, 0, 0, 4, aws.data_ptr(), aws.numel(), cur.cuda_stream),
+              "pbk_quest_attend_parts (combine)")
+    # the current stream joined the side stream before the combine, so later work (and the
+    # allocator's reuse of the workspaces and `pages`) on it is ordered after the side stream
+    return pages, out
+
+
 def gather_pages(keys: torch.Tensor, values: torch.Tensor, n_arch: int, page: int, pages: torch.Tensor,
                  q: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Keys/values of `pages` [nq,KV,sel] followed by the partial tail: [nq,KV,sel*page+tail,128]."""
@@ -286,7 +347,7 @@ def retrieve_attend(archive: Archive, q: torch.Tensor, groups: int, win_keys: to
     if full:
         _check_flat(archive, full, min(budget, full), is_decode)
     qi = q.to(torch.bfloat16)[0].transpose(0, 1).unsqueeze(0)
-    pages = select_pages(qi, archive.kmax[0], archive.kmin[0], archive.length, page, budget)
-    out = attend_pages(qi, qpos.to(torch.int32).view(1, t), archive.keys[0], archive.values[0], archive.length, page,
-                       pages, win_keys[0], win_values[0], kpos.to(torch.int32), window, sinks, out_dtype=out_dtype)
+    _, out = select_attend_pages(qi, qpos.to(torch.int32).view(1, t), archive.keys[0], archive.values[0],
+                                 archive.kmax[0], archive.kmin[0], archive.length, page, budget, win_keys[0],
+                                 win_values[0], kpos.to(torch.int32), window, sinks, out_dtype=out_dtype)
     return out[0].transpose(0, 1).unsqueeze(0)

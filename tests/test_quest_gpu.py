@@ -208,3 +208,33 @@ def test_quest_rejects_bad_arguments(cuda_device):
                        kmax[:2, :5])
     with pytest.raises(RuntimeError):
         M.select_pages(q.cpu(), kmax, kmax, 160, 16, 4)
+
+
+def test_select_attend_pages_equals_select_then_attend(cuda_device):
+    """select_attend_pages (window attention on a side stream beside the top-k) gives exactly
+    select_pages + attend_pages (the same kernels over the same workspace layout), eagerly and
+    replayed from a CUDA graph."""
+    from pseudobrain_b200 import exact_memory as M
+    from pseudobrain_b200.synthetic import quest_inputs
+    xq = quest_inputs(device=cuda_device, seed=17, n_tokens=1 << 16, kv=4, heads=16, d=128, page=16, window=512,
+                      nq=4, budget_tokens=1024)
+    args = (xq["q"], xq["qpos"], xq["keys"], xq["values"], xq["kmax"], xq["kmin"], xq["n_arch"], xq["page"],
+            xq["budget"], xq["win_keys"], xq["win_values"], xq["kpos"], xq["window"])
+    pages = M.select_pages(xq["q"], xq["kmax"], xq["kmin"], xq["n_arch"], xq["page"], xq["budget"])
+    out = M.attend_pages(xq["q"], xq["qpos"], xq["keys"], xq["values"], xq["n_arch"], xq["page"], pages,
+                         xq["win_keys"], xq["win_values"], xq["kpos"], xq["window"])
+    p2, o2 = M.select_attend_pages(*args)
+    assert torch.equal(p2, pages) and torch.equal(o2, out)
+    holder = {}
+
+    def step():
+        holder["r"] = M.select_attend_pages(*args)
+
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(holder["r"][0], pages) and torch.equal(holder["r"][1], out)
