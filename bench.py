@@ -282,26 +282,19 @@ def measure_quest(args, timed, dev, rank, world, pk):
     xq = quest_inputs(device=dev, seed=3 + 1000 * rank, **Q)
     kv, npages = Q["kv"], xq["kmax"].shape[1]
 
-    def retrieve_attend(q):
-        return M.select_attend_pages(q, xq["qpos"], xq["keys"], xq["values"], xq["kmax"], xq["kmin"], xq["n_arch"],
-                                 xq["page"], xq["budget"], xq["win_keys"], xq["win_values"], xq["kpos"], xq["window"])
+    def retrieve_attend(q):  # select_pages then attend_pages, one stream
+        pages = M.select_pages(q, xq["kmax"], xq["kmin"], xq["n_arch"], xq["page"], xq["budget"])
+        return pages, M.attend_pages(q, xq["qpos"], xq["keys"], xq["values"], xq["n_arch"], xq["page"], pages,
+                                     xq["win_keys"], xq["win_values"], xq["kpos"], xq["window"])
 
-    def step():  # scores, then the window attention beside the top-k, the pages' attention, combine
+    def step():
         retrieve_attend(xq["q"])
-
-    def step_sequential():  # select_pages then attend_pages on one stream
-        pages = M.select_pages(xq["q"], xq["kmax"], xq["kmin"], xq["n_arch"], xq["page"], xq["budget"])
-        M.attend_pages(xq["q"], xq["qpos"], xq["keys"], xq["values"], xq["n_arch"], xq["page"], pages,
-                       xq["win_keys"], xq["win_values"], xq["kpos"], xq["window"])
 
     qsteps = max(args.steps, 20)
     t_eager = timed(step, qsteps, max(args.warmup, 3))
-    replay, graph = graphed(torch, step)  # the 5 launches of a batch replayed as a CUDA graph
+    replay, graph = graphed(torch, step)  # the 4 launches of a batch replayed as a CUDA graph
     t = timed(replay, qsteps, max(args.warmup, 3))
     del graph
-    replay_seq, graph_seq = graphed(torch, step_sequential)
-    t_seq = timed(replay_seq, qsteps, max(args.warmup, 3))
-    del graph_seq
     per_step = t / qsteps
     bound_bytes = 2 * npages * kv * Q["d"] * 2
     page_bytes = xq["budget"] * Q["page"] * kv * Q["d"] * 2 * 2
@@ -323,17 +316,14 @@ def measure_quest(args, timed, dev, rank, world, pk):
     return {
         "metric": "Quest q/s (config 3)", "value": world * Q["nq"] * qsteps / t, "unit": "q/s",
         "us_per_batch": per_step * 1e6, "us_per_batch_eager": t_eager / qsteps * 1e6,
-        "us_per_batch_sequential": t_seq / qsteps * 1e6,
-        "timing": "CUDA-graph replay of the batch (select_attend_pages: the window attention overlaps the top-k); "
-                  "the eager figure includes the host's launch cost; the sequential one is select_pages then "
-                  "attend_pages on one stream",
+        "timing": "CUDA-graph replay of the batch; the eager figure includes the host's launch cost",
         "roofline": {"bound": "hbm", "achieved": nbytes / per_step / 1e9, "peak": pk["hbm"], "unit": "GB/s",
                      "frac": nbytes / per_step / 1e9 / pk["hbm"], "traffic": traffic("quest_score_tc_kernel"),
                      "algorithmic_bytes": nbytes},
         "select_gbps": bound_bytes / (t_sel / qsteps) / 1e9,
         "e2e": {"value": world * Q["nq"] * qsteps / t_e2e, "unit": "q/s",
                 "h2d_bytes_per_step": host_q.numel() * 2, "d2h_bytes_per_step": host_out.numel() * 4},
-        "gpu_launches": 5 * qsteps,
+        "gpu_launches": 4 * qsteps,
     }
 
 
