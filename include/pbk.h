@@ -330,6 +330,44 @@ PBK_API int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d,
                              int64_t key_stride_kv, int64_t key_stride_n, void* kmax, void* kmin,
                              int64_t bnd_stride_kv, int64_t bnd_stride_p, int32_t first_page, void* stream);
 
+/* Super-block bounds (exact_memory.py:53-63 _superbounds; pb27_vllm/memory.py:280-306
+ * _update_superbounds): for super-blocks s in [first_sb, min(end_sb, ceil(n_blk / sblk))),
+ * smax[h][s] = elementwise max of kmax[h][b] and smin[h][s] = min of kmin[h][b] over the
+ * blocks b in [s * sblk, min(n_blk, (s + 1) * sblk)). Page bounds [kv, >= n_blk, d] and
+ * super-block bounds [kv, *, d] are bf16 with element strides. */
+PBK_API int pbk_quest_superbounds(const void* kmax, const void* kmin, int32_t kv, int32_t n_blk, int32_t d,
+                                  int32_t sblk, int64_t bnd_stride_kv, int64_t bnd_stride_p, void* smax, void* smin,
+                                  int64_t sb_stride_kv, int64_t sb_stride_p, int32_t first_sb, int32_t end_sb,
+                                  void* stream);
+
+/* Options of pbk_quest_select_levels. */
+typedef struct pbk_quest_levels {
+  const void* smax;         /* bf16 super-block bounds [kv, >= ceil(full / sblk), d]; NULL: one level */
+  const void* smin;
+  int64_t sb_stride_kv, sb_stride_p;
+  int32_t sblk;             /* pages per super-block (>= 2 with smax) */
+  int32_t m_sb;             /* super-blocks kept, 1 .. ceil(full / sblk); the reference takes
+                               min(max(16, ceil(2 k / sblk)), ceil(full / sblk)) */
+  int32_t hole_lo, hole_hi; /* pages [hole_lo, hole_hi) score -inf (hole_hi <= hole_lo: no hole) */
+  int32_t pad_;
+} pbk_quest_levels;
+
+/* Page selection with the reference's other scoring modes, full = n_arch / page pages:
+ * - two levels (lv->smax given; exact_memory.py:107-122, pb27_vllm/memory.py:802-836): the
+ *   m_sb super-blocks of highest bound score (the page score formula on smax/smin over
+ *   super-blocks 0 .. ceil(full / sblk) - 1, ties to the lowest), then the bound scores of
+ *   their pages s * sblk + j, those at or past `full` or inside the hole scoring -inf, and
+ *   the best k = min(budget, full, m_sb * sblk) of those candidates;
+ * - one level with a hole (lv->smax NULL; memory.py:848-853): pbk_quest_select's scores with
+ *   the hole's pages at -inf, best k = min(budget, full).
+ * Ties go to the lowest candidate (page) index; the k pages go to desc->pages [nq, kv, k] in
+ * ascending order. A caller whose hole leaves fewer than budget valid pages passes the
+ * smaller budget, as the reference does (memory.py:788). desc->scores is not used. Workspace
+ * bytes from pbk_quest_select_levels_workspace(desc, lv). */
+PBK_API size_t pbk_quest_select_levels_workspace(const pbk_quest_desc* desc, const pbk_quest_levels* lv);
+PBK_API int pbk_quest_select_levels(const pbk_quest_desc* desc, const pbk_quest_levels* lv, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * Causal sliding-window attention with sinks (the hybrid model's attention branch,
  * pseudobrain/transplant.py:417-436 causal_attention and its exact chunked form

@@ -1,7 +1,8 @@
 """Quest page-bounded exact memory, restated in numpy. TEST INFRASTRUCTURE ONLY.
 
-Follows pseudobrain/exact_memory.py (flat, single-level mode: ``superblock=0``,
-``rerank=0``, ``neighbors=0``) and the exact attention of its caller
+Follows pseudobrain/exact_memory.py (the flat mode in ``retrieve``; the two-level
+super-block selection, the exact rerank, ``prompt_top`` and ``neighbors`` in
+``retrieve_modes``) and the exact attention of its caller
 pseudobrain/transplant.py:612-628. Layouts: keys/values [B,KV,N,D], page bounds
 [B,KV,P,D], queries [B,H,T,D] with H = KV * groups (head h reads key head
 h // groups).
@@ -121,6 +122,106 @@ def retrieve(archive: Archive | None, q: np.ndarray, groups: int, page: int, bud
         parts_k.append(archive.keys[:, :, full * page:])
         parts_v.append(archive.values[:, :, full * page:])
     return np.concatenate(parts_k, axis=2), np.concatenate(parts_v, axis=2), top
+
+
+def super_bounds(kmax: np.ndarray, kmin: np.ndarray, sblk: int) -> tuple[np.ndarray, np.ndarray]:
+    """Super-block bounds, exact_memory.py:53-63: the max of ``sblk`` consecutive page
+    maxima and the min of their minima; a trailing partial super-block is padded with its
+    last page, so it takes the bounds of the pages it holds. [..., P, D] -> [..., ceil(P/sblk), D]."""
+    p, d = kmax.shape[-2:]
+    pad = (-p) % sblk
+    if pad:
+        kmax = np.concatenate((kmax, np.repeat(kmax[..., -1:, :], pad, axis=-2)), axis=-2)
+        kmin = np.concatenate((kmin, np.repeat(kmin[..., -1:, :], pad, axis=-2)), axis=-2)
+    shape = kmax.shape[:-2] + (-1, sblk, d)
+    return kmax.reshape(shape).max(axis=-2), kmin.reshape(shape).min(axis=-2)
+
+
+def _bound_scores(qg: np.ndarray, bmax: np.ndarray, bmin: np.ndarray) -> np.ndarray:
+    """max over rows r of sum_d max(q_rd,0) bmax_pd + min(q_rd,0) bmin_pd: qg [..., R, D],
+    bmax/bmin [..., P, D] -> [..., P] (fp64 sums of the exact fp32 products)."""
+    q = qg.astype(np.float64)
+    pos, neg = np.maximum(q, 0), np.minimum(q, 0)
+    return (pos @ bmax.astype(np.float64).swapaxes(-1, -2) + neg @ bmin.astype(np.float64).swapaxes(-1, -2)).max(-2)
+
+
+def _topk_lowest(score: np.ndarray, k: int) -> np.ndarray:
+    """Indices of the k largest entries of each row (ties to the lowest index), ascending."""
+    order = np.argsort(-score.astype(np.float64), axis=-1, kind="stable")[..., :k]
+    return np.sort(order, axis=-1)
+
+
+def select_two_level(qg: np.ndarray, kmax: np.ndarray, kmin: np.ndarray, smax: np.ndarray, smin: np.ndarray,
+                     full: int, k: int, sblk: int, hole: tuple[int, int] = (0, 0)) -> np.ndarray:
+    """Two-level Quest selection, exact_memory.py:107-122 (pb27_vllm/memory.py:802-836 with its
+    archive hole): score the ceil(full/sblk) super-blocks on smax/smin, keep
+    m_sb = min(max(16, ceil(2k/sblk)), n_sb) of them, score their pages (pages at or past
+    ``full`` and pages in [hole) score -inf; indices clamp to full-1) and keep the best
+    min(k, m_sb*sblk). qg [..., R, D] query rows of each key head; bounds [..., P, D].
+    Ties go to the lowest index at both levels. Returns [..., k'] page indices, ascending."""
+    n_sb = (full + sblk - 1) // sblk
+    sb_score = _bound_scores(qg, smax[..., :n_sb, :], smin[..., :n_sb, :])
+    m_sb = min(max(16, (2 * k + sblk - 1) // sblk), n_sb)
+    top_sb = _topk_lowest(sb_score, m_sb)                                    # ascending
+    raw = (top_sb[..., :, None] * sblk + np.arange(sblk)).reshape(top_sb.shape[:-1] + (m_sb * sblk,))
+    idx = np.minimum(raw, full - 1)
+    bmax = np.take_along_axis(kmax[..., :full, :], idx[..., None], axis=-2)
+    bmin = np.take_along_axis(kmin[..., :full, :], idx[..., None], axis=-2)
+    sub = _bound_scores(qg, bmax, bmin)
+    invalid = (raw >= full) | ((idx >= hole[0]) & (idx < hole[1]))
+    sub = np.where(invalid, -np.inf, sub)
+    keep = _topk_lowest(sub, min(k, m_sb * sblk))
+    return np.take_along_axis(idx, keep, axis=-1)
+
+
+def rerank_pages(qg: np.ndarray, keys: np.ndarray, cand: np.ndarray, page: int, k: int) -> np.ndarray:
+    """Exact rerank, exact_memory.py:126-133: candidate page c scores the max over the head's
+    query rows and the page's tokens of q.k; keep the best k (ties to the lowest candidate
+    position). qg [..., R, D], keys [..., N, D], cand [..., c] ascending -> [..., k] ascending."""
+    idx = (cand[..., :, None] * page + np.arange(page)).reshape(cand.shape[:-1] + (-1,))
+    ck = np.take_along_axis(keys, idx[..., None], axis=-2).astype(np.float64)
+    exact = (qg.astype(np.float64) @ ck.swapaxes(-1, -2)).max(-2).reshape(cand.shape + (page,)).max(-1)
+    return np.take_along_axis(cand, _topk_lowest(exact, k), axis=-1)
+
+
+def retrieve_modes(keys, values, kmax, kmin, q, groups: int, page: int, budget: int, superblock: int = 0,
+                   rerank: int = 0, neighbors: int = 0, prompt_top=None):
+    """retrieve, exact_memory.py:88-152, with its other modes: the two-level super-block
+    selection for decode queries (t <= 64, rerank <= k, superblock > 1, full > 16 superblock;
+    :107-122), the exact rerank of the best ``rerank`` pages (:126-133), a prompt selection
+    prepended to a decode selection (:138-140) and ``neighbors`` following pages (:141-143).
+    keys/values [B,KV,N,D], bounds [B,KV,P,D], q [B,H,T,D]. Returns (keys, values, top)."""
+    b, h, t, d = q.shape
+    kv = h // groups
+    n = keys.shape[2]
+    full, tail = n // page, n % page
+    qg = q.astype(np.float32).reshape(b, kv, groups * t, d)
+    parts_k, parts_v = [], []
+    top = np.zeros((b, kv, 0), dtype=np.int64)
+    if full:
+        k = min(budget, full)
+        if t <= 64 and rerank <= k and superblock > 1 and full > superblock * 16:
+            smax, smin = super_bounds(kmax, kmin, superblock)
+            top = select_two_level(qg, kmax, kmin, smax, smin, full, k, superblock)
+        else:
+            score = _bound_scores(qg, kmax[:, :, :full], kmin[:, :, :full])
+            if rerank > k:
+                cand = _topk_lowest(score, min(rerank, full))
+                top = rerank_pages(qg, keys, cand, page, k)
+            else:
+                top = _topk_lowest(score, k)
+        if t <= 64 and prompt_top is not None:
+            top = np.concatenate((np.minimum(prompt_top, full - 1), top), axis=-1)
+        if neighbors:
+            top = np.concatenate([top] + [np.minimum(top + j, full - 1) for j in range(1, neighbors + 1)], axis=-1)
+        top = np.sort(top, axis=-1)
+        idx = (top[..., None] * page + np.arange(page)).reshape(b, kv, -1)
+        parts_k.append(np.take_along_axis(keys, idx[..., None], axis=2))
+        parts_v.append(np.take_along_axis(values, idx[..., None], axis=2))
+    if tail:
+        parts_k.append(keys[:, :, full * page:])
+        parts_v.append(values[:, :, full * page:])
+    return np.concatenate(parts_k, axis=2), np.concatenate(parts_v, axis=2), top.astype(np.int64)
 
 
 def window_mask(qpos: np.ndarray, kpos: np.ndarray, window: int, sinks: int) -> np.ndarray:

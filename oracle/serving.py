@@ -2,10 +2,12 @@
 TEST INFRASTRUCTURE ONLY.
 
 Follows serving/pb27_vllm/pb27_vllm/memory.py:
-* ``retrieve_blocks`` (:760-878) in its flat mode: bound scores of the full blocks of an
+* ``retrieve_blocks`` (:760-878): bound scores of the full blocks of an
   archive [KV, cap, D] whose blocks start after ORIGIN sink positions (:764, :845-853),
   ``topk(k)`` (:877) or, with ``rerank``, the ``rerank_pool`` best blocks by bound
-  rescored exactly (max over query rows and block tokens of q.k, :854-872), then sorted.
+  rescored exactly (max over query rows and block tokens of q.k, :854-872), then sorted;
+  the two-level super-block selection (:802-839), the archive hole (:769-777) and block
+  neighbours (:873-875).
   Budget: decode_blocks when reranking, else blocks (:779-780); the SCALE thresholds
   (:781-787) only raise it for archives of more than 2048 blocks.
 * ``piece_attention`` (:1311-1490), SDPA branch with own=None: keys are the sinks
@@ -41,29 +43,64 @@ def budget(memory: dict, full: int, rerank: bool, prompt_len: int, limit: int) -
     return b
 
 
-def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_len):
-    """keys [KV, cap, D]; kmax/kmin [KV, n_blk, D]; q [T, H, D] -> [KV, k] block indices or None."""
+def super_bounds(kmax, kmin, n_blk: int, sblk: int):
+    """Archive._update_superbounds (memory.py:280-306) over blocks [0, n_blk): super-block s
+    takes the max of the maxima and the min of the minima of blocks [s sblk, min(n_blk,
+    (s+1) sblk))."""
+    n_sb = (n_blk + sblk - 1) // sblk
+    smax = np.stack([kmax[:, s * sblk:min(n_blk, (s + 1) * sblk)].max(1) for s in range(n_sb)], axis=1)
+    smin = np.stack([kmin[:, s * sblk:min(n_blk, (s + 1) * sblk)].min(1) for s in range(n_sb)], axis=1)
+    return smax, smin
+
+
+def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_len, smax=None, smin=None, sblk=0,
+                    hole=(0, 0)):
+    """keys [KV, cap, D]; kmax/kmin [KV, n_blk, D]; q [T, H, D] -> [KV, k] block indices or None.
+
+    With smax/smin [KV, n_sb, D] and sblk > 1, a call without rerank over more than 16 sblk
+    full blocks takes the two-level selection (memory.py:802-839). ``hole`` = (hole_lo,
+    hole_hi) archive positions whose blocks score -inf (memory.py:769-777, 834-835, 852-853);
+    memory["neighbors"] adds the following blocks (:873-875)."""
+    from .quest import select_two_level
     block = memory["block_size"]
     full = (limit - ORIGIN) // block
     if full <= 0:
         return None
     t, h, d = q.shape
     kv = h // groups
-    k = min(budget(memory, full, rerank, prompt_len, limit), full)
+    n_valid, hb0, hb1 = full, 0, 0
+    if hole[1] > hole[0]:
+        hb0 = max(0, hole[0] - ORIGIN) // block
+        hb1 = min(full, (hole[1] - ORIGIN + block - 1) // block)
+        if hb1 > hb0:
+            n_valid = full - (hb1 - hb0)
+        if n_valid <= 0:
+            return None
+    k = min(budget(memory, full, rerank, prompt_len, limit), n_valid)
     qg = np.asarray(q, np.float64).transpose(1, 0, 2).reshape(kv, groups * t, d)   # [KV, G*T, D]
+    nb = memory.get("neighbors", 0)
+
+    def with_neighbors(top):
+        if nb:
+            top = np.concatenate([top] + [np.minimum(top + j, full - 1) for j in range(1, nb + 1)], axis=-1)
+        return np.sort(top, axis=-1)
+
+    if not rerank and sblk > 1 and smax is not None and full > sblk * 16:
+        return with_neighbors(select_two_level(qg, kmax, kmin, smax, smin, full, k, sblk, (hb0, hb1)))
     pos, neg = np.maximum(qg, 0), np.minimum(qg, 0)
     score = (np.einsum("grd,gnd->grn", pos, kmax[:, :full].astype(np.float64))
              + np.einsum("grd,gnd->grn", neg, kmin[:, :full].astype(np.float64))).max(1)      # [KV, full]
+    score[:, hb0:hb1] = -np.inf
     pool = max(memory["rerank"], 2 * k) if memory["rerank"] > 0 else 0
     if rerank and pool > k:
-        c = min(pool, full)
+        c = min(pool, n_valid)
         cand = _topk_sorted(score, c)                                                   # [KV, c] ascending
         blk = keys[:, ORIGIN:ORIGIN + full * block].reshape(kv, full, block, d).astype(np.float64)
         ck = np.take_along_axis(blk, cand[:, :, None, None], axis=1)                    # [KV, c, block, D]
         exact = np.einsum("grd,gcsd->grcs", qg, ck).max(axis=(1, 3))                   # [KV, c]
         keep = _topk_sorted(exact, k)
-        return np.take_along_axis(cand, keep, axis=1)
-    return _topk_sorted(score, k)
+        return with_neighbors(np.take_along_axis(cand, keep, axis=1))
+    return with_neighbors(_topk_sorted(score, k))
 
 
 def piece_attention(keys, values, q, q_pos, top, groups, window, scale, block):

@@ -78,7 +78,14 @@ class PbkSwaDesc(ctypes.Structure):
                 ("q", PbkView), ("k", PbkView), ("v", PbkView), ("o", PbkView)]
 
 
+class PbkQuestLevels(ctypes.Structure):
+    _fields_ = [("smax", ctypes.c_void_p), ("smin", ctypes.c_void_p), ("sb_stride_kv", ctypes.c_int64),
+                ("sb_stride_p", ctypes.c_int64), ("sblk", ctypes.c_int32), ("m_sb", ctypes.c_int32),
+                ("hole_lo", ctypes.c_int32), ("hole_hi", ctypes.c_int32), ("pad_", ctypes.c_int32)]
+
+
 _QD = ctypes.POINTER(PbkQuestDesc)
+_QL = ctypes.POINTER(PbkQuestLevels)
 _VP, _I32, _I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
 
 # name -> (restype, argtypes); every symbol include/pbk.h declares.
@@ -113,6 +120,10 @@ SIGNATURES = {
     "pbk_quest_rerank": (ctypes.c_int, [_QD, _VP, _I32, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_gather": (ctypes.c_int, [_QD, _I32, _VP, _VP, _VP]),
     "pbk_quest_bounds": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I64, _I64, _VP, _VP, _I64, _I64, _I32, _VP]),
+    "pbk_quest_superbounds": (ctypes.c_int, [_VP, _VP, _I32, _I32, _I32, _I32, _I64, _I64, _VP, _VP, _I64, _I64,
+                                             _I32, _I32, _VP]),
+    "pbk_quest_select_levels_workspace": (ctypes.c_size_t, [_QD, _QL]),
+    "pbk_quest_select_levels": (ctypes.c_int, [_QD, _QL, _VP, ctypes.c_size_t, _VP]),
     "pbk_swa_prefill": (ctypes.c_int, [ctypes.POINTER(PbkSwaDesc), _VP]),
 }
 

@@ -453,6 +453,58 @@ int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d, int32_t
                                   bnd_stride_p, first_page, static_cast<cudaStream_t>(stream)));
 }
 
+int pbk_quest_superbounds(const void* kmax, const void* kmin, int32_t kv, int32_t n_blk, int32_t d, int32_t sblk,
+                          int64_t bnd_stride_kv, int64_t bnd_stride_p, void* smax, void* smin, int64_t sb_stride_kv,
+                          int64_t sb_stride_p, int32_t first_sb, int32_t end_sb, void* stream) {
+  if (kv < 1 || n_blk < 0 || sblk < 1 || first_sb < 0) return PBK_ERR_INVALID;
+  if (d != 128) return PBK_ERR_SHAPE;
+  if (n_blk == 0 || end_sb <= first_sb || first_sb * (int64_t)sblk >= n_blk) return PBK_OK;
+  if (!kmax || !kmin || !smax || !smin) return PBK_ERR_INVALID;
+  if (!aligned16(kmax) || !aligned16(kmin) || !aligned16(smax) || !aligned16(smin) || bnd_stride_kv % 8 ||
+      bnd_stride_p % 8 || sb_stride_kv % 8 || sb_stride_p % 8)
+    return PBK_ERR_ALIGN;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_quest_superbounds(kmax, kmin, kv, n_blk, sblk, bnd_stride_kv, bnd_stride_p, smax,
+                                                     smin, sb_stride_kv, sb_stride_p, first_sb, end_sb,
+                                                     static_cast<cudaStream_t>(stream)));
+}
+
+namespace {
+int validate_levels(const pbk_quest_desc* d, const pbk_quest_levels* lv) {
+  int st = validate_quest(d, 1);
+  if (st != PBK_OK) return st;
+  if (lv == nullptr) return PBK_ERR_INVALID;
+  if (lv->smax == nullptr) return lv->smin == nullptr ? PBK_OK : PBK_ERR_INVALID;
+  const int full = d->n_arch / d->page;
+  if (!lv->smin || lv->sblk < 2) return PBK_ERR_INVALID;
+  const int n_sb = (full + lv->sblk - 1) / lv->sblk;
+  if (full > 0 && (lv->m_sb < 1 || lv->m_sb > n_sb)) return PBK_ERR_INVALID;
+  if ((int64_t)lv->m_sb * lv->sblk > INT32_MAX / 2) return PBK_ERR_SHAPE;
+  if (!aligned16(lv->smax) || !aligned16(lv->smin) || !aligned_elems(lv->sb_stride_kv, 8) ||
+      !aligned_elems(lv->sb_stride_p, 8))
+    return PBK_ERR_ALIGN;
+  return PBK_OK;
+}
+}  // namespace
+
+size_t pbk_quest_select_levels_workspace(const pbk_quest_desc* desc, const pbk_quest_levels* lv) {
+  if (validate_levels(desc, lv) != PBK_OK) return 0;
+  return round_up(pbk::quest_levels_bytes(*desc, *lv));
+}
+
+int pbk_quest_select_levels(const pbk_quest_desc* desc, const pbk_quest_levels* lv, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  int st = validate_levels(desc, lv);
+  if (st != PBK_OK) return st;
+  if (desc->nq == 0 || desc->n_arch / desc->page == 0 || desc->budget == 0) return PBK_OK;
+  const size_t need = pbk::quest_levels_bytes(*desc, *lv);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return PBK_ERR_WORKSPACE;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return launch_status(pbk::launch_quest_select_levels(*desc, *lv, static_cast<uint8_t*>(workspace),
+                                                       static_cast<cudaStream_t>(stream)));
+}
+
 int pbk_swa_prefill(const pbk_swa_desc* desc, void* stream) {
   int st = validate_swa(desc);
   if (st != PBK_OK || desc->batch == 0 || desc->seqlen == 0) return st;

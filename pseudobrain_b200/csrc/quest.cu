@@ -713,6 +713,109 @@ __global__ void quest_map_kernel(const int32_t* cand, int c, int k, int nrows, i
 }
 
 // ---------------------------------------------------------------------------------
+// Super-block bounds (exact_memory.py:53-63, memory.py:280-306): warp per (super-block,
+// key head), lane l owns dims 4l..4l+3; max of the blocks' maxima, min of their minima.
+// ---------------------------------------------------------------------------------
+__global__ void quest_superbounds_kernel(const bf16* kmax, const bf16* kmin, int64_t bs_kv, int64_t bs_p, int n_blk,
+                                         int sblk, bf16* smax, bf16* smin, int64_t ss_kv, int64_t ss_p, int first_sb,
+                                         int nsb) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= nsb) return;
+  const int s = first_sb + warp, h = blockIdx.y;
+  const int b0 = s * sblk, b1 = min(b0 + sblk, n_blk);
+  float mx[4], mn[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mx[i] = -FLT_MAX, mn[i] = FLT_MAX;
+  for (int b = b0; b < b1; ++b) {
+    const int64_t off = h * bs_kv + (int64_t)b * bs_p + 4 * lane;
+    const uint2 ra = *reinterpret_cast<const uint2*>(kmax + off);
+    const uint2 rb = *reinterpret_cast<const uint2*>(kmin + off);
+    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&ra);
+    const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&rb);
+    const float2 a0 = __bfloat1622float2(pa[0]), a1 = __bfloat1622float2(pa[1]);
+    const float2 c0 = __bfloat1622float2(pb[0]), c1 = __bfloat1622float2(pb[1]);
+    const float va[4] = {a0.x, a0.y, a1.x, a1.y}, vb[4] = {c0.x, c0.y, c1.x, c1.y};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mx[i] = fmaxf(mx[i], va[i]), mn[i] = fminf(mn[i], vb[i]);
+  }
+  bf16* omx = smax + h * ss_kv + (int64_t)s * ss_p + 4 * lane;
+  bf16* omn = smin + h * ss_kv + (int64_t)s * ss_p + 4 * lane;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // max/min of bf16 values are bf16 values: exact
+    omx[i] = __float2bfloat16_rn(mx[i]);
+    omn[i] = __float2bfloat16_rn(mn[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Candidate scores of the two-level selection (exact_memory.py:113-121, memory.py:814-835):
+// candidate c of row (group n, key head h) is page idx = min(raw, full - 1), raw =
+// top_sb[c / sblk] * sblk + c % sblk; its score is the page bound score, -inf when raw >=
+// full or idx lies in [hole0, hole1). top_sb ascending makes the candidates' pages
+// non-decreasing in c. CTA = (128 candidates, row); thread = candidate; the group's query
+// rows pass through shared memory 32 at a time.
+// ---------------------------------------------------------------------------------
+constexpr int kSubRows = 32;
+__global__ void __launch_bounds__(kScoreThreads) quest_sub_score_kernel(const pbk_quest_desc d, const int32_t* top_sb,
+                                                                       int m_sb, int sblk, int full, int hole0,
+                                                                       int hole1, float* scores, int32_t* cand) {
+  __shared__ __align__(16) float qs[kSubRows][kD];
+  const int row = blockIdx.y, n = row / d.kv, h = row % d.kv, groups = d.h / d.kv, rows = d.t * groups;
+  const int nc = m_sb * sblk, c = blockIdx.x * kScoreThreads + threadIdx.x;
+  const bool live = c < nc;
+  const int cc = live ? c : nc - 1;
+  const int raw = top_sb[(int64_t)row * m_sb + cc / sblk] * sblk + cc % sblk;
+  const int idx = min(raw, full - 1);
+  const bool valid = raw < full && !(idx >= hole0 && idx < hole1);
+  const bf16* bmax = reinterpret_cast<const bf16*>(d.kmax) + h * d.bnd_stride_kv + (int64_t)idx * d.bnd_stride_p;
+  const bf16* bmin = reinterpret_cast<const bf16*>(d.kmin) + h * d.bnd_stride_kv + (int64_t)idx * d.bnd_stride_p;
+  float best = -INFINITY;
+  for (int r0 = 0; r0 < rows; r0 += kSubRows) {
+    const int nr = min(kSubRows, rows - r0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < nr * kD; e += kScoreThreads) {
+      const int r = e / kD, dd = e % kD, ti = (r0 + r) / groups, g = (r0 + r) % groups;
+      qs[r][dd] = __bfloat162float(reinterpret_cast<const bf16*>(d.q)[n * d.q_stride_n + ti * d.q_stride_t +
+                                                                        (int64_t)(h * groups + g) * d.q_stride_h + dd]);
+    }
+    __syncthreads();
+    for (int rb = 0; rb < nr; rb += kRowBlock) {
+      const int nb = min(kRowBlock, nr - rb);
+      float acc[kRowBlock] = {0.f, 0.f, 0.f, 0.f};
+      for (int d0 = 0; d0 < kD; d0 += 8) {
+        float mx[8], mn[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmax + d0), mx);
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmin + d0), mn);
+#pragma unroll
+        for (int r = 0; r < kRowBlock; ++r) {
+          if (r < nb) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float qv = qs[rb + r][d0 + j];
+              acc[r] = fmaf(qv, qv > 0.f ? mx[j] : mn[j], acc[r]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kRowBlock; ++r)
+        if (r < nb) best = fmaxf(best, acc[r]);
+    }
+  }
+  if (!live) return;
+  scores[(int64_t)row * nc + c] = valid ? best : -INFINITY;
+  cand[(int64_t)row * nc + c] = idx;
+}
+
+// Pages [lo, hi) of every score row score -inf (the archive hole, memory.py:852-853).
+__global__ void quest_hole_kernel(float* scores, int npages, int nrows, int lo, int hi) {
+  const int w = hi - lo;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= (int64_t)nrows * w) return;
+  scores[(i / w) * npages + lo + i % w] = -INFINITY;
+}
+
+// ---------------------------------------------------------------------------------
 // Launch helpers (called from capi.cu after validation).
 // ---------------------------------------------------------------------------------
 int quest_k(const pbk_quest_desc& d) { return min(d.budget, d.n_arch / d.page); }
@@ -863,6 +966,100 @@ cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int page, int64
   quest_bounds_kernel<<<dim3((npages + 7) / 8, kv), 256, 0, st>>>(
       static_cast<const bf16*>(keys), n, page, ks_kv, ks_n, static_cast<bf16*>(kmax), static_cast<bf16*>(kmin), bs_kv,
       bs_p, first_page, npages);
+  return cudaGetLastError();
+}
+
+
+// ---------------------------------------------------------------------------------
+// Two-level and hole-masked selection (pbk_quest_select_levels).
+// ---------------------------------------------------------------------------------
+namespace {
+size_t round_ws(size_t bytes) { return (bytes + 255) / 256 * 256; }
+
+// The super-block descriptor: the page-score pass over smax/smin, m_sb kept into top_sb.
+pbk_quest_desc superblock_desc(const pbk_quest_desc& d, const pbk_quest_levels& lv, int32_t* top_sb) {
+  const int full = d.n_arch / d.page, n_sb = (full + lv.sblk - 1) / lv.sblk;
+  pbk_quest_desc ds = d;
+  ds.kmax = lv.smax;
+  ds.kmin = lv.smin;
+  ds.bnd_stride_kv = lv.sb_stride_kv;
+  ds.bnd_stride_p = lv.sb_stride_p;
+  ds.n_arch = n_sb * d.page;
+  ds.budget = lv.m_sb;
+  ds.pages = top_sb;
+  ds.scores = nullptr;
+  return ds;
+}
+
+cudaError_t launch_topk(const float* scores, int npages, int k, int nrows, int32_t* pages, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(quest_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(TopkSmem));
+  if (e != cudaSuccess) return e;
+  quest_topk_kernel<<<nrows, kTopkThreads, sizeof(TopkSmem), st>>>(scores, nullptr, npages, 0, k, pages);
+  return cudaGetLastError();
+}
+}  // namespace
+
+size_t quest_levels_bytes(const pbk_quest_desc& d, const pbk_quest_levels& lv) {
+  const size_t rows = (size_t)d.nq * d.kv;
+  const int full = d.n_arch / d.page;
+  if (lv.smax == nullptr) {  // scores, then the segment maxima of the score pass
+    pbk_quest_desc dd = d;
+    dd.scores = nullptr;
+    return round_ws(rows * full * sizeof(float)) + round_ws(rows * quest_nseg(dd) * sizeof(float));
+  }
+  const pbk_quest_desc ds = superblock_desc(d, lv, nullptr);
+  const size_t nc = (size_t)lv.m_sb * lv.sblk;
+  return round_ws(quest_score_bytes(ds)) + round_ws(rows * lv.m_sb * sizeof(int32_t)) +
+         round_ws(rows * nc * sizeof(float)) + round_ws(rows * nc * sizeof(int32_t));
+}
+
+cudaError_t launch_quest_select_levels(const pbk_quest_desc& d, const pbk_quest_levels& lv, uint8_t* ws,
+                                       cudaStream_t st) {
+  const int full = d.n_arch / d.page, k = quest_k(d), nrows = d.nq * d.kv;
+  if (full == 0 || k == 0 || nrows == 0) return cudaSuccess;
+  if (lv.smax == nullptr) {
+    float* scores = reinterpret_cast<float*>(ws);
+    pbk_quest_desc dd = d;
+    dd.scores = scores;
+    float* segmax = reinterpret_cast<float*>(ws + round_ws((size_t)nrows * full * sizeof(float)));
+    cudaError_t e = launch_quest_select_parts(dd, segmax, 1, st);
+    if (e != cudaSuccess) return e;
+    const int lo = max(lv.hole_lo, 0), hi = min(lv.hole_hi, full);
+    if (hi > lo) {
+      const int64_t n = (int64_t)nrows * (hi - lo);
+      quest_hole_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(scores, full, nrows, lo, hi);
+    }
+    return launch_topk(scores, full, k, nrows, d.pages, st);  // segment maxima may hold hole pages: not used
+  }
+  const int nc = lv.m_sb * lv.sblk, k2 = min(k, nc);
+  const pbk_quest_desc probe = superblock_desc(d, lv, nullptr);
+  uint8_t* p = ws;
+  float* sb_scratch = reinterpret_cast<float*>(p);
+  p += round_ws(quest_score_bytes(probe));
+  int32_t* top_sb = reinterpret_cast<int32_t*>(p);
+  p += round_ws((size_t)nrows * lv.m_sb * sizeof(int32_t));
+  float* sub = reinterpret_cast<float*>(p);
+  p += round_ws((size_t)nrows * nc * sizeof(float));
+  int32_t* cand = reinterpret_cast<int32_t*>(p);
+  cudaError_t e = launch_quest_select_parts(superblock_desc(d, lv, top_sb), sb_scratch, 3, st);
+  if (e != cudaSuccess) return e;
+  quest_sub_score_kernel<<<dim3((nc + kScoreThreads - 1) / kScoreThreads, nrows), kScoreThreads, 0, st>>>(
+      d, top_sb, lv.m_sb, lv.sblk, full, lv.hole_lo, lv.hole_hi, sub, cand);
+  e = launch_topk(sub, nc, k2, nrows, d.pages, st);
+  if (e != cudaSuccess) return e;
+  quest_map_kernel<<<(nrows * k2 + 255) / 256, 256, 0, st>>>(cand, nc, k2, nrows, d.pages);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quest_superbounds(const void* kmax, const void* kmin, int kv, int n_blk, int sblk, int64_t bs_kv,
+                                     int64_t bs_p, void* smax, void* smin, int64_t ss_kv, int64_t ss_p, int first_sb,
+                                     int end_sb, cudaStream_t st) {
+  const int nsb = min(end_sb, (n_blk + sblk - 1) / sblk) - first_sb;
+  if (nsb <= 0) return cudaSuccess;
+  quest_superbounds_kernel<<<dim3((nsb + 7) / 8, kv), 256, 0, st>>>(
+      static_cast<const bf16*>(kmax), static_cast<const bf16*>(kmin), bs_kv, bs_p, n_blk, sblk,
+      static_cast<bf16*>(smax), static_cast<bf16*>(smin), ss_kv, ss_p, first_sb, nsb);
   return cudaGetLastError();
 }
 

@@ -43,6 +43,13 @@ cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, fl
 // k = min(budget, c) into desc.pages, ascending; `exact` holds nq * kv * c floats.
 cudaError_t launch_quest_rerank(const pbk_quest_desc& d, const int32_t* cand, int c, float* exact, cudaStream_t st);
 cudaError_t launch_quest_gather(const pbk_quest_desc& d, int sel, void* ok, void* ov, cudaStream_t st);
+// Two-level / hole-masked selection (pbk_quest_select_levels): workspace bytes and launch.
+size_t quest_levels_bytes(const pbk_quest_desc& d, const pbk_quest_levels& lv);
+cudaError_t launch_quest_select_levels(const pbk_quest_desc& d, const pbk_quest_levels& lv, uint8_t* ws,
+                                       cudaStream_t st);
+cudaError_t launch_quest_superbounds(const void* kmax, const void* kmin, int kv, int n_blk, int sblk, int64_t bs_kv,
+                                     int64_t bs_p, void* smax, void* smin, int64_t ss_kv, int64_t ss_p, int first_sb,
+                                     int end_sb, cudaStream_t st);
 cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int page, int64_t ks_kv, int64_t ks_n, void* kmax,
                                 void* kmin, int64_t bs_kv, int64_t bs_p, int first_page, cudaStream_t st);
 }  // namespace pbk

@@ -16,10 +16,11 @@ plus the fused path of this build, which never materialises the gathered keys:
     retrieve_attend(...)      the same for one Archive, with the reference's mask
                               (pseudobrain/transplant.py:612-628)
 
-Only the flat, single-level Quest mode runs here: ``superblock`` two-level selection
-and exact ``rerank`` raise NotImplementedError when the reference would take them.
-Keys are bf16 with head_dim 128; every call runs CUDA kernels from libpbk.so and
-there is no CPU path.
+``retrieve`` takes every selection mode of the reference: flat, the two-level
+super-block selection of decode queries (pbk_quest_select_levels over the super-block
+bounds that ``archive_append`` keeps), the exact ``rerank`` (pbk_quest_rerank), a kept
+prompt selection and ``neighbors``. Keys are bf16 with head_dim 128; every call runs CUDA
+kernels from libpbk.so and there is no CPU path.
 """
 from __future__ import annotations
 
@@ -29,7 +30,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _capi
-from ._capi import LIB, PbkQuestDesc, check
+from ._capi import LIB, PbkQuestDesc, PbkQuestLevels, check
 
 EXACT_MEMORY = {"enabled": False, "blocks": 64, "block_size": 64, "decode_blocks": 64, "neighbors": 0, "rerank": 0,
                 "decode_rerank": 0, "superblock": 64, "keys_like_values": False}
@@ -95,17 +96,54 @@ def page_bounds(keys: torch.Tensor, page: int) -> tuple[torch.Tensor, torch.Tens
     return kmax, kmin
 
 
+def super_bounds_(kmax: torch.Tensor, kmin: torch.Tensor, n_blk: int, sblk: int, smax: torch.Tensor,
+                  smin: torch.Tensor, first_sb: int = 0, end_sb: int | None = None) -> None:
+    """Write the bounds of super-blocks [first_sb, end_sb) (all from first_sb when None) of
+    the pages [0, n_blk) of kmax/kmin [KV,P,hd] into smax/smin [KV,S,hd]: the max of sblk
+    consecutive page maxima and the min of their minima, a trailing partial super-block over
+    the pages it holds (reference: _superbounds, exact_memory.py:53-63;
+    Archive._update_superbounds, pb27_vllm/memory.py:280-306)."""
+    for t_, w in ((kmax, "kmax"), (kmin, "kmin"), (smax, "smax"), (smin, "smin")):
+        _require(t_, w)
+    kv, _, d = kmax.shape
+    n_sb = (n_blk + sblk - 1) // sblk
+    end = n_sb if end_sb is None else min(end_sb, n_sb)
+    if smax.shape != smin.shape or smax.shape[0] != kv or smax.shape[1] < end:
+        raise ValueError(f"super-block bounds {tuple(smax.shape)} too small for {end} super-blocks")
+    with torch.cuda.device(kmax.device):
+        check(LIB.pbk_quest_superbounds(kmax.data_ptr(), kmin.data_ptr(), kv, n_blk, d, sblk, kmax.stride(0),
+                                        kmax.stride(1), smax.data_ptr(), smin.data_ptr(), smax.stride(0),
+                                        smax.stride(1), first_sb, end, _stream(kmax)), "pbk_quest_superbounds")
+
+
+def super_bounds(kmax: torch.Tensor, kmin: torch.Tensor, sblk: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(smax, smin) [B,KV,ceil(P/sblk),hd] of page bounds [B,KV,P,hd] (exact_memory.py:53-63)."""
+    b, kv, p, d = kmax.shape
+    smax = torch.empty(b, kv, (p + sblk - 1) // sblk, d, dtype=kmax.dtype, device=kmax.device)
+    smin = torch.empty_like(smax)
+    for i in range(b):
+        super_bounds_(kmax[i], kmin[i], p, sblk, smax[i], smin[i])
+    return smax, smin
+
+
+def _superblock() -> int:
+    return int(EXACT_MEMORY.get("superblock", 64) or 0)
+
+
 def archive_append(archive: Archive | None, keys: torch.Tensor, values: torch.Tensor) -> Archive | None:
-    """Append evicted keys/values and refresh the bounds from the first incomplete page
-    on (reference: exact_memory.py:66-85). Super-block bounds are not kept (flat mode)."""
+    """Append evicted keys/values and refresh the page bounds from the first incomplete page
+    on, and the super-block bounds from the super-block holding it (reference:
+    exact_memory.py:66-85; super-blocks of EXACT_MEMORY["superblock"] pages when > 1)."""
     if keys.shape[2] == 0:
         return archive
     page = EXACT_MEMORY["block_size"]
+    sblk = _superblock()
     if EXACT_MEMORY["keys_like_values"]:
         keys = keys.to(values.dtype)
     if archive is None:
         kmax, kmin = page_bounds(keys, page)
-        return Archive(keys, values, kmax, kmin)
+        smax, smin = super_bounds(kmax, kmin, sblk) if sblk > 1 else (None, None)
+        return Archive(keys, values, kmax, kmin, smax, smin)
     full = archive.length // page
     new_k = torch.cat((archive.keys, keys), dim=2)
     new_v = torch.cat((archive.values, values), dim=2)
@@ -117,7 +155,19 @@ def archive_append(archive: Archive | None, keys: torch.Tensor, values: torch.Te
     kmin[:, :, :full] = archive.kmin[:, :, :full]
     for i in range(b):
         page_bounds_(new_k[i], page, kmax[i], kmin[i], first_page=full)
-    return Archive(new_k, new_v, kmax, kmin, None, None, archive.prompt_top)
+    smax = smin = None
+    if sblk > 1:
+        first_sb = full // sblk  # earlier super-blocks hold complete pages only: final
+        smax = torch.empty(b, kv, (p + sblk - 1) // sblk, d, dtype=kmax.dtype, device=kmax.device)
+        smin = torch.empty_like(smax)
+        if archive.smax is not None and archive.smin is not None and first_sb > 0:
+            smax[:, :, :first_sb] = archive.smax[:, :, :first_sb]
+            smin[:, :, :first_sb] = archive.smin[:, :, :first_sb]
+        else:
+            first_sb = 0
+        for i in range(b):
+            super_bounds_(kmax[i], kmin[i], p, sblk, smax[i], smin[i], first_sb)
+    return Archive(new_k, new_v, kmax, kmin, smax, smin, archive.prompt_top)
 
 
 def _desc(q: torch.Tensor, page: int, n_arch: int, budget: int, *, kmax=None, kmin=None, keys=None, values=None,
@@ -158,6 +208,63 @@ def select_pages(q: torch.Tensor, kmax: torch.Tensor, kmin: torch.Tensor, n_arch
     ws = _workspace(LIB.pbk_quest_select_workspace(desc), q.device)
     with torch.cuda.device(q.device):
         check(LIB.pbk_quest_select(desc, ws.data_ptr(), ws.numel(), _stream(q)), "pbk_quest_select")
+    return pages
+
+
+def m_superblocks(k: int, full: int, sblk: int) -> int:
+    """Super-blocks the two-level selection keeps for k pages (exact_memory.py:116,
+    pb27_vllm/memory.py:814): min(max(16, ceil(2k / sblk)), ceil(full / sblk))."""
+    return min(max(16, (2 * k + sblk - 1) // sblk), (full + sblk - 1) // sblk)
+
+
+def select_pages_levels(q: torch.Tensor, kmax: torch.Tensor, kmin: torch.Tensor, n_arch: int, page: int,
+                        budget: int, smax: torch.Tensor | None = None, smin: torch.Tensor | None = None,
+                        sblk: int = 0, hole: tuple[int, int] = (0, 0)) -> torch.Tensor:
+    """select_pages with the reference's other scoring modes (pbk_quest_select_levels): with
+    super-block bounds smax/smin [KV,S,128] and sblk > 1, the two-level selection
+    (exact_memory.py:107-122, pb27_vllm/memory.py:802-836): the best m_superblocks(k) super-
+    blocks, then the best min(k, m_sb * sblk) of their pages; pages [hole) score -inf
+    (memory.py:834-835, 852-853). k = min(budget, n_arch // page): a caller whose hole leaves
+    fewer pages passes the smaller budget. Returns int32 [nq, KV, k'] ascending."""
+    _require(kmax, "kmax")
+    _require(kmin, "kmin")
+    nq = q.shape[0]
+    kv = kmax.shape[0]
+    full = n_arch // page
+    k = min(budget, full)
+    lv = PbkQuestLevels(hole_lo=int(hole[0]), hole_hi=int(hole[1]))
+    if smax is not None:
+        _require(smax, "smax")
+        _require(smin, "smin")
+        if sblk < 2:
+            raise ValueError("two-level selection needs sblk >= 2")
+        lv.smax, lv.smin = smax.data_ptr(), smin.data_ptr()
+        lv.sb_stride_kv, lv.sb_stride_p = smax.stride(0), smax.stride(1)
+        lv.sblk = sblk
+        lv.m_sb = m_superblocks(k, full, sblk) if full else 0
+        k = min(k, lv.m_sb * sblk)
+    pages = torch.empty(nq, kv, k, dtype=torch.int32, device=q.device)
+    desc = _desc(q, page, n_arch, budget, kmax=kmax, kmin=kmin, pages=pages)
+    ws = _workspace(LIB.pbk_quest_select_levels_workspace(desc, lv), q.device)
+    with torch.cuda.device(q.device):
+        check(LIB.pbk_quest_select_levels(desc, lv, ws.data_ptr(), ws.numel(), _stream(q)), "pbk_quest_select_levels")
+    return pages
+
+
+def rerank_pages(q: torch.Tensor, keys: torch.Tensor, cand: torch.Tensor, page: int, k: int) -> torch.Tensor:
+    """Exact rerank (exact_memory.py:126-133, pb27_vllm/memory.py:854-872): each candidate page
+    of cand [nq,KV,c] int32 (ascending) scores the max over the head's query rows and the
+    page's tokens of q.k (fp32 on bf16 keys [KV,N,128]); the best k (ties to the lowest) are
+    returned as int32 [nq,KV,k] ascending (pbk_quest_rerank)."""
+    _require(keys, "keys")
+    nq, kv, c = cand.shape
+    k = min(k, c)
+    pages = torch.empty(nq, kv, k, dtype=torch.int32, device=q.device)
+    cand = cand.to(torch.int32).contiguous()
+    desc = _desc(q, page, keys.shape[1], k, keys=keys, values=keys, pages=pages)
+    ws = _workspace(LIB.pbk_quest_rerank_workspace(desc, c), q.device)
+    with torch.cuda.device(q.device):
+        check(LIB.pbk_quest_rerank(desc, cand.data_ptr(), c, ws.data_ptr(), ws.numel(), _stream(q)), "pbk_quest_rerank")
     return pages
 
 
@@ -282,19 +389,35 @@ def _budget(t: int) -> tuple[int, bool]:
     return budget, is_decode
 
 
-def _check_flat(archive: Archive, full: int, k: int, is_decode: bool) -> None:
-    sblk = int(EXACT_MEMORY.get("superblock", 64) or 0)
+def _mode(archive: Archive, full: int, k: int, is_decode: bool) -> str:
+    """Which selection retrieve makes (exact_memory.py:107, :126): 'levels', 'rerank' or 'flat'."""
+    sblk = _superblock()
     rerank = int(EXACT_MEMORY.get("decode_rerank", 0) if is_decode else EXACT_MEMORY.get("rerank", 0))
-    if is_decode and rerank <= k and sblk > 1 and full > sblk * 16:
-        raise NotImplementedError("two-level super-block selection is not built; set EXACT_MEMORY['superblock']=0")
-    if rerank > k:
-        raise NotImplementedError("exact rerank is not built; set EXACT_MEMORY['rerank']=0")
+    if (is_decode and rerank <= k and sblk > 1 and archive.smax is not None and archive.smin is not None
+            and full > sblk * 16):
+        return "levels"
+    return "rerank" if rerank > k else "flat"
+
+
+def _select(archive: Archive, i: int, qi: torch.Tensor, full: int, budget: int, is_decode: bool) -> torch.Tensor:
+    """int32 [1, KV, k] pages of batch row i for the query group qi [1,T,H,128]."""
+    k = min(budget, full)
+    mode = _mode(archive, full, k, is_decode)
+    page = EXACT_MEMORY["block_size"]
+    if mode == "levels":
+        return select_pages_levels(qi, archive.kmax[i], archive.kmin[i], archive.length, page, budget,
+                                   archive.smax[i], archive.smin[i], _superblock())
+    if mode == "rerank":
+        c = int(EXACT_MEMORY.get("decode_rerank", 0) if is_decode else EXACT_MEMORY.get("rerank", 0))
+        cand = select_pages(qi, archive.kmax[i], archive.kmin[i], archive.length, page, min(c, full))
+        return rerank_pages(qi, archive.keys[i], cand, page, k)
+    return select_pages(qi, archive.kmax[i], archive.kmin[i], archive.length, page, budget)
 
 
 def retrieve(archive: Archive | None, q: torch.Tensor, groups: int) -> tuple[torch.Tensor, torch.Tensor] | None:
     """Top pages per key head for query chunk q [B,H,T,hd]: (keys, values) [B,KV,R,hd] or None
-    (reference: exact_memory.py:88-152, flat mode; ``prompt_top`` and ``neighbors`` behave as
-    there)."""
+    (reference: exact_memory.py:88-152: the flat, two-level and rerank selections,
+    ``prompt_top`` and ``neighbors`` behave as there)."""
     if archive is None or archive.length == 0:
         return None
     page = EXACT_MEMORY["block_size"]
@@ -302,14 +425,11 @@ def retrieve(archive: Archive | None, q: torch.Tensor, groups: int) -> tuple[tor
     full = archive.length // page
     out_k, out_v = [], []
     budget, is_decode = _budget(t)
-    k = min(budget, full)
-    if full:
-        _check_flat(archive, full, k, is_decode)
     qs = q.to(torch.bfloat16)
     tops = []
     for i in range(b):
         qi = qs[i].transpose(0, 1).unsqueeze(0)  # [1, T, H, hd] view
-        top = (select_pages(qi, archive.kmax[i], archive.kmin[i], archive.length, page, budget)[0]
+        top = (_select(archive, i, qi, full, budget, is_decode)[0]
                if full else torch.empty(h // groups, 0, dtype=torch.int32, device=q.device))
         tops.append(top)
     top = torch.stack(tops).long()
@@ -336,18 +456,23 @@ def retrieve_attend(archive: Archive, q: torch.Tensor, groups: int, win_keys: to
                     sinks: int = 0, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """Fused retrieve + exact attention for one archive: q [1,H,T,hd] at positions qpos [T];
     window cache win_keys/win_values [1,KV,S,hd] at positions kpos [S]. Equals
-    SDPA(q, [retrieve(archive, q) ; window], mask) of transplant.py:612-628 (decode budget,
-    flat mode, no prompt_top). Returns [1,H,T,hd]."""
+    SDPA(q, [retrieve(archive, q) ; window], mask) of transplant.py:612-628 for the query's
+    budget and selection mode (flat, two-level or rerank; without a kept prompt selection or
+    neighbours). Returns [1,H,T,hd]."""
     page = EXACT_MEMORY["block_size"]
     b, h, t, d = q.shape
     if b != 1:
         raise ValueError("retrieve_attend takes one archive (B=1)")
     budget, is_decode = _budget(t)
     full = archive.length // page
-    if full:
-        _check_flat(archive, full, min(budget, full), is_decode)
     qi = q.to(torch.bfloat16)[0].transpose(0, 1).unsqueeze(0)
-    _, out = select_attend_pages(qi, qpos.to(torch.int32).view(1, t), archive.keys[0], archive.values[0],
-                                 archive.kmax[0], archive.kmin[0], archive.length, page, budget, win_keys[0],
-                                 win_values[0], kpos.to(torch.int32), window, sinks, out_dtype=out_dtype)
+    qpos32, kpos32 = qpos.to(torch.int32).view(1, t), kpos.to(torch.int32)
+    if full and _mode(archive, full, min(budget, full), is_decode) != "flat":
+        pages = _select(archive, 0, qi, full, budget, is_decode)
+        out = attend_pages(qi, qpos32, archive.keys[0], archive.values[0], archive.length, page, pages, win_keys[0],
+                           win_values[0], kpos32, window, sinks, out_dtype=out_dtype)
+    else:
+        _, out = select_attend_pages(qi, qpos32, archive.keys[0], archive.values[0], archive.kmax[0],
+                                     archive.kmin[0], archive.length, page, budget, win_keys[0], win_values[0],
+                                     kpos32, window, sinks, out_dtype=out_dtype)
     return out[0].transpose(0, 1).unsqueeze(0)

@@ -8,16 +8,18 @@ Any object with those attributes (and ``prompt_len``, ``hole_lo``, ``hole_hi``, 
 ``smax`` and ``dirty_lo``/``dirty_hi``) can be passed, the reference's ``Archive``
 included; dirty bounds are refreshed with this package's bounds kernel.
 
-Covered: flat block scoring, the exact rerank of the ``rerank`` best candidates
-(memory.py:854-872), the budget rules (:779-787), and the attention over [sinks ;
-retrieved blocks ; partial block before the window ; masked window] (the SDPA branch,
-own=None; the reference's LSE-merge branch computes the same softmax). Not covered (they
-raise NotImplementedError): super-block selection (:800-840), archive holes, block
-neighbours, the ORACLE diagnostic, per-token selection and own-block masks, global
-landmarks, and contexts past ROPE_HORIZON where RoPE repositioning applies (:574-711).
+Covered: flat block scoring, the two-level super-block selection (:802-839, super-block
+bounds refreshed with the block bounds, :280-306), the archive hole (:769-777), block
+neighbours (:873-875), the exact rerank of the ``rerank`` best candidates (:854-872), the
+budget rules (:779-787), the query's RoPE-dims mask for scoring past ROPE_HORIZON
+(:795-797), and the attention over [sinks ; retrieved blocks ; partial block before the
+window ; masked window] (the SDPA branch, own=None; the reference's LSE-merge branch
+computes the same softmax). Not covered (they raise NotImplementedError): the ORACLE
+diagnostic, per-token selection and own-block masks, global landmarks, and the RoPE
+repositioning of keys past ROPE_HORIZON (:574-711) in the rerank and the attention.
 
-Kernels: pbk_quest_select (scores + top-k), pbk_quest_rerank, pbk_quest_attend_sinks
-(libpbk.so, sm_100a); head dim 128.
+Kernels: pbk_quest_select (scores + top-k), pbk_quest_select_levels, pbk_quest_rerank,
+pbk_quest_superbounds, pbk_quest_attend_sinks (libpbk.so, sm_100a); head dim 128.
 """
 from __future__ import annotations
 
@@ -25,7 +27,8 @@ import torch
 
 from . import _capi
 from ._capi import LIB, check
-from .exact_memory import _attend_desc, _desc, _workspace, page_bounds_, select_pages
+from .exact_memory import (_attend_desc, _workspace, page_bounds_, rerank_pages, select_pages, select_pages_levels,
+                           super_bounds_)
 
 # memory.py:33-34 defaults (window: PB27_WINDOW, 16384)
 MEMORY: dict = {"enabled": True, "blocks": 256, "block_size": 64, "decode_blocks": 256, "neighbors": 0,
@@ -38,15 +41,23 @@ SBLK = 64                                   # memory.py:79
 
 
 def _refresh(arc, block: int) -> None:
-    """Recompute the bounds of blocks [dirty_lo, dirty_hi] (memory.py:399-430)."""
+    """Recompute the bounds of blocks [dirty_lo, dirty_hi] and of the super-blocks holding
+    them (memory.py:280-306, 399-430)."""
     lo, hi = getattr(arc, "dirty_lo", 1 << 60), getattr(arc, "dirty_hi", -1)
     if hi < lo:
         return
+    size = min(arc.keys.shape[1], getattr(arc, "size", arc.keys.shape[1]))
     # written keys after the sinks, up to the end of block dirty_hi and of the bounds array
-    n = min(arc.keys.shape[1], getattr(arc, "size", arc.keys.shape[1])) - ORIGIN
-    n = min(n, (hi + 1) * block, arc.kmax.shape[1] * block)
+    n = min(size - ORIGIN, (hi + 1) * block, arc.kmax.shape[1] * block)
     if n > 0 and lo * block < n:
         page_bounds_(arc.keys[:, ORIGIN:ORIGIN + n], block, arc.kmax, arc.kmin, first_page=lo)
+    smax, smin = getattr(arc, "smax", None), getattr(arc, "smin", None)
+    if smax is not None and smin is not None and size > ORIGIN:
+        n_blk = min(arc.kmax.shape[1], (size - ORIGIN + block - 1) // block)
+        sb0 = max(0, lo // SBLK)
+        sb1 = min(smax.shape[1] - 1, min(hi, max(0, n_blk - 1)) // SBLK)
+        if sb1 >= sb0:
+            super_bounds_(arc.kmax, arc.kmin, n_blk, SBLK, smax, smin, sb0, sb1 + 1)
     arc.dirty_lo, arc.dirty_hi = 1 << 60, -1
 
 
@@ -70,34 +81,46 @@ def retrieve_blocks(arc, q: torch.Tensor, groups: int, limit: int, rerank: bool,
     full = (limit - ORIGIN) // block
     if full <= 0:
         return None
-    if MEMORY["neighbors"]:
-        raise NotImplementedError("block neighbours (memory.py:873-875)")
-    if getattr(arc, "hole_hi", 0) > getattr(arc, "hole_lo", 0):
-        raise NotImplementedError("archive holes (memory.py:769-777)")
-    if limit > ROPE_HORIZON:
-        raise NotImplementedError("RoPE repositioning past ROPE_HORIZON (memory.py:798-800, 861-862)")
-    if not rerank and SBLK > 1 and getattr(arc, "smax", None) is not None and full > SBLK * 16:
-        raise NotImplementedError("super-block selection (memory.py:802-840)")
-    _refresh(arc, block)
+    n_valid, hb0, hb1 = full, 0, 0
+    hole_lo, hole_hi = getattr(arc, "hole_lo", 0), getattr(arc, "hole_hi", 0)
+    if hole_hi > hole_lo:  # memory.py:769-777
+        hb0 = max(0, hole_lo - ORIGIN) // block
+        hb1 = min(full, (hole_hi - ORIGIN + block - 1) // block)
+        if hb1 > hb0:
+            n_valid = full - (hb1 - hb0)
+        if n_valid <= 0:
+            return None
+    hole = (hb0, hb1) if hb1 > hb0 else (0, 0)
     t, h, d = q.shape
-    kv = h // groups
-    k = min(budget_for(full, rerank, arc.prompt_len, limit, budget), full)
-    qi = q.to(torch.bfloat16).unsqueeze(0)                        # [1, T, H, D]
-    kmax, kmin = arc.kmax[:, :full], arc.kmin[:, :full]
+    k = min(budget_for(full, rerank, arc.prompt_len, limit, budget), n_valid)
     pool = max(MEMORY["rerank"], 2 * k) if MEMORY["rerank"] > 0 else 0
-    if rerank and pool > k:
-        c = min(pool, full)
-        cand = select_pages(qi, kmax, kmin, full * block, block, c)   # [1, KV, c] ascending
-        pages = torch.empty(1, kv, k, dtype=torch.int32, device=q.device)
-        keys = arc.keys[:, ORIGIN:]
-        desc = _desc(qi, block, full * block, k, keys=keys, values=arc.values[:, ORIGIN:], pages=pages)
-        ws = _workspace(LIB.pbk_quest_rerank_workspace(desc, c), q.device)
-        with torch.cuda.device(q.device):
-            check(LIB.pbk_quest_rerank(desc, cand.data_ptr(), c, ws.data_ptr(), ws.numel(),
-                                       torch.cuda.current_stream(q.device).cuda_stream), "pbk_quest_rerank")
+    if limit > ROPE_HORIZON and rerank and pool > k:
+        raise NotImplementedError("RoPE repositioning of reranked keys past ROPE_HORIZON (memory.py:861-862)")
+    _refresh(arc, block)
+    qi = q.to(torch.bfloat16).unsqueeze(0)                        # [1, T, H, D]
+    if limit > ROPE_HORIZON:  # memory.py:795-797: the RoPE'd dims do not score
+        qi = qi.clone()
+        qi[..., : d // 4] = 0
+    kmax, kmin = arc.kmax[:, :full], arc.kmin[:, :full]
+    smax, smin = getattr(arc, "smax", None), getattr(arc, "smin", None)
+
+    def select(kk: int) -> torch.Tensor:
+        if hole != (0, 0):
+            return select_pages_levels(qi, kmax, kmin, full * block, block, kk, hole=hole)
+        return select_pages(qi, kmax, kmin, full * block, block, kk)
+
+    if not rerank and SBLK > 1 and smax is not None and smin is not None and full > SBLK * 16:
+        pages = select_pages_levels(qi, kmax, kmin, full * block, block, k, smax, smin, SBLK, hole)
+    elif rerank and pool > k:
+        cand = select(min(pool, n_valid))                         # [1, KV, c] ascending
+        pages = rerank_pages(qi, arc.keys[:, ORIGIN:], cand, block, k)
     else:
-        pages = select_pages(qi, kmax, kmin, full * block, block, k)
-    return pages[0].long()
+        pages = select(k)
+    top = pages[0].long()
+    if MEMORY["neighbors"]:  # memory.py:873-875
+        top = torch.cat([top] + [(top + j).clamp(max=full - 1) for j in range(1, MEMORY["neighbors"] + 1)], dim=-1)
+        top = top.sort(-1).values
+    return top
 
 
 def piece_attention(arc, q: torch.Tensor, q_pos: torch.Tensor, top: torch.Tensor | None, groups: int,

@@ -29,6 +29,10 @@ Fixtures:
   gdn_io.npz      the layer pieces around the recurrence: short_convolution with a carried
                   tail (width 4), l2_normalize in both modes, the gating and gated output
                   norm expressions of GatedDeltaNetLayer.forward.
+  quest_levels.npz  retrieve's two-level super-block selection (page 16, super-blocks of 2
+                  pages, 101 full pages), exact rerank, neighbours and a kept prompt selection;
+                  the serving retrieve_blocks' super-block path, with and without an archive
+                  hole, its flat path with a hole and its rerank path with a hole.
   quest.npz       archive_append + retrieve (flat mode, page 16, budget 4 pages) for a
                   decode query (T=1) and a 3-token query, plus the exact attention over
                   [retrieved ; window] as pseudobrain/transplant.py:619-628 computes it.
@@ -141,6 +145,87 @@ def make_quest(E):
     np.savez_compressed(os.path.join(HERE, "quest.npz"), **out)
 
 
+def _pages_of(arc_keys, rk, page, sel):
+    """Page index of each of the first `sel` gathered pages, matched against the archive."""
+    import torch
+    kv, d = arc_keys.shape[1], arc_keys.shape[3]
+    full = arc_keys.shape[2] // page
+    pages = arc_keys[0, :, : full * page].reshape(kv, full, page * d)
+    got = rk[0, :, : sel * page].reshape(kv, sel, page * d)
+    return torch.stack([torch.tensor([int(torch.nonzero((pages[h] == got[h, j]).all(-1))[0]) for j in range(sel)])
+                        for h in range(kv)]).unsqueeze(0)
+
+
+def make_quest_levels(E, MEM):
+    """retrieve's other modes (two-level super-blocks, exact rerank, neighbours, a prompt
+    selection kept for decode) and the serving retrieve_blocks' super-block path with and
+    without an archive hole, the flat path with a hole, and the rerank path with a hole."""
+    import torch
+    page, budget, kv, groups, d, sblk = 16, 8, 2, 4, 128, 2
+    gen = torch.Generator().manual_seed(107)
+    n_arch = 101 * page + 5
+    keys = torch.randn(1, kv, n_arch, d, generator=gen).to(torch.bfloat16)
+    values = torch.randn(1, kv, n_arch, d, generator=gen).to(torch.bfloat16)
+    base = dict(enabled=True, block_size=page, blocks=budget, decode_blocks=budget, superblock=sblk, rerank=0,
+                decode_rerank=0, neighbors=0, keys_like_values=False)
+    E.EXACT_MEMORY.update(base)
+    arc = E.archive_append(None, keys[:, :, :700], values[:, :, :700])
+    arc = E.archive_append(arc, keys[:, :, 700:], values[:, :, 700:])
+    out = dict(keys=_bits(keys), values=_bits(values), kmax=_bits(arc.kmax), kmin=_bits(arc.kmin),
+               smax=_bits(arc.smax), smin=_bits(arc.smin), page=np.int64(page), budget=np.int64(budget),
+               groups=np.int64(groups), sblk=np.int64(sblk))
+    cases = (("sb_t1", 1, {}), ("sb_t3", 3, {}), ("rerank_t1", 1, {"decode_rerank": 24}),
+             ("sb_nb_t1", 1, {"neighbors": 1}), ("prompt_t80", 80, {}), ("sb_after_prompt_t1", 1, {}))
+    for name, t, extra in cases:
+        E.EXACT_MEMORY.update(base)
+        E.EXACT_MEMORY.update(extra)
+        if name != "sb_after_prompt_t1":
+            arc.prompt_top = None
+        q = torch.randn(1, kv * groups, t, d, generator=gen).to(torch.bfloat16)
+        rk, _ = E.retrieve(arc, q, groups)
+        sel = (rk.shape[2] - n_arch % page) // page
+        out.update({f"{name}_q": _bits(q), f"{name}_top": _pages_of(arc.keys, rk, page, sel).numpy().astype(np.int64),
+                    f"{name}_extra": np.array(sorted(extra.items()), dtype=object).astype(str)})
+    E.EXACT_MEMORY.update(base)
+    # serving: an archive of 2 key heads, 16-token blocks after the sinks, super-blocks of 2
+    MEM.SBLK = sblk
+    MEM.MEMORY.update(blocks=8, decode_blocks=8, rerank=0, block_size=page, neighbors=0, window=64)
+    cap = MEM.ORIGIN + 101 * page + 20
+    skeys = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    svalues = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    n_blk = cap // page
+    n_sb = (n_blk + sblk - 1) // sblk
+    sarc = MEM.Archive(skeys, svalues, torch.empty(kv, n_blk, d), torch.empty(kv, n_blk, d))
+    sarc.smax, sarc.smin = torch.empty(kv, n_sb, d), torch.empty(kv, n_sb, d)
+    sarc.size = sarc.prompt_len = cap
+    sarc.dirty_lo, sarc.dirty_hi = 0, n_blk - 1
+    sarc.refresh_bounds(page)
+    out.update(s_keys=_bits(skeys.to(torch.bfloat16)), s_kmax=_bits(sarc.kmax.to(torch.bfloat16)),
+               s_kmin=_bits(sarc.kmin.to(torch.bfloat16)), s_smax=_bits(sarc.smax.to(torch.bfloat16)),
+               s_smin=_bits(sarc.smin.to(torch.bfloat16)), s_origin=np.int64(MEM.ORIGIN), s_limit=np.int64(cap - 40))
+    hole = (MEM.ORIGIN + 30 * page + 3, MEM.ORIGIN + 52 * page)  # positions: blocks 30 .. 51
+    for name, t, rerank, hole_on, no_sb, extra in (("s_sb", 1, False, False, False, {}),
+                                                 ("s_sb_hole", 2, False, True, False, {}),
+                                                 ("s_sb_nb", 1, False, False, False, {"neighbors": 1}),
+                                                 ("s_flat_hole", 1, False, True, True, {}),
+                                                 ("s_rerank_hole", 1, True, True, False, {"rerank": 12})):
+        MEM.MEMORY.update(rerank=0, neighbors=0)
+        MEM.MEMORY.update(extra)
+        sarc.hole_lo, sarc.hole_hi = hole if hole_on else (0, 0)
+        saved = (sarc.smax, sarc.smin)
+        if no_sb:
+            sarc.smax = sarc.smin = None
+        q = torch.randn(t, kv * groups, d, generator=gen).to(torch.bfloat16).float()
+        top = MEM.retrieve_blocks(sarc, q, groups, cap - 40, rerank)
+        sarc.smax, sarc.smin = saved
+        out.update({f"{name}_q": _bits(q.to(torch.bfloat16)), f"{name}_top": top.numpy().astype(np.int64),
+                    f"{name}_rerank": np.int64(rerank), f"{name}_hole": np.array(hole if hole_on else (0, 0)),
+                    f"{name}_nosb": np.int64(no_sb), f"{name}_neighbors": np.int64(extra.get("neighbors", 0)),
+                    f"{name}_pool": np.int64(extra.get("rerank", 0))})
+    MEM.MEMORY.update(rerank=0, neighbors=0)
+    np.savez_compressed(os.path.join(HERE, "quest_levels.npz"), **out)
+
+
 def make_swa(TR):
     import torch
     out = {}
@@ -244,7 +329,8 @@ def main(reference_root: str) -> None:
     os.environ.setdefault("PB27_MEMORY_OFFLOAD", "")
     import pb27_vllm.memory as MEM
     makers = {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR),
-              "serving": lambda: make_serving(MEM), "gdn_io": lambda: make_gdn_io(G)}
+              "serving": lambda: make_serving(MEM), "gdn_io": lambda: make_gdn_io(G),
+              "quest_levels": lambda: make_quest_levels(E, MEM)}
     for name in (sys.argv[2:] if len(sys.argv) > 2 else makers):  # all, or only the named fixtures
         makers[name]()
     for name in sorted(os.listdir(HERE)):

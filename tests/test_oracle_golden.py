@@ -168,3 +168,54 @@ def test_gdn_layer_pieces_match_reference():
     assert ogdn.rel_err(g, f["g"]) < 1e-6 and ogdn.rel_err(beta, f["beta"]) < 1e-6
     out = ogdn.gated_out_norm(f["o"], f["gate"].reshape(f["o"].shape), f["o_norm"])
     assert ogdn.rel_err(out, f["out"]) < 1e-5
+
+
+LEVEL_CASES = {"sb_t1": {}, "sb_t3": {}, "rerank_t1": {"rerank": 24}, "sb_nb_t1": {"neighbors": 1},
+               "prompt_t80": {}, "sb_after_prompt_t1": {"prompt": "prompt_t80"}}
+
+
+@pytest.fixture(scope="module")
+def levels():
+    return load_golden("quest_levels.npz")
+
+
+def test_super_bounds_bit_exact(levels):
+    """oracle super_bounds against the reference archive's smax/smin (exact_memory.py:53-63)."""
+    f = levels
+    smax, smin = oq.super_bounds(_f32(f["kmax"]), _f32(f["kmin"]), int(f["sblk"]))
+    assert np.array_equal(oq.bf16_bits(smax), f["smax"])
+    assert np.array_equal(oq.bf16_bits(smin), f["smin"])
+
+
+@pytest.mark.parametrize("case", list(LEVEL_CASES))
+def test_retrieve_modes_match_reference(levels, case):
+    """Two-level super-block selection, exact rerank, neighbours and a kept prompt selection
+    (exact_memory.py:88-152) against the reference's own retrieve."""
+    f = levels
+    page, budget, groups, sblk = (int(f[x]) for x in ("page", "budget", "groups", "sblk"))
+    opt = LEVEL_CASES[case]
+    prompt = f[f"{opt['prompt']}_top"] if "prompt" in opt else None
+    _, _, top = oq.retrieve_modes(_f32(f["keys"]), _f32(f["values"]), _f32(f["kmax"]), _f32(f["kmin"]),
+                                  _f32(f[f"{case}_q"]), groups, page, budget, superblock=sblk,
+                                  rerank=opt.get("rerank", 0), neighbors=opt.get("neighbors", 0), prompt_top=prompt)
+    assert np.array_equal(top, f[f"{case}_top"])
+
+
+@pytest.mark.parametrize("case", ["s_sb", "s_sb_hole", "s_sb_nb", "s_flat_hole", "s_rerank_hole"])
+def test_serving_levels_match_reference(levels, case):
+    """The serving retrieve_blocks' super-block path, archive hole and neighbours
+    (pb27_vllm/memory.py:760-878) against the reference."""
+    from oracle import serving as osv
+    f = levels
+    page, sblk, groups = int(f["page"]), int(f["sblk"]), int(f["groups"])
+    kmax, kmin = _f32(f["s_kmax"]), _f32(f["s_kmin"])
+    smax, smin = osv.super_bounds(kmax, kmin, kmax.shape[1], sblk)
+    assert np.array_equal(oq.bf16_bits(smax), f["s_smax"]) and np.array_equal(oq.bf16_bits(smin), f["s_smin"])
+    keys = _f32(f["s_keys"])
+    mem = dict(blocks=8, decode_blocks=8, rerank=int(f[f"{case}_pool"]), block_size=page, window=64,
+               neighbors=int(f[f"{case}_neighbors"]))
+    use_sb = not int(f[f"{case}_nosb"])
+    top = osv.retrieve_blocks(keys, kmax, kmin, _f32(f[f"{case}_q"]), groups, int(f["s_limit"]),
+                              bool(f[f"{case}_rerank"]), mem, keys.shape[1], smax if use_sb else None,
+                              smin if use_sb else None, sblk, tuple(int(x) for x in f[f"{case}_hole"]))
+    assert np.array_equal(top, f[f"{case}_top"])
