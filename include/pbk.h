@@ -340,6 +340,44 @@ PBK_API int pbk_quest_superbounds(const void* kmax, const void* kmin, int32_t kv
                                   int64_t sb_stride_kv, int64_t sb_stride_p, int32_t first_sb, int32_t end_sb,
                                   void* stream);
 
+/* RoPE repositioning of archived keys fused with their gather (pb27_vllm/memory.py:574-677:
+ * _reposition_rope_sinks, _reposition_rope_blocks). For key head h, output row r < n_blk *
+ * block is row s = r % block of block j = r / block, read from archive row origin +
+ * blocks[h][j] * block + s (blocks NULL: block j itself); rows n_blk * block .. + tail_n are
+ * archive rows tail0 .. tail0 + tail_n, copied as they are. Block j's keys turn by the angle
+ * delta_j * inv_freq[i] in the pairs (i, i + d/8), i < d/8 (the first d/4 dims; the rest are
+ * copied), in fp32 with the products and the difference rounded apart, then to bf16:
+ *   mode 0: delta 0 (a plain gather);
+ *   mode 1 (contiguous runs, the attention's retrieved blocks, :644-664): blocks placed in
+ *     [ref_pos - max(arc_span, n_blk block), ref_pos) one block apart plus a share of the
+ *     slack proportional to the historical gaps before them (blocks ascending);
+ *   mode 2 (proportional, the rerank's candidates, :640-643): delta_j =
+ *     round(max(ref_pos - pos_j, 0) * scale), pos_j = origin + blocks[h][j] * block;
+ *   mode 3: delta_j = const_delta for every block (the sink keys, :585-596).
+ * Values are gathered the same way, never rotated. Archive rows outside [0, n_rows) read as
+ * zeros. Outputs out_keys / out_values (NULL: keys only) are bf16 [kv, n_blk * block +
+ * tail_n, d], contiguous; delta (fp32 [kv, n_blk], required for modes 1 and 2, written) holds
+ * each block's shift. */
+typedef struct pbk_rope_gather_desc {
+  int32_t kv, d, block, n_blk;   /* d must be 128 */
+  int32_t origin, n_rows;        /* archive position of block 0; archive rows */
+  int32_t ref_pos, arc_span;
+  int32_t mode, tail0, tail_n;
+  float scale;                   /* mode 2 */
+  float const_delta;             /* mode 3 */
+  int32_t pad_;
+  const int32_t* blocks;         /* [kv, n_blk] block indices, or NULL */
+  const float* inv_freq;         /* [d / 8] rotary inverse frequencies */
+  const void* keys;
+  const void* values;            /* may be NULL (keys only) */
+  int64_t stride_kv, stride_n;   /* archive element strides (keys and values alike) */
+  void* out_keys;
+  void* out_values;
+  float* delta;
+} pbk_rope_gather_desc;
+
+PBK_API int pbk_quest_rope_gather(const pbk_rope_gather_desc* desc, void* stream);
+
 /* Options of pbk_quest_select_levels. */
 typedef struct pbk_quest_levels {
   const void* smax;         /* bf16 super-block bounds [kv, >= ceil(full / sblk), d]; NULL: one level */

@@ -12,8 +12,8 @@ Follows serving/pb27_vllm/pb27_vllm/memory.py:
   (:781-787) only raise it for archives of more than 2048 blocks.
 * ``piece_attention`` (:1311-1490), SDPA branch with own=None: keys are the sinks
   [0, ns), the retrieved blocks, the partial block [tail0, lo) and the window [lo, hi)
-  with the causal sliding-window mask (:1433-1490); RoPE repositioning is a no-op while
-  lo <= ROPE_HORIZON (:583, :628).
+  with the causal sliding-window mask (:1433-1490); past ROPE_HORIZON the sinks and the
+  retrieved blocks' keys move to new RoPE positions (:574-677, :1402-1425).
 Ties in the top-k go to the lowest block index (torch.topk leaves them unspecified).
 """
 from __future__ import annotations
@@ -23,6 +23,90 @@ import numpy as np
 ORIGIN = 4        # memory.py:46 (FAITHFUL, SINKS = 4)
 SINKS = 4         # memory.py:37
 SCALE = [2048, 384, 4096, 512, 8192, 1024]  # memory.py:49
+
+
+ROPE_HORIZON = 262144  # memory.py:50
+ROPE_ARC_SPAN = 98304  # memory.py:51
+ROPE_THETA = 10000000.0  # memory.py:52
+
+
+def inv_freq(d_rot: int, theta: float = ROPE_THETA) -> np.ndarray:
+    """memory.py:563-571, in fp32."""
+    return (np.float32(1.0) / (np.float32(theta) ** (np.arange(0, d_rot, 2, dtype=np.float32)
+                                                     / np.float32(d_rot)))).astype(np.float32)
+
+
+def _rotate(x: np.ndarray, delta: np.ndarray, theta: float, bf16: bool = True) -> np.ndarray:
+    """Turn the first d/4 dims of x [..., D] in the pairs (i, i + d/8) by delta [...] * inv_freq,
+    fp32 with each product and sum rounded, then to the keys' dtype: bf16, or fp32 when
+    bf16=False (memory.py:598-606, 665-677)."""
+    from .quest import bf16_round as _r
+    bf16_round = _r if bf16 else (lambda v: v)
+    d = x.shape[-1]
+    half = d // 8
+    ang = (delta[..., None].astype(np.float32) * inv_freq(d // 4, theta)).astype(np.float32)
+    c, s = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    x1, x2 = x[..., :half].astype(np.float32), x[..., half:2 * half].astype(np.float32)
+    out = np.array(x, dtype=np.float32)
+    out[..., :half] = bf16_round((x1 * c).astype(np.float32) - (x2 * s).astype(np.float32))
+    out[..., half:2 * half] = bf16_round((x2 * c).astype(np.float32) + (x1 * s).astype(np.float32))
+    return out
+
+
+def block_shifts(blk_idx: np.ndarray, block: int, ref_pos: int, contiguous_runs: bool,
+                 arc_span: int = ROPE_ARC_SPAN) -> np.ndarray:
+    """Per-block RoPE position shift of _reposition_rope_blocks (memory.py:640-664), fp32:
+    blk_idx [KV, n] -> [KV, n]."""
+    f32 = np.float32
+    idx = blk_idx.astype(np.int64)
+    n = idx.shape[1]
+    orig = (ORIGIN + idx * block).astype(f32)
+    if not contiguous_runs:
+        scale = f32(1.0 - min(1.0, float(arc_span) / float(max(1, ref_pos))))
+        target = orig + np.rint(np.maximum(f32(ref_pos) - orig, f32(0)) * scale).astype(f32)
+        return np.maximum(target - orig, f32(0))
+    eff_span = max(arc_span, n * block)
+    base_start = max(ORIGIN, ref_pos - eff_span)
+    slack = f32(max(0, (ref_pos - base_start) - n * block))
+    g_pre = np.maximum(orig[:, :1] - f32(ORIGIN), f32(0))
+    if n > 1:
+        g_mid = (np.maximum(idx[:, 1:] - idx[:, :-1] - 1, 0) * block).astype(f32)
+        g_cum = np.concatenate((g_pre, g_pre + np.cumsum(g_mid, axis=1, dtype=f32)), axis=1)
+        g_mid_sum = g_mid.sum(axis=1, keepdims=True, dtype=f32)
+    else:
+        g_cum, g_mid_sum = g_pre, np.zeros_like(g_pre)
+    g_post = np.maximum(f32(ref_pos) - (orig[:, -1:] + f32(block)), f32(0))
+    g_tot = np.maximum(g_pre + g_mid_sum + g_post, f32(1))
+    j_steps = (np.arange(n, dtype=f32) * f32(block))[None]
+    target = (f32(base_start) + j_steps) + np.rint(g_cum * (slack / g_tot)).astype(f32)
+    return np.maximum(target - orig, f32(0))
+
+
+def reposition_blocks(rk: np.ndarray, blk_idx: np.ndarray, block: int, ref_pos: int, contiguous_runs: bool,
+                      horizon: int = ROPE_HORIZON, arc_span: int = ROPE_ARC_SPAN,
+                      theta: float = ROPE_THETA, bf16: bool = True) -> np.ndarray:
+    """_reposition_rope_blocks (memory.py:610-677): rk [KV, n*block, D] of blocks blk_idx [KV, n]."""
+    if ref_pos <= horizon or rk.size == 0:
+        return rk
+    kv, total, d = rk.shape
+    n = blk_idx.shape[1]
+    delta = block_shifts(blk_idx, block, ref_pos, contiguous_runs, arc_span)
+    return _rotate(rk.reshape(kv, n, block, d), np.repeat(delta[:, :, None], block, axis=2), theta,
+                   bf16).reshape(kv, total, d)
+
+
+def reposition_sinks(sk: np.ndarray, ref_pos: int, n_blk: int, block: int, horizon: int = ROPE_HORIZON,
+                     arc_span: int = ROPE_ARC_SPAN, theta: float = ROPE_THETA, bf16: bool = True) -> np.ndarray:
+    """_reposition_rope_sinks (memory.py:574-607): sk [KV, ns, D] moved to end before the first
+    repositioned block."""
+    if ref_pos <= horizon or sk.size == 0:
+        return sk
+    ns = sk.shape[1]
+    base_start = max(ORIGIN, ref_pos - max(arc_span, n_blk * block))
+    delta = max(0, base_start - ns)
+    if delta <= 0:
+        return sk
+    return _rotate(sk, np.full(sk.shape[:2], delta, dtype=np.float32), theta, bf16)
 
 
 def _topk_sorted(score: np.ndarray, k: int) -> np.ndarray:
@@ -54,13 +138,15 @@ def super_bounds(kmax, kmin, n_blk: int, sblk: int):
 
 
 def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_len, smax=None, smin=None, sblk=0,
-                    hole=(0, 0)):
+                    hole=(0, 0), rope=(ROPE_HORIZON, ROPE_ARC_SPAN, ROPE_THETA), bf16_keys=True):
     """keys [KV, cap, D]; kmax/kmin [KV, n_blk, D]; q [T, H, D] -> [KV, k] block indices or None.
 
     With smax/smin [KV, n_sb, D] and sblk > 1, a call without rerank over more than 16 sblk
     full blocks takes the two-level selection (memory.py:802-839). ``hole`` = (hole_lo,
     hole_hi) archive positions whose blocks score -inf (memory.py:769-777, 834-835, 852-853);
-    memory["neighbors"] adds the following blocks (:873-875)."""
+    memory["neighbors"] adds the following blocks (:873-875). Past the horizon (rope =
+    (horizon, arc_span, theta)) the first d/4 query dims do not score the bounds (:795-797)
+    and the rerank's candidate keys move in proportion (:861-862)."""
     from .quest import select_two_level
     block = memory["block_size"]
     full = (limit - ORIGIN) // block
@@ -78,6 +164,9 @@ def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_l
             return None
     k = min(budget(memory, full, rerank, prompt_len, limit), n_valid)
     qg = np.asarray(q, np.float64).transpose(1, 0, 2).reshape(kv, groups * t, d)   # [KV, G*T, D]
+    qs = qg.copy()
+    if limit > rope[0]:
+        qs[..., : d // 4] = 0
     nb = memory.get("neighbors", 0)
 
     def with_neighbors(top):
@@ -86,8 +175,8 @@ def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_l
         return np.sort(top, axis=-1)
 
     if not rerank and sblk > 1 and smax is not None and full > sblk * 16:
-        return with_neighbors(select_two_level(qg, kmax, kmin, smax, smin, full, k, sblk, (hb0, hb1)))
-    pos, neg = np.maximum(qg, 0), np.minimum(qg, 0)
+        return with_neighbors(select_two_level(qs, kmax, kmin, smax, smin, full, k, sblk, (hb0, hb1)))
+    pos, neg = np.maximum(qs, 0), np.minimum(qs, 0)
     score = (np.einsum("grd,gnd->grn", pos, kmax[:, :full].astype(np.float64))
              + np.einsum("grd,gnd->grn", neg, kmin[:, :full].astype(np.float64))).max(1)      # [KV, full]
     score[:, hb0:hb1] = -np.inf
@@ -97,32 +186,48 @@ def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_l
         cand = _topk_sorted(score, c)                                                   # [KV, c] ascending
         blk = keys[:, ORIGIN:ORIGIN + full * block].reshape(kv, full, block, d).astype(np.float64)
         ck = np.take_along_axis(blk, cand[:, :, None, None], axis=1)                    # [KV, c, block, D]
+        if limit > rope[0]:
+            ck = reposition_blocks(ck.reshape(kv, -1, d), cand, block, limit, False, *rope,
+                                   bf16=bf16_keys).reshape(ck.shape)
         exact = np.einsum("grd,gcsd->grcs", qg, ck).max(axis=(1, 3))                   # [KV, c]
         keep = _topk_sorted(exact, k)
         return with_neighbors(np.take_along_axis(cand, keep, axis=1))
     return with_neighbors(_topk_sorted(score, k))
 
 
-def piece_attention(keys, values, q, q_pos, top, groups, window, scale, block):
-    """q [T, H, D] at positions q_pos -> [T, H, D] float64 (SDPA branch, own=None)."""
+def piece_attention(keys, values, q, q_pos, top, groups, window, scale, block,
+                    rope=(ROPE_HORIZON, ROPE_ARC_SPAN, ROPE_THETA), bf16_keys=True):
+    """q [T, H, D] at positions q_pos -> [T, H, D] float64 (SDPA branch, own=None). Past the
+    horizon (lo > rope[0]) the sinks and the retrieved blocks' keys move (memory.py:1402-1425),
+    rounded to bf16 (bf16_keys) or kept in fp32 as an fp32 archive keeps them."""
     t, h, d = q.shape
     kv = h // groups
     q_min, q_max = int(q_pos.min()), int(q_pos.max())
     lo, hi = max(0, q_min - window + 1), q_max + 1
     ns = min(SINKS, lo)
     tail0 = ORIGIN + ((lo - ORIGIN) // block) * block
+    keys_sink = reposition_sinks(keys[:, :ns], lo, top.shape[1] if top is not None else 0, block, *rope,
+                                 bf16=bf16_keys)
+    keys_blk = None
+    if top is not None:
+        gathered = np.stack([np.concatenate([keys[g, ORIGIN + b * block:ORIGIN + (b + 1) * block] for b in top[g]])
+                             for g in range(kv)]) if top.shape[1] else np.zeros((kv, 0, d), np.float32)
+        keys_blk = reposition_blocks(gathered, top, block, lo, True, *rope, bf16=bf16_keys)
     out = np.zeros((t, h, d))
     for g in range(kv):
-        parts_k, parts_v, vis = [], [], []
         idx = list(range(ns))
+        kparts = [keys_sink[g]]
         if top is not None:
             for b in top[g]:
                 idx += list(range(ORIGIN + b * block, ORIGIN + (b + 1) * block))
+            kparts.append(keys_blk[g])
             if lo > tail0:
                 idx += list(range(tail0, lo))
+                kparts.append(keys[g, tail0:lo])
         always = len(idx)
         idx += list(range(lo, hi))
-        kk, vv = keys[g, idx].astype(np.float64), values[g, idx].astype(np.float64)
+        kparts.append(keys[g, lo:hi])
+        kk, vv = np.concatenate(kparts).astype(np.float64), values[g, idx].astype(np.float64)
         wpos = np.arange(lo, hi)
         for j in range(groups):
             hq = g * groups + j

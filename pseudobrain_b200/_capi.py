@@ -84,6 +84,17 @@ class PbkQuestLevels(ctypes.Structure):
                 ("hole_lo", ctypes.c_int32), ("hole_hi", ctypes.c_int32), ("pad_", ctypes.c_int32)]
 
 
+class PbkRopeGatherDesc(ctypes.Structure):
+    _fields_ = [("kv", ctypes.c_int32), ("d", ctypes.c_int32), ("block", ctypes.c_int32), ("n_blk", ctypes.c_int32),
+                ("origin", ctypes.c_int32), ("n_rows", ctypes.c_int32), ("ref_pos", ctypes.c_int32),
+                ("arc_span", ctypes.c_int32), ("mode", ctypes.c_int32), ("tail0", ctypes.c_int32),
+                ("tail_n", ctypes.c_int32), ("scale", ctypes.c_float), ("const_delta", ctypes.c_float),
+                ("pad_", ctypes.c_int32), ("blocks", ctypes.c_void_p), ("inv_freq", ctypes.c_void_p),
+                ("keys", ctypes.c_void_p), ("values", ctypes.c_void_p), ("stride_kv", ctypes.c_int64),
+                ("stride_n", ctypes.c_int64), ("out_keys", ctypes.c_void_p), ("out_values", ctypes.c_void_p),
+                ("delta", ctypes.c_void_p)]
+
+
 _QD = ctypes.POINTER(PbkQuestDesc)
 _QL = ctypes.POINTER(PbkQuestLevels)
 _VP, _I32, _I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
@@ -124,6 +135,7 @@ SIGNATURES = {
                                              _I32, _I32, _VP]),
     "pbk_quest_select_levels_workspace": (ctypes.c_size_t, [_QD, _QL]),
     "pbk_quest_select_levels": (ctypes.c_int, [_QD, _QL, _VP, ctypes.c_size_t, _VP]),
+    "pbk_quest_rope_gather": (ctypes.c_int, [ctypes.POINTER(PbkRopeGatherDesc), _VP]),
     "pbk_swa_prefill": (ctypes.c_int, [ctypes.POINTER(PbkSwaDesc), _VP]),
 }
 

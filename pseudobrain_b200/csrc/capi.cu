@@ -470,6 +470,24 @@ int pbk_quest_superbounds(const void* kmax, const void* kmin, int32_t kv, int32_
                                                      static_cast<cudaStream_t>(stream)));
 }
 
+int pbk_quest_rope_gather(const pbk_rope_gather_desc* d, void* stream) {
+  if (d == nullptr) return PBK_ERR_INVALID;
+  if (d->kv < 1 || d->block < 1 || d->n_blk < 0 || d->tail_n < 0 || d->n_rows < 0 || d->mode < 0 || d->mode > 3)
+    return PBK_ERR_INVALID;
+  if (d->d != 128) return PBK_ERR_SHAPE;
+  if ((int64_t)d->n_blk * d->block + d->tail_n > INT32_MAX) return PBK_ERR_SHAPE;
+  if ((int64_t)d->n_blk * d->block + d->tail_n == 0) return PBK_OK;
+  if (!d->keys || !d->out_keys || (d->out_values && !d->values)) return PBK_ERR_INVALID;
+  if (d->mode != 0 && d->n_blk > 0 && !d->inv_freq) return PBK_ERR_INVALID;
+  if ((d->mode == 1 || d->mode == 2) && d->n_blk > 0 && (!d->blocks || !d->delta)) return PBK_ERR_INVALID;
+  if (!aligned16(d->keys) || !aligned16(d->out_keys) || (d->values && !aligned16(d->values)) ||
+      (d->out_values && !aligned16(d->out_values)) || !aligned_elems(d->stride_kv, 8) || !aligned_elems(d->stride_n, 8))
+    return PBK_ERR_ALIGN;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_quest_rope_gather(*d, static_cast<cudaStream_t>(stream)));
+}
+
 namespace {
 int validate_levels(const pbk_quest_desc* d, const pbk_quest_levels* lv) {
   int st = validate_quest(d, 1);

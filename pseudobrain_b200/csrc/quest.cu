@@ -13,6 +13,11 @@ namespace {
 constexpr int kD = 128;
 using bf16 = __nv_bfloat16;
 
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 raw, float* out) {
   const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
@@ -807,6 +812,114 @@ __global__ void __launch_bounds__(kScoreThreads) quest_sub_score_kernel(const pb
   cand[(int64_t)row * nc + c] = idx;
 }
 
+// ---------------------------------------------------------------------------------
+// RoPE repositioning (pb27_vllm/memory.py:574-677). One warp per key head computes every
+// block's shift in the reference's fp32 operation order (each product, quotient and sum
+// rounded apart; integer positions are exact in fp32 below 2^24); mode 1 needs the running
+// sum of the gaps between consecutive blocks (a warp scan, 32 blocks per step).
+// ---------------------------------------------------------------------------------
+__global__ void __launch_bounds__(32) quest_rope_delta_kernel(const pbk_rope_gather_desc d) {
+  const int h = blockIdx.x, lane = threadIdx.x;
+  const int32_t* idx = d.blocks + (int64_t)h * d.n_blk;
+  float* out = d.delta + (int64_t)h * d.n_blk;
+  const float ref = (float)d.ref_pos, blk = (float)d.block;
+  auto pos_of = [&](int j) { return (float)((int64_t)d.origin + (int64_t)idx[j] * d.block); };
+  if (d.mode == 2) {
+    for (int j = lane; j < d.n_blk; j += 32) {
+      const float orig = pos_of(j);
+      const float target = __fadd_rn(orig, rintf(__fmul_rn(fmaxf(__fsub_rn(ref, orig), 0.f), d.scale)));
+      out[j] = fmaxf(__fsub_rn(target, orig), 0.f);
+    }
+    return;
+  }
+  // mode 1
+  const int64_t nb = (int64_t)d.n_blk * d.block;
+  const int64_t eff_span = max((int64_t)d.arc_span, nb);
+  const int64_t base_i = max((int64_t)d.origin, (int64_t)d.ref_pos - eff_span);
+  const float base_start = (float)base_i;
+  const float slack = (float)max((int64_t)0, ((int64_t)d.ref_pos - base_i) - nb);
+  const float g_pre = fmaxf(__fsub_rn(pos_of(0), (float)d.origin), 0.f);
+  auto gap = [&](int i) {  // g_mid[i], i < n_blk - 1
+    return (float)((int64_t)max(idx[i + 1] - idx[i] - 1, 0) * d.block);
+  };
+  float total = 0.f;  // sum of g_mid
+  for (int i = lane; i < d.n_blk - 1; i += 32) total = __fadd_rn(total, gap(i));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) total = __fadd_rn(total, __shfl_xor_sync(0xffffffffu, total, o));
+  const float g_post = fmaxf(__fsub_rn(ref, __fadd_rn(pos_of(d.n_blk - 1), blk)), 0.f);
+  const float g_tot = fmaxf(__fadd_rn(__fadd_rn(g_pre, total), g_post), 1.f);
+  const float ratio = __fdiv_rn(slack, g_tot);
+  float carry = g_pre;  // g_cum of the first block of this step
+  for (int j0 = 0; j0 < d.n_blk; j0 += 32) {
+    const int j = j0 + lane;
+    // g_cum[j] = g_pre + sum_{i < j} g_mid[i]: inclusive scan of g_mid[j - 1] (0 for j = 0)
+    float x = (j > 0 && j < d.n_blk) ? gap(j - 1) : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x = __fadd_rn(x, y);
+    }
+    const float g_cum = __fadd_rn(carry, x);
+    if (j < d.n_blk) {
+      const float target = __fadd_rn(__fadd_rn(base_start, (float)((int64_t)j * d.block)), rintf(__fmul_rn(g_cum, ratio)));
+      out[j] = fmaxf(__fsub_rn(target, pos_of(j)), 0.f);
+    }
+    carry = __shfl_sync(0xffffffffu, g_cum, 31);
+  }
+}
+
+// Gather (and rotate) one output row per warp; lane l holds dims 4l .. 4l + 3, so the
+// rotated pairs (i, i + 16), i < 16, sit in lanes l and l + 4 for l < 4.
+__global__ void __launch_bounds__(256) quest_rope_gather_kernel(const pbk_rope_gather_desc d) {
+  const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp, nb = (int64_t)d.n_blk * d.block;
+  if (row >= nb + d.tail_n) return;
+  int64_t src;
+  float dl = 0.f;
+  if (row < nb) {
+    const int j = (int)(row / d.block), s = (int)(row % d.block);
+    const int b = d.blocks ? d.blocks[(int64_t)h * d.n_blk + j] : j;
+    src = (int64_t)d.origin + (int64_t)b * d.block + s;
+    if (d.mode == 3) dl = d.const_delta;
+    else if (d.mode != 0) dl = d.delta[(int64_t)h * d.n_blk + j];
+  } else {
+    src = (int64_t)d.tail0 + (row - nb);
+  }
+  const bool ok = src >= 0 && src < d.n_rows;
+  const int64_t at = h * d.stride_kv + src * d.stride_n + 4 * lane;
+  const int64_t out_at = ((int64_t)h * (nb + d.tail_n) + row) * kD + 4 * lane;
+  uint2 kr = make_uint2(0u, 0u);
+  if (ok) kr = *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(d.keys) + at);
+  if (d.mode != 0 && row < nb) {
+    const uint2 pr = make_uint2(__shfl_xor_sync(0xffffffffu, kr.x, 4), __shfl_xor_sync(0xffffffffu, kr.y, 4));
+    if (lane < 8) {
+      const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&kr);
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&pr);
+      const float2 a0 = __bfloat1622float2(a[0]), a1 = __bfloat1622float2(a[1]);
+      const float2 b0 = __bfloat1622float2(b[0]), b1 = __bfloat1622float2(b[1]);
+      const float own[4] = {a0.x, a0.y, a1.x, a1.y}, other[4] = {b0.x, b0.y, b1.x, b1.y};
+      float r[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * (lane & 3) + e;  // pair index
+        const float ang = __fmul_rn(dl, d.inv_freq[i]);
+        const float c = cosf(ang), sn = sinf(ang);
+        // lanes 0-3 hold x1 (r1 = x1 cos - x2 sin), lanes 4-7 hold x2 (r2 = x2 cos + x1 sin)
+        r[e] = lane < 4 ? __fsub_rn(__fmul_rn(own[e], c), __fmul_rn(other[e], sn))
+                        : __fadd_rn(__fmul_rn(own[e], c), __fmul_rn(other[e], sn));
+      }
+      kr.x = bf16x2_bits(r[0], r[1]);
+      kr.y = bf16x2_bits(r[2], r[3]);
+    }
+  }
+  *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(d.out_keys) + out_at) = kr;
+  if (d.out_values != nullptr) {
+    uint2 vr = make_uint2(0u, 0u);
+    if (ok) vr = *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(d.values) + at);
+    *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(d.out_values) + out_at) = vr;
+  }
+}
+
 // Pages [lo, hi) of every score row score -inf (the archive hole, memory.py:852-853).
 __global__ void quest_hole_kernel(float* scores, int npages, int nrows, int lo, int hi) {
   const int w = hi - lo;
@@ -1060,6 +1173,14 @@ cudaError_t launch_quest_superbounds(const void* kmax, const void* kmin, int kv,
   quest_superbounds_kernel<<<dim3((nsb + 7) / 8, kv), 256, 0, st>>>(
       static_cast<const bf16*>(kmax), static_cast<const bf16*>(kmin), bs_kv, bs_p, n_blk, sblk,
       static_cast<bf16*>(smax), static_cast<bf16*>(smin), ss_kv, ss_p, first_sb, nsb);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quest_rope_gather(const pbk_rope_gather_desc& d, cudaStream_t st) {
+  const int64_t rows = (int64_t)d.n_blk * d.block + d.tail_n;
+  if (rows == 0) return cudaSuccess;
+  if ((d.mode == 1 || d.mode == 2) && d.n_blk > 0) quest_rope_delta_kernel<<<d.kv, 32, 0, st>>>(d);
+  quest_rope_gather_kernel<<<dim3((unsigned)((rows + 7) / 8), d.kv), 256, 0, st>>>(d);
   return cudaGetLastError();
 }
 

@@ -15,13 +15,18 @@ budget rules (:779-787), the query's RoPE-dims mask for scoring past ROPE_HORIZO
 (:795-797), and the attention over [sinks ; retrieved blocks ; partial block before the
 window ; masked window] (the SDPA branch, own=None; the reference's LSE-merge branch
 computes the same softmax). Not covered (they raise NotImplementedError): the ORACLE
-diagnostic, per-token selection and own-block masks, global landmarks, and the RoPE
-repositioning of keys past ROPE_HORIZON (:574-711) in the rerank and the attention.
+diagnostic, per-token selection and own-block masks, and global landmarks. Past
+ROPE_HORIZON the reranked candidates' keys, the sinks and the retrieved blocks move to new
+RoPE positions as the reference moves them (:574-677, 861-862, 1402-1425), gathered with
+the move (pbk_quest_rope_gather).
 
 Kernels: pbk_quest_select (scores + top-k), pbk_quest_select_levels, pbk_quest_rerank,
-pbk_quest_superbounds, pbk_quest_attend_sinks (libpbk.so, sm_100a); head dim 128.
+pbk_quest_superbounds, pbk_quest_rope_gather, pbk_quest_attend_sinks (libpbk.so, sm_100a);
+head dim 128.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -37,7 +42,66 @@ SINKS = 4                                   # memory.py:37
 ORIGIN = SINKS                              # memory.py:46 (FAITHFUL)
 SCALE = [2048, 384, 4096, 512, 8192, 1024]  # memory.py:49
 ROPE_HORIZON = 262144                       # memory.py:50
+ROPE_ARC_SPAN = 98304                       # memory.py:51
+ROPE_THETA = float(os.environ.get("PB27_MEMORY_ROPE_THETA", "10000000.0") or 10000000.0)  # memory.py:52
 SBLK = 64                                   # memory.py:79
+
+_INV_FREQ: dict = {}
+
+
+def _inv_freq(device: torch.device, d_rot: int) -> torch.Tensor:
+    """The rotary inverse frequencies of the first d_rot dims, computed on the device by the
+    reference's expression (memory.py:563-571), once per (device, d_rot, theta)."""
+    key = (str(device), d_rot, ROPE_THETA)
+    if key not in _INV_FREQ:
+        _INV_FREQ[key] = 1.0 / (ROPE_THETA ** (torch.arange(0, d_rot, 2, device=device, dtype=torch.float32)
+                                               / float(d_rot)))
+    return _INV_FREQ[key]
+
+
+ROPE_MODES = {"none": 0, "runs": 1, "proportional": 2, "constant": 3}
+
+
+def rope_gather(keys: torch.Tensor, values: torch.Tensor | None, blocks: torch.Tensor | None, block: int,
+                origin: int, n_blk: int, mode: str, ref_pos: int = 0, arc_span: int = 0, tail0: int = 0,
+                tail_n: int = 0, const_delta: float = 0.0):
+    """Gather blocks of an archive [KV, N, 128] with their keys moved to new RoPE positions
+    (pbk_quest_rope_gather; memory.py:574-677): block j of key head h is archive rows origin +
+    blocks[h][j] * block .. (blocks None: block j), followed by rows [tail0, tail0 + tail_n) as
+    they are. mode 'runs' is _reposition_rope_blocks with contiguous_runs=True, 'proportional'
+    with contiguous_runs=False, 'constant' turns every block by const_delta positions
+    (_reposition_rope_sinks), 'none' only gathers. Returns (keys, values or None)
+    [KV, n_blk * block + tail_n, 128] bf16."""
+    kv, n_rows, d = keys.shape
+    rows = n_blk * block + tail_n
+    ok = torch.empty(kv, rows, d, dtype=keys.dtype, device=keys.device)
+    ov = torch.empty_like(ok) if values is not None else None
+    blk32 = blocks.to(torch.int32).contiguous() if blocks is not None else None
+    delta = torch.empty(kv, max(n_blk, 1), dtype=torch.float32, device=keys.device)
+    inv = _inv_freq(keys.device, d // 4)
+    span = arc_span if arc_span > 0 else ROPE_ARC_SPAN
+    desc = _capi.PbkRopeGatherDesc(
+        kv=kv, d=d, block=block, n_blk=n_blk, origin=origin, n_rows=n_rows, ref_pos=ref_pos, arc_span=span,
+        mode=ROPE_MODES[mode], tail0=tail0, tail_n=tail_n,
+        scale=1.0 - min(1.0, float(span) / float(max(1, ref_pos))), const_delta=float(const_delta),
+        blocks=blk32.data_ptr() if blk32 is not None else None, inv_freq=inv.data_ptr(), keys=keys.data_ptr(),
+        values=values.data_ptr() if values is not None else None, stride_kv=keys.stride(0), stride_n=keys.stride(1),
+        out_keys=ok.data_ptr(), out_values=ov.data_ptr() if ov is not None else None, delta=delta.data_ptr())
+    if values is not None and (values.stride(0), values.stride(1)) != (keys.stride(0), keys.stride(1)):
+        raise ValueError("keys and values must share strides")
+    with torch.cuda.device(keys.device):
+        check(LIB.pbk_quest_rope_gather(desc, torch.cuda.current_stream(keys.device).cuda_stream),
+              "pbk_quest_rope_gather")
+    return ok, ov
+
+
+def sink_shift(ref_pos: int, ns: int, n_blk: int, block: int) -> int:
+    """Positions the sink keys move by past ROPE_HORIZON (memory.py:585-596): to just before
+    the first repositioned block."""
+    if ref_pos <= ROPE_HORIZON or ns == 0:
+        return 0
+    base_start = max(ORIGIN, ref_pos - max(ROPE_ARC_SPAN, n_blk * block))
+    return max(0, base_start - ns)
 
 
 def _refresh(arc, block: int) -> None:
@@ -94,26 +158,31 @@ def retrieve_blocks(arc, q: torch.Tensor, groups: int, limit: int, rerank: bool,
     t, h, d = q.shape
     k = min(budget_for(full, rerank, arc.prompt_len, limit, budget), n_valid)
     pool = max(MEMORY["rerank"], 2 * k) if MEMORY["rerank"] > 0 else 0
-    if limit > ROPE_HORIZON and rerank and pool > k:
-        raise NotImplementedError("RoPE repositioning of reranked keys past ROPE_HORIZON (memory.py:861-862)")
     _refresh(arc, block)
     qi = q.to(torch.bfloat16).unsqueeze(0)                        # [1, T, H, D]
-    if limit > ROPE_HORIZON:  # memory.py:795-797: the RoPE'd dims do not score
-        qi = qi.clone()
-        qi[..., : d // 4] = 0
+    qs = qi
+    if limit > ROPE_HORIZON:  # memory.py:795-797: the RoPE'd dims do not score the bounds
+        qs = qi.clone()
+        qs[..., : d // 4] = 0
     kmax, kmin = arc.kmax[:, :full], arc.kmin[:, :full]
     smax, smin = getattr(arc, "smax", None), getattr(arc, "smin", None)
 
     def select(kk: int) -> torch.Tensor:
         if hole != (0, 0):
-            return select_pages_levels(qi, kmax, kmin, full * block, block, kk, hole=hole)
-        return select_pages(qi, kmax, kmin, full * block, block, kk)
+            return select_pages_levels(qs, kmax, kmin, full * block, block, kk, hole=hole)
+        return select_pages(qs, kmax, kmin, full * block, block, kk)
 
     if not rerank and SBLK > 1 and smax is not None and smin is not None and full > SBLK * 16:
-        pages = select_pages_levels(qi, kmax, kmin, full * block, block, k, smax, smin, SBLK, hole)
+        pages = select_pages_levels(qs, kmax, kmin, full * block, block, k, smax, smin, SBLK, hole)
     elif rerank and pool > k:
         cand = select(min(pool, n_valid))                         # [1, KV, c] ascending
-        pages = rerank_pages(qi, arc.keys[:, ORIGIN:], cand, block, k)
+        if limit > ROPE_HORIZON:  # the candidates' keys moved in proportion (memory.py:861-862)
+            c = cand.shape[-1]
+            ck, _ = rope_gather(arc.keys, None, cand[0], block, ORIGIN, c, "proportional", ref_pos=limit)
+            ident = torch.arange(c, dtype=torch.int32, device=q.device).expand(1, cand.shape[1], c).contiguous()
+            pages = cand.gather(-1, rerank_pages(qi, ck, ident, block, k).long()).to(torch.int32)
+        else:
+            pages = rerank_pages(qi, arc.keys[:, ORIGIN:], cand, block, k)
     else:
         pages = select(k)
     top = pages[0].long()
@@ -138,15 +207,26 @@ def piece_attention(arc, q: torch.Tensor, q_pos: torch.Tensor, top: torch.Tensor
     if q_min is None or q_max is None:
         q_min, q_max = int(q_pos.min()), int(q_pos.max())
     lo, hi = max(0, q_min - window + 1), q_max + 1
-    if lo > ROPE_HORIZON:
-        raise NotImplementedError("RoPE repositioning past ROPE_HORIZON (memory.py:574-711)")
     ns = min(SINKS, lo)
     qi = q.to(torch.bfloat16).unsqueeze(0)
     out = torch.empty(1, t, h, d, dtype=torch.float32, device=q.device)
     qpos = q_pos.to(device=q.device, dtype=torch.int32).view(1, t)
     kpos = torch.arange(lo, hi, dtype=torch.int32, device=q.device)
     win = (arc.keys[:, lo:hi], arc.values[:, lo:hi], kpos, window, 0, scale, out)
-    if top is not None:  # retrieved blocks + the partial block before the window
+    rope = lo > ROPE_HORIZON  # sinks and retrieved blocks move to new RoPE positions (memory.py:1402-1425)
+    n_blk = top.shape[1] if top is not None else 0
+    sink_k, sink_v = arc.keys, arc.values
+    shift = sink_shift(lo, ns, n_blk, block) if rope else 0
+    if shift > 0:
+        sink_k, sink_v = rope_gather(arc.keys, arc.values, None, ns, 0, 1, "constant", const_delta=shift)
+    if top is not None and rope:  # [moved blocks ; partial block before the window], gathered
+        tail0 = ORIGIN + ((lo - ORIGIN) // block) * block
+        tail_n = lo - tail0 if lo > tail0 else 0
+        rk, rv = rope_gather(arc.keys, arc.values, top, block, ORIGIN, n_blk, "runs", ref_pos=lo, tail0=tail0,
+                             tail_n=tail_n)
+        ident = torch.arange(n_blk, dtype=torch.int32, device=q.device).expand(1, h // groups, n_blk).contiguous()
+        desc = _attend_desc(qi, qpos, rk, rv, n_blk * block + tail_n, block, ident, *win)
+    elif top is not None:  # retrieved blocks + the partial block before the window, in place
         desc = _attend_desc(qi, qpos, arc.keys[:, ORIGIN:], arc.values[:, ORIGIN:], max(0, lo - ORIGIN), block,
                             top.to(torch.int32).unsqueeze(0).contiguous(), *win)
     else:  # sinks and window only: no archive part
@@ -155,8 +235,8 @@ def piece_attention(arc, q: torch.Tensor, q_pos: torch.Tensor, top: torch.Tensor
         desc.n_arch, desc.budget = 0, 0
     ws = _workspace(LIB.pbk_quest_attend_sinks_workspace(desc, ns), q.device)
     with torch.cuda.device(q.device):
-        check(LIB.pbk_quest_attend_sinks(desc, arc.keys.data_ptr(), arc.values.data_ptr(), ns, arc.keys.stride(0),
-                                         arc.keys.stride(1), ws.data_ptr(), ws.numel(),
+        check(LIB.pbk_quest_attend_sinks(desc, sink_k.data_ptr(), sink_v.data_ptr(), ns, sink_k.stride(0),
+                                         sink_k.stride(1), ws.data_ptr(), ws.numel(),
                                          torch.cuda.current_stream(q.device).cuda_stream),
               "pbk_quest_attend_sinks")
     return out[0].to(q.dtype)

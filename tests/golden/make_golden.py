@@ -33,6 +33,9 @@ Fixtures:
                   pages, 101 full pages), exact rerank, neighbours and a kept prompt selection;
                   the serving retrieve_blocks' super-block path, with and without an archive
                   hole, its flat path with a hole and its rerank path with a hole.
+  rope.npz        RoPE repositioning past the horizon (lowered to 1500 tokens): the block moves
+                  in both modes and the sink move called directly, and retrieve_blocks (rerank,
+                  flat) + piece_attention on a 3000-token serving archive.
   quest.npz       archive_append + retrieve (flat mode, page 16, budget 4 pages) for a
                   decode query (T=1) and a 3-token query, plus the exact attention over
                   [retrieved ; window] as pseudobrain/transplant.py:619-628 computes it.
@@ -226,6 +229,50 @@ def make_quest_levels(E, MEM):
     np.savez_compressed(os.path.join(HERE, "quest_levels.npz"), **out)
 
 
+def make_rope(MEM):
+    """RoPE repositioning past the horizon (pb27_vllm/memory.py:574-677): the block and sink
+    moves called directly, then retrieve_blocks (rerank and flat) and piece_attention on an
+    archive whose window starts past the horizon. The horizon and arc span are lowered
+    (ROPE_HORIZON 1500, ROPE_ARC_SPAN 600) so a 3000-token archive crosses them."""
+    import torch
+    MEM.ROPE_HORIZON, MEM.ROPE_ARC_SPAN = 1500, 600
+    kv, groups, d, block = 2, 3, 128, 16
+    gen = torch.Generator().manual_seed(109)
+    out = dict(horizon=np.int64(1500), arc_span=np.int64(600), theta=np.float64(MEM.ROPE_THETA), block=np.int64(block))
+    # direct: 9 blocks with runs and gaps, ref_pos 2900
+    idx = torch.tensor([[3, 4, 5, 9, 20, 21, 40, 41, 42], [0, 7, 8, 9, 10, 60, 61, 70, 100]])
+    rk = torch.randn(kv, 9 * block, d, generator=gen).to(torch.bfloat16)
+    sk = torch.randn(kv, 4, d, generator=gen).to(torch.bfloat16)
+    out.update(rk=_bits(rk), idx=idx.numpy().astype(np.int64), sk=_bits(sk), ref_pos=np.int64(2900),
+               rk_runs=_bits(MEM._reposition_rope_blocks(rk, idx, block, 2900, contiguous_runs=True)),
+               rk_prop=_bits(MEM._reposition_rope_blocks(rk, idx, block, 2900, contiguous_runs=False, span=0)),
+               sk_moved=_bits(MEM._reposition_rope_sinks(sk, 2900, n_blk=9, block=block)))
+    # end to end on an archive
+    MEM.MEMORY.update(blocks=4, decode_blocks=4, rerank=12, block_size=block, neighbors=0, window=256)
+    cap = MEM.ORIGIN + 190 * block + 9
+    keys = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    values = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    n_blk = cap // block
+    arc = MEM.Archive(keys, values, torch.empty(kv, n_blk, d), torch.empty(kv, n_blk, d))
+    arc.size = arc.prompt_len = cap
+    arc.dirty_lo, arc.dirty_hi = 0, n_blk - 1
+    arc.refresh_bounds(block)
+    out.update(keys=_bits(keys.to(torch.bfloat16)), values=_bits(values.to(torch.bfloat16)), window=np.int64(256),
+               groups=np.int64(groups))
+    for name, t, rerank in (("rr", 1, True), ("flat", 2, False)):
+        q = torch.randn(t, kv * groups, d, generator=gen).to(torch.bfloat16).float()
+        q_pos = torch.arange(cap - t, cap)
+        q_min, q_max = int(q_pos[0]), int(q_pos[-1])
+        limit = q_min - 256 + 1
+        top = MEM.retrieve_blocks(arc, q, groups, limit, rerank)
+        o = MEM.piece_attention(arc, q, q_pos, top, groups, 256, d ** -0.5, None, q_min=q_min, q_max=q_max)
+        out.update({f"{name}_q": _bits(q.to(torch.bfloat16)), f"{name}_pos": q_pos.numpy().astype(np.int64),
+                    f"{name}_limit": np.int64(limit), f"{name}_rerank": np.int64(rerank),
+                    f"{name}_top": top.numpy().astype(np.int64), f"{name}_out": o.float().numpy()})
+    MEM.ROPE_HORIZON, MEM.ROPE_ARC_SPAN = 262144, 98304
+    np.savez_compressed(os.path.join(HERE, "rope.npz"), **out)
+
+
 def make_swa(TR):
     import torch
     out = {}
@@ -330,7 +377,7 @@ def main(reference_root: str) -> None:
     import pb27_vllm.memory as MEM
     makers = {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR),
               "serving": lambda: make_serving(MEM), "gdn_io": lambda: make_gdn_io(G),
-              "quest_levels": lambda: make_quest_levels(E, MEM)}
+              "quest_levels": lambda: make_quest_levels(E, MEM), "rope": lambda: make_rope(MEM)}
     for name in (sys.argv[2:] if len(sys.argv) > 2 else makers):  # all, or only the named fixtures
         makers[name]()
     for name in sorted(os.listdir(HERE)):

@@ -219,3 +219,44 @@ def test_serving_levels_match_reference(levels, case):
                               bool(f[f"{case}_rerank"]), mem, keys.shape[1], smax if use_sb else None,
                               smin if use_sb else None, sblk, tuple(int(x) for x in f[f"{case}_hole"]))
     assert np.array_equal(top, f[f"{case}_top"])
+
+
+@pytest.fixture(scope="module")
+def rope():
+    return load_golden("rope.npz")
+
+
+def test_rope_moves_match_reference(rope):
+    """The block moves (contiguous runs, proportional) and the sink move (pb27_vllm/memory.py:
+    574-677): bf16 outputs equal the reference's but for rare last-bit differences of cos/sin."""
+    from oracle import serving as osv
+    f = rope
+    args = (int(f["horizon"]), int(f["arc_span"]), float(f["theta"]))
+    rk, sk, idx, block, ref_pos = _f32(f["rk"]), _f32(f["sk"]), f["idx"], int(f["block"]), int(f["ref_pos"])
+    for got, want in ((osv.reposition_blocks(rk, idx, block, ref_pos, True, *args), f["rk_runs"]),
+                      (osv.reposition_blocks(rk, idx, block, ref_pos, False, *args), f["rk_prop"]),
+                      (osv.reposition_sinks(sk, ref_pos, idx.shape[1], block, *args), f["sk_moved"])):
+        w = _f32(want)
+        assert np.mean(oq.bf16_bits(got) != want) < 1e-3
+        assert np.allclose(got, w, rtol=1e-2, atol=1e-2)
+    assert not np.array_equal(f["rk_runs"], f["rk"])  # the moves did turn the keys
+
+
+@pytest.mark.parametrize("case", ["rr", "flat"])
+def test_rope_serving_matches_reference(rope, case):
+    """retrieve_blocks (rerank with moved candidate keys; flat with the RoPE dims masked) and
+    piece_attention with moved sinks and blocks, past a lowered horizon."""
+    from oracle import serving as osv
+    f = rope
+    args = (int(f["horizon"]), int(f["arc_span"]), float(f["theta"]))
+    keys, values = _f32(f["keys"]), _f32(f["values"])
+    block, groups, window = int(f["block"]), int(f["groups"]), int(f["window"])
+    kmax, kmin = oq.page_bounds(keys[None, :, 4:4 + ((keys.shape[1] - 4) // block) * block], block)
+    mem = dict(blocks=4, decode_blocks=4, rerank=12, block_size=block, window=window)
+    q = _f32(f[f"{case}_q"])
+    top = osv.retrieve_blocks(keys, kmax[0], kmin[0], q, groups, int(f[f"{case}_limit"]), bool(f[f"{case}_rerank"]),
+                              mem, keys.shape[1], rope=args, bf16_keys=False)  # the reference ran on fp32 keys
+    assert np.array_equal(top, f[f"{case}_top"])
+    o = osv.piece_attention(keys, values, q, f[f"{case}_pos"], top, groups, window, 128 ** -0.5, block, rope=args,
+                            bf16_keys=False)
+    assert ogdn.rel_err(o, f[f"{case}_out"]) < 1e-4
