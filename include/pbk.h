@@ -378,6 +378,45 @@ typedef struct pbk_rope_gather_desc {
 
 PBK_API int pbk_quest_rope_gather(const pbk_rope_gather_desc* desc, void* stream);
 
+/* The serving archive's KV write fused with its block summaries (pb27_vllm/memory.py:310-395
+ * Archive.write, :399-430 _refresh_range). New rows [n, kv, d] (token-major, as the KV cache
+ * hands them over) go to archive rows p0 .. p0 + n - 1 (pos NULL) or pos[i] (int32, any
+ * order). For every block b in [blk_lo, blk_hi] (rows origin + b * block ..) over the rows
+ * written so far, end = max(size, p0 + n) (contiguous) or size: kmax / kmin = elementwise
+ * max / min of the keys, kmean / vmean (optional) = mean of the keys / values with a partial
+ * block padded by its last row (as the reference pads it); new rows are read once, from the
+ * input, and written as they are summarised. A contiguous write passes the blocks it touches
+ * (the reference's fast path plus its refresh of the partial ends); a write with pos passes
+ * none (blk_hi < blk_lo) and refreshes its blocks later with n = 0. All bf16. */
+typedef struct pbk_archive_write_desc {
+  int32_t kv, d, block, origin;  /* d must be 128 */
+  int32_t cap, size;             /* archive rows; rows written before this call */
+  int32_t p0, n;
+  int32_t blk_lo, blk_hi;
+  const int32_t* pos;            /* [n] rows, or NULL: contiguous from p0 */
+  const void* k;
+  const void* v;
+  int64_t in_stride_n, in_stride_kv;
+  void* keys;
+  void* values;
+  int64_t arc_stride_kv, arc_stride_n;
+  void* kmax;
+  void* kmin;
+  void* kmean;                   /* may be NULL */
+  void* vmean;                   /* may be NULL */
+  int64_t bnd_stride_kv, bnd_stride_p;
+} pbk_archive_write_desc;
+
+PBK_API int pbk_quest_archive_write(const pbk_archive_write_desc* desc, void* stream);
+
+/* Super-block means (memory.py:296-306): smean[h][s] = mean of bmean[h][b] over the blocks b
+ * in [s * sblk, min(n_blk, (s + 1) * sblk)), for s in [first_sb, min(end_sb, ceil(n_blk /
+ * sblk))); bf16, fp32 sums. Same arguments as pbk_quest_superbounds with one input and one
+ * output. */
+PBK_API int pbk_quest_supermeans(const void* bmean, int32_t kv, int32_t n_blk, int32_t d, int32_t sblk,
+                                 int64_t bnd_stride_kv, int64_t bnd_stride_p, void* smean, int64_t sb_stride_kv,
+                                 int64_t sb_stride_p, int32_t first_sb, int32_t end_sb, void* stream);
+
 /* Options of pbk_quest_select_levels. */
 typedef struct pbk_quest_levels {
   const void* smax;         /* bf16 super-block bounds [kv, >= ceil(full / sblk), d]; NULL: one level */

@@ -240,3 +240,93 @@ def piece_attention(keys, values, q, q_pos, top, groups, window, scale, block,
             p /= p.sum(-1, keepdims=True)
             out[:, hq] = p @ vv
     return out
+
+
+class ArchiveState:
+    """The serving archive's storage and block summaries, memory.py:120-431, restated: keys /
+    values [KV, cap, D] (fp32 holding bf16 values), per-block kmax, kmin, bmean_k, bmean_v
+    [KV, cap // block, D] and per-super-block smax, smin, smean_k, smean_v (fp32; the GPU
+    keeps them in bf16). Blocks start after ORIGIN sink positions."""
+
+    def __init__(self, kv: int, d: int, cap: int, block: int, sblk: int):
+        n_blk = cap // block
+        n_sb = (n_blk + sblk - 1) // sblk
+        self.block, self.sblk, self.size = block, sblk, 0
+        self.keys = np.zeros((kv, cap, d), np.float32)
+        self.values = np.zeros((kv, cap, d), np.float32)
+        for name, rows in (("kmax", n_blk), ("kmin", n_blk), ("bmean_k", n_blk), ("bmean_v", n_blk),
+                           ("smax", n_sb), ("smin", n_sb), ("smean_k", n_sb), ("smean_v", n_sb)):
+            setattr(self, name, np.zeros((kv, rows, d), np.float32))
+        self.dirty_lo, self.dirty_hi = 1 << 60, -1
+
+    def _refresh_range(self, lo_b: int, hi_b: int) -> None:
+        """memory.py:399-421: the summaries of blocks lo_b .. hi_b over the rows written, a
+        partial block padded with its last row."""
+        block = self.block
+        lo, hi = ORIGIN + lo_b * block, min(self.size, ORIGIN + (hi_b + 1) * block)
+        if hi <= lo:
+            return
+        seg, seg_v = self.keys[:, lo:hi], self.values[:, lo:hi]
+        pad = (-seg.shape[1]) % block
+        if pad:
+            seg = np.concatenate((seg, np.repeat(seg[:, -1:], pad, axis=1)), axis=1)
+            seg_v = np.concatenate((seg_v, np.repeat(seg_v[:, -1:], pad, axis=1)), axis=1)
+        kvh, _, d = seg.shape
+        blocks, blocks_v = seg.reshape(kvh, -1, block, d), seg_v.reshape(kvh, -1, block, d)
+        nb = blocks.shape[1]
+        self.kmax[:, lo_b:lo_b + nb] = blocks.max(2)
+        self.kmin[:, lo_b:lo_b + nb] = blocks.min(2)
+        self.bmean_k[:, lo_b:lo_b + nb] = blocks.astype(np.float64).mean(2)
+        self.bmean_v[:, lo_b:lo_b + nb] = blocks_v.astype(np.float64).mean(2)
+
+    def _update_superbounds(self, lo_b: int, hi_b: int) -> None:
+        """memory.py:280-306."""
+        sblk = self.sblk
+        if hi_b < lo_b or self.size <= ORIGIN:
+            return
+        n_blk = min(self.kmax.shape[1], (self.size - ORIGIN + self.block - 1) // self.block)
+        sb0 = max(0, lo_b // sblk)
+        sb1 = min(self.smax.shape[1] - 1, min(hi_b, max(0, n_blk - 1)) // sblk)
+        for sb in range(sb0, sb1 + 1):
+            b0, b1 = sb * sblk, min(n_blk, (sb + 1) * sblk)
+            if b1 > b0:
+                self.smax[:, sb] = self.kmax[:, b0:b1].max(1)
+                self.smin[:, sb] = self.kmin[:, b0:b1].min(1)
+                self.smean_k[:, sb] = self.bmean_k[:, b0:b1].astype(np.float64).mean(1)
+                self.smean_v[:, sb] = self.bmean_v[:, b0:b1].astype(np.float64).mean(1)
+
+    def write(self, pos: np.ndarray, k: np.ndarray, v: np.ndarray) -> None:
+        """Archive.write (memory.py:310-395) for an archive that holds `pos`: k/v [N, KV, D]."""
+        block = self.block
+        hi, p0, n = int(pos.max()) + 1, int(pos.min()), pos.size
+        contig = hi - p0 == n
+        self.keys[:, pos] = k.transpose(1, 0, 2)
+        self.values[:, pos] = v.transpose(1, 0, 2)
+        fast, b_start, b_end = False, 0, 0
+        if hi - 1 >= ORIGIN and contig and n >= block:
+            b_start = max(0, (p0 - ORIGIN + block - 1) // block)
+            b_end = max(b_start, (hi - ORIGIN) // block)
+            if b_end > b_start:
+                self.size = max(self.size, hi)
+                self._refresh_range(b_start, b_end - 1)  # full blocks: the same summaries as the fast path
+                fast = True
+        self.size = max(self.size, hi)
+        if hi - 1 < ORIGIN:
+            return
+        lo_b, hi_b = max(0, p0 - ORIGIN) // block, (hi - 1 - ORIGIN) // block
+        if fast:
+            if lo_b < b_start:
+                self._refresh_range(lo_b, b_start - 1)
+            if hi_b >= b_end:
+                self._refresh_range(b_end, hi_b)
+            self._update_superbounds(lo_b, hi_b)
+            return
+        self.dirty_lo, self.dirty_hi = min(self.dirty_lo, lo_b), max(self.dirty_hi, hi_b)
+
+    def refresh_bounds(self) -> None:
+        """memory.py:423-430."""
+        if self.dirty_hi < self.dirty_lo:
+            return
+        self._refresh_range(self.dirty_lo, self.dirty_hi)
+        self._update_superbounds(self.dirty_lo, self.dirty_hi)
+        self.dirty_lo, self.dirty_hi = 1 << 60, -1

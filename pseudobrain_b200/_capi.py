@@ -95,6 +95,17 @@ class PbkRopeGatherDesc(ctypes.Structure):
                 ("delta", ctypes.c_void_p)]
 
 
+class PbkArchiveWriteDesc(ctypes.Structure):
+    _fields_ = [("kv", ctypes.c_int32), ("d", ctypes.c_int32), ("block", ctypes.c_int32), ("origin", ctypes.c_int32),
+                ("cap", ctypes.c_int32), ("size", ctypes.c_int32), ("p0", ctypes.c_int32), ("n", ctypes.c_int32),
+                ("blk_lo", ctypes.c_int32), ("blk_hi", ctypes.c_int32), ("pos", ctypes.c_void_p),
+                ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("in_stride_n", ctypes.c_int64),
+                ("in_stride_kv", ctypes.c_int64), ("keys", ctypes.c_void_p), ("values", ctypes.c_void_p),
+                ("arc_stride_kv", ctypes.c_int64), ("arc_stride_n", ctypes.c_int64), ("kmax", ctypes.c_void_p),
+                ("kmin", ctypes.c_void_p), ("kmean", ctypes.c_void_p), ("vmean", ctypes.c_void_p),
+                ("bnd_stride_kv", ctypes.c_int64), ("bnd_stride_p", ctypes.c_int64)]
+
+
 _QD = ctypes.POINTER(PbkQuestDesc)
 _QL = ctypes.POINTER(PbkQuestLevels)
 _VP, _I32, _I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
@@ -136,6 +147,9 @@ SIGNATURES = {
     "pbk_quest_select_levels_workspace": (ctypes.c_size_t, [_QD, _QL]),
     "pbk_quest_select_levels": (ctypes.c_int, [_QD, _QL, _VP, ctypes.c_size_t, _VP]),
     "pbk_quest_rope_gather": (ctypes.c_int, [ctypes.POINTER(PbkRopeGatherDesc), _VP]),
+    "pbk_quest_archive_write": (ctypes.c_int, [ctypes.POINTER(PbkArchiveWriteDesc), _VP]),
+    "pbk_quest_supermeans": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I64, _I64, _VP, _I64, _I64, _I32, _I32,
+                                            _VP]),
     "pbk_swa_prefill": (ctypes.c_int, [ctypes.POINTER(PbkSwaDesc), _VP]),
 }
 

@@ -488,6 +488,51 @@ int pbk_quest_rope_gather(const pbk_rope_gather_desc* d, void* stream) {
   return launch_status(pbk::launch_quest_rope_gather(*d, static_cast<cudaStream_t>(stream)));
 }
 
+int pbk_quest_archive_write(const pbk_archive_write_desc* d, void* stream) {
+  if (d == nullptr) return PBK_ERR_INVALID;
+  if (d->kv < 1 || d->block < 1 || d->origin < 0 || d->cap < 0 || d->size < 0 || d->n < 0 || d->p0 < 0)
+    return PBK_ERR_INVALID;
+  if (d->d != 128) return PBK_ERR_SHAPE;
+  const bool blocks = d->blk_hi >= d->blk_lo;
+  if (blocks && (d->blk_lo < 0 || (int64_t)d->origin + ((int64_t)d->blk_hi + 1) * d->block > (int64_t)d->cap + d->block))
+    return PBK_ERR_INVALID;  // summarised blocks start inside the archive
+  if (d->pos == nullptr && (int64_t)d->p0 + d->n > d->cap) return PBK_ERR_INVALID;
+  if (d->n == 0 && !blocks) return PBK_OK;
+  if (!d->keys || !d->values) return PBK_ERR_INVALID;
+  if (d->n > 0 && (!d->k || !d->v)) return PBK_ERR_INVALID;
+  if (blocks && (!d->kmax || !d->kmin)) return PBK_ERR_INVALID;
+  if (!aligned16(d->keys) || !aligned16(d->values) || !aligned_elems(d->arc_stride_kv, 8) ||
+      !aligned_elems(d->arc_stride_n, 8))
+    return PBK_ERR_ALIGN;
+  if (d->n > 0 && (!aligned16(d->k) || !aligned16(d->v) || !aligned_elems(d->in_stride_n, 8) ||
+                   !aligned_elems(d->in_stride_kv, 8)))
+    return PBK_ERR_ALIGN;
+  if (blocks && (!aligned16(d->kmax) || !aligned16(d->kmin) || (d->kmean && !aligned16(d->kmean)) ||
+                 (d->vmean && !aligned16(d->vmean)) || !aligned_elems(d->bnd_stride_kv, 8) ||
+                 !aligned_elems(d->bnd_stride_p, 8)))
+    return PBK_ERR_ALIGN;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_quest_archive_write(*d, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_quest_supermeans(const void* bmean, int32_t kv, int32_t n_blk, int32_t d, int32_t sblk, int64_t bnd_stride_kv,
+                         int64_t bnd_stride_p, void* smean, int64_t sb_stride_kv, int64_t sb_stride_p,
+                         int32_t first_sb, int32_t end_sb, void* stream) {
+  if (kv < 1 || n_blk < 0 || sblk < 1 || first_sb < 0) return PBK_ERR_INVALID;
+  if (d != 128) return PBK_ERR_SHAPE;
+  if (n_blk == 0 || end_sb <= first_sb || first_sb * (int64_t)sblk >= n_blk) return PBK_OK;
+  if (!bmean || !smean) return PBK_ERR_INVALID;
+  if (!aligned16(bmean) || !aligned16(smean) || bnd_stride_kv % 8 || bnd_stride_p % 8 || sb_stride_kv % 8 ||
+      sb_stride_p % 8)
+    return PBK_ERR_ALIGN;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_quest_supermeans(bmean, kv, n_blk, sblk, bnd_stride_kv, bnd_stride_p, smean,
+                                                    sb_stride_kv, sb_stride_p, first_sb, end_sb,
+                                                    static_cast<cudaStream_t>(stream)));
+}
+
 namespace {
 int validate_levels(const pbk_quest_desc* d, const pbk_quest_levels* lv) {
   int st = validate_quest(d, 1);

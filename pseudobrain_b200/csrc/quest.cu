@@ -920,6 +920,107 @@ __global__ void __launch_bounds__(256) quest_rope_gather_kernel(const pbk_rope_g
   }
 }
 
+// ---------------------------------------------------------------------------------
+// Archive write (pb27_vllm/memory.py:310-430). Rows that no summarised block covers are
+// copied by one warp per (row, key head); each summarised block is one warp per (block, key
+// head) that reads its rows once (new rows from the input, which it also writes, older rows
+// from the archive) and keeps max, min and the fp32 sums of keys and values in registers.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ void ld4(const bf16* p, float (&x)[4]) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  const float2 a = __bfloat1622float2(pr[0]), b = __bfloat1622float2(pr[1]);
+  x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y;
+}
+__device__ __forceinline__ void st4(bf16* p, const float (&x)[4]) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(bf16x2_bits(x[0], x[1]), bf16x2_bits(x[2], x[3]));
+}
+
+__global__ void __launch_bounds__(256) quest_archive_copy_kernel(const pbk_archive_write_desc d) {
+  const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * 8 + warp;
+  if (i >= d.n) return;
+  const int64_t r = d.pos ? (int64_t)d.pos[i] : (int64_t)d.p0 + i;
+  if (r < 0 || r >= d.cap) return;
+  if (r >= d.origin) {  // rows of a summarised block are written by its warp
+    const int64_t b = (r - d.origin) / d.block;
+    if (b >= d.blk_lo && b <= d.blk_hi) return;
+  }
+  const int64_t src = (int64_t)i * d.in_stride_n + h * d.in_stride_kv + 4 * lane;
+  const int64_t dst = h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
+  *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(d.keys) + dst) =
+      *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(d.k) + src);
+  *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(d.values) + dst) =
+      *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(d.v) + src);
+}
+
+__global__ void __launch_bounds__(256) quest_archive_block_kernel(const pbk_archive_write_desc d, int nblocks) {
+  const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = blockIdx.x * 8 + warp;
+  if (w >= nblocks) return;
+  const int64_t b = (int64_t)d.blk_lo + w;
+  const int64_t r0 = d.origin + b * d.block;
+  const int64_t end = d.pos ? (int64_t)d.size : max((int64_t)d.size, (int64_t)d.p0 + d.n);
+  const int64_t r1 = min(r0 + d.block, min(end, (int64_t)d.cap));
+  if (r1 <= r0) return;  // nothing written in this block yet
+  const bf16* in_k = reinterpret_cast<const bf16*>(d.k);
+  const bf16* in_v = reinterpret_cast<const bf16*>(d.v);
+  bf16* ak = reinterpret_cast<bf16*>(d.keys);
+  bf16* av = reinterpret_cast<bf16*>(d.values);
+  float mx[4], mn[4], sk[4] = {0.f, 0.f, 0.f, 0.f}, sv[4] = {0.f, 0.f, 0.f, 0.f}, kl[4], vl[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) mx[e] = -FLT_MAX, mn[e] = FLT_MAX;
+  for (int64_t r = r0; r < r1; ++r) {
+    const bool fresh = d.pos == nullptr && r >= d.p0 && r < (int64_t)d.p0 + d.n;
+    const int64_t at = h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
+    if (fresh) {
+      const int64_t src = (r - d.p0) * d.in_stride_n + h * d.in_stride_kv + 4 * lane;
+      ld4(in_k + src, kl);
+      ld4(in_v + src, vl);
+      st4(ak + at, kl);  // bf16 in, bf16 out: the row as it came
+      st4(av + at, vl);
+    } else {
+      ld4(ak + at, kl);
+      ld4(av + at, vl);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      mx[e] = fmaxf(mx[e], kl[e]), mn[e] = fminf(mn[e], kl[e]);
+      sk[e] += kl[e], sv[e] += vl[e];
+    }
+  }
+  const float pad = (float)(r0 + d.block - r1);  // a partial block counts its last row again
+  const int64_t bo = h * d.bnd_stride_kv + b * d.bnd_stride_p + 4 * lane;
+  float km[4], vm[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    km[e] = (sk[e] + pad * kl[e]) / (float)d.block;
+    vm[e] = (sv[e] + pad * vl[e]) / (float)d.block;
+  }
+  st4(reinterpret_cast<bf16*>(d.kmax) + bo, mx);
+  st4(reinterpret_cast<bf16*>(d.kmin) + bo, mn);
+  if (d.kmean) st4(reinterpret_cast<bf16*>(d.kmean) + bo, km);
+  if (d.vmean) st4(reinterpret_cast<bf16*>(d.vmean) + bo, vm);
+}
+
+// Super-block means (memory.py:296-306): warp per (super-block, key head).
+__global__ void quest_supermeans_kernel(const bf16* bmean, int64_t bs_kv, int64_t bs_p, int n_blk, int sblk,
+                                        bf16* smean, int64_t ss_kv, int64_t ss_p, int first_sb, int nsb) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= nsb) return;
+  const int s = first_sb + warp, h = blockIdx.y;
+  const int b0 = s * sblk, b1 = min(b0 + sblk, n_blk);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, x[4];
+  for (int b = b0; b < b1; ++b) {
+    ld4(bmean + h * bs_kv + (int64_t)b * bs_p + 4 * lane, x);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[e] += x[e];
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) acc[e] /= (float)(b1 - b0);
+  st4(smean + h * ss_kv + (int64_t)s * ss_p + 4 * lane, acc);
+}
+
 // Pages [lo, hi) of every score row score -inf (the archive hole, memory.py:852-853).
 __global__ void quest_hole_kernel(float* scores, int npages, int nrows, int lo, int hi) {
   const int w = hi - lo;
@@ -1181,6 +1282,24 @@ cudaError_t launch_quest_rope_gather(const pbk_rope_gather_desc& d, cudaStream_t
   if (rows == 0) return cudaSuccess;
   if ((d.mode == 1 || d.mode == 2) && d.n_blk > 0) quest_rope_delta_kernel<<<d.kv, 32, 0, st>>>(d);
   quest_rope_gather_kernel<<<dim3((unsigned)((rows + 7) / 8), d.kv), 256, 0, st>>>(d);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quest_archive_write(const pbk_archive_write_desc& d, cudaStream_t st) {
+  if (d.n > 0) quest_archive_copy_kernel<<<dim3((unsigned)((d.n + 7) / 8), d.kv), 256, 0, st>>>(d);
+  const int nblocks = d.blk_hi - d.blk_lo + 1;
+  if (nblocks > 0) quest_archive_block_kernel<<<dim3((unsigned)((nblocks + 7) / 8), d.kv), 256, 0, st>>>(d, nblocks);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quest_supermeans(const void* bmean, int kv, int n_blk, int sblk, int64_t bs_kv, int64_t bs_p,
+                                    void* smean, int64_t ss_kv, int64_t ss_p, int first_sb, int end_sb,
+                                    cudaStream_t st) {
+  const int nsb = min(end_sb, (n_blk + sblk - 1) / sblk) - first_sb;
+  if (nsb <= 0) return cudaSuccess;
+  quest_supermeans_kernel<<<dim3((nsb + 7) / 8, kv), 256, 0, st>>>(static_cast<const bf16*>(bmean), bs_kv, bs_p, n_blk,
+                                                                    sblk, static_cast<bf16*>(smean), ss_kv, ss_p,
+                                                                    first_sb, nsb);
   return cudaGetLastError();
 }
 

@@ -20,9 +20,12 @@ ROPE_HORIZON the reranked candidates' keys, the sinks and the retrieved blocks m
 RoPE positions as the reference moves them (:574-677, 861-862, 1402-1425), gathered with
 the move (pbk_quest_rope_gather).
 
+``archive_write`` is Archive.write (:310-395) for an archive in HBM: the KV write fused
+with the block summaries (max, min, key and value means) and the super-block refresh.
+
 Kernels: pbk_quest_select (scores + top-k), pbk_quest_select_levels, pbk_quest_rerank,
-pbk_quest_superbounds, pbk_quest_rope_gather, pbk_quest_attend_sinks (libpbk.so, sm_100a);
-head dim 128.
+pbk_quest_superbounds, pbk_quest_supermeans, pbk_quest_archive_write, pbk_quest_rope_gather,
+pbk_quest_attend_sinks (libpbk.so, sm_100a); head dim 128.
 """
 from __future__ import annotations
 
@@ -32,7 +35,7 @@ import torch
 
 from . import _capi
 from ._capi import LIB, check
-from .exact_memory import (_attend_desc, _workspace, page_bounds_, rerank_pages, select_pages, select_pages_levels,
+from .exact_memory import (_attend_desc, _workspace, rerank_pages, select_pages, select_pages_levels,
                            super_bounds_)
 
 # memory.py:33-34 defaults (window: PB27_WINDOW, 16384)
@@ -104,25 +107,130 @@ def sink_shift(ref_pos: int, ns: int, n_blk: int, block: int) -> int:
     return max(0, base_start - ns)
 
 
+def _write(arc, block: int, size: int, blk_lo: int, blk_hi: int, k=None, v=None, p0: int = 0,
+           pos: torch.Tensor | None = None) -> None:
+    """pbk_quest_archive_write: new rows k/v [N, KV, D] at p0.. (or at pos) into the archive,
+    and the max, min and (when the archive keeps them) mean summaries of blocks
+    [blk_lo, blk_hi] over the rows written so far."""
+    kv, cap, d = arc.keys.shape
+    bmean_k, bmean_v = getattr(arc, "bmean_k", None), getattr(arc, "bmean_v", None)
+    if blk_hi >= blk_lo and blk_hi >= arc.kmax.shape[1]:
+        raise ValueError(f"block {blk_hi} past the bounds array ({arc.kmax.shape[1]} blocks)")
+    if (arc.values.stride(0), arc.values.stride(1)) != (arc.keys.stride(0), arc.keys.stride(1)):
+        raise ValueError("archive keys and values must share strides")
+    for t_ in (bmean_k, bmean_v):
+        if t_ is not None and (t_.dtype != torch.bfloat16 or t_.stride() != arc.kmax.stride()):
+            raise ValueError("block means must be bf16 in the bounds' layout")
+    n = 0 if k is None else k.shape[0]
+    pos32 = pos.to(device=arc.keys.device, dtype=torch.int32).contiguous() if pos is not None else None
+    if k is not None:
+        k, v = k.to(torch.bfloat16), v.to(torch.bfloat16)
+        if k.stride(-1) != 1 or v.stride() != k.stride():
+            raise ValueError("k and v must share strides with a contiguous last dim")
+    desc = _capi.PbkArchiveWriteDesc(
+        kv=kv, d=d, block=block, origin=ORIGIN, cap=cap, size=size, p0=p0, n=n, blk_lo=blk_lo, blk_hi=blk_hi,
+        pos=pos32.data_ptr() if pos32 is not None else None, k=k.data_ptr() if k is not None else None,
+        v=v.data_ptr() if v is not None else None, in_stride_n=k.stride(0) if k is not None else 0,
+        in_stride_kv=k.stride(1) if k is not None else 0, keys=arc.keys.data_ptr(), values=arc.values.data_ptr(),
+        arc_stride_kv=arc.keys.stride(0), arc_stride_n=arc.keys.stride(1), kmax=arc.kmax.data_ptr(),
+        kmin=arc.kmin.data_ptr(), kmean=bmean_k.data_ptr() if bmean_k is not None else None,
+        vmean=bmean_v.data_ptr() if bmean_v is not None else None, bnd_stride_kv=arc.kmax.stride(0),
+        bnd_stride_p=arc.kmax.stride(1))
+    with torch.cuda.device(arc.keys.device):
+        check(LIB.pbk_quest_archive_write(desc, torch.cuda.current_stream(arc.keys.device).cuda_stream),
+              "pbk_quest_archive_write")
+
+
+def _update_super(arc, lo_b: int, hi_b: int, block: int) -> None:
+    """Super-block bounds and means over the blocks [lo_b, hi_b] touched (memory.py:280-306)."""
+    smax, smin = getattr(arc, "smax", None), getattr(arc, "smin", None)
+    size = min(arc.keys.shape[1], getattr(arc, "size", arc.keys.shape[1]))
+    if smax is None or smin is None or hi_b < lo_b or size <= ORIGIN:
+        return
+    n_blk = min(arc.kmax.shape[1], (size - ORIGIN + block - 1) // block)
+    sb0 = max(0, lo_b // SBLK)
+    sb1 = min(smax.shape[1] - 1, min(hi_b, max(0, n_blk - 1)) // SBLK)
+    if sb1 < sb0:
+        return
+    super_bounds_(arc.kmax, arc.kmin, n_blk, SBLK, smax, smin, sb0, sb1 + 1)
+    for src, dst in (("bmean_k", "smean_k"), ("bmean_v", "smean_v")):
+        bm, sm = getattr(arc, src, None), getattr(arc, dst, None)
+        if bm is None or sm is None:
+            continue
+        with torch.cuda.device(bm.device):
+            check(LIB.pbk_quest_supermeans(bm.data_ptr(), bm.shape[0], n_blk, bm.shape[2], SBLK, bm.stride(0),
+                                           bm.stride(1), sm.data_ptr(), sm.stride(0), sm.stride(1), sb0, sb1 + 1,
+                                           torch.cuda.current_stream(bm.device).cuda_stream), "pbk_quest_supermeans")
+
+
 def _refresh(arc, block: int) -> None:
-    """Recompute the bounds of blocks [dirty_lo, dirty_hi] and of the super-blocks holding
-    them (memory.py:280-306, 399-430)."""
+    """Recompute the summaries of blocks [dirty_lo, dirty_hi] (max, min and the means the
+    archive keeps) and of the super-blocks holding them (memory.py:280-306, 399-430)."""
     lo, hi = getattr(arc, "dirty_lo", 1 << 60), getattr(arc, "dirty_hi", -1)
     if hi < lo:
         return
     size = min(arc.keys.shape[1], getattr(arc, "size", arc.keys.shape[1]))
-    # written keys after the sinks, up to the end of block dirty_hi and of the bounds array
-    n = min(size - ORIGIN, (hi + 1) * block, arc.kmax.shape[1] * block)
-    if n > 0 and lo * block < n:
-        page_bounds_(arc.keys[:, ORIGIN:ORIGIN + n], block, arc.kmax, arc.kmin, first_page=lo)
-    smax, smin = getattr(arc, "smax", None), getattr(arc, "smin", None)
-    if smax is not None and smin is not None and size > ORIGIN:
-        n_blk = min(arc.kmax.shape[1], (size - ORIGIN + block - 1) // block)
-        sb0 = max(0, lo // SBLK)
-        sb1 = min(smax.shape[1] - 1, min(hi, max(0, n_blk - 1)) // SBLK)
-        if sb1 >= sb0:
-            super_bounds_(arc.kmax, arc.kmin, n_blk, SBLK, smax, smin, sb0, sb1 + 1)
+    hi_c = min(hi, arc.kmax.shape[1] - 1)
+    if size > ORIGIN and hi_c >= lo:
+        _write(arc, block, size, lo, hi_c)
+    _update_super(arc, lo, hi, block)
     arc.dirty_lo, arc.dirty_hi = 1 << 60, -1
+
+
+def _grow(arc, need: int, block: int) -> None:
+    """Archive.grow (memory.py:225-278) for an archive in HBM: capacity doubled until it holds
+    `need` rows; block and super-block arrays extended with zeros."""
+    cap = arc.keys.shape[1]
+    if need <= cap:
+        return
+    new_cap = max(cap, 1)
+    while new_cap < need:
+        new_cap *= 2
+    kv, d = arc.keys.shape[0], arc.keys.shape[2]
+    for name in ("keys", "values"):
+        old = getattr(arc, name)
+        buf = torch.empty(kv, new_cap, d, dtype=old.dtype, device=old.device)
+        buf[:, :cap] = old
+        setattr(arc, name, buf)
+    n_blk, n_sb = new_cap // block, (new_cap // block + SBLK - 1) // SBLK
+    for names, rows in ((("kmax", "kmin", "bmean_k", "bmean_v"), n_blk), (("smax", "smin", "smean_k", "smean_v"), n_sb)):
+        for name in names:
+            old = getattr(arc, name, None)
+            if old is not None and old.shape[1] < rows:
+                buf = torch.zeros(kv, rows, d, dtype=old.dtype, device=old.device)
+                buf[:, : old.shape[1]] = old
+                setattr(arc, name, buf)
+
+
+def archive_write(arc, pos: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block: int, p0: int | None = None,
+                  hi: int | None = None) -> None:
+    """Archive.write (memory.py:310-395) for an archive in HBM: k/v [N, KV, D] stored at
+    positions pos [N] (grown as needed). A contiguous write (pos = p0 .. hi - 1) summarises
+    every block it touches as it writes them, one pass over the new rows
+    (pbk_quest_archive_write), then the super-blocks holding them; the reference summarises
+    full blocks at once and the partial ends at the next retrieval, which reads the same
+    summaries. Other writes scatter the rows and leave their blocks dirty for the next
+    refresh, as the reference does."""
+    if p0 is None or hi is None:
+        hi = int(pos.max()) + 1
+        p0 = int(pos.min())
+    n = int(pos.numel())
+    contig = hi - p0 == n
+    _grow(arc, hi, block)
+    size = getattr(arc, "size", 0)
+    lo_b, hi_b = max(0, p0 - ORIGIN) // block, (hi - 1 - ORIGIN) // block
+    if contig:
+        blk_hi = min(hi_b, arc.kmax.shape[1] - 1) if hi - 1 >= ORIGIN else -1
+        _write(arc, block, size, lo_b, blk_hi, k, v, p0=p0)
+        arc.size = max(size, hi)
+        if hi - 1 >= ORIGIN:
+            _update_super(arc, lo_b, hi_b, block)
+        return
+    _write(arc, block, size, 0, -1, k, v, pos=pos)
+    arc.size = max(size, hi)
+    if hi - 1 >= ORIGIN:
+        arc.dirty_lo = min(getattr(arc, "dirty_lo", 1 << 60), lo_b)
+        arc.dirty_hi = max(getattr(arc, "dirty_hi", -1), hi_b)
 
 
 def budget_for(full: int, rerank: bool, prompt_len: int, limit: int, budget: int = 0) -> int:

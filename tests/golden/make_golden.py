@@ -36,6 +36,9 @@ Fixtures:
   rope.npz        RoPE repositioning past the horizon (lowered to 1500 tokens): the block moves
                   in both modes and the sink move called directly, and retrieve_blocks (rerank,
                   flat) + piece_attention on a 3000-token serving archive.
+  archive_write.npz  the serving Archive.write: a prefill write, short and scattered writes
+                  and a long write across super-blocks into a CPU archive, then
+                  refresh_bounds; its final storage, block and super-block summaries.
   quest.npz       archive_append + retrieve (flat mode, page 16, budget 4 pages) for a
                   decode query (T=1) and a 3-token query, plus the exact attention over
                   [retrieved ; window] as pseudobrain/transplant.py:619-628 computes it.
@@ -273,6 +276,34 @@ def make_rope(MEM):
     np.savez_compressed(os.path.join(HERE, "rope.npz"), **out)
 
 
+def make_archive_write(MEM):
+    """Archive.write (pb27_vllm/memory.py:310-395) on a CPU archive (fp32 storage and
+    summaries) with 16-token blocks and super-blocks of 2: a contiguous prefill write, two
+    short contiguous writes, a scattered write, a long contiguous write across super-blocks,
+    then refresh_bounds. The inputs and the final storage and summaries are kept."""
+    import torch
+    MEM.SBLK = 2
+    kv, d, block, cap = 2, 128, 16, 640
+    gen = torch.Generator().manual_seed(111)
+    arc = MEM.Archive.new(kv, d, cap, block, torch.float32, torch.device("cpu"))
+    writes = [np.arange(0, 41), np.arange(41, 44), np.arange(44, 45), np.array([10, 30, 50, 43]),
+              np.arange(45, 300)]
+    out = dict(block=np.int64(block), sblk=np.int64(2), cap=np.int64(cap), n_writes=np.int64(len(writes)))
+    for i, pos in enumerate(writes):
+        k = torch.randn(len(pos), kv, d, generator=gen).to(torch.bfloat16).float()
+        v = torch.randn(len(pos), kv, d, generator=gen).to(torch.bfloat16).float()
+        arc.write(torch.from_numpy(pos), k, v, block)
+        out.update({f"w{i}_pos": pos.astype(np.int64), f"w{i}_k": _bits(k.to(torch.bfloat16)),
+                    f"w{i}_v": _bits(v.to(torch.bfloat16))})
+    arc.refresh_bounds(block)
+    out.update(size=np.int64(arc.size), keys=_bits(arc.keys.to(torch.bfloat16)),
+               values=_bits(arc.values.to(torch.bfloat16)))
+    for name in ("kmax", "kmin", "bmean_k", "bmean_v", "smax", "smin", "smean_k", "smean_v"):
+        out[name] = getattr(arc, name).float().numpy()
+    MEM.SBLK = 64
+    np.savez_compressed(os.path.join(HERE, "archive_write.npz"), **out)
+
+
 def make_swa(TR):
     import torch
     out = {}
@@ -377,7 +408,8 @@ def main(reference_root: str) -> None:
     import pb27_vllm.memory as MEM
     makers = {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR),
               "serving": lambda: make_serving(MEM), "gdn_io": lambda: make_gdn_io(G),
-              "quest_levels": lambda: make_quest_levels(E, MEM), "rope": lambda: make_rope(MEM)}
+              "quest_levels": lambda: make_quest_levels(E, MEM), "rope": lambda: make_rope(MEM),
+              "archive_write": lambda: make_archive_write(MEM)}
     for name in (sys.argv[2:] if len(sys.argv) > 2 else makers):  # all, or only the named fixtures
         makers[name]()
     for name in sorted(os.listdir(HERE)):

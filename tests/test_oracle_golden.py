@@ -260,3 +260,28 @@ def test_rope_serving_matches_reference(rope, case):
     o = osv.piece_attention(keys, values, q, f[f"{case}_pos"], top, groups, window, 128 ** -0.5, block, rope=args,
                             bf16_keys=False)
     assert ogdn.rel_err(o, f[f"{case}_out"]) < 1e-4
+
+
+def test_archive_write_matches_reference():
+    """oracle ArchiveState.write / refresh_bounds against pb27_vllm/memory.py's Archive.write
+    (fast path, short and scattered writes, a write across super-blocks): storage and max /
+    min summaries exact, means to fp32 rounding."""
+    from oracle import serving as osv
+    f = load_golden("archive_write.npz")
+    block, sblk, cap = int(f["block"]), int(f["sblk"]), int(f["cap"])
+    kv, d = f["keys"].shape[0], f["keys"].shape[2]
+    arc = osv.ArchiveState(kv, d, cap, block, sblk)
+    for i in range(int(f["n_writes"])):
+        arc.write(f[f"w{i}_pos"], _f32(f[f"w{i}_k"]), _f32(f[f"w{i}_v"]))
+    arc.refresh_bounds()
+    size = int(f["size"])
+    assert arc.size == size
+    # the reference allocates with torch.empty: only written rows, blocks and super-blocks count
+    assert np.array_equal(oq.bf16_bits(arc.keys[:, :size]), f["keys"][:, :size])
+    assert np.array_equal(oq.bf16_bits(arc.values[:, :size]), f["values"][:, :size])
+    nb = (size - osv.ORIGIN + block - 1) // block
+    nsb = (nb + sblk - 1) // sblk
+    for name, n in (("kmax", nb), ("kmin", nb), ("smax", nsb), ("smin", nsb)):
+        assert np.array_equal(getattr(arc, name)[:, :n], f[name][:, :n]), name
+    for name, n in (("bmean_k", nb), ("bmean_v", nb), ("smean_k", nsb), ("smean_v", nsb)):
+        assert np.allclose(getattr(arc, name)[:, :n], f[name][:, :n], rtol=0, atol=1e-6), name
