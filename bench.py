@@ -1,7 +1,7 @@
 """Benchmark of the PseudoBrain hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload all|prefill|decode|quest] [--size full|small]
+                    [--workload all|prefill|decode|quest|hybrid|serving|widen] [--size full|small]
 
 Headline (``value``): GDN chunked prefill of benchmark config 1 (B=4, T=32768, 16 key /
 32 value heads, dk=dv=128, chunk 64, bf16 q/k/v/beta, fp32 g and state) in tok/s,
@@ -12,6 +12,10 @@ carries the other two parts of the metric, each with its own roofline:
 sliding-window attention layer over a 1M-token sequence, heads split over the ranks with
 an NCCL all-gather of each branch's output; tok/s, strong scaling). ``e2e`` times the public API with
 pinned host inputs copied in and outputs copied back inside the timed region.
+
+``widen`` times the rows around the hot path (the GDN layer's conv / gating / output norm at
+config-1 shapes, the two-level Quest selection, the serving archive write and the RoPE move
++ gather), each against the HBM roofline.
 
 Multi-GPU (torchrun, one rank per GPU): weak scaling. Every rank runs its own shard of
 (sequence x value head) chains of the same per-GPU size; the recurrence has no
@@ -389,6 +393,113 @@ def measure_serving(args, timed, dev, rank, world, pk):
             "gpu_launches": 8 * steps}
 
 
+def measure_widen(args, timed, dev, rank, world, pk):
+    """The rows widened around the hot path, each timed alone with its own HBM roofline
+    (weak scaling, per-rank shapes): the GDN layer's pieces around the recurrence at config-1
+    shapes (short conv + SiLU + q/k L2 norm, gating, gated output norm), the two-level Quest
+    selection at the research defaults (64-token pages, super-blocks of 64, 64 pages kept) over
+    a 1M-token archive for 8 queries, the serving archive write of a 65536-token piece into a
+    1M-token archive (8 key heads, 64-token blocks, max / min / means), and the RoPE move with
+    the gather of 1024 retrieved blocks per key head."""
+    import types
+    import torch
+    from pseudobrain_b200 import exact_memory as M
+    from pseudobrain_b200 import gdn_layer as L
+    from pseudobrain_b200 import serving as S
+    small = args.size == "small"
+    gen = torch.Generator(device=dev).manual_seed(11 + 1000 * rank)
+    steps = max(args.steps, 10)
+    hbm = pk["hbm"]
+
+    def entry(seconds, nbytes, launches, **extra):
+        return {"us": seconds * 1e6, "achieved_gbps": nbytes / seconds / 1e9, "frac": nbytes / seconds / 1e9 / hbm,
+                "algorithmic_bytes": nbytes, "launches_per_call": launches, **extra}
+
+    out = {}
+    # GDN layer pieces (config 1 shapes)
+    b, t, hk, hv = (1, 8192, 16, 32) if small else (4, 32768, 16, 32)
+    c = (2 * hk + hv) * 128
+    x = torch.randn(b, t, c, device=dev, generator=gen).to(torch.bfloat16)
+    wconv = torch.randn(c, 4, device=dev, generator=gen) * 0.5
+    tail = torch.randn(b, 3, c, device=dev, generator=gen).to(torch.bfloat16)
+    new_tail = torch.empty_like(tail)
+    tc_ = timed(lambda: L.conv_qkv(x, tail, wconv, hk, hv, "max", new_tail), steps, 3) / steps
+    out["conv_qkv"] = entry(tc_, 2 * x.numel() * 2 + 2 * tail.numel() * 2 + wconv.numel() * 4, 1,
+                            shape=f"x [{b},{t},{c}] bf16 -> q, k [{b},{t},{hk},128], v [{b},{t},{hv},128] bf16")
+    del x
+    decay = torch.randn(b, t, 2 * hv, device=dev, generator=gen).to(torch.bfloat16)
+    a_log, dt_bias = torch.randn(hv, device=dev, generator=gen), torch.randn(hv, device=dev, generator=gen)
+    tg = timed(lambda: L.gdn_gating(decay, a_log, dt_bias, torch.bfloat16), steps, 3) / steps
+    out["gating"] = entry(tg, decay.numel() * 2 + b * t * hv * (4 + 2), 1)
+    o = torch.randn(b, t, hv, 128, device=dev, generator=gen)
+    gate = torch.randn(b, t, hv * 128, device=dev, generator=gen).to(torch.bfloat16)
+    wn = torch.randn(128, device=dev, generator=gen)
+    tn = timed(lambda: L.gated_out_norm(o, gate, wn, out_dtype=torch.bfloat16), steps, 3) / steps
+    out["gated_out_norm"] = entry(tn, o.numel() * 4 + gate.numel() * 2 + o.numel() * 2, 1,
+                                  shape="o fp32, gate bf16 -> out bf16")
+    del o, gate, decay
+    torch.cuda.empty_cache()
+    # two-level Quest selection (research defaults)
+    kv, heads, d, page, sblk, nq, budget = 8, 32, 128, 64, 64, 8, 64
+    n_tok = (1 << 19) if small else (1 << 20)
+    full = n_tok // page
+    kmax = torch.randn(kv, full, d, device=dev, generator=gen).to(torch.bfloat16)
+    kmin = (kmax.float() - torch.rand(kv, full, d, device=dev, generator=gen) * 2).to(torch.bfloat16)
+    smax, smin = M.super_bounds(kmax[None], kmin[None], sblk)
+    smax, smin = smax[0], smin[0]
+    q = torch.randn(nq, 1, heads, d, device=dev, generator=gen).to(torch.bfloat16)
+
+    def levels():
+        M.select_pages_levels(q, kmax, kmin, n_tok, page, budget, smax, smin, sblk)
+
+    replay, graph = graphed(torch, levels)
+    tl = timed(replay, steps * 4, 3) / (steps * 4)
+    del graph
+    m_sb = M.m_superblocks(budget, full, sblk)
+    lv_bytes = smax.numel() * 2 * 2 + nq * kv * m_sb * sblk * d * 2 * 2
+    tf = timed(lambda: M.select_pages(q, kmax, kmin, n_tok, page, budget), steps * 4, 3) / (steps * 4)
+    out["quest_two_level"] = entry(tl, lv_bytes, 5, flat_us=tf * 1e6, flat_bytes=kmax.numel() * 2 * 2,
+                                   config=f"{n_tok} tokens, pages of {page}, super-blocks of {sblk}, {nq} queries, "
+                                          f"{heads}/{kv} heads, {budget} pages kept, {m_sb} super-blocks",
+                                   timing="CUDA-graph replay (5 launches)")
+    del kmax, kmin, smax, smin
+    torch.cuda.empty_cache()
+    # serving archive write
+    block, n_new = 64, (16384 if small else 65536)
+    cap = n_tok + S.ORIGIN
+    n_blk = cap // block
+    n_sb = (n_blk + S.SBLK - 1) // S.SBLK
+    z = lambda rows: torch.zeros(kv, rows, d, dtype=torch.bfloat16, device=dev)  # noqa: E731
+    arc = types.SimpleNamespace(keys=z(cap), values=z(cap), kmax=z(n_blk), kmin=z(n_blk), bmean_k=z(n_blk),
+                                bmean_v=z(n_blk), smax=z(n_sb), smin=z(n_sb), smean_k=z(n_sb), smean_v=z(n_sb),
+                                size=cap - 4096, dirty_lo=1 << 60, dirty_hi=-1)
+    p0 = S.ORIGIN + 40 * block
+    kn = torch.randn(n_new, kv, d, device=dev, generator=gen).to(torch.bfloat16)
+    vn = torch.randn(n_new, kv, d, device=dev, generator=gen).to(torch.bfloat16)
+    pos = torch.arange(p0, p0 + n_new, device=dev)
+    tw = timed(lambda: S.archive_write(arc, pos, kn, vn, block, p0, p0 + n_new), steps, 3) / steps
+    nb_touch = n_new // block
+    w_bytes = 2 * kn.numel() * 2 * 2 + nb_touch * kv * d * 2 * 4
+    out["archive_write"] = entry(tw, w_bytes, 5, config=f"{n_new} tokens x {kv} key heads into a {cap}-row archive, "
+                                                        f"blocks of {block}, super-blocks of {S.SBLK}")
+    # RoPE move + gather of the retrieved blocks
+    nsel = 1024
+    blocks = torch.sort(torch.stack([torch.randperm(n_blk - 1, device=dev, generator=gen)[:nsel]
+                                     for _ in range(kv)]), dim=-1).values.to(torch.int32)
+    tr = timed(lambda: S.rope_gather(arc.keys, arc.values, blocks, block, S.ORIGIN, nsel, "runs",
+                                     ref_pos=cap - 1024), steps, 3) / steps
+    out["rope_gather"] = entry(tr, 2 * 2 * kv * nsel * block * d * 2, 2,
+                               config=f"{nsel} blocks of {block} x {kv} key heads, keys moved, values gathered")
+    del arc, kn, vn
+    torch.cuda.empty_cache()
+    out["gpu_launches"] = 3 * steps + 5 * (steps * 4 + 3) + 5 * steps + 2 * steps
+    cv = out["conv_qkv"]  # the line's own fields when this part runs alone
+    out.update(metric="widened rows: HBM GB/s of each piece", value=cv["achieved_gbps"], unit="GB/s",
+               roofline={"bound": "hbm", "achieved": cv["achieved_gbps"], "peak": hbm, "unit": "GB/s",
+                         "frac": cv["frac"], "traffic": None, "kernel": "gdn_conv_norm_kernel"})
+    return out
+
+
 def swa_pairs(t, window):
     """Visible (query, key) pairs of a causal window over t tokens."""
     w = min(window, t)
@@ -482,7 +593,7 @@ def run_ours(args, rank, world, local_rank):
     parts = {}
     clk = Clocks(local_rank)
     for name, fn in (("prefill", measure_prefill), ("decode", measure_decode), ("quest", measure_quest),
-                     ("hybrid", measure_hybrid), ("serving", measure_serving)):
+                     ("hybrid", measure_hybrid), ("serving", measure_serving), ("widen", measure_widen)):
         if args.workload in ("all", name):
             if name == "prefill":
                 with clk:
@@ -509,8 +620,8 @@ def run_ours(args, rank, world, local_rank):
         "roofline": head["roofline"], "e2e": head.get("e2e"), "gpu_launches": head["gpu_launches"],
         "clocks": clk.summary(),
     }
-    for name in ("decode", "quest", "hybrid", "serving"):
-        if name in parts and parts[name] is not None and parts[name] is not head:
+    for name in ("decode", "quest", "hybrid", "serving", "widen"):
+        if name in parts and parts[name] is not None and (parts[name] is not head or name == "widen"):
             line[name] = parts[name]
     if world == 1 and not args.no_cpu_baseline and "prefill" in parts:
         line["cpu_baseline"] = cpu_baseline(samples=1)
@@ -581,7 +692,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("all", "prefill", "decode", "quest", "hybrid", "serving"), default="all",
+    ap.add_argument("--workload", choices=("all", "prefill", "decode", "quest", "hybrid", "serving", "widen"),
+                    default="all",
                     help="run one part only (profiling); the JSON line then carries that part")
     ap.add_argument("--size", choices=("full", "small"), default="full",
                     help="small: a reduced case of the same kernels for ncu captures (not a bench number)")

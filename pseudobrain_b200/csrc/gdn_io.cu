@@ -86,6 +86,80 @@ __global__ void __launch_bounds__(kHd) gdn_conv_norm_kernel(const pbk_conv_desc 
   }
 }
 
+// The same for bf16 inputs and outputs with a contiguous channel dim (the common case): the
+// tile's input rows (and the width - 1 before it) are staged in shared memory with 16-byte
+// loads, all in flight at once; each thread then convolves one channel from shared memory;
+// the normalised rows leave as 8-byte stores (lane = 4 channels).
+// SiLU for bf16 outputs: __expf and the fast quotient (relative error near 1e-6, far below
+// the bf16 rounding of the result; 0 for large negative y).
+__device__ __forceinline__ float silu_fast(float y) { return __fdividef(y, 1.f + __expf(-y)); }
+
+template <int K>
+__global__ void __launch_bounds__(kHd) gdn_conv_norm_vec_kernel(const pbk_conv_desc d) {
+  __shared__ __align__(16) __nv_bfloat16 xs[kTile + kMaxWidth - 1][kHd];
+  __shared__ __align__(16) float ys[kTile][kHd + 4];
+  const int tile = blockIdx.x, hd = blockIdx.y, b = blockIdx.z, c = threadIdx.x;
+  constexpr int H = K - 1;
+  const int t0 = tile * kTile;
+  const int nt = min(kTile, d.seqlen - t0);
+  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(d.x.data);
+  const __nv_bfloat16* tb = reinterpret_cast<const __nv_bfloat16*>(d.tail.data);
+  // stage rows r = 0 .. H + nt - 1 (token t0 - H + r); 16 vectors of 8 channels per row
+  for (int e = c; e < (H + nt) * 16; e += kHd) {
+    const int r = e >> 4, vq = e & 15, t = t0 - H + r;
+    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+    const int64_t ch = (int64_t)hd * kHd + 8 * vq;
+    if (t >= 0) {
+      val = *reinterpret_cast<const uint4*>(xb + b * d.x.stride_b + (int64_t)t * d.x.stride_t + ch);
+    } else if (tb != nullptr) {  // the carried tail: row H + t of [B, K - 1, C]
+      val = *reinterpret_cast<const uint4*>(tb + b * d.tail.stride_b + (int64_t)(H + t) * d.tail.stride_t + ch);
+    }
+    *reinterpret_cast<uint4*>(&xs[r][8 * vq]) = val;
+  }
+  float w[K], win[K];  // taps and the sliding window x_{t-K+1} .. x_t of this channel
+#pragma unroll
+  for (int j = 0; j < K; ++j) w[j] = d.weight != nullptr ? d.weight[((int64_t)hd * kHd + c) * K + j] : 0.f;
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < H; ++j) win[j] = __bfloat162float(xs[j][c]);
+  for (int i = 0; i < nt; ++i) {
+    win[H] = __bfloat162float(xs[i + H][c]);
+    float y = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) y = fmaf(w[j], win[j], y);
+    ys[i][c] = silu_fast(d.weight != nullptr ? y : win[H]);
+#pragma unroll
+    for (int j = 0; j < H; ++j) win[j] = win[j + 1];
+  }
+  if (d.new_tail.data != nullptr && t0 + nt == d.seqlen) {
+    for (int j = 0; j < H; ++j)  // the last K - 1 inputs: staged rows nt .. nt + H - 1
+      store_any(d.new_tail.data, b * d.new_tail.stride_b + (int64_t)j * d.new_tail.stride_t +
+                                     ((int64_t)hd * kHd + c) * d.new_tail.stride_h,
+                d.new_tail.dtype, __bfloat162float(xs[nt + j][c]));
+  }
+  __syncthreads();
+  const bool is_q = hd < d.hk, is_k = !is_q && hd < 2 * d.hk;
+  const pbk_view& out = is_q ? d.q : (is_k ? d.k : d.v);
+  const int oh = is_q ? hd : (is_k ? hd - d.hk : hd - 2 * d.hk);
+  const int warp = c >> 5, lane = c & 31;
+  for (int i = warp; i < nt; i += kHd / 32) {
+    const float4 v = *reinterpret_cast<const float4*>(&ys[i][4 * lane]);
+    float scale = 1.f;
+    if ((is_q || is_k) && d.l2mode != 0) {
+      const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+      scale = d.l2mode == 1 ? 1.f / fmaxf(sqrtf(ss), d.eps) : rsqrtf(ss + d.eps);
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x * scale, v.y * scale);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(v.z * scale, v.w * scale);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+    __nv_bfloat16* ob = const_cast<__nv_bfloat16*>(reinterpret_cast<const __nv_bfloat16*>(out.data));
+    *reinterpret_cast<uint2*>(ob + b * out.stride_b + (int64_t)(t0 + i) * out.stride_t + (int64_t)oh * out.stride_h +
+                              4 * lane) = pk;
+  }
+}
+
 __global__ void gdn_gating_kernel(const pbk_gating_desc d) {
   const int64_t n = (int64_t)d.batch * d.seqlen * d.hv;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
@@ -132,9 +206,86 @@ __global__ void __launch_bounds__(256) gdn_out_norm_kernel(const pbk_out_norm_de
 
 }  // namespace
 
+namespace {
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+// bf16 in and out, contiguous channels, 16-byte rows in (8-byte out): the staged kernel.
+bool conv_vec_ok(const pbk_conv_desc& d) {
+  const pbk_view& x = d.x;
+  if (x.dtype != PBK_BF16 || x.stride_h != 1 || !aligned(x.data, 16) || x.stride_b % 8 || x.stride_t % 8) return false;
+  if (d.tail.data != nullptr && (d.tail.dtype != PBK_BF16 || d.tail.stride_h != 1 || !aligned(d.tail.data, 16) ||
+                                 d.tail.stride_b % 8 || d.tail.stride_t % 8))
+    return false;
+  const pbk_view* outs[3] = {&d.q, &d.k, &d.v};
+  for (const pbk_view* o : outs)
+    if (o->dtype != PBK_BF16 || !aligned(o->data, 8) || o->stride_b % 4 || o->stride_t % 4 || o->stride_h % 4)
+      return false;
+  return true;
+}
+// The output norm with lane = 4 consecutive dims (16-byte fp32 / 8-byte bf16 accesses) for
+// contiguous rows, gate bf16, weight fp32; SiLU as silu_fast when the output is bf16.
+template <typename TO, typename TG>
+__global__ void __launch_bounds__(256) gdn_out_norm_vec_kernel(const pbk_out_norm_desc d) {
+  const int64_t rows = (int64_t)d.batch * d.seqlen * d.hv;
+  const int64_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int h = (int)(r % d.hv), t = (int)((r / d.hv) % d.seqlen), b = (int)(r / ((int64_t)d.hv * d.seqlen));
+  const int64_t ob = b * d.o.stride_b + (int64_t)t * d.o.stride_t + (int64_t)h * d.o.stride_h + 4 * lane;
+  const int64_t gb = b * d.gate.stride_b + (int64_t)t * d.gate.stride_t + (int64_t)h * d.gate.stride_h + 4 * lane;
+  const int64_t yb = b * d.out.stride_b + (int64_t)t * d.out.stride_t + (int64_t)h * d.out.stride_h + 4 * lane;
+  float v[4], g[4];
+  if constexpr (sizeof(TO) == 4) {
+    const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(d.o.data) + ob);
+    v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
+  } else {
+    const uint2 x = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(d.o.data) + ob);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.x));
+    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.y));
+    v[0] = a.x, v[1] = a.y, v[2] = c.x, v[3] = c.y;
+  }
+  {
+    const uint2 x = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(d.gate.data) + gb);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.x));
+    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x.y));
+    g[0] = a.x, g[1] = a.y, g[2] = c.x, g[3] = c.y;
+  }
+  const float4 wt = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(d.weight) + 4 * lane);
+  const float ww[4] = {wt.x, wt.y, wt.z, wt.w};
+  const float inv = rsqrtf(warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]) / kHd + d.eps);
+  float y[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) y[u] = v[u] * inv * ww[u] * (sizeof(TG) == 2 ? silu_fast(g[u]) : silu(g[u]));
+  if constexpr (sizeof(TG) == 4) {
+    float* op = const_cast<float*>(reinterpret_cast<const float*>(d.out.data)) + yb;  // 16-byte aligned
+    *reinterpret_cast<float4*>(op) = make_float4(y[0], y[1], y[2], y[3]);
+  } else {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(y[0], y[1]), hi = __floats2bfloat162_rn(y[2], y[3]);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+    __nv_bfloat16* op = const_cast<__nv_bfloat16*>(reinterpret_cast<const __nv_bfloat16*>(d.out.data)) + yb;
+    *reinterpret_cast<uint2*>(op) = pk;  // 8-byte aligned
+  }
+}
+
+}  // namespace
+
 cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st) {
   const dim3 grid((unsigned)((d.seqlen + kTile - 1) / kTile), (unsigned)(2 * d.hk + d.hv), (unsigned)d.batch);
-  gdn_conv_norm_kernel<<<grid, kHd, 0, st>>>(d);
+  if (conv_vec_ok(d)) {
+    switch (d.weight != nullptr ? d.width : 1) {
+      case 1: gdn_conv_norm_vec_kernel<1><<<grid, kHd, 0, st>>>(d); break;
+      case 2: gdn_conv_norm_vec_kernel<2><<<grid, kHd, 0, st>>>(d); break;
+      case 3: gdn_conv_norm_vec_kernel<3><<<grid, kHd, 0, st>>>(d); break;
+      case 4: gdn_conv_norm_vec_kernel<4><<<grid, kHd, 0, st>>>(d); break;
+      case 5: gdn_conv_norm_vec_kernel<5><<<grid, kHd, 0, st>>>(d); break;
+      case 6: gdn_conv_norm_vec_kernel<6><<<grid, kHd, 0, st>>>(d); break;
+      case 7: gdn_conv_norm_vec_kernel<7><<<grid, kHd, 0, st>>>(d); break;
+      default: gdn_conv_norm_vec_kernel<8><<<grid, kHd, 0, st>>>(d); break;
+    }
+  } else {
+    gdn_conv_norm_kernel<<<grid, kHd, 0, st>>>(d);
+  }
   return cudaGetLastError();
 }
 
@@ -147,7 +298,19 @@ cudaError_t launch_gdn_gating(const pbk_gating_desc& d, cudaStream_t st) {
 
 cudaError_t launch_gdn_out_norm(const pbk_out_norm_desc& d, cudaStream_t st) {
   const int64_t rows = (int64_t)d.batch * d.seqlen * d.hv;
-  gdn_out_norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(d);
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  auto rows_ok = [](const pbk_view& x, int64_t elems) {  // 16-byte (fp32) or 8-byte (bf16) lanes
+    return aligned(x.data, 4 * elems) && x.stride_b % 4 == 0 && x.stride_t % 4 == 0 && x.stride_h % 4 == 0;
+  };
+  const bool o32 = d.o.dtype == PBK_F32, out32 = d.out.dtype == PBK_F32;
+  const bool vec = (o32 || d.o.dtype == PBK_BF16) && d.gate.dtype == PBK_BF16 && d.weight_dtype == PBK_F32 &&
+                   aligned(d.weight, 16) && rows_ok(d.o, o32 ? 4 : 2) && rows_ok(d.gate, 2) &&
+                   rows_ok(d.out, out32 ? 4 : 2);
+  if (!vec) gdn_out_norm_kernel<<<grid, 256, 0, st>>>(d);
+  else if (o32 && out32) gdn_out_norm_vec_kernel<float, float><<<grid, 256, 0, st>>>(d);
+  else if (o32) gdn_out_norm_vec_kernel<float, __nv_bfloat16><<<grid, 256, 0, st>>>(d);
+  else if (out32) gdn_out_norm_vec_kernel<__nv_bfloat16, float><<<grid, 256, 0, st>>>(d);
+  else gdn_out_norm_vec_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, st>>>(d);
   return cudaGetLastError();
 }
 

@@ -868,55 +868,76 @@ __global__ void __launch_bounds__(32) quest_rope_delta_kernel(const pbk_rope_gat
   }
 }
 
-// Gather (and rotate) one output row per warp; lane l holds dims 4l .. 4l + 3, so the
-// rotated pairs (i, i + 16), i < 16, sit in lanes l and l + 4 for l < 4.
+// Gather (and rotate) the rows of one (block, key head) per CTA, after its cos / sin table
+// (16 pairs, computed once per block); warp = row, lane l holds dims 4l .. 4l + 3, so the
+// rotated pairs (i, i + 16), i < 16, sit in lanes l and l + 4 for l < 4. The tail rows
+// (unrotated) are the CTAs past the blocks, kTailRows rows each.
+constexpr int kTailRows = 64;
 __global__ void __launch_bounds__(256) quest_rope_gather_kernel(const pbk_rope_gather_desc d) {
+  __shared__ float cs[2][16];
   const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + warp, nb = (int64_t)d.n_blk * d.block;
-  if (row >= nb + d.tail_n) return;
-  int64_t src;
-  float dl = 0.f;
-  if (row < nb) {
-    const int j = (int)(row / d.block), s = (int)(row % d.block);
+  const int64_t nb = (int64_t)d.n_blk * d.block;
+  const bool in_blocks = (int)blockIdx.x < d.n_blk;
+  int64_t src0, out0, nrows;
+  bool rot = false;
+  if (in_blocks) {
+    const int j = blockIdx.x;
     const int b = d.blocks ? d.blocks[(int64_t)h * d.n_blk + j] : j;
-    src = (int64_t)d.origin + (int64_t)b * d.block + s;
-    if (d.mode == 3) dl = d.const_delta;
-    else if (d.mode != 0) dl = d.delta[(int64_t)h * d.n_blk + j];
-  } else {
-    src = (int64_t)d.tail0 + (row - nb);
-  }
-  const bool ok = src >= 0 && src < d.n_rows;
-  const int64_t at = h * d.stride_kv + src * d.stride_n + 4 * lane;
-  const int64_t out_at = ((int64_t)h * (nb + d.tail_n) + row) * kD + 4 * lane;
-  uint2 kr = make_uint2(0u, 0u);
-  if (ok) kr = *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(d.keys) + at);
-  if (d.mode != 0 && row < nb) {
-    const uint2 pr = make_uint2(__shfl_xor_sync(0xffffffffu, kr.x, 4), __shfl_xor_sync(0xffffffffu, kr.y, 4));
-    if (lane < 8) {
-      const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&kr);
-      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&pr);
-      const float2 a0 = __bfloat1622float2(a[0]), a1 = __bfloat1622float2(a[1]);
-      const float2 b0 = __bfloat1622float2(b[0]), b1 = __bfloat1622float2(b[1]);
-      const float own[4] = {a0.x, a0.y, a1.x, a1.y}, other[4] = {b0.x, b0.y, b1.x, b1.y};
-      float r[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = 4 * (lane & 3) + e;  // pair index
-        const float ang = __fmul_rn(dl, d.inv_freq[i]);
-        const float c = cosf(ang), sn = sinf(ang);
-        // lanes 0-3 hold x1 (r1 = x1 cos - x2 sin), lanes 4-7 hold x2 (r2 = x2 cos + x1 sin)
-        r[e] = lane < 4 ? __fsub_rn(__fmul_rn(own[e], c), __fmul_rn(other[e], sn))
-                        : __fadd_rn(__fmul_rn(own[e], c), __fmul_rn(other[e], sn));
-      }
-      kr.x = bf16x2_bits(r[0], r[1]);
-      kr.y = bf16x2_bits(r[2], r[3]);
+    src0 = (int64_t)d.origin + (int64_t)b * d.block;
+    out0 = (int64_t)j * d.block;
+    nrows = d.block;
+    rot = d.mode != 0;
+    if (rot && threadIdx.x < 16) {
+      const float dl = d.mode == 3 ? d.const_delta : d.delta[(int64_t)h * d.n_blk + j];
+      const float ang = __fmul_rn(dl, d.inv_freq[threadIdx.x]);
+      cs[0][threadIdx.x] = cosf(ang);
+      cs[1][threadIdx.x] = sinf(ang);
     }
+    __syncthreads();
+  } else {
+    const int64_t t = (int64_t)(blockIdx.x - d.n_blk) * kTailRows;
+    src0 = (int64_t)d.tail0 + t;
+    out0 = nb + t;
+    nrows = min((int64_t)kTailRows, (int64_t)d.tail_n - t);
   }
-  *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(d.out_keys) + out_at) = kr;
-  if (d.out_values != nullptr) {
-    uint2 vr = make_uint2(0u, 0u);
-    if (ok) vr = *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(d.values) + at);
-    *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(d.out_values) + out_at) = vr;
+  float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+  if (rot && lane < 8) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[e] = cs[0][4 * (lane & 3) + e], sn[e] = cs[1][4 * (lane & 3) + e];
+  }
+  const bf16* kin = reinterpret_cast<const bf16*>(d.keys);
+  const bf16* vin = reinterpret_cast<const bf16*>(d.values);
+  bf16* kout = reinterpret_cast<bf16*>(d.out_keys) + (int64_t)h * (nb + d.tail_n) * kD;
+  bf16* vout = d.out_values ? reinterpret_cast<bf16*>(d.out_values) + (int64_t)h * (nb + d.tail_n) * kD : nullptr;
+  for (int64_t s = warp; s < nrows; s += 8) {
+    const int64_t src = src0 + s;
+    const bool ok = src >= 0 && src < d.n_rows;
+    const int64_t at = h * d.stride_kv + src * d.stride_n + 4 * lane;
+    uint2 kr = make_uint2(0u, 0u), vr = make_uint2(0u, 0u);
+    if (ok) {
+      kr = *reinterpret_cast<const uint2*>(kin + at);
+      if (vout) vr = *reinterpret_cast<const uint2*>(vin + at);
+    }
+    if (rot) {
+      const uint2 pr = make_uint2(__shfl_xor_sync(0xffffffffu, kr.x, 4), __shfl_xor_sync(0xffffffffu, kr.y, 4));
+      if (lane < 8) {
+        const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&kr);
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&pr);
+        const float2 a0 = __bfloat1622float2(a[0]), a1 = __bfloat1622float2(a[1]);
+        const float2 b0 = __bfloat1622float2(b[0]), b1 = __bfloat1622float2(b[1]);
+        const float own[4] = {a0.x, a0.y, a1.x, a1.y}, other[4] = {b0.x, b0.y, b1.x, b1.y};
+        float r[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)  // lanes 0-3: r1 = x1 cos - x2 sin; lanes 4-7: r2 = x2 cos + x1 sin
+          r[e] = lane < 4 ? __fsub_rn(__fmul_rn(own[e], c[e]), __fmul_rn(other[e], sn[e]))
+                          : __fadd_rn(__fmul_rn(own[e], c[e]), __fmul_rn(other[e], sn[e]));
+        kr.x = bf16x2_bits(r[0], r[1]);
+        kr.y = bf16x2_bits(r[2], r[3]);
+      }
+    }
+    const int64_t o = (out0 + s) * kD + 4 * lane;
+    *reinterpret_cast<uint2*>(kout + o) = kr;
+    if (vout) *reinterpret_cast<uint2*>(vout + o) = vr;
   }
 }
 
@@ -970,23 +991,37 @@ __global__ void __launch_bounds__(256) quest_archive_block_kernel(const pbk_arch
   float mx[4], mn[4], sk[4] = {0.f, 0.f, 0.f, 0.f}, sv[4] = {0.f, 0.f, 0.f, 0.f}, kl[4], vl[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) mx[e] = -FLT_MAX, mn[e] = FLT_MAX;
-  for (int64_t r = r0; r < r1; ++r) {
-    const bool fresh = d.pos == nullptr && r >= d.p0 && r < (int64_t)d.p0 + d.n;
-    const int64_t at = h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
-    if (fresh) {
-      const int64_t src = (r - d.p0) * d.in_stride_n + h * d.in_stride_kv + 4 * lane;
-      ld4(in_k + src, kl);
-      ld4(in_v + src, vl);
-      st4(ak + at, kl);  // bf16 in, bf16 out: the row as it came
-      st4(av + at, vl);
-    } else {
-      ld4(ak + at, kl);
-      ld4(av + at, vl);
+  constexpr int kBatch = 8;  // rows loaded before any is stored: eight loads of each in flight
+  for (int64_t rb = r0; rb < r1; rb += kBatch) {
+    uint2 kr[kBatch], vr[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t r = rb + u;
+      if (r >= r1) break;
+      const bool fresh = d.pos == nullptr && r >= d.p0 && r < (int64_t)d.p0 + d.n;
+      const bf16* sk_ = fresh ? in_k + (r - d.p0) * d.in_stride_n + h * d.in_stride_kv + 4 * lane
+                              : ak + h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
+      const bf16* sv_ = fresh ? in_v + (r - d.p0) * d.in_stride_n + h * d.in_stride_kv + 4 * lane
+                              : av + h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
+      kr[u] = *reinterpret_cast<const uint2*>(sk_);
+      vr[u] = *reinterpret_cast<const uint2*>(sv_);
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      mx[e] = fmaxf(mx[e], kl[e]), mn[e] = fminf(mn[e], kl[e]);
-      sk[e] += kl[e], sv[e] += vl[e];
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t r = rb + u;
+      if (r >= r1) break;
+      if (d.pos == nullptr && r >= d.p0 && r < (int64_t)d.p0 + d.n) {  // bf16 in, bf16 out: the row as it came
+        const int64_t at = h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
+        *reinterpret_cast<uint2*>(ak + at) = kr[u];
+        *reinterpret_cast<uint2*>(av + at) = vr[u];
+      }
+      ld4(reinterpret_cast<const bf16*>(&kr[u]), kl);
+      ld4(reinterpret_cast<const bf16*>(&vr[u]), vl);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        mx[e] = fmaxf(mx[e], kl[e]), mn[e] = fminf(mn[e], kl[e]);
+        sk[e] += kl[e], sv[e] += vl[e];
+      }
     }
   }
   const float pad = (float)(r0 + d.block - r1);  // a partial block counts its last row again
@@ -1281,7 +1316,8 @@ cudaError_t launch_quest_rope_gather(const pbk_rope_gather_desc& d, cudaStream_t
   const int64_t rows = (int64_t)d.n_blk * d.block + d.tail_n;
   if (rows == 0) return cudaSuccess;
   if ((d.mode == 1 || d.mode == 2) && d.n_blk > 0) quest_rope_delta_kernel<<<d.kv, 32, 0, st>>>(d);
-  quest_rope_gather_kernel<<<dim3((unsigned)((rows + 7) / 8), d.kv), 256, 0, st>>>(d);
+  const int64_t ctas = (int64_t)d.n_blk + (d.tail_n + kTailRows - 1) / kTailRows;
+  quest_rope_gather_kernel<<<dim3((unsigned)ctas, d.kv), 256, 0, st>>>(d);
   return cudaGetLastError();
 }
 

@@ -54,6 +54,29 @@ def test_conv_short_sequences_and_no_weight(cuda_device):
     assert ogdn.rel_err(got, ogdn.short_convolution(x, None, None)[0]) < 1e-5
 
 
+@pytest.mark.parametrize("width", [1, 2, 4, 8])
+def test_conv_bf16_staged_path(cuda_device, width):
+    """bf16 inputs and outputs with contiguous channels take the staged kernel: against the
+    oracle on the same bf16 values (short, ragged and multi-tile T; the tail carried exactly)."""
+    from oracle.quest import bf16_round
+    from pseudobrain_b200.gdn_layer import conv_qkv
+    rng = np.random.default_rng(width)
+    for t in (1, 2, 33, 97, 200):
+        x = bf16_round(rng.standard_normal((2, t, 640)).astype(np.float32))
+        tail = bf16_round(rng.standard_normal((2, width - 1, 640)).astype(np.float32))
+        w = (0.5 * rng.standard_normal((640, width))).astype(np.float32)
+        new_tail = torch.empty(2, width - 1, 640, device=cuda_device, dtype=torch.bfloat16)
+        q, k, v = conv_qkv(_t(x, cuda_device, torch.bfloat16), _t(tail, cuda_device, torch.bfloat16),
+                           _t(w, cuda_device), 1, 3, "max", new_tail, torch.bfloat16)
+        y, nt = ogdn.short_convolution(x, tail, w)
+        y = y.reshape(2, t, 5, 128)
+        qn, kn = ogdn.l2_normalize(y[:, :, 0], "max"), ogdn.l2_normalize(y[:, :, 1], "max")
+        assert ogdn.rel_err(q[:, :, 0].float().cpu().numpy(), qn) < 4e-3, t
+        assert ogdn.rel_err(k[:, :, 0].float().cpu().numpy(), kn) < 4e-3, t
+        assert ogdn.rel_err(v.float().cpu().numpy(), y[:, :, 2:]) < 4e-3, t
+        assert np.array_equal(new_tail.float().cpu().numpy(), nt), t
+
+
 def test_gating_matches_reference(cuda_device):
     from pseudobrain_b200.gdn_layer import gdn_gating
     f = load_golden("gdn_io.npz")
