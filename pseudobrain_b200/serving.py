@@ -30,6 +30,7 @@ pbk_quest_attend_sinks (libpbk.so, sm_100a); head dim 128.
 from __future__ import annotations
 
 import os
+import types
 
 import torch
 
@@ -108,10 +109,16 @@ def sink_shift(ref_pos: int, ns: int, n_blk: int, block: int) -> int:
 
 
 def _write(arc, block: int, size: int, blk_lo: int, blk_hi: int, k=None, v=None, p0: int = 0,
-           pos: torch.Tensor | None = None) -> None:
+           pos: torch.Tensor | None = None, origin: int | None = None) -> None:
     """pbk_quest_archive_write: new rows k/v [N, KV, D] at p0.. (or at pos) into the archive,
     and the max, min and (when the archive keeps them) mean summaries of blocks
-    [blk_lo, blk_hi] over the rows written so far."""
+    [blk_lo, blk_hi] (block b at row origin + b block, origin ORIGIN by default) over the rows
+    written so far. A host-resident archive (offload_archive) takes its new rows by a
+    device-to-host copy, and the summarised blocks' rows are staged into HBM for the kernel."""
+    if not arc.keys.is_cuda:
+        _write_host(arc, block, size, blk_lo, blk_hi, k, v, p0, pos)
+        return
+    origin = ORIGIN if origin is None else origin
     kv, cap, d = arc.keys.shape
     bmean_k, bmean_v = getattr(arc, "bmean_k", None), getattr(arc, "bmean_v", None)
     if blk_hi >= blk_lo and blk_hi >= arc.kmax.shape[1]:
@@ -128,7 +135,7 @@ def _write(arc, block: int, size: int, blk_lo: int, blk_hi: int, k=None, v=None,
         if k.stride(-1) != 1 or v.stride() != k.stride():
             raise ValueError("k and v must share strides with a contiguous last dim")
     desc = _capi.PbkArchiveWriteDesc(
-        kv=kv, d=d, block=block, origin=ORIGIN, cap=cap, size=size, p0=p0, n=n, blk_lo=blk_lo, blk_hi=blk_hi,
+        kv=kv, d=d, block=block, origin=origin, cap=cap, size=size, p0=p0, n=n, blk_lo=blk_lo, blk_hi=blk_hi,
         pos=pos32.data_ptr() if pos32 is not None else None, k=k.data_ptr() if k is not None else None,
         v=v.data_ptr() if v is not None else None, in_stride_n=k.stride(0) if k is not None else 0,
         in_stride_kv=k.stride(1) if k is not None else 0, keys=arc.keys.data_ptr(), values=arc.values.data_ptr(),
@@ -139,6 +146,84 @@ def _write(arc, block: int, size: int, blk_lo: int, blk_hi: int, k=None, v=None,
     with torch.cuda.device(arc.keys.device):
         check(LIB.pbk_quest_archive_write(desc, torch.cuda.current_stream(arc.keys.device).cuda_stream),
               "pbk_quest_archive_write")
+
+
+def _host_rows(t: torch.Tensor, rows: torch.Tensor, dev: torch.device) -> torch.Tensor:
+    """Rows `rows` [KV, n] (int64, host) of a host tensor t [KV, N, D], per key head, into HBM
+    [KV, n, D] through pinned memory."""
+    kv, n = rows.shape
+    buf = torch.empty(kv, n, t.shape[2], dtype=t.dtype, pin_memory=True)
+    for h in range(kv):
+        torch.index_select(t[h], 0, rows[h], out=buf[h])
+    return buf.to(dev, non_blocking=True)
+
+
+def _host_range(t: torch.Tensor, lo: int, hi: int, dev: torch.device) -> torch.Tensor:
+    """Rows [lo, hi) of a host tensor [KV, N, D] into HBM, through pinned memory."""
+    buf = torch.empty(t.shape[0], hi - lo, t.shape[2], dtype=t.dtype, pin_memory=True)
+    buf.copy_(t[:, lo:hi])
+    return buf.to(dev, non_blocking=True)
+
+
+def _write_host(arc, block, size, blk_lo, blk_hi, k, v, p0, pos) -> None:
+    dev = arc.kmax.device
+    if k is not None:  # the new rows into the mapped archive
+        kt, vt = k.to(arc.keys.dtype).transpose(0, 1).cpu(), v.to(arc.values.dtype).transpose(0, 1).cpu()
+        if pos is None:
+            arc.keys[:, p0:p0 + k.shape[0]] = kt
+            arc.values[:, p0:p0 + k.shape[0]] = vt
+        else:
+            idx = pos.to("cpu", torch.int64)
+            arc.keys[:, idx] = kt
+            arc.values[:, idx] = vt
+    if blk_hi < blk_lo:
+        return
+    end = size if pos is not None or k is None else max(size, p0 + k.shape[0])
+    r_lo = ORIGIN + blk_lo * block
+    r_hi = min(end, ORIGIN + (blk_hi + 1) * block, arc.keys.shape[1])
+    if r_hi <= r_lo:
+        return
+    bmean_k, bmean_v = getattr(arc, "bmean_k", None), getattr(arc, "bmean_v", None)
+    staged = types.SimpleNamespace(
+        keys=_host_range(arc.keys, r_lo, r_hi, dev), values=_host_range(arc.values, r_lo, r_hi, dev),
+        kmax=arc.kmax[:, blk_lo:], kmin=arc.kmin[:, blk_lo:],
+        bmean_k=bmean_k[:, blk_lo:] if bmean_k is not None else None,
+        bmean_v=bmean_v[:, blk_lo:] if bmean_v is not None else None)
+    # the staged rows begin with block blk_lo: origin 0 there, every row already in place
+    _write(staged, block, r_hi - r_lo, 0, blk_hi - blk_lo, origin=0)
+
+
+def offload_archive(kv: int, d: int, cap: int, block: int, device: torch.device, directory: str | None = None):
+    """A serving archive whose keys and values live in host memory backed by unlinked sparse
+    files (the reference's NVMe offload format, memory.py:457-469: one raw bf16 [KV, cap, D]
+    array per file; only the pages touched use disk or page cache), with every block and
+    super-block summary in HBM. archive_write, retrieve_blocks and piece_attention accept it:
+    new rows go to the files by device-to-host copies, and the rows a call reads (the blocks
+    being summarised, the rerank's candidates, the attention's sinks, blocks, tail and window)
+    are gathered on the host into pinned memory and copied to HBM for the same kernels."""
+    import mmap
+    import tempfile
+
+    def mapped():
+        nbytes = kv * cap * d * 2
+        fd, path = tempfile.mkstemp(dir=directory, prefix="pbk_arc_")
+        try:
+            os.unlink(path)
+            os.ftruncate(fd, nbytes)
+            mm = mmap.mmap(fd, nbytes)
+        except Exception:
+            os.close(fd)
+            raise
+        return torch.frombuffer(mm, dtype=torch.bfloat16).view(kv, cap, d), (fd, mm)
+
+    (keys, fk), (values, fv) = mapped(), mapped()
+    n_blk = cap // block
+    n_sb = (n_blk + SBLK - 1) // SBLK
+    z = lambda rows: torch.zeros(kv, rows, d, dtype=torch.bfloat16, device=device)  # noqa: E731
+    return types.SimpleNamespace(keys=keys, values=values, kmax=z(n_blk), kmin=z(n_blk), bmean_k=z(n_blk),
+                                 bmean_v=z(n_blk), smax=z(n_sb), smin=z(n_sb), smean_k=z(n_sb), smean_v=z(n_sb),
+                                 size=0, prompt_len=0, hole_lo=0, hole_hi=0, dirty_lo=1 << 60, dirty_hi=-1,
+                                 mapped_files=[fk, fv])
 
 
 def _update_super(arc, lo_b: int, hi_b: int, block: int) -> None:
@@ -183,6 +268,8 @@ def _grow(arc, need: int, block: int) -> None:
     cap = arc.keys.shape[1]
     if need <= cap:
         return
+    if not arc.keys.is_cuda:
+        raise RuntimeError(f"offloaded archive full: need {need} rows > {cap}")
     new_cap = max(cap, 1)
     while new_cap < need:
         new_cap *= 2
@@ -284,7 +371,15 @@ def retrieve_blocks(arc, q: torch.Tensor, groups: int, limit: int, rerank: bool,
         pages = select_pages_levels(qs, kmax, kmin, full * block, block, k, smax, smin, SBLK, hole)
     elif rerank and pool > k:
         cand = select(min(pool, n_valid))                         # [1, KV, c] ascending
-        if limit > ROPE_HORIZON:  # the candidates' keys moved in proportion (memory.py:861-862)
+        if not arc.keys.is_cuda:  # the candidates' blocks staged from the host archive
+            if limit > ROPE_HORIZON:
+                raise NotImplementedError("RoPE moves on an offloaded archive")
+            c = cand.shape[-1]
+            rows = (ORIGIN + cand[0].long().cpu()[:, :, None] * block + torch.arange(block)).reshape(cand.shape[1], -1)
+            ck = _host_rows(arc.keys, rows, q.device)
+            ident = torch.arange(c, dtype=torch.int32, device=q.device).expand(1, cand.shape[1], c).contiguous()
+            pages = cand.gather(-1, rerank_pages(qi, ck, ident, block, k).long()).to(torch.int32)
+        elif limit > ROPE_HORIZON:  # the candidates' keys moved in proportion (memory.py:861-862)
             c = cand.shape[-1]
             ck, _ = rope_gather(arc.keys, None, cand[0], block, ORIGIN, c, "proportional", ref_pos=limit)
             ident = torch.arange(c, dtype=torch.int32, device=q.device).expand(1, cand.shape[1], c).contiguous()
@@ -323,6 +418,10 @@ def piece_attention(arc, q: torch.Tensor, q_pos: torch.Tensor, top: torch.Tensor
     win = (arc.keys[:, lo:hi], arc.values[:, lo:hi], kpos, window, 0, scale, out)
     rope = lo > ROPE_HORIZON  # sinks and retrieved blocks move to new RoPE positions (memory.py:1402-1425)
     n_blk = top.shape[1] if top is not None else 0
+    if not arc.keys.is_cuda:
+        if rope:
+            raise NotImplementedError("RoPE moves on an offloaded archive")
+        return _piece_attention_host(arc, qi, qpos, kpos, top, groups, window, scale, lo, hi, ns, block, out, q.dtype)
     sink_k, sink_v = arc.keys, arc.values
     shift = sink_shift(lo, ns, n_blk, block) if rope else 0
     if shift > 0:
@@ -348,3 +447,38 @@ def piece_attention(arc, q: torch.Tensor, q_pos: torch.Tensor, top: torch.Tensor
                                          torch.cuda.current_stream(q.device).cuda_stream),
               "pbk_quest_attend_sinks")
     return out[0].to(q.dtype)
+
+
+def _piece_attention_host(arc, qi, qpos, kpos, top, groups, window, scale, lo, hi, ns, block, out, dtype):
+    """piece_attention over an offloaded archive: the sinks, the retrieved blocks with the
+    partial block before the window, and the window are gathered on the host and copied to
+    HBM, then attended as an archive of the retrieved blocks in order (the same kernel and key
+    order as the in-HBM archive)."""
+    dev = qi.device
+    kv = arc.keys.shape[0]
+    h = qi.shape[2]
+    wk, wv = _host_range(arc.keys, lo, hi, dev), _host_range(arc.values, lo, hi, dev)
+    if ns > 0:
+        sk, sv = _host_range(arc.keys, 0, ns, dev), _host_range(arc.values, 0, ns, dev)
+    else:
+        sk, sv = wk, wv
+    win = (wk, wv, kpos, window, 0, scale, out)
+    if top is not None:
+        n_blk = top.shape[1]
+        tail0 = ORIGIN + ((lo - ORIGIN) // block) * block
+        tail = torch.arange(tail0, lo) if lo > tail0 else torch.zeros(0, dtype=torch.int64)
+        blk_rows = (ORIGIN + top.long().cpu()[:, :, None] * block + torch.arange(block)).reshape(kv, -1)
+        rows = torch.cat((blk_rows, tail[None].expand(kv, -1)), dim=1)
+        rk, rv = _host_rows(arc.keys, rows, dev), _host_rows(arc.values, rows, dev)
+        ident = torch.arange(n_blk, dtype=torch.int32, device=dev).expand(1, h // groups, n_blk).contiguous()
+        desc = _attend_desc(qi, qpos, rk, rv, n_blk * block + tail.numel(), block, ident, *win)
+    else:
+        dummy = torch.zeros(1, h // groups, 1, dtype=torch.int32, device=dev)
+        desc = _attend_desc(qi, qpos, wk, wv, block, block, dummy, *win)
+        desc.n_arch, desc.budget = 0, 0
+    ws = _workspace(LIB.pbk_quest_attend_sinks_workspace(desc, ns), dev)
+    with torch.cuda.device(dev):
+        check(LIB.pbk_quest_attend_sinks(desc, sk.data_ptr(), sv.data_ptr(), ns, sk.stride(0), sk.stride(1),
+                                         ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream),
+              "pbk_quest_attend_sinks")
+    return out[0].to(dtype)

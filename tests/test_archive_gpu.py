@@ -107,3 +107,50 @@ def test_writes_with_growth_match_oracle(cuda_device, sblk2, block):
     _check(arc, want, p, block, 2)
     from pseudobrain_b200._capi import device_error
     assert device_error() == 0
+
+
+@pytest.mark.parametrize("rerank,sb", [(False, False), (False, True), (True, False)])
+def test_offloaded_archive_equals_hbm_archive(cuda_device, sblk2, rerank, sb, tmp_path):
+    """offload_archive (keys and values in unlinked sparse files mapped into host memory, the
+    reference's NVMe format; summaries in HBM) gives the same summaries, block selections and
+    attention as the same writes into an archive in HBM (the same kernels on the same rows)."""
+    S = sblk2
+    saved = dict(S.MEMORY)
+    try:
+        S.MEMORY.update(blocks=6, decode_blocks=6, rerank=12, block_size=16, neighbors=0, window=64)
+        kv, d, block, cap, groups = 2, 128, 16, 1600, 3
+        host = S.offload_archive(kv, d, cap, block, cuda_device, directory=str(tmp_path))
+        dev = _archive(kv, d, cap, block, 2, cuda_device)
+        if not sb:
+            host.smax = dev.smax = None
+        rng = np.random.default_rng(int(rerank) + 2 * int(sb))
+        p = 0
+        for n in (300, 5, 1, 700, 37, 400):
+            kk = torch.from_numpy(oq.bf16_round(rng.standard_normal((n, kv, d)).astype(np.float32))).to(cuda_device,
+                                                                                                         torch.bfloat16)
+            vv = torch.from_numpy(oq.bf16_round(rng.standard_normal((n, kv, d)).astype(np.float32))).to(cuda_device,
+                                                                                                         torch.bfloat16)
+            pos = torch.arange(p, p + n, device=cuda_device)
+            for arc in (host, dev):
+                S.archive_write(arc, pos, kk, vv, block)
+            p += n
+        scat = torch.tensor([20, 700, 1000], device=cuda_device)  # scattered re-writes
+        kk = torch.randn(3, kv, d, device=cuda_device).to(torch.bfloat16)
+        for arc in (host, dev):
+            S.archive_write(arc, scat, kk, kk, block)
+        for arc in (host, dev):
+            arc.prompt_len = p
+            arc.hole_lo, arc.hole_hi = 4 + 16 * 20, 4 + 16 * 31
+        q = torch.randn(2, kv * groups, d, device=cuda_device).to(torch.bfloat16)
+        limit = p - 64
+        tops = [S.retrieve_blocks(arc, q, groups, limit, rerank) for arc in (host, dev)]
+        assert torch.equal(tops[0], tops[1])
+        for name in ("kmax", "kmin", "bmean_k", "bmean_v") + (("smax", "smin", "smean_k", "smean_v") if sb else ()):
+            assert torch.equal(getattr(host, name), getattr(dev, name)), name
+        q_pos = torch.tensor([p - 2, p - 1], device=cuda_device)
+        outs = [S.piece_attention(arc, q, q_pos, tops[0], groups, 64, d ** -0.5) for arc in (host, dev)]
+        assert torch.equal(outs[0], outs[1])
+        assert torch.equal(host.keys[:, :p], dev.keys[:, :p].cpu())
+    finally:
+        S.MEMORY.clear()
+        S.MEMORY.update(saved)
