@@ -183,6 +183,11 @@ PBK_API int pbk_gdn_prefill_varlen(const pbk_gdn_desc* desc, const int32_t* cu_s
  * (l2_normalize, :59-70); fp32 arithmetic, outputs in their views' dtypes. new_tail must not
  * overlap tail. */
 PBK_API int pbk_gdn_conv_norm(const pbk_conv_desc* desc, void* stream);
+/* Row-wise L2 normalisation of x [B, T, H, 128] into out (same shape; bf16 or fp32 each,
+ * last dim contiguous): mode 1 x / max(|x|, eps) (F.normalize, gated_deltanet.py:59-70),
+ * mode 2 x rsqrt(|x|^2 + eps) (the in-kernel q/k norm of vLLM's GDN ops), fp32 arithmetic. */
+PBK_API int pbk_l2norm(pbk_view x, pbk_view out, int32_t batch, int32_t seqlen, int32_t heads, int32_t mode,
+                       float eps, void* stream);
 /* g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (gated_deltanet.py:427-429). */
 PBK_API int pbk_gdn_gating(const pbk_gating_desc* desc, void* stream);
 /* out = o rsqrt(mean(o^2) + eps) weight SiLU(gate) per 128-wide head row

@@ -150,6 +150,7 @@ SIGNATURES = {
     "pbk_quest_archive_write": (ctypes.c_int, [ctypes.POINTER(PbkArchiveWriteDesc), _VP]),
     "pbk_quest_supermeans": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I64, _I64, _VP, _I64, _I64, _I32, _I32,
                                             _VP]),
+    "pbk_l2norm": (ctypes.c_int, [PbkView, PbkView, _I32, _I32, _I32, _I32, ctypes.c_float, _VP]),
     "pbk_swa_prefill": (ctypes.c_int, [ctypes.POINTER(PbkSwaDesc), _VP]),
 }
 

@@ -16,6 +16,8 @@ size_t gdn_prefill_varlen_workspace(const pbk_gdn_desc& d, int num_seqs);
 cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_gating(const pbk_gating_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_out_norm(const pbk_out_norm_desc& d, cudaStream_t st);
+cudaError_t launch_gdn_l2norm(const pbk_view& x, const pbk_view& out, int batch, int seqlen, int heads, int mode,
+                              float eps, cudaStream_t st);
 bool gdn_conv_width_ok(int width);
 cudaError_t launch_gdn_prefill_varlen(const pbk_gdn_desc& d, const int32_t* cu_seqlens, int num_seqs, void* ws,
                                       cudaStream_t st);
@@ -268,6 +270,16 @@ int pbk_gdn_out_norm(const pbk_out_norm_desc* d, void* stream) {
   int st = check_current_device();
   if (st != PBK_OK) return st;
   return launch_status(pbk::launch_gdn_out_norm(*d, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_l2norm(pbk_view x, pbk_view out, int32_t batch, int32_t seqlen, int32_t heads, int32_t mode, float eps,
+               void* stream) {
+  if (batch < 0 || seqlen < 0 || heads < 1 || (mode != 1 && mode != 2) || !(eps >= 0.f)) return PBK_ERR_INVALID;
+  if (batch == 0 || seqlen == 0) return PBK_OK;
+  if (!view_ok(x) || !view_ok(out)) return PBK_ERR_INVALID;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_l2norm(x, out, batch, seqlen, heads, mode, eps, static_cast<cudaStream_t>(stream)));
 }
 
 // Packed varlen prefill (tensor-core path): desc describes [1, T, H, 128] tensors.

@@ -268,7 +268,37 @@ __global__ void __launch_bounds__(256) gdn_out_norm_vec_kernel(const pbk_out_nor
   }
 }
 
+// Row L2 norm: one warp per (sequence, token, head) row of 128, lane = 4 dims.
+__global__ void __launch_bounds__(256) gdn_l2norm_kernel(const pbk_view x, const pbk_view out, int batch, int seqlen,
+                                                         int heads, int mode, float eps) {
+  const int64_t rows = (int64_t)batch * seqlen * heads;
+  const int64_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int h = (int)(r % heads), t = (int)((r / heads) % seqlen), b = (int)(r / ((int64_t)heads * seqlen));
+  const int64_t xb = b * x.stride_b + (int64_t)t * x.stride_t + (int64_t)h * x.stride_h;
+  const int64_t yb = b * out.stride_b + (int64_t)t * out.stride_t + (int64_t)h * out.stride_h;
+  float v[4], ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    v[u] = load_any(x.data, xb + lane + 32 * u, x.dtype);
+    ss = fmaf(v[u], v[u], ss);
+  }
+  ss = warp_sum(ss);
+  const float scale = mode == 1 ? 1.f / fmaxf(sqrtf(ss), eps) : rsqrtf(ss + eps);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) store_any(out.data, yb + lane + 32 * u, out.dtype, v[u] * scale);
+}
+
 }  // namespace
+
+cudaError_t launch_gdn_l2norm(const pbk_view& x, const pbk_view& out, int batch, int seqlen, int heads, int mode,
+                              float eps, cudaStream_t st) {
+  const int64_t rows = (int64_t)batch * seqlen * heads;
+  if (rows == 0) return cudaSuccess;
+  gdn_l2norm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(x, out, batch, seqlen, heads, mode, eps);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st) {
   const dim3 grid((unsigned)((d.seqlen + kTile - 1) / kTile), (unsigned)(2 * d.hk + d.hv), (unsigned)d.batch);
