@@ -957,10 +957,11 @@ __device__ __forceinline__ void st4(bf16* p, const float (&x)[4]) {
   *reinterpret_cast<uint2*>(p) = make_uint2(bf16x2_bits(x[0], x[1]), bf16x2_bits(x[2], x[3]));
 }
 
-__global__ void __launch_bounds__(256) quest_archive_copy_kernel(const pbk_archive_write_desc d) {
+// Input rows [i0, i1) of the write (all of them for a scattered write).
+__global__ void __launch_bounds__(256) quest_archive_copy_kernel(const pbk_archive_write_desc d, int i0, int i1) {
   const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i = blockIdx.x * 8 + warp;
-  if (i >= d.n) return;
+  const int i = i0 + blockIdx.x * 8 + warp;
+  if (i >= i1) return;
   const int64_t r = d.pos ? (int64_t)d.pos[i] : (int64_t)d.p0 + i;
   if (r < 0 || r >= d.cap) return;
   if (r >= d.origin) {  // rows of a summarised block are written by its warp
@@ -1322,7 +1323,18 @@ cudaError_t launch_quest_rope_gather(const pbk_rope_gather_desc& d, cudaStream_t
 }
 
 cudaError_t launch_quest_archive_write(const pbk_archive_write_desc& d, cudaStream_t st) {
-  if (d.n > 0) quest_archive_copy_kernel<<<dim3((unsigned)((d.n + 7) / 8), d.kv), 256, 0, st>>>(d);
+  auto copy = [&](int i0, int i1) {
+    if (i1 > i0) quest_archive_copy_kernel<<<dim3((unsigned)((i1 - i0 + 7) / 8), d.kv), 256, 0, st>>>(d, i0, i1);
+  };
+  if (d.pos != nullptr || d.blk_hi < d.blk_lo) {
+    copy(0, d.n);
+  } else {  // only the rows outside the summarised blocks (whose warps write their own rows)
+    const int64_t c0 = (int64_t)d.origin + (int64_t)d.blk_lo * d.block;
+    const int64_t c1 = (int64_t)d.origin + ((int64_t)d.blk_hi + 1) * d.block;
+    const int64_t lo = min(max(c0 - d.p0, (int64_t)0), (int64_t)d.n), hi = min(max(c1 - d.p0, lo), (int64_t)d.n);
+    copy(0, (int)lo);
+    copy((int)hi, d.n);
+  }
   const int nblocks = d.blk_hi - d.blk_lo + 1;
   if (nblocks > 0) quest_archive_block_kernel<<<dim3((unsigned)((nblocks + 7) / 8), d.kv), 256, 0, st>>>(d, nblocks);
   return cudaGetLastError();
