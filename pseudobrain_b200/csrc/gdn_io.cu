@@ -94,18 +94,23 @@ __global__ void __launch_bounds__(kHd) gdn_conv_norm_kernel(const pbk_conv_desc 
 // the bf16 rounding of the result; 0 for large negative y).
 __device__ __forceinline__ float silu_fast(float y) { return __fdividef(y, 1.f + __expf(-y)); }
 
+// Two threads per channel, each convolving half of the tile's tokens.
+constexpr int kVecThreads = 2 * kHd;
 template <int K>
-__global__ void __launch_bounds__(kHd) gdn_conv_norm_vec_kernel(const pbk_conv_desc d) {
+__global__ void __launch_bounds__(kVecThreads) gdn_conv_norm_vec_kernel(const pbk_conv_desc d) {
   __shared__ __align__(16) __nv_bfloat16 xs[kTile + kMaxWidth - 1][kHd];
   __shared__ __align__(16) float ys[kTile][kHd + 4];
-  const int tile = blockIdx.x, hd = blockIdx.y, b = blockIdx.z, c = threadIdx.x;
+  // head fastest in the grid: CTAs running together read neighbouring 256-byte slices of the
+  // same input rows (and write neighbouring heads of the same output rows)
+  const int hd = blockIdx.x, tile = blockIdx.y, b = blockIdx.z, c = threadIdx.x & (kHd - 1);
+  const int half = threadIdx.x / kHd;
   constexpr int H = K - 1;
   const int t0 = tile * kTile;
   const int nt = min(kTile, d.seqlen - t0);
   const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(d.x.data);
   const __nv_bfloat16* tb = reinterpret_cast<const __nv_bfloat16*>(d.tail.data);
   // stage rows r = 0 .. H + nt - 1 (token t0 - H + r); 16 vectors of 8 channels per row
-  for (int e = c; e < (H + nt) * 16; e += kHd) {
+  for (int e = threadIdx.x; e < (H + nt) * 16; e += kVecThreads) {
     const int r = e >> 4, vq = e & 15, t = t0 - H + r;
     uint4 val = make_uint4(0u, 0u, 0u, 0u);
     const int64_t ch = (int64_t)hd * kHd + 8 * vq;
@@ -120,9 +125,10 @@ __global__ void __launch_bounds__(kHd) gdn_conv_norm_vec_kernel(const pbk_conv_d
 #pragma unroll
   for (int j = 0; j < K; ++j) w[j] = d.weight != nullptr ? d.weight[((int64_t)hd * kHd + c) * K + j] : 0.f;
   __syncthreads();
+  const int i0 = half * (kTile / 2), i1 = min(i0 + kTile / 2, nt);
 #pragma unroll
-  for (int j = 0; j < H; ++j) win[j] = __bfloat162float(xs[j][c]);
-  for (int i = 0; i < nt; ++i) {
+  for (int j = 0; j < H; ++j) win[j] = __bfloat162float(xs[i0 + j][c]);
+  for (int i = i0; i < i1; ++i) {
     win[H] = __bfloat162float(xs[i + H][c]);
     float y = 0.f;
 #pragma unroll
@@ -131,7 +137,7 @@ __global__ void __launch_bounds__(kHd) gdn_conv_norm_vec_kernel(const pbk_conv_d
 #pragma unroll
     for (int j = 0; j < H; ++j) win[j] = win[j + 1];
   }
-  if (d.new_tail.data != nullptr && t0 + nt == d.seqlen) {
+  if (half == 0 && d.new_tail.data != nullptr && t0 + nt == d.seqlen) {
     for (int j = 0; j < H; ++j)  // the last K - 1 inputs: staged rows nt .. nt + H - 1
       store_any(d.new_tail.data, b * d.new_tail.stride_b + (int64_t)j * d.new_tail.stride_t +
                                      ((int64_t)hd * kHd + c) * d.new_tail.stride_h,
@@ -141,8 +147,8 @@ __global__ void __launch_bounds__(kHd) gdn_conv_norm_vec_kernel(const pbk_conv_d
   const bool is_q = hd < d.hk, is_k = !is_q && hd < 2 * d.hk;
   const pbk_view& out = is_q ? d.q : (is_k ? d.k : d.v);
   const int oh = is_q ? hd : (is_k ? hd - d.hk : hd - 2 * d.hk);
-  const int warp = c >> 5, lane = c & 31;
-  for (int i = warp; i < nt; i += kHd / 32) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = warp; i < nt; i += kVecThreads / 32) {
     const float4 v = *reinterpret_cast<const float4*>(&ys[i][4 * lane]);
     float scale = 1.f;
     if ((is_q || is_k) && d.l2mode != 0) {
@@ -302,16 +308,17 @@ cudaError_t launch_gdn_l2norm(const pbk_view& x, const pbk_view& out, int batch,
 
 cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st) {
   const dim3 grid((unsigned)((d.seqlen + kTile - 1) / kTile), (unsigned)(2 * d.hk + d.hv), (unsigned)d.batch);
-  if (conv_vec_ok(d)) {
+  const dim3 vgrid((unsigned)(2 * d.hk + d.hv), grid.x, (unsigned)d.batch);
+  if (conv_vec_ok(d) && grid.x <= 65535u) {
     switch (d.weight != nullptr ? d.width : 1) {
-      case 1: gdn_conv_norm_vec_kernel<1><<<grid, kHd, 0, st>>>(d); break;
-      case 2: gdn_conv_norm_vec_kernel<2><<<grid, kHd, 0, st>>>(d); break;
-      case 3: gdn_conv_norm_vec_kernel<3><<<grid, kHd, 0, st>>>(d); break;
-      case 4: gdn_conv_norm_vec_kernel<4><<<grid, kHd, 0, st>>>(d); break;
-      case 5: gdn_conv_norm_vec_kernel<5><<<grid, kHd, 0, st>>>(d); break;
-      case 6: gdn_conv_norm_vec_kernel<6><<<grid, kHd, 0, st>>>(d); break;
-      case 7: gdn_conv_norm_vec_kernel<7><<<grid, kHd, 0, st>>>(d); break;
-      default: gdn_conv_norm_vec_kernel<8><<<grid, kHd, 0, st>>>(d); break;
+      case 1: gdn_conv_norm_vec_kernel<1><<<vgrid, kVecThreads, 0, st>>>(d); break;
+      case 2: gdn_conv_norm_vec_kernel<2><<<vgrid, kVecThreads, 0, st>>>(d); break;
+      case 3: gdn_conv_norm_vec_kernel<3><<<vgrid, kVecThreads, 0, st>>>(d); break;
+      case 4: gdn_conv_norm_vec_kernel<4><<<vgrid, kVecThreads, 0, st>>>(d); break;
+      case 5: gdn_conv_norm_vec_kernel<5><<<vgrid, kVecThreads, 0, st>>>(d); break;
+      case 6: gdn_conv_norm_vec_kernel<6><<<vgrid, kVecThreads, 0, st>>>(d); break;
+      case 7: gdn_conv_norm_vec_kernel<7><<<vgrid, kVecThreads, 0, st>>>(d); break;
+      default: gdn_conv_norm_vec_kernel<8><<<vgrid, kVecThreads, 0, st>>>(d); break;
     }
   } else {
     gdn_conv_norm_kernel<<<grid, kHd, 0, st>>>(d);
