@@ -425,7 +425,8 @@ def measure_widen(args, timed, dev, rank, world, pk):
     new_tail = torch.empty_like(tail)
     tc_ = timed(lambda: L.conv_qkv(x, tail, wconv, hk, hv, "max", new_tail), steps, 3) / steps
     out["conv_qkv"] = entry(tc_, 2 * x.numel() * 2 + 2 * tail.numel() * 2 + wconv.numel() * 4, 1,
-                            shape=f"x [{b},{t},{c}] bf16 -> q, k [{b},{t},{hk},128], v [{b},{t},{hv},128] bf16")
+                            shape=f"x [{b},{t},{c}] bf16 -> q, k [{b},{t},{hk},128], v [{b},{t},{hv},128] bf16",
+                            traffic=traffic("gdn_conv_norm_vec_kernel"))
     del x
     decay = torch.randn(b, t, 2 * hv, device=dev, generator=gen).to(torch.bfloat16)
     a_log, dt_bias = torch.randn(hv, device=dev, generator=gen), torch.randn(hv, device=dev, generator=gen)
@@ -436,7 +437,7 @@ def measure_widen(args, timed, dev, rank, world, pk):
     wn = torch.randn(128, device=dev, generator=gen)
     tn = timed(lambda: L.gated_out_norm(o, gate, wn, out_dtype=torch.bfloat16), steps, 3) / steps
     out["gated_out_norm"] = entry(tn, o.numel() * 4 + gate.numel() * 2 + o.numel() * 2, 1,
-                                  shape="o fp32, gate bf16 -> out bf16")
+                                  shape="o fp32, gate bf16 -> out bf16", traffic=traffic("gdn_out_norm_vec_kernel"))
     del o, gate, decay
     torch.cuda.empty_cache()
     # two-level Quest selection (research defaults)
@@ -480,8 +481,9 @@ def measure_widen(args, timed, dev, rank, world, pk):
     tw = timed(lambda: S.archive_write(arc, pos, kn, vn, block, p0, p0 + n_new), steps, 3) / steps
     nb_touch = n_new // block
     w_bytes = 2 * kn.numel() * 2 * 2 + nb_touch * kv * d * 2 * 4
-    out["archive_write"] = entry(tw, w_bytes, 5, config=f"{n_new} tokens x {kv} key heads into a {cap}-row archive, "
-                                                        f"blocks of {block}, super-blocks of {S.SBLK}")
+    out["archive_write"] = entry(tw, w_bytes, 4, config=f"{n_new} tokens x {kv} key heads into a {cap}-row archive, "
+                                                        f"blocks of {block}, super-blocks of {S.SBLK}",
+                                 traffic=traffic("quest_archive_block_kernel"))
     # RoPE move + gather of the retrieved blocks
     nsel = 1024
     blocks = torch.sort(torch.stack([torch.randperm(n_blk - 1, device=dev, generator=gen)[:nsel]
@@ -489,14 +491,15 @@ def measure_widen(args, timed, dev, rank, world, pk):
     tr = timed(lambda: S.rope_gather(arc.keys, arc.values, blocks, block, S.ORIGIN, nsel, "runs",
                                      ref_pos=cap - 1024), steps, 3) / steps
     out["rope_gather"] = entry(tr, 2 * 2 * kv * nsel * block * d * 2, 2,
-                               config=f"{nsel} blocks of {block} x {kv} key heads, keys moved, values gathered")
+                               config=f"{nsel} blocks of {block} x {kv} key heads, keys moved, values gathered",
+                               traffic=traffic("quest_rope_gather_kernel"))
     del arc, kn, vn
     torch.cuda.empty_cache()
-    out["gpu_launches"] = 3 * steps + 5 * (steps * 4 + 3) + 5 * steps + 2 * steps
+    out["gpu_launches"] = 3 * steps + 5 * (steps * 4 + 3) + 4 * steps + 2 * steps
     cv = out["conv_qkv"]  # the line's own fields when this part runs alone
     out.update(metric="widened rows: HBM GB/s of each piece", value=cv["achieved_gbps"], unit="GB/s",
                roofline={"bound": "hbm", "achieved": cv["achieved_gbps"], "peak": hbm, "unit": "GB/s",
-                         "frac": cv["frac"], "traffic": None, "kernel": "gdn_conv_norm_kernel"})
+                         "frac": cv["frac"], "traffic": cv.get("traffic"), "kernel": "gdn_conv_norm_vec_kernel"})
     return out
 
 
