@@ -176,10 +176,13 @@ __global__ void __launch_bounds__(kVecThreads) gdn_conv_norm_vec_kernel(const pb
   }
 }
 
+// One thread per (sequence, token, head); 32-bit index arithmetic (the launcher checks that
+// the element count fits), as 64-bit divisions would cost more than the element's work.
 __global__ void gdn_gating_kernel(const pbk_gating_desc d) {
-  const int64_t n = (int64_t)d.batch * d.seqlen * d.hv;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
-    const int h = (int)(e % d.hv), t = (int)((e / d.hv) % d.seqlen), b = (int)(e / ((int64_t)d.hv * d.seqlen));
+  const uint32_t n = (uint32_t)d.batch * d.seqlen * d.hv;
+  for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+    const uint32_t row = e / (uint32_t)d.hv;
+    const int h = (int)(e - row * (uint32_t)d.hv), t = (int)(row % (uint32_t)d.seqlen), b = (int)(row / (uint32_t)d.seqlen);
     const int64_t ab = b * d.decay.stride_b + (int64_t)t * d.decay.stride_t;
     const float a = load_any(d.decay.data, ab + (int64_t)h * d.decay.stride_h, d.decay.dtype);
     const float bb = load_any(d.decay.data, ab + (int64_t)(d.hv + h) * d.decay.stride_h, d.decay.dtype);
@@ -338,6 +341,7 @@ cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st) {
 
 cudaError_t launch_gdn_gating(const pbk_gating_desc& d, cudaStream_t st) {
   const int64_t n = (int64_t)d.batch * d.seqlen * d.hv;
+  if (n > 0x7fffffffLL) return cudaErrorInvalidValue;  // 32-bit element indices
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
   gdn_gating_kernel<<<blocks, 256, 0, st>>>(d);
   return cudaGetLastError();
