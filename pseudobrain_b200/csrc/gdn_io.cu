@@ -244,11 +244,13 @@ bool conv_vec_ok(const pbk_conv_desc& d) {
 // contiguous rows, gate bf16, weight fp32; SiLU as silu_fast when the output is bf16.
 template <typename TO, typename TG>
 __global__ void __launch_bounds__(256) gdn_out_norm_vec_kernel(const pbk_out_norm_desc d) {
-  const int64_t rows = (int64_t)d.batch * d.seqlen * d.hv;
-  const int64_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  // 32-bit row arithmetic (the launcher takes this kernel only below 2^31 rows)
+  const uint32_t rows = (uint32_t)d.batch * d.seqlen * d.hv;
+  const uint32_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
   const int lane = threadIdx.x & 31;
-  const int h = (int)(r % d.hv), t = (int)((r / d.hv) % d.seqlen), b = (int)(r / ((int64_t)d.hv * d.seqlen));
+  const uint32_t bt = r / (uint32_t)d.hv;
+  const int h = (int)(r - bt * (uint32_t)d.hv), t = (int)(bt % (uint32_t)d.seqlen), b = (int)(bt / (uint32_t)d.seqlen);
   const int64_t ob = b * d.o.stride_b + (int64_t)t * d.o.stride_t + (int64_t)h * d.o.stride_h + 4 * lane;
   const int64_t gb = b * d.gate.stride_b + (int64_t)t * d.gate.stride_t + (int64_t)h * d.gate.stride_h + 4 * lane;
   const int64_t yb = b * d.out.stride_b + (int64_t)t * d.out.stride_t + (int64_t)h * d.out.stride_h + 4 * lane;
@@ -354,7 +356,8 @@ cudaError_t launch_gdn_out_norm(const pbk_out_norm_desc& d, cudaStream_t st) {
     return aligned(x.data, 4 * elems) && x.stride_b % 4 == 0 && x.stride_t % 4 == 0 && x.stride_h % 4 == 0;
   };
   const bool o32 = d.o.dtype == PBK_F32, out32 = d.out.dtype == PBK_F32;
-  const bool vec = (o32 || d.o.dtype == PBK_BF16) && d.gate.dtype == PBK_BF16 && d.weight_dtype == PBK_F32 &&
+  const bool vec = rows < 0x7fffffffLL && (o32 || d.o.dtype == PBK_BF16) && d.gate.dtype == PBK_BF16 &&
+                   d.weight_dtype == PBK_F32 &&
                    aligned(d.weight, 16) && rows_ok(d.o, o32 ? 4 : 2) && rows_ok(d.gate, 2) &&
                    rows_ok(d.out, out32 ? 4 : 2);
   if (!vec) gdn_out_norm_kernel<<<grid, 256, 0, st>>>(d);
