@@ -25,6 +25,21 @@ __device__ __forceinline__ void store_any(const void* p, int64_t i, int dtype, f
   else const_cast<float*>(reinterpret_cast<const float*>(p))[i] = x;
 }
 
+// Row r of a [B, T, H] row space into (b, t, h): 32-bit division below 2^31 rows (64-bit
+// division costs far more than a row's work).
+__device__ __forceinline__ void split_row(int64_t r, int heads, int seqlen, int& b, int& t, int& h) {
+  if (r < 0x7fffffffLL) {
+    const uint32_t bt = (uint32_t)r / (uint32_t)heads;
+    h = (int)((uint32_t)r - bt * (uint32_t)heads);
+    t = (int)(bt % (uint32_t)seqlen);
+    b = (int)(bt / (uint32_t)seqlen);
+  } else {
+    h = (int)(r % heads);
+    t = (int)((r / heads) % seqlen);
+    b = (int)(r / ((int64_t)heads * seqlen));
+  }
+}
+
 // CTA = (token tile, head of the q | k | v channel layout, sequence); thread = channel.
 __global__ void __launch_bounds__(kHd) gdn_conv_norm_kernel(const pbk_conv_desc d) {
   __shared__ float ys[kTile][kHd + 1];
@@ -202,7 +217,8 @@ __global__ void __launch_bounds__(256) gdn_out_norm_kernel(const pbk_out_norm_de
   const int64_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
   const int lane = threadIdx.x & 31;
-  const int h = (int)(r % d.hv), t = (int)((r / d.hv) % d.seqlen), b = (int)(r / ((int64_t)d.hv * d.seqlen));
+  int b, t, h;
+  split_row(r, d.hv, d.seqlen, b, t, h);
   const int64_t ob = b * d.o.stride_b + (int64_t)t * d.o.stride_t + (int64_t)h * d.o.stride_h;
   const int64_t gb = b * d.gate.stride_b + (int64_t)t * d.gate.stride_t + (int64_t)h * d.gate.stride_h;
   const int64_t yb = b * d.out.stride_b + (int64_t)t * d.out.stride_t + (int64_t)h * d.out.stride_h;
@@ -296,7 +312,8 @@ __global__ void __launch_bounds__(256) gdn_l2norm_kernel(const pbk_view x, const
   const int64_t r = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
   const int lane = threadIdx.x & 31;
-  const int h = (int)(r % heads), t = (int)((r / heads) % seqlen), b = (int)(r / ((int64_t)heads * seqlen));
+  int b, t, h;
+  split_row(r, heads, seqlen, b, t, h);
   const int64_t xb = b * x.stride_b + (int64_t)t * x.stride_t + (int64_t)h * x.stride_h;
   const int64_t yb = b * out.stride_b + (int64_t)t * out.stride_t + (int64_t)h * out.stride_h;
   float v[4], ss = 0.f;
