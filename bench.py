@@ -50,6 +50,9 @@ HYBRID_HEADS = dict(hk=16, hv=32, heads=32, kv=8, d=128, window=4096)
 QUEST_SHAPE = dict(kv=8, heads=32, d=128, page=16, window=4096, nq=8, budget_tokens=4096)
 
 
+PREFILL_KERNELS = ("gdn_solve_kernel", "gdn_prefill_tc_kernel")  # the kernels of one prefill step
+
+
 def prefill_flops_per_token_head(c=64, d=128):
     """5 C x C x d products (KK^T, QK^T, W, U', (QK*D)U) + 3 d x d products per token
     (WS, QS, K^T U) + the triangular inverse (C^2/3 per token)."""
@@ -204,6 +207,8 @@ def measure_prefill(args, timed, dev, rank, world, pk):
     t_rec = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps / 1e3
     del ws
     achieved = (flops - solve_flops) / t_rec / 1e12
+    tr_parts = [traffic(kn) for kn in PREFILL_KERNELS]
+    step_traffic = sum(tr_parts) if all(x is not None for x in tr_parts) else None
     # e2e through the public API: pinned host inputs in, bf16 outputs back, every step
     host = {n: x[n].cpu().pin_memory() for n in ("q", "k", "v", "g", "beta")}
     dev_in = {n: torch.empty_like(x[n]) for n in host}
@@ -220,15 +225,18 @@ def measure_prefill(args, timed, dev, rank, world, pk):
     return {
         "value": world * tokens * args.steps / t, "unit": "tok/s", "ms_per_step": per_step * 1e3,
         "tokens": tokens,
+        # the kernel is timed alone over regions of tens of ms: the burst tensor peak applies
         "roofline": {"bound": "tensor", "kernel": "gdn_prefill_tc_kernel", "achieved": achieved,
-                     "peak": pk["tc_sustained"], "unit": "TFLOP/s", "frac": achieved / pk["tc_sustained"],
-                     "traffic": traffic("gdn_prefill_tc_kernel"), "peak_source": f"{pk['src']} bf16 sustained",
+                     "peak": pk["tc"], "unit": "TFLOP/s", "frac": achieved / pk["tc"],
+                     "traffic": traffic("gdn_prefill_tc_kernel"), "peak_source": f"{pk['src']} bf16 burst",
                      "algorithmic_flops": flops - solve_flops, "ms": t_rec * 1e3},
         "kernels": {"gdn_solve_kernel": {"ms": t_solve * 1e3, "tflops": solve_flops / t_solve / 1e12,
                                          "traffic": traffic("gdn_solve_kernel")},
                     "gdn_prefill_tc_kernel": {"ms": t_rec * 1e3, "tflops": (flops - solve_flops) / t_rec / 1e12}},
-        "step": {"tflops": flops / per_step / 1e12, "frac": flops / per_step / 1e12 / pk["tc_sustained"],
-                 "algorithmic_bytes": algo_bytes, "hbm_frac": algo_bytes / per_step / 1e9 / pk["hbm"]},
+        "step": {"tflops": flops / per_step / 1e12, "frac": flops / per_step / 1e12 / pk["tc"],
+                 "algorithmic_bytes": algo_bytes, "hbm_frac": algo_bytes / per_step / 1e9 / pk["hbm"],
+                 "traffic": step_traffic,
+                 "traffic_over_algorithmic": step_traffic / algo_bytes if step_traffic else None},
         "e2e": {"value": world * tokens * e2e_steps / t_e2e, "unit": "tok/s",
                 "h2d_bytes_per_step": sum(tt.numel() * tt.element_size() for tt in host.values()),
                 "d2h_bytes_per_step": host_o.numel() * host_o.element_size()},
@@ -571,12 +579,12 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         "per_gpu": t / t_step / world, "scaling": "strong", "ms_per_step": t_step * 1e3,
         "config": {"seqlen": t, "gdn_heads_per_gpu": hv, "gdn_segments": segs, "swa_q_heads_per_gpu": heads,
                    "window": H["window"], "size": args.size},
-        "roofline": {"bound": "tensor", "achieved": per_gpu / t_step / 1e12, "peak": pk["tc_sustained"],
-                     "unit": "TFLOP/s", "frac": per_gpu / t_step / 1e12 / pk["tc_sustained"],
-                     "traffic": None, "peak_source": f"{pk['src']} bf16 sustained"},
+        "roofline": {"bound": "tensor", "achieved": per_gpu / t_step / 1e12, "peak": pk["tc"],
+                     "unit": "TFLOP/s", "frac": per_gpu / t_step / 1e12 / pk["tc"],
+                     "traffic": None, "peak_source": f"{pk['src']} bf16 burst (timed regions under a second)"},
         "gdn": {"ms": t_gdn * 1e3, "tflops": gdn_flops / world / t_gdn / 1e12},
         "swa": {"ms": t_swa * 1e3, "tflops": swa_flops / world / t_swa / 1e12,
-                "frac": swa_flops / world / t_swa / 1e12 / pk["tc_sustained"]},
+                "frac": swa_flops / world / t_swa / 1e12 / pk["tc"]},
         "e2e": None,
         "gpu_launches": steps * (1 + 4 + 1 + 1),  # one chunk solve, 4 recurrence runs, scan, attention
     }
@@ -584,6 +592,16 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         out["all_gather"] = {"ms": t_ag * 1e3, "bytes_received_per_gpu": ag_bytes,
                              "gbps": ag_bytes / t_ag / 1e9 if t_ag > 0 else None}
     return out
+
+
+def headline_config(args, world):
+    """The `config` object of the line (the reference arm prints the same one)."""
+    return {"workload": ("benchmark config 1: GDN chunked prefill B=4 T=32768 Hk=16 Hv=32 dk=dv=128 chunk=64 "
+                         "per GPU") if args.workload in ("all", "prefill") else f"{args.workload} part only",
+            "size": args.size, "global_batch": PREFILL[args.size]["batch"] * world,
+            "seq_len": PREFILL[args.size]["seqlen"],
+            "parallelism": f"(sequence x value-head) shards, {world} GPU(s), no collective",
+            "l2": "inputs larger than L2 (126 MB) in every timed part"}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -614,79 +632,191 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 inputs, fp32 state/accumulation", "data": "synthetic (seeded, benchmark config distributions)",
-        "config": {"workload": ("benchmark config 1: GDN chunked prefill B=4 T=32768 Hk=16 Hv=32 dk=dv=128 chunk=64 "
-                                "per GPU") if "prefill" in parts else f"{args.workload} part only",
-                   "size": args.size, "global_batch": PREFILL[args.size]["batch"] * world,
-                   "seq_len": PREFILL[args.size]["seqlen"],
-                   "parallelism": f"(sequence x value-head) shards, {world} GPU(s), no collective",
-                   "l2": "inputs larger than L2 (126 MB) in every timed part"},
+        "config": headline_config(args, world),
         "roofline": head["roofline"], "e2e": head.get("e2e"), "gpu_launches": head["gpu_launches"],
         "clocks": clk.summary(),
     }
-    for name in ("decode", "quest", "hybrid", "serving", "widen"):
+    # the large, secondary parts first and decode / quest last: a reader of the end of the
+    # line (a log tail) sees the two other headline parts of the metric
+    for name in ("widen", "serving", "hybrid", "decode", "quest"):
         if name in parts and parts[name] is not None and (parts[name] is not head or name == "widen"):
             line[name] = parts[name]
-    if world == 1 and not args.no_cpu_baseline and "prefill" in parts:
-        line["cpu_baseline"] = cpu_baseline()
+    if world == 1 and not args.no_cpu_baseline:
+        if "prefill" in parts:
+            line["cpu_baseline"] = cpu_baseline()
+        for name, fn in (("hybrid", cpu_baseline_hybrid), ("decode", cpu_baseline_decode),
+                         ("quest", cpu_baseline_quest)):
+            if line.get(name) is not None and args.size == "full":
+                line[name]["cpu_baseline"] = fn()
+        for name in ("decode", "quest"):  # keep the two at the end of the line
+            if name in line:
+                line[name] = line.pop(name)
     return line
 
 
 # --------------------------------------------------------------------------------------------
-# CPU baseline / reference arm: the oracle (numpy restatement of the reference algorithm)
+# CPU baseline / reference arm: the reference's CPU path restated with the same torch CPU
+# operations (oracle/cpu_reference.py), on all host cores, over bounded samples of each config
 # --------------------------------------------------------------------------------------------
-def _cpu_threads():
-    n = len(os.sched_getaffinity(0))
-    try:
-        from threadpoolctl import threadpool_limits
-        threadpool_limits(n)
-    except Exception:  # noqa: BLE001 - threadpoolctl is optional
-        pass
-    return n
+def _cpu_gdn_inputs(torch, batch, t, hk, hv, seed, state_std=0.0):
+    """Config-0 distributions on the host, q and k expanded from the key heads to the value
+    heads as the reference's caller does (gated_deltanet.py:422-424)."""
+    import torch.nn.functional as F
+    g_ = torch.Generator().manual_seed(seed)
+    q = F.normalize(torch.randn(batch, t, hk, 128, generator=g_), dim=-1).to(torch.bfloat16).float()
+    k = F.normalize(torch.randn(batch, t, hk, 128, generator=g_), dim=-1).to(torch.bfloat16).float()
+    v = torch.randn(batch, t, hv, 128, generator=g_).to(torch.bfloat16).float()
+    beta = torch.sigmoid(torch.randn(batch, t, hv, generator=g_)).to(torch.bfloat16).float()
+    g = F.logsigmoid(torch.randn(batch, t, hv, generator=g_) + 2.0)
+    rep = hv // hk
+    if state_std:  # a tiled random state: the values do not change the work
+        base = torch.randn(1, hv, 128, 128, generator=g_) * state_std
+        h0 = base.expand(batch, -1, -1, -1).contiguous()
+    else:
+        h0 = torch.zeros(batch, hv, 128, 128)
+    return q.repeat_interleave(rep, 2), k.repeat_interleave(rep, 2), v, g, beta, h0
 
 
-def cpu_baseline(samples=4):
-    """Prefill tok/s of the oracle's delta_rule_chunked on a bounded slice of config 1:
-    B=1, T=16384 (256 chunks), 32 value heads (q, k repeated from 16 key heads), fp32; each
-    sample about 2.5 s on 16 host threads, the tokens of all samples over their total time."""
-    import numpy as np
-    from oracle import gdn as ogdn
-    cores = _cpu_threads()
-    rng = np.random.default_rng(0)
-    t, hk, hv = 16384, PREFILL_HEADS["hk"], PREFILL_HEADS["hv"]
+def cpu_prefill_step(t=8192, seed=0):
+    """One bounded sample of config 1 on the host: B=1, T=t, 16 key / 32 value heads, fp32
+    compute (delta_rule_chunked). Returns (tokens, seconds)."""
+    import torch
+    from oracle import cpu_reference as cr
+    q, k, v, g, beta, h0 = _cpu_gdn_inputs(torch, 1, t, PREFILL_HEADS["hk"], PREFILL_HEADS["hv"], seed)
+    t0 = time.perf_counter()
+    cr.chunked_prefill(q, k, v, g, beta, 128 ** -0.5, h0)
+    return t, time.perf_counter() - t0
 
-    def unit(shape):
-        a = rng.standard_normal(shape, dtype=np.float32)
-        return a / np.linalg.norm(a, axis=-1, keepdims=True)
 
-    q, k = unit((1, t, hk, 128)), unit((1, t, hk, 128))
-    v = rng.standard_normal((1, t, hv, 128), dtype=np.float32)
-    beta = (1 / (1 + np.exp(-rng.standard_normal((1, t, hv))))).astype(np.float32)
-    g = (-np.logaddexp(0, -(rng.standard_normal((1, t, hv)) + 2))).astype(np.float32)
-    h0 = np.zeros((1, hv, 128, 128), np.float32)
-    qe, ke = ogdn.expand_key_heads(q, hv), ogdn.expand_key_heads(k, hv)
+def cpu_baseline(samples=3, t=8192):
+    """Config-1 prefill tok/s of the reference's CPU path (oracle/cpu_reference.py, torch,
+    all host cores) over `samples` samples of B=1, T=t, after one warm-up sample."""
+    from oracle import cpu_reference as cr
+    cores = cr.use_all_cores()
+    cpu_prefill_step(t)
+    toks = secs = 0.0
+    for i in range(samples):
+        n, dt = cpu_prefill_step(t, seed=i + 1)
+        toks, secs = toks + n, secs + dt
+    return {"value": toks / secs, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"delta_rule_chunked (torch fp32 CPU restatement), B=1 T={t} Hk=16 Hv=32, {samples} samples "
+                      f"after 1 warm-up, {secs:.1f} s"}
+
+
+def cpu_baseline_decode(steps=5):
+    """Config-2 decode steps/s on the host: gated_delta_rule(..., "sequential") of B=256
+    one-token sequences, 32 value heads, the 537 MB fp32 state (the median of `steps` steps
+    after one warm-up)."""
+    import torch
+    from oracle import cpu_reference as cr
+    cores = cr.use_all_cores()
+    q, k, v, g, beta, h0 = _cpu_gdn_inputs(torch, 256, 1, DECODE_HEADS["hk"], DECODE_HEADS["hv"], 2, state_std=0.02)
     times = []
-    for _ in range(samples):
+    for i in range(steps + 1):
         t0 = time.perf_counter()
-        ogdn.delta_rule_chunked(qe, ke, v, g, beta, 128 ** -0.5, h0)
+        _, h0 = cr.sequential_steps(q, k, v, g, beta, 128 ** -0.5, h0)
         times.append(time.perf_counter() - t0)
-    total = sum(times)
-    return {"value": t * samples / total, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"oracle delta_rule_chunked (numpy fp32), B=1 T={t} Hv={hv}, {samples} run(s), {total:.2f} s"}
+    med = statistics.median(times[1:])
+    return {"value": 1.0 / med, "unit": "steps/s", "cores": cores, "kind": "port",
+            "sample": f"delta_rule_sequential (torch fp32 CPU restatement), B=256 Hv=32, median of {steps} in-place "
+                      f"steps after 1 warm-up ({med * 1e3:.0f} ms per step)"}
 
 
-def run_reference(args, rank):
+def cpu_baseline_quest(nq=8):
+    """Config-3 Quest q/s on the host: per query, the reference's flat retrieve (fp32 bound
+    scores, topk, sort, gather + tail) and SDPA over [retrieved ; window] over a 1M-token bf16
+    cache with its page bounds precomputed (not timed). The cache is 64 copies of a seeded
+    16384-token block, each shifted by its own seeded offset (drawing 2G normals on the host
+    would take a minute; the work per query depends only on the sizes)."""
+    import torch
+    from oracle import cpu_reference as cr
+    cores = cr.use_all_cores()
+    Q = {**QUEST["full"], **QUEST_SHAPE}
+    kv, d, n = Q["kv"], Q["d"], Q["n_tokens"]
+    g_ = torch.Generator().manual_seed(3)
+    blk = 16384
+    reps = n // blk
+
+    def cache():
+        base = torch.randn(1, kv, 1, blk, d, generator=g_)
+        shift = torch.randn(1, kv, reps, 1, d, generator=g_) * 0.5
+        return (base + shift).reshape(1, kv, n, d).to(torch.bfloat16)
+
+    keys, values = cache(), cache()
+    n_arch = n - Q["window"]
+    kmax, kmin = cr.page_bounds(keys[:, :, :n_arch], Q["page"])
+    q = torch.randn(nq, 1, Q["heads"], d, generator=g_).to(torch.bfloat16)
+    qpos = torch.tensor([n - 1])
+    kpos = torch.arange(n_arch, n)
+    times = []
+    for i in range(nq + 1):  # the first query warms up
+        t0 = time.perf_counter()
+        cr.quest_retrieve_attend(q[i % nq].transpose(0, 1)[None], keys[:, :, :n_arch], values[:, :, :n_arch],
+                                 kmax, kmin, n_arch, Q["page"], Q["budget_tokens"] // Q["page"], keys[:, :, n_arch:],
+                                 values[:, :, n_arch:], qpos, kpos, Q["window"])
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times[1:])
+    return {"value": 1.0 / per, "unit": "q/s", "cores": cores, "kind": "port",
+            "sample": f"retrieve (flat, fp32 scores) + SDPA per query over a 1M-token cache, median of {nq} queries "
+                      f"after 1 warm-up ({per * 1e3:.0f} ms per query; page bounds built once, not timed)"}
+
+
+def cpu_baseline_hybrid(t=16384):
+    """Config-4 hybrid layer tok/s on the host, extrapolated from a t-token slice: the GDN
+    branch (delta_rule_chunked, 16/32 heads) plus the window attention branch (32/8 heads,
+    window 4096, query chunks of 4096 through SDPA), each scaled to 1M tokens by its work
+    (GDN linear in T; attention by the visible (query, key) pairs)."""
+    import torch
+    from oracle import cpu_reference as cr
+    cores = cr.use_all_cores()
+    H = HYBRID_HEADS
+    q, k, v, g, beta, h0 = _cpu_gdn_inputs(torch, 1, t, H["hk"], H["hv"], 4)
+    t0 = time.perf_counter()
+    cr.chunked_prefill(q, k, v, g, beta, 128 ** -0.5, h0)
+    t_gdn = time.perf_counter() - t0
+    g_ = torch.Generator().manual_seed(5)
+    qa = torch.randn(1, H["heads"], t, H["d"], generator=g_).to(torch.bfloat16).float()
+    ka = torch.randn(1, H["kv"], t, H["d"], generator=g_).to(torch.bfloat16).float()
+    va = torch.randn(1, H["kv"], t, H["d"], generator=g_).to(torch.bfloat16).float()
+    t0 = time.perf_counter()
+    cr.window_attention(qa, ka, va, H["window"])
+    t_swa = time.perf_counter() - t0
+    full = HYBRID["full"]["seqlen"]
+    est = t_gdn * full / t + t_swa * swa_pairs(full, H["window"]) / swa_pairs(t, H["window"])
+    return {"value": full / est, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{t}-token slice ({t_gdn:.1f} s GDN + {t_swa:.1f} s window attention), extrapolated to "
+                      f"{full} tokens ({est:.0f} s): GDN by T, attention by visible (query, key) pairs"}
+
+
+def run_reference(args, rank, config):
+    """The reference arm: the reference's CPU path (torch CPU restatement, all host cores) on
+    the headline metric, config 1 prefill tok/s, W warm-up and K timed steps of one bounded
+    B=1, T=8192 sample each; plus one CPU figure per other config."""
     if rank != 0:
         return None
-    base = cpu_baseline(samples=1)  # warm-up sample
-    vals = [cpu_baseline(samples=1)["value"] for _ in range(max(1, min(args.steps, 5)))]
-    value = statistics.median(vals)
-    return {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(vals),
-            "warmup": 1, "ms_per_step": 16384 / value * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, benchmark config distributions)",
-            "impl": "reference",
-            "config": {"workload": "benchmark config 1 prefill, bounded CPU sample B=1 T=16384 Hv=32 per step"},
-            "cpu_baseline": {**base, "value": value},
+    from oracle import cpu_reference as cr
+    cores = cr.use_all_cores()
+    t = 8192
+    for i in range(args.warmup):
+        cpu_prefill_step(t, seed=100 + i)
+    toks = secs = 0.0
+    for i in range(args.steps):
+        n, dt = cpu_prefill_step(t, seed=i)
+        toks, secs = toks + n, secs + dt
+    value = toks / secs
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, benchmark config "
+            "distributions)", "impl": "reference", "config": config,
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"delta_rule_chunked (torch fp32 CPU restatement of gated_deltanet.py:110-165),"
+                                       f" one B=1 T={t} Hk=16 Hv=32 sample per step"},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.workload == "all":
+        line["decode"] = cpu_baseline_decode()
+        line["quest"] = cpu_baseline_quest()
+        line["hybrid"] = cpu_baseline_hybrid()
+    return line
 
 
 def main():
@@ -708,7 +838,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        line = run_reference(args, rank)
+        line = run_reference(args, rank, headline_config(args, world))
     else:
         if world > 1:
             import datetime

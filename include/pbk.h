@@ -127,7 +127,9 @@ PBK_API int pbk_device_check(int device);
 /* Reads (and with clear != 0 resets) the current device's error word, which the
  * tensor-core kernels set to a nonzero code when a bounded device-side wait gives up
  * (the PBK_ERR_TIMEOUT condition; the code names the wait). Synchronises with the
- * device: a diagnostic, not for hot paths. */
+ * device: a diagnostic, not for hot paths. The word's device address is looked up once
+ * per device and kept: a device reset (cudaDeviceReset) while libpbk is loaded is not
+ * supported. */
 PBK_API int pbk_device_error(int* code, int clear);
 
 /* Gated delta rule over few tokens per sequence with the state held in registers:
@@ -259,7 +261,13 @@ PBK_API size_t pbk_quest_attend_workspace(const pbk_quest_desc* desc);
 /* Page scores and top-k selection (exact_memory.py:94-98,124-125,135,144): for every
  * group and key head, score page p as the maximum over the group's t * h/kv query rows
  * of sum_d max(q_d kmax_pd, q_d kmin_pd) in fp32, keep the k highest (ties to the
- * lowest page index) and write them to desc->pages in ascending order. */
+ * lowest page index) and write them to desc->pages in ascending order.
+ * The selection is bit-exact with respect to one fixed order: each row's fp32 sum runs
+ * over d = 0 .. 127 in order (products of two bf16 values are exact in fp32). Up to 64
+ * query rows per key head the scores come from the tensor cores, whose sums differ from
+ * that order by at most 2^-12 ||q_r||_1 max|bound|; the top-k re-scores every page within
+ * twice that of its threshold in the fixed order, so the pages equal the fixed order's
+ * selection. desc->scores (when given) receives the tensor-core scores. */
 PBK_API int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 /* pbk_quest_select in parts (bit mask): 1 the page scores and segment maxima into the
  * workspace, 2 the top-k selection from them (3: both). A caller overlaps other work with
@@ -269,7 +277,8 @@ PBK_API int pbk_quest_select_parts(const pbk_quest_desc* desc, int32_t parts, vo
 
 /* Largest number of page scores (nq * kv * (n_arch / page)) pbk_quest_select_noalloc
  * can hold: 4,194,304 fp32 = 16 MiB, enough for 8 query groups x 8 key heads over a
- * 1M-token archive in 16-token pages. */
+ * 1M-token archive in 16-token pages. Its array also holds the per-32-page and per-128-
+ * page maxima (16.8 MiB in all). */
 #define PBK_QUEST_NOALLOC_MAX_SCORES 4194304
 
 /* pbk_quest_select for callers that cannot allocate device memory. This entry point has
@@ -277,15 +286,19 @@ PBK_API int pbk_quest_select_parts(const pbk_quest_desc* desc, int32_t parts, vo
  * engine that has reserved the free HBM for its KV cache, or a foreign-language caller
  * with no handle on the framework's allocator): for them a workspace allocation fails or
  * stalls the device. This variant takes no workspace: the page scores and their per-32-
- * page maxima go to a fixed 16.5 MiB array that libpbk places in device memory (every GPU
- * that loads the library holds it until the process exits); when desc->scores is given,
- * the scores go there instead. It calls no allocator. Problems with more than
- * PBK_QUEST_NOALLOC_MAX_SCORES scores return PBK_ERR_TOO_LARGE and launch nothing. The
- * first call on a device looks up the array's device address (once per device, with that
- * device current); make that first call before any stream capture. All calls share the
- * one array: calls that overlap on the GPU (two streams at once) race on it, so serialise
- * them. Nothing in the array needs to start at zero: each call overwrites every value it
- * reads. Results equal pbk_quest_select's. */
+ * page maxima and the per-tile bound magnitudes go to a fixed 16.8 MiB array that libpbk
+ * places in device memory (every GPU that loads the library holds it until the process
+ * exits); when desc->scores is given, the scores go there instead. It calls no allocator.
+ * Problems with more than PBK_QUEST_NOALLOC_MAX_SCORES scores, or whose maxima alone
+ * exceed the array, return PBK_ERR_TOO_LARGE and launch nothing; every problem of at most
+ * PBK_QUEST_NOALLOC_MAX_SCORES scores over at least 128 pages per row fits. The first call
+ * on a device looks up the array's device address (once per device, with that device
+ * current) and keeps it for the life of the process; make that first call before any
+ * stream capture, and do not reset the device (cudaDeviceReset) while libpbk is loaded:
+ * the kept address would then be stale. All calls share the one array: calls that overlap
+ * on the GPU (two streams at once) race on it, so serialise them. Nothing in the array
+ * needs to start at zero: each call overwrites every value it reads. Results equal
+ * pbk_quest_select's. */
 PBK_API int pbk_quest_select_noalloc(const pbk_quest_desc* desc, void* stream);
 
 /* Exact softmax attention of every query row over [selected pages ; partial tail ;

@@ -1,7 +1,7 @@
 """CPU oracle for the PseudoBrain hot path. TEST INFRASTRUCTURE ONLY.
 
-This package restates, in numpy (and, for the Quest page score, in plain C), the
-reference algorithms of defnotean/pseudobrain's data-parallel hot path:
+This package restates, in numpy, the reference algorithms of defnotean/pseudobrain's
+data-parallel hot path:
 
 * ``oracle.gdn``   -- the gated delta rule: the per-step recurrence
   (pseudobrain/gated_deltanet.py:93-107) and the chunkwise WY algorithm
@@ -9,7 +9,9 @@ reference algorithms of defnotean/pseudobrain's data-parallel hot path:
 * ``oracle.quest`` -- Quest page-bounded exact memory: page bounds
   (pseudobrain/exact_memory.py:43-50), archive append (:66-85), flat bound score,
   top-k page selection and gather (:88-152), and the exact attention over
-  retrieved pages plus the sliding window (pseudobrain/transplant.py:612-628).
+  retrieved pages plus the sliding window (pseudobrain/transplant.py:612-628); and the
+  canonical-order page scores (fp32, dimension order) that pin the kernels' page
+  selections bit for bit.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline and
 reference legs may import it, and only as the checker or as the timed CPU

@@ -10,7 +10,10 @@ h // groups).
 Scores are computed the way the reference's CPU path computes them: q cast to
 fp32, split into its positive and negative parts, two fp32 products against the
 page maxima and minima, then the maximum over the G*T query rows that share a key
-head (exact_memory.py:94-98,124-125). Page selection keeps the ``budget`` highest
+head (exact_memory.py:94-98,124-125). The ``canonical_*`` functions sum the same
+exact products in a fixed order (dimension 0..127, fp32): the order every selection
+kernel of this build selects on, so they pin its page indices bit for bit, where the
+GEMM-order scores agree only up to near-ties. Page selection keeps the ``budget`` highest
 scores with ties going to the lowest page index (the tie rule of this build; the
 reference's ``torch.topk`` leaves it unspecified) and returns them in position
 order (exact_memory.py:135,144).
@@ -145,6 +148,52 @@ def _bound_scores(qg: np.ndarray, bmax: np.ndarray, bmin: np.ndarray) -> np.ndar
     return (pos @ bmax.astype(np.float64).swapaxes(-1, -2) + neg @ bmin.astype(np.float64).swapaxes(-1, -2)).max(-2)
 
 
+def canonical_bound_scores(qg: np.ndarray, bmax: np.ndarray, bmin: np.ndarray) -> np.ndarray:
+    """The bound scores in this build's canonical order, bit for bit what every selection kernel
+    selects on: for each query row, an fp32 sum over d = 0..127 in order of the exact fp32
+    products t_d = q_d * (kmax_d if q_d > 0 else kmin_d), then the max over rows.
+
+    The reference sums the same products in its GEMM's order (exact_memory.py:97-98,124-125),
+    which no other implementation reproduces; near-ties may resolve either way there. Fixing
+    the order makes the selection a function of the inputs alone. qg [..., R, D] query rows of
+    each key head; bmax/bmin [..., P, D] -> [..., P] fp32."""
+    q = np.asarray(qg, dtype=np.float32)
+    bx = np.moveaxis(np.asarray(bmax, dtype=np.float32), -1, 0)  # [D, ..., P]
+    bn = np.moveaxis(np.asarray(bmin, dtype=np.float32), -1, 0)
+    acc = np.zeros(q.shape[:-1] + (bx.shape[-1],), np.float32)   # [..., R, P]
+    for d in range(q.shape[-1]):
+        qd = q[..., d][..., None]
+        acc += qd * np.where(qd > 0, bx[d][..., None, :], bn[d][..., None, :])  # exact product, fp32 add
+    return acc.max(axis=-2)
+
+
+def canonical_page_scores(q: np.ndarray, kmax: np.ndarray, kmin: np.ndarray, groups: int) -> np.ndarray:
+    """page_scores in the canonical order (canonical_bound_scores). q [B,H,T,D] -> [B,KV,P]."""
+    b, h, t, d = q.shape
+    return canonical_bound_scores(q.reshape(b, h // groups, groups * t, d), kmax, kmin)
+
+
+def canonical_key_scores(qg: np.ndarray, ck: np.ndarray) -> np.ndarray:
+    """The exact rerank score in the canonical order: for candidate c, the max over the head's
+    query rows and the candidate's keys of an fp32 sum over d = 0..127 in order of q_d * k_d
+    (each product exact). qg [..., R, D], ck [..., c, S, D] -> [..., c] fp32."""
+    q = np.asarray(qg, dtype=np.float32)
+    c, s_, d_ = ck.shape[-3:]
+    kf = np.asarray(ck, dtype=np.float32).reshape(ck.shape[:-3] + (c * s_, d_))
+    acc = np.zeros(q.shape[:-1] + (c * s_,), np.float32)
+    for d in range(q.shape[-1]):
+        acc += q[..., d][..., None] * kf[..., d][..., None, :]
+    return acc.max(axis=-2).reshape(ck.shape[:-3] + (c, s_)).max(axis=-1)
+
+
+def canonical_rerank_scores(qg: np.ndarray, keys: np.ndarray, cand: np.ndarray, page: int) -> np.ndarray:
+    """canonical_key_scores of the candidate pages' keys. qg [..., R, D], keys [..., N, D],
+    cand [..., c] -> [..., c] fp32."""
+    idx = (cand[..., :, None] * page + np.arange(page)).reshape(cand.shape[:-1] + (-1,))
+    ck = np.take_along_axis(np.asarray(keys, dtype=np.float32), idx[..., None], axis=-2)  # [..., c*page, D]
+    return canonical_key_scores(qg, ck.reshape(cand.shape + (page, ck.shape[-1])))
+
+
 def _topk_lowest(score: np.ndarray, k: int) -> np.ndarray:
     """Indices of the k largest entries of each row (ties to the lowest index), ascending."""
     order = np.argsort(-score.astype(np.float64), axis=-1, kind="stable")[..., :k]
@@ -152,32 +201,38 @@ def _topk_lowest(score: np.ndarray, k: int) -> np.ndarray:
 
 
 def select_two_level(qg: np.ndarray, kmax: np.ndarray, kmin: np.ndarray, smax: np.ndarray, smin: np.ndarray,
-                     full: int, k: int, sblk: int, hole: tuple[int, int] = (0, 0)) -> np.ndarray:
+                     full: int, k: int, sblk: int, hole: tuple[int, int] = (0, 0), canonical: bool = False) -> np.ndarray:
     """Two-level Quest selection, exact_memory.py:107-122 (pb27_vllm/memory.py:802-836 with its
     archive hole): score the ceil(full/sblk) super-blocks on smax/smin, keep
     m_sb = min(max(16, ceil(2k/sblk)), n_sb) of them, score their pages (pages at or past
     ``full`` and pages in [hole) score -inf; indices clamp to full-1) and keep the best
     min(k, m_sb*sblk). qg [..., R, D] query rows of each key head; bounds [..., P, D].
-    Ties go to the lowest index at both levels. Returns [..., k'] page indices, ascending."""
+    Ties go to the lowest index at both levels. Returns [..., k'] page indices, ascending.
+    canonical: score in the canonical order (canonical_bound_scores) at both levels."""
+    score_fn = canonical_bound_scores if canonical else _bound_scores
     n_sb = (full + sblk - 1) // sblk
-    sb_score = _bound_scores(qg, smax[..., :n_sb, :], smin[..., :n_sb, :])
+    sb_score = score_fn(qg, smax[..., :n_sb, :], smin[..., :n_sb, :])
     m_sb = min(max(16, (2 * k + sblk - 1) // sblk), n_sb)
     top_sb = _topk_lowest(sb_score, m_sb)                                    # ascending
     raw = (top_sb[..., :, None] * sblk + np.arange(sblk)).reshape(top_sb.shape[:-1] + (m_sb * sblk,))
     idx = np.minimum(raw, full - 1)
     bmax = np.take_along_axis(kmax[..., :full, :], idx[..., None], axis=-2)
     bmin = np.take_along_axis(kmin[..., :full, :], idx[..., None], axis=-2)
-    sub = _bound_scores(qg, bmax, bmin)
+    sub = score_fn(qg, bmax, bmin)
     invalid = (raw >= full) | ((idx >= hole[0]) & (idx < hole[1]))
     sub = np.where(invalid, -np.inf, sub)
     keep = _topk_lowest(sub, min(k, m_sb * sblk))
     return np.take_along_axis(idx, keep, axis=-1)
 
 
-def rerank_pages(qg: np.ndarray, keys: np.ndarray, cand: np.ndarray, page: int, k: int) -> np.ndarray:
+def rerank_pages(qg: np.ndarray, keys: np.ndarray, cand: np.ndarray, page: int, k: int,
+                 canonical: bool = False) -> np.ndarray:
     """Exact rerank, exact_memory.py:126-133: candidate page c scores the max over the head's
     query rows and the page's tokens of q.k; keep the best k (ties to the lowest candidate
-    position). qg [..., R, D], keys [..., N, D], cand [..., c] ascending -> [..., k] ascending."""
+    position). qg [..., R, D], keys [..., N, D], cand [..., c] ascending -> [..., k] ascending.
+    canonical: q.k summed in the canonical order (canonical_rerank_scores)."""
+    if canonical:
+        return np.take_along_axis(cand, _topk_lowest(canonical_rerank_scores(qg, keys, cand, page), k), axis=-1)
     idx = (cand[..., :, None] * page + np.arange(page)).reshape(cand.shape[:-1] + (-1,))
     ck = np.take_along_axis(keys, idx[..., None], axis=-2).astype(np.float64)
     exact = (qg.astype(np.float64) @ ck.swapaxes(-1, -2)).max(-2).reshape(cand.shape + (page,)).max(-1)
@@ -185,12 +240,13 @@ def rerank_pages(qg: np.ndarray, keys: np.ndarray, cand: np.ndarray, page: int, 
 
 
 def retrieve_modes(keys, values, kmax, kmin, q, groups: int, page: int, budget: int, superblock: int = 0,
-                   rerank: int = 0, neighbors: int = 0, prompt_top=None):
+                   rerank: int = 0, neighbors: int = 0, prompt_top=None, canonical: bool = False):
     """retrieve, exact_memory.py:88-152, with its other modes: the two-level super-block
     selection for decode queries (t <= 64, rerank <= k, superblock > 1, full > 16 superblock;
     :107-122), the exact rerank of the best ``rerank`` pages (:126-133), a prompt selection
     prepended to a decode selection (:138-140) and ``neighbors`` following pages (:141-143).
-    keys/values [B,KV,N,D], bounds [B,KV,P,D], q [B,H,T,D]. Returns (keys, values, top)."""
+    keys/values [B,KV,N,D], bounds [B,KV,P,D], q [B,H,T,D]. Returns (keys, values, top).
+    canonical: every score in the canonical order (canonical_bound_scores)."""
     b, h, t, d = q.shape
     kv = h // groups
     n = keys.shape[2]
@@ -202,12 +258,12 @@ def retrieve_modes(keys, values, kmax, kmin, q, groups: int, page: int, budget: 
         k = min(budget, full)
         if t <= 64 and rerank <= k and superblock > 1 and full > superblock * 16:
             smax, smin = super_bounds(kmax, kmin, superblock)
-            top = select_two_level(qg, kmax, kmin, smax, smin, full, k, superblock)
+            top = select_two_level(qg, kmax, kmin, smax, smin, full, k, superblock, canonical=canonical)
         else:
-            score = _bound_scores(qg, kmax[:, :, :full], kmin[:, :, :full])
+            score = (canonical_bound_scores if canonical else _bound_scores)(qg, kmax[:, :, :full], kmin[:, :, :full])
             if rerank > k:
                 cand = _topk_lowest(score, min(rerank, full))
-                top = rerank_pages(qg, keys, cand, page, k)
+                top = rerank_pages(qg, keys, cand, page, k, canonical=canonical)
             else:
                 top = _topk_lowest(score, k)
         if t <= 64 and prompt_top is not None:

@@ -138,7 +138,8 @@ def super_bounds(kmax, kmin, n_blk: int, sblk: int):
 
 
 def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_len, smax=None, smin=None, sblk=0,
-                    hole=(0, 0), rope=(ROPE_HORIZON, ROPE_ARC_SPAN, ROPE_THETA), bf16_keys=True):
+                    hole=(0, 0), rope=(ROPE_HORIZON, ROPE_ARC_SPAN, ROPE_THETA), bf16_keys=True,
+                    canonical=False):
     """keys [KV, cap, D]; kmax/kmin [KV, n_blk, D]; q [T, H, D] -> [KV, k] block indices or None.
 
     With smax/smin [KV, n_sb, D] and sblk > 1, a call without rerank over more than 16 sblk
@@ -146,8 +147,9 @@ def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_l
     hole_hi) archive positions whose blocks score -inf (memory.py:769-777, 834-835, 852-853);
     memory["neighbors"] adds the following blocks (:873-875). Past the horizon (rope =
     (horizon, arc_span, theta)) the first d/4 query dims do not score the bounds (:795-797)
-    and the rerank's candidate keys move in proportion (:861-862)."""
-    from .quest import select_two_level
+    and the rerank's candidate keys move in proportion (:861-862). canonical: every score in
+    the canonical order of oracle.quest (the bit-exact pin of the kernels' selections)."""
+    from .quest import canonical_bound_scores, canonical_key_scores, select_two_level
     block = memory["block_size"]
     full = (limit - ORIGIN) // block
     if full <= 0:
@@ -175,10 +177,14 @@ def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_l
         return np.sort(top, axis=-1)
 
     if not rerank and sblk > 1 and smax is not None and full > sblk * 16:
-        return with_neighbors(select_two_level(qs, kmax, kmin, smax, smin, full, k, sblk, (hb0, hb1)))
-    pos, neg = np.maximum(qs, 0), np.minimum(qs, 0)
-    score = (np.einsum("grd,gnd->grn", pos, kmax[:, :full].astype(np.float64))
-             + np.einsum("grd,gnd->grn", neg, kmin[:, :full].astype(np.float64))).max(1)      # [KV, full]
+        return with_neighbors(select_two_level(qs, kmax, kmin, smax, smin, full, k, sblk, (hb0, hb1),
+                                               canonical=canonical))
+    if canonical:
+        score = canonical_bound_scores(qs, kmax[:, :full], kmin[:, :full]).astype(np.float64)   # [KV, full]
+    else:
+        pos, neg = np.maximum(qs, 0), np.minimum(qs, 0)
+        score = (np.einsum("grd,gnd->grn", pos, kmax[:, :full].astype(np.float64))
+                 + np.einsum("grd,gnd->grn", neg, kmin[:, :full].astype(np.float64))).max(1)  # [KV, full]
     score[:, hb0:hb1] = -np.inf
     pool = max(memory["rerank"], 2 * k) if memory["rerank"] > 0 else 0
     if rerank and pool > k:
@@ -189,7 +195,10 @@ def retrieve_blocks(keys, kmax, kmin, q, groups, limit, rerank, memory, prompt_l
         if limit > rope[0]:
             ck = reposition_blocks(ck.reshape(kv, -1, d), cand, block, limit, False, *rope,
                                    bf16=bf16_keys).reshape(ck.shape)
-        exact = np.einsum("grd,gcsd->grcs", qg, ck).max(axis=(1, 3))                   # [KV, c]
+        if canonical:
+            exact = canonical_key_scores(qg, ck).astype(np.float64)                      # [KV, c]
+        else:
+            exact = np.einsum("grd,gcsd->grcs", qg, ck).max(axis=(1, 3))               # [KV, c]
         keep = _topk_sorted(exact, k)
         return with_neighbors(np.take_along_axis(cand, keep, axis=1))
     return with_neighbors(_topk_sorted(score, k))

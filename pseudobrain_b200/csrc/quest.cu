@@ -291,26 +291,130 @@ __device__ __forceinline__ void collect_in_order(KeyOf key_of, IdxOf idx_of, int
 constexpr int kCandCap = 4096;  // candidates held in shared memory
 constexpr int kSegCap = 4096;   // segment maxima held in shared memory (131072 pages)
 constexpr int kSegRegs = 16;    // candidate segments a warp keeps in registers per pass
+constexpr int kRefineRows = 64; // query rows per (group, key head) the refinement holds (the tensor-core limit)
+
+// Canonical page score: the maximum over a group's query rows r of
+//   fl( ... fl(fl(t_r0 + 0) + t_r1) ... + t_r127 ),  t_rd = q_rd * (q_rd > 0 ? kmax_d : kmin_d),
+// an fp32 sum in dimension order 0..127 (each product of two bf16 values is exact in fp32, so an
+// fma chain and a multiply-then-add chain agree bit for bit). The SIMT score, candidate and
+// rerank kernels produce it directly. The tensor-core scores differ from it by at most
+// c ||q_r||_1 max|bound| (the rounding of both sums); the top-k re-scores, in this order, every
+// page within twice that of its threshold, so every selection is exactly the selection of the
+// canonical scores, which a CPU restatement reproduces bit for bit.
+struct RefineArgs {
+  const bf16* q;             // null: the scores are canonical already (no refinement)
+  int64_t q_stride_n, q_stride_t, q_stride_h;
+  const bf16* kmax;
+  const bf16* kmin;
+  int64_t bnd_stride_kv, bnd_stride_p;
+  const float* tile_abs;     // [kv][abs_per_kv] largest |bound| per tile part (the score kernel's)
+  int abs_per_kv;
+  int kv, groups, t;
+};
+
+// Relative weight of the error bound: the fp32 rounding of a 256-term tensor-core sum and of
+// the 128-term canonical sum are each below 2^-15 ||q||_1 max|bound|; 2^-12 leaves a factor
+// of four on their sum.
+constexpr int kRefineEpsExp = -12;
+
+__device__ __forceinline__ float canonical_row_sum(const float* qrow, const bf16* bmax, const bf16* bmin) {
+  float acc = 0.f;
+#pragma unroll 2
+  for (int d0 = 0; d0 < kD; d0 += 8) {
+    float mx[8], mn[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmax + d0), mx);
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmin + d0), mn);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float qv = qrow[d0 + j];
+      acc = fmaf(qv, qv > 0.f ? mx[j] : mn[j], acc);
+    }
+  }
+  return acc;
+}
+
+__device__ __forceinline__ float ordered_key_inv(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 
 struct TopkSmem {
   SelectSmem ss;
-  uint32_t seg_key[kSegCap];  // ordered keys of the row's segment maxima
-  int32_t cseg[kSegCap];      // candidate segments, ascending
+  uint32_t seg_key[kSegCap];  // ordered keys of the row's segment maxima; then canonical keys
+  int32_t cseg[kSegCap];      // candidate segments, ascending; then the pages to re-score
   uint32_t cand_key[kCandCap];
   int32_t cand_idx[kCandCap];
+  float qs[kRefineRows][kD];  // the row's query rows (refinement)
+  float red[kTopkWarps];
+  float qs_l1[kTopkWarps];
+  float eps2;                 // twice the error bound of the row's scores
+  int n_unc;
 };
+
+// The refinement's set-up: the group's query rows into shared memory and eps2 = 2 eps,
+// eps = 2^kRefineEpsExp max_r ||q_r||_1 max|bound| over the key head's tiles.
+__device__ __forceinline__ void refine_setup(const RefineArgs& rf, int row, TopkSmem& ts) {
+  const int n = row / rf.kv, h = row % rf.kv, rpg = rf.t * rf.groups;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < rpg * kD; e += kTopkThreads) {
+    const int r = e / kD, dd = e % kD, ti = r / rf.groups, g = r % rf.groups;
+    ts.qs[r][dd] = __bfloat162float(rf.q[n * rf.q_stride_n + ti * rf.q_stride_t +
+                                         (int64_t)(h * rf.groups + g) * rf.q_stride_h + dd]);
+  }
+  float babs = 0.f;
+  for (int i = threadIdx.x; i < rf.abs_per_kv; i += kTopkThreads)
+    babs = fmaxf(babs, rf.tile_abs[(int64_t)h * rf.abs_per_kv + i]);
+  __syncthreads();
+  // this warp's largest ||q_r||_1 times the largest bound magnitude it read; the max over
+  // warps of both is taken apart (a product of maxima, not a max of products)
+  float l1 = 0.f;
+  for (int r = warp; r < rpg; r += kTopkWarps) {
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < kD / 32; ++j) a += fabsf(ts.qs[r][lane + 32 * j]);
+    l1 = fmaxf(l1, warp_sum(a));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) babs = fmaxf(babs, __shfl_xor_sync(0xffffffffu, babs, o));
+  if (lane == 0) {
+    ts.red[warp] = babs;
+    ts.qs_l1[warp] = l1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float bm = 0.f, lm = 0.f;
+    for (int w = 0; w < kTopkWarps; ++w) bm = fmaxf(bm, ts.red[w]), lm = fmaxf(lm, ts.qs_l1[w]);
+    // an fp32 sum of 128 magnitudes may round below the exact sum: 2^-20 relative covers it;
+    // the other steps round up, so eps2 is a bound, not an estimate
+    lm = __fmul_ru(lm, 1.f + 0x1p-20f);
+    ts.eps2 = __fmul_ru(2.f, ldexpf(__fmul_ru(lm, bm), kRefineEpsExp));
+  }
+  __syncthreads();
+}
+
+// Band of the tensor-core keys around the threshold key `prefix`: pages above hi are in the
+// canonical top k whatever their rounding, pages below lo are out; the band in between is
+// re-scored. -inf scores (masked pages) are exact and stay as they are.
+__device__ __forceinline__ void refine_band(uint32_t prefix, float eps2, uint32_t& lo, uint32_t& hi) {
+  const float tau = ordered_key_inv(prefix);
+  hi = ordered_key(__fadd_ru(tau, eps2));
+  lo = ordered_key(__fadd_rd(tau, -eps2));
+}
 
 // One CTA per (group, key head) row of scores. With segment maxima (the max of every 32
 // consecutive pages), the k-th largest segment maximum bounds the k-th largest page score
 // from below (the top k segments hold k distinct pages scoring at least that), and so does
-// any tau below it (here: its top 22 bits), so the top k are among the pages scoring >= tau,
-// all inside segments whose maximum is >= tau. Those
+// any tau below it (here: its top 22 bits, less the refinement band), so the top k are
+// among the pages scoring >= tau, all inside segments whose maximum is >= tau. Those
 // segments are listed in index order, only their pages are read (one warp-wide load per
 // segment, in registers), the pages scoring >= tau are placed in index order into shared
 // memory, and the exact selection runs there. When there are too few segments, too many
 // segments or too many candidates, the selection runs over the whole row.
+// With rf.q set (tensor-core scores), the pages within the error band of the threshold get
+// their canonical scores and the final selection runs on keys: MAX for the pages above the
+// band, the canonical key inside it, 0 below it (n above < k <= n above + n inside).
 __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* scores, const float* segmax, int npages,
-                                                                  int nseg, int k, int32_t* pages) {
+                                                                  int nseg, int k, int32_t* pages,
+                                                                  const RefineArgs rf) {
   extern __shared__ __align__(16) uint8_t topk_raw[];
   TopkSmem& ts = *reinterpret_cast<TopkSmem*>(topk_raw);
   SelectSmem& ss = ts.ss;
@@ -318,15 +422,24 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
   const float* s = scores + (int64_t)row * npages;
   int32_t* out = pages + (int64_t)row * k;
   const uint32_t lt = (1u << lane) - 1u;
+  const bool refine = rf.q != nullptr;
+  const int rh = refine ? row % rf.kv : 0, rpg = refine ? rf.t * rf.groups : 0;
+  if (refine) refine_setup(rf, row, ts);
+  const float eps2 = refine ? ts.eps2 : 0.f;
   uint32_t prefix, kk;
   if (segmax != nullptr && nseg >= k && nseg <= kSegCap) {
     const float* sg = segmax + (int64_t)row * nseg;
     for (int i = threadIdx.x; i < nseg; i += kTopkThreads) ts.seg_key[i] = ordered_key(sg[i]);
     __syncthreads();
     // tau: a lower bound of the k-th largest segment maximum (two digits: any bound at or
-    // below it keeps every top-k page among the candidates, the exact select comes later)
+    // below it keeps every top-k page among the candidates, the exact select comes later),
+    // lowered by the refinement band so the band's pages are candidates too
     uint32_t tau, unused;
     radix_select([&](int i) { return ts.seg_key[i]; }, nseg, (uint32_t)k, ss, tau, unused, 2);
+    if (refine) {
+      const float t0 = ordered_key_inv(tau);
+      if (t0 != -INFINITY) tau = ordered_key(__fadd_rd(t0, -eps2));
+    }
     // candidate segments (key >= tau) in index order
     {
       const int R = warp_range(nseg);
@@ -389,6 +502,34 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
         }
         __syncthreads();
         radix_select([&](int i) { return ts.cand_key[i]; }, ptotal, (uint32_t)k, ss, prefix, kk);
+        if (refine) {
+          // the band's pages: listed (any order), re-scored per (page, query row), written back
+          uint32_t lo, hi;
+          refine_band(prefix, eps2, lo, hi);
+          const uint32_t ninf = ordered_key(-INFINITY);
+          if (threadIdx.x == 0) ts.n_unc = 0;
+          __syncthreads();
+          for (int i = threadIdx.x; i < ptotal; i += kTopkThreads) {
+            const uint32_t key = ts.cand_key[i];
+            if (key == ninf) continue;  // masked: exact already
+            if (key > hi) ts.cand_key[i] = 0xFFFFFFFFu;
+            else if (key >= lo) ts.cseg[atomicAdd(&ts.n_unc, 1)] = i;
+            else ts.cand_key[i] = 0u;
+          }
+          __syncthreads();
+          const int nu = ts.n_unc;
+          for (int u = threadIdx.x; u < nu; u += kTopkThreads) ts.seg_key[u] = 0u;
+          __syncthreads();
+          for (int w = threadIdx.x; w < nu * rpg; w += kTopkThreads) {
+            const int u = w / rpg, r = w % rpg, page = ts.cand_idx[ts.cseg[u]];
+            const int64_t off = rh * rf.bnd_stride_kv + (int64_t)page * rf.bnd_stride_p;
+            atomicMax(&ts.seg_key[u], ordered_key(canonical_row_sum(ts.qs[r], rf.kmax + off, rf.kmin + off)));
+          }
+          __syncthreads();
+          for (int u = threadIdx.x; u < nu; u += kTopkThreads) ts.cand_key[ts.cseg[u]] = ts.seg_key[u];
+          __syncthreads();
+          radix_select([&](int i) { return ts.cand_key[i]; }, ptotal, (uint32_t)k, ss, prefix, kk);
+        }
         collect_in_order([&](int i) { return ts.cand_key[i]; }, [&](int i) { return ts.cand_idx[i]; }, ptotal,
                          prefix, kk, ss, out);
         return;
@@ -396,6 +537,25 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
     }
   }
   radix_select([&](int i) { return ordered_key(s[i]); }, npages, (uint32_t)k, ss, prefix, kk);
+  if (refine) {
+    // whole row: the band's canonical keys are computed where they are read (rare path)
+    uint32_t lo, hi;
+    refine_band(prefix, eps2, lo, hi);
+    const uint32_t ninf = ordered_key(-INFINITY);
+    auto key2 = [&](int i) -> uint32_t {
+      const uint32_t key = ordered_key(s[i]);
+      if (key == ninf) return key;
+      if (key > hi) return 0xFFFFFFFFu;
+      if (key < lo) return 0u;
+      const int64_t off = rh * rf.bnd_stride_kv + (int64_t)i * rf.bnd_stride_p;
+      float best = -INFINITY;
+      for (int r = 0; r < rpg; ++r) best = fmaxf(best, canonical_row_sum(ts.qs[r], rf.kmax + off, rf.kmin + off));
+      return ordered_key(best);
+    };
+    radix_select(key2, npages, (uint32_t)k, ss, prefix, kk);
+    collect_in_order(key2, [&](int i) { return i; }, npages, prefix, kk, ss, out);
+    return;
+  }
   collect_in_order([&](int i) { return ordered_key(s[i]); }, [&](int i) { return i; }, npages, prefix, kk, ss, out);
 }
 
@@ -1081,12 +1241,39 @@ int quest_nseg(const pbk_quest_desc& d) {
   const int npages = d.n_arch / d.page;
   return npages >= kSegMinPages ? (npages + 31) / 32 : 0;
 }
+// Largest bound magnitude per (key head, 128-page tile), written by the tensor-core score
+// kernel for the top-k's refinement.
+size_t quest_tile_abs_floats(const pbk_quest_desc& d) {
+  return quest_score_tc_supported(d) ? (size_t)d.kv * quest_score_tc_tiles(d) * quest_score_tc_abs_slots() : 0;
+}
 // Scratch of one select call, in floats: the scores (unless the caller keeps them in
-// desc.scores), then the segment maxima.
+// desc.scores), then the segment maxima, then the tile bound magnitudes.
 size_t quest_select_floats(const pbk_quest_desc& d) {
   const size_t rows = (size_t)d.nq * d.kv;
-  return (d.scores ? 0 : rows * (d.n_arch / d.page)) + rows * quest_nseg(d);
+  return (d.scores ? 0 : rows * (d.n_arch / d.page)) + rows * quest_nseg(d) + quest_tile_abs_floats(d);
 }
+
+namespace {
+// The top-k's refinement arguments for scores of desc `d` (tile_abs null: canonical scores).
+RefineArgs refine_args(const pbk_quest_desc& d, const float* tile_abs) {
+  RefineArgs r{};
+  if (tile_abs == nullptr) return r;
+  r.q = static_cast<const bf16*>(d.q);
+  r.q_stride_n = d.q_stride_n;
+  r.q_stride_t = d.q_stride_t;
+  r.q_stride_h = d.q_stride_h;
+  r.kmax = static_cast<const bf16*>(d.kmax);
+  r.kmin = static_cast<const bf16*>(d.kmin);
+  r.bnd_stride_kv = d.bnd_stride_kv;
+  r.bnd_stride_p = d.bnd_stride_p;
+  r.tile_abs = tile_abs;
+  r.abs_per_kv = quest_score_tc_tiles(d) * quest_score_tc_abs_slots();
+  r.kv = d.kv;
+  r.groups = d.h / d.kv;
+  r.t = d.t;
+  return r;
+}
+}  // namespace
 size_t quest_score_bytes(const pbk_quest_desc& d) { return quest_select_floats(d) * sizeof(float); }
 size_t quest_partial_bytes(const pbk_quest_desc& d, int n_sink) {
   return (size_t)d.nq * d.t * d.h * quest_splits(d, n_sink) * (kD + 2) * sizeof(float);
@@ -1103,11 +1290,13 @@ cudaError_t launch_quest_select_parts(const pbk_quest_desc& d, float* scratch, i
   if (npages == 0 || k == 0) return cudaSuccess;
   float* scores = d.scores ? d.scores : scratch;
   const int nseg = quest_nseg(d);
-  float* segmax = nseg ? scratch + (d.scores ? 0 : (size_t)d.nq * d.kv * npages) : nullptr;
+  float* after_scores = scratch + (d.scores ? 0 : (size_t)d.nq * d.kv * npages);
+  float* segmax = nseg ? after_scores : nullptr;
+  float* tile_abs = quest_score_tc_supported(d) ? after_scores + (size_t)d.nq * d.kv * nseg : nullptr;
   if (!(parts & 1)) {
   } else if (quest_score_tc_supported(d)) {
     // Up to 64 query rows per key head: tensor-core scores (tcgen05, TMA-fed).
-    cudaError_t e = launch_quest_score_tc(d, scores, segmax, nseg, st);
+    cudaError_t e = launch_quest_score_tc(d, scores, segmax, nseg, tile_abs, st);
     if (e != cudaSuccess) return e;
   } else {
     const int rows = d.nq * d.t * (d.h / d.kv);
@@ -1125,7 +1314,8 @@ cudaError_t launch_quest_select_parts(const pbk_quest_desc& d, float* scratch, i
                                          (int)sizeof(TopkSmem));
     if (e != cudaSuccess) return e;
   }
-  quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, sizeof(TopkSmem), st>>>(scores, segmax, npages, nseg, k, d.pages);
+  quest_topk_kernel<<<d.nq * d.kv, kTopkThreads, sizeof(TopkSmem), st>>>(scores, segmax, npages, nseg, k, d.pages,
+                                                                          refine_args(d, tile_abs));
   return cudaGetLastError();
 }
 
@@ -1196,7 +1386,8 @@ cudaError_t launch_quest_rerank(const pbk_quest_desc& d, const int32_t* cand, in
   cudaError_t e = cudaFuncSetAttribute(quest_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sizeof(TopkSmem));
   if (e != cudaSuccess) return e;
-  quest_topk_kernel<<<nrows, kTopkThreads, sizeof(TopkSmem), st>>>(exact, nullptr, c, 0, k, d.pages);
+  quest_topk_kernel<<<nrows, kTopkThreads, sizeof(TopkSmem), st>>>(exact, nullptr, c, 0, k, d.pages,
+                                                                    RefineArgs{});  // canonical rerank scores
   quest_map_kernel<<<(nrows * k + 255) / 256, 256, 0, st>>>(cand, c, k, nrows, d.pages);
   return cudaGetLastError();
 }
@@ -1241,11 +1432,12 @@ pbk_quest_desc superblock_desc(const pbk_quest_desc& d, const pbk_quest_levels& 
   return ds;
 }
 
-cudaError_t launch_topk(const float* scores, int npages, int k, int nrows, int32_t* pages, cudaStream_t st) {
+cudaError_t launch_topk(const float* scores, int npages, int k, int nrows, int32_t* pages, const RefineArgs& rf,
+                        cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(quest_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sizeof(TopkSmem));
   if (e != cudaSuccess) return e;
-  quest_topk_kernel<<<nrows, kTopkThreads, sizeof(TopkSmem), st>>>(scores, nullptr, npages, 0, k, pages);
+  quest_topk_kernel<<<nrows, kTopkThreads, sizeof(TopkSmem), st>>>(scores, nullptr, npages, 0, k, pages, rf);
   return cudaGetLastError();
 }
 }  // namespace
@@ -1253,10 +1445,10 @@ cudaError_t launch_topk(const float* scores, int npages, int k, int nrows, int32
 size_t quest_levels_bytes(const pbk_quest_desc& d, const pbk_quest_levels& lv) {
   const size_t rows = (size_t)d.nq * d.kv;
   const int full = d.n_arch / d.page;
-  if (lv.smax == nullptr) {  // scores, then the segment maxima of the score pass
+  if (lv.smax == nullptr) {  // scores, then the segment maxima and tile bound magnitudes of the score pass
     pbk_quest_desc dd = d;
-    dd.scores = nullptr;
-    return round_ws(rows * full * sizeof(float)) + round_ws(rows * quest_nseg(dd) * sizeof(float));
+    dd.scores = reinterpret_cast<float*>(16);  // kept apart: the scratch holds the rest
+    return round_ws(rows * full * sizeof(float)) + round_ws(quest_select_floats(dd) * sizeof(float));
   }
   const pbk_quest_desc ds = superblock_desc(d, lv, nullptr);
   const size_t nc = (size_t)lv.m_sb * lv.sblk;
@@ -1280,7 +1472,9 @@ cudaError_t launch_quest_select_levels(const pbk_quest_desc& d, const pbk_quest_
       const int64_t n = (int64_t)nrows * (hi - lo);
       quest_hole_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(scores, full, nrows, lo, hi);
     }
-    return launch_topk(scores, full, k, nrows, d.pages, st);  // segment maxima may hold hole pages: not used
+    // segment maxima may hold hole pages: not used; the tile bound magnitudes follow them
+    const float* tile_abs = quest_score_tc_supported(dd) ? segmax + (size_t)nrows * quest_nseg(dd) : nullptr;
+    return launch_topk(scores, full, k, nrows, d.pages, refine_args(dd, tile_abs), st);
   }
   const int nc = lv.m_sb * lv.sblk, k2 = min(k, nc);
   const pbk_quest_desc probe = superblock_desc(d, lv, nullptr);
@@ -1296,7 +1490,7 @@ cudaError_t launch_quest_select_levels(const pbk_quest_desc& d, const pbk_quest_
   if (e != cudaSuccess) return e;
   quest_sub_score_kernel<<<dim3((nc + kScoreThreads - 1) / kScoreThreads, nrows), kScoreThreads, 0, st>>>(
       d, top_sb, lv.m_sb, lv.sblk, full, lv.hole_lo, lv.hole_hi, sub, cand);
-  e = launch_topk(sub, nc, k2, nrows, d.pages, st);
+  e = launch_topk(sub, nc, k2, nrows, d.pages, RefineArgs{}, st);  // canonical candidate scores
   if (e != cudaSuccess) return e;
   quest_map_kernel<<<(nrows * k2 + 255) / 256, 256, 0, st>>>(cand, nc, k2, nrows, d.pages);
   return cudaGetLastError();

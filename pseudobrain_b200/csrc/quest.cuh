@@ -21,14 +21,20 @@ int quest_splits(const pbk_quest_desc& d, int n_sink);
 size_t quest_score_bytes(const pbk_quest_desc& d);
 size_t quest_select_floats(const pbk_quest_desc& d);
 // Floats of the fixed scratch of pbk_quest_select_noalloc: the largest allowed score count
-// plus its segment maxima (rows of at least 1024 pages keep ceil(pages / 32) of them).
+// plus its segment maxima (rows of at least 1024 pages keep ceil(pages / 32) of them) and
+// the tile bound magnitudes (one per 128 pages and key head: at most scores / 64 for rows
+// of at least 128 pages).
 constexpr size_t kNoAllocFloats = (size_t)PBK_QUEST_NOALLOC_MAX_SCORES + PBK_QUEST_NOALLOC_MAX_SCORES / 32 +
-                                  PBK_QUEST_NOALLOC_MAX_SCORES / 1024;
+                                  PBK_QUEST_NOALLOC_MAX_SCORES / 1024 + PBK_QUEST_NOALLOC_MAX_SCORES / 64;
 size_t quest_partial_bytes(const pbk_quest_desc& d, int n_sink);
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st);
 cudaError_t launch_quest_select_parts(const pbk_quest_desc& d, float* scratch, int parts, cudaStream_t st);
 bool quest_score_tc_supported(const pbk_quest_desc& d);
-cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float* segmax, int nseg, cudaStream_t st);
+// Tiles of 128 pages per key head and values per tile in the score kernel's tile_abs output.
+int quest_score_tc_tiles(const pbk_quest_desc& d);
+int quest_score_tc_abs_slots();
+cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float* segmax, int nseg, float* tile_abs,
+                                  cudaStream_t st);
 cudaError_t launch_quest_select_noalloc(const pbk_quest_desc& d, cudaStream_t st);
 // parts (bit mask): 1 the retrieved splits, 2 the window splits, 4 the combine (all: 7).
 cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const SinkKeys& sk, int parts, cudaStream_t st);

@@ -14,6 +14,11 @@
 //   warps 2-9: two epilogue warpgroups, one per TMEM accumulator buffer (even / odd
 //              tiles): read D from TMEM, reduce per query group and store the scores; the
 //              group that meets a key head's first tile builds B for it.
+//   warp 10: the tile's largest bound magnitude max |kmax|, |kmin| (read from the staged
+//              tile in shared memory) into tile_abs. It bounds the
+//              rounding error of the tensor-core sums, |D - exact| <= c ||q||_1 max|bound|,
+//              which the top-k uses to re-score the pages near its threshold in the
+//              canonical order (quest.cu), so the selection is bit-exact.
 // Every mbarrier wait is bounded: on timeout the kernel records an error code in the
 // library's device error word and winds down (waiting, bounded, for its own loads and
 // MMAs), frees its TMEM and returns.
@@ -32,7 +37,8 @@ constexpr int kMaxRows = 64;                    // query rows per key head = MMA
 constexpr int kAtomBytes = kTileP * 128;        // [128 rows x 64 bf16] swizzled atom
 constexpr int kStageBytes = 4 * kAtomBytes;     // kmax d0-63 | kmax d64-127 | kmin d0-63 | kmin d64-127
 constexpr int kBAtomBytes = kMaxRows * 128;
-constexpr int kThreads = 320;
+constexpr int kAbsWarps = 1;                    // warp 10: bound magnitude of each tile
+constexpr int kThreads = 320 + 32 * kAbsWarps;
 constexpr int kTmemCols = 2 * kMaxRows;         // two accumulator buffers
 
 struct __align__(1024) ScoreSmem {
@@ -48,6 +54,7 @@ struct ScoreArgs {
   int64_t q_stride_n, q_stride_t, q_stride_h;
   float* scores;
   float* segmax;  // max of every 32 consecutive pages per (group, key head), or null
+  float* tile_abs;  // [kv * tiles_per_kv] largest |bound| of each tile, or null
   int nseg;
   int* err;
   int nq, t, groups, kv, npages, rows, n_pad, tiles_per_kv, total_tiles;
@@ -111,7 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(&sm.full[s], 1);
-      tc::mbar_init(&sm.empty[s], 1);
+      // the MMA commit, plus one arrival per bound-magnitude warp once it has read the stage
+      tc::mbar_init(&sm.empty[s], 1 + (args.tile_abs != nullptr ? kAbsWarps : 0));
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&sm.acc_full[b], 1);
@@ -189,6 +197,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Our MMAs must complete before TMEM is freed (bounded).
       if (issued > 0 && !tc::mbar_wait(&sm.acc_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, 200000000ull))
         record_error(args.err, 6, sm);
+    }
+  } else if (warp >= 10) {
+    // ---------------- bound magnitudes: warp 10 reads every stage once ----------------
+    // |x| of a bf16 is its bit pattern with the sign cleared, and for non-NaN values the
+    // order of those patterns as unsigned integers is the order of |x|: a packed 16-bit
+    // integer max over the staged bytes (their swizzled order does not matter).
+    if (args.tile_abs != nullptr) {
+      const int aw = warp - 10;
+      for (int i = 0; i < ntiles; ++i) {
+        if (__any_sync(0xffffffffu, sm.abort)) break;  // warp-uniform exit
+        const int s = i % kStages;
+        const bool ok = tc::mbar_wait(&sm.full[s], (i / kStages) & 1);
+        if (!__all_sync(0xffffffffu, ok)) {
+          record_error(args.err, 9, sm);
+          break;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(sm.a[s] + aw * (kStageBytes / kAbsWarps));
+        uint32_t m0 = 0, m1 = 0;
+#pragma unroll 8
+        for (int j = lane; j < kStageBytes / kAbsWarps / 16; j += 32) {
+          const uint4 x = src[j];
+          m0 = __vmaxu2(m0, x.x & 0x7fff7fffu);
+          m1 = __vmaxu2(m1, x.y & 0x7fff7fffu);
+          m0 = __vmaxu2(m0, x.z & 0x7fff7fffu);
+          m1 = __vmaxu2(m1, x.w & 0x7fff7fffu);
+        }
+        const uint32_t m2 = __vmaxu2(m0, m1);
+        uint32_t m = __reduce_max_sync(0xffffffffu, max(m2 & 0xffffu, m2 >> 16));
+        m = min(m, 0x7f80u);  // NaN patterns count as +inf
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&sm.empty[s]);  // this warp is done with the stage
+          args.tile_abs[(int64_t)(t_begin + i) * kAbsWarps + aw] = __uint_as_float(m << 16);  // bf16 -> fp32
+        }
+      }
     }
   } else {
     // ---------------- epilogue: warps 2..9, group eg takes tiles i = eg, eg + 2, ... ----------------
@@ -277,7 +320,11 @@ bool quest_score_tc_supported(const pbk_quest_desc& d) {
   return rows <= kMaxRows && d.n_arch / d.page > 0;
 }
 
-cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float* segmax, int nseg, cudaStream_t st) {
+int quest_score_tc_tiles(const pbk_quest_desc& d) { return (d.n_arch / d.page + kTileP - 1) / kTileP; }
+int quest_score_tc_abs_slots() { return kAbsWarps; }
+
+cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float* segmax, int nseg, float* tile_abs,
+                                  cudaStream_t st) {
   const int npages = d.n_arch / d.page;
   CUtensorMap tmax, tmin;
   const uint64_t dims[3] = {128, (uint64_t)npages, (uint64_t)d.kv};
@@ -293,6 +340,7 @@ cudaError_t launch_quest_score_tc(const pbk_quest_desc& d, float* scores, float*
   a.q_stride_h = d.q_stride_h;
   a.scores = scores;
   a.segmax = segmax;
+  a.tile_abs = tile_abs;
   a.nseg = nseg;
   a.err = device_error_word();
   a.nq = d.nq;

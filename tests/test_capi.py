@@ -92,3 +92,20 @@ def test_every_module_imports(lib):
     import importlib
     for m in ("gated_deltanet", "gdn_prefill", "exact_memory", "transplant", "serving", "sharding", "synthetic"):
         importlib.import_module(f"pseudobrain_b200.{m}")
+
+
+def test_noalloc_select_too_large_when_scores_are_given(lib):
+    """With desc->scores given, only the segment and tile maxima go to the fixed array; a
+    problem whose maxima alone exceed it returns PBK_ERR_TOO_LARGE on the host, before any
+    device call (the pointers below are never dereferenced)."""
+    from pseudobrain_b200 import _capi
+    d = _capi.PbkQuestDesc()
+    d.nq, d.t, d.h, d.kv, d.d, d.page = 64, 1, 64, 64, 128, 16
+    d.n_arch, d.budget = 65536 * 16, 256  # 64 x 64 rows of 65536 pages: 8.4M segment maxima
+    fake = 1 << 20                         # 16-byte aligned, never read
+    d.q = d.kmax = d.kmin = fake
+    d.pages = fake
+    d.scores = fake
+    d.q_stride_n, d.q_stride_t, d.q_stride_h = 64 * 128, 64 * 128, 128
+    d.bnd_stride_kv, d.bnd_stride_p = 65536 * 128, 128
+    assert _capi.LIB.pbk_quest_select_noalloc(ctypes.byref(d), None) == _capi.PBK_ERR_TOO_LARGE

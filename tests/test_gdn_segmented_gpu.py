@@ -93,3 +93,29 @@ def test_segmented_long_sequence(cuda_device):
     assert ogdn.rel_err(o.float().cpu().numpy(), o1.float().cpu().numpy()) < TOL_BF16
     assert ogdn.rel_err(s.cpu().numpy(), s1.cpu().numpy()) < TOL_BF16
     assert _capi.device_error() == 0
+
+
+def test_segmented_config4_length_matches_oracle(cuda_device):
+    """The config-4 GDN shard of one GPU of 8 (2 key / 4 value heads) over T = 262144 + 100
+    tokens, split into segments by auto_segments, against the oracle (the reference's
+    algorithm on the host, fp32, the whole sequence in order) with a slow decay, so the
+    state carries across every segment boundary. Relative errors printed."""
+    from oracle import cpu_reference as cr
+    from pseudobrain_b200 import _capi
+    from pseudobrain_b200.gdn_prefill import auto_segments, gdn_prefill_segmented
+    t = 262144 + 100
+    inp = _slow_inputs(21, 1, t, 2, 4)
+    d = to_device(inp, cuda_device)
+    args = [d[n] for n in ("q", "k", "v", "g", "beta")]
+    segs = auto_segments(1, 4, t)
+    assert segs > 1
+    o, s = gdn_prefill_segmented(*args, inp["scale"], d["h0"], out_dtype=torch.bfloat16)
+    cr.use_all_cores()
+    hq = {n: torch.from_numpy(inp[n]) for n in ("q", "k", "v", "g", "beta", "h0")}
+    ro, rs = cr.chunked_prefill(hq["q"].repeat_interleave(2, dim=2), hq["k"].repeat_interleave(2, dim=2), hq["v"],
+                                hq["g"], hq["beta"], inp["scale"], hq["h0"])
+    eo = ogdn.rel_err(o.float().cpu().numpy(), ro.numpy())
+    es = ogdn.rel_err(s.cpu().numpy(), rs.numpy())
+    print(f"[segmented prefill, T={t}, {segs} segments vs oracle] rel err o {eo:.2e}, final state {es:.2e}")
+    assert eo < TOL_BF16 and es < TOL_BF16
+    assert _capi.device_error() == 0

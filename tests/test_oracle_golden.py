@@ -285,3 +285,83 @@ def test_archive_write_matches_reference():
         assert np.array_equal(getattr(arc, name)[:, :n], f[name][:, :n]), name
     for name, n in (("bmean_k", nb), ("bmean_v", nb), ("smean_k", nsb), ("smean_v", nsb)):
         assert np.allclose(getattr(arc, name)[:, :n], f[name][:, :n], rtol=0, atol=1e-6), name
+
+
+def test_canonical_scores_follow_the_fixed_order():
+    """canonical_bound_scores equals a scalar fp32 loop over d = 0..127 (each product exact,
+    each addition rounded), row by row, and stays within fp32 summation error of the fp64
+    bound scores."""
+    rng = np.random.default_rng(9)
+    q = oq.bf16_round(rng.standard_normal((2, 3, 128)).astype(np.float32))
+    kmax = oq.bf16_round(rng.standard_normal((2, 5, 128)).astype(np.float32) * 3)
+    kmin = oq.bf16_round(kmax - np.abs(rng.standard_normal((2, 5, 128))).astype(np.float32))
+    got = oq.canonical_bound_scores(q, kmax, kmin)
+    for h in range(2):
+        for p in range(5):
+            best = np.float32(-np.inf)
+            for r in range(3):
+                acc = np.float32(0)
+                for d in range(128):
+                    qd = q[h, r, d]
+                    acc = np.float32(acc + np.float32(qd * (kmax[h, p, d] if qd > 0 else kmin[h, p, d])))
+                best = max(best, acc)
+            assert got[h, p] == best
+    ref = oq._bound_scores(q, kmax, kmin)
+    assert np.allclose(got, ref, rtol=1e-5, atol=1e-5)
+    cand = np.array([[0, 2], [1, 4]])
+    keys = oq.bf16_round(rng.standard_normal((2, 5 * 4, 128)).astype(np.float32))
+    ex = oq.canonical_rerank_scores(q, keys, cand, 4)
+    for h in range(2):
+        for c in range(2):
+            best = np.float32(-np.inf)
+            for r in range(3):
+                for s in range(4):
+                    acc = np.float32(0)
+                    for d in range(128):
+                        acc = np.float32(acc + np.float32(q[h, r, d] * keys[h, cand[h, c] * 4 + s, d]))
+                    best = max(best, acc)
+            assert ex[h, c] == best
+
+
+@pytest.mark.parametrize("case", ["t1", "t3"])
+def test_canonical_selection_equals_reference_selection(quest, case):
+    """On the reference's golden retrieval the canonical-order selection picks the same pages
+    as the reference's own (GEMM-order) scores: no near-tie decides these cases."""
+    f, arc, _, _ = quest
+    page, budget, groups = (int(f[x]) for x in ("page", "budget", "groups"))
+    full = arc.length // page
+    s = oq.canonical_page_scores(_f32(f[f"{case}_q"]), arc.kmax[:, :, :full], arc.kmin[:, :, :full], groups)
+    assert np.array_equal(oq.select_pages(s, budget), f[f"{case}_top"])
+
+
+@pytest.mark.parametrize("case", list(LEVEL_CASES))
+def test_canonical_retrieve_modes_equal_reference(levels, case):
+    """The two-level, rerank, neighbour and prompt modes in the canonical order pick the
+    reference's pages on its golden cases."""
+    f = levels
+    page, budget, groups, sblk = (int(f[x]) for x in ("page", "budget", "groups", "sblk"))
+    opt = LEVEL_CASES[case]
+    prompt = f[f"{opt['prompt']}_top"] if "prompt" in opt else None
+    _, _, top = oq.retrieve_modes(_f32(f["keys"]), _f32(f["values"]), _f32(f["kmax"]), _f32(f["kmin"]),
+                                  _f32(f[f"{case}_q"]), groups, page, budget, superblock=sblk,
+                                  rerank=opt.get("rerank", 0), neighbors=opt.get("neighbors", 0), prompt_top=prompt,
+                                  canonical=True)
+    assert np.array_equal(top, f[f"{case}_top"])
+
+
+@pytest.mark.parametrize("case", ["s_sb", "s_sb_hole", "s_sb_nb", "s_flat_hole", "s_rerank_hole"])
+def test_canonical_serving_levels_equal_reference(levels, case):
+    from oracle import serving as osv
+    f = levels
+    page, sblk, groups = int(f["page"]), int(f["sblk"]), int(f["groups"])
+    kmax, kmin = _f32(f["s_kmax"]), _f32(f["s_kmin"])
+    smax, smin = osv.super_bounds(kmax, kmin, kmax.shape[1], sblk)
+    keys = _f32(f["s_keys"])
+    mem = dict(blocks=8, decode_blocks=8, rerank=int(f[f"{case}_pool"]), block_size=page, window=64,
+               neighbors=int(f[f"{case}_neighbors"]))
+    use_sb = not int(f[f"{case}_nosb"])
+    top = osv.retrieve_blocks(keys, kmax, kmin, _f32(f[f"{case}_q"]), groups, int(f["s_limit"]),
+                              bool(f[f"{case}_rerank"]), mem, keys.shape[1], smax if use_sb else None,
+                              smin if use_sb else None, sblk, tuple(int(x) for x in f[f"{case}_hole"]),
+                              canonical=True)
+    assert np.array_equal(top, f[f"{case}_top"])

@@ -77,8 +77,8 @@ def test_matches_oracle(cuda_device, memory_settings, t, rerank):
     top = S.retrieve_blocks(arc, q, groups, limit, rerank)
     kmax = arc.kmax.float().cpu().numpy()
     kmin = arc.kmin.float().cpu().numpy()
-    want = osv.retrieve_blocks(keys, kmax, kmin, q_np, groups, limit, rerank, mem, cap)
-    assert np.array_equal(top.cpu().numpy(), want)
+    want = osv.retrieve_blocks(keys, kmax, kmin, q_np, groups, limit, rerank, mem, cap, canonical=True)
+    assert np.array_equal(top.cpu().numpy(), want)  # canonical-order scores: bit-exact
     out = S.piece_attention(arc, q, torch.from_numpy(q_pos).to(cuda_device), top, groups, 512, d ** -0.5)
     assert out.dtype == torch.bfloat16
     ref = osv.piece_attention(keys, values, q_np, q_pos, want, groups, 512, d ** -0.5, block)

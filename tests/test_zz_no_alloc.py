@@ -20,10 +20,10 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _problem(seed, nq, kv, heads, npages, page, budget, device):
+def _problem(seed, nq, kv, heads, npages, page, budget, device, t=1):
     from pseudobrain_b200 import exact_memory as M
     gen = torch.Generator(device=device).manual_seed(seed)
-    q = torch.randn(nq, 1, heads, 128, generator=gen, device=device).to(torch.bfloat16)
+    q = torch.randn(nq, t, heads, 128, generator=gen, device=device).to(torch.bfloat16)
     a = torch.randn(kv, npages, 128, generator=gen, device=device)
     b = torch.randn(kv, npages, 128, generator=gen, device=device)
     kmax, kmin = torch.maximum(a, b).to(torch.bfloat16), torch.minimum(a, b).to(torch.bfloat16)
@@ -62,6 +62,20 @@ def test_noalloc_select_matches_workspace_select_on_consecutive_calls(cuda_devic
         assert torch.equal(pages, expected)
         assert bool((pages >= 0).all())
         # the same call again gives the same pages
+        pages.fill_(-1)
+        _select_noalloc(desc, cuda_device)
+        torch.cuda.synchronize()
+        assert torch.equal(pages, expected)
+
+
+def test_noalloc_select_matches_on_the_simt_score_path(cuda_device):
+    """More than 64 query rows per key head (3 groups x 6 tokens x 16 query heads over one key
+    head: 288 rows) take the SIMT score kernel instead of the tensor-core one; the array then
+    holds its scores and segment maxima without tile bound magnitudes."""
+    q, kmax, kmin, pages, desc = _problem(14, 3, 1, 16, 4100, 16, 33, cuda_device, t=6)
+    _select_with_workspace(desc, cuda_device)
+    expected = pages.clone()
+    for _ in range(2):
         pages.fill_(-1)
         _select_noalloc(desc, cuda_device)
         torch.cuda.synchronize()
