@@ -140,6 +140,41 @@ PBK_API int pbk_device_error(int* code, int clear);
  * g/beta bf16 or fp32; o bf16 or fp32. */
 PBK_API int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream);
 
+/* What vLLM's decode ops add around pbk_gdn_decode's recurrence, for pbk_gdn_decode_ext:
+ * vllm/model_executor/layers/fla/ops/fused_recurrent.py:256-336
+ * (fused_recurrent_gated_delta_rule_packed_decode), :20-170 (fused_recurrent_gated_delta_rule)
+ * and fused_sigmoid_gating.py:24-180 (fused_sigmoid_gating_delta_rule_update). */
+typedef struct pbk_decode_ext {
+  int32_t gating;            /* 1: g = -exp(A_log) softplus(a + dt_bias) and beta = sigmoid(b) per token and
+                                value head (desc->g and desc->beta are not read); 0: desc->g, desc->beta */
+  int32_t beta_round;        /* 1: sigmoid(b) is rounded to b's dtype before use (the packed decode) */
+  float softplus_beta;       /* softplus(x) = log(1 + exp(sb x)) / sb while sb x <= threshold, else x */
+  float softplus_threshold;  /* (vLLM: sb = 1, threshold = 20) */
+  pbk_view a, b;             /* [B, T, Hv] raw gate inputs (gating = 1) */
+  const void* a_log;         /* [Hv] */
+  const void* dt_bias;       /* [Hv] */
+  int32_t a_log_dtype, dt_bias_dtype;
+  int32_t l2norm;            /* q and k per head before the query scale: 0 none, 1 x / sqrt(sum x^2 + eps),
+                                2 x rsqrt(sum x^2 + eps) (fp32) */
+  float eps;                 /* 1e-6 in vLLM */
+  int32_t null_slot;         /* 1: a state index <= 0 is vLLM's null block (the sequence is skipped);
+                                0: only a negative index skips (pbk_gdn_decode's rule) */
+  int32_t zero_skipped;      /* 1: a skipped sequence's outputs are written as zeros (the packed decode) */
+  const int32_t* cu_seqlens; /* [batch + 1] row offsets of each sequence in [1, rows, H, D] tensors, or NULL:
+                                dense [batch, seqlen, ...] */
+  int64_t index_stride;      /* > 0: state_indices is [batch, index_stride] (speculative decoding): the initial
+                                state is column num_accepted[n] - 1 (0 without num_accepted) of row n, and the
+                                state after token t is written to column t (null columns skipped); 0: one
+                                slot per sequence, read and written */
+  const int32_t* num_accepted; /* [batch] accepted tokens per sequence, or NULL */
+} pbk_decode_ext;
+
+/* pbk_gdn_decode with vLLM's decode-op semantics (pbk_decode_ext): the same kernel, reading
+ * and writing each state once per token span (and once more per token under speculative
+ * decoding). desc->seqlen is the dense token count (ignored with cu_seqlens); the state pool
+ * is updated in place (desc->h0 NULL or equal to desc->state). */
+PBK_API int pbk_gdn_decode_ext(const pbk_gdn_desc* desc, const pbk_decode_ext* ext, void* stream);
+
 /* Chunked gated delta rule (prefill): the chunkwise WY algorithm of
  * delta_rule_chunked, pseudobrain/gated_deltanet.py:110-165 (chunk 64), reading h0
  * (NULL = zeros) and writing the final state into `state` (h0 == state is allowed:

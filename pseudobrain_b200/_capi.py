@@ -25,6 +25,15 @@ class PbkView(ctypes.Structure):
                 ("stride_h", ctypes.c_int64), ("dtype", ctypes.c_int32), ("pad_", ctypes.c_int32)]
 
 
+class PbkDecodeExt(ctypes.Structure):
+    _fields_ = [("gating", ctypes.c_int32), ("beta_round", ctypes.c_int32), ("softplus_beta", ctypes.c_float),
+                ("softplus_threshold", ctypes.c_float), ("a", PbkView), ("b", PbkView), ("a_log", ctypes.c_void_p),
+                ("dt_bias", ctypes.c_void_p), ("a_log_dtype", ctypes.c_int32), ("dt_bias_dtype", ctypes.c_int32),
+                ("l2norm", ctypes.c_int32), ("eps", ctypes.c_float), ("null_slot", ctypes.c_int32),
+                ("zero_skipped", ctypes.c_int32), ("cu_seqlens", ctypes.c_void_p), ("index_stride", ctypes.c_int64),
+                ("num_accepted", ctypes.c_void_p)]
+
+
 class PbkConvDesc(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hk", ctypes.c_int32), ("hv", ctypes.c_int32),
                 ("width", ctypes.c_int32), ("l2mode", ctypes.c_int32), ("eps", ctypes.c_float), ("pad_", ctypes.c_int32),
@@ -118,6 +127,8 @@ SIGNATURES = {
     "pbk_device_check": (ctypes.c_int, [ctypes.c_int]),
     "pbk_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "pbk_gdn_decode": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
+    "pbk_gdn_decode_ext": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.POINTER(PbkDecodeExt),
+                                          ctypes.c_void_p]),
     "pbk_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
     "pbk_gdn_prefill_workspace": (ctypes.c_size_t, [ctypes.POINTER(PbkGdnDesc)]),
     "pbk_gdn_prefill_ws": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),

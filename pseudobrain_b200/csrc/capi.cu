@@ -8,6 +8,7 @@
 
 namespace pbk {
 cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st);
+cudaError_t launch_gdn_decode_ext(const pbk_gdn_desc& d, const pbk_decode_ext& e, cudaStream_t st);
 cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st);
 bool gdn_prefill_tc_supported(const pbk_gdn_desc& d);
 size_t gdn_prefill_tc_workspace(const pbk_gdn_desc& d);
@@ -181,6 +182,32 @@ int pbk_gdn_decode(const pbk_gdn_desc* desc, void* stream) {
   if (desc->batch == 0) return PBK_OK;  // seqlen 0 still copies h0 into state
   if ((st = check_current_device()) != PBK_OK) return st;
   return launch_status(pbk::launch_gdn_decode(*desc, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_gdn_decode_ext(const pbk_gdn_desc* desc, const pbk_decode_ext* ext, void* stream) {
+  if (ext == nullptr) return PBK_ERR_INVALID;
+  pbk_gdn_desc d = *desc;
+  if (ext->gating) {  // desc->g / desc->beta are not read: let validation see the gate inputs
+    d.g = ext->a;
+    d.beta = ext->b;
+  }
+  if (ext->cu_seqlens != nullptr) d.seqlen = 1;  // rows come from cu_seqlens (validated on the device side)
+  int st = validate_gdn(&d);
+  if (st != PBK_OK) return st;
+  if (desc->h0 != nullptr && desc->h0 != desc->state) return PBK_ERR_INVALID;  // the pool is updated in place
+  if (ext->l2norm < 0 || ext->l2norm > 2 || !(ext->eps >= 0.f)) return PBK_ERR_INVALID;
+  if (ext->gating) {
+    if (!ext->a.data || !ext->b.data || !ext->a_log || !ext->dt_bias) return PBK_ERR_INVALID;
+    if (!dtype_ok(ext->a.dtype) || !dtype_ok(ext->b.dtype) || !dtype_ok(ext->a_log_dtype) ||
+        !dtype_ok(ext->dt_bias_dtype))
+      return PBK_ERR_DTYPE;
+    if (!(ext->softplus_beta > 0.f)) return PBK_ERR_INVALID;
+  }
+  if (ext->index_stride < 0 || (ext->index_stride > 0 && desc->state_indices == nullptr)) return PBK_ERR_INVALID;
+  if (ext->num_accepted != nullptr && ext->index_stride == 0) return PBK_ERR_INVALID;
+  if (desc->batch == 0) return PBK_OK;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_decode_ext(*desc, *ext, static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream) {

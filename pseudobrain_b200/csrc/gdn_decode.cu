@@ -14,9 +14,31 @@
 //     transposed tile; each row's dot products are warp-shuffle reductions and
 //     need no shared memory.
 // The HBM roofline bound is (read + write of the fp32 state) / bandwidth.
+//
+// The extended form (kExt, pbk_gdn_decode_ext) adds what vLLM's decode ops do around the
+// same recurrence (vllm/model_executor/layers/fla/ops/fused_recurrent.py:256-336 packed
+// decode, :20-170 fused recurrent; fused_sigmoid_gating.py:24-180): the gating
+// g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) computed from the raw gate
+// inputs, the per-head L2 norm of q and k, packed sequences of any length (cu_seqlens),
+// vLLM's null slot (index <= 0), and speculative decoding (2-D state indices: the initial
+// state from column num_accepted - 1, the state after token t into column t).
 #include "common.cuh"
 
 namespace pbk {
+
+// Device-side copy of pbk_decode_ext (plus nothing): passed by value to the kernel.
+struct DecodeExt {
+  int gating, beta_round, l2norm, null_slot, zero_skipped;
+  float softplus_beta, softplus_threshold, eps;
+  pbk_view a, b;
+  const void* a_log;
+  const void* dt_bias;
+  int a_log_dtype, dt_bias_dtype;
+  const int32_t* cu_seqlens;
+  int64_t index_stride;
+  const int32_t* num_accepted;
+};
+
 namespace {
 
 constexpr int kDim = 128;        // dk == dv
@@ -24,17 +46,45 @@ constexpr int kThreads = 256;    // 8 warps
 constexpr int kWarps = kThreads / 32;
 constexpr int kRows = kDim / kWarps;  // 16 state rows per thread, 4 columns each
 
-template <typename TIn, typename TOut, int LAYOUT>
-__global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const pbk_gdn_desc d) {
-  const int b = blockIdx.x / d.hv;
-  const int h = blockIdx.x - b * d.hv;
-  int64_t slot = b;
-  if (d.state_indices != nullptr) {
-    slot = d.state_indices[b];
-    if (slot < 0) return;  // padding slot: nothing to read or write
+__device__ __forceinline__ float round_to(float x, int dtype) {
+  return dtype == PBK_BF16 ? __bfloat162float(__float2bfloat16_rn(x)) : x;
+}
+
+template <typename TIn, typename TOut, int LAYOUT, bool kExt>
+__global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const pbk_gdn_desc d, const DecodeExt x) {
+  const int n = blockIdx.x / d.hv;  // sequence
+  const int h = blockIdx.x - n * d.hv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // this sequence's rows: dense [B, T, ..] (batch n, rows 0 .. seqlen) or packed (batch 0)
+  int64_t bsel = n, row0 = 0;
+  int ntok = d.seqlen;
+  if (kExt && x.cu_seqlens != nullptr) {
+    bsel = 0;
+    row0 = x.cu_seqlens[n];
+    ntok = x.cu_seqlens[n + 1] - x.cu_seqlens[n];
   }
   const int hk = h / (d.hv / d.hk);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  TOut* ob = reinterpret_cast<TOut*>(const_cast<void*>(d.o.data)) + bsel * d.o.stride_b + row0 * d.o.stride_t +
+             h * d.o.stride_h;
+  // the state slot read (and, without per-token columns, written)
+  int64_t slot = n;
+  const bool per_token = kExt && x.index_stride > 0;
+  if (d.state_indices != nullptr) {
+    if (per_token) {
+      const int col = x.num_accepted != nullptr ? x.num_accepted[n] - 1 : 0;
+      slot = d.state_indices[(int64_t)n * x.index_stride + col];
+    } else {
+      slot = d.state_indices[n];
+    }
+    const bool skip = (kExt && x.null_slot) ? slot <= 0 : slot < 0;
+    if (skip) {  // padding / null slot (uniform for the CTA): nothing to read or write
+      if (kExt && x.zero_skipped)
+        for (int i = tid; i < ntok * kDim; i += kThreads)
+          ob[(int64_t)(i / kDim) * d.o.stride_t + (i % kDim)] = from_f32<TOut>(0.f);
+      return;
+    }
+  }
+  if (kExt && ntok <= 0) return;
   const int64_t tile = slot * d.state_slot_stride + (int64_t)h * kDim * kDim;
   float* S = d.state + tile;
   const float* S0 = (d.h0 != nullptr ? d.h0 + tile : S);
@@ -42,26 +92,53 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const pbk_gdn_d
   __shared__ float sh_k[kDim], sh_q[kDim], sh_v[kDim], sh_u[kDim];
   __shared__ __align__(16) float red[2][kWarps][kDim];
   __shared__ float sh_kq;
+  __shared__ float sh_norm[2][4];
 
   float4 s[kRows];
 #pragma unroll
   for (int i = 0; i < kRows; ++i) s[i] = ld_f4_stream(S0 + (int64_t)(warp + kWarps * i) * kDim + 4 * lane);
 
-  const TIn* qb = reinterpret_cast<const TIn*>(d.q.data) + b * d.q.stride_b + hk * d.q.stride_h;
-  const TIn* kb = reinterpret_cast<const TIn*>(d.k.data) + b * d.k.stride_b + hk * d.k.stride_h;
-  const TIn* vb = reinterpret_cast<const TIn*>(d.v.data) + b * d.v.stride_b + h * d.v.stride_h;
-  TOut* ob = reinterpret_cast<TOut*>(const_cast<void*>(d.o.data)) + b * d.o.stride_b + h * d.o.stride_h;
+  const TIn* qb = reinterpret_cast<const TIn*>(d.q.data) + bsel * d.q.stride_b + row0 * d.q.stride_t + hk * d.q.stride_h;
+  const TIn* kb = reinterpret_cast<const TIn*>(d.k.data) + bsel * d.k.stride_b + row0 * d.k.stride_t + hk * d.k.stride_h;
+  const TIn* vb = reinterpret_cast<const TIn*>(d.v.data) + bsel * d.v.stride_b + row0 * d.v.stride_t + h * d.v.stride_h;
 
-  for (int t = 0; t < d.seqlen; ++t) {
+  for (int t = 0; t < ntok; ++t) {
+    float gam, bet;
+    if (kExt && x.gating) {
+      // vLLM's gating: g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
+      const int64_t at = bsel * x.a.stride_b + (row0 + t) * x.a.stride_t + h * x.a.stride_h;
+      const int64_t bt = bsel * x.b.stride_b + (row0 + t) * x.b.stride_t + h * x.b.stride_h;
+      const float xa = load_any(x.a.data, at, x.a.dtype) + load_any(x.dt_bias, h, x.dt_bias_dtype);
+      const float sb = x.softplus_beta;
+      const float sp = sb * xa <= x.softplus_threshold ? logf(1.f + expf(sb * xa)) / sb : xa;
+      const float g = -expf(load_any(x.a_log, h, x.a_log_dtype)) * sp;
+      gam = expf(g);
+      const float sig = 1.f / (1.f + expf(-load_any(x.b.data, bt, x.b.dtype)));
+      bet = x.beta_round ? round_to(sig, x.b.dtype) : sig;
+    } else {
+      gam = expf(load_any(d.g.data, bsel * d.g.stride_b + (row0 + t) * d.g.stride_t + h * d.g.stride_h, d.g.dtype));
+      bet = load_any(d.beta.data, bsel * d.beta.stride_b + (row0 + t) * d.beta.stride_t + h * d.beta.stride_h,
+                     d.beta.dtype);
+    }
     if (tid < kDim) {
       sh_k[tid] = to_f32(kb[t * d.k.stride_t + tid]);
       sh_v[tid] = to_f32(vb[t * d.v.stride_t + tid]);
     } else {
-      sh_q[tid - kDim] = to_f32(qb[t * d.q.stride_t + tid - kDim]) * d.scale;
+      const float qv = to_f32(qb[t * d.q.stride_t + tid - kDim]);
+      sh_q[tid - kDim] = (kExt && x.l2norm) ? qv : qv * d.scale;
     }
-    const float gam = expf(load_any(d.g.data, b * d.g.stride_b + t * d.g.stride_t + h * d.g.stride_h, d.g.dtype));
-    const float bet = load_any(d.beta.data, b * d.beta.stride_b + t * d.beta.stride_t + h * d.beta.stride_h,
-                               d.beta.dtype);
+    if (kExt && x.l2norm) {
+      // per-head L2 norm of k (warps 0-3) and q (warps 4-7) in fp32, then q's scale
+      const float own = tid < kDim ? sh_k[tid] : sh_q[tid - kDim];
+      const float ss = warp_sum(own * own);
+      if (lane == 0) sh_norm[warp >> 2][warp & 3] = ss;
+      __syncthreads();
+      const int which = tid < kDim ? 0 : 1;
+      const float tot = sh_norm[which][0] + sh_norm[which][1] + sh_norm[which][2] + sh_norm[which][3] + x.eps;
+      const float nv = x.l2norm == 1 ? own / sqrtf(tot) : own * rsqrtf(tot);
+      if (tid < kDim) sh_k[tid] = nv;
+      else sh_q[tid - kDim] = nv * d.scale;
+    }
     __syncthreads();
     TOut* ot = ob + t * d.o.stride_t;
     if constexpr (LAYOUT == PBK_STATE_KV) {
@@ -121,30 +198,65 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const pbk_gdn_d
         if (lane == 0) ot[c] = from_f32<TOut>(fmaf(kq, u, pq));
       }
     }
+    if (per_token) {  // speculative decoding: the state after token t into column t (if not null)
+      const int64_t st = d.state_indices[(int64_t)n * x.index_stride + t];
+      if (x.null_slot ? st > 0 : st >= 0) {
+        float* Sd = d.state + st * d.state_slot_stride + (int64_t)h * kDim * kDim;
+#pragma unroll
+        for (int i = 0; i < kRows; ++i) st_f4_stream(Sd + (int64_t)(warp + kWarps * i) * kDim + 4 * lane, s[i]);
+      }
+    }
     __syncthreads();  // the next token restages shared memory
   }
+  if (!per_token) {
 #pragma unroll
-  for (int i = 0; i < kRows; ++i) st_f4_stream(S + (int64_t)(warp + kWarps * i) * kDim + 4 * lane, s[i]);
+    for (int i = 0; i < kRows; ++i) st_f4_stream(S + (int64_t)(warp + kWarps * i) * kDim + 4 * lane, s[i]);
+  }
 }
 
-template <typename TIn, typename TOut>
-cudaError_t launch_layout(const pbk_gdn_desc& d, cudaStream_t st) {
+template <typename TIn, typename TOut, bool kExt>
+cudaError_t launch_layout(const pbk_gdn_desc& d, const DecodeExt& x, cudaStream_t st) {
   const dim3 grid((unsigned)((int64_t)d.batch * d.hv));
   if (d.state_layout == PBK_STATE_KV)
-    gdn_decode_kernel<TIn, TOut, PBK_STATE_KV><<<grid, kThreads, 0, st>>>(d);
+    gdn_decode_kernel<TIn, TOut, PBK_STATE_KV, kExt><<<grid, kThreads, 0, st>>>(d, x);
   else
-    gdn_decode_kernel<TIn, TOut, PBK_STATE_VK><<<grid, kThreads, 0, st>>>(d);
+    gdn_decode_kernel<TIn, TOut, PBK_STATE_VK, kExt><<<grid, kThreads, 0, st>>>(d, x);
   return cudaGetLastError();
+}
+
+template <bool kExt>
+cudaError_t launch_any(const pbk_gdn_desc& d, const DecodeExt& x, cudaStream_t st) {
+  const bool in_bf16 = d.q.dtype == PBK_BF16, out_bf16 = d.o.dtype == PBK_BF16;
+  if (in_bf16 && out_bf16) return launch_layout<__nv_bfloat16, __nv_bfloat16, kExt>(d, x, st);
+  if (in_bf16) return launch_layout<__nv_bfloat16, float, kExt>(d, x, st);
+  if (out_bf16) return launch_layout<float, __nv_bfloat16, kExt>(d, x, st);
+  return launch_layout<float, float, kExt>(d, x, st);
 }
 
 }  // namespace
 
-cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st) {
-  const bool in_bf16 = d.q.dtype == PBK_BF16, out_bf16 = d.o.dtype == PBK_BF16;
-  if (in_bf16 && out_bf16) return launch_layout<__nv_bfloat16, __nv_bfloat16>(d, st);
-  if (in_bf16) return launch_layout<__nv_bfloat16, float>(d, st);
-  if (out_bf16) return launch_layout<float, __nv_bfloat16>(d, st);
-  return launch_layout<float, float>(d, st);
+cudaError_t launch_gdn_decode(const pbk_gdn_desc& d, cudaStream_t st) { return launch_any<false>(d, DecodeExt{}, st); }
+
+cudaError_t launch_gdn_decode_ext(const pbk_gdn_desc& d, const pbk_decode_ext& e, cudaStream_t st) {
+  DecodeExt x;
+  x.gating = e.gating;
+  x.beta_round = e.beta_round;
+  x.l2norm = e.l2norm;
+  x.null_slot = e.null_slot;
+  x.zero_skipped = e.zero_skipped;
+  x.softplus_beta = e.softplus_beta;
+  x.softplus_threshold = e.softplus_threshold;
+  x.eps = e.eps;
+  x.a = e.a;
+  x.b = e.b;
+  x.a_log = e.a_log;
+  x.dt_bias = e.dt_bias;
+  x.a_log_dtype = e.a_log_dtype;
+  x.dt_bias_dtype = e.dt_bias_dtype;
+  x.cu_seqlens = e.cu_seqlens;
+  x.index_stride = e.index_stride;
+  x.num_accepted = e.num_accepted;
+  return launch_any<true>(d, x, st);
 }
 
 }  // namespace pbk

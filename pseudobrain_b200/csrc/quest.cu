@@ -319,18 +319,40 @@ constexpr int kRefineEpsExp = -12;
 
 __device__ __forceinline__ float canonical_row_sum(const float* qrow, const bf16* bmax, const bf16* bmin) {
   float acc = 0.f;
-#pragma unroll 2
-  for (int d0 = 0; d0 < kD; d0 += 8) {
-    float mx[8], mn[8];
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmax + d0), mx);
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmin + d0), mn);
+  for (int d0 = 0; d0 < kD; d0 += 16) {
+    uint4 rx[2], rn[2];  // 16 dims of both bounds in flight at once
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float qv = qrow[d0 + j];
-      acc = fmaf(qv, qv > 0.f ? mx[j] : mn[j], acc);
+    for (int c = 0; c < 2; ++c) {
+      rx[c] = *reinterpret_cast<const uint4*>(bmax + d0 + 8 * c);
+      rn[c] = *reinterpret_cast<const uint4*>(bmin + d0 + 8 * c);
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float mx[8], mn[8];
+      bf16x8_to_f32(rx[c], mx);
+      bf16x8_to_f32(rn[c], mn);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float qv = qrow[d0 + 8 * c + j];
+        acc = fmaf(qv, qv > 0.f ? mx[j] : mn[j], acc);
+      }
     }
   }
   return acc;
+}
+
+// Canonical keys of the listed pages: ckey[u] = ordered key of the max over the rpg query
+// rows of page list[u]'s canonical sum, one (page, row) pair per thread.
+__device__ __forceinline__ void canonical_keys(const RefineArgs& rf, const float (*qs)[kD], int rpg, int h,
+                                               const int32_t* list, int n, uint32_t* ckey) {
+  for (int u = threadIdx.x; u < n; u += kTopkThreads) ckey[u] = 0u;
+  __syncthreads();
+  for (int w = threadIdx.x; w < n * rpg; w += kTopkThreads) {
+    const int u = w / rpg, r = w % rpg;
+    const int64_t off = h * rf.bnd_stride_kv + (int64_t)list[u] * rf.bnd_stride_p;
+    atomicMax(&ckey[u], ordered_key(canonical_row_sum(qs[r], rf.kmax + off, rf.kmin + off)));
+  }
+  __syncthreads();
 }
 
 __device__ __forceinline__ float ordered_key_inv(uint32_t k) {
@@ -344,6 +366,7 @@ struct TopkSmem {
   uint32_t cand_key[kCandCap];
   int32_t cand_idx[kCandCap];
   float qs[kRefineRows][kD];  // the row's query rows (refinement)
+  int32_t band_page[kCandCap]; // pages of the band (candidate path)
   float red[kTopkWarps];
   float qs_l1[kTopkWarps];
   float eps2;                 // twice the error bound of the row's scores
@@ -518,14 +541,10 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
           }
           __syncthreads();
           const int nu = ts.n_unc;
-          for (int u = threadIdx.x; u < nu; u += kTopkThreads) ts.seg_key[u] = 0u;
+          // the band's pages (cseg holds candidate positions): their page indices into cand_page
+          for (int u = threadIdx.x; u < nu; u += kTopkThreads) ts.band_page[u] = ts.cand_idx[ts.cseg[u]];
           __syncthreads();
-          for (int w = threadIdx.x; w < nu * rpg; w += kTopkThreads) {
-            const int u = w / rpg, r = w % rpg, page = ts.cand_idx[ts.cseg[u]];
-            const int64_t off = rh * rf.bnd_stride_kv + (int64_t)page * rf.bnd_stride_p;
-            atomicMax(&ts.seg_key[u], ordered_key(canonical_row_sum(ts.qs[r], rf.kmax + off, rf.kmin + off)));
-          }
-          __syncthreads();
+          canonical_keys(rf, ts.qs, rpg, rh, ts.band_page, nu, ts.seg_key);
           for (int u = threadIdx.x; u < nu; u += kTopkThreads) ts.cand_key[ts.cseg[u]] = ts.seg_key[u];
           __syncthreads();
           radix_select([&](int i) { return ts.cand_key[i]; }, ptotal, (uint32_t)k, ss, prefix, kk);
@@ -538,15 +557,48 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
   }
   radix_select([&](int i) { return ordered_key(s[i]); }, npages, (uint32_t)k, ss, prefix, kk);
   if (refine) {
-    // whole row: the band's canonical keys are computed where they are read (rare path)
+    // whole row: the band's pages listed in index order, their canonical keys computed once
+    // (read back by binary search); a band too large for shared memory computes them where
+    // they are read
     uint32_t lo, hi;
     refine_band(prefix, eps2, lo, hi);
     const uint32_t ninf = ordered_key(-INFINITY);
+    auto in_band = [&](uint32_t key) { return key != ninf && key >= lo && key <= hi; };
+    const int R = warp_range(npages);
+    const int lo_i = min(warp * R, npages), hi_i = min(lo_i + R, npages);
+    int cnt = 0;
+    for (int j = lo_i; j < hi_i; j += 32) {
+      const int i = j + lane;
+      cnt += __popc(__ballot_sync(0xffffffffu, i < hi_i && in_band(ordered_key(s[i]))));
+    }
+    int pos, zero, nb;
+    warp_bases(cnt, 0, ss, pos, zero, nb);
+    const bool listed = nb <= kSegCap;
+    if (listed) {
+      for (int j = lo_i; j < hi_i; j += 32) {
+        const int i = j + lane;
+        const bool c = i < hi_i && in_band(ordered_key(s[i]));
+        const uint32_t bc = __ballot_sync(0xffffffffu, c);
+        if (c) ts.cseg[pos + __popc(bc & lt)] = i;
+        pos += __popc(bc);
+      }
+      __syncthreads();
+      canonical_keys(rf, ts.qs, rpg, rh, ts.cseg, nb, ts.seg_key);
+    }
     auto key2 = [&](int i) -> uint32_t {
       const uint32_t key = ordered_key(s[i]);
       if (key == ninf) return key;
       if (key > hi) return 0xFFFFFFFFu;
       if (key < lo) return 0u;
+      if (listed) {  // cseg[0 .. nb) ascending: find i
+        int a = 0, b = nb - 1;
+        while (a < b) {
+          const int m = (a + b) >> 1;
+          if (ts.cseg[m] < i) a = m + 1;
+          else b = m;
+        }
+        return ts.seg_key[a];
+      }
       const int64_t off = rh * rf.bnd_stride_kv + (int64_t)i * rf.bnd_stride_p;
       float best = -INFINITY;
       for (int r = 0; r < rpg; ++r) best = fmaxf(best, canonical_row_sum(ts.qs[r], rf.kmax + off, rf.kmin + off));

@@ -58,7 +58,8 @@ def test_abi_version_and_status_strings(lib):
                                           ("pbk_out_norm_desc", "PbkOutNormDesc"),
                                           ("pbk_quest_levels", "PbkQuestLevels"),
                                           ("pbk_rope_gather_desc", "PbkRopeGatherDesc"),
-                                          ("pbk_archive_write_desc", "PbkArchiveWriteDesc")])
+                                          ("pbk_archive_write_desc", "PbkArchiveWriteDesc"),
+                                          ("pbk_decode_ext", "PbkDecodeExt")])
 def test_descriptor_layout_matches_header(cname, pyname):
     """Offsets of every field of the ctypes mirror equal the C struct's (checked by
     compiling a probe against include/pbk.h)."""

@@ -83,6 +83,9 @@ def test_chunk_rule_dense_batch_without_state(cuda_device):
 
 @pytest.mark.parametrize("inplace", [True, False])
 def test_fused_recurrent_on_a_state_pool(cuda_device, inplace):
+    """One token per sequence on a state pool: in place through ssm_state_indices (indices 0
+    and -1 are vLLM's null block: skipped), or out of place into a new state per sequence."""
+    from oracle import vllm_decode as ovd
     from pseudobrain_b200.vllm_adapter import fused_recurrent_gated_delta_rule
     rng = np.random.default_rng(11 + inplace)
     hk, hv, n, slots = 2, 4, 5, 9
@@ -97,21 +100,17 @@ def test_fused_recurrent_on_a_state_pool(cuda_device, inplace):
         _dev(beta, cuda_device), None, dpool, inplace, cu,
         torch.from_numpy(idx).to(cuda_device) if idx is not None else None, None, True)
     assert o.shape == (1, n, hv, 128)
+    ro, rpool = ovd.recurrent(q, k, v, g, beta, 128 ** -0.5, pool if inplace else pool[:n], cu_seqlens=cu.cpu().numpy(),
+                              indices=idx, l2=1)
     for s in range(n):
         slot = int(idx[s]) if inplace else s
-        if slot < 0:
+        if slot <= 0 and inplace:
             continue
-        # the norm writes bf16 rows (the input dtype), which the recurrence then reads
-        qs = bf16_round(ogdn.l2_normalize(q[:, s:s + 1], "hf", 1e-6))
-        ks = bf16_round(ogdn.l2_normalize(k[:, s:s + 1], "hf", 1e-6))
-        ro, rs = ogdn.delta_rule_sequential(ogdn.expand_key_heads(qs, hv), ogdn.expand_key_heads(ks, hv),
-                                            v[:, s:s + 1], g[:, s:s + 1], beta[:, s:s + 1], 128 ** -0.5,
-                                            pool[slot:slot + 1].transpose(0, 1, 3, 2))
-        assert ogdn.rel_err(o[:, s:s + 1].float().cpu().numpy(), ro) < TOL, s
-        assert ogdn.rel_err(final[slot:slot + 1].cpu().numpy(), rs.transpose(0, 1, 3, 2)) < 1e-4, s
+        assert ogdn.rel_err(o[:, s:s + 1].float().cpu().numpy(), ro[:, s:s + 1]) < TOL, s
+        assert ogdn.rel_err(final[slot:slot + 1].cpu().numpy(), rpool[slot:slot + 1]) < 1e-4, s
     if inplace:
         assert final is dpool
-        for slot in (1, 2, 4, 6, 8):  # untouched slots, the padding index included
+        for slot in (0, 1, 2, 4, 6, 8):  # untouched slots, the null slot 0 included
             assert torch.equal(dpool[slot], before[slot])
     else:
         assert torch.equal(dpool, before)
