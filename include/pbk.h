@@ -195,6 +195,17 @@ PBK_API int pbk_gdn_prefill(const pbk_gdn_desc* desc, void* stream);
 PBK_API size_t pbk_gdn_prefill_workspace(const pbk_gdn_desc* desc);
 PBK_API int pbk_gdn_prefill_ws(const pbk_gdn_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
 
+/* pbk_gdn_prefill_ws that also writes the chunk quantities the reference's fla custom op
+ * returns beside (o, final state) -- pseudobrain::gated_delta_chunk, gated_deltanet.py:200-216,
+ * whose backward consumes them: gc [B, T, Hv] fp32, the cumulative sum of g within each
+ * 64-token chunk (fla's chunk-local cumsum), and a [B, T, Hv, 64] (bf16 or fp32, last dim
+ * contiguous, 16-byte aligned rows), row t of its chunk's T = (I + A)^-1 with
+ * A_ti = beta_t (k_t . k_i) exp(gc_t - gc_i) for i < t (fla's solve_tril output, the
+ * reference's `solve`, gated_deltanet.py:145-150); entries past the chunk's last valid step
+ * are zero. o.data must be set. Same workspace as pbk_gdn_prefill_ws. */
+PBK_API int pbk_gdn_prefill_aux(const pbk_gdn_desc* desc, const pbk_view* gc, const pbk_view* a, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* The two halves of pbk_gdn_prefill_ws, tensor-core path only (PBK_ERR_INVALID otherwise):
  * pbk_gdn_chunk_solve writes the workspace from k, g and beta; pbk_gdn_prefill_solved runs
  * the recurrence from a workspace holding the solve of the same chunks. Slot (b, chunk, h)

@@ -122,6 +122,35 @@ def delta_rule_chunked(q, k, v, g, beta, scale, h0, chunk: int | None = None):
     return np.ascontiguousarray(o.transpose(0, 2, 1, 3)), state
 
 
+def chunk_aux(k, g, beta, chunk: int = CHUNK):
+    """The chunk quantities the reference's fla op returns beside (o, state)
+    (pseudobrain::gated_delta_chunk, gated_deltanet.py:200-216): gc [B,T,H], the cumulative g
+    within each chunk of ``chunk`` steps, and a [B,T,H,chunk], row t of its chunk's
+    T = (I + A)^-1 with A_ti = beta_t k_t.k_i exp(c_t - c_i) (i < t) -- the reference's
+    `solve` (gated_deltanet.py:141-150), chunks of the fixed fla size with identity padding."""
+    batch, length, heads, dk = k.shape
+    pad = (-length) % chunk
+    dt = _compute_dtype(k)
+    kh = np.ascontiguousarray(k.astype(dt).transpose(0, 2, 1, 3))
+    gh = np.ascontiguousarray(g.astype(dt).transpose(0, 2, 1))
+    bh = np.ascontiguousarray(beta.astype(dt).transpose(0, 2, 1))
+    if pad:
+        kh = np.pad(kh, ((0, 0), (0, 0), (0, pad), (0, 0)))
+        gh, bh = (np.pad(x, ((0, 0), (0, 0), (0, pad))) for x in (gh, bh))
+    count = (length + pad) // chunk
+    kh = kh.reshape(batch, heads, count, chunk, dk)
+    c = np.cumsum(gh.reshape(batch, heads, count, chunk), axis=-1, dtype=dt)
+    bh = bh.reshape(batch, heads, count, chunk)
+    strict = np.tril(np.ones((chunk, chunk), dtype=bool), -1)
+    with np.errstate(over="ignore"):
+        diff = np.where(strict, c[..., :, None] - c[..., None, :], 0.0)
+    a = np.where(strict, bh[..., :, None] * (kh @ kh.swapaxes(-1, -2)) * np.exp(diff), 0.0).astype(dt)
+    solve = _unit_lower_inverse(a)
+    gc = c.reshape(batch, heads, count * chunk)[:, :, :length].transpose(0, 2, 1)
+    ta = solve.reshape(batch, heads, count * chunk, chunk)[:, :, :length].transpose(0, 2, 1, 3)
+    return np.ascontiguousarray(gc), np.ascontiguousarray(ta)
+
+
 def rel_err(x: np.ndarray, ref: np.ndarray) -> float:
     """Norm-wise relative error ||x - ref|| / ||ref|| in fp64 (the parity metric)."""
     x = np.asarray(x, dtype=np.float64)

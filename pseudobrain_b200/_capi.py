@@ -132,6 +132,8 @@ SIGNATURES = {
     "pbk_gdn_prefill": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.c_void_p]),
     "pbk_gdn_prefill_workspace": (ctypes.c_size_t, [ctypes.POINTER(PbkGdnDesc)]),
     "pbk_gdn_prefill_ws": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),
+    "pbk_gdn_prefill_aux": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), ctypes.POINTER(PbkView),
+                                           ctypes.POINTER(PbkView), _VP, ctypes.c_size_t, _VP]),
     "pbk_gdn_chunk_solve": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),
     "pbk_gdn_conv_norm": (ctypes.c_int, [ctypes.POINTER(PbkConvDesc), _VP]),
     "pbk_gdn_gating": (ctypes.c_int, [ctypes.POINTER(PbkGatingDesc), _VP]),

@@ -12,7 +12,10 @@ cudaError_t launch_gdn_decode_ext(const pbk_gdn_desc& d, const pbk_decode_ext& e
 cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st);
 bool gdn_prefill_tc_supported(const pbk_gdn_desc& d);
 size_t gdn_prefill_tc_workspace(const pbk_gdn_desc& d);
-cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t st);
+cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t st, const pbk_view* gc = nullptr,
+                                   const pbk_view* ta = nullptr);
+cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st, const pbk_view* gc,
+                                    const pbk_view* ta);
 size_t gdn_prefill_varlen_workspace(const pbk_gdn_desc& d, int num_seqs);
 cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_gating(const pbk_gating_desc& d, cudaStream_t st);
@@ -243,6 +246,27 @@ int pbk_gdn_prefill_ws(const pbk_gdn_desc* desc, void* workspace, size_t workspa
   if (!aligned16(workspace)) return PBK_ERR_ALIGN;
   if ((st = check_current_device()) != PBK_OK) return st;
   return launch_status(pbk::launch_gdn_prefill_tc(*desc, workspace, false, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_gdn_prefill_aux(const pbk_gdn_desc* desc, const pbk_view* gc, const pbk_view* a, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  int st = validate_gdn(desc);
+  if (st != PBK_OK) return st;
+  if (gc == nullptr || a == nullptr || gc->data == nullptr || a->data == nullptr) return PBK_ERR_INVALID;
+  if (gc->dtype != PBK_F32 || !dtype_ok(a->dtype)) return PBK_ERR_DTYPE;
+  if (!aligned16(a->data) || a->stride_b % 8 || a->stride_t % 8 || a->stride_h % 8) return PBK_ERR_ALIGN;
+  if (desc->batch == 0) return PBK_OK;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!pbk::gdn_prefill_tc_supported(*desc)) {
+    if ((st = check_current_device()) != PBK_OK) return st;
+    return launch_status(pbk::launch_gdn_prefill_simt(*desc, s, gc, a));
+  }
+  if (workspace == nullptr || workspace_bytes < pbk::gdn_prefill_tc_workspace(*desc)) return PBK_ERR_INVALID;
+  if (!aligned16(workspace)) return PBK_ERR_ALIGN;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  cudaError_t e = pbk::launch_gdn_chunk_solve(*desc, workspace, s, gc, a);
+  if (e != cudaSuccess) return launch_status(e);
+  return launch_status(pbk::launch_gdn_prefill_tc(*desc, workspace, true, s));
 }
 
 // The two halves of pbk_gdn_prefill_ws (tensor-core path only).

@@ -64,8 +64,18 @@ __device__ __forceinline__ void simt_gemm(FA a, FB b, FO out) {
     for (int c = 0; c < RN; ++c) out(ty + TY * r, tx + TX * c, r, c, acc[r][c]);
 }
 
+// Optional chunk outputs (pbk_gdn_prefill_aux), written by the first value-column slice: the
+// in-chunk cumulative g [B, T, Hv] fp32 and the rows of T = (I + A)^-1 [B, T, Hv, 64].
+struct ChunkAux {
+  float* gc;
+  int64_t gc_sb, gc_st, gc_sh;
+  void* ta;
+  int64_t ta_sb, ta_st, ta_sh;
+  int ta_dtype;
+};
+
 template <typename TIn, typename TOut, int DVB>
-__global__ void __launch_bounds__(NT, 1) gdn_prefill_simt_kernel(const pbk_gdn_desc d) {
+__global__ void __launch_bounds__(NT, 1) gdn_prefill_simt_kernel(const pbk_gdn_desc d, const ChunkAux aux) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem<DVB>& sm = *reinterpret_cast<Smem<DVB>*>(smem_raw);
   const int j0 = blockIdx.x * DVB;
@@ -153,6 +163,20 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_simt_kernel(const pbk_gdn_d
       }
     }
     __syncthreads();
+    if (blockIdx.x == 0 && (aux.gc != nullptr || aux.ta != nullptr)) {
+      for (int e = tid; e < C * C; e += NT) {
+        const int t = e / C, i = e % C;
+        if (t0 + t >= d.seqlen) continue;
+        if (aux.ta != nullptr) {
+          const int64_t o = b * aux.ta_sb + (int64_t)(t0 + t) * aux.ta_st + h * aux.ta_sh + i;
+          const float x = sm.T[t * PC + i];
+          if (aux.ta_dtype == PBK_BF16) static_cast<__nv_bfloat16*>(aux.ta)[o] = __float2bfloat16_rn(x);
+          else static_cast<float*>(aux.ta)[o] = x;
+        }
+        if (aux.gc != nullptr && i == 0)
+          aux.gc[b * aux.gc_sb + (int64_t)(t0 + t) * aux.gc_st + h * aux.gc_sh] = sm.cum[t];
+      }
+    }
 
     // ---- W = T (K beta gamma) [C x D];  U' = T (V beta) [C x DVB] ----
     simt_gemm<C, D, C, 4, 8>(
@@ -209,30 +233,49 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_simt_kernel(const pbk_gdn_d
 }
 
 template <typename TIn, typename TOut, int DVB>
-cudaError_t launch_split(const pbk_gdn_desc& d, cudaStream_t st) {
+cudaError_t launch_split(const pbk_gdn_desc& d, const ChunkAux& aux, cudaStream_t st) {
   auto kern = gdn_prefill_simt_kernel<TIn, TOut, DVB>;
   const int bytes = (int)sizeof(Smem<DVB>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(D / DVB, (unsigned)((int64_t)d.batch * d.hv)), NT, bytes, st>>>(d);
+  kern<<<dim3(D / DVB, (unsigned)((int64_t)d.batch * d.hv)), NT, bytes, st>>>(d, aux);
   return cudaGetLastError();
 }
 
 template <typename TIn, typename TOut>
-cudaError_t launch_types(const pbk_gdn_desc& d, cudaStream_t st) {
+cudaError_t launch_types(const pbk_gdn_desc& d, const ChunkAux& aux, cudaStream_t st) {
   // Few chains: split the value columns four ways so more SMs work; many: two.
-  if ((int64_t)d.batch * d.hv * 2 < 148) return launch_split<TIn, TOut, 32>(d, st);
-  return launch_split<TIn, TOut, 64>(d, st);
+  if ((int64_t)d.batch * d.hv * 2 < 148) return launch_split<TIn, TOut, 32>(d, aux, st);
+  return launch_split<TIn, TOut, 64>(d, aux, st);
 }
 
 }  // namespace
 
-cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st) {
+cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st, const pbk_view* gc,
+                                    const pbk_view* ta) {
+  ChunkAux aux{};
+  if (gc != nullptr) {
+    aux.gc = static_cast<float*>(const_cast<void*>(gc->data));
+    aux.gc_sb = gc->stride_b;
+    aux.gc_st = gc->stride_t;
+    aux.gc_sh = gc->stride_h;
+  }
+  if (ta != nullptr) {
+    aux.ta = const_cast<void*>(ta->data);
+    aux.ta_sb = ta->stride_b;
+    aux.ta_st = ta->stride_t;
+    aux.ta_sh = ta->stride_h;
+    aux.ta_dtype = ta->dtype;
+  }
   const bool in_bf16 = d.q.dtype == PBK_BF16, out_bf16 = d.o.dtype == PBK_BF16;
-  if (in_bf16 && out_bf16) return launch_types<__nv_bfloat16, __nv_bfloat16>(d, st);
-  if (in_bf16) return launch_types<__nv_bfloat16, float>(d, st);
-  if (out_bf16) return launch_types<float, __nv_bfloat16>(d, st);
-  return launch_types<float, float>(d, st);
+  if (in_bf16 && out_bf16) return launch_types<__nv_bfloat16, __nv_bfloat16>(d, aux, st);
+  if (in_bf16) return launch_types<__nv_bfloat16, float>(d, aux, st);
+  if (out_bf16) return launch_types<float, __nv_bfloat16>(d, aux, st);
+  return launch_types<float, float>(d, aux, st);
+}
+
+cudaError_t launch_gdn_prefill_simt(const pbk_gdn_desc& d, cudaStream_t st) {
+  return launch_gdn_prefill_simt(d, st, nullptr, nullptr);
 }
 
 }  // namespace pbk

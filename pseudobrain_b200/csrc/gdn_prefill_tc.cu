@@ -334,6 +334,13 @@ struct SolveArgs {
   const int32_t* cu_seqlens;
   const int32_t* chunk_off;
   int num_seqs;
+  // optional chunk outputs (pbk_gdn_prefill_aux): the in-chunk cumulative g (fp32) and the rows
+  // of T = (I + A)^-1, [B, T, Hv] and [B, T, Hv, 64] views; null: not written
+  float* gc;
+  int64_t gc_sb, gc_st, gc_sh;
+  void* ta;
+  int64_t ta_sb, ta_st, ta_sh;
+  int ta_dtype;
 };
 
 // Rows [t0, t0 + len) of packed sequence s, clamped into [0, T] (offsets out of order or out of
@@ -457,6 +464,11 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
     for (int o = 1; o < 32; o <<= 1) {
       const float y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
+    }
+    if (p.gc != nullptr) {  // the in-chunk cumulative g (natural log units)
+      float* gcp = p.gc + b * p.gc_sb + tg * p.gc_st + h * p.gc_sh;
+      if (t < len) gcp[0] = incl - pair + g0;
+      if (t + 1 < len) gcp[p.gc_st] = incl;
     }
     const float c0 = (incl - pair + g0) * kLog2e, c1 = incl * kLog2e;
     const float ga0 = exp2f(c0), ga1 = exp2f(c1);
@@ -615,6 +627,22 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
       } else {
 #pragma unroll
         for (int e = 0; e < 16; ++e) v[e] = 0.f;
+      }
+      if (p.ta != nullptr && m * C + t < len) {  // row t of T, columns 16 cb ..
+        const int64_t o = b * p.ta_sb + (int64_t)(t0 + m * C + t) * p.ta_st + h * p.ta_sh + 16 * cb;
+        if (p.ta_dtype == PBK_BF16) {
+          uint4 w[2];
+          uint32_t* wp = reinterpret_cast<uint32_t*>(w);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) wp[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
+          *reinterpret_cast<uint4*>(static_cast<bf16*>(p.ta) + o) = w[0];
+          *reinterpret_cast<uint4*>(static_cast<bf16*>(p.ta) + o + 8) = w[1];
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            *reinterpret_cast<float4*>(static_cast<float*>(p.ta) + o + 4 * e) =
+                make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+        }
       }
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
@@ -1249,8 +1277,18 @@ size_t gdn_prefill_tc_workspace(const pbk_gdn_desc& d) {
 
 // The chunk solve of every (sequence, chunk, value head) of d into ws
 // (gdn_prefill_tc_workspace(d) bytes, 16-byte aligned).
-cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t st) {
+cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t st, const pbk_view* gc,
+                                   const pbk_view* ta) {
   SolveArgs sa;
+  sa.gc = gc != nullptr ? static_cast<float*>(const_cast<void*>(gc->data)) : nullptr;
+  sa.gc_sb = gc ? gc->stride_b : 0;
+  sa.gc_st = gc ? gc->stride_t : 0;
+  sa.gc_sh = gc ? gc->stride_h : 0;
+  sa.ta = ta != nullptr ? const_cast<void*>(ta->data) : nullptr;
+  sa.ta_sb = ta ? ta->stride_b : 0;
+  sa.ta_st = ta ? ta->stride_t : 0;
+  sa.ta_sh = ta ? ta->stride_h : 0;
+  sa.ta_dtype = ta ? ta->dtype : PBK_F32;
   sa.k = static_cast<const bf16*>(d.k.data);
   sa.k_sb = d.k.stride_b;
   sa.k_st = d.k.stride_t;
@@ -1301,7 +1339,7 @@ cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, bool so
   fill_args(a, d);
   a.solve = static_cast<const uint8_t*>(solve_ws);
   if (solve_ws != nullptr && !solved) {
-    cudaError_t e = launch_gdn_chunk_solve(d, solve_ws, st);
+    cudaError_t e = launch_gdn_chunk_solve(d, solve_ws, st, nullptr, nullptr);
     if (e != cudaSuccess) return e;
   }
   const dim3 grid((unsigned)((int64_t)d.batch * d.hv));
@@ -1355,6 +1393,8 @@ cudaError_t launch_gdn_prefill_varlen(const pbk_gdn_desc& d, const int32_t* cu_s
   sa.cu_seqlens = cu_seqlens;
   sa.chunk_off = chunk_off;
   sa.num_seqs = num_seqs;
+  sa.gc = nullptr;
+  sa.ta = nullptr;
   if ((e = cudaFuncSetAttribute(gdn_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)sizeof(SolveSmem))) != cudaSuccess)
     return e;

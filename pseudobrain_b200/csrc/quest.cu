@@ -341,22 +341,62 @@ __device__ __forceinline__ float canonical_row_sum(const float* qrow, const bf16
   return acc;
 }
 
+__device__ __forceinline__ float ordered_key_inv(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 // Canonical keys of the listed pages: ckey[u] = ordered key of the max over the rpg query
-// rows of page list[u]'s canonical sum, one (page, row) pair per thread.
+// rows of page list[u]'s canonical sum. One warp per page: lanes 0-15 load kmax and lanes
+// 16-31 kmin (8 dims each, one load for the whole page), and lane r runs row r's sum in
+// dimension order, taking each bound value from its lane with a shuffle.
 __device__ __forceinline__ void canonical_keys(const RefineArgs& rf, const float (*qs)[kD], int rpg, int h,
                                                const int32_t* list, int n, uint32_t* ckey) {
-  for (int u = threadIdx.x; u < n; u += kTopkThreads) ckey[u] = 0u;
-  __syncthreads();
-  for (int w = threadIdx.x; w < n * rpg; w += kTopkThreads) {
-    const int u = w / rpg, r = w % rpg;
-    const int64_t off = h * rf.bnd_stride_kv + (int64_t)list[u] * rf.bnd_stride_p;
-    atomicMax(&ckey[u], ordered_key(canonical_row_sum(qs[r], rf.kmax + off, rf.kmin + off)));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int u = warp; u < n; u += kTopkWarps) {
+    const int64_t off = h * rf.bnd_stride_kv + (int64_t)list[u] * rf.bnd_stride_p + 8 * (lane & 15);
+    const uint4 raw = *reinterpret_cast<const uint4*>((lane < 16 ? rf.kmax : rf.kmin) + off);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    float best = -INFINITY;
+    for (int r0 = 0; r0 < rpg; r0 += 32) {
+      const float* qrow = qs[min(r0 + lane, rpg - 1)];
+      float acc = 0.f;
+      for (int d0 = 0; d0 < kD; d0 += 8) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float qv = qrow[d0 + j];
+          const uint32_t wv = __shfl_sync(0xffffffffu, w[j >> 1], (qv > 0.f ? 0 : 16) + (d0 >> 3));
+          acc = fmaf(qv, __uint_as_float((j & 1) ? (wv & 0xffff0000u) : (wv << 16)), acc);
+        }
+      }
+      if (r0 + lane < rpg) best = fmaxf(best, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if (lane == 0) ckey[u] = ordered_key(best);
   }
   __syncthreads();
 }
 
-__device__ __forceinline__ float ordered_key_inv(uint32_t k) {
-  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+// The final selection from the band: the n_in pages above it are in; of the nb band pages
+// (ckey, page) the need = k - n_in best by canonical key (ties to the lowest page) join them:
+// key[pos[u]] = MAX for those, 0 for the rest. Returns false (nothing written) when the band
+// is too large for the pairwise ranking.
+constexpr int kRankCap = 1024;
+__device__ __forceinline__ bool rank_band(const uint32_t* ckey, const int32_t* page, int nb, int need,
+                                          const int32_t* pos, uint32_t* key) {
+  if (nb > kRankCap) return false;
+  for (int u = threadIdx.x; u < nb; u += kTopkThreads) {
+    const uint32_t c = ckey[u];
+    const int p = page[u];
+    int rank = 0;
+    for (int v = 0; v < nb; ++v) {
+      const uint32_t cv = ckey[v];
+      rank += (cv > c) || (cv == c && page[v] < p);
+    }
+    key[pos != nullptr ? pos[u] : u] = rank < need ? 0xFFFFFFFFu : 0u;
+  }
+  __syncthreads();
+  return true;
 }
 
 struct TopkSmem {
@@ -370,12 +410,14 @@ struct TopkSmem {
   float red[kTopkWarps];
   float qs_l1[kTopkWarps];
   float eps2;                 // twice the error bound of the row's scores
-  int n_unc;
+  int n_unc, n_in;
 };
 
-// The refinement's set-up: the group's query rows into shared memory and eps2 = 2 eps,
-// eps = 2^kRefineEpsExp max_r ||q_r||_1 max|bound| over the key head's tiles.
-__device__ __forceinline__ void refine_setup(const RefineArgs& rf, int row, TopkSmem& ts) {
+// The refinement's set-up, in two halves around a barrier the caller places: refine_load
+// issues the loads (the group's query rows into shared memory; per warp, the largest bound
+// magnitude of the key head's tiles), refine_finish forms eps2 = 2 eps,
+// eps = 2^kRefineEpsExp max_r ||q_r||_1 max|bound|.
+__device__ __forceinline__ void refine_load(const RefineArgs& rf, int row, TopkSmem& ts) {
   const int n = row / rf.kv, h = row % rf.kv, rpg = rf.t * rf.groups;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < rpg * kD; e += kTopkThreads) {
@@ -386,9 +428,14 @@ __device__ __forceinline__ void refine_setup(const RefineArgs& rf, int row, Topk
   float babs = 0.f;
   for (int i = threadIdx.x; i < rf.abs_per_kv; i += kTopkThreads)
     babs = fmaxf(babs, rf.tile_abs[(int64_t)h * rf.abs_per_kv + i]);
-  __syncthreads();
-  // this warp's largest ||q_r||_1 times the largest bound magnitude it read; the max over
-  // warps of both is taken apart (a product of maxima, not a max of products)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) babs = fmaxf(babs, __shfl_xor_sync(0xffffffffu, babs, o));
+  if (lane == 0) ts.red[warp] = babs;
+}
+
+__device__ __forceinline__ void refine_finish(const RefineArgs& rf, TopkSmem& ts) {
+  const int rpg = rf.t * rf.groups, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // this warp's largest ||q_r||_1; the product of the two maxima bounds every page
   float l1 = 0.f;
   for (int r = warp; r < rpg; r += kTopkWarps) {
     float a = 0.f;
@@ -396,12 +443,7 @@ __device__ __forceinline__ void refine_setup(const RefineArgs& rf, int row, Topk
     for (int j = 0; j < kD / 32; ++j) a += fabsf(ts.qs[r][lane + 32 * j]);
     l1 = fmaxf(l1, warp_sum(a));
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) babs = fmaxf(babs, __shfl_xor_sync(0xffffffffu, babs, o));
-  if (lane == 0) {
-    ts.red[warp] = babs;
-    ts.qs_l1[warp] = l1;
-  }
+  if (lane == 0) ts.qs_l1[warp] = l1;
   __syncthreads();
   if (threadIdx.x == 0) {
     float bm = 0.f, lm = 0.f;
@@ -447,13 +489,17 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
   const uint32_t lt = (1u << lane) - 1u;
   const bool refine = rf.q != nullptr;
   const int rh = refine ? row % rf.kv : 0, rpg = refine ? rf.t * rf.groups : 0;
-  if (refine) refine_setup(rf, row, ts);
-  const float eps2 = refine ? ts.eps2 : 0.f;
-  uint32_t prefix, kk;
-  if (segmax != nullptr && nseg >= k && nseg <= kSegCap) {
+  const bool seg_path = segmax != nullptr && nseg >= k && nseg <= kSegCap;
+  if (refine) refine_load(rf, row, ts);
+  if (seg_path) {
     const float* sg = segmax + (int64_t)row * nseg;
     for (int i = threadIdx.x; i < nseg; i += kTopkThreads) ts.seg_key[i] = ordered_key(sg[i]);
-    __syncthreads();
+  }
+  __syncthreads();
+  if (refine) refine_finish(rf, ts);
+  const float eps2 = refine ? ts.eps2 : 0.f;
+  uint32_t prefix, kk;
+  if (seg_path) {
     // tau: a lower bound of the k-th largest segment maximum (two digits: any bound at or
     // below it keeps every top-k page among the candidates, the exact select comes later),
     // lowered by the refinement band so the band's pages are candidates too
@@ -525,29 +571,42 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
         }
         __syncthreads();
         radix_select([&](int i) { return ts.cand_key[i]; }, ptotal, (uint32_t)k, ss, prefix, kk);
-        if (refine) {
-          // the band's pages: listed (any order), re-scored per (page, query row), written back
+        const uint32_t ninf = ordered_key(-INFINITY);
+        if (refine && prefix != ninf) {  // (a -inf threshold: every finite page is in, exactly)
+          // the band's pages: listed (any order) with their page indices, re-scored in the
+          // canonical order; the pages above the band are counted
           uint32_t lo, hi;
           refine_band(prefix, eps2, lo, hi);
-          const uint32_t ninf = ordered_key(-INFINITY);
-          if (threadIdx.x == 0) ts.n_unc = 0;
+          if (threadIdx.x == 0) ts.n_unc = ts.n_in = 0;
           __syncthreads();
-          for (int i = threadIdx.x; i < ptotal; i += kTopkThreads) {
-            const uint32_t key = ts.cand_key[i];
-            if (key == ninf) continue;  // masked: exact already
-            if (key > hi) ts.cand_key[i] = 0xFFFFFFFFu;
-            else if (key >= lo) ts.cseg[atomicAdd(&ts.n_unc, 1)] = i;
-            else ts.cand_key[i] = 0u;
+          for (int base = 0; base < ptotal; base += kTopkThreads) {
+            const int i = base + threadIdx.x;
+            const uint32_t key = i < ptotal ? ts.cand_key[i] : ninf;
+            const bool above = key != ninf && key > hi;
+            const uint32_t ba = __ballot_sync(0xffffffffu, above);
+            if (lane == 0 && ba) atomicAdd(&ts.n_in, __popc(ba));
+            if (key == ninf) continue;  // masked (or past the end): exact already
+            if (above) ts.cand_key[i] = 0xFFFFFFFFu;
+            else if (key >= lo) {
+              const int at = atomicAdd(&ts.n_unc, 1);
+              ts.cseg[at] = i;
+              ts.band_page[at] = ts.cand_idx[i];
+            } else {
+              ts.cand_key[i] = 0u;
+            }
           }
           __syncthreads();
           const int nu = ts.n_unc;
-          // the band's pages (cseg holds candidate positions): their page indices into cand_page
-          for (int u = threadIdx.x; u < nu; u += kTopkThreads) ts.band_page[u] = ts.cand_idx[ts.cseg[u]];
-          __syncthreads();
           canonical_keys(rf, ts.qs, rpg, rh, ts.band_page, nu, ts.seg_key);
-          for (int u = threadIdx.x; u < nu; u += kTopkThreads) ts.cand_key[ts.cseg[u]] = ts.seg_key[u];
-          __syncthreads();
-          radix_select([&](int i) { return ts.cand_key[i]; }, ptotal, (uint32_t)k, ss, prefix, kk);
+          if (rank_band(ts.seg_key, ts.band_page, nu, k - ts.n_in, ts.cseg, ts.cand_key)) {
+            // exactly k keys are MAX now: collect them in index order
+            prefix = 0xFFFFFFFFu;
+            kk = (uint32_t)k;
+          } else {
+            for (int u = threadIdx.x; u < nu; u += kTopkThreads) ts.cand_key[ts.cseg[u]] = ts.seg_key[u];
+            __syncthreads();
+            radix_select([&](int i) { return ts.cand_key[i]; }, ptotal, (uint32_t)k, ss, prefix, kk);
+          }
         }
         collect_in_order([&](int i) { return ts.cand_key[i]; }, [&](int i) { return ts.cand_idx[i]; }, ptotal,
                          prefix, kk, ss, out);
@@ -556,24 +615,30 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
     }
   }
   radix_select([&](int i) { return ordered_key(s[i]); }, npages, (uint32_t)k, ss, prefix, kk);
-  if (refine) {
+  const uint32_t ninf = ordered_key(-INFINITY);
+  if (refine && prefix != ninf) {  // (a -inf threshold: every finite page is in, exactly)
     // whole row: the band's pages listed in index order, their canonical keys computed once
-    // (read back by binary search); a band too large for shared memory computes them where
-    // they are read
+    // (read back by binary search) and, for a band of at most kRankCap pages, ranked into
+    // MAX / 0 selection keys; a band too large for shared memory computes its keys where they
+    // are read
     uint32_t lo, hi;
     refine_band(prefix, eps2, lo, hi);
-    const uint32_t ninf = ordered_key(-INFINITY);
     auto in_band = [&](uint32_t key) { return key != ninf && key >= lo && key <= hi; };
     const int R = warp_range(npages);
     const int lo_i = min(warp * R, npages), hi_i = min(lo_i + R, npages);
-    int cnt = 0;
+    if (threadIdx.x == 0) ts.n_in = 0;
+    int cnt = 0, above = 0;
     for (int j = lo_i; j < hi_i; j += 32) {
       const int i = j + lane;
-      cnt += __popc(__ballot_sync(0xffffffffu, i < hi_i && in_band(ordered_key(s[i]))));
+      const uint32_t key = i < hi_i ? ordered_key(s[i]) : ninf;
+      cnt += __popc(__ballot_sync(0xffffffffu, in_band(key)));
+      above += __popc(__ballot_sync(0xffffffffu, key != ninf && key > hi));
     }
     int pos, zero, nb;
-    warp_bases(cnt, 0, ss, pos, zero, nb);
+    warp_bases(cnt, 0, ss, pos, zero, nb);  // (its barriers also order the n_in reset)
+    if (lane == 0 && above) atomicAdd(&ts.n_in, above);
     const bool listed = nb <= kSegCap;
+    bool ranked = false;
     if (listed) {
       for (int j = lo_i; j < hi_i; j += 32) {
         const int i = j + lane;
@@ -584,6 +649,8 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
       }
       __syncthreads();
       canonical_keys(rf, ts.qs, rpg, rh, ts.cseg, nb, ts.seg_key);
+      ranked = rank_band(ts.seg_key, ts.cseg, nb, k - ts.n_in, nullptr,
+                         reinterpret_cast<uint32_t*>(ts.band_page));
     }
     auto key2 = [&](int i) -> uint32_t {
       const uint32_t key = ordered_key(s[i]);
@@ -597,14 +664,19 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
           if (ts.cseg[m] < i) a = m + 1;
           else b = m;
         }
-        return ts.seg_key[a];
+        return ranked ? reinterpret_cast<const uint32_t*>(ts.band_page)[a] : ts.seg_key[a];
       }
       const int64_t off = rh * rf.bnd_stride_kv + (int64_t)i * rf.bnd_stride_p;
       float best = -INFINITY;
       for (int r = 0; r < rpg; ++r) best = fmaxf(best, canonical_row_sum(ts.qs[r], rf.kmax + off, rf.kmin + off));
       return ordered_key(best);
     };
-    radix_select(key2, npages, (uint32_t)k, ss, prefix, kk);
+    if (ranked) {  // exactly k keys are MAX: collect them in index order
+      prefix = 0xFFFFFFFFu;
+      kk = (uint32_t)k;
+    } else {
+      radix_select(key2, npages, (uint32_t)k, ss, prefix, kk);
+    }
     collect_in_order(key2, [&](int i) { return i; }, npages, prefix, kk, ss, out);
     return;
   }
