@@ -522,54 +522,59 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
     (16 key / 32 value heads) is split by value head over the ranks, and within a rank along
     T (segments chained by the segment scan) so a few heads still fill the SMs; the
     sliding-window attention branch (32 query / 8 key heads, window 4096) is split by key
-    head. Each branch's [T, heads/N * 128] output is all-gathered (NCCL) into a head-major
-    [N, T, heads/N * 128] buffer, the hidden-4096 layout the output projection reads.
-    Strong scaling: the job is one layer pass whatever N."""
+    head. Each branch's output is all-gathered (NCCL) into head-major [N, rows, heads/N * 128]
+    buffers, the hidden-4096 layout the output projection reads: the attention in query
+    chunks whose gathers run while the next chunk computes, then the GDN branch and its
+    gather (sharding.hybrid_layer_sharded). Strong scaling: the job is one layer pass
+    whatever N; at N > 1 rank 0 also times the unsharded layer (all heads on one GPU) for
+    the strong-scaling efficiency t1 / (N tN)."""
     import torch
     import torch.distributed as dist
     from pseudobrain_b200.gdn_prefill import auto_segments, gdn_prefill_segmented
+    from pseudobrain_b200.sharding import hybrid_layer_sharded
     from pseudobrain_b200.synthetic import gdn_inputs
     from pseudobrain_b200.transplant import window_attention_
     H = HYBRID_HEADS
     t = HYBRID[args.size]["seqlen"]
     if H["hv"] % world or H["kv"] % world:
         return None
-    hv, hk, heads, kv = H["hv"] // world, H["hk"] // world, H["heads"] // world, H["kv"] // world
-    x = gdn_inputs(1, t, hk, hv, device=dev, seed=4 + 1000 * rank)
-    o_gdn = torch.empty(1, t, hv, H["d"], device=dev, dtype=torch.bfloat16)
-    gen = torch.Generator(device=dev).manual_seed(5 + 1000 * rank)
-    qa = torch.randn(1, t, heads, H["d"], device=dev, generator=gen).to(torch.bfloat16)
-    ka = torch.randn(1, t, kv, H["d"], device=dev, generator=gen).to(torch.bfloat16)
-    va = torch.randn(1, t, kv, H["d"], device=dev, generator=gen).to(torch.bfloat16)
-    o_swa = torch.empty_like(qa)
-    gath_gdn = torch.empty(world * t, hv * H["d"], device=dev, dtype=torch.bfloat16) if world > 1 else None
-    gath_swa = torch.empty(world * t, heads * H["d"], device=dev, dtype=torch.bfloat16) if world > 1 else None
-    segs = auto_segments(1, hv, t)
 
-    def gdn():
-        gdn_prefill_segmented(x["q"], x["k"], x["v"], x["g"], x["beta"], x["scale"], None, segments=segs, o=o_gdn)
+    def shard_inputs(nshard, seed):
+        hv, hk, heads, kv = H["hv"] // nshard, H["hk"] // nshard, H["heads"] // nshard, H["kv"] // nshard
+        x = gdn_inputs(1, t, hk, hv, device=dev, seed=seed)
+        gen = torch.Generator(device=dev).manual_seed(seed + 1)
+        qa = torch.randn(1, t, heads, H["d"], device=dev, generator=gen).to(torch.bfloat16)
+        ka = torch.randn(1, t, kv, H["d"], device=dev, generator=gen).to(torch.bfloat16)
+        va = torch.randn(1, t, kv, H["d"], device=dev, generator=gen).to(torch.bfloat16)
+        return x, qa, ka, va
 
-    def swa():
-        window_attention_(qa, ka, va, o_swa, H["window"], 0, H["d"] ** -0.5)
+    x, qa, ka, va = shard_inputs(world, 4 + 1000 * rank)
+    hv, heads = H["hv"] // world, H["heads"] // world
+    scale = H["d"] ** -0.5
 
-    def gather():
-        if world > 1:
-            dist.all_gather_into_tensor(gath_gdn, o_gdn.view(t, -1))
-            dist.all_gather_into_tensor(gath_swa, o_swa.view(t, -1))
-
-    def step():  # the GDN branch's all-gather runs under the attention branch
-        gdn()
-        w = dist.all_gather_into_tensor(gath_gdn, o_gdn.view(t, -1), async_op=True) if world > 1 else None
-        swa()
-        if world > 1:
-            dist.all_gather_into_tensor(gath_swa, o_swa.view(t, -1))
-            w.wait()
+    def step():
+        hybrid_layer_sharded(x, qa, ka, va, H["window"], scale)
 
     steps = max(3, min(args.steps, 5))
     t_step = timed(step, steps, 3) / steps
-    t_gdn = timed(gdn, 2, 1) / 2
-    t_swa = timed(swa, 2, 1) / 2
-    t_ag = timed(gather, 2, 1) / 2 if world > 1 else 0.0
+    o_gdn = torch.empty(1, t, hv, H["d"], device=dev, dtype=torch.bfloat16)
+    o_swa = torch.empty_like(qa)
+    segs = auto_segments(1, hv, t)
+    t_gdn = timed(lambda: gdn_prefill_segmented(x["q"], x["k"], x["v"], x["g"], x["beta"], x["scale"], None,
+                                                segments=segs, o=o_gdn), 2, 1) / 2
+    t_swa = timed(lambda: window_attention_(qa, ka, va, o_swa, H["window"], 0, scale), 2, 1) / 2
+    t_ag = 0.0
+    if world > 1:
+        gath_gdn = torch.empty(world * t, hv * H["d"], device=dev, dtype=torch.bfloat16)
+        gath_swa = torch.empty(world * t, heads * H["d"], device=dev, dtype=torch.bfloat16)
+
+        def gather():
+            dist.all_gather_into_tensor(gath_gdn, o_gdn.view(t, -1))
+            dist.all_gather_into_tensor(gath_swa, o_swa.view(t, -1))
+
+        t_ag = timed(gather, 2, 1) / 2
+        del gath_gdn, gath_swa
+    del o_gdn, o_swa
     gdn_flops = t * H["hv"] * prefill_flops_per_token_head(64, H["d"])
     swa_flops = 4 * H["d"] * swa_pairs(t, H["window"]) * H["heads"]
     per_gpu = (gdn_flops + swa_flops) / world
@@ -578,7 +583,7 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         "metric": "hybrid layer tok/s (config 4)", "value": t / t_step, "unit": "tok/s",
         "per_gpu": t / t_step / world, "scaling": "strong", "ms_per_step": t_step * 1e3,
         "config": {"seqlen": t, "gdn_heads_per_gpu": hv, "gdn_segments": segs, "swa_q_heads_per_gpu": heads,
-                   "window": H["window"], "size": args.size},
+                   "window": H["window"], "size": args.size, "swa_query_chunks": 8},
         "roofline": {"bound": "tensor", "achieved": per_gpu / t_step / 1e12, "peak": pk["tc"],
                      "unit": "TFLOP/s", "frac": per_gpu / t_step / 1e12 / pk["tc"],
                      "traffic": None, "peak_source": f"{pk['src']} bf16 burst (timed regions under a second)"},
@@ -586,11 +591,39 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         "swa": {"ms": t_swa * 1e3, "tflops": swa_flops / world / t_swa / 1e12,
                 "frac": swa_flops / world / t_swa / 1e12 / pk["tc"]},
         "e2e": None,
-        "gpu_launches": steps * (1 + 4 + 1 + 1),  # one chunk solve, 4 recurrence runs, scan, attention
+        "gpu_launches": steps * (8 + 1 + 4 + 1),  # attention chunks, chunk solve, 4 recurrence runs, scan
     }
     if world > 1:
+        # the gathers timed alone: their share of the step, and what the overlap hid
         out["all_gather"] = {"ms": t_ag * 1e3, "bytes_received_per_gpu": ag_bytes,
-                             "gbps": ag_bytes / t_ag / 1e9 if t_ag > 0 else None}
+                             "gbps": ag_bytes / t_ag / 1e9 if t_ag > 0 else None,
+                             "share_of_step_if_serial": t_ag / (t_ag + t_gdn + t_swa)}
+        # strong scaling: the unsharded layer (all heads) on rank 0 while the others wait
+        t1 = None
+        del x, qa, ka, va
+        torch.cuda.empty_cache()
+        if rank == 0:
+            x1, qa1, ka1, va1 = shard_inputs(1, 4)
+
+            def step1():
+                hybrid_layer_sharded(x1, qa1, ka1, va1, H["window"], scale, gather=False)
+
+            step1()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(2):
+                step1()
+            e1.record()
+            torch.cuda.synchronize()
+            t1 = e0.elapsed_time(e1) / 2 / 1e3
+            del x1, qa1, ka1, va1
+            torch.cuda.empty_cache()
+        dist.barrier()
+        if t1 is not None:
+            out["strong_scaling"] = {"t1_ms": t1 * 1e3, "tN_ms": t_step * 1e3, "n": world,
+                                     "efficiency": t1 / (world * t_step),
+                                     "note": "t1: the same layer, all 32/32 heads on one GPU (rank 0), no exchange"}
     return out
 
 

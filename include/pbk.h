@@ -311,7 +311,7 @@ PBK_API size_t pbk_quest_attend_workspace(const pbk_quest_desc* desc);
  * The selection is bit-exact with respect to one fixed order: each row's fp32 sum runs
  * over d = 0 .. 127 in order (products of two bf16 values are exact in fp32). Up to 64
  * query rows per key head the scores come from the tensor cores, whose sums differ from
- * that order by at most 2^-12 ||q_r||_1 max|bound|; the top-k re-scores every page within
+ * that order by at most 2^-14 ||q_r||_1 max|bound|; the top-k re-scores every page within
  * twice that of its threshold in the fixed order, so the pages equal the fixed order's
  * selection. desc->scores (when given) receives the tensor-core scores. */
 PBK_API int pbk_quest_select(const pbk_quest_desc* desc, void* workspace, size_t workspace_bytes, void* stream);
@@ -324,7 +324,7 @@ PBK_API int pbk_quest_select_parts(const pbk_quest_desc* desc, int32_t parts, vo
 /* Largest number of page scores (nq * kv * (n_arch / page)) pbk_quest_select_noalloc
  * can hold: 4,194,304 fp32 = 16 MiB, enough for 8 query groups x 8 key heads over a
  * 1M-token archive in 16-token pages. Its array also holds the per-32-page and per-128-
- * page maxima (16.8 MiB in all). */
+ * page maxima (17.0 MiB in all). */
 #define PBK_QUEST_NOALLOC_MAX_SCORES 4194304
 
 /* pbk_quest_select for callers that cannot allocate device memory. This entry point has
@@ -332,7 +332,7 @@ PBK_API int pbk_quest_select_parts(const pbk_quest_desc* desc, int32_t parts, vo
  * engine that has reserved the free HBM for its KV cache, or a foreign-language caller
  * with no handle on the framework's allocator): for them a workspace allocation fails or
  * stalls the device. This variant takes no workspace: the page scores and their per-32-
- * page maxima and the per-tile bound magnitudes go to a fixed 16.8 MiB array that libpbk
+ * page maxima and the per-tile bound magnitudes go to a fixed 17.0 MiB array that libpbk
  * places in device memory (every GPU that loads the library holds it until the process
  * exits); when desc->scores is given, the scores go there instead. It calls no allocator.
  * Problems with more than PBK_QUEST_NOALLOC_MAX_SCORES scores, or whose maxima alone

@@ -312,10 +312,14 @@ struct RefineArgs {
   int kv, groups, t;
 };
 
-// Relative weight of the error bound: the fp32 rounding of a 256-term tensor-core sum and of
-// the 128-term canonical sum are each below 2^-15 ||q||_1 max|bound|; 2^-12 leaves a factor
-// of four on their sum.
-constexpr int kRefineEpsExp = -12;
+// Relative weight of the error bound. Each page score is a sum of 256 exact products whose
+// magnitudes add up to at most U = ||q_r||_1 max|bound|. Every partial sum, and so every
+// rounding step, is at most U in magnitude; the tensor cores round each of the 256 additions
+// once (possibly by truncation: one ulp), so their sum differs from the exact one by at most
+// 256 * 2^-23 U = 2^-15 U, and the canonical fp32 sum by at most 128 * 2^-24 U = 2^-17 U.
+// 2^-14 U covers both (1.25 * 2^-15 U) with a margin of 1.6; the measured difference at
+// config 3 is 2^-23 U.
+constexpr int kRefineEpsExp = -14;
 
 __device__ __forceinline__ float canonical_row_sum(const float* qrow, const bf16* bmax, const bf16* bmin) {
   float acc = 0.f;
@@ -346,53 +350,59 @@ __device__ __forceinline__ float ordered_key_inv(uint32_t k) {
 }
 
 // Canonical keys of the listed pages: ckey[u] = ordered key of the max over the rpg query
-// rows of page list[u]'s canonical sum. One warp per page: lanes 0-15 load kmax and lanes
-// 16-31 kmin (8 dims each, one load for the whole page), and lane r runs row r's sum in
-// dimension order, taking each bound value from its lane with a shuffle.
+// rows of page list[u]'s canonical sum. The pages' bounds are staged in shared memory
+// kStagePages at a time (one coalesced 512-byte load per page: lanes 0-15 kmax, 16-31 kmin;
+// rows padded by 4 bytes so 32 pages sit in 32 banks), then one thread per (page, row) --
+// pages fastest within a warp, so a warp reads one query row as a broadcast -- runs the sum
+// in dimension order from shared memory.
+constexpr int kStagePages = 128;
+constexpr int kStageRow = 2 * kD + 2;  // bf16 per staged page: kmax | kmin | pad
 __device__ __forceinline__ void canonical_keys(const RefineArgs& rf, const float (*qs)[kD], int rpg, int h,
-                                               const int32_t* list, int n, uint32_t* ckey) {
+                                               const int32_t* list, int n, uint32_t* ckey, bf16* stage) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int u = warp; u < n; u += kTopkWarps) {
-    const int64_t off = h * rf.bnd_stride_kv + (int64_t)list[u] * rf.bnd_stride_p + 8 * (lane & 15);
-    const uint4 raw = *reinterpret_cast<const uint4*>((lane < 16 ? rf.kmax : rf.kmin) + off);
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    float best = -INFINITY;
-    for (int r0 = 0; r0 < rpg; r0 += 32) {
-      const float* qrow = qs[min(r0 + lane, rpg - 1)];
-      float acc = 0.f;
-      for (int d0 = 0; d0 < kD; d0 += 8) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float qv = qrow[d0 + j];
-          const uint32_t wv = __shfl_sync(0xffffffffu, w[j >> 1], (qv > 0.f ? 0 : 16) + (d0 >> 3));
-          acc = fmaf(qv, __uint_as_float((j & 1) ? (wv & 0xffff0000u) : (wv << 16)), acc);
-        }
-      }
-      if (r0 + lane < rpg) best = fmaxf(best, acc);
+  for (int u = threadIdx.x; u < n; u += kTopkThreads) ckey[u] = 0u;
+  for (int base = 0; base < n; base += kStagePages) {
+    const int np = min(kStagePages, n - base);
+    for (int u = warp; u < np; u += kTopkWarps) {
+      const int64_t off = h * rf.bnd_stride_kv + (int64_t)list[base + u] * rf.bnd_stride_p + 8 * (lane & 15);
+      const uint4 raw = *reinterpret_cast<const uint4*>((lane < 16 ? rf.kmax : rf.kmin) + off);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(stage + u * kStageRow + (lane < 16 ? 0 : kD) + 8 * (lane & 15));
+      dst[0] = raw.x, dst[1] = raw.y, dst[2] = raw.z, dst[3] = raw.w;  // 4-byte stores: rows are 4-aligned
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if (lane == 0) ckey[u] = ordered_key(best);
+    __syncthreads();
+    for (int w = threadIdx.x; w < np * rpg; w += kTopkThreads) {
+      const int u = w % np, r = w / np;
+      const bf16* bx = stage + u * kStageRow;
+      const float* qrow = qs[r];
+      float acc = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < kD; ++d) {
+        const float qv = qrow[d];
+        acc = fmaf(qv, __bfloat162float(bx[qv > 0.f ? d : kD + d]), acc);
+      }
+      atomicMax(&ckey[base + u], ordered_key(acc));
+    }
+    __syncthreads();
   }
-  __syncthreads();
 }
 
 // The final selection from the band: the n_in pages above it are in; of the nb band pages
 // (ckey, page) the need = k - n_in best by canonical key (ties to the lowest page) join them:
-// key[pos[u]] = MAX for those, 0 for the rest. Returns false (nothing written) when the band
-// is too large for the pairwise ranking.
+// key[pos[u]] (key[u] without pos) = MAX for those, 0 for the rest. Each page's rank is the
+// count of band pages ahead of it, on packed 64-bit keys (ckey high, ~page low: larger is
+// better). Returns false (nothing written) when the band is too large for this pairwise count.
 constexpr int kRankCap = 1024;
 __device__ __forceinline__ bool rank_band(const uint32_t* ckey, const int32_t* page, int nb, int need,
-                                          const int32_t* pos, uint32_t* key) {
+                                          const int32_t* pos, uint32_t* key, uint64_t* packed) {
   if (nb > kRankCap) return false;
+  for (int u = threadIdx.x; u < nb; u += kTopkThreads)
+    packed[u] = ((uint64_t)ckey[u] << 32) | (uint32_t)~page[u];
+  __syncthreads();
   for (int u = threadIdx.x; u < nb; u += kTopkThreads) {
-    const uint32_t c = ckey[u];
-    const int p = page[u];
+    const uint64_t c = packed[u];
     int rank = 0;
-    for (int v = 0; v < nb; ++v) {
-      const uint32_t cv = ckey[v];
-      rank += (cv > c) || (cv == c && page[v] < p);
-    }
+#pragma unroll 8
+    for (int v = 0; v < nb; ++v) rank += packed[v] > c;
     key[pos != nullptr ? pos[u] : u] = rank < need ? 0xFFFFFFFFu : 0u;
   }
   __syncthreads();
@@ -407,6 +417,7 @@ struct TopkSmem {
   int32_t cand_idx[kCandCap];
   float qs[kRefineRows][kD];  // the row's query rows (refinement)
   int32_t band_page[kCandCap]; // pages of the band (candidate path)
+  __align__(16) bf16 stage[kStagePages * kStageRow];  // staged bounds of band pages; packed rank keys
   float red[kTopkWarps];
   float qs_l1[kTopkWarps];
   float eps2;                 // twice the error bound of the row's scores
@@ -597,8 +608,9 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
           }
           __syncthreads();
           const int nu = ts.n_unc;
-          canonical_keys(rf, ts.qs, rpg, rh, ts.band_page, nu, ts.seg_key);
-          if (rank_band(ts.seg_key, ts.band_page, nu, k - ts.n_in, ts.cseg, ts.cand_key)) {
+          canonical_keys(rf, ts.qs, rpg, rh, ts.band_page, nu, ts.seg_key, ts.stage);
+          if (rank_band(ts.seg_key, ts.band_page, nu, k - ts.n_in, ts.cseg, ts.cand_key,
+                        reinterpret_cast<uint64_t*>(ts.stage))) {
             // exactly k keys are MAX now: collect them in index order
             prefix = 0xFFFFFFFFu;
             kk = (uint32_t)k;
@@ -648,9 +660,9 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
         pos += __popc(bc);
       }
       __syncthreads();
-      canonical_keys(rf, ts.qs, rpg, rh, ts.cseg, nb, ts.seg_key);
+      canonical_keys(rf, ts.qs, rpg, rh, ts.cseg, nb, ts.seg_key, ts.stage);
       ranked = rank_band(ts.seg_key, ts.cseg, nb, k - ts.n_in, nullptr,
-                         reinterpret_cast<uint32_t*>(ts.band_page));
+                         reinterpret_cast<uint32_t*>(ts.band_page), reinterpret_cast<uint64_t*>(ts.stage));
     }
     auto key2 = [&](int i) -> uint32_t {
       const uint32_t key = ordered_key(s[i]);

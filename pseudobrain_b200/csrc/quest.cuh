@@ -22,10 +22,10 @@ size_t quest_score_bytes(const pbk_quest_desc& d);
 size_t quest_select_floats(const pbk_quest_desc& d);
 // Floats of the fixed scratch of pbk_quest_select_noalloc: the largest allowed score count
 // plus its segment maxima (rows of at least 1024 pages keep ceil(pages / 32) of them) and
-// the tile bound magnitudes (one per 128 pages and key head: at most scores / 64 for rows
+// the tile bound magnitudes (two per 128 pages and key head: at most scores / 32 for rows
 // of at least 128 pages).
 constexpr size_t kNoAllocFloats = (size_t)PBK_QUEST_NOALLOC_MAX_SCORES + PBK_QUEST_NOALLOC_MAX_SCORES / 32 +
-                                  PBK_QUEST_NOALLOC_MAX_SCORES / 1024 + PBK_QUEST_NOALLOC_MAX_SCORES / 64;
+                                  PBK_QUEST_NOALLOC_MAX_SCORES / 1024 + PBK_QUEST_NOALLOC_MAX_SCORES / 32;
 size_t quest_partial_bytes(const pbk_quest_desc& d, int n_sink);
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st);
 cudaError_t launch_quest_select_parts(const pbk_quest_desc& d, float* scratch, int parts, cudaStream_t st);

@@ -14,8 +14,11 @@
 //   warps 2-9: two epilogue warpgroups, one per TMEM accumulator buffer (even / odd
 //              tiles): read D from TMEM, reduce per query group and store the scores; the
 //              group that meets a key head's first tile builds B for it.
-//   warp 10: the tile's largest bound magnitude max |kmax|, |kmin| (read from the staged
-//              tile in shared memory) into tile_abs. It bounds the
+//   warps 12-13: the tile's largest bound magnitude max |kmax|, |kmin| (read from the staged
+//              tile in shared memory, half each) into tile_abs. Warps 12 and 13 run on SM
+//              sub-partitions 0 and 1, beside the producer and MMA warps, which issue little
+//              (on sub-partition 2, beside two epilogue warps, this work slowed the kernel by
+//              15%); warps 10-11 have no role. It bounds the
 //              rounding error of the tensor-core sums, |D - exact| <= c ||q||_1 max|bound|,
 //              which the top-k uses to re-score the pages near its threshold in the
 //              canonical order (quest.cu), so the selection is bit-exact.
@@ -37,8 +40,9 @@ constexpr int kMaxRows = 64;                    // query rows per key head = MMA
 constexpr int kAtomBytes = kTileP * 128;        // [128 rows x 64 bf16] swizzled atom
 constexpr int kStageBytes = 4 * kAtomBytes;     // kmax d0-63 | kmax d64-127 | kmin d0-63 | kmin d64-127
 constexpr int kBAtomBytes = kMaxRows * 128;
-constexpr int kAbsWarps = 1;                    // warp 10: bound magnitude of each tile
-constexpr int kThreads = 320 + 32 * kAbsWarps;
+constexpr int kAbsWarps = 2;                    // warps 12-13: bound magnitudes of each tile
+constexpr int kAbsWarp0 = 12;
+constexpr int kThreads = 32 * (kAbsWarp0 + kAbsWarps);
 constexpr int kTmemCols = 2 * kMaxRows;         // two accumulator buffers
 
 struct __align__(1024) ScoreSmem {
@@ -54,7 +58,7 @@ struct ScoreArgs {
   int64_t q_stride_n, q_stride_t, q_stride_h;
   float* scores;
   float* segmax;  // max of every 32 consecutive pages per (group, key head), or null
-  float* tile_abs;  // [kv * tiles_per_kv] largest |bound| of each tile, or null
+  float* tile_abs;  // [kv * tiles_per_kv][kAbsWarps] largest |bound| of each tile half, or null
   int nseg;
   int* err;
   int nq, t, groups, kv, npages, rows, n_pad, tiles_per_kv, total_tiles;
@@ -198,13 +202,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (issued > 0 && !tc::mbar_wait(&sm.acc_full[(issued - 1) & 1], ((issued - 1) >> 1) & 1, 200000000ull))
         record_error(args.err, 6, sm);
     }
-  } else if (warp >= 10) {
-    // ---------------- bound magnitudes: warp 10 reads every stage once ----------------
+  } else if (warp >= kAbsWarp0) {
+    // ---------------- bound magnitudes: warps 12-13, half of every stage each ----------------
     // |x| of a bf16 is its bit pattern with the sign cleared, and for non-NaN values the
     // order of those patterns as unsigned integers is the order of |x|: a packed 16-bit
     // integer max over the staged bytes (their swizzled order does not matter).
     if (args.tile_abs != nullptr) {
-      const int aw = warp - 10;
+      const int aw = warp - kAbsWarp0;
       for (int i = 0; i < ntiles; ++i) {
         if (__any_sync(0xffffffffu, sm.abort)) break;  // warp-uniform exit
         const int s = i % kStages;
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else {
+  } else if (warp < 10) {
     // ---------------- epilogue: warps 2..9, group eg takes tiles i = eg, eg + 2, ... ----------------
     const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
     const int eg = (warp - 2) >> 2, etid = (threadIdx.x - 64) & 127;

@@ -102,3 +102,100 @@ def causal_attention_head_sharded(q, k, v, window=None, sinks=0, group=None, att
     dist.all_gather_into_tensor(o_all, o_loc.contiguous(), group=group)
     # [N, B, H/N, T, hd] -> [B, H, T, hd]
     return o_all.view((world,) + tuple(o_loc.shape)).transpose(0, 1).reshape(b, h, t, d)
+
+
+# ------------------------------------------------------------------------------------------
+# The hybrid layer (benchmark config 4) split over the ranks, with its all-gathers overlapped
+# ------------------------------------------------------------------------------------------
+def swa_chunk_plan(t: int, window: int, chunks: int, first: int | None = None) -> list[tuple[int, int, int]]:
+    """Query chunks [s, e) of a T-token sliding-window pass, each with the halo h of earlier
+    rows its queries read (s - h >= 0, h >= window - 1 unless the chunk starts earlier): the
+    rows [s - h, e) then form a self-contained window-attention problem whose last e - s rows
+    are exact. The first chunk is `first` rows (default T / (2 chunks)), so its output is
+    ready -- and its all-gather can start -- early; the rest split evenly. Row counts are
+    multiples of 128 (the attention kernel's query tile) except at T."""
+    if t <= 0:
+        return []
+    chunks = max(1, chunks)
+    first = first if first is not None else max(128, t // (2 * chunks))
+    first = min(t, -(-first // 128) * 128)
+    bounds = [0, first]
+    rest = t - first
+    if rest > 0:
+        n = max(1, chunks - 1)
+        step = -(-(-(-rest // n)) // 128) * 128
+        s = first
+        while s < t:
+            s = min(t, s + step)
+            bounds.append(s)
+    halo = -(-(window - 1) // 128) * 128 if window > 0 else None
+    plan = []
+    for s, e in zip(bounds[:-1], bounds[1:]):
+        h = s if halo is None else min(s, halo)
+        plan.append((s, e, h))
+    return plan
+
+
+def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: float, group=None, swa_chunks: int = 8,
+                         gdn=None, attention=None, gather: bool = True):
+    """One hybrid layer (GDN branch + sliding-window attention branch, pseudobrain/transplant.py
+    WindowedHybridLayer, benchmark config 4) on this rank's heads, with every branch output
+    all-gathered over `group` into the head-major layout the output projection reads.
+
+    gdn_in: this rank's GDN shard {q, k [1,T,hk/N,128], v [1,T,hv/N,128], g, beta [1,T,hv/N],
+    scale}; qa [1,T,H/N,128], ka, va [1,T,KV/N,128]: this rank's attention heads (window sinks
+    0). Order, chosen so the all-gathers (bound by each GPU's NVLink ingress) start early and
+    stay busy: the attention in query chunks (swa_chunk_plan; each chunk's rows gathered as
+    soon as they are written, on the communicator's stream, while the next chunk computes),
+    then the GDN branch (segmented over T) and its gather. Returns (gdn_all [N, T,
+    hv/N*128], [(s, e, swa_all [N, e - s, H/N*128]) for each chunk]). ``gdn(gdn_in, o)`` and
+    ``attention(q, k, v, o, window, scale)`` replace the CUDA kernels (CPU tests); gather=False
+    runs the layer on these heads alone (N = 1 layouts, no exchange)."""
+    world = dist.get_world_size(group) if (gather and dist.is_initialized()) else 1
+    if gdn is None:
+        from .gdn_prefill import auto_segments, gdn_prefill_segmented
+
+        def gdn(x, o):
+            segs = auto_segments(1, x["v"].shape[2], x["q"].shape[1])
+            gdn_prefill_segmented(x["q"], x["k"], x["v"], x["g"], x["beta"], x["scale"], None, segments=segs, o=o)
+    if attention is None:
+        from .transplant import window_attention_
+
+        def attention(q, k, v, o, win, scale):
+            window_attention_(q, k, v, o, win, 0, scale)
+    t = qa.shape[1]
+    heads, d = qa.shape[2], qa.shape[3]
+    works, swa_out = [], []
+    for s, e, h in swa_chunk_plan(t, window, swa_chunks):
+        rows = e - s + h
+        stage = torch.empty(1, rows, heads, d, dtype=qa.dtype, device=qa.device)
+        attention(qa[:, s - h:e], ka[:, s - h:e], va[:, s - h:e], stage, window, attn_scale)
+        mine = stage.view(rows, heads * d)[h:]  # this chunk's exact rows (contiguous)
+        if world > 1:
+            gathered = torch.empty(world * (e - s), heads * d, dtype=qa.dtype, device=qa.device)
+            works.append(dist.all_gather_into_tensor(gathered, mine, group=group, async_op=True))
+            swa_out.append((s, e, gathered.view(world, e - s, heads * d)))
+        else:
+            swa_out.append((s, e, mine.view(1, e - s, heads * d)))
+    hv = gdn_in["v"].shape[2]
+    o_gdn = torch.empty(1, t, hv, gdn_in["v"].shape[3], dtype=torch.bfloat16, device=qa.device)
+    gdn(gdn_in, o_gdn)
+    if world > 1:
+        gdn_all = torch.empty(world * t, hv * o_gdn.shape[-1], dtype=o_gdn.dtype, device=o_gdn.device)
+        works.append(dist.all_gather_into_tensor(gdn_all, o_gdn.view(t, -1), group=group, async_op=True))
+        gdn_all = gdn_all.view(world, t, -1)
+    else:
+        gdn_all = o_gdn.view(1, t, -1)
+    for w in works:
+        w.wait()
+    return gdn_all, swa_out
+
+
+def assemble_heads(pieces, t: int) -> torch.Tensor:
+    """[(s, e, [N, e - s, W])...] -> [T, N * W]: the gathered attention chunks in the hidden
+    layout (token-major, rank-major heads)."""
+    n, _, w = pieces[0][2].shape
+    out = torch.empty(t, n * w, dtype=pieces[0][2].dtype, device=pieces[0][2].device)
+    for s, e, x in pieces:
+        out[s:e] = x.permute(1, 0, 2).reshape(e - s, n * w)
+    return out

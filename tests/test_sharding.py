@@ -55,6 +55,9 @@ def _worker(rank, world, port, mode, outdir):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from pseudobrain_b200 import sharding
+        if mode == "hybrid":
+            _hybrid_worker(rank, world, outdir)
+            return
         if mode == "attention":
             q, k, v = _attn_inputs()
             o = sharding.causal_attention_head_sharded(q, k, v, 50, 3, attention=_oracle_attention)
@@ -102,3 +105,71 @@ def test_shard_maps():
         head_shard(32, 8, 16, 0)  # 2 value heads per rank would split a key head of 4
     with pytest.raises(ValueError):
         batch_shard(3, 2, 0)
+
+
+# ---- the hybrid layer pipeline (sharding.hybrid_layer_sharded) with CPU stand-ins -------------
+HYB_T, HYB_W = 700, 100
+
+
+def _hybrid_inputs():
+    """Full-layer inputs: GDN 2 key / 4 value heads, attention 4 query / 2 key heads, [1,T,H,D]."""
+    from tests.inputs import gdn_inputs
+    inp = gdn_inputs(51, 1, HYB_T, 2, 4)
+    x = {n: torch.from_numpy(inp[n]) for n in ("q", "k", "v", "g", "beta")}
+    x["scale"] = inp["scale"]
+    g = torch.Generator().manual_seed(52)
+    qa, ka, va = (torch.randn(1, HYB_T, h, 128, generator=g) for h in (4, 2, 2))
+    return x, qa, ka, va
+
+
+def _cpu_gdn(x, o):
+    hv = x["v"].shape[2]
+    out, _ = _oracle_prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], x["scale"], None)
+    o.copy_(out.view(o.shape))
+
+
+def _cpu_attention(q, k, v, o, window, scale):
+    # [1, T, H, D] views -> the oracle's [B, H, T, D]
+    got = _oracle_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), window, 0)
+    o.copy_(got.transpose(1, 2))
+
+
+def _hybrid_worker(rank, world, outdir):
+    from pseudobrain_b200 import sharding
+    x, qa, ka, va = _hybrid_inputs()
+    v0, v1, k0, k1 = sharding.head_shard(4, 2, world, rank)
+    xs = {"q": x["q"][:, :, k0:k1], "k": x["k"][:, :, k0:k1], "v": x["v"][:, :, v0:v1], "g": x["g"][:, :, v0:v1],
+          "beta": x["beta"][:, :, v0:v1], "scale": x["scale"]}
+    a0, a1 = rank, rank + 1  # one key head (2 query heads) per rank
+    gdn_all, pieces = sharding.hybrid_layer_sharded(xs, qa[:, :, 2 * a0:2 * a1], ka[:, :, a0:a1], va[:, :, a0:a1],
+                                                    HYB_W, 128 ** -0.5, swa_chunks=3, gdn=_cpu_gdn,
+                                                    attention=_cpu_attention)
+    torch.save({"gdn": gdn_all, "swa": sharding.assemble_heads(pieces, HYB_T)},
+               os.path.join(outdir, f"hybrid_{rank}.pt"))
+
+
+def test_hybrid_layer_pipeline_equals_unsharded(tmp_path):
+    """Head-sharded hybrid layer on 2 gloo ranks: the attention in halo'd query chunks with a
+    gather per chunk, the GDN branch and its gather; the assembled outputs equal the unsharded
+    branches (the same CPU stand-ins over all heads) on every rank."""
+    from pseudobrain_b200 import sharding
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), "hybrid", str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    x, qa, ka, va = _hybrid_inputs()
+    o_gdn = torch.empty(1, HYB_T, 4, 128)
+    _cpu_gdn(x, o_gdn)
+    o_att = torch.empty(1, HYB_T, 4, 128)
+    _cpu_attention(qa, ka, va, o_att, HYB_W, 128 ** -0.5)
+    want_gdn = o_gdn.view(HYB_T, 2, 2 * 128).transpose(0, 1)  # [N, T, 2 heads * 128]
+    want_att = o_att.view(HYB_T, 4 * 128)
+    for rank in range(world):
+        got = torch.load(os.path.join(tmp_path, f"hybrid_{rank}.pt"))
+        assert got["gdn"].dtype == torch.bfloat16  # the gathered GDN output is bf16 (as the model's)
+        assert torch.equal(got["gdn"].float(), want_gdn.to(torch.bfloat16).float())
+        assert torch.allclose(got["swa"], want_att, rtol=1e-5, atol=1e-6)
+    # the chunk plan covers every row once, halos within the window
+    plan = sharding.swa_chunk_plan(HYB_T, HYB_W, 3)
+    assert plan[0][0] == 0 and plan[-1][1] == HYB_T
+    assert all(a[1] == b[0] for a, b in zip(plan, plan[1:]))
+    assert all(h == min(s, 128) for s, _, h in plan)
