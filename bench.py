@@ -40,7 +40,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GDN prefill tok/s & decode steps/s per B200; Quest q/s; % TC/HBM roofline"
-PREFILL = {"full": dict(batch=4, seqlen=32768), "small": dict(batch=1, seqlen=8192)}
+PREFILL = {"full": dict(batch=4, seqlen=32768), "small": dict(batch=4, seqlen=8192)}
 PREFILL_HEADS = dict(hk=16, hv=32, dk=128, dv=128, chunk=64)
 DECODE = {"full": dict(batch=256), "small": dict(batch=64)}
 DECODE_HEADS = dict(hk=16, hv=32, dk=128, dv=128)
