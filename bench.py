@@ -523,9 +523,9 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
     T (segments chained by the segment scan) so a few heads still fill the SMs; the
     sliding-window attention branch (32 query / 8 key heads, window 4096) is split by key
     head. Each branch's output is all-gathered (NCCL) into head-major [N, rows, heads/N * 128]
-    buffers, the hidden-4096 layout the output projection reads: the attention in query
-    chunks whose gathers run while the next chunk computes, then the GDN branch and its
-    gather (sharding.hybrid_layer_sharded). Strong scaling: the job is one layer pass
+    buffers, the hidden-4096 layout the output projection reads: the GDN branch, its gather
+    running under the attention, then the attention in query chunks whose gathers run while
+    the next chunk computes (sharding.hybrid_layer_sharded). Strong scaling: the job is one layer pass
     whatever N; at N > 1 rank 0 also times the unsharded layer (all heads on one GPU) for
     the strong-scaling efficiency t1 / (N tN)."""
     import torch
@@ -672,7 +672,7 @@ def run_ours(args, rank, world, local_rank):
     # the large, secondary parts first and decode / quest last: a reader of the end of the
     # line (a log tail) sees the two other headline parts of the metric
     for name in ("widen", "serving", "hybrid", "decode", "quest"):
-        if name in parts and parts[name] is not None and (parts[name] is not head or name == "widen"):
+        if name in parts and parts[name] is not None:  # (the head part too: its own figures)
             line[name] = parts[name]
     if world == 1 and not args.no_cpu_baseline:
         if "prefill" in parts:
