@@ -669,6 +669,9 @@ def run_ours(args, rank, world, local_rank):
         "roofline": head["roofline"], "e2e": head.get("e2e"), "gpu_launches": head["gpu_launches"],
         "clocks": clk.summary(),
     }
+    for key in ("kernels", "step"):  # the prefill step's two kernels and its whole-step figures
+        if key in head:
+            line[key] = head[key]
     # the large, secondary parts first and decode / quest last: a reader of the end of the
     # line (a log tail) sees the two other headline parts of the metric
     for name in ("widen", "serving", "hybrid", "decode", "quest"):
