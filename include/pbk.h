@@ -299,6 +299,42 @@ typedef struct pbk_quest_desc {
   int32_t pad_;
 } pbk_quest_desc;
 
+/* Per-token block scores and exact rescoring of the serving path's per-token selector
+ * (pb27_vllm/memory.py:1009-1294). Query token t of q [T, H, D] (bf16, element strides) and
+ * key head h score candidate j of n_pool: block b = cand[h * cand_stride_kv + j] (or j when
+ * cand is NULL). out [KV, T, n_pool] fp32 at element strides out_stride_kv, out_stride_t. */
+typedef struct pbk_token_desc {
+  int32_t t, h, kv, d;          /* query tokens, query heads, key heads; d must be 128; h / kv <= 32 */
+  int32_t n_pool;               /* candidates per key head */
+  int32_t full;                 /* scores: blocks [0, full) carry bounds; others score -inf */
+  int32_t hole_lo, hole_hi;     /* scores: blocks in [hole_lo, hole_hi) score -inf (none if hole_hi <= hole_lo) */
+  int32_t rope_mask;            /* scores: nonzero zeroes the query dims below d / 4 (memory.py:1043-1045) */
+  int32_t block;                /* rescoring: tokens per block */
+  const void* q;
+  int64_t q_stride_t, q_stride_h;
+  const void* kmax;             /* scores: [KV, >= full, D] bf16 block bounds */
+  const void* kmin;
+  int64_t bnd_stride_kv, bnd_stride_p;
+  const void* keys;             /* rescoring: [KV, rows, D] bf16, block b = rows b * block .. + block - 1 */
+  int64_t key_stride_kv, key_stride_n;
+  const int32_t* cand;
+  int64_t cand_stride_kv;
+  float* out;
+  int64_t out_stride_kv, out_stride_t;
+} pbk_token_desc;
+
+/* out[h][t][j] = max over the query heads of key head h (token t) of
+ * sum_d q_d * (q_d > 0 ? kmax : kmin)[b][d], summed over d = 0 .. 127 in order, or -inf for
+ * a block outside [0, full) or inside the hole (memory.py:1079-1098). */
+PBK_API int pbk_quest_token_scores(const pbk_token_desc* desc, void* stream);
+/* out[h][t][j] = max over the query heads of key head h (token t) and the block's tokens of
+ * q . k in fp32 (the exact rescoring, memory.py:1192-1202). */
+PBK_API int pbk_quest_token_rerank(const pbk_token_desc* desc, void* stream);
+/* ranks[r][i] = position of x[r][i] in row r sorted descending, ties in index order
+ * (_ranks, memory.py:881-885), for `rows` rows of n <= 16384 fp32 values. */
+PBK_API int pbk_quest_row_ranks(const float* x, int64_t x_stride, int32_t rows, int32_t n, int32_t* ranks,
+                                int64_t ranks_stride, void* stream);
+
 /* Bytes of caller-provided device workspace pbk_quest_select / pbk_quest_attend need
  * for `desc` (0 when none; 256-byte aligned pointers). */
 PBK_API size_t pbk_quest_select_workspace(const pbk_quest_desc* desc);

@@ -53,6 +53,17 @@ class PbkOutNormDesc(ctypes.Structure):
                 ("o", PbkView), ("gate", PbkView), ("out", PbkView), ("weight", ctypes.c_void_p)]
 
 
+class PbkTokenDesc(ctypes.Structure):
+    _fields_ = [("t", ctypes.c_int32), ("h", ctypes.c_int32), ("kv", ctypes.c_int32), ("d", ctypes.c_int32),
+                ("n_pool", ctypes.c_int32), ("full", ctypes.c_int32), ("hole_lo", ctypes.c_int32),
+                ("hole_hi", ctypes.c_int32), ("rope_mask", ctypes.c_int32), ("block", ctypes.c_int32),
+                ("q", ctypes.c_void_p), ("q_stride_t", ctypes.c_int64), ("q_stride_h", ctypes.c_int64),
+                ("kmax", ctypes.c_void_p), ("kmin", ctypes.c_void_p), ("bnd_stride_kv", ctypes.c_int64),
+                ("bnd_stride_p", ctypes.c_int64), ("keys", ctypes.c_void_p), ("key_stride_kv", ctypes.c_int64),
+                ("key_stride_n", ctypes.c_int64), ("cand", ctypes.c_void_p), ("cand_stride_kv", ctypes.c_int64),
+                ("out", ctypes.c_void_p), ("out_stride_kv", ctypes.c_int64), ("out_stride_t", ctypes.c_int64)]
+
+
 class PbkGdnDesc(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hk", ctypes.c_int32),
                 ("hv", ctypes.c_int32), ("dk", ctypes.c_int32), ("dv", ctypes.c_int32),
@@ -165,6 +176,9 @@ SIGNATURES = {
                                             _VP]),
     "pbk_l2norm": (ctypes.c_int, [PbkView, PbkView, _I32, _I32, _I32, _I32, ctypes.c_float, _VP]),
     "pbk_swa_prefill": (ctypes.c_int, [ctypes.POINTER(PbkSwaDesc), _VP]),
+    "pbk_quest_token_scores": (ctypes.c_int, [ctypes.POINTER(PbkTokenDesc), _VP]),
+    "pbk_quest_token_rerank": (ctypes.c_int, [ctypes.POINTER(PbkTokenDesc), _VP]),
+    "pbk_quest_row_ranks": (ctypes.c_int, [_VP, _I64, _I32, _I32, _VP, _I64, _VP]),
 }
 
 

@@ -26,6 +26,10 @@ bool gdn_conv_width_ok(int width);
 cudaError_t launch_gdn_prefill_varlen(const pbk_gdn_desc& d, const int32_t* cu_seqlens, int num_seqs, void* ws,
                                       cudaStream_t st);
 cudaError_t launch_gdn_prefill_tc(const pbk_gdn_desc& d, void* solve_ws, bool solved, cudaStream_t st);
+cudaError_t launch_quest_token_scores(const pbk_token_desc& d, cudaStream_t st);
+cudaError_t launch_quest_token_rerank(const pbk_token_desc& d, cudaStream_t st);
+cudaError_t launch_quest_row_ranks(const float* x, int64_t x_stride, int rows, int n, int32_t* ranks,
+                                   int64_t r_stride, cudaStream_t st);
 cudaError_t launch_gdn_segment_scan(const float* b, const float* m, const float* h0, float* starts, int batch,
                                     int nseg, int hv, cudaStream_t st);
 }
@@ -637,6 +641,63 @@ int pbk_swa_prefill(const pbk_swa_desc* desc, void* stream) {
   st = check_current_device();
   if (st != PBK_OK) return st;
   return launch_status(pbk::launch_swa_tc(*desc, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ per-token selection
+namespace {
+// `need`: 1 scores (bounds), 2 rescoring (keys).
+int validate_token(const pbk_token_desc* d, int need) {
+  if (d == nullptr) return PBK_ERR_INVALID;
+  if (d->t < 0 || d->kv < 1 || d->h < d->kv || d->n_pool < 0) return PBK_ERR_INVALID;
+  if (d->h % d->kv != 0 || d->h / d->kv > 32) return PBK_ERR_SHAPE;
+  if (d->d != 128) return PBK_ERR_SHAPE;
+  if (d->t == 0 || d->n_pool == 0) return PBK_OK;
+  if (!d->q || !d->out) return PBK_ERR_INVALID;
+  if (!aligned16(d->q) || !aligned_elems(d->q_stride_t, 8) || !aligned_elems(d->q_stride_h, 8)) return PBK_ERR_ALIGN;
+  if (need & 1) {
+    if (d->full < 1 || !d->kmax || !d->kmin) return PBK_ERR_INVALID;
+    if (!aligned16(d->kmax) || !aligned16(d->kmin) || !aligned_elems(d->bnd_stride_kv, 8) ||
+        !aligned_elems(d->bnd_stride_p, 8))
+      return PBK_ERR_ALIGN;
+  }
+  if (need & 2) {
+    if (d->block < 1 || !d->keys) return PBK_ERR_INVALID;
+    if (!aligned16(d->keys) || !aligned_elems(d->key_stride_kv, 8) || !aligned_elems(d->key_stride_n, 8))
+      return PBK_ERR_ALIGN;
+  }
+  return PBK_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int pbk_quest_token_scores(const pbk_token_desc* desc, void* stream) {
+  int st = validate_token(desc, 1);
+  if (st != PBK_OK) return st;
+  if (desc->t == 0 || desc->n_pool == 0) return PBK_OK;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return launch_status(pbk::launch_quest_token_scores(*desc, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_quest_token_rerank(const pbk_token_desc* desc, void* stream) {
+  int st = validate_token(desc, 2);
+  if (st != PBK_OK) return st;
+  if (desc->t == 0 || desc->n_pool == 0) return PBK_OK;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return launch_status(pbk::launch_quest_token_rerank(*desc, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_quest_row_ranks(const float* x, int64_t x_stride, int32_t rows, int32_t n, int32_t* ranks,
+                        int64_t ranks_stride, void* stream) {
+  if (rows < 0 || n < 0 || n > 16384) return n > 16384 ? PBK_ERR_SHAPE : PBK_ERR_INVALID;
+  if (rows == 0 || n == 0) return PBK_OK;
+  if (x == nullptr || ranks == nullptr || x_stride < n || ranks_stride < n) return PBK_ERR_INVALID;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_quest_row_ranks(x, x_stride, rows, n, ranks, ranks_stride,
+                                                   static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -14,8 +14,10 @@ neighbours (:873-875), the exact rerank of the ``rerank`` best candidates (:854-
 budget rules (:779-787), the query's RoPE-dims mask for scoring past ROPE_HORIZON
 (:795-797), and the attention over [sinks ; retrieved blocks ; partial block before the
 window ; masked window] (the SDPA branch, own=None; the reference's LSE-merge branch
-computes the same softmax). Not covered (they raise NotImplementedError): the ORACLE
-diagnostic, per-token selection and own-block masks, and global landmarks. Past
+computes the same softmax), with the super-block landmarks after the sinks under dense
+global aggregation (:1332, 1411-1416). The per-token selector retrieve_blocks_per_token
+(:1009-1294) is in pertoken.py. Not covered: the ORACLE diagnostic and per-query own-block
+masks (NotImplementedError; the reference's selectors never produce them). Past
 ROPE_HORIZON the reranked candidates' keys, the sinks and the retrieved blocks move to new
 RoPE positions as the reference moves them (:574-677, 861-862, 1402-1425), gathered with
 the move (pbk_quest_rope_gather).
@@ -401,10 +403,8 @@ def piece_attention(arc, q: torch.Tensor, q_pos: torch.Tensor, top: torch.Tensor
     """Exact attention of piece q [T, H, D] at positions q_pos over its sinks, retrieved
     blocks `top` [KV, k], the partial block before its window and its causal sliding
     window, all read from the archive: [T, H, D] in q's dtype (memory.py:1311)."""
-    if own is not None:
-        raise NotImplementedError("per-token own-block masks (memory.py:1009-1294)")
-    if getattr(arc, "is_global_agg", False):
-        raise NotImplementedError("global super-block landmarks")
+    if own is not None:  # the reference's selectors return none (memory.py:1023, 1140, 1294)
+        raise NotImplementedError("per-query own-block masks")
     block = MEMORY["block_size"]
     t, h, d = q.shape
     if q_min is None or q_max is None:
@@ -426,6 +426,14 @@ def piece_attention(arc, q: torch.Tensor, q_pos: torch.Tensor, top: torch.Tensor
     shift = sink_shift(lo, ns, n_blk, block) if rope else 0
     if shift > 0:
         sink_k, sink_v = rope_gather(arc.keys, arc.values, None, ns, 0, 1, "constant", const_delta=shift)
+    n_land = _landmark_count(arc, lo, block)
+    if n_land > 0:  # dense global aggregation: the super-block mean keys follow the sinks (memory.py:1332, 1411-1416)
+        land_k = _move_landmarks(arc.smean_k[:, :n_land].to(torch.bfloat16), block, lo)
+        sink_k = torch.cat((sink_k[:, :ns].to(torch.bfloat16), land_k), dim=1)
+        sink_v = torch.cat((sink_v[:, :ns].to(torch.bfloat16), arc.smean_v[:, :n_land].to(torch.bfloat16)), dim=1)
+        ns += n_land
+    if top is not None:  # the reference's cache of the last retrieved set (memory.py:1427-1436)
+        arc.cached_top = top if getattr(arc, "prompt_top", None) is not None else None
     if top is not None and rope:  # [moved blocks ; partial block before the window], gathered
         tail0 = ORIGIN + ((lo - ORIGIN) // block) * block
         tail_n = lo - tail0 if lo > tail0 else 0
@@ -449,6 +457,37 @@ def piece_attention(arc, q: torch.Tensor, q_pos: torch.Tensor, top: torch.Tensor
     return out[0].to(q.dtype)
 
 
+def _landmark_count(arc, lo: int, block: int) -> int:
+    """Super-block landmarks a piece sees under dense global aggregation: the super-blocks
+    wholly before its window (memory.py:1332)."""
+    if not getattr(arc, "is_global_agg", False):
+        return 0
+    if getattr(arc, "smean_k", None) is None or getattr(arc, "smean_v", None) is None:
+        return 0
+    return max(0, ((lo - ORIGIN) // block) // SBLK)
+
+
+def _move_landmarks(smk: torch.Tensor, block: int, ref_pos: int) -> torch.Tensor:
+    """Past ROPE_HORIZON, super-block landmark keys [KV, n, D] at their centres ORIGIN + (i +
+    1/2) * SBLK * block move toward ref_pos in proportion (memory.py:680-711): the pairs (i,
+    i + d/8) of the first d/4 dims turn by delta * inv_freq, in fp32."""
+    if ROPE_HORIZON <= 0 or ref_pos <= ROPE_HORIZON or smk.numel() == 0:
+        return smk
+    kv, n_sb, d = smk.shape
+    d_rot = d // 4
+    half = d_rot // 2
+    scale = 1.0 - min(1.0, float(ROPE_ARC_SPAN) / float(max(1, ref_pos)))
+    orig = float(ORIGIN) + (torch.arange(n_sb, device=smk.device, dtype=torch.float32) + 0.5) * float(SBLK * block)
+    delta = (orig + torch.round((float(ref_pos) - orig).clamp(min=0.0) * scale) - orig).clamp(min=0.0)
+    ang = delta[None, :, None] * _inv_freq(smk.device, d_rot)
+    cos, sin = ang.cos(), ang.sin()
+    x1, x2 = smk[..., :half].float(), smk[..., half:d_rot].float()
+    out = smk.clone()
+    out[..., :half] = (x1 * cos - x2 * sin).to(smk.dtype)
+    out[..., half:d_rot] = (x2 * cos + x1 * sin).to(smk.dtype)
+    return out
+
+
 def _piece_attention_host(arc, qi, qpos, kpos, top, groups, window, scale, lo, hi, ns, block, out, dtype):
     """piece_attention over an offloaded archive: the sinks, the retrieved blocks with the
     partial block before the window, and the window are gathered on the host and copied to
@@ -462,6 +501,11 @@ def _piece_attention_host(arc, qi, qpos, kpos, top, groups, window, scale, lo, h
         sk, sv = _host_range(arc.keys, 0, ns, dev), _host_range(arc.values, 0, ns, dev)
     else:
         sk, sv = wk, wv
+    n_land = _landmark_count(arc, lo, block)
+    if n_land > 0:  # the super-block landmarks (in HBM) after the sinks
+        sk = torch.cat((sk[:, :ns], arc.smean_k[:, :n_land].to(torch.bfloat16)), dim=1)
+        sv = torch.cat((sv[:, :ns], arc.smean_v[:, :n_land].to(torch.bfloat16)), dim=1)
+        ns += n_land
     win = (wk, wv, kpos, window, 0, scale, out)
     if top is not None:
         n_blk = top.shape[1]

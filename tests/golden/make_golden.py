@@ -36,6 +36,9 @@ Fixtures:
   rope.npz        RoPE repositioning past the horizon (lowered to 1500 tokens): the block moves
                   in both modes and the sink move called directly, and retrieve_blocks (rerank,
                   flat) + piece_attention on a 3000-token serving archive.
+  pertoken.npz    the serving per-token selector retrieve_blocks_per_token: prompt, decode,
+                  no-lead, global-aggregation and holed-archive steps with the selector state
+                  before and after each.
   archive_write.npz  the serving Archive.write: a prefill write, short and scattered writes
                   and a long write across super-blocks into a CPU archive, then
                   refresh_bounds; its final storage, block and super-block summaries.
@@ -354,6 +357,105 @@ def make_serving(MEM):
     np.savez_compressed(os.path.join(HERE, "serving.npz"), **out)
 
 
+def make_pertoken(MEM):
+    """The per-token selector retrieve_blocks_per_token (pb27_vllm/memory.py:1009-1294) on a
+    CPU archive of 2 key heads x 3 query heads, 16-token blocks, super-blocks of 2: a prompt
+    piece (48 tokens: the prompt branch with exact rescoring and the second hop), two decode
+    steps with a query history (the super-block path, the prompt and decode merges), a piece
+    without a lead, the same with dense global aggregation forced (stratified peaks, visit
+    counts, the novelty penalty on the next decode step) and a prompt piece over an archive
+    hole. Each step records the selector's state before and after it. The reference's topk
+    and argsort run with ties in index order (torch's CPU order among equal values, e.g. the
+    tied integer tier keys, is implementation-defined), the tie rule this build uses."""
+    import torch
+    orig_sort = torch.Tensor.sort
+
+    def topk(self, k, dim=-1, largest=True, sorted=True):
+        idx = orig_sort(self, dim=dim, descending=largest, stable=True).indices.narrow(dim, 0, k)
+        return torch.return_types.topk((self.gather(dim, idx), idx))
+
+    def argsort(self, dim=-1, descending=False, stable=False):
+        return orig_sort(self, dim=dim, descending=descending, stable=True).indices
+
+    saved = (torch.Tensor.topk, torch.Tensor.argsort)
+    torch.Tensor.topk, torch.Tensor.argsort = topk, argsort
+    try:
+        _make_pertoken(MEM)
+    finally:
+        torch.Tensor.topk, torch.Tensor.argsort = saved
+
+
+def _make_pertoken(MEM):
+    import torch
+    kv, groups, d, block = 2, 3, 128, 16
+    MEM.SBLK = 2
+    MEM.MEMORY.update(blocks=8, decode_blocks=8, rerank=12, block_size=block, neighbors=0, window=64, chunk=64)
+    cap = MEM.ORIGIN + 300 * block + 10
+    gen = torch.Generator().manual_seed(207)
+    keys = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    values = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    n_blk = cap // block
+    n_sb = (n_blk + MEM.SBLK - 1) // MEM.SBLK
+    arc = MEM.Archive(keys, values, torch.empty(kv, n_blk, d), torch.empty(kv, n_blk, d))
+    arc.smax, arc.smin = torch.empty(kv, n_sb, d), torch.empty(kv, n_sb, d)
+    arc.bmean_k, arc.bmean_v = torch.empty(kv, n_blk, d), torch.empty(kv, n_blk, d)
+    arc.smean_k, arc.smean_v = torch.empty(kv, n_sb, d), torch.empty(kv, n_sb, d)
+    arc.size = arc.prompt_len = cap
+    arc.dirty_lo, arc.dirty_hi = 0, n_blk - 1
+    arc.refresh_bounds(block)
+    out = dict(keys=_bits(keys.to(torch.bfloat16)), values=_bits(values.to(torch.bfloat16)),
+               kmax=_bits(arc.kmax.to(torch.bfloat16)), kmin=_bits(arc.kmin.to(torch.bfloat16)),
+               smax=_bits(arc.smax.to(torch.bfloat16)), smin=_bits(arc.smin.to(torch.bfloat16)),
+               smean_k=arc.smean_k.numpy(), smean_v=arc.smean_v.numpy(), origin=np.int64(MEM.ORIGIN),
+               sblk=np.int64(MEM.SBLK), block=np.int64(block), groups=np.int64(groups), prompt_len=np.int64(cap),
+               window=np.int64(64))
+    limit = cap - 80  # a decode piece at limit + 63 keeps its 64-key window inside the archive
+    hole = (MEM.ORIGIN + 120 * block + 5, MEM.ORIGIN + 150 * block)
+
+    def state(prefix):
+        st = {}
+        for name in ("prompt_top", "decode_top", "last_hop_head", "visit_counts"):
+            v = getattr(arc, name, None)
+            st[f"{prefix}_{name}"] = np.zeros((0,), np.int64) if v is None else v.numpy().astype(np.int64)
+        st[f"{prefix}_decode_step"] = np.int64(arc.decode_step)
+        st[f"{prefix}_global"] = np.int64(bool(arc.is_global_agg))
+        return st
+
+    steps = (("prompt", 48, -1, False, "auto", False), ("dec1", 1, 0, True, "auto", False),
+             ("dec2", 1, 0, True, "auto", False), ("nolead", 1, None, False, "auto", False),
+             ("gprompt", 40, -1, False, "1", False), ("gdec", 1, 0, True, "1", False),
+             ("hole", 44, -1, False, "auto", True))
+    hist = torch.randn(24, kv * groups, d, generator=gen).to(torch.bfloat16).float()
+    names = []
+    for name, t, lead, with_hist, gagg, hole_on in steps:
+        MEM.GLOBAL_AGG = gagg
+        arc.hole_lo, arc.hole_hi = hole if hole_on else (0, 0)
+        q = torch.randn(t, kv * groups, d, generator=gen).to(torch.bfloat16).float()
+        q_hist = None
+        if with_hist:
+            hist = torch.cat((hist[1:], q[:1]), 0)
+            q_hist = hist[-16:]
+        out.update(state(f"{name}_before"))
+        res = MEM.retrieve_blocks_per_token(arc, q, groups, limit, 0, lead, 0, q_hist)
+        blk = res[0] if res is not None else torch.zeros(0, dtype=torch.int64)
+        out.update(state(f"{name}_after"))
+        if name in ("dec2", "gdec"):  # the piece's attention over sinks, landmarks, blocks, tail and window
+            q_pos = torch.tensor([limit + 63])
+            o = MEM.piece_attention(arc, q, q_pos, blk, groups, 64, d ** -0.5, None, q_min=limit + 63,
+                                    q_max=limit + 63)
+            out[f"{name}_attn"] = o.float().numpy()
+        out.update({f"{name}_q": _bits(q.to(torch.bfloat16)), f"{name}_lead": np.int64(-9 if lead is None else lead),
+                    f"{name}_hist": (_bits(q_hist.to(torch.bfloat16)) if q_hist is not None
+                                     else np.zeros((0,), np.uint16)),
+                    f"{name}_gagg": np.int64(gagg == "1"), f"{name}_hole": np.array(hole if hole_on else (0, 0)),
+                    f"{name}_top": blk.numpy().astype(np.int64)})
+        names.append(name)
+    MEM.GLOBAL_AGG = "auto"
+    out["steps"] = np.array(names)
+    out["limit"] = np.int64(limit)
+    np.savez_compressed(os.path.join(HERE, "pertoken.npz"), **out)
+
+
 def make_gdn_io(G):
     """The layer pieces around the recurrence: short_convolution (with a carried tail) and
     l2_normalize (both modes) are the reference's functions; gating and the gated output
@@ -409,7 +511,7 @@ def main(reference_root: str) -> None:
     makers = {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR),
               "serving": lambda: make_serving(MEM), "gdn_io": lambda: make_gdn_io(G),
               "quest_levels": lambda: make_quest_levels(E, MEM), "rope": lambda: make_rope(MEM),
-              "archive_write": lambda: make_archive_write(MEM)}
+              "archive_write": lambda: make_archive_write(MEM), "pertoken": lambda: make_pertoken(MEM)}
     for name in (sys.argv[2:] if len(sys.argv) > 2 else makers):  # all, or only the named fixtures
         makers[name]()
     for name in sorted(os.listdir(HERE)):

@@ -59,7 +59,7 @@ def test_abi_version_and_status_strings(lib):
                                           ("pbk_quest_levels", "PbkQuestLevels"),
                                           ("pbk_rope_gather_desc", "PbkRopeGatherDesc"),
                                           ("pbk_archive_write_desc", "PbkArchiveWriteDesc"),
-                                          ("pbk_decode_ext", "PbkDecodeExt")])
+                                          ("pbk_decode_ext", "PbkDecodeExt"), ("pbk_token_desc", "PbkTokenDesc")])
 def test_descriptor_layout_matches_header(cname, pyname):
     """Offsets of every field of the ctypes mirror equal the C struct's (checked by
     compiling a probe against include/pbk.h)."""
@@ -91,7 +91,8 @@ def test_no_device_returns_error_without_launching(lib):
 def test_every_module_imports(lib):
     """The Python mirrors import on a host without a GPU (they fail only when called)."""
     import importlib
-    for m in ("gated_deltanet", "gdn_prefill", "exact_memory", "transplant", "serving", "sharding", "synthetic"):
+    for m in ("gated_deltanet", "gdn_prefill", "exact_memory", "transplant", "serving", "pertoken", "sharding",
+              "synthetic"):
         importlib.import_module(f"pseudobrain_b200.{m}")
 
 
@@ -110,3 +111,16 @@ def test_noalloc_select_too_large_when_scores_are_given(lib):
     d.q_stride_n, d.q_stride_t, d.q_stride_h = 64 * 128, 64 * 128, 128
     d.bnd_stride_kv, d.bnd_stride_p = 65536 * 128, 128
     assert _capi.LIB.pbk_quest_select_noalloc(ctypes.byref(d), None) == _capi.PBK_ERR_TOO_LARGE
+
+
+def test_token_entry_points_validate_on_the_host(lib):
+    """The per-token selector's entry points reject bad shapes before touching the device."""
+    from pseudobrain_b200 import _capi
+    d = _capi.PbkTokenDesc(t=1, h=40, kv=1, d=128, n_pool=4, full=4)
+    assert _capi.LIB.pbk_quest_token_scores(ctypes.byref(d), None) == -2  # 40 heads per key head
+    d = _capi.PbkTokenDesc(t=1, h=8, kv=2, d=256, n_pool=4, full=4)
+    assert _capi.LIB.pbk_quest_token_scores(ctypes.byref(d), None) == -2  # head dim 256
+    d = _capi.PbkTokenDesc(t=0, h=8, kv=2, d=128, n_pool=4, full=4)
+    assert _capi.LIB.pbk_quest_token_rerank(ctypes.byref(d), None) == 0   # nothing to do
+    assert _capi.LIB.pbk_quest_row_ranks(None, 20000, 1, 20000, None, 20000, None) == -2
+    assert _capi.LIB.pbk_quest_row_ranks(None, 8, 1, 8, None, 8, None) == -1
