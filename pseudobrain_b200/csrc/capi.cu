@@ -79,6 +79,10 @@ constexpr size_t kWsAlign = 256;
 size_t round_up(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
 bool aligned_elems(int64_t stride, int64_t elems) { return stride % elems == 0; }
 
+// Head dims of the Quest, serving and per-token kernels (128: tensor-core scores and
+// attention; 256: the SIMT kernels).
+bool quest_dim_ok(int d) { return d == 128 || d == 256; }
+
 int validate_swa(const pbk_swa_desc* d) {
   if (d == nullptr) return PBK_ERR_INVALID;
   if (d->batch < 0 || d->seqlen < 0 || d->h < 1 || d->kv < 1 || d->sinks < 0 || !(d->scale > 0.f))
@@ -107,9 +111,9 @@ int validate_quest(const pbk_quest_desc* d, int need) {
       d->n_win < 0)
     return PBK_ERR_INVALID;
   if (d->h % d->kv != 0) return PBK_ERR_SHAPE;
-  if (d->d != 128) return PBK_ERR_SHAPE;
+  if (!quest_dim_ok(d->d)) return PBK_ERR_SHAPE;
   const int64_t rows_per_head = (int64_t)d->nq * d->t * (d->h / d->kv);
-  if (rows_per_head * 128 * 4 > 220 * 1024) return PBK_ERR_SHAPE;  // query rows of one key head in shared memory
+  if (rows_per_head * d->d * 4 > 220 * 1024) return PBK_ERR_SHAPE;  // query rows of one key head in shared memory
   if (!d->q || !d->pages) return PBK_ERR_INVALID;
   if (!aligned16(d->q) || !aligned_elems(d->q_stride_n, 8) || !aligned_elems(d->q_stride_t, 8) ||
       !aligned_elems(d->q_stride_h, 8))
@@ -478,7 +482,7 @@ int pbk_quest_rerank(const pbk_quest_desc* desc, const int32_t* cand, int32_t c,
   if (desc == nullptr || cand == nullptr || c < 1) return PBK_ERR_INVALID;
   if (desc->nq < 0 || desc->t < 1 || desc->kv < 1 || desc->h % desc->kv != 0 || desc->page < 1 || desc->budget < 1)
     return PBK_ERR_INVALID;
-  if (desc->d != 128) return PBK_ERR_SHAPE;
+  if (!quest_dim_ok(desc->d)) return PBK_ERR_SHAPE;
   if (!desc->q || !desc->keys || !desc->pages) return PBK_ERR_INVALID;
   if (!aligned16(desc->q) || !aligned_elems(desc->q_stride_n, 8) || !aligned_elems(desc->q_stride_t, 8) ||
       !aligned_elems(desc->q_stride_h, 8) || !aligned16(desc->keys) || !aligned_elems(desc->arc_stride_kv, 8) ||
@@ -508,7 +512,7 @@ int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d, int32_t
                      int64_t key_stride_n, void* kmax, void* kmin, int64_t bnd_stride_kv, int64_t bnd_stride_p,
                      int32_t first_page, void* stream) {
   if (kv < 1 || n < 0 || page < 1 || first_page < 0) return PBK_ERR_INVALID;
-  if (d != 128) return PBK_ERR_SHAPE;
+  if (!quest_dim_ok(d)) return PBK_ERR_SHAPE;
   if (n == 0 || first_page * (int64_t)page >= n) return PBK_OK;
   if (!keys || !kmax || !kmin) return PBK_ERR_INVALID;
   if (!aligned16(keys) || !aligned16(kmax) || !aligned16(kmin) || key_stride_n % 8 || key_stride_kv % 8 ||
@@ -516,7 +520,7 @@ int pbk_quest_bounds(const void* keys, int32_t kv, int32_t n, int32_t d, int32_t
     return PBK_ERR_ALIGN;
   int st = check_current_device();
   if (st != PBK_OK) return st;
-  return launch_status(pbk::launch_quest_bounds(keys, kv, n, page, key_stride_kv, key_stride_n, kmax, kmin, bnd_stride_kv,
+  return launch_status(pbk::launch_quest_bounds(keys, kv, n, d, page, key_stride_kv, key_stride_n, kmax, kmin, bnd_stride_kv,
                                   bnd_stride_p, first_page, static_cast<cudaStream_t>(stream)));
 }
 
@@ -524,7 +528,7 @@ int pbk_quest_superbounds(const void* kmax, const void* kmin, int32_t kv, int32_
                           int64_t bnd_stride_kv, int64_t bnd_stride_p, void* smax, void* smin, int64_t sb_stride_kv,
                           int64_t sb_stride_p, int32_t first_sb, int32_t end_sb, void* stream) {
   if (kv < 1 || n_blk < 0 || sblk < 1 || first_sb < 0) return PBK_ERR_INVALID;
-  if (d != 128) return PBK_ERR_SHAPE;
+  if (!quest_dim_ok(d)) return PBK_ERR_SHAPE;
   if (n_blk == 0 || end_sb <= first_sb || first_sb * (int64_t)sblk >= n_blk) return PBK_OK;
   if (!kmax || !kmin || !smax || !smin) return PBK_ERR_INVALID;
   if (!aligned16(kmax) || !aligned16(kmin) || !aligned16(smax) || !aligned16(smin) || bnd_stride_kv % 8 ||
@@ -532,7 +536,7 @@ int pbk_quest_superbounds(const void* kmax, const void* kmin, int32_t kv, int32_
     return PBK_ERR_ALIGN;
   int st = check_current_device();
   if (st != PBK_OK) return st;
-  return launch_status(pbk::launch_quest_superbounds(kmax, kmin, kv, n_blk, sblk, bnd_stride_kv, bnd_stride_p, smax,
+  return launch_status(pbk::launch_quest_superbounds(kmax, kmin, kv, n_blk, d, sblk, bnd_stride_kv, bnd_stride_p, smax,
                                                      smin, sb_stride_kv, sb_stride_p, first_sb, end_sb,
                                                      static_cast<cudaStream_t>(stream)));
 }
@@ -541,7 +545,7 @@ int pbk_quest_rope_gather(const pbk_rope_gather_desc* d, void* stream) {
   if (d == nullptr) return PBK_ERR_INVALID;
   if (d->kv < 1 || d->block < 1 || d->n_blk < 0 || d->tail_n < 0 || d->n_rows < 0 || d->mode < 0 || d->mode > 3)
     return PBK_ERR_INVALID;
-  if (d->d != 128) return PBK_ERR_SHAPE;
+  if (!quest_dim_ok(d->d)) return PBK_ERR_SHAPE;
   if ((int64_t)d->n_blk * d->block + d->tail_n > INT32_MAX) return PBK_ERR_SHAPE;
   if ((int64_t)d->n_blk * d->block + d->tail_n == 0) return PBK_OK;
   if (!d->keys || !d->out_keys || (d->out_values && !d->values)) return PBK_ERR_INVALID;
@@ -559,7 +563,7 @@ int pbk_quest_archive_write(const pbk_archive_write_desc* d, void* stream) {
   if (d == nullptr) return PBK_ERR_INVALID;
   if (d->kv < 1 || d->block < 1 || d->origin < 0 || d->cap < 0 || d->size < 0 || d->n < 0 || d->p0 < 0)
     return PBK_ERR_INVALID;
-  if (d->d != 128) return PBK_ERR_SHAPE;
+  if (!quest_dim_ok(d->d)) return PBK_ERR_SHAPE;
   const bool blocks = d->blk_hi >= d->blk_lo;
   if (blocks && (d->blk_lo < 0 || (int64_t)d->origin + ((int64_t)d->blk_hi + 1) * d->block > (int64_t)d->cap + d->block))
     return PBK_ERR_INVALID;  // summarised blocks start inside the archive
@@ -587,7 +591,7 @@ int pbk_quest_supermeans(const void* bmean, int32_t kv, int32_t n_blk, int32_t d
                          int64_t bnd_stride_p, void* smean, int64_t sb_stride_kv, int64_t sb_stride_p,
                          int32_t first_sb, int32_t end_sb, void* stream) {
   if (kv < 1 || n_blk < 0 || sblk < 1 || first_sb < 0) return PBK_ERR_INVALID;
-  if (d != 128) return PBK_ERR_SHAPE;
+  if (!quest_dim_ok(d)) return PBK_ERR_SHAPE;
   if (n_blk == 0 || end_sb <= first_sb || first_sb * (int64_t)sblk >= n_blk) return PBK_OK;
   if (!bmean || !smean) return PBK_ERR_INVALID;
   if (!aligned16(bmean) || !aligned16(smean) || bnd_stride_kv % 8 || bnd_stride_p % 8 || sb_stride_kv % 8 ||
@@ -595,7 +599,7 @@ int pbk_quest_supermeans(const void* bmean, int32_t kv, int32_t n_blk, int32_t d
     return PBK_ERR_ALIGN;
   int st = check_current_device();
   if (st != PBK_OK) return st;
-  return launch_status(pbk::launch_quest_supermeans(bmean, kv, n_blk, sblk, bnd_stride_kv, bnd_stride_p, smean,
+  return launch_status(pbk::launch_quest_supermeans(bmean, kv, n_blk, d, sblk, bnd_stride_kv, bnd_stride_p, smean,
                                                     sb_stride_kv, sb_stride_p, first_sb, end_sb,
                                                     static_cast<cudaStream_t>(stream)));
 }
@@ -652,7 +656,7 @@ int validate_token(const pbk_token_desc* d, int need) {
   if (d == nullptr) return PBK_ERR_INVALID;
   if (d->t < 0 || d->kv < 1 || d->h < d->kv || d->n_pool < 0) return PBK_ERR_INVALID;
   if (d->h % d->kv != 0 || d->h / d->kv > 32) return PBK_ERR_SHAPE;
-  if (d->d != 128) return PBK_ERR_SHAPE;
+  if (!quest_dim_ok(d->d)) return PBK_ERR_SHAPE;
   if (d->t == 0 || d->n_pool == 0) return PBK_OK;
   if (!d->q || !d->out) return PBK_ERR_INVALID;
   if (!aligned16(d->q) || !aligned_elems(d->q_stride_t, 8) || !aligned_elems(d->q_stride_h, 8)) return PBK_ERR_ALIGN;

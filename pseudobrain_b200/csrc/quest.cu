@@ -3,6 +3,7 @@
 // pseudobrain/exact_memory.py:43-152 and the attention of pseudobrain/transplant.py:612-628).
 #include <cfloat>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "quest.cuh"
@@ -10,6 +11,9 @@
 namespace pbk {
 namespace {
 
+// Head dims of the tensor-core score path and of the top-k's refinement (which only runs on
+// tensor-core scores); the SIMT kernels below take the head dim as a template parameter
+// (128 or 256).
 constexpr int kD = 128;
 using bf16 = __nv_bfloat16;
 
@@ -28,34 +32,57 @@ __device__ __forceinline__ void bf16x8_to_f32(const uint4 raw, float* out) {
   }
 }
 
+// A row of D bf16 spread over a warp: lane l holds dims kPer l .. kPer l + kPer - 1 (kPer =
+// D / 32: 4 or 8), moved as one 8- or 16-byte vector.
+template <int D>
+struct WarpRow {
+  static constexpr int kPer = D / 32;
+  using Vec = typename std::conditional<kPer == 4, uint2, uint4>::type;
+  __device__ static Vec raw(const bf16* p) { return *reinterpret_cast<const Vec*>(p); }
+  __device__ static void put(bf16* p, const Vec& v) { *reinterpret_cast<Vec*>(p) = v; }
+  __device__ static void unpack(const Vec& v, float (&x)[kPer]) {
+    const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int i = 0; i < kPer / 2; ++i) {
+      const float2 f = __bfloat1622float2(pr[i]);
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
+  }
+  __device__ static Vec pack(const float (&x)[kPer]) {
+    Vec v;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+    for (int i = 0; i < kPer / 2; ++i) w[i] = bf16x2_bits(x[2 * i], x[2 * i + 1]);
+    return v;
+  }
+  __device__ static void load(const bf16* p, float (&x)[kPer]) { unpack(raw(p), x); }
+  __device__ static void store(bf16* p, const float (&x)[kPer]) { put(p, pack(x)); }
+};
+
 // ---------------------------------------------------------------------------------
-// Page bounds: one warp per (page, key head); lane l owns dims 4l..4l+3.
+// Page bounds: one warp per (page, key head); lane l owns dims kPer l .. kPer l + kPer - 1.
 // ---------------------------------------------------------------------------------
+template <int D>
 __global__ void quest_bounds_kernel(const bf16* keys, int n, int page, int64_t ks_kv, int64_t ks_n, bf16* kmax,
                                     bf16* kmin, int64_t bs_kv, int64_t bs_p, int first_page, int npages) {
+  using R = WarpRow<D>;
+  constexpr int P = R::kPer;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= npages) return;
   const int p = first_page + warp, h = blockIdx.y;
   const int t0 = p * page, t1 = min(t0 + page, n);
-  float mx[4], mn[4];
+  float mx[P], mn[P], v[P];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) mx[i] = -FLT_MAX, mn[i] = FLT_MAX;
+  for (int i = 0; i < P; ++i) mx[i] = -FLT_MAX, mn[i] = FLT_MAX;
   for (int t = t0; t < t1; ++t) {
-    const bf16* row = keys + h * ks_kv + (int64_t)t * ks_n + 4 * lane;
-    const uint2 raw = *reinterpret_cast<const uint2*>(row);
-    const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
-    const float2 a = __bfloat1622float2(pr[0]), b = __bfloat1622float2(pr[1]);
-    const float v[4] = {a.x, a.y, b.x, b.y};
+    R::load(keys + h * ks_kv + (int64_t)t * ks_n + P * lane, v);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) mx[i] = fmaxf(mx[i], v[i]), mn[i] = fminf(mn[i], v[i]);
+    for (int i = 0; i < P; ++i) mx[i] = fmaxf(mx[i], v[i]), mn[i] = fminf(mn[i], v[i]);
   }
-  bf16* omx = kmax + h * bs_kv + (int64_t)p * bs_p + 4 * lane;
-  bf16* omn = kmin + h * bs_kv + (int64_t)p * bs_p + 4 * lane;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {  // max/min of bf16 values are bf16 values: exact
-    omx[i] = __float2bfloat16_rn(mx[i]);
-    omn[i] = __float2bfloat16_rn(mn[i]);
-  }
+  // max/min of bf16 values are bf16 values: exact
+  R::store(kmax + h * bs_kv + (int64_t)p * bs_p + P * lane, mx);
+  R::store(kmin + h * bs_kv + (int64_t)p * bs_p + P * lane, mn);
 }
 
 // ---------------------------------------------------------------------------------
@@ -66,13 +93,14 @@ __global__ void quest_bounds_kernel(const bf16* keys, int n, int page, int64_t k
 constexpr int kScoreThreads = 128;
 constexpr int kRowBlock = 4;
 
+template <int D>
 __global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_quest_desc d, int npages, float* scores,
                                                                    float* segmax, int nseg) {
-  extern __shared__ __align__(16) float qs[];  // [rows of one key head][kD]
+  extern __shared__ __align__(16) float qs[];  // [rows of one key head][D]
   const int h = blockIdx.y, groups = d.h / d.kv, rows_per_group = d.t * groups;
   const int rows = d.nq * rows_per_group;
-  for (int e = threadIdx.x; e < rows * kD; e += kScoreThreads) {
-    const int r = e / kD, dd = e % kD;
+  for (int e = threadIdx.x; e < rows * D; e += kScoreThreads) {
+    const int r = e / D, dd = e % D;
     const int n = r / rows_per_group, rem = r % rows_per_group, ti = rem / groups, g = rem % groups;
     const bf16* qp = reinterpret_cast<const bf16*>(d.q) + n * d.q_stride_n + ti * d.q_stride_t +
                      (int64_t)(h * groups + g) * d.q_stride_h;
@@ -88,9 +116,9 @@ __global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_qu
     float best = -INFINITY;
     for (int r0 = 0; r0 < rows_per_group; r0 += kRowBlock) {
       const int nr = min(kRowBlock, rows_per_group - r0);
-      const float* qb = qs + (n * rows_per_group + r0) * kD;
+      const float* qb = qs + (n * rows_per_group + r0) * D;
       float acc[kRowBlock] = {0.f, 0.f, 0.f, 0.f};
-      for (int d0 = 0; d0 < kD; d0 += 8) {
+      for (int d0 = 0; d0 < D; d0 += 8) {
         float mx[8], mn[8];
         bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmax + d0), mx);
         bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmin + d0), mn);
@@ -99,7 +127,7 @@ __global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(const pbk_qu
           if (r < nr) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const float qv = qb[r * kD + d0 + j];
+              const float qv = qb[r * D + d0 + j];
               acc[r] = fmaf(qv, qv > 0.f ? mx[j] : mn[j], acc[r]);
             }
           }
@@ -698,16 +726,18 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
 // ---------------------------------------------------------------------------------
 // Gather of the selected pages + partial tail (what retrieve() returns).
 // ---------------------------------------------------------------------------------
+template <int D>
 __global__ void quest_gather_kernel(const pbk_quest_desc d, int k, int tail, bf16* ok, bf16* ov) {
+  constexpr int kParts = D / 8;  // 16-byte parts per row
   const int n = blockIdx.z, h = blockIdx.y;
   const int rows = k * d.page + tail;
-  const int row = blockIdx.x * (blockDim.x / 16) + threadIdx.x / 16, part = threadIdx.x % 16;
+  const int row = blockIdx.x * (blockDim.x / kParts) + threadIdx.x / kParts, part = threadIdx.x % kParts;
   if (row >= rows) return;
   int src;
   if (row < k * d.page) src = d.pages[((int64_t)n * d.kv + h) * k + row / d.page] * d.page + row % d.page;
   else src = (d.n_arch / d.page) * d.page + (row - k * d.page);
   const int64_t so = h * d.arc_stride_kv + (int64_t)src * d.arc_stride_n + part * 8;
-  const int64_t dst = (((int64_t)n * d.kv + h) * rows + row) * kD + part * 8;
+  const int64_t dst = (((int64_t)n * d.kv + h) * rows + row) * D + part * 8;
   *reinterpret_cast<uint4*>(ok + dst) = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(d.keys) + so);
   *reinterpret_cast<uint4*>(ov + dst) = *reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(d.values) + so);
 }
@@ -734,15 +764,15 @@ __device__ __forceinline__ bool key_visible(int kp, int qp, int window, int sink
   return kp <= qp && ((qp - kp) < window || kp < sinks);
 }
 
-template <int kAttRows>
+template <int D, int kAttRows>
 __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_quest_desc d, int k, int tail, int splits,
                                                                      float* part, int split0, const SinkKeys sk) {
-  __shared__ __align__(16) float qs[kAttRows][kD];
+  __shared__ __align__(16) float qs[kAttRows][D];
   __shared__ float prob[kAttRows][kSplitKeys];
   __shared__ int kidx[kSplitKeys];     // archive token, or -1 - window index
   __shared__ float red[kAttRows][kAttWarps];
   __shared__ float sh_m[kAttRows], sh_l[kAttRows];
-  __shared__ __align__(16) float accs[kAttWarps][kAttRows][kD];
+  __shared__ __align__(16) float accs[kAttWarps][kAttRows][D];
   const int split = split0 + blockIdx.x, n = blockIdx.y / d.kv, h = blockIdx.y % d.kv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int groups = d.h / d.kv, rows = d.t * groups;
@@ -775,8 +805,8 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
   for (int r0 = 0; r0 < rows; r0 += kAttRows) {
     const int nr = min(kAttRows, rows - r0);
     __syncthreads();
-    for (int e = tid; e < kAttRows * kD; e += kAttThreads) {
-      const int r = e / kD, dd = e % kD;
+    for (int e = tid; e < kAttRows * D; e += kAttThreads) {
+      const int r = e / D, dd = e % D;
       float v = 0.f;
       if (r < nr) {
         const int rr = r0 + r, ti = rr / groups, g = rr % groups;
@@ -795,21 +825,24 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
         const bf16* kr = idx >= 0         ? keys + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
                          : idx > kSinkTag ? wkeys + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n
                                           : sk.k + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
-        uint4 raw[kD / 8];
 #pragma unroll
-        for (int c = 0; c < kD / 8; ++c) raw[c] = *reinterpret_cast<const uint4*>(kr + 8 * c);
+        for (int c0 = 0; c0 < D / 8; c0 += 16) {  // 128 dims (16 loads) in flight at a time
+          uint4 raw[16];
 #pragma unroll
-        for (int c = 0; c < kD / 8; ++c) {
-          float kv8[8];
-          bf16x8_to_f32(raw[c], kv8);
+          for (int c = 0; c < 16; ++c) raw[c] = *reinterpret_cast<const uint4*>(kr + 8 * (c0 + c));
 #pragma unroll
-          for (int r = 0; r < kAttRows; ++r) {
-            const float4 qa = *reinterpret_cast<const float4*>(&qs[r][8 * c]);
-            const float4 qb = *reinterpret_cast<const float4*>(&qs[r][8 * c + 4]);
-            acc[r] = fmaf(qa.x, kv8[0], acc[r]); acc[r] = fmaf(qa.y, kv8[1], acc[r]);
-            acc[r] = fmaf(qa.z, kv8[2], acc[r]); acc[r] = fmaf(qa.w, kv8[3], acc[r]);
-            acc[r] = fmaf(qb.x, kv8[4], acc[r]); acc[r] = fmaf(qb.y, kv8[5], acc[r]);
-            acc[r] = fmaf(qb.z, kv8[6], acc[r]); acc[r] = fmaf(qb.w, kv8[7], acc[r]);
+          for (int c = 0; c < 16; ++c) {
+            float kv8[8];
+            bf16x8_to_f32(raw[c], kv8);
+#pragma unroll
+            for (int r = 0; r < kAttRows; ++r) {
+              const float4 qa = *reinterpret_cast<const float4*>(&qs[r][8 * (c0 + c)]);
+              const float4 qb = *reinterpret_cast<const float4*>(&qs[r][8 * (c0 + c) + 4]);
+              acc[r] = fmaf(qa.x, kv8[0], acc[r]); acc[r] = fmaf(qa.y, kv8[1], acc[r]);
+              acc[r] = fmaf(qa.z, kv8[2], acc[r]); acc[r] = fmaf(qa.w, kv8[3], acc[r]);
+              acc[r] = fmaf(qb.x, kv8[4], acc[r]); acc[r] = fmaf(qb.y, kv8[5], acc[r]);
+              acc[r] = fmaf(qb.z, kv8[6], acc[r]); acc[r] = fmaf(qb.w, kv8[7], acc[r]);
+            }
           }
         }
       }
@@ -852,10 +885,11 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
       for (int w = 0; w < kAttWarps; ++w) x += red[tid][w];
       sh_l[tid] = x;
     }
-    // P V: warp keys 32 warp .., lane dims 4 lane ..
-    float acc[kAttRows][4] = {};
+    // P V: warp keys 32 warp .., lane dims 4 lane .. of each 128-dim half
     const int jb = 32 * warp, kn = min(32, nkeys - jb);
-    {  // all 32 value rows of the warp in flight at once
+#pragma unroll
+    for (int half = 0; half < D / 128; ++half) {  // all 32 value rows of the warp in flight at once
+      float acc[kAttRows][4] = {};
       uint2 raw[32];
 #pragma unroll
       for (int u = 0; u < 32; ++u) {
@@ -865,7 +899,7 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
           const bf16* vr = idx >= 0         ? vals + h * d.arc_stride_kv + (int64_t)idx * d.arc_stride_n
                            : idx > kSinkTag ? wvals + h * d.win_stride_kv + (int64_t)(-1 - idx) * d.win_stride_n
                                             : sk.v + h * sk.s_kv + (int64_t)(kSinkTag - idx) * sk.s_n;
-          raw[u] = *reinterpret_cast<const uint2*>(vr + 4 * lane);
+          raw[u] = *reinterpret_cast<const uint2*>(vr + 128 * half + 4 * lane);
         }
       }
 #pragma unroll
@@ -881,21 +915,22 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
           acc[r][3] = fmaf(pr, v3, acc[r][3]);
         }
       }
-    }
 #pragma unroll
-    for (int r = 0; r < kAttRows; ++r)
-      *reinterpret_cast<float4*>(&accs[warp][r][4 * lane]) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+      for (int r = 0; r < kAttRows; ++r)
+        *reinterpret_cast<float4*>(&accs[warp][r][128 * half + 4 * lane]) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    }
     __syncthreads();
-    for (int e = tid; e < nr * kD; e += kAttThreads) {
-      const int r = e / kD, dd = e % kD;
+    for (int e = tid; e < nr * D; e += kAttThreads) {
+      const int r = e / D, dd = e % D;
       float x = 0.f;
 #pragma unroll
       for (int w = 0; w < kAttWarps; ++w) x += accs[w][r][dd];
       const int rr = r0 + r, ti = rr / groups, g = rr % groups;
       const int64_t row = (((int64_t)n * d.t + ti) * d.h + h * groups + g) * splits + split;
-      float* pp = part + row * (kD + 2);
+      float* pp = part + row * (D + 2);
       pp[dd] = x;
-      if (dd == 0) pp[kD] = sh_m[r], pp[kD + 1] = sh_l[r];
+      if (dd == 0) pp[D] = sh_m[r], pp[D + 1] = sh_l[r];
     }
   }
 }
@@ -904,6 +939,7 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
 // in shared memory (max and sum over the splits in parallel), then each warp sums a quarter
 // of the splits for the 32 dims (lane = dim, eight independent loads in flight) and the
 // four partial sums meet in shared memory.
+template <int D>
 __global__ void __launch_bounds__(128) quest_combine_kernel(const pbk_quest_desc d, int splits, const float* part) {
   extern __shared__ float w[];  // [splits]
   __shared__ float red[4];
@@ -911,9 +947,9 @@ __global__ void __launch_bounds__(128) quest_combine_kernel(const pbk_quest_desc
   const int row = blockIdx.x;  // (n, ti, head); blockIdx.y: dims 32 y .. 32 y + 31
   const int head = row % d.h, ti = (row / d.h) % d.t, n = row / (d.h * d.t);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float* pp = part + (int64_t)row * splits * (kD + 2);
+  const float* pp = part + (int64_t)row * splits * (D + 2);
   float m = -INFINITY;
-  for (int s = tid; s < splits; s += 128) m = fmaxf(m, pp[s * (kD + 2) + kD]);
+  for (int s = tid; s < splits; s += 128) m = fmaxf(m, pp[s * (D + 2) + D]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
@@ -922,10 +958,10 @@ __global__ void __launch_bounds__(128) quest_combine_kernel(const pbk_quest_desc
   __syncthreads();
   float l = 0.f;
   for (int s = tid; s < splits; s += 128) {
-    const float ms = pp[s * (kD + 2) + kD];
+    const float ms = pp[s * (D + 2) + D];
     const float ws = ms == -INFINITY ? 0.f : exp2f(ms - M);
     w[s] = ws;
-    l = fmaf(pp[s * (kD + 2) + kD + 1], ws, l);
+    l = fmaf(pp[s * (D + 2) + D + 1], ws, l);
   }
   l = warp_sum(l);
   if (lane == 0) red[warp] = l;
@@ -938,11 +974,11 @@ __global__ void __launch_bounds__(128) quest_combine_kernel(const pbk_quest_desc
   for (; s + 28 < splits; s += 32) {
     float x[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) x[u] = pd[(s + 4 * u) * (kD + 2)];
+    for (int u = 0; u < 8; ++u) x[u] = pd[(s + 4 * u) * (D + 2)];
 #pragma unroll
     for (int u = 0; u < 8; ++u) acc[u] = fmaf(x[u], w[s + 4 * u], acc[u]);
   }
-  for (; s < splits; s += 4) acc[0] = fmaf(pd[s * (kD + 2)], w[s], acc[0]);
+  for (; s < splits; s += 4) acc[0] = fmaf(pd[s * (D + 2)], w[s], acc[0]);
   accs[warp][lane] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
   __syncthreads();
   if (warp == 0) {
@@ -961,10 +997,11 @@ __global__ void __launch_bounds__(128) quest_combine_kernel(const pbk_quest_desc
 // candidates, group*kv + key head), warp = one candidate page, lane = tokens lane,
 // lane + 32, ...; the query rows sit in shared memory.
 // ---------------------------------------------------------------------------------
-constexpr int kRerankRows = 64;  // query rows in shared memory per pass
+constexpr int kRerankRows = 32;  // query rows in shared memory per pass
+template <int D>
 __global__ void __launch_bounds__(256) quest_rerank_kernel(const pbk_quest_desc d, const int32_t* cand, int c,
                                                            float* exact) {
-  __shared__ __align__(16) float qs[kRerankRows][kD];
+  __shared__ __align__(16) float qs[kRerankRows][D];
   const int n = blockIdx.y / d.kv, h = blockIdx.y % d.kv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = d.h / d.kv, rows = d.t * groups;
   const int ci = blockIdx.x * 8 + warp;
@@ -974,8 +1011,8 @@ __global__ void __launch_bounds__(256) quest_rerank_kernel(const pbk_quest_desc 
   for (int r0 = 0; r0 < rows; r0 += kRerankRows) {
     const int nr = min(kRerankRows, rows - r0);
     __syncthreads();
-    for (int e = threadIdx.x; e < nr * kD; e += blockDim.x) {
-      const int r = e / kD, dd = e % kD, ti = (r0 + r) / groups, g = (r0 + r) % groups;
+    for (int e = threadIdx.x; e < nr * D; e += blockDim.x) {
+      const int r = e / D, dd = e % D, ti = (r0 + r) / groups, g = (r0 + r) % groups;
       qs[r][dd] = __bfloat162float(reinterpret_cast<const bf16*>(d.q)[n * d.q_stride_n + ti * d.q_stride_t +
                                                                         (int64_t)(h * groups + g) * d.q_stride_h + dd]);
     }
@@ -983,21 +1020,33 @@ __global__ void __launch_bounds__(256) quest_rerank_kernel(const pbk_quest_desc 
     if (ci >= c) continue;
     for (int s = lane; s < d.page; s += 32) {
       const bf16* kr = base + ((int64_t)page * d.page + s) * d.arc_stride_n;
-      float kf[kD];
+      float acc[kRerankRows];
 #pragma unroll
-      for (int c8 = 0; c8 < kD / 8; ++c8) bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + 8 * c8), kf + 8 * c8);
-      for (int r = 0; r < nr; ++r) {
-        float acc = 0.f;
+      for (int r = 0; r < kRerankRows; ++r) acc[r] = 0.f;
+      for (int d0 = 0; d0 < D; d0 += 8) {  // dims in order, 8 at a time, every row
+        float kf[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + d0), kf);
 #pragma unroll
-        for (int dd = 0; dd < kD; dd += 4) {
-          const float4 qa = *reinterpret_cast<const float4*>(&qs[r][dd]);
-          acc = fmaf(qa.x, kf[dd], acc);
-          acc = fmaf(qa.y, kf[dd + 1], acc);
-          acc = fmaf(qa.z, kf[dd + 2], acc);
-          acc = fmaf(qa.w, kf[dd + 3], acc);
+        for (int r = 0; r < kRerankRows; ++r) {
+          if (r < nr) {
+            const float4 qa = *reinterpret_cast<const float4*>(&qs[r][d0]);
+            const float4 qb = *reinterpret_cast<const float4*>(&qs[r][d0 + 4]);
+            float a = acc[r];
+            a = fmaf(qa.x, kf[0], a);
+            a = fmaf(qa.y, kf[1], a);
+            a = fmaf(qa.z, kf[2], a);
+            a = fmaf(qa.w, kf[3], a);
+            a = fmaf(qb.x, kf[4], a);
+            a = fmaf(qb.y, kf[5], a);
+            a = fmaf(qb.z, kf[6], a);
+            a = fmaf(qb.w, kf[7], a);
+            acc[r] = a;
+          }
         }
-        best = fmaxf(best, acc);
       }
+#pragma unroll
+      for (int r = 0; r < kRerankRows; ++r)
+        if (r < nr) best = fmaxf(best, acc[r]);
     }
   }
   if (ci >= c) return;
@@ -1017,35 +1066,29 @@ __global__ void quest_map_kernel(const int32_t* cand, int c, int k, int nrows, i
 // Super-block bounds (exact_memory.py:53-63, memory.py:280-306): warp per (super-block,
 // key head), lane l owns dims 4l..4l+3; max of the blocks' maxima, min of their minima.
 // ---------------------------------------------------------------------------------
+template <int D>
 __global__ void quest_superbounds_kernel(const bf16* kmax, const bf16* kmin, int64_t bs_kv, int64_t bs_p, int n_blk,
                                          int sblk, bf16* smax, bf16* smin, int64_t ss_kv, int64_t ss_p, int first_sb,
                                          int nsb) {
+  using R = WarpRow<D>;
+  constexpr int P = R::kPer;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= nsb) return;
   const int s = first_sb + warp, h = blockIdx.y;
   const int b0 = s * sblk, b1 = min(b0 + sblk, n_blk);
-  float mx[4], mn[4];
+  float mx[P], mn[P], va[P], vb[P];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) mx[i] = -FLT_MAX, mn[i] = FLT_MAX;
+  for (int i = 0; i < P; ++i) mx[i] = -FLT_MAX, mn[i] = FLT_MAX;
   for (int b = b0; b < b1; ++b) {
-    const int64_t off = h * bs_kv + (int64_t)b * bs_p + 4 * lane;
-    const uint2 ra = *reinterpret_cast<const uint2*>(kmax + off);
-    const uint2 rb = *reinterpret_cast<const uint2*>(kmin + off);
-    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&ra);
-    const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&rb);
-    const float2 a0 = __bfloat1622float2(pa[0]), a1 = __bfloat1622float2(pa[1]);
-    const float2 c0 = __bfloat1622float2(pb[0]), c1 = __bfloat1622float2(pb[1]);
-    const float va[4] = {a0.x, a0.y, a1.x, a1.y}, vb[4] = {c0.x, c0.y, c1.x, c1.y};
+    const int64_t off = h * bs_kv + (int64_t)b * bs_p + P * lane;
+    R::load(kmax + off, va);
+    R::load(kmin + off, vb);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) mx[i] = fmaxf(mx[i], va[i]), mn[i] = fminf(mn[i], vb[i]);
+    for (int i = 0; i < P; ++i) mx[i] = fmaxf(mx[i], va[i]), mn[i] = fminf(mn[i], vb[i]);
   }
-  bf16* omx = smax + h * ss_kv + (int64_t)s * ss_p + 4 * lane;
-  bf16* omn = smin + h * ss_kv + (int64_t)s * ss_p + 4 * lane;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {  // max/min of bf16 values are bf16 values: exact
-    omx[i] = __float2bfloat16_rn(mx[i]);
-    omn[i] = __float2bfloat16_rn(mn[i]);
-  }
+  // max/min of bf16 values are bf16 values: exact
+  R::store(smax + h * ss_kv + (int64_t)s * ss_p + P * lane, mx);
+  R::store(smin + h * ss_kv + (int64_t)s * ss_p + P * lane, mn);
 }
 
 // ---------------------------------------------------------------------------------
@@ -1057,10 +1100,11 @@ __global__ void quest_superbounds_kernel(const bf16* kmax, const bf16* kmin, int
 // rows pass through shared memory 32 at a time.
 // ---------------------------------------------------------------------------------
 constexpr int kSubRows = 32;
+template <int D>
 __global__ void __launch_bounds__(kScoreThreads) quest_sub_score_kernel(const pbk_quest_desc d, const int32_t* top_sb,
                                                                        int m_sb, int sblk, int full, int hole0,
                                                                        int hole1, float* scores, int32_t* cand) {
-  __shared__ __align__(16) float qs[kSubRows][kD];
+  __shared__ __align__(16) float qs[kSubRows][D];
   const int row = blockIdx.y, n = row / d.kv, h = row % d.kv, groups = d.h / d.kv, rows = d.t * groups;
   const int nc = m_sb * sblk, c = blockIdx.x * kScoreThreads + threadIdx.x;
   const bool live = c < nc;
@@ -1074,8 +1118,8 @@ __global__ void __launch_bounds__(kScoreThreads) quest_sub_score_kernel(const pb
   for (int r0 = 0; r0 < rows; r0 += kSubRows) {
     const int nr = min(kSubRows, rows - r0);
     __syncthreads();
-    for (int e = threadIdx.x; e < nr * kD; e += kScoreThreads) {
-      const int r = e / kD, dd = e % kD, ti = (r0 + r) / groups, g = (r0 + r) % groups;
+    for (int e = threadIdx.x; e < nr * D; e += kScoreThreads) {
+      const int r = e / D, dd = e % D, ti = (r0 + r) / groups, g = (r0 + r) % groups;
       qs[r][dd] = __bfloat162float(reinterpret_cast<const bf16*>(d.q)[n * d.q_stride_n + ti * d.q_stride_t +
                                                                         (int64_t)(h * groups + g) * d.q_stride_h + dd]);
     }
@@ -1083,7 +1127,7 @@ __global__ void __launch_bounds__(kScoreThreads) quest_sub_score_kernel(const pb
     for (int rb = 0; rb < nr; rb += kRowBlock) {
       const int nb = min(kRowBlock, nr - rb);
       float acc[kRowBlock] = {0.f, 0.f, 0.f, 0.f};
-      for (int d0 = 0; d0 < kD; d0 += 8) {
+      for (int d0 = 0; d0 < D; d0 += 8) {
         float mx[8], mn[8];
         bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmax + d0), mx);
         bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmin + d0), mn);
@@ -1165,12 +1209,15 @@ __global__ void __launch_bounds__(32) quest_rope_delta_kernel(const pbk_rope_gat
 }
 
 // Gather (and rotate) the rows of one (block, key head) per CTA, after its cos / sin table
-// (16 pairs, computed once per block); warp = row, lane l holds dims 4l .. 4l + 3, so the
-// rotated pairs (i, i + 16), i < 16, sit in lanes l and l + 4 for l < 4. The tail rows
-// (unrotated) are the CTAs past the blocks, kTailRows rows each.
+// (D / 8 pairs, computed once per block); warp = row, lane l holds dims P l .. P l + P - 1
+// (P = D / 32), so the rotated pairs (i, i + D / 8), i < D / 8, sit in lanes l and l + 4 for
+// l < 4. The tail rows (unrotated) are the CTAs past the blocks, kTailRows rows each.
 constexpr int kTailRows = 64;
+template <int D>
 __global__ void __launch_bounds__(256) quest_rope_gather_kernel(const pbk_rope_gather_desc d) {
-  __shared__ float cs[2][16];
+  using R = WarpRow<D>;
+  constexpr int P = R::kPer, kHalf = D / 8;
+  __shared__ float cs[2][kHalf];
   const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t nb = (int64_t)d.n_blk * d.block;
   const bool in_blocks = (int)blockIdx.x < d.n_blk;
@@ -1183,7 +1230,7 @@ __global__ void __launch_bounds__(256) quest_rope_gather_kernel(const pbk_rope_g
     out0 = (int64_t)j * d.block;
     nrows = d.block;
     rot = d.mode != 0;
-    if (rot && threadIdx.x < 16) {
+    if (rot && threadIdx.x < kHalf) {
       const float dl = d.mode == 3 ? d.const_delta : d.delta[(int64_t)h * d.n_blk + j];
       const float ang = __fmul_rn(dl, d.inv_freq[threadIdx.x]);
       cs[0][threadIdx.x] = cosf(ang);
@@ -1196,44 +1243,46 @@ __global__ void __launch_bounds__(256) quest_rope_gather_kernel(const pbk_rope_g
     out0 = nb + t;
     nrows = min((int64_t)kTailRows, (int64_t)d.tail_n - t);
   }
-  float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+  float c[P], sn[P];
+#pragma unroll
+  for (int e = 0; e < P; ++e) c[e] = 1.f, sn[e] = 0.f;
   if (rot && lane < 8) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) c[e] = cs[0][4 * (lane & 3) + e], sn[e] = cs[1][4 * (lane & 3) + e];
+    for (int e = 0; e < P; ++e) c[e] = cs[0][P * (lane & 3) + e], sn[e] = cs[1][P * (lane & 3) + e];
   }
   const bf16* kin = reinterpret_cast<const bf16*>(d.keys);
   const bf16* vin = reinterpret_cast<const bf16*>(d.values);
-  bf16* kout = reinterpret_cast<bf16*>(d.out_keys) + (int64_t)h * (nb + d.tail_n) * kD;
-  bf16* vout = d.out_values ? reinterpret_cast<bf16*>(d.out_values) + (int64_t)h * (nb + d.tail_n) * kD : nullptr;
+  bf16* kout = reinterpret_cast<bf16*>(d.out_keys) + (int64_t)h * (nb + d.tail_n) * D;
+  bf16* vout = d.out_values ? reinterpret_cast<bf16*>(d.out_values) + (int64_t)h * (nb + d.tail_n) * D : nullptr;
   for (int64_t s = warp; s < nrows; s += 8) {
     const int64_t src = src0 + s;
     const bool ok = src >= 0 && src < d.n_rows;
-    const int64_t at = h * d.stride_kv + src * d.stride_n + 4 * lane;
-    uint2 kr = make_uint2(0u, 0u), vr = make_uint2(0u, 0u);
+    const int64_t at = h * d.stride_kv + src * d.stride_n + P * lane;
+    typename R::Vec kr{}, vr{};
     if (ok) {
-      kr = *reinterpret_cast<const uint2*>(kin + at);
-      if (vout) vr = *reinterpret_cast<const uint2*>(vin + at);
+      kr = R::raw(kin + at);
+      if (vout) vr = R::raw(vin + at);
     }
     if (rot) {
-      const uint2 pr = make_uint2(__shfl_xor_sync(0xffffffffu, kr.x, 4), __shfl_xor_sync(0xffffffffu, kr.y, 4));
-      if (lane < 8) {
-        const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&kr);
-        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&pr);
-        const float2 a0 = __bfloat1622float2(a[0]), a1 = __bfloat1622float2(a[1]);
-        const float2 b0 = __bfloat1622float2(b[0]), b1 = __bfloat1622float2(b[1]);
-        const float own[4] = {a0.x, a0.y, a1.x, a1.y}, other[4] = {b0.x, b0.y, b1.x, b1.y};
-        float r[4];
+      typename R::Vec pr;
+      const uint32_t* kw = reinterpret_cast<const uint32_t*>(&kr);
+      uint32_t* pw = reinterpret_cast<uint32_t*>(&pr);
 #pragma unroll
-        for (int e = 0; e < 4; ++e)  // lanes 0-3: r1 = x1 cos - x2 sin; lanes 4-7: r2 = x2 cos + x1 sin
+      for (int w = 0; w < P / 2; ++w) pw[w] = __shfl_xor_sync(0xffffffffu, kw[w], 4);
+      if (lane < 8) {
+        float own[P], other[P], r[P];
+        R::unpack(kr, own);
+        R::unpack(pr, other);
+#pragma unroll
+        for (int e = 0; e < P; ++e)  // lanes 0-3: r1 = x1 cos - x2 sin; lanes 4-7: r2 = x2 cos + x1 sin
           r[e] = lane < 4 ? __fsub_rn(__fmul_rn(own[e], c[e]), __fmul_rn(other[e], sn[e]))
                           : __fadd_rn(__fmul_rn(own[e], c[e]), __fmul_rn(other[e], sn[e]));
-        kr.x = bf16x2_bits(r[0], r[1]);
-        kr.y = bf16x2_bits(r[2], r[3]);
+        kr = R::pack(r);
       }
     }
-    const int64_t o = (out0 + s) * kD + 4 * lane;
-    *reinterpret_cast<uint2*>(kout + o) = kr;
-    if (vout) *reinterpret_cast<uint2*>(vout + o) = vr;
+    const int64_t o = (out0 + s) * D + P * lane;
+    R::put(kout + o, kr);
+    if (vout) R::put(vout + o, vr);
   }
 }
 
@@ -1243,18 +1292,11 @@ __global__ void __launch_bounds__(256) quest_rope_gather_kernel(const pbk_rope_g
 // head) that reads its rows once (new rows from the input, which it also writes, older rows
 // from the archive) and keeps max, min and the fp32 sums of keys and values in registers.
 // ---------------------------------------------------------------------------------
-__device__ __forceinline__ void ld4(const bf16* p, float (&x)[4]) {
-  const uint2 raw = *reinterpret_cast<const uint2*>(p);
-  const __nv_bfloat162* pr = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  const float2 a = __bfloat1622float2(pr[0]), b = __bfloat1622float2(pr[1]);
-  x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y;
-}
-__device__ __forceinline__ void st4(bf16* p, const float (&x)[4]) {
-  *reinterpret_cast<uint2*>(p) = make_uint2(bf16x2_bits(x[0], x[1]), bf16x2_bits(x[2], x[3]));
-}
-
 // Input rows [i0, i1) of the write (all of them for a scattered write).
+template <int D>
 __global__ void __launch_bounds__(256) quest_archive_copy_kernel(const pbk_archive_write_desc d, int i0, int i1) {
+  using R = WarpRow<D>;
+  constexpr int P = R::kPer;
   const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = i0 + blockIdx.x * 8 + warp;
   if (i >= i1) return;
@@ -1264,15 +1306,16 @@ __global__ void __launch_bounds__(256) quest_archive_copy_kernel(const pbk_archi
     const int64_t b = (r - d.origin) / d.block;
     if (b >= d.blk_lo && b <= d.blk_hi) return;
   }
-  const int64_t src = (int64_t)i * d.in_stride_n + h * d.in_stride_kv + 4 * lane;
-  const int64_t dst = h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
-  *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(d.keys) + dst) =
-      *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(d.k) + src);
-  *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(d.values) + dst) =
-      *reinterpret_cast<const uint2*>(reinterpret_cast<const bf16*>(d.v) + src);
+  const int64_t src = (int64_t)i * d.in_stride_n + h * d.in_stride_kv + P * lane;
+  const int64_t dst = h * d.arc_stride_kv + r * d.arc_stride_n + P * lane;
+  R::put(reinterpret_cast<bf16*>(d.keys) + dst, R::raw(reinterpret_cast<const bf16*>(d.k) + src));
+  R::put(reinterpret_cast<bf16*>(d.values) + dst, R::raw(reinterpret_cast<const bf16*>(d.v) + src));
 }
 
+template <int D>
 __global__ void __launch_bounds__(256) quest_archive_block_kernel(const pbk_archive_write_desc d, int nblocks) {
+  using R = WarpRow<D>;
+  constexpr int P = R::kPer;
   const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = blockIdx.x * 8 + warp;
   if (w >= nblocks) return;
@@ -1285,72 +1328,77 @@ __global__ void __launch_bounds__(256) quest_archive_block_kernel(const pbk_arch
   const bf16* in_v = reinterpret_cast<const bf16*>(d.v);
   bf16* ak = reinterpret_cast<bf16*>(d.keys);
   bf16* av = reinterpret_cast<bf16*>(d.values);
-  float mx[4], mn[4], sk[4] = {0.f, 0.f, 0.f, 0.f}, sv[4] = {0.f, 0.f, 0.f, 0.f}, kl[4], vl[4];
+  float mx[P], mn[P], sk[P], sv[P], kl[P], vl[P];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) mx[e] = -FLT_MAX, mn[e] = FLT_MAX;
+  for (int e = 0; e < P; ++e) mx[e] = -FLT_MAX, mn[e] = FLT_MAX, sk[e] = 0.f, sv[e] = 0.f;
   constexpr int kBatch = 8;  // rows loaded before any is stored: eight loads of each in flight
   for (int64_t rb = r0; rb < r1; rb += kBatch) {
-    uint2 kr[kBatch], vr[kBatch];
+    typename R::Vec kr[kBatch], vr[kBatch];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       const int64_t r = rb + u;
       if (r >= r1) break;
       const bool fresh = d.pos == nullptr && r >= d.p0 && r < (int64_t)d.p0 + d.n;
-      const bf16* sk_ = fresh ? in_k + (r - d.p0) * d.in_stride_n + h * d.in_stride_kv + 4 * lane
-                              : ak + h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
-      const bf16* sv_ = fresh ? in_v + (r - d.p0) * d.in_stride_n + h * d.in_stride_kv + 4 * lane
-                              : av + h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
-      kr[u] = *reinterpret_cast<const uint2*>(sk_);
-      vr[u] = *reinterpret_cast<const uint2*>(sv_);
+      const bf16* sk_ = fresh ? in_k + (r - d.p0) * d.in_stride_n + h * d.in_stride_kv + P * lane
+                              : ak + h * d.arc_stride_kv + r * d.arc_stride_n + P * lane;
+      const bf16* sv_ = fresh ? in_v + (r - d.p0) * d.in_stride_n + h * d.in_stride_kv + P * lane
+                              : av + h * d.arc_stride_kv + r * d.arc_stride_n + P * lane;
+      kr[u] = R::raw(sk_);
+      vr[u] = R::raw(sv_);
     }
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       const int64_t r = rb + u;
       if (r >= r1) break;
       if (d.pos == nullptr && r >= d.p0 && r < (int64_t)d.p0 + d.n) {  // bf16 in, bf16 out: the row as it came
-        const int64_t at = h * d.arc_stride_kv + r * d.arc_stride_n + 4 * lane;
-        *reinterpret_cast<uint2*>(ak + at) = kr[u];
-        *reinterpret_cast<uint2*>(av + at) = vr[u];
+        const int64_t at = h * d.arc_stride_kv + r * d.arc_stride_n + P * lane;
+        R::put(ak + at, kr[u]);
+        R::put(av + at, vr[u]);
       }
-      ld4(reinterpret_cast<const bf16*>(&kr[u]), kl);
-      ld4(reinterpret_cast<const bf16*>(&vr[u]), vl);
+      R::unpack(kr[u], kl);
+      R::unpack(vr[u], vl);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < P; ++e) {
         mx[e] = fmaxf(mx[e], kl[e]), mn[e] = fminf(mn[e], kl[e]);
         sk[e] += kl[e], sv[e] += vl[e];
       }
     }
   }
   const float pad = (float)(r0 + d.block - r1);  // a partial block counts its last row again
-  const int64_t bo = h * d.bnd_stride_kv + b * d.bnd_stride_p + 4 * lane;
-  float km[4], vm[4];
+  const int64_t bo = h * d.bnd_stride_kv + b * d.bnd_stride_p + P * lane;
+  float km[P], vm[P];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
+  for (int e = 0; e < P; ++e) {
     km[e] = (sk[e] + pad * kl[e]) / (float)d.block;
     vm[e] = (sv[e] + pad * vl[e]) / (float)d.block;
   }
-  st4(reinterpret_cast<bf16*>(d.kmax) + bo, mx);
-  st4(reinterpret_cast<bf16*>(d.kmin) + bo, mn);
-  if (d.kmean) st4(reinterpret_cast<bf16*>(d.kmean) + bo, km);
-  if (d.vmean) st4(reinterpret_cast<bf16*>(d.vmean) + bo, vm);
+  R::store(reinterpret_cast<bf16*>(d.kmax) + bo, mx);
+  R::store(reinterpret_cast<bf16*>(d.kmin) + bo, mn);
+  if (d.kmean) R::store(reinterpret_cast<bf16*>(d.kmean) + bo, km);
+  if (d.vmean) R::store(reinterpret_cast<bf16*>(d.vmean) + bo, vm);
 }
 
 // Super-block means (memory.py:296-306): warp per (super-block, key head).
+template <int D>
 __global__ void quest_supermeans_kernel(const bf16* bmean, int64_t bs_kv, int64_t bs_p, int n_blk, int sblk,
                                         bf16* smean, int64_t ss_kv, int64_t ss_p, int first_sb, int nsb) {
+  using R = WarpRow<D>;
+  constexpr int P = R::kPer;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= nsb) return;
   const int s = first_sb + warp, h = blockIdx.y;
   const int b0 = s * sblk, b1 = min(b0 + sblk, n_blk);
-  float acc[4] = {0.f, 0.f, 0.f, 0.f}, x[4];
-  for (int b = b0; b < b1; ++b) {
-    ld4(bmean + h * bs_kv + (int64_t)b * bs_p + 4 * lane, x);
+  float acc[P], x[P];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[e] += x[e];
+  for (int e = 0; e < P; ++e) acc[e] = 0.f;
+  for (int b = b0; b < b1; ++b) {
+    R::load(bmean + h * bs_kv + (int64_t)b * bs_p + P * lane, x);
+#pragma unroll
+    for (int e = 0; e < P; ++e) acc[e] += x[e];
   }
 #pragma unroll
-  for (int e = 0; e < 4; ++e) acc[e] /= (float)(b1 - b0);
-  st4(smean + h * ss_kv + (int64_t)s * ss_p + 4 * lane, acc);
+  for (int e = 0; e < P; ++e) acc[e] /= (float)(b1 - b0);
+  R::store(smean + h * ss_kv + (int64_t)s * ss_p + P * lane, acc);
 }
 
 // Pages [lo, hi) of every score row score -inf (the archive hole, memory.py:852-853).
@@ -1364,6 +1412,16 @@ __global__ void quest_hole_kernel(float* scores, int npages, int nrows, int lo, 
 // ---------------------------------------------------------------------------------
 // Launch helpers (called from capi.cu after validation).
 // ---------------------------------------------------------------------------------
+namespace {
+// f(std::integral_constant<int, D>{}) for head dim d (128 or 256; the entry points admit no
+// other).
+template <typename F>
+cudaError_t with_dim(int d, F&& f) {
+  if (d == 256) return f(std::integral_constant<int, 256>{});
+  return f(std::integral_constant<int, 128>{});
+}
+}  // namespace
+
 int quest_k(const pbk_quest_desc& d) { return min(d.budget, d.n_arch / d.page); }
 // Splits of the retrieved keys (pages and tail) and of the window keys.
 int quest_ret_splits(const pbk_quest_desc& d, int n_sink) {
@@ -1412,7 +1470,7 @@ RefineArgs refine_args(const pbk_quest_desc& d, const float* tile_abs) {
 }  // namespace
 size_t quest_score_bytes(const pbk_quest_desc& d) { return quest_select_floats(d) * sizeof(float); }
 size_t quest_partial_bytes(const pbk_quest_desc& d, int n_sink) {
-  return (size_t)d.nq * d.t * d.h * quest_splits(d, n_sink) * (kD + 2) * sizeof(float);
+  return (size_t)d.nq * d.t * d.h * quest_splits(d, n_sink) * (d.d + 2) * sizeof(float);
 }
 
 cudaError_t launch_quest_select(const pbk_quest_desc& d, float* scratch, cudaStream_t st) {
@@ -1436,13 +1494,19 @@ cudaError_t launch_quest_select_parts(const pbk_quest_desc& d, float* scratch, i
     if (e != cudaSuccess) return e;
   } else {
     const int rows = d.nq * d.t * (d.h / d.kv);
-    const size_t smem = (size_t)rows * kD * sizeof(float);
-    if (smem > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(quest_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-    }
-    quest_score_kernel<<<dim3((npages + kScoreThreads - 1) / kScoreThreads, d.kv), kScoreThreads, smem, st>>>(
-        d, npages, scores, segmax, nseg);
+    const size_t smem = (size_t)rows * d.d * sizeof(float);
+    cudaError_t e = with_dim(d.d, [&](auto D) {
+      constexpr int kDim = decltype(D)::value;
+      if (smem > 48 * 1024) {
+        cudaError_t e2 = cudaFuncSetAttribute(quest_score_kernel<kDim>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem);
+        if (e2 != cudaSuccess) return e2;
+      }
+      quest_score_kernel<kDim><<<dim3((npages + kScoreThreads - 1) / kScoreThreads, d.kv), kScoreThreads, smem, st>>>(
+          d, npages, scores, segmax, nseg);
+      return cudaGetLastError();
+    });
+    if (e != cudaSuccess) return e;
   }
   if (!(parts & 2)) return cudaGetLastError();
   {
@@ -1499,26 +1563,36 @@ cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const Sink
     const int sr = quest_ret_splits(d, sk.n);
     const int s0 = (parts & 1) ? 0 : sr, s1 = (parts & 2) ? splits : sr;
     if (s1 > s0) {
-      if (d.t * (d.h / d.kv) > 4)
-        quest_attend_kernel<8><<<dim3(s1 - s0, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
+      const dim3 grid(s1 - s0, d.nq * d.kv);
+      if (d.d == 256)  // 4 query rows per pass: the partial sums of 8 x 256 dims exceed static shared memory
+        quest_attend_kernel<256, 4><<<grid, kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
+      else if (d.t * (d.h / d.kv) > 4)
+        quest_attend_kernel<128, 8><<<grid, kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
       else
-        quest_attend_kernel<4><<<dim3(s1 - s0, d.nq * d.kv), kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
+        quest_attend_kernel<128, 4><<<grid, kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
     }
   }
   if (!(parts & 4)) return cudaGetLastError();
   const int wbytes = splits * (int)sizeof(float);
-  if (wbytes > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(quest_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, wbytes);
-    if (e != cudaSuccess) return e;
-  }
-  quest_combine_kernel<<<dim3(d.nq * d.t * d.h, kD / 32), 128, wbytes, st>>>(d, splits, part);
-  return cudaGetLastError();
+  return with_dim(d.d, [&](auto D) {
+    constexpr int kDim = decltype(D)::value;
+    if (wbytes > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(quest_combine_kernel<kDim>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           wbytes);
+      if (e != cudaSuccess) return e;
+    }
+    quest_combine_kernel<kDim><<<dim3(d.nq * d.t * d.h, kDim / 32), 128, wbytes, st>>>(d, splits, part);
+    return cudaGetLastError();
+  });
 }
 
 cudaError_t launch_quest_rerank(const pbk_quest_desc& d, const int32_t* cand, int c, float* exact, cudaStream_t st) {
   const int k = min(d.budget, c), nrows = d.nq * d.kv;
   if (k <= 0) return cudaSuccess;
-  quest_rerank_kernel<<<dim3((c + 7) / 8, nrows), 256, 0, st>>>(d, cand, c, exact);
+  with_dim(d.d, [&](auto D) {
+    quest_rerank_kernel<decltype(D)::value><<<dim3((c + 7) / 8, nrows), 256, 0, st>>>(d, cand, c, exact);
+    return cudaSuccess;
+  });
   cudaError_t e = cudaFuncSetAttribute(quest_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sizeof(TopkSmem));
   if (e != cudaSuccess) return e;
@@ -1531,19 +1605,24 @@ cudaError_t launch_quest_rerank(const pbk_quest_desc& d, const int32_t* cand, in
 cudaError_t launch_quest_gather(const pbk_quest_desc& d, int sel, void* ok, void* ov, cudaStream_t st) {
   const int k = sel, tail = d.n_arch % d.page, rows = k * d.page + tail;
   if (rows == 0) return cudaSuccess;
-  quest_gather_kernel<<<dim3((rows + 15) / 16, d.kv, d.nq), 256, 0, st>>>(d, k, tail, static_cast<bf16*>(ok),
-                                                                           static_cast<bf16*>(ov));
-  return cudaGetLastError();
+  return with_dim(d.d, [&](auto D) {
+    constexpr int kDim = decltype(D)::value, kRowsPerCta = 256 / (kDim / 8);
+    quest_gather_kernel<kDim><<<dim3((rows + kRowsPerCta - 1) / kRowsPerCta, d.kv, d.nq), 256, 0, st>>>(
+        d, k, tail, static_cast<bf16*>(ok), static_cast<bf16*>(ov));
+    return cudaGetLastError();
+  });
 }
 
-cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int page, int64_t ks_kv, int64_t ks_n, void* kmax,
-                                void* kmin, int64_t bs_kv, int64_t bs_p, int first_page, cudaStream_t st) {
+cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int dim, int page, int64_t ks_kv, int64_t ks_n,
+                                void* kmax, void* kmin, int64_t bs_kv, int64_t bs_p, int first_page, cudaStream_t st) {
   const int npages = (n + page - 1) / page - first_page;
   if (npages <= 0) return cudaSuccess;
-  quest_bounds_kernel<<<dim3((npages + 7) / 8, kv), 256, 0, st>>>(
-      static_cast<const bf16*>(keys), n, page, ks_kv, ks_n, static_cast<bf16*>(kmax), static_cast<bf16*>(kmin), bs_kv,
-      bs_p, first_page, npages);
-  return cudaGetLastError();
+  return with_dim(dim, [&](auto D) {
+    quest_bounds_kernel<decltype(D)::value><<<dim3((npages + 7) / 8, kv), 256, 0, st>>>(
+        static_cast<const bf16*>(keys), n, page, ks_kv, ks_n, static_cast<bf16*>(kmax), static_cast<bf16*>(kmin),
+        bs_kv, bs_p, first_page, npages);
+    return cudaGetLastError();
+  });
 }
 
 
@@ -1624,23 +1703,29 @@ cudaError_t launch_quest_select_levels(const pbk_quest_desc& d, const pbk_quest_
   int32_t* cand = reinterpret_cast<int32_t*>(p);
   cudaError_t e = launch_quest_select_parts(superblock_desc(d, lv, top_sb), sb_scratch, 3, st);
   if (e != cudaSuccess) return e;
-  quest_sub_score_kernel<<<dim3((nc + kScoreThreads - 1) / kScoreThreads, nrows), kScoreThreads, 0, st>>>(
-      d, top_sb, lv.m_sb, lv.sblk, full, lv.hole_lo, lv.hole_hi, sub, cand);
+  with_dim(d.d, [&](auto D) {
+    quest_sub_score_kernel<decltype(D)::value>
+        <<<dim3((nc + kScoreThreads - 1) / kScoreThreads, nrows), kScoreThreads, 0, st>>>(
+            d, top_sb, lv.m_sb, lv.sblk, full, lv.hole_lo, lv.hole_hi, sub, cand);
+    return cudaSuccess;
+  });
   e = launch_topk(sub, nc, k2, nrows, d.pages, RefineArgs{}, st);  // canonical candidate scores
   if (e != cudaSuccess) return e;
   quest_map_kernel<<<(nrows * k2 + 255) / 256, 256, 0, st>>>(cand, nc, k2, nrows, d.pages);
   return cudaGetLastError();
 }
 
-cudaError_t launch_quest_superbounds(const void* kmax, const void* kmin, int kv, int n_blk, int sblk, int64_t bs_kv,
-                                     int64_t bs_p, void* smax, void* smin, int64_t ss_kv, int64_t ss_p, int first_sb,
-                                     int end_sb, cudaStream_t st) {
+cudaError_t launch_quest_superbounds(const void* kmax, const void* kmin, int kv, int n_blk, int dim, int sblk,
+                                     int64_t bs_kv, int64_t bs_p, void* smax, void* smin, int64_t ss_kv, int64_t ss_p,
+                                     int first_sb, int end_sb, cudaStream_t st) {
   const int nsb = min(end_sb, (n_blk + sblk - 1) / sblk) - first_sb;
   if (nsb <= 0) return cudaSuccess;
-  quest_superbounds_kernel<<<dim3((nsb + 7) / 8, kv), 256, 0, st>>>(
-      static_cast<const bf16*>(kmax), static_cast<const bf16*>(kmin), bs_kv, bs_p, n_blk, sblk,
-      static_cast<bf16*>(smax), static_cast<bf16*>(smin), ss_kv, ss_p, first_sb, nsb);
-  return cudaGetLastError();
+  return with_dim(dim, [&](auto D) {
+    quest_superbounds_kernel<decltype(D)::value><<<dim3((nsb + 7) / 8, kv), 256, 0, st>>>(
+        static_cast<const bf16*>(kmax), static_cast<const bf16*>(kmin), bs_kv, bs_p, n_blk, sblk,
+        static_cast<bf16*>(smax), static_cast<bf16*>(smin), ss_kv, ss_p, first_sb, nsb);
+    return cudaGetLastError();
+  });
 }
 
 cudaError_t launch_quest_rope_gather(const pbk_rope_gather_desc& d, cudaStream_t st) {
@@ -1648,13 +1733,17 @@ cudaError_t launch_quest_rope_gather(const pbk_rope_gather_desc& d, cudaStream_t
   if (rows == 0) return cudaSuccess;
   if ((d.mode == 1 || d.mode == 2) && d.n_blk > 0) quest_rope_delta_kernel<<<d.kv, 32, 0, st>>>(d);
   const int64_t ctas = (int64_t)d.n_blk + (d.tail_n + kTailRows - 1) / kTailRows;
-  quest_rope_gather_kernel<<<dim3((unsigned)ctas, d.kv), 256, 0, st>>>(d);
-  return cudaGetLastError();
+  return with_dim(d.d, [&](auto D) {
+    quest_rope_gather_kernel<decltype(D)::value><<<dim3((unsigned)ctas, d.kv), 256, 0, st>>>(d);
+    return cudaGetLastError();
+  });
 }
 
-cudaError_t launch_quest_archive_write(const pbk_archive_write_desc& d, cudaStream_t st) {
+namespace {
+template <int D>
+cudaError_t archive_write_dim(const pbk_archive_write_desc& d, cudaStream_t st) {
   auto copy = [&](int i0, int i1) {
-    if (i1 > i0) quest_archive_copy_kernel<<<dim3((unsigned)((i1 - i0 + 7) / 8), d.kv), 256, 0, st>>>(d, i0, i1);
+    if (i1 > i0) quest_archive_copy_kernel<D><<<dim3((unsigned)((i1 - i0 + 7) / 8), d.kv), 256, 0, st>>>(d, i0, i1);
   };
   if (d.pos != nullptr || d.blk_hi < d.blk_lo) {
     copy(0, d.n);
@@ -1666,19 +1755,27 @@ cudaError_t launch_quest_archive_write(const pbk_archive_write_desc& d, cudaStre
     copy((int)hi, d.n);
   }
   const int nblocks = d.blk_hi - d.blk_lo + 1;
-  if (nblocks > 0) quest_archive_block_kernel<<<dim3((unsigned)((nblocks + 7) / 8), d.kv), 256, 0, st>>>(d, nblocks);
+  if (nblocks > 0)
+    quest_archive_block_kernel<D><<<dim3((unsigned)((nblocks + 7) / 8), d.kv), 256, 0, st>>>(d, nblocks);
   return cudaGetLastError();
 }
+}  // namespace
 
-cudaError_t launch_quest_supermeans(const void* bmean, int kv, int n_blk, int sblk, int64_t bs_kv, int64_t bs_p,
-                                    void* smean, int64_t ss_kv, int64_t ss_p, int first_sb, int end_sb,
+cudaError_t launch_quest_archive_write(const pbk_archive_write_desc& d, cudaStream_t st) {
+  return with_dim(d.d, [&](auto D) { return archive_write_dim<decltype(D)::value>(d, st); });
+}
+
+cudaError_t launch_quest_supermeans(const void* bmean, int kv, int n_blk, int dim, int sblk, int64_t bs_kv,
+                                    int64_t bs_p, void* smean, int64_t ss_kv, int64_t ss_p, int first_sb, int end_sb,
                                     cudaStream_t st) {
   const int nsb = min(end_sb, (n_blk + sblk - 1) / sblk) - first_sb;
   if (nsb <= 0) return cudaSuccess;
-  quest_supermeans_kernel<<<dim3((nsb + 7) / 8, kv), 256, 0, st>>>(static_cast<const bf16*>(bmean), bs_kv, bs_p, n_blk,
-                                                                    sblk, static_cast<bf16*>(smean), ss_kv, ss_p,
-                                                                    first_sb, nsb);
-  return cudaGetLastError();
+  return with_dim(dim, [&](auto D) {
+    quest_supermeans_kernel<decltype(D)::value><<<dim3((nsb + 7) / 8, kv), 256, 0, st>>>(
+        static_cast<const bf16*>(bmean), bs_kv, bs_p, n_blk, sblk, static_cast<bf16*>(smean), ss_kv, ss_p, first_sb,
+        nsb);
+    return cudaGetLastError();
+  });
 }
 
 }  // namespace pbk

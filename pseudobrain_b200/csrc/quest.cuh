@@ -53,14 +53,14 @@ cudaError_t launch_quest_gather(const pbk_quest_desc& d, int sel, void* ok, void
 size_t quest_levels_bytes(const pbk_quest_desc& d, const pbk_quest_levels& lv);
 cudaError_t launch_quest_select_levels(const pbk_quest_desc& d, const pbk_quest_levels& lv, uint8_t* ws,
                                        cudaStream_t st);
-cudaError_t launch_quest_superbounds(const void* kmax, const void* kmin, int kv, int n_blk, int sblk, int64_t bs_kv,
-                                     int64_t bs_p, void* smax, void* smin, int64_t ss_kv, int64_t ss_p, int first_sb,
-                                     int end_sb, cudaStream_t st);
+cudaError_t launch_quest_superbounds(const void* kmax, const void* kmin, int kv, int n_blk, int dim, int sblk,
+                                     int64_t bs_kv, int64_t bs_p, void* smax, void* smin, int64_t ss_kv, int64_t ss_p,
+                                     int first_sb, int end_sb, cudaStream_t st);
 cudaError_t launch_quest_rope_gather(const pbk_rope_gather_desc& d, cudaStream_t st);
 cudaError_t launch_quest_archive_write(const pbk_archive_write_desc& d, cudaStream_t st);
-cudaError_t launch_quest_supermeans(const void* bmean, int kv, int n_blk, int sblk, int64_t bs_kv, int64_t bs_p,
-                                    void* smean, int64_t ss_kv, int64_t ss_p, int first_sb, int end_sb,
+cudaError_t launch_quest_supermeans(const void* bmean, int kv, int n_blk, int dim, int sblk, int64_t bs_kv,
+                                    int64_t bs_p, void* smean, int64_t ss_kv, int64_t ss_p, int first_sb, int end_sb,
                                     cudaStream_t st);
-cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int page, int64_t ks_kv, int64_t ks_n, void* kmax,
-                                void* kmin, int64_t bs_kv, int64_t bs_p, int first_page, cudaStream_t st);
+cudaError_t launch_quest_bounds(const void* keys, int kv, int n, int dim, int page, int64_t ks_kv, int64_t ks_n,
+                                void* kmax, void* kmin, int64_t bs_kv, int64_t bs_p, int first_page, cudaStream_t st);
 }  // namespace pbk

@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
 
 }  // namespace
 
-bool quest_attend_mma_supported(const pbk_quest_desc& d) { return d.t * (d.h / d.kv) <= 16; }
+bool quest_attend_mma_supported(const pbk_quest_desc& d) { return d.d == 128 && d.t * (d.h / d.kv) <= 16; }
 
 // Split length S in [256, 512] (a multiple of 16) that minimises waves x S, the launch's
 // length in key tiles: with `slots` resident blocks, the fewest waves, then the shortest

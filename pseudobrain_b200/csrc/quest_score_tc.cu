@@ -321,7 +321,7 @@ constexpr size_t kSmemBytes = sizeof(ScoreSmem) + 1024;
 
 bool quest_score_tc_supported(const pbk_quest_desc& d) {
   const int rows = d.nq * d.t * (d.h / d.kv);
-  return rows <= kMaxRows && d.n_arch / d.page > 0;
+  return d.d == 128 && rows <= kMaxRows && d.n_arch / d.page > 0;
 }
 
 int quest_score_tc_tiles(const pbk_quest_desc& d) { return (d.n_arch / d.page + kTileP - 1) / kTileP; }

@@ -10,7 +10,6 @@
 namespace pbk {
 namespace {
 
-constexpr int kD = 128;
 using bf16 = __nv_bfloat16;
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4 raw, float* out) {
@@ -31,22 +30,23 @@ __device__ __forceinline__ uint32_t ordered_key(float f) {
 // ---------------------------------------------------------------------------------
 // Per-token block scores (memory.py:1079-1086, 1094-1098): out[kv][t][j] = max over the key
 // head's query heads g of sum_d q_{t,g,d} * (q > 0 ? kmax : kmin)_{b,d}, b = cand[kv][j] (or
-// j), summed over d = 0 .. 127 in order; -inf for b >= full and for b in the hole. Thread =
+// j), summed over d = 0 .. D - 1 in order; -inf for b >= full and for b in the hole. Thread =
 // candidate; the rows of kTokRows / groups tokens sit in shared memory as fp32.
 // ---------------------------------------------------------------------------------
 constexpr int kTokThreads = 128;
 constexpr int kTokRows = 32;  // query rows (token x head) per pass
 
+template <int D>
 __global__ void __launch_bounds__(kTokThreads) quest_token_score_kernel(const pbk_token_desc d) {
-  __shared__ __align__(16) float qs[kTokRows][kD];
+  __shared__ __align__(16) float qs[kTokRows][D];
   const int h = blockIdx.y, groups = d.h / d.kv;
   const int tpb = max(1, kTokRows / groups);  // tokens per pass
   const int t0 = blockIdx.z * tpb, nt = min(tpb, d.t - t0);
   const int rows = nt * groups;
-  for (int e = threadIdx.x; e < rows * kD; e += kTokThreads) {
-    const int r = e / kD, dd = e % kD, ti = t0 + r / groups, g = r % groups;
+  for (int e = threadIdx.x; e < rows * D; e += kTokThreads) {
+    const int r = e / D, dd = e % D, ti = t0 + r / groups, g = r % groups;
     const bf16* qp = reinterpret_cast<const bf16*>(d.q) + ti * d.q_stride_t + (int64_t)(h * groups + g) * d.q_stride_h;
-    qs[r][dd] = (d.rope_mask && dd < kD / 4) ? 0.f : __bfloat162float(qp[dd]);
+    qs[r][dd] = (d.rope_mask && dd < D / 4) ? 0.f : __bfloat162float(qp[dd]);
   }
   __syncthreads();
   const int j = blockIdx.x * kTokThreads + threadIdx.x;
@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(kTokThreads) quest_token_score_kernel(const pb
   float acc[kTokRows];
 #pragma unroll
   for (int r = 0; r < kTokRows; ++r) acc[r] = 0.f;
-  for (int d0 = 0; d0 < kD; d0 += 8) {
+  for (int d0 = 0; d0 < D; d0 += 8) {
     float mx[8], mn[8];
     bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmax + d0), mx);
     bf16x8_to_f32(*reinterpret_cast<const uint4*>(bmin + d0), mn);
@@ -94,14 +94,15 @@ __global__ void __launch_bounds__(kTokThreads) quest_token_score_kernel(const pb
 // CTA = (8 candidates, key head, tokens of one pass); warp = candidate, lane = tokens lane,
 // lane + 32, ...
 // ---------------------------------------------------------------------------------
+template <int D>
 __global__ void __launch_bounds__(256) quest_token_rerank_kernel(const pbk_token_desc d) {
-  __shared__ __align__(16) float qs[kTokRows][kD];
+  __shared__ __align__(16) float qs[kTokRows][D];
   const int h = blockIdx.y, groups = d.h / d.kv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tpb = max(1, kTokRows / groups);
   const int t0 = blockIdx.z * tpb, nt = min(tpb, d.t - t0);
   const int rows = nt * groups;
-  for (int e = threadIdx.x; e < rows * kD; e += blockDim.x) {
-    const int r = e / kD, dd = e % kD, ti = t0 + r / groups, g = r % groups;
+  for (int e = threadIdx.x; e < rows * D; e += blockDim.x) {
+    const int r = e / D, dd = e % D, ti = t0 + r / groups, g = r % groups;
     qs[r][dd] = __bfloat162float(reinterpret_cast<const bf16*>(d.q)[ti * d.q_stride_t +
                                                                      (int64_t)(h * groups + g) * d.q_stride_h + dd]);
   }
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(256) quest_token_rerank_kernel(const pbk_token
     float acc[kTokRows];
 #pragma unroll
     for (int r = 0; r < kTokRows; ++r) acc[r] = 0.f;
-    for (int d0 = 0; d0 < kD; d0 += 8) {  // dims in order, 8 at a time
+    for (int d0 = 0; d0 < D; d0 += 8) {  // dims in order, 8 at a time
       float kf[8];
       bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + d0), kf);
 #pragma unroll
@@ -212,14 +213,16 @@ cudaError_t launch_quest_token_scores(const pbk_token_desc& d, cudaStream_t st) 
   const int tpb = tokens_per_pass(d);
   const dim3 grid((unsigned)((d.n_pool + kTokThreads - 1) / kTokThreads), (unsigned)d.kv,
                   (unsigned)((d.t + tpb - 1) / tpb));
-  quest_token_score_kernel<<<grid, kTokThreads, 0, st>>>(d);
+  if (d.d == 256) quest_token_score_kernel<256><<<grid, kTokThreads, 0, st>>>(d);
+  else quest_token_score_kernel<128><<<grid, kTokThreads, 0, st>>>(d);
   return cudaGetLastError();
 }
 
 cudaError_t launch_quest_token_rerank(const pbk_token_desc& d, cudaStream_t st) {
   const int tpb = tokens_per_pass(d);
   const dim3 grid((unsigned)((d.n_pool + 7) / 8), (unsigned)d.kv, (unsigned)((d.t + tpb - 1) / tpb));
-  quest_token_rerank_kernel<<<grid, 256, 0, st>>>(d);
+  if (d.d == 256) quest_token_rerank_kernel<256><<<grid, 256, 0, st>>>(d);
+  else quest_token_rerank_kernel<128><<<grid, 256, 0, st>>>(d);
   return cudaGetLastError();
 }
 

@@ -19,7 +19,8 @@ plus the fused path of this build, which never materialises the gathered keys:
 ``retrieve`` takes every selection mode of the reference: flat, the two-level
 super-block selection of decode queries (pbk_quest_select_levels over the super-block
 bounds that ``archive_append`` keeps), the exact ``rerank`` (pbk_quest_rerank), a kept
-prompt selection and ``neighbors``. Keys are bf16 with head_dim 128; every call runs CUDA
+prompt selection and ``neighbors``. Keys are bf16 with head_dim 128 or 256 (256 on the SIMT
+kernels: the tensor-core score and attention kernels are written for 128); every call runs CUDA
 kernels from libpbk.so and there is no CPU path.
 """
 from __future__ import annotations
@@ -58,8 +59,8 @@ def _require(t: torch.Tensor, what: str) -> None:
         raise RuntimeError(f"{what}: pseudobrain_b200 runs on CUDA only (no CPU fallback)")
     if t.dtype != torch.bfloat16:
         raise TypeError(f"{what}: bf16 expected, got {t.dtype}")
-    if t.shape[-1] != 128 or t.stride(-1) != 1:
-        raise ValueError(f"{what}: head_dim must be 128 and contiguous")
+    if t.shape[-1] not in (128, 256) or t.stride(-1) != 1:
+        raise ValueError(f"{what}: head_dim must be 128 or 256 and contiguous")
 
 
 def _ptr(t: torch.Tensor | None):

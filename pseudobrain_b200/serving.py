@@ -27,7 +27,8 @@ with the block summaries (max, min, key and value means) and the super-block ref
 
 Kernels: pbk_quest_select (scores + top-k), pbk_quest_select_levels, pbk_quest_rerank,
 pbk_quest_superbounds, pbk_quest_supermeans, pbk_quest_archive_write, pbk_quest_rope_gather,
-pbk_quest_attend_sinks (libpbk.so, sm_100a); head dim 128.
+pbk_quest_attend_sinks (libpbk.so, sm_100a); head dims 128 and 256 (PB-27's 24 query / 4 key
+heads at 256 run on the SIMT score and attention kernels).
 """
 from __future__ import annotations
 

@@ -39,6 +39,10 @@ Fixtures:
   pertoken.npz    the serving per-token selector retrieve_blocks_per_token: prompt, decode,
                   no-lead, global-aggregation and holed-archive steps with the selector state
                   before and after each.
+  pertoken256.npz the same at PB-27's attention shape (4 key heads x 6 query heads, head dim 256).
+  serving256.npz  the serving twins at PB-27's shape: archive summaries, retrieve_blocks (flat,
+                  super-block, rerank, holed rerank, rerank past a lowered RoPE horizon) and
+                  piece_attention.
   archive_write.npz  the serving Archive.write: a prefill write, short and scattered writes
                   and a long write across super-blocks into a CPU archive, then
                   refresh_bounds; its final storage, block and super-block summaries.
@@ -380,17 +384,18 @@ def make_pertoken(MEM):
     saved = (torch.Tensor.topk, torch.Tensor.argsort)
     torch.Tensor.topk, torch.Tensor.argsort = topk, argsort
     try:
-        _make_pertoken(MEM)
+        _make_pertoken(MEM, 2, 3, 128, 300, "pertoken.npz")
+        _make_pertoken(MEM, 4, 6, 256, 120, "pertoken256.npz")  # PB-27's attention shape: 24 query / 4 key heads
     finally:
         torch.Tensor.topk, torch.Tensor.argsort = saved
 
 
-def _make_pertoken(MEM):
+def _make_pertoken(MEM, kv, groups, d, n_blocks, fname):
     import torch
-    kv, groups, d, block = 2, 3, 128, 16
+    block = 16
     MEM.SBLK = 2
     MEM.MEMORY.update(blocks=8, decode_blocks=8, rerank=12, block_size=block, neighbors=0, window=64, chunk=64)
-    cap = MEM.ORIGIN + 300 * block + 10
+    cap = MEM.ORIGIN + n_blocks * block + 10
     gen = torch.Generator().manual_seed(207)
     keys = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
     values = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
@@ -453,7 +458,66 @@ def _make_pertoken(MEM):
     MEM.GLOBAL_AGG = "auto"
     out["steps"] = np.array(names)
     out["limit"] = np.int64(limit)
-    np.savez_compressed(os.path.join(HERE, "pertoken.npz"), **out)
+    np.savez_compressed(os.path.join(HERE, fname), **out)
+
+
+def make_serving256(MEM):
+    """The serving twins at PB-27's attention shape (24 query / 4 key heads, head dim 256):
+    the archive summaries (block bounds and means, super-block bounds and means after the
+    refresh), retrieve_blocks in its flat, super-block (super-blocks of 2), rerank and
+    holed-rerank paths, and past a lowered RoPE horizon (1000) the rerank with moved
+    candidates, each followed by piece_attention over sinks, blocks, tail and window."""
+    import torch
+    kv, groups, d, block = 4, 6, 256, 16
+    MEM.SBLK = 2
+    MEM.MEMORY.update(blocks=6, decode_blocks=6, rerank=12, block_size=block, neighbors=0, window=256)
+    cap = MEM.ORIGIN + 100 * block + 9
+    gen = torch.Generator().manual_seed(311)
+    keys = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    values = torch.randn(kv, cap, d, generator=gen).to(torch.bfloat16).float()
+    n_blk = cap // block
+    n_sb = (n_blk + MEM.SBLK - 1) // MEM.SBLK
+    arc = MEM.Archive(keys, values, torch.empty(kv, n_blk, d), torch.empty(kv, n_blk, d))
+    arc.smax, arc.smin = torch.empty(kv, n_sb, d), torch.empty(kv, n_sb, d)
+    arc.bmean_k, arc.bmean_v = torch.empty(kv, n_blk, d), torch.empty(kv, n_blk, d)
+    arc.smean_k, arc.smean_v = torch.empty(kv, n_sb, d), torch.empty(kv, n_sb, d)
+    arc.size = arc.prompt_len = cap
+    arc.dirty_lo, arc.dirty_hi = 0, n_blk - 1
+    arc.refresh_bounds(block)
+    out = dict(keys=_bits(keys.to(torch.bfloat16)), values=_bits(values.to(torch.bfloat16)),
+               kmax=_bits(arc.kmax.to(torch.bfloat16)), kmin=_bits(arc.kmin.to(torch.bfloat16)),
+               smax=_bits(arc.smax.to(torch.bfloat16)), smin=_bits(arc.smin.to(torch.bfloat16)),
+               bmean_k=arc.bmean_k.numpy(), bmean_v=arc.bmean_v.numpy(), smean_k=arc.smean_k.numpy(),
+               smean_v=arc.smean_v.numpy(), origin=np.int64(MEM.ORIGIN), sblk=np.int64(MEM.SBLK),
+               block=np.int64(block), groups=np.int64(groups), window=np.int64(256), cap=np.int64(cap))
+    hole = (MEM.ORIGIN + 40 * block + 3, MEM.ORIGIN + 70 * block)
+    for name, t, rerank, use_sb, hole_on, horizon in (("flat", 1, False, False, False, 0),
+                                                      ("sb", 1, False, True, False, 0),
+                                                      ("rr", 1, True, False, False, 0),
+                                                      ("hole_rr", 2, True, True, True, 0),
+                                                      ("rope_rr", 1, True, False, False, 1000)):
+        if horizon:
+            MEM.ROPE_HORIZON = horizon
+        arc.hole_lo, arc.hole_hi = hole if hole_on else (0, 0)
+        saved = (arc.smax, arc.smin)
+        if not use_sb:
+            arc.smax = arc.smin = None
+        q = torch.randn(t, kv * groups, d, generator=gen).to(torch.bfloat16).float()
+        q_pos = torch.arange(cap - t, cap)
+        q_min, q_max = int(q_pos[0]), int(q_pos[-1])
+        limit = q_min - 256 + 1
+        top = MEM.retrieve_blocks(arc, q, groups, limit, rerank)
+        arc.smax, arc.smin = saved
+        o = MEM.piece_attention(arc, q, q_pos, top, groups, 256, d ** -0.5, None, q_min=q_min, q_max=q_max)
+        out.update({f"{name}_q": _bits(q.to(torch.bfloat16)), f"{name}_limit": np.int64(limit),
+                    f"{name}_rerank": np.int64(rerank), f"{name}_sb": np.int64(use_sb),
+                    f"{name}_hole": np.array(hole if hole_on else (0, 0)), f"{name}_horizon": np.int64(horizon),
+                    f"{name}_top": top.numpy().astype(np.int64), f"{name}_out": o.float().numpy()})
+        MEM.ROPE_HORIZON = 262144
+    arc.hole_lo = arc.hole_hi = 0
+    MEM.SBLK = 64
+    out["cases"] = np.array(["flat", "sb", "rr", "hole_rr", "rope_rr"])
+    np.savez_compressed(os.path.join(HERE, "serving256.npz"), **out)
 
 
 def make_gdn_io(G):
@@ -511,7 +575,8 @@ def main(reference_root: str) -> None:
     makers = {"gdn": lambda: make_gdn(G), "quest": lambda: make_quest(E), "swa": lambda: make_swa(TR),
               "serving": lambda: make_serving(MEM), "gdn_io": lambda: make_gdn_io(G),
               "quest_levels": lambda: make_quest_levels(E, MEM), "rope": lambda: make_rope(MEM),
-              "archive_write": lambda: make_archive_write(MEM), "pertoken": lambda: make_pertoken(MEM)}
+              "archive_write": lambda: make_archive_write(MEM), "pertoken": lambda: make_pertoken(MEM),
+              "serving256": lambda: make_serving256(MEM)}
     for name in (sys.argv[2:] if len(sys.argv) > 2 else makers):  # all, or only the named fixtures
         makers[name]()
     for name in sorted(os.listdir(HERE)):

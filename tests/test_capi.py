@@ -118,8 +118,10 @@ def test_token_entry_points_validate_on_the_host(lib):
     from pseudobrain_b200 import _capi
     d = _capi.PbkTokenDesc(t=1, h=40, kv=1, d=128, n_pool=4, full=4)
     assert _capi.LIB.pbk_quest_token_scores(ctypes.byref(d), None) == -2  # 40 heads per key head
+    d = _capi.PbkTokenDesc(t=1, h=8, kv=2, d=192, n_pool=4, full=4)
+    assert _capi.LIB.pbk_quest_token_scores(ctypes.byref(d), None) == -2  # head dims 128 and 256 only
     d = _capi.PbkTokenDesc(t=1, h=8, kv=2, d=256, n_pool=4, full=4)
-    assert _capi.LIB.pbk_quest_token_scores(ctypes.byref(d), None) == -2  # head dim 256
+    assert _capi.LIB.pbk_quest_token_scores(ctypes.byref(d), None) == -1  # 256 is a shape; q is missing
     d = _capi.PbkTokenDesc(t=0, h=8, kv=2, d=128, n_pool=4, full=4)
     assert _capi.LIB.pbk_quest_token_rerank(ctypes.byref(d), None) == 0   # nothing to do
     assert _capi.LIB.pbk_quest_row_ranks(None, 20000, 1, 20000, None, 20000, None) == -2

@@ -42,9 +42,12 @@ def selector(cuda_device):
     serving.SBLK, pertoken.GLOBAL_AGG = saved[1], saved[2]
 
 
-def test_per_token_selection_matches_reference(cuda_device, selector):
+@pytest.mark.parametrize("fixture", ["pertoken.npz", "pertoken256.npz"])
+def test_per_token_selection_matches_reference(cuda_device, selector, fixture):
+    """pertoken.npz: 2 key heads x 3 query heads at head dim 128; pertoken256.npz: PB-27's
+    attention shape, 4 key heads x 6 query heads at head dim 256."""
     pertoken, serving = selector
-    f = np.load(FIX)
+    f = np.load(os.path.join(ROOT, "tests", "golden", fixture))
     dev = cuda_device
     serving.MEMORY.update(blocks=8, decode_blocks=8, rerank=12, block_size=int(f["block"]), neighbors=0, window=64,
                           chunk=64)
@@ -76,7 +79,7 @@ def test_per_token_selection_matches_reference(cuda_device, selector):
         top = res[0].cpu().numpy()
         want = f[f"{name}_top"]
         diffs[name] = int((top != want).sum()) if top.shape == want.shape else -1
-        print(f"[per-token] {name}: {diffs[name]} differing block indices of {want.size}")
+        print(f"[per-token {fixture}] {name}: {diffs[name]} differing block indices of {want.size}")
         assert top.shape == want.shape and np.array_equal(top, want), name
         assert bool(arc.is_global_agg) == bool(f[f"{name}_after_global"]), name
         assert arc.decode_step == int(f[f"{name}_after_decode_step"]), name
@@ -89,10 +92,10 @@ def test_per_token_selection_matches_reference(cuda_device, selector):
         if f"{name}_attn" in f.files:  # the piece's attention (landmarks after the sinks under global aggregation)
             qpos = torch.tensor([limit + 63], device=dev)
             o = serving.piece_attention(arc, _bf(f[f"{name}_q"], dev), qpos, res[0], groups, int(f["window"]),
-                                        128 ** -0.5, None, q_min=limit + 63, q_max=limit + 63)
+                                        keys.shape[-1] ** -0.5, None, q_min=limit + 63, q_max=limit + 63)
             ref = f[f"{name}_attn"]
             err = float(np.linalg.norm(o.float().cpu().numpy() - ref) / np.linalg.norm(ref))
-            print(f"[per-token] {name}: attention rel err {err:.2e}")
+            print(f"[per-token {fixture}] {name}: attention rel err {err:.2e}")
             assert err < 2e-2, name
             assert arc.cached_top is res[0]  # the reference caches the set when a prompt set exists
 
