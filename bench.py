@@ -21,9 +21,13 @@ Multi-GPU (torchrun, one rank per GPU): weak scaling. Every rank runs its own sh
 (sequence x value head) chains of the same per-GPU size; the recurrence has no
 exchange step, so there is no collective inside the timed region.
 
-``--impl reference`` times the CPU restatement of the reference algorithm (oracle/,
-numpy, all host cores) on bounded samples of the same workload and prints the same
-metric; under torchrun only rank 0 runs it. ``--workload``/``--size small`` run one part
+``serving`` times the serving twins at PB-27's attention shape (head dim 256; the head-dim-128
+figures beside them) and the per-token selector's decode selection.
+
+``--impl reference`` times the CPU restatement of the reference algorithm
+(oracle/cpu_reference.py: the reference's own torch CPU operations, all host cores) on
+bounded samples of the same workload and prints the same metric; under torchrun only rank 0
+runs it. ``--workload``/``--size small`` run one part
 on a reduced case, for profiler captures only (such a line is not a bench number).
 """
 from __future__ import annotations
@@ -356,15 +360,15 @@ def graphed(torch, fn):
     return g.replay, g
 
 
-def measure_serving(args, timed, dev, rank, world, pk):
-    """The serving twins (pb27_vllm/memory.py retrieve_blocks with exact rerank +
-    piece_attention) for one decode token of a PB-27-shaped layer (24 query / 4 key heads,
-    head dim 128 here), a 262144-token archive in 64-token blocks, window 16384 and the
-    reference's defaults: 512 candidates reranked exactly, 256 blocks kept."""
+def _serving_piece(args, timed, dev, rank, world, pk, d):
+    """One decode token of a PB-27-shaped layer (24 query / 4 key heads, head dim d) through the
+    serving twins (retrieve_blocks with exact rerank + piece_attention): a 262144-token archive
+    in 64-token blocks, window 16384 and the reference's defaults (512 candidates reranked
+    exactly, 256 blocks kept)."""
     import types
     import torch
     from pseudobrain_b200 import serving as S
-    kv, heads, d, block, window = 4, 24, 128, 64, 16384
+    kv, heads, block, window = 4, 24, 64, 16384
     cap = 262144 if args.size == "full" else 65536
     gen = torch.Generator(device=dev).manual_seed(6 + 1000 * rank)
     keys = torch.randn(kv, cap, d, device=dev, generator=gen).to(torch.bfloat16)
@@ -399,6 +403,52 @@ def measure_serving(args, timed, dev, rank, world, pk):
             "roofline": {"bound": "hbm", "achieved": nbytes / t / 1e9, "peak": pk["hbm"], "unit": "GB/s",
                          "frac": nbytes / t / 1e9 / pk["hbm"], "traffic": None, "algorithmic_bytes": nbytes},
             "gpu_launches": 8 * steps}
+
+
+def _pertoken_decode(args, timed, dev, rank, d):
+    """The serving default selector (retrieve_blocks_per_token) on a decode step of the same
+    layer: a 16-token query history over the archive's 4096 blocks (super-blocks of 64), merged
+    with a prompt selection, recomputed every call (the reference recomputes it every 64th
+    decode step and reuses the set in between)."""
+    import types
+    import torch
+    from pseudobrain_b200 import pertoken as P
+    from pseudobrain_b200 import serving as S
+    kv, heads, block, window = 4, 24, 64, 16384
+    cap = 262144 if args.size == "full" else 65536
+    gen = torch.Generator(device=dev).manual_seed(8 + 1000 * rank)
+    keys = torch.randn(kv, cap, d, device=dev, generator=gen).to(torch.bfloat16)
+    n_blk = cap // block
+    n_sb = (n_blk + S.SBLK - 1) // S.SBLK
+    z = lambda rows: torch.zeros(kv, rows, d, dtype=torch.bfloat16, device=dev)  # noqa: E731
+    arc = types.SimpleNamespace(keys=keys, values=keys, kmax=z(n_blk), kmin=z(n_blk), smax=z(n_sb), smin=z(n_sb),
+                                size=cap, prompt_len=cap, hole_lo=0, hole_hi=0, dirty_lo=0, dirty_hi=n_blk - 1)
+    limit = cap - window
+    qp = torch.randn(64, heads, d, device=dev, generator=gen).to(torch.bfloat16)
+    P.retrieve_blocks_per_token(arc, qp, heads // kv, limit, 0, -1)  # the prompt's selection (kept)
+    hist = torch.randn(16, heads, d, device=dev, generator=gen).to(torch.bfloat16)
+
+    def step():
+        arc.cached_top = None
+        P.retrieve_blocks_per_token(arc, hist[-1:], heads // kv, limit, 0, 0, 0, hist)
+
+    steps = max(args.steps, 20)
+    t = timed(step, steps, max(args.warmup, 3)) / steps
+    return {"us_per_selection": t * 1e6, "us_per_decode_step": t * 1e6 / P.DECODE_STRIDE,
+            "timing": f"eager, one uncached decode selection per call (recomputed every {P.DECODE_STRIDE}th step)",
+            "config": {"archive_tokens": cap, "kv_heads": kv, "q_heads": heads, "head_dim": d, "block": block,
+                       "query_history": 16, "decode_blocks": P.DECODE_BLOCKS}}
+
+
+def measure_serving(args, timed, dev, rank, world, pk):
+    """The serving twins at PB-27's attention shape (head dim 256, the SIMT score and attention
+    kernels), with the head-dim-128 figures (tensor-core score and attention kernels) and the
+    per-token selector's decode selection beside them."""
+    main = _serving_piece(args, timed, dev, rank, world, pk, 256)
+    hd128 = _serving_piece(args, timed, dev, rank, world, pk, 128)
+    main["hd128"] = {key: hd128[key] for key in ("value", "us_per_piece", "roofline")}
+    main["pertoken"] = _pertoken_decode(args, timed, dev, rank, 256)
+    return main
 
 
 def measure_widen(args, timed, dev, rank, world, pk):
