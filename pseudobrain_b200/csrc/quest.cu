@@ -772,7 +772,10 @@ __global__ void __launch_bounds__(kAttThreads, 2) quest_attend_kernel(const pbk_
   __shared__ int kidx[kSplitKeys];     // archive token, or -1 - window index
   __shared__ float red[kAttRows][kAttWarps];
   __shared__ float sh_m[kAttRows], sh_l[kAttRows];
-  __shared__ __align__(16) float accs[kAttWarps][kAttRows][D];
+  // the warps' partial P V sums, [kAttWarps][kAttRows][D] in dynamic shared memory (64 KB at
+  // 8 rows x 256 dims, past the 48 KB of static shared memory)
+  extern __shared__ __align__(16) float accs_raw[];
+  auto accs = reinterpret_cast<float (*)[kAttRows][D]>(accs_raw);
   const int split = split0 + blockIdx.x, n = blockIdx.y / d.kv, h = blockIdx.y % d.kv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int groups = d.h / d.kv, rows = d.t * groups;
@@ -997,19 +1000,20 @@ __global__ void __launch_bounds__(128) quest_combine_kernel(const pbk_quest_desc
 // candidates, group*kv + key head), warp = one candidate page, lane = tokens lane,
 // lane + 32, ...; the query rows sit in shared memory.
 // ---------------------------------------------------------------------------------
-constexpr int kRerankRows = 32;  // query rows in shared memory per pass
-template <int D>
+// kRows query rows per pass (8, 16 or 32: the launch picks the smallest that holds the key
+// head's rows, so the unrolled row loop does no dead iterations).
+template <int D, int kRows>
 __global__ void __launch_bounds__(256) quest_rerank_kernel(const pbk_quest_desc d, const int32_t* cand, int c,
                                                            float* exact) {
-  __shared__ __align__(16) float qs[kRerankRows][D];
+  __shared__ __align__(16) float qs[kRows][D];
   const int n = blockIdx.y / d.kv, h = blockIdx.y % d.kv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = d.h / d.kv, rows = d.t * groups;
   const int ci = blockIdx.x * 8 + warp;
   const int page = ci < c ? cand[((int64_t)n * d.kv + h) * c + ci] : 0;
   const bf16* base = reinterpret_cast<const bf16*>(d.keys) + h * d.arc_stride_kv;
   float best = -INFINITY;
-  for (int r0 = 0; r0 < rows; r0 += kRerankRows) {
-    const int nr = min(kRerankRows, rows - r0);
+  for (int r0 = 0; r0 < rows; r0 += kRows) {
+    const int nr = min(kRows, rows - r0);
     __syncthreads();
     for (int e = threadIdx.x; e < nr * D; e += blockDim.x) {
       const int r = e / D, dd = e % D, ti = (r0 + r) / groups, g = (r0 + r) % groups;
@@ -1020,32 +1024,39 @@ __global__ void __launch_bounds__(256) quest_rerank_kernel(const pbk_quest_desc 
     if (ci >= c) continue;
     for (int s = lane; s < d.page; s += 32) {
       const bf16* kr = base + ((int64_t)page * d.page + s) * d.arc_stride_n;
-      float acc[kRerankRows];
+      float acc[kRows];
 #pragma unroll
-      for (int r = 0; r < kRerankRows; ++r) acc[r] = 0.f;
-      for (int d0 = 0; d0 < D; d0 += 8) {  // dims in order, 8 at a time, every row
-        float kf[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + d0), kf);
+      for (int r = 0; r < kRows; ++r) acc[r] = 0.f;
+#pragma unroll 1
+      for (int h0 = 0; h0 < D; h0 += 64) {  // 64 dims (8 loads) of the key in flight
+        uint4 raw[8];
 #pragma unroll
-        for (int r = 0; r < kRerankRows; ++r) {
-          if (r < nr) {
-            const float4 qa = *reinterpret_cast<const float4*>(&qs[r][d0]);
-            const float4 qb = *reinterpret_cast<const float4*>(&qs[r][d0 + 4]);
-            float a = acc[r];
-            a = fmaf(qa.x, kf[0], a);
-            a = fmaf(qa.y, kf[1], a);
-            a = fmaf(qa.z, kf[2], a);
-            a = fmaf(qa.w, kf[3], a);
-            a = fmaf(qb.x, kf[4], a);
-            a = fmaf(qb.y, kf[5], a);
-            a = fmaf(qb.z, kf[6], a);
-            a = fmaf(qb.w, kf[7], a);
-            acc[r] = a;
+        for (int c8 = 0; c8 < 8; ++c8) raw[c8] = *reinterpret_cast<const uint4*>(kr + h0 + 8 * c8);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {  // dims in order
+          float kf[8];
+          bf16x8_to_f32(raw[c8], kf);
+#pragma unroll
+          for (int r = 0; r < kRows; ++r) {
+            if (r < nr) {
+              const float4 qa = *reinterpret_cast<const float4*>(&qs[r][h0 + 8 * c8]);
+              const float4 qb = *reinterpret_cast<const float4*>(&qs[r][h0 + 8 * c8 + 4]);
+              float a = acc[r];
+              a = fmaf(qa.x, kf[0], a);
+              a = fmaf(qa.y, kf[1], a);
+              a = fmaf(qa.z, kf[2], a);
+              a = fmaf(qa.w, kf[3], a);
+              a = fmaf(qb.x, kf[4], a);
+              a = fmaf(qb.y, kf[5], a);
+              a = fmaf(qb.z, kf[6], a);
+              a = fmaf(qb.w, kf[7], a);
+              acc[r] = a;
+            }
           }
         }
       }
 #pragma unroll
-      for (int r = 0; r < kRerankRows; ++r)
+      for (int r = 0; r < kRows; ++r)
         if (r < nr) best = fmaxf(best, acc[r]);
     }
   }
@@ -1564,12 +1575,19 @@ cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const Sink
     const int s0 = (parts & 1) ? 0 : sr, s1 = (parts & 2) ? splits : sr;
     if (s1 > s0) {
       const dim3 grid(s1 - s0, d.nq * d.kv);
-      if (d.d == 256)  // 4 query rows per pass: the partial sums of 8 x 256 dims exceed static shared memory
-        quest_attend_kernel<256, 4><<<grid, kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
-      else if (d.t * (d.h / d.kv) > 4)
-        quest_attend_kernel<128, 8><<<grid, kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
-      else
-        quest_attend_kernel<128, 4><<<grid, kAttThreads, 0, st>>>(d, k, tail, splits, part, s0, sk);
+      const bool eight = d.t * (d.h / d.kv) > 4;  // 8 query rows per pass, else 4
+      auto go = [&](auto kernel, int rows_per_pass) {
+        const size_t smem = (size_t)kAttWarps * rows_per_pass * d.d * sizeof(float);
+        if (smem > 48 * 1024) {
+          cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+          if (e != cudaSuccess) return e;
+        }
+        kernel<<<grid, kAttThreads, smem, st>>>(d, k, tail, splits, part, s0, sk);
+        return cudaGetLastError();
+      };
+      cudaError_t e = d.d == 256 ? (eight ? go(quest_attend_kernel<256, 8>, 8) : go(quest_attend_kernel<256, 4>, 4))
+                                 : (eight ? go(quest_attend_kernel<128, 8>, 8) : go(quest_attend_kernel<128, 4>, 4));
+      if (e != cudaSuccess) return e;
     }
   }
   if (!(parts & 4)) return cudaGetLastError();
@@ -1589,8 +1607,13 @@ cudaError_t launch_quest_attend(const pbk_quest_desc& d, float* part, const Sink
 cudaError_t launch_quest_rerank(const pbk_quest_desc& d, const int32_t* cand, int c, float* exact, cudaStream_t st) {
   const int k = min(d.budget, c), nrows = d.nq * d.kv;
   if (k <= 0) return cudaSuccess;
+  const int rows = d.t * (d.h / d.kv);
   with_dim(d.d, [&](auto D) {
-    quest_rerank_kernel<decltype(D)::value><<<dim3((c + 7) / 8, nrows), 256, 0, st>>>(d, cand, c, exact);
+    constexpr int kDim = decltype(D)::value;
+    const dim3 grid((c + 7) / 8, nrows);
+    if (rows <= 8) quest_rerank_kernel<kDim, 8><<<grid, 256, 0, st>>>(d, cand, c, exact);
+    else if (rows <= 16) quest_rerank_kernel<kDim, 16><<<grid, 256, 0, st>>>(d, cand, c, exact);
+    else quest_rerank_kernel<kDim, 32><<<grid, 256, 0, st>>>(d, cand, c, exact);
     return cudaSuccess;
   });
   cudaError_t e = cudaFuncSetAttribute(quest_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

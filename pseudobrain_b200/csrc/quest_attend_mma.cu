@@ -28,14 +28,16 @@ constexpr int kTile = 16;       // keys per stage
 constexpr int kStages = 2;
 constexpr int kWarps = 4;
 constexpr int kSinkTag = -(1 << 30);  // same key encoding as quest.cu
-constexpr int kRowBytes = kD * 2;     // 256 bytes per key row
 
-struct WarpSmem {
-  uint8_t k[kStages][kTile * kRowBytes];  // 4 KB a stage, row r at r * 256, chunk c at (c ^ (r & 7))
-  uint8_t v[kStages][kTile * kRowBytes];
+// A warp's staging ring for head dim D: row r at r * 2D bytes, 16-byte chunk c at (c ^ (r & 7)).
+template <int D>
+struct WarpSmemT {
+  uint8_t k[kStages][kTile * D * 2];
+  uint8_t v[kStages][kTile * D * 2];
   int kpos[kStages][kTile];  // window keys' positions (for the mask)
   int kidx[kMaxSplit];       // the split's key indices (encoding as in quest.cu)
 };
+using WarpSmem = WarpSmemT<kD>;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -71,8 +73,9 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
-// byte offset of 16-byte chunk c of row r in a swizzled 256-byte-row tile
-__device__ __forceinline__ uint32_t sw_off(int r, int c) { return r * kRowBytes + ((c ^ (r & 7)) << 4); }
+// byte offset of 16-byte chunk c of row r in a swizzled tile of 2D-byte rows
+template <int D = kD>
+__device__ __forceinline__ uint32_t sw_off(int r, int c) { return r * (2 * D) + ((c ^ (r & 7)) << 4); }
 
 __device__ __forceinline__ bool visible(int kp, int qp, int window, int sinks) {
   return kp <= qp && ((qp - kp) < window || kp < sinks);
@@ -91,17 +94,19 @@ __device__ __forceinline__ int key_index(const pbk_quest_desc& d, int k, const S
 // Tile s of the warp's split into stage b: 16 key and 16 value rows of 16 chunks (8 of each
 // per lane), and the window keys' positions; rows past the split are zeroed (their
 // probabilities are 0, and 0 * (stale bits) could be NaN). One cp.async group per tile.
-__device__ __forceinline__ void stage_tile(WarpSmem& ws, int s, int b, int lane, const pbk_quest_desc& d,
+template <int D>
+__device__ __forceinline__ void stage_tile(WarpSmemT<D>& ws, int s, int b, int lane, const pbk_quest_desc& d,
                                            const SinkKeys& sk, int h) {
+  constexpr int kChunks = D / 8;  // 16-byte chunks per row
   const bf16* keys = reinterpret_cast<const bf16*>(d.keys);
   const bf16* vals = reinterpret_cast<const bf16*>(d.values);
   const bf16* wkeys = reinterpret_cast<const bf16*>(d.win_keys);
   const bf16* wvals = reinterpret_cast<const bf16*>(d.win_values);
 #pragma unroll
-  for (int it = 0; it < kTile * 16 / 32; ++it) {
-    const int c = it * 32 + lane, r = c >> 4, ch = c & 15;
+  for (int it = 0; it < kTile * kChunks / 32; ++it) {
+    const int c = it * 32 + lane, r = c / kChunks, ch = c % kChunks;
     const int idx = ws.kidx[s * kTile + r];
-    const uint32_t ko = smem_u32(ws.k[b]) + sw_off(r, ch), vo = smem_u32(ws.v[b]) + sw_off(r, ch);
+    const uint32_t ko = smem_u32(ws.k[b]) + sw_off<D>(r, ch), vo = smem_u32(ws.v[b]) + sw_off<D>(r, ch);
     if (idx == INT32_MIN) {
       asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(ko), "r"(0u) : "memory");
       asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vo), "r"(0u) : "memory");
@@ -312,12 +317,14 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
 // shapes, and a quarter of its O registers. A window task serves every query of a
 // group of qpg = 8 / rows-per-query queries at once: the window keys are the same for all
 // queries of a key head (only the mask differs), so they are staged once per group.
-__global__ void __launch_bounds__(32 * kWarps, 3)
+template <int D>
+__global__ void __launch_bounds__(32 * kWarps, D == 128 ? 3 : 1)
     quest_attend_n8_kernel(const pbk_quest_desc d, int k, int tail, int split_keys, int sr, int sw, int qpg,
                            float* part, SinkKeys sk, int task0, int task_end) {
+  constexpr int kK = D / 16;  // k-steps of S^T = K Q^T, m-tiles of O^T
   extern __shared__ __align__(16) uint8_t attn_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  WarpSmem& ws = reinterpret_cast<WarpSmem*>(attn_raw)[warp];
+  WarpSmemT<D>& ws = reinterpret_cast<WarpSmemT<D>*>(attn_raw)[warp];
   const int task = task0 + blockIdx.x * kWarps + warp;
   const int ret_tasks = d.nq * d.kv * sr;
   if (task >= task_end) return;
@@ -359,12 +366,12 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
   };
   auto row_pos = [&](int r) { return d.qpos[(n0 + r / rpq) * d.t + (r % rpq) / groups]; };
   // Q^T fragments (B: k = dims, n = row g): b0 = Q[g][16kk + 2t..], b1 = Q[g][16kk + 8 + 2t..]
-  uint32_t qb[8][2];
+  uint32_t qb[kK][2];
   {
     const bool ok = g < rows;
     const bf16* qr = ok ? row_q(g) : q;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
+    for (int kk = 0; kk < kK; ++kk) {
       qb[kk][0] = ok ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 2 * t) : 0u;
       qb[kk][1] = ok ? *reinterpret_cast<const uint32_t*>(qr + 16 * kk + 8 + 2 * t) : 0u;
     }
@@ -373,9 +380,9 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
 #pragma unroll
   for (int e = 0; e < 2; ++e) qp[e] = 2 * t + e < rows ? row_pos(2 * t + e) : 0;
 
-  float o[8][4];  // O^T: dims 16 mt + g (+ 8) x rows 2t, 2t + 1
+  float o[kK][4];  // O^T: dims 16 mt + g (+ 8) x rows 2t, 2t + 1
 #pragma unroll
-  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  for (int mt = 0; mt < kK; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // rows 2t, 2t + 1 (lane partial l)
 
   for (int s = 0; s < ntiles; ++s) {
@@ -386,11 +393,11 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
     // S^T = K Q^T: keys g, g + 8 (c0/c1 and c2/c3) x rows 2t, 2t + 1; even and odd k-steps apart
     float sc[4] = {0.f, 0.f, 0.f, 0.f}, sc2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
+    for (int kk = 0; kk < kK; ++kk) {
       // matrices: (keys 0-7, dims 16kk..+7), (keys 8-15, same), (keys 0-7, +8..15), (keys 8-15, +8..15)
       const int mi = lane >> 3, row = (mi & 1) * 8 + (lane & 7);
       uint32_t a0, a1, a2, a3;
-      ldsm_x4(kb + sw_off(row, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
+      ldsm_x4(kb + sw_off<D>(row, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
       if (kk & 1) mma_bf16(sc2, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
       else mma_bf16(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
     }
@@ -425,7 +432,7 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
     for (int r = 0; r < 2; ++r) l_run[r] = l_run[r] * fac[r] + (p[r] + p[2 + r]);
     if (__any_sync(0xffffffffu, fac[0] != 1.f || fac[1] != 1.f)) {
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
+      for (int mt = 0; mt < kK; ++mt) {
         o[mt][0] *= fac[0];
         o[mt][1] *= fac[1];
         o[mt][2] *= fac[0];
@@ -436,11 +443,11 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
     const uint32_t pb0 = movmatrix_t(pack_bf16(p[0], p[1])), pb1 = movmatrix_t(pack_bf16(p[2], p[3]));
     // O^T += V^T P^T: A = V^T (dims 16 mt .. x keys) by ldmatrix.trans of the V rows
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
+    for (int mt = 0; mt < kK; ++mt) {
       // matrices: (keys 0-7, dims 16mt..+7), (keys 0-7, +8..15), (keys 8-15, ..+7), (keys 8-15, +8..15)
       const int mi = lane >> 3, row = (mi >> 1) * 8 + (lane & 7), ch = 2 * mt + (mi & 1);
       uint32_t a0, a1, a2, a3;
-      ldsm_x4_t(vb + sw_off(row, ch), a0, a1, a2, a3);
+      ldsm_x4_t(vb + sw_off<D>(row, ch), a0, a1, a2, a3);
       mma_bf16(o[mt], a0, a1, a2, a3, pb0, pb1);
     }
     __syncwarp();  // stage b is rewritten by tile s + 2
@@ -460,26 +467,32 @@ __global__ void __launch_bounds__(32 * kWarps, 3)
     if (r >= rows) continue;
     const int n = n0 + r / rpq, rem = r % rpq, ti = rem / groups, gg = rem % groups;
     const int64_t prow = (((int64_t)n * d.t + ti) * d.h + h * groups + gg) * splits + split;
-    float* pp = part + prow * (kD + 2);
+    float* pp = part + prow * (D + 2);
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
+    for (int mt = 0; mt < kK; ++mt) {
       pp[16 * mt + g] = o[mt][e];
       pp[16 * mt + 8 + g] = o[mt][2 + e];
     }
-    if (g == 0) pp[kD] = m_run[e], pp[kD + 1] = l_run[e];
+    if (g == 0) pp[D] = m_run[e], pp[D + 1] = l_run[e];
   }
 }
 
 }  // namespace
 
-bool quest_attend_mma_supported(const pbk_quest_desc& d) { return d.d == 128 && d.t * (d.h / d.kv) <= 16; }
+// Head dim 128: up to 16 query rows per key head (8-row and 16-row kernels); head dim 256: up
+// to 8 (the 8-row kernel).
+bool quest_attend_mma_supported(const pbk_quest_desc& d) {
+  const int rpq = d.t * (d.h / d.kv);
+  return (d.d == 128 && rpq <= 16) || (d.d == 256 && rpq <= 8);
+}
 
 // Split length S in [256, 512] (a multiple of 16) that minimises waves x S, the launch's
 // length in key tiles: with `slots` resident blocks, the fewest waves, then the shortest
 // splits. Returns the number of splits per (query, key head) through *splits_out.
 static int slots_for(const void* kernel, size_t smem, cudaError_t* err) {
-  static int slots[2][64] = {};  // resident blocks per device (SMs x blocks per SM), per kernel
-  const int which = kernel == (const void*)quest_attend_n8_kernel ? 1 : 0;
+  static int slots[3][64] = {};  // resident blocks per device (SMs x blocks per SM), per kernel
+  const int which = kernel == (const void*)quest_attend_n8_kernel<128> ? 1
+                    : kernel == (const void*)quest_attend_n8_kernel<256> ? 2 : 0;
   int dev = 0;
   if ((*err = cudaGetDevice(&dev)) != cudaSuccess) return 0;
   if (dev >= 64) return 148;
@@ -495,10 +508,12 @@ static int slots_for(const void* kernel, size_t smem, cudaError_t* err) {
 
 cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, float* part, const SinkKeys& sk,
                                     int parts, int* splits_out, cudaStream_t st) {
-  const size_t smem = sizeof(WarpSmem) * kWarps;
+  const bool wide = d.d == 256;
+  const size_t smem = (wide ? sizeof(WarpSmemT<256>) : sizeof(WarpSmem)) * kWarps;
   const int rpq = d.t * (d.h / d.kv);
   const bool n8 = rpq <= 8;
-  const void* kernel = n8 ? (const void*)quest_attend_n8_kernel : (const void*)quest_attend_mma_kernel;
+  const void* kernel = wide ? (const void*)quest_attend_n8_kernel<256>
+                       : n8 ? (const void*)quest_attend_n8_kernel<128> : (const void*)quest_attend_mma_kernel;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int slots = slots_for(kernel, smem, &e);
@@ -524,8 +539,12 @@ cudaError_t launch_quest_attend_mma(const pbk_quest_desc& d, int k, int tail, fl
   const int task0 = (parts & 1) ? 0 : ret_tasks, task_end = (parts & 2) ? all_tasks : ret_tasks;
   if (task_end <= task0) return cudaSuccess;
   const unsigned blocks = (unsigned)((task_end - task0 + kWarps - 1) / kWarps);
-  if (n8)
-    quest_attend_n8_kernel<<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sw, qpg, part, sk, task0, task_end);
+  if (wide)
+    quest_attend_n8_kernel<256><<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sw, qpg, part, sk, task0,
+                                                                   task_end);
+  else if (n8)
+    quest_attend_n8_kernel<128><<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sw, qpg, part, sk, task0,
+                                                                   task_end);
   else
     quest_attend_mma_kernel<<<blocks, 32 * kWarps, smem, st>>>(d, k, tail, best, sr, sr + sw, part, sk, task0,
                                                                task_end);

@@ -119,9 +119,16 @@ __global__ void __launch_bounds__(256) quest_token_rerank_kernel(const pbk_token
     float acc[kTokRows];
 #pragma unroll
     for (int r = 0; r < kTokRows; ++r) acc[r] = 0.f;
-    for (int d0 = 0; d0 < D; d0 += 8) {  // dims in order, 8 at a time
+#pragma unroll 1
+    for (int h0 = 0; h0 < D; h0 += 64) {  // 64 dims (8 loads) of the key in flight, dims in order
+      uint4 raw[8];
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) raw[c8] = *reinterpret_cast<const uint4*>(kr + h0 + 8 * c8);
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+      const int d0 = h0 + 8 * c8;
       float kf[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(kr + d0), kf);
+      bf16x8_to_f32(raw[c8], kf);
 #pragma unroll
       for (int r = 0; r < kTokRows; ++r) {
         if (r < rows) {
@@ -138,6 +145,7 @@ __global__ void __launch_bounds__(256) quest_token_rerank_kernel(const pbk_token
           a = fmaf(qb.w, kf[7], a);
           acc[r] = a;
         }
+      }
       }
     }
 #pragma unroll
