@@ -739,6 +739,15 @@ __global__ void __launch_bounds__(NT, 1)
   const uint32_t i_kmn = tc::idesc_bf16_f32(128, 64, false, true);   // A K-major, B MN-major, N=64
   const uint32_t i_mnk = tc::idesc_bf16_f32(128, 64, true, false);   // A MN-major, B K-major, N=64
   const uint32_t i_s = tc::idesc_bf16_f32(128, 128, false, true);    // S update, N=128
+  // Operand descriptors: one 128B-swizzle descriptor per leading-byte offset at the start of
+  // the shared struct; a tile's descriptor adds its byte offset / 16 (the 14-bit address
+  // field never carries: shared addresses stay below 256 KB). Rebuilding a descriptor from a
+  // runtime address at every MMA costs the issuing thread more than the MMA itself.
+  const uint32_t s_base = tc::smem_u32(&sm);
+  const uint64_t d16 = tc::sdesc_sw128(s_base, 16, 1024);      // K-major; MN-major one atom wide
+  const uint64_t d16k = tc::sdesc_sw128(s_base, 16384, 1024);  // MN-major over the two K|Q atoms
+  const uint64_t d8k = tc::sdesc_sw128(s_base, 8192, 1024);    // MN-major over the two V atoms
+  auto kq_desc = [&](uint64_t base, int buf) { return base + ((offsetof(PrefillSmem, kq) + (size_t)buf * 32768) >> 4); };
 
   // TMA loads (4-D maps over [B,T,H,128], rows past T zero-filled, no multicast). K|Q of
   // chunk m go to buffer m&1 (issued by the serial leader once chunk m-2's state update is
@@ -796,23 +805,16 @@ __global__ void __launch_bounds__(NT, 1)
     int last_v = 0;  // last V load issued (for the bounded drain)
     for (int m = 0; m < nchunks && ok; ++m) {
       const int buf = m & 1, sb = m & 3;
-      // K|Q, V (and TB | TBG) of chunk m + 2 into L2 now: their loads into shared memory wait
-      // for buffers that free up one chunk later, and then hit L2
-      if (pt == 0 && m + 2 < nchunks) {
-        for (int a = 0; a < 2; ++a) {
-          tc::tma_prefetch_4d(&tm_k, 64 * a, t0 + (m + 2) * C, hk, b);
-          tc::tma_prefetch_4d(&tm_q, 64 * a, t0 + (m + 2) * C, hk, b);
-          tc::tma_prefetch_4d(&tm_v, 64 * a, t0 + (m + 2) * C, h, b);
-        }
-        if (kOffload) tc::bulk_prefetch_l2(p.solve + ((cbase + m + 2) * p.hv + h) * kSolveBytes, kSolveBytes);
-      }
+      // (No L2 prefetch of later chunks: issuing it queues behind this SM's loads in the TMA
+      // unit and delays the prep leader by more than it saves.)
       // ---- [K;Q] K^T first: the scalar scan below runs under the MMA
       if (!pwait(&sm.bar_kq[buf], (m >> 1) & 1, 1)) break;
       if (pt == 0) {
+        const uint64_t kd = kq_desc(d16, buf);
+#pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t base = tc::smem_u32(sm.kq[buf][kk >> 2]) + (kk & 3) * 32;
-          tc::mma_f16(tmem + kColD1, tc::sdesc_sw128(base, 16, 1024), tc::sdesc_sw128(base, 16, 1024), i_kk,
-                      kk != 0);
+          const uint64_t dsc = kd + (kk >> 2) * 1024 + (kk & 3) * 2;
+          tc::mma_f16(tmem + kColD1, dsc, dsc, i_kk, kk != 0);
         }
         tc::mma_commit(&sm.bar_p1);
       }
@@ -917,16 +919,13 @@ __global__ void __launch_bounds__(NT, 1)
       // ---- W^T = K^T TBG^T -> D1; U'^T = V^T TB^T -> UP[buf]
       if (!pwait(&sm.bar_v, m & 1, 3)) break;
       if (pt == 0) {
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][0]) + kk * 2048, 16384, 1024);
-          const uint64_t bd = tc::sdesc_sw128(tc::smem_u32(sm.tbg) + kk * 32, 16, 1024);
-          tc::mma_f16(tmem + kColD1, ad, bd, i_mnk, kk != 0);
-        }
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.v[0]) + kk * 2048, 8192, 1024);
-          const uint64_t bd = tc::sdesc_sw128(tc::smem_u32(sm.tb) + kk * 32, 16, 1024);
-          tc::mma_f16(tmem + kColUP + 64 * buf, ad, bd, i_mnk, kk != 0);
-        }
+        const uint64_t kmn = kq_desc(d16k, buf), tbg = d16 + (offsetof(PrefillSmem, tbg) >> 4);
+        const uint64_t vmn = d8k + (offsetof(PrefillSmem, v) >> 4), tb = d16 + (offsetof(PrefillSmem, tb) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + kColD1, kmn + kk * 128, tbg + kk * 2, i_mnk, kk != 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_f16(tmem + kColUP + 64 * buf, vmn + kk * 128, tb + kk * 2, i_mnk, kk != 0);
         tc::mma_commit(&sm.bar_p3);
       }
       if (!pwait(&sm.bar_p3, m & 1, 4)) break;
@@ -995,12 +994,13 @@ __global__ void __launch_bounds__(NT, 1)
     // (QS)^T = S^T Q^T of chunk n (thread 0): the state's bf16 copy in st, Q in chunk n's K|Q.
     // Its TMEM columns must have been read for chunk n-1, and st stays unchanged until the
     // chunk's S update commits (which covers QS: commits track every earlier MMA).
+    const uint64_t st_d = d16 + (offsetof(PrefillSmem, st) >> 4);
     auto issue_qs = [&](int n) {
-      const int buf = n & 1;
+      const uint64_t qd = kq_desc(d16, n & 1) + (8192 >> 4);
+#pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
-        const uint64_t bq = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][kk >> 2]) + 8192 + (kk & 3) * 32, 16, 1024);
-        tc::mma_f16(tmem + kColQS, ad, bq, i_kk, kk != 0);
+        const uint64_t o = (kk >> 2) * 1024 + (kk & 3) * 2;
+        tc::mma_f16(tmem + kColQS, st_d + o, qd + o, i_kk, kk != 0);
       }
     };
     auto state_step = [&](int n) {
@@ -1029,11 +1029,10 @@ __global__ void __launch_bounds__(NT, 1)
       role_sync(1);
       if (tid == 0) {
         tc::fence_after_sync();
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.st[kk >> 2]) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bw = tc::sdesc_sw128(tc::smem_u32(sm.wt[buf]) + kk * 2048, 16, 1024);
-          tc::mma_f16(tmem + kColWS, ad, bw, i_kmn, kk != 0);
-        }
+        const uint64_t wd = d16 + ((offsetof(PrefillSmem, wt) + (size_t)buf * 16384) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc::mma_f16(tmem + kColWS, st_d + (kk >> 2) * 1024 + (kk & 3) * 2, wd + kk * 128, i_kmn, kk != 0);
         // With U diag(e) in its own buffer (offloaded solve) QS leaves the critical path: it
         // is issued once the previous chunk's outputs have been read (issue_qs below).
         if (!kOffload) issue_qs(n);
@@ -1077,6 +1076,7 @@ __global__ void __launch_bounds__(NT, 1)
     // U diag(e), the A operand of the state update: its own tile when the solve is offloaded
     // (the unused A scratch), else st[0] once the S^T products are done
     uint8_t* const ue = kOffload ? reinterpret_cast<uint8_t*>(sm.a) : sm.st[0];
+    const uint64_t ue_d = d16 + ((kOffload ? offsetof(PrefillSmem, a) : offsetof(PrefillSmem, st)) >> 4);
     if (swait(&sm.prep_ready, 0, 1)) {
       state_step(0);
       if (kOffload && p.o != nullptr && tid == 0) issue_qs(0);
@@ -1103,16 +1103,13 @@ __global__ void __launch_bounds__(NT, 1)
       role_sync(1);
       if (tid == 0) {
         tc::fence_after_sync();
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(sm.ut) + kk * 32, 16, 1024);
-          const uint64_t bm = tc::sdesc_sw128(tc::smem_u32(sm.m[buf]) + kk * 32, 16, 1024);
-          tc::mma_f16(tmem + kColUM, ad, bm, i_kk, kk != 0);
-        }
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(tc::smem_u32(ue) + kk * 32, 16, 1024);
-          const uint64_t bk = tc::sdesc_sw128(tc::smem_u32(sm.kq[buf][0]) + kk * 2048, 16384, 1024);
-          tc::mma_f16(tmem + kColS, ad, bk, i_s, 1);
-        }
+        const uint64_t ud = d16 + (offsetof(PrefillSmem, ut) >> 4);
+        const uint64_t md = d16 + ((offsetof(PrefillSmem, m) + (size_t)buf * 8192) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + kColUM, ud + kk * 2, md + kk * 2, i_kk, kk != 0);
+        const uint64_t kmn = kq_desc(d16k, buf);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc::mma_f16(tmem + kColS, ue_d + kk * 2, kmn + kk * 128, i_s, 1);
         tc::mma_commit(&sm.bar_s);
       }
       if (!swait(&sm.bar_s, n & 1, 3)) break;
