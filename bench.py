@@ -11,7 +11,9 @@ carries the other two parts of the metric, each with its own roofline:
 (config 3: 8 queries over a 1M-token cache, q/s) and ``hybrid`` (config 4: one GDN +
 sliding-window attention layer over a 1M-token sequence, heads split over the ranks with
 an NCCL all-gather of each branch's output; tok/s, strong scaling). ``e2e`` times the public API with
-pinned host inputs copied in and outputs copied back inside the timed region.
+pinned host inputs copied in and outputs copied back inside the timed region: streamed (prefill
+by sequence, decode by step) so that the copies in, the kernels and the copies out overlap,
+with the one-stream figure beside it as ``serial_value``.
 
 ``widen`` times the rows around the hot path (the GDN layer's conv / gating / output norm at
 config-1 shapes, the two-level Quest selection, the serving archive write and the RoPE move
@@ -172,6 +174,30 @@ class Timer:
         return self.max_over_ranks(st.elapsed_time(en) / 1e3)
 
 
+def timed_streams(timed, fn, steps, warmup, first, others):
+    """Device time of K calls of a step that spreads its work over several streams: the start
+    event on `first` (the stream each step's first work goes to), the end event on the current
+    stream after it has waited for `first` and every stream in `others`; barrier + synchronize
+    on both sides, max over ranks."""
+    torch = timed.torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    timed.barrier()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record(first)
+    for _ in range(steps):
+        fn()
+    cur = torch.cuda.current_stream(timed.dev)
+    for s in (first, *others):
+        cur.wait_stream(s)
+    en.record(cur)
+    torch.cuda.synchronize()
+    timed.barrier()
+    return timed.max_over_ranks(st.elapsed_time(en) / 1e3)
+
+
 def measure_prefill(args, timed, dev, rank, world, pk):
     import torch
     from pseudobrain_b200.gdn_prefill import chunk_solve, gdn_prefill_, prefill_solved
@@ -218,14 +244,48 @@ def measure_prefill(args, timed, dev, rank, world, pk):
     dev_in = {n: torch.empty_like(x[n]) for n in host}
     host_o = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
 
-    def e2e():
+    def e2e_serial():
         for n, tt in host.items():
             dev_in[n].copy_(tt, non_blocking=True)
         gdn_prefill_(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], None, state, o, x["scale"])
         host_o.copy_(o, non_blocking=True)
 
+    # The same step streamed by sequence: sequence b's inputs go up on a copy stream while
+    # sequence b-1 computes, and its output comes back on a second copy stream (PCIe is full
+    # duplex) while sequence b+1's inputs go up. Every step still copies all its inputs and
+    # reads back all its outputs.
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_comp = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    nb = P["batch"]
+    ev_in, ev_comp, ev_out = ([torch.cuda.Event() for _ in range(nb)] for _ in range(3))
+    started = [False]
+
+    def e2e_streamed():
+        for bb in range(nb):
+            with torch.cuda.stream(s_in):
+                if started[0]:
+                    s_in.wait_event(ev_comp[bb])  # the previous step's sequence bb has read its inputs
+                for n, tt in host.items():
+                    dev_in[n][bb].copy_(tt[bb], non_blocking=True)
+                ev_in[bb].record(s_in)
+            sc = s_comp[bb % 2]
+            sc.wait_event(ev_in[bb])
+            if started[0]:
+                sc.wait_event(ev_out[bb])  # the previous step's output of sequence bb is back
+            with torch.cuda.stream(sc):
+                sl = slice(bb, bb + 1)
+                gdn_prefill_(dev_in["q"][sl], dev_in["k"][sl], dev_in["v"][sl], dev_in["g"][sl], dev_in["beta"][sl],
+                             None, state[sl], o[sl], x["scale"])
+                ev_comp[bb].record(sc)
+            s_out.wait_event(ev_comp[bb])
+            with torch.cuda.stream(s_out):
+                host_o[bb].copy_(o[bb], non_blocking=True)
+                ev_out[bb].record(s_out)
+        started[0] = True
+
     e2e_steps = max(3, args.steps // 2)
-    t_e2e = timed(e2e, e2e_steps, min(args.warmup, 3))
+    t_e2e_serial = timed(e2e_serial, e2e_steps, min(args.warmup, 3))
+    t_e2e = timed_streams(timed, e2e_streamed, e2e_steps, min(args.warmup, 3), s_in, [s_out, *s_comp])
     return {
         "value": world * tokens * args.steps / t, "unit": "tok/s", "ms_per_step": per_step * 1e3,
         "tokens": tokens,
@@ -243,7 +303,9 @@ def measure_prefill(args, timed, dev, rank, world, pk):
                  "traffic_over_algorithmic": step_traffic / algo_bytes if step_traffic else None},
         "e2e": {"value": world * tokens * e2e_steps / t_e2e, "unit": "tok/s",
                 "h2d_bytes_per_step": sum(tt.numel() * tt.element_size() for tt in host.values()),
-                "d2h_bytes_per_step": host_o.numel() * host_o.element_size()},
+                "d2h_bytes_per_step": host_o.numel() * host_o.element_size(),
+                "copies": f"streamed by sequence ({nb} slices): input copies, compute and output copies overlap",
+                "serial_value": world * tokens * e2e_steps / t_e2e_serial},
         "gpu_launches": 2 * args.steps,  # chunk solve + recurrence
     }
 
@@ -269,14 +331,47 @@ def measure_decode(args, timed, dev, rank, world, pk):
     dev_in = {n: torch.empty_like(xd[n]) for n in host}
     host_o = torch.empty(od.shape, dtype=od.dtype, pin_memory=True)
 
-    def e2e():
+    def e2e_serial():
         for n, tt in host.items():
             dev_in[n].copy_(tt, non_blocking=True)
         G.gdn_recurrent_(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], None, xd["h0"], od,
                          xd["scale"])
         host_o.copy_(od, non_blocking=True)
 
-    t_e2e = timed(e2e, 200, 10)
+    # Streamed: step i+1's inputs go up (into the other of two input slots) while step i
+    # computes, and step i's output comes back while step i+1 computes; the steps themselves
+    # stay in order on one stream (each updates the state in place).
+    s_in, s_c, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    slots = [dev_in, {n: torch.empty_like(xd[n]) for n in host}]
+    outs = [od, torch.empty_like(od)]
+    host_os = [host_o, torch.empty(od.shape, dtype=od.dtype, pin_memory=True)]
+    ev_in, ev_comp, ev_out = ([torch.cuda.Event(), torch.cuda.Event()] for _ in range(3))
+    it = [0]
+
+    def e2e_streamed():
+        i = it[0]
+        sl = i & 1
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_comp[sl])  # step i-2 has read this input slot
+            for n, tt in host.items():
+                slots[sl][n].copy_(tt, non_blocking=True)
+            ev_in[sl].record(s_in)
+        s_c.wait_event(ev_in[sl])
+        if i >= 2:
+            s_c.wait_event(ev_out[sl])  # step i-2's output is back on the host
+        with torch.cuda.stream(s_c):
+            d = slots[sl]
+            G.gdn_recurrent_(d["q"], d["k"], d["v"], d["g"], d["beta"], None, xd["h0"], outs[sl], xd["scale"])
+            ev_comp[sl].record(s_c)
+        s_out.wait_event(ev_comp[sl])
+        with torch.cuda.stream(s_out):
+            host_os[sl].copy_(outs[sl], non_blocking=True)
+            ev_out[sl].record(s_out)
+        it[0] = i + 1
+
+    t_e2e_serial = timed(e2e_serial, 200, 10)
+    t_e2e = timed_streams(timed, e2e_streamed, 200, 10, s_in, [s_c, s_out])
     return {
         "metric": "GDN decode steps/s (config 2)", "value": world * nsteps / t, "unit": "steps/s",
         "us_per_step": per_step * 1e6,
@@ -285,7 +380,9 @@ def measure_decode(args, timed, dev, rank, world, pk):
                      "algorithmic_bytes": nbytes},
         "e2e": {"value": world * 200 / t_e2e, "unit": "steps/s",
                 "h2d_bytes_per_step": sum(tt.numel() * tt.element_size() for tt in host.values()),
-                "d2h_bytes_per_step": host_o.numel() * host_o.element_size()},
+                "d2h_bytes_per_step": host_o.numel() * host_o.element_size(),
+                "copies": "streamed: step i+1's input copy and step i-1's output copy overlap step i",
+                "serial_value": world * 200 / t_e2e_serial},
         "gpu_launches": nsteps,
     }
 
