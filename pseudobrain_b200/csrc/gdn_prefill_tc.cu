@@ -285,14 +285,16 @@ __device__ __forceinline__ void store_tb_tbg(const float* ts, const float* beta,
 
 // ------------------------------------------------------------------ chunk solve kernel
 // The state-independent part of every chunk, for all chunks of all (sequence, value head)
-// chains at once: one CTA (4 warps) per (chunk, value head, sequence) computes the chunk's
-// cumulative decay, A = strict_lower(beta_t K K^T * D) (K K^T by bf16 mma.sync, fp32
-// accumulate) in 16x16 blocks, T = (I + A)^-1 (diagonal blocks by substitution in fp32, the
-// off-diagonal blocks by tf32 mma.sync products in three levels, the same arithmetic as the
-// in-kernel solve), and writes TB and TBG (16 KB: the two bf16 tiles in the byte image the
-// prefill kernel's MMAs read) to workspace slot (sequence, chunk, head). The prefill kernel
-// then only copies them in.
-constexpr int kSolveThreads = 128;
+// chains at once: one CTA per (chunk, group of G value heads sharing a key head, sequence)
+// computes K K^T once (bf16 mma.sync, fp32 accumulate, 16x16 blocks) and, per value head in
+// a group of 4 warps, the chunk's cumulative decay, A = strict_lower(beta_t K K^T * D),
+// T = (I + A)^-1 (diagonal blocks by substitution in fp32, the off-diagonal blocks by tf32
+// mma.sync products in three levels, the same arithmetic as the in-kernel solve), and writes
+// TB and TBG (16 KB: the two bf16 tiles in the byte image the prefill kernel's MMAs read) to
+// workspace slot (sequence, chunk, head). The prefill kernel then only copies them in. G = 2
+// when the value heads per key head are even (the two heads of a pair share K and K K^T),
+// else 1.
+constexpr int kSolveThreads = 128;  // per value head
 // TB | TBG | ChunkScalars per (sequence, chunk, value head)
 constexpr uint32_t kSolveBytes = 2 * 8192 + sizeof(ChunkScalars);
 static_assert(sizeof(ChunkScalars) % 16 == 0, "bulk copies move multiples of 16 bytes");
@@ -305,17 +307,33 @@ __device__ __forceinline__ int bidx(int r, int c) { return r * 16 + (c ^ bsw(r))
 // Off-diagonal block (i > j) number: (1,0) 0, (2,0) 1, (2,1) 2, (3,0) 3, (3,1) 4, (3,2) 5.
 __host__ __device__ constexpr int oidx(int i, int j) { return i * (i - 1) / 2 + j; }
 
+struct SolveTX {       // one value head's inverse blocks
+  float t[10][256];    // T blocks: diagonal b at b, off-diagonal (i, j) at 4 + oidx(i, j)
+  float x[4][256];     // X_20, X_21, X_30, X_31 (level 1 scratch in x[0], x[1])
+};
+struct SolveHead {     // one value head's A and scalars
+  float at[4][16][16]; // diagonal blocks of A, transposed: at[b][m][r] = A[16b + r][16b + m]
+  float ao[6][256];    // off-diagonal blocks of A
+  float c2[C], gam[C], beta[C];
+};
+template <int G>
 struct SolveSmem {
   union {
     uint8_t k[C * 256];  // K rows of the chunk, 16-byte chunk c of row r at (c ^ (r & 7))
-    struct {             // after K K^T:
-      float t[10][256];  // T blocks: diagonal b at b, off-diagonal (i, j) at 4 + oidx(i, j)
-      float x[4][256];   // X_20, X_21, X_30, X_31 (level 1 scratch in x[0], x[1])
-    } w;
+    SolveTX w;           // after K K^T: head 0's inverse
   };
-  float at[4][16][16];  // diagonal blocks of A, transposed: at[b][m][r] = A[16b + r][16b + m]
-  float ao[6][256];     // off-diagonal blocks of A
-  float c2[C], gam[C], beta[C];
+  SolveTX w_more[G - 1];  // heads 1 .. G-1
+  SolveHead hd[G];
+  __device__ __forceinline__ SolveTX& tx(int g) { return g == 0 ? w : w_more[g - 1]; }
+};
+template <>
+struct SolveSmem<1> {
+  union {
+    uint8_t k[C * 256];
+    SolveTX w;
+  };
+  SolveHead hd[1];
+  __device__ __forceinline__ SolveTX& tx(int) { return w; }
 };
 
 struct SolveArgs {
@@ -416,10 +434,26 @@ __global__ void __launch_bounds__(1024) gdn_chunk_offsets_kernel(const int32_t* 
   if (tid == 1023) chunk_off[num_seqs] = warp_tot[31];
 }
 
-__global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArgs p) {
+// Barrier of the 4 warps of value-head group g (named barrier 1 + g), or of the CTA when it
+// holds one group.
+template <int G>
+__device__ __forceinline__ void group_sync(int g) {
+  static_assert(G <= 2, "named barriers 1 and 2");
+  if constexpr (G == 1) {
+    __syncthreads();
+  } else if (g == 0) {
+    asm volatile("bar.sync 1, %0;" ::"n"(kSolveThreads) : "memory");
+  } else {
+    asm volatile("bar.sync 2, %0;" ::"n"(kSolveThreads) : "memory");
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const SolveArgs p) {
   extern __shared__ __align__(16) uint8_t solve_raw[];
-  SolveSmem& sm = *reinterpret_cast<SolveSmem*>(solve_raw);
-  const int h = blockIdx.y, b = blockIdx.z;
+  SolveSmem<G>& sm = *reinterpret_cast<SolveSmem<G>*>(solve_raw);
+  constexpr int NT = kSolveThreads * G, kWarps = NT / 32;
+  const int b = blockIdx.z;
   // this CTA's chunk m of a sequence at rows t0 .. t0 + len, workspace slot `cslot`
   int m = blockIdx.x, t0 = 0, len = p.seqlen;
   int64_t cslot = (int64_t)b * gridDim.x + m;
@@ -430,10 +464,15 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
     cslot = m;
     m -= p.chunk_off[s];
   }
-  const int hkh = h / (p.hv / p.hk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // value-head group: warps 4 gi .. 4 gi + 3 (threads gt = 0..127 of it) own head h; the G
+  // heads of the CTA are consecutive and share key head hkh
+  const int gi = warp >> 2, gw = warp & 3, gt = tid & (kSolveThreads - 1);
+  const int h = blockIdx.y * G + gi;
+  const int hkh = (blockIdx.y * G) / (p.hv / p.hk);
+  SolveHead& hd = sm.hd[gi];
   // K rows (zero past the sequence end, the reference's padding)
-  for (int c = tid; c < C * 16; c += kSolveThreads) {
+  for (int c = tid; c < C * 16; c += NT) {
     const int r = c >> 4, ch = c & 15, t = m * C + r;
     const uint32_t dst = tc::smem_u32(sm.k) + r * 256 + ((ch ^ (r & 7)) << 4);
     if (t < len) {
@@ -444,8 +483,9 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
     }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
-  // cumulative log2 decay and gamma (warp 0; lane l: steps 2l, 2l + 1; zero past the end)
-  if (warp == 0) {
+  // cumulative log2 decay and gamma (the group's first warp; lane l: steps 2l, 2l + 1; zero
+  // past the end)
+  if (gw == 0) {
     constexpr float kLog2e = 1.4426950408889634f;
     const int t = m * C + 2 * lane;
     const int64_t tg = t0 + t;  // row in the (packed) tensor
@@ -472,12 +512,12 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
     }
     const float c0 = (incl - pair + g0) * kLog2e, c1 = incl * kLog2e;
     const float ga0 = exp2f(c0), ga1 = exp2f(c1);
-    sm.c2[2 * lane] = c0;
-    sm.c2[2 * lane + 1] = c1;
-    sm.gam[2 * lane] = ga0;
-    sm.gam[2 * lane + 1] = ga1;
-    sm.beta[2 * lane] = b0;
-    sm.beta[2 * lane + 1] = b1;
+    hd.c2[2 * lane] = c0;
+    hd.c2[2 * lane + 1] = c1;
+    hd.gam[2 * lane] = ga0;
+    hd.gam[2 * lane + 1] = ga1;
+    hd.beta[2 * lane] = b0;
+    hd.beta[2 * lane + 1] = b1;
     // the chunk's scalar record for the recurrence kernel (after TB | TBG): e = exp2(c_last -
     // c), and the factored decay about c_ref = c_31 while the log2 span stays below 60
     ChunkScalars* rec = reinterpret_cast<ChunkScalars*>(p.ws + (cslot * p.hv + h) * kSolveBytes + 2 * 8192);
@@ -500,23 +540,24 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
   __syncthreads();
   const int g = lane >> 2, t4 = lane & 3, mi = lane >> 3;
   // ---- K K^T on the 10 lower 16x16 blocks (rb, cb), cb <= rb, numbered row by row; warp w
-  // takes blocks w, w + 4, w + 8. Epilogue: A = beta_t K K^T exp2(c_t - c_i) below the
-  // diagonal, zero on and above it; diagonal blocks stored transposed (substitution), the
-  // others in the block layout (mma operands).
+  // takes blocks w, w + kWarps, ... Epilogue, for each head of the CTA: A = beta_t K K^T
+  // exp2(c_t - c_i) below the diagonal, zero on and above it; diagonal blocks stored
+  // transposed (substitution), the others in the block layout (mma operands).
   {
+    constexpr int kQ = (10 + kWarps - 1) / kWarps;
     auto rb_of = [](int j) { return j >= 6 ? 3 : (j >= 3 ? 2 : (j >= 1 ? 1 : 0)); };
     auto cb_of = [&](int j) { return j - rb_of(j) * (rb_of(j) + 1) / 2; };
     const uint32_t kb = tc::smem_u32(sm.k);
-    float acc[3][2][4];
+    float acc[kQ][2][4];
 #pragma unroll
-    for (int q = 0; q < 3; ++q)
+    for (int q = 0; q < kQ; ++q)
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) acc[q][nt][0] = acc[q][nt][1] = acc[q][nt][2] = acc[q][nt][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {  // k-steps of 16 dims
 #pragma unroll
-      for (int q = 0; q < 3; ++q) {
-        const int j = warp + 4 * q;
+      for (int q = 0; q < kQ; ++q) {
+        const int j = warp + kWarps * q;
         if (j >= 10) continue;
         uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
         {  // A: rows 16 rb + (0..7 | 8..15), dims 16 kk + (0..7 | 8..15)
@@ -532,30 +573,36 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
       }
     }
 #pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      const int j = warp + 4 * q;
+    for (int q = 0; q < kQ; ++q) {
+      const int j = warp + kWarps * q;
       if (j >= 10) continue;
       const int rb = rb_of(j), cb = cb_of(j);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int hh = 0; hh < G; ++hh) {
+        SolveHead& ho = sm.hd[hh];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int r = g + 8 * (e >> 1), c = 8 * nt + 2 * t4 + (e & 1);
-          const int t = 16 * rb + r, i = 16 * cb + c;
-          const float a = i < t ? sm.beta[t] * acc[q][nt][e] * exp2f(sm.c2[t] - sm.c2[i]) : 0.f;
-          if (rb == cb) sm.at[rb][c][r] = a;
-          else sm.ao[oidx(rb, cb)][bidx(r, c)] = a;
-        }
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int r = g + 8 * (e >> 1), c = 8 * nt + 2 * t4 + (e & 1);
+            const int t = 16 * rb + r, i = 16 * cb + c;
+            const float a = i < t ? ho.beta[t] * acc[q][nt][e] * exp2f(ho.c2[t] - ho.c2[i]) : 0.f;
+            if (rb == cb) ho.at[rb][c][r] = a;
+            else ho.ao[oidx(rb, cb)][bidx(r, c)] = a;
+          }
+      }
     }
   }
-  __syncthreads();  // K is dead: its space holds the T and X blocks from here
+  __syncthreads();  // K is dead: its space holds head 0's T and X blocks from here
+  // From here each group of 4 warps inverts its own head's (I + A).
+  SolveTX& w = sm.tx(gi);
   auto rd = [](const float* blk) { return [=](int r, int c) { return blk[bidx(r, c)]; }; };
   auto wr = [](float* blk) { return [=](int r, int c, float x) { blk[bidx(r, c)] = x; }; };
-  // ---- diagonal blocks T_bb (warps 0-1, lane = column c of block 2 w + lane / 16):
+  // ---- diagonal blocks T_bb (group warps 0-1, lane = column c of block 2 gw + lane / 16):
   // right-looking substitution, v[r] accumulates sum_{m<r} A_rm x_m and becomes x_r when its
   // turn comes
-  if (warp < 2) {
-    const int bb = 2 * warp + (lane >> 4), c = lane & 15;
+  if (gw < 2) {
+    const int bb = 2 * gw + (lane >> 4), c = lane & 15;
     float v[16];
 #pragma unroll
     for (int r = 0; r < 16; ++r) v[r] = 0.f;
@@ -563,7 +610,7 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
     for (int mm = 0; mm < 16; ++mm) {
       const float x = mm < c ? 0.f : (mm == c ? 1.f : -v[mm]);
       v[mm] = x;
-      const float4* col = reinterpret_cast<const float4*>(sm.at[bb][mm]);
+      const float4* col = reinterpret_cast<const float4*>(hd.at[bb][mm]);
 #pragma unroll
       for (int q4 = (mm + 1) / 4; q4 < 4; ++q4) {
         const float4 a4 = col[q4];
@@ -574,51 +621,51 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
       }
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) sm.w.t[bb][bidx(r, c)] = v[r];
+    for (int r = 0; r < 16; ++r) w.t[bb][bidx(r, c)] = v[r];
   }
-  __syncthreads();
+  group_sync<G>(gi);
   // ---- off-diagonal blocks, T_ij = -T_ii (sum_{k=j}^{i-1} A_ik T_kj): warp = (block, n-tile)
-  {  // level 1: T_10 (warps 0-1), T_32 (warps 2-3) via Y = A_ij T_jj
-    const int blk = warp >> 1, nt = warp & 1, i = 2 * blk + 1, j = 2 * blk;
+  {  // level 1: T_10 (group warps 0-1), T_32 (group warps 2-3) via Y = A_ij T_jj
+    const int blk = gw >> 1, nt = gw & 1, i = 2 * blk + 1, j = 2 * blk;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    tile_mma(acc, rd(sm.ao[oidx(i, j)]), rd(sm.w.t[j]), nt, lane);
-    tile_store(acc, 1.f, wr(sm.w.x[blk]), nt, lane);
+    tile_mma(acc, rd(hd.ao[oidx(i, j)]), rd(w.t[j]), nt, lane);
+    tile_store(acc, 1.f, wr(w.x[blk]), nt, lane);
     __syncwarp();
     float acc2[4] = {0.f, 0.f, 0.f, 0.f};
-    tile_mma(acc2, rd(sm.w.t[i]), rd(sm.w.x[blk]), nt, lane);
-    tile_store(acc2, -1.f, wr(sm.w.t[4 + oidx(i, j)]), nt, lane);
+    tile_mma(acc2, rd(w.t[i]), rd(w.x[blk]), nt, lane);
+    tile_store(acc2, -1.f, wr(w.t[4 + oidx(i, j)]), nt, lane);
   }
-  __syncthreads();
+  group_sync<G>(gi);
 #pragma unroll
   for (int q = 0; q < 2; ++q) {  // level 2: X_rc = sum_{k=c}^{1} A_rk T_kc, r = 2, 3; c = 0, 1
-    const int u = warp + 4 * q, xb = u >> 1, nt = u & 1, r = 2 + (xb >> 1), c = xb & 1;
+    const int u = gw + 4 * q, xb = u >> 1, nt = u & 1, r = 2 + (xb >> 1), c = xb & 1;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k = c; k < 2; ++k)
-      tile_mma(acc, rd(sm.ao[oidx(r, k)]), rd(k == c ? sm.w.t[k] : sm.w.t[4 + oidx(1, 0)]), nt, lane);
-    tile_store(acc, 1.f, wr(sm.w.x[xb]), nt, lane);
+      tile_mma(acc, rd(hd.ao[oidx(r, k)]), rd(k == c ? w.t[k] : w.t[4 + oidx(1, 0)]), nt, lane);
+    tile_store(acc, 1.f, wr(w.x[xb]), nt, lane);
   }
-  __syncthreads();
+  group_sync<G>(gi);
 #pragma unroll
   for (int q = 0; q < 2; ++q) {  // level 3: T_rc = -sum_{k=2}^{r} T_rk X_kc
-    const int u = warp + 4 * q, xb = u >> 1, nt = u & 1, r = 2 + (xb >> 1), c = xb & 1;
+    const int u = gw + 4 * q, xb = u >> 1, nt = u & 1, r = 2 + (xb >> 1), c = xb & 1;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k = 2; k <= r; ++k)
-      tile_mma(acc, rd(k == r ? sm.w.t[r] : sm.w.t[4 + oidx(3, 2)]), rd(sm.w.x[2 * (k - 2) + c]), nt, lane);
-    tile_store(acc, -1.f, wr(sm.w.t[4 + oidx(r, c)]), nt, lane);
+      tile_mma(acc, rd(k == r ? w.t[r] : w.t[4 + oidx(3, 2)]), rd(w.x[2 * (k - 2) + c]), nt, lane);
+    tile_store(acc, -1.f, wr(w.t[4 + oidx(r, c)]), nt, lane);
   }
-  __syncthreads();
+  group_sync<G>(gi);
   // ---- TB = T diag(beta), TBG = T diag(beta gamma) as bf16 128B-swizzled [64 t x 64 i]
   // tiles (zero above the diagonal blocks) into the workspace; thread: row t, columns
   // 32 hh .. 32 hh + 31
   {
     uint8_t* dst = p.ws + (cslot * p.hv + h) * kSolveBytes;
-    const int t = tid >> 1, hh = tid & 1, rb = t >> 4, rl = t & 15;
+    const int t = gt >> 1, hh = gt & 1, rb = t >> 4, rl = t & 15;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       const int cb = 2 * hh + cc;
       float v[16];
       if (cb <= rb) {
-        const float* blk = cb == rb ? sm.w.t[rb] : sm.w.t[4 + oidx(rb, cb)];
+        const float* blk = cb == rb ? w.t[rb] : w.t[4 + oidx(rb, cb)];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const float4 x = *reinterpret_cast<const float4*>(blk + rl * 16 + ((4 * q4) ^ bsw(rl)));
@@ -631,12 +678,12 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
       if (p.ta != nullptr && m * C + t < len) {  // row t of T, columns 16 cb ..
         const int64_t o = b * p.ta_sb + (int64_t)(t0 + m * C + t) * p.ta_st + h * p.ta_sh + 16 * cb;
         if (p.ta_dtype == PBK_BF16) {
-          uint4 w[2];
-          uint32_t* wp = reinterpret_cast<uint32_t*>(w);
+          uint4 wv[2];
+          uint32_t* wp = reinterpret_cast<uint32_t*>(wv);
 #pragma unroll
           for (int e = 0; e < 8; ++e) wp[e] = pack_bf16x2(v[2 * e], v[2 * e + 1]);
-          *reinterpret_cast<uint4*>(static_cast<bf16*>(p.ta) + o) = w[0];
-          *reinterpret_cast<uint4*>(static_cast<bf16*>(p.ta) + o + 8) = w[1];
+          *reinterpret_cast<uint4*>(static_cast<bf16*>(p.ta) + o) = wv[0];
+          *reinterpret_cast<uint4*>(static_cast<bf16*>(p.ta) + o + 8) = wv[1];
         } else {
 #pragma unroll
           for (int e = 0; e < 4; ++e)
@@ -650,8 +697,8 @@ __global__ void __launch_bounds__(kSolveThreads) gdn_solve_kernel(const SolveArg
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int i = 16 * cb + 8 * u + e;
-          vb[e] = v[8 * u + e] * sm.beta[i];
-          vbg[e] = vb[e] * sm.gam[i];
+          vb[e] = v[8 * u + e] * hd.beta[i];
+          vbg[e] = vb[e] * hd.gam[i];
         }
         uint4 w1, w2;
         w1.x = pack_bf16x2(vb[0], vb[1]);
@@ -1251,6 +1298,19 @@ void fill_args(PrefillArgs& a, const pbk_gdn_desc& d) {
   a.solve_slots = 0;
 }
 
+// The chunk solve over grid (chunks, value-head groups, sequences): two value heads per CTA
+// (sharing K and K K^T) when the heads per key head are even, else one.
+cudaError_t launch_solve(const SolveArgs& sa, unsigned chunks, unsigned seqs, int hv, int hk, cudaStream_t st) {
+  auto go = [&](auto kern, int g, size_t smem) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kern<<<dim3(chunks, (unsigned)(hv / g), seqs), kSolveThreads * g, smem, st>>>(sa);
+    return cudaGetLastError();
+  };
+  if ((hv / hk) % 2 == 0) return go(gdn_solve_kernel<2>, 2, sizeof(SolveSmem<2>));
+  return go(gdn_solve_kernel<1>, 1, sizeof(SolveSmem<1>));
+}
+
 }  // namespace
 
 bool gdn_prefill_tc_supported(const pbk_gdn_desc& d) {
@@ -1307,12 +1367,7 @@ cudaError_t launch_gdn_chunk_solve(const pbk_gdn_desc& d, void* ws, cudaStream_t
   sa.cu_seqlens = nullptr;
   sa.chunk_off = nullptr;
   sa.num_seqs = 0;
-  cudaError_t e =
-      cudaFuncSetAttribute(gdn_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SolveSmem));
-  if (e != cudaSuccess) return e;
-  const dim3 sgrid((unsigned)((d.seqlen + C - 1) / C), (unsigned)d.hv, (unsigned)d.batch);
-  gdn_solve_kernel<<<sgrid, kSolveThreads, sizeof(SolveSmem), st>>>(sa);
-  return cudaGetLastError();
+  return launch_solve(sa, (unsigned)((d.seqlen + C - 1) / C), (unsigned)d.batch, d.hv, d.hk, st);
 }
 
 // solve_ws: gdn_prefill_tc_workspace(d) bytes (16-byte aligned) holding the chunk solve of d
@@ -1392,11 +1447,7 @@ cudaError_t launch_gdn_prefill_varlen(const pbk_gdn_desc& d, const int32_t* cu_s
   sa.num_seqs = num_seqs;
   sa.gc = nullptr;
   sa.ta = nullptr;
-  if ((e = cudaFuncSetAttribute(gdn_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(SolveSmem))) != cudaSuccess)
-    return e;
-  gdn_solve_kernel<<<dim3((unsigned)max_chunks, (unsigned)d.hv, 1), kSolveThreads, sizeof(SolveSmem), st>>>(sa);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = launch_solve(sa, (unsigned)max_chunks, 1, d.hv, d.hk, st)) != cudaSuccess) return e;
   // the recurrence: one CTA per (sequence, value head) over the packed tensors
   pbk_gdn_desc dv = d;
   dv.batch = num_seqs;  // CTAs and state slots per sequence; the tensors stay [1, T, H, 128]
