@@ -272,15 +272,16 @@ __device__ __forceinline__ void warp_bases(int a, int b, SelectSmem& ss, int& ba
     ss.warp_tot[1][warp] = b;
   }
   __syncthreads();
-  int ea = 0, eb = 0, ta = 0;
-  for (int w = 0; w < kTopkWarps; ++w) {  // one broadcast read per warp
-    const int x = ss.warp_tot[0][w], y = ss.warp_tot[1][w];
-    if (w < warp) ea += x, eb += y;
-    ta += x;
+  // every warp scans the warp totals itself (lane l holds warp l's): inclusive sums by shuffles
+  int x = lane < kTopkWarps ? ss.warp_tot[0][lane] : 0, y = lane < kTopkWarps ? ss.warp_tot[1][lane] : 0;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int tx = __shfl_up_sync(0xffffffffu, x, o), ty = __shfl_up_sync(0xffffffffu, y, o);
+    if (lane >= o) x += tx, y += ty;
   }
-  base_a = ea;
-  base_b = eb;
-  tot_a = ta;
+  base_a = __shfl_sync(0xffffffffu, x, warp) - a;
+  base_b = __shfl_sync(0xffffffffu, y, warp) - b;
+  tot_a = __shfl_sync(0xffffffffu, x, 31);
   __syncthreads();
 }
 
@@ -571,6 +572,11 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
       // lane = page within the segment
       const int nc = total, P = (nc + kTopkWarps - 1) / kTopkWarps;
       const int c0 = min(warp * P, nc), c1 = min(c0 + P, nc);
+      // The scores read here are kept in shared memory for the placement pass (the staging
+      // area of the band's bounds is idle until then) when the candidate segments fit, so the
+      // placement reads them back without a second global round trip.
+      float* seg_scores = reinterpret_cast<float*>(ts.stage);
+      const bool staged = nc * 32 * (int)sizeof(float) <= (int)sizeof(ts.stage);
       int pcnt = 0;
       for (int b0 = c0; b0 < c1; b0 += kSegRegs) {
         float x[kSegRegs];
@@ -580,9 +586,11 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
           x[u] = page < npages ? s[page] : -INFINITY;
         }
 #pragma unroll
-        for (int u = 0; u < kSegRegs; ++u)
+        for (int u = 0; u < kSegRegs; ++u) {
           pcnt += __popc(__ballot_sync(0xffffffffu, b0 + u < c1 && ordered_key(x[u]) >= tau &&
                                                         ts.cseg[min(b0 + u, c1 - 1)] * 32 + lane < npages));
+          if (staged && b0 + u < c1) seg_scores[(b0 + u) * 32 + lane] = x[u];
+        }
       }
       int ppos, pzero, ptotal;
       warp_bases(pcnt, 0, ss, ppos, pzero, ptotal);
@@ -592,7 +600,7 @@ __global__ void __launch_bounds__(kTopkThreads) quest_topk_kernel(const float* s
 #pragma unroll
           for (int u = 0; u < kSegRegs; ++u) {
             const int page = b0 + u < c1 ? ts.cseg[b0 + u] * 32 + lane : npages;
-            x[u] = page < npages ? s[page] : -INFINITY;
+            x[u] = page >= npages ? -INFINITY : (staged ? seg_scores[(b0 + u) * 32 + lane] : s[page]);
           }
 #pragma unroll
           for (int u = 0; u < kSegRegs; ++u) {
