@@ -137,22 +137,24 @@ def swa_chunk_plan(t: int, window: int, chunks: int, first: int | None = None) -
 
 
 def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: float, group=None, swa_chunks: int = 8,
-                         gdn=None, attention=None, gather: bool = True):
+                         gdn=None, attention=None, gather: bool = True, gdn_parts: int | None = None):
     """One hybrid layer (GDN branch + sliding-window attention branch, pseudobrain/transplant.py
     WindowedHybridLayer, benchmark config 4) on this rank's heads, with every branch output
     all-gathered over `group` into the head-major layout the output projection reads.
 
     gdn_in: this rank's GDN shard {q, k [1,T,hk/N,128], v [1,T,hv/N,128], g, beta [1,T,hv/N],
     scale}; qa [1,T,H/N,128], ka, va [1,T,KV/N,128]: this rank's attention heads (window sinks
-    0). Order, chosen so the all-gathers (bound by each GPU's NVLink ingress) run under the
-    compute: the GDN branch (segmented over T) first, its output gathered on the communicator's
-    stream while the attention runs; then the attention in query chunks (swa_chunk_plan), each
+    0). Order, chosen so the all-gathers (bound by each GPU's NVLink ingress) start early and
+    run under the compute: the GDN branch (segmented over T) first, in `gdn_parts` launches over
+    consecutive groups of whole key heads (default 2 when N > 1 and the rank's key heads split
+    evenly, else 1), each part's output gathered on the communicator's stream while the next
+    part and then the attention run; then the attention in query chunks (swa_chunk_plan), each
     chunk's rows gathered as soon as they are written, while the next chunk computes. Only the
-    last chunk's gather is left after the compute (the attention branch is the longer one: 42
-    against 23 ms at 2 GPUs). Returns (gdn_all [N, T,
-    hv/N*128], [(s, e, swa_all [N, e - s, H/N*128]) for each chunk]). ``gdn(gdn_in, o)`` and
-    ``attention(q, k, v, o, window, scale)`` replace the CUDA kernels (CPU tests); gather=False
-    runs the layer on these heads alone (N = 1 layouts, no exchange)."""
+    last chunk's gather is left after the compute. Returns ([(v0, v1, gdn_part [N, T,
+    (v1 - v0)*128]) for each part: the rank-local value heads [v0, v1)], [(s, e, swa_all [N,
+    e - s, H/N*128]) for each chunk]); assemble_gdn joins the parts into [N, T, hv/N*128].
+    ``gdn(gdn_in, o)`` and ``attention(q, k, v, o, window, scale)`` replace the CUDA kernels (CPU
+    tests); gather=False runs the layer on these heads alone (N = 1 layouts, no exchange)."""
     world = dist.get_world_size(group) if (gather and dist.is_initialized()) else 1
     if gdn is None:
         from .gdn_prefill import auto_segments, gdn_prefill_segmented
@@ -167,16 +169,26 @@ def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: floa
             window_attention_(q, k, v, o, win, 0, scale)
     t = qa.shape[1]
     heads, d = qa.shape[2], qa.shape[3]
-    works, swa_out = [], []
-    hv = gdn_in["v"].shape[2]
-    o_gdn = torch.empty(1, t, hv, gdn_in["v"].shape[3], dtype=torch.bfloat16, device=qa.device)
-    gdn(gdn_in, o_gdn)
-    if world > 1:
-        gdn_all = torch.empty(world * t, hv * o_gdn.shape[-1], dtype=o_gdn.dtype, device=o_gdn.device)
-        works.append(dist.all_gather_into_tensor(gdn_all, o_gdn.view(t, -1), group=group, async_op=True))
-        gdn_all = gdn_all.view(world, t, -1)
-    else:
-        gdn_all = o_gdn.view(1, t, -1)
+    works, swa_out, gdn_out = [], [], []
+    hv, hk, dv = gdn_in["v"].shape[2], gdn_in["k"].shape[2], gdn_in["v"].shape[3]
+    if gdn_parts is None:
+        gdn_parts = 2 if world > 1 and hk % 2 == 0 else 1
+    if gdn_parts < 1 or hk % gdn_parts:
+        raise ValueError(f"{hk} key heads do not split into {gdn_parts} parts")
+    ratio = hv // hk
+    for part in range(gdn_parts):
+        k0, k1 = part * hk // gdn_parts, (part + 1) * hk // gdn_parts
+        v0, v1 = k0 * ratio, k1 * ratio
+        x = {"q": gdn_in["q"][:, :, k0:k1], "k": gdn_in["k"][:, :, k0:k1], "v": gdn_in["v"][:, :, v0:v1],
+             "g": gdn_in["g"][:, :, v0:v1], "beta": gdn_in["beta"][:, :, v0:v1], "scale": gdn_in["scale"]}
+        o_part = torch.empty(1, t, v1 - v0, dv, dtype=torch.bfloat16, device=qa.device)
+        gdn(x, o_part)
+        if world > 1:
+            gathered = torch.empty(world * t, (v1 - v0) * dv, dtype=o_part.dtype, device=o_part.device)
+            works.append(dist.all_gather_into_tensor(gathered, o_part.view(t, -1), group=group, async_op=True))
+            gdn_out.append((v0, v1, gathered.view(world, t, -1)))
+        else:
+            gdn_out.append((v0, v1, o_part.view(1, t, -1)))
     for s, e, h in swa_chunk_plan(t, window, swa_chunks):
         rows = e - s + h
         stage = torch.empty(1, rows, heads, d, dtype=qa.dtype, device=qa.device)
@@ -190,7 +202,13 @@ def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: floa
             swa_out.append((s, e, mine.view(1, e - s, heads * d)))
     for w in works:
         w.wait()
-    return gdn_all, swa_out
+    return gdn_out, swa_out
+
+
+def assemble_gdn(parts) -> torch.Tensor:
+    """[(v0, v1, [N, T, (v1 - v0) * V])...] in head order -> [N, T, (heads per rank) * V]: the
+    gathered GDN parts joined along each rank's heads (the layout of one gather of all of them)."""
+    return torch.cat([x for _, _, x in parts], dim=-1)
 
 
 def assemble_heads(pieces, t: int) -> torch.Tensor:

@@ -144,8 +144,24 @@ def _hybrid_worker(rank, world, outdir):
     gdn_all, pieces = sharding.hybrid_layer_sharded(xs, qa[:, :, 2 * a0:2 * a1], ka[:, :, a0:a1], va[:, :, a0:a1],
                                                     HYB_W, 128 ** -0.5, swa_chunks=3, gdn=_cpu_gdn,
                                                     attention=_cpu_attention)
-    torch.save({"gdn": gdn_all, "swa": sharding.assemble_heads(pieces, HYB_T)},
+    torch.save({"gdn": sharding.assemble_gdn(gdn_all), "swa": sharding.assemble_heads(pieces, HYB_T)},
                os.path.join(outdir, f"hybrid_{rank}.pt"))
+
+
+def test_hybrid_layer_gdn_parts_join_to_one_launch():
+    """The GDN branch run in two launches over groups of whole key heads (each gathered on its
+    own at N > 1) joins, by assemble_gdn, to the output of one launch over all heads; a split
+    that would cut a key head's group of value heads is refused."""
+    from pseudobrain_b200 import sharding
+    x, qa, ka, va = _hybrid_inputs()
+    kw = dict(swa_chunks=2, gdn=_cpu_gdn, attention=_cpu_attention, gather=False)
+    g1, p1 = sharding.hybrid_layer_sharded(x, qa, ka, va, HYB_W, 128 ** -0.5, gdn_parts=1, **kw)
+    g2, p2 = sharding.hybrid_layer_sharded(x, qa, ka, va, HYB_W, 128 ** -0.5, gdn_parts=2, **kw)
+    assert [(v0, v1) for v0, v1, _ in g2] == [(0, 2), (2, 4)]
+    assert torch.equal(sharding.assemble_gdn(g2), sharding.assemble_gdn(g1))
+    assert torch.equal(sharding.assemble_heads(p2, HYB_T), sharding.assemble_heads(p1, HYB_T))
+    with pytest.raises(ValueError):
+        sharding.hybrid_layer_sharded(x, qa, ka, va, HYB_W, 128 ** -0.5, gdn_parts=3, **kw)
 
 
 def test_hybrid_layer_pipeline_equals_unsharded(tmp_path):

@@ -60,10 +60,10 @@ def _worker(rank, world, port, outdir):
         a0, a1 = rank * per, (rank + 1) * per
         gdn_all, pieces = sharding.hybrid_layer_sharded(xs, qa[:, :, a0 * groups:a1 * groups], ka[:, :, a0:a1],
                                                         va[:, :, a0:a1], WINDOW, 128 ** -0.5, swa_chunks=4)
-        out = {"gdn": gdn_all.cpu(), "swa": sharding.assemble_heads(pieces, T).cpu()}
+        out = {"gdn": sharding.assemble_gdn(gdn_all).cpu(), "swa": sharding.assemble_heads(pieces, T).cpu()}
         if rank == 0:  # the unsharded layer: all heads on this GPU, no exchange
             g1, p1 = sharding.hybrid_layer_sharded(x, qa, ka, va, WINDOW, 128 ** -0.5, swa_chunks=1, gather=False)
-            out["gdn_ref"] = g1.cpu()
+            out["gdn_ref"] = sharding.assemble_gdn(g1).cpu()
             out["swa_ref"] = sharding.assemble_heads(p1, T).cpu()
         from pseudobrain_b200._capi import device_error
         out["device_error"] = device_error()
