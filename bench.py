@@ -595,6 +595,8 @@ def measure_widen(args, timed, dev, rank, world, pk):
                                   shape="o fp32, gate bf16 -> out bf16", traffic=traffic("gdn_out_norm_vec_kernel"))
     del o, gate, decay
     torch.cuda.empty_cache()
+    out["gdn_layer"] = _gdn_layer_fused(torch, L, dev, gen, small, steps, hbm)
+    torch.cuda.empty_cache()
     # two-level Quest selection (research defaults)
     kv, heads, d, page, sblk, nq, budget = 8, 32, 128, 64, 64, 8, 64
     n_tok = (1 << 19) if small else (1 << 20)
@@ -651,11 +653,102 @@ def measure_widen(args, timed, dev, rank, world, pk):
     del arc, kn, vn
     torch.cuda.empty_cache()
     out["gpu_launches"] = 3 * steps + 5 * (steps * 4 + 3) + 4 * steps + 2 * steps
+    lay_p, lay_d = max(3, steps // 3), max(20, steps * 4)  # the fused-layer comparisons
+    out["gpu_launches"] += (3 + 5) * (lay_p + 3) + (1 + 4) * (lay_d + 5)
     cv = out["conv_qkv"]  # the line's own fields when this part runs alone
     out.update(metric="widened rows: HBM GB/s of each piece", value=cv["achieved_gbps"], unit="GB/s",
                roofline={"bound": "hbm", "achieved": cv["achieved_gbps"], "peak": hbm, "unit": "GB/s",
                          "frac": cv["frac"], "traffic": cv.get("traffic"), "kernel": "gdn_conv_norm_vec_kernel"})
     return out
+
+
+def _gdn_layer_fused(torch, L, dev, gen, small, steps, hbm):
+    """GatedDeltaNetLayer.forward from the projection's output to the gated, normed output:
+    the prefill at config-1 shapes as pbk_gdn_prefill_layer (conv, norm and gating fused into
+    the chunk solve; 3 launches) against the same layer as the separate pieces (conv + norm,
+    gating, chunk solve, recurrence, output norm: 5 launches), and the decode step at config-2
+    shapes as pbk_gdn_decode_layer (1 launch) against conv + gating + decode + output norm."""
+    res = {}
+    b, t, hk, hv = (1, 8192, 16, 32) if small else (4, 32768, 16, 32)
+    c = (2 * hk + hv) * 128
+    qkv = torch.randn(b, t, c, device=dev, generator=gen).to(torch.bfloat16)
+    gate = torch.randn(b, t, hv * 128, device=dev, generator=gen).to(torch.bfloat16)
+    decay = torch.randn(b, t, 2 * hv, device=dev, generator=gen).to(torch.bfloat16)
+    wconv = torch.randn(c, 4, device=dev, generator=gen) * 0.5
+    tail = torch.randn(b, 3, c, device=dev, generator=gen).to(torch.bfloat16)
+    new_tail = torch.empty_like(tail)
+    a_log, dt_bias = torch.randn(hv, device=dev, generator=gen) * 0.5, torch.randn(hv, device=dev, generator=gen)
+    o_norm = torch.ones(128, device=dev)
+    state = torch.zeros(b, hv, 128, 128, device=dev)
+    from pseudobrain_b200.gdn_prefill import gdn_prefill_
+
+    def fused():
+        L.gated_deltanet_prefill(qkv, gate, decay, tail, wconv, a_log, dt_bias, o_norm, state, hk, hv,
+                                 new_tail=new_tail, out_dtype=torch.bfloat16)
+
+    o = torch.empty(b, t, hv, 128, device=dev, dtype=torch.bfloat16)
+
+    def unfused():
+        q, k, v = L.conv_qkv(qkv, tail, wconv, hk, hv, "max", new_tail)
+        g, beta = L.gdn_gating(decay, a_log, dt_bias, torch.bfloat16)
+        gdn_prefill_(q, k, v, g, beta, state, state, o, 128 ** -0.5)
+        L.gated_out_norm(o, gate, o_norm, out_dtype=torch.bfloat16)
+
+    reps = max(3, steps // 3)
+    tf = timed_plain(torch, fused, reps, 3)
+    tu = timed_plain(torch, unfused, reps, 3)
+    tokens = b * t
+    res["prefill"] = {"config": f"B={b} T={t} Hk={hk} Hv={hv}, conv width 4, bf16 in / out",
+                      "fused_ms": tf * 1e3, "unfused_ms": tu * 1e3, "speedup": tu / tf,
+                      "fused_tok_s": tokens / tf, "launches": {"fused": 3, "unfused": 5}}
+    del qkv, gate, decay, tail, new_tail, state, o
+    torch.cuda.empty_cache()
+    b, t = 256, 1
+    qkv = torch.randn(b, t, c, device=dev, generator=gen).to(torch.bfloat16)
+    gate = torch.randn(b, t, hv * 128, device=dev, generator=gen).to(torch.bfloat16)
+    decay = torch.randn(b, t, 2 * hv, device=dev, generator=gen).to(torch.bfloat16)
+    tail = torch.randn(b, 3, c, device=dev, generator=gen).to(torch.bfloat16)
+    tail2 = tail.clone()
+    state = torch.randn(b, hv, 128, 128, device=dev, generator=gen) * 0.02
+
+    def dec_fused():
+        L.gated_deltanet_decode(qkv, gate, decay, tail, wconv, a_log, dt_bias, o_norm, state, hk, hv,
+                                out_dtype=torch.bfloat16)
+
+    o = torch.empty(b, t, hv, 128, device=dev, dtype=torch.bfloat16)
+    from pseudobrain_b200.gated_deltanet import gdn_recurrent_
+
+    def dec_unfused():
+        q, k, v = L.conv_qkv(qkv, tail, wconv, hk, hv, "max", tail2)
+        g, beta = L.gdn_gating(decay, a_log, dt_bias, torch.bfloat16)
+        gdn_recurrent_(q, k, v, g, beta, state, state, o, 128 ** -0.5)
+        L.gated_out_norm(o, gate, o_norm, out_dtype=torch.bfloat16)
+
+    reps = max(20, steps * 4)
+    tdf = timed_plain(torch, dec_fused, reps, 5)
+    tdu = timed_plain(torch, dec_unfused, reps, 5)
+    sbytes = 2 * state.numel() * 4
+    res["decode"] = {"config": f"B={b} T=1 Hk={hk} Hv={hv}, conv width 4, tail in place",
+                     "fused_us": tdf * 1e6, "unfused_us": tdu * 1e6, "speedup": tdu / tdf,
+                     "fused_steps_s": 1.0 / tdf, "fused_hbm_frac": sbytes / tdf / 1e9 / hbm,
+                     "launches": {"fused": 1, "unfused": 4}}
+    del qkv, gate, decay, tail, tail2, state, o
+    return res
+
+
+def timed_plain(torch, fn, reps, warmup):
+    """Seconds per call: CUDA events around `reps` back-to-back calls on the current stream,
+    after `warmup` untimed calls (inputs larger than L2 where the piece's shapes make them)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / reps
 
 
 def swa_pairs(t, window):

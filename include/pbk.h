@@ -238,6 +238,62 @@ PBK_API int pbk_l2norm(pbk_view x, pbk_view out, int32_t batch, int32_t seqlen, 
                        float eps, void* stream);
 /* g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (gated_deltanet.py:427-429). */
 PBK_API int pbk_gdn_gating(const pbk_gating_desc* desc, void* stream);
+
+/* The decode step of GatedDeltaNetLayer.forward (pseudobrain/gated_deltanet.py:411-440, the
+ * few-token case select_kernel sends to delta_rule_sequential, :291-294) from the input
+ * projection's output to the gated, normed per-step output, for pbk_gdn_decode_layer. */
+typedef struct pbk_gdn_layer_desc {
+  int32_t batch, seqlen, hk, hv; /* dense [B, T, ..]; dk == dv == 128 */
+  int32_t width;       /* conv taps 1..8 (conv_weight[:, width-1] multiplies the current input) */
+  int32_t l2mode;      /* q/k normalisation: 0 none, 1 'max' (x / max(|x|, eps)), 2 'hf' (x rsqrt(|x|^2 + eps)) */
+  float l2_eps;        /* 1e-6 in the reference */
+  float norm_eps;      /* the output RMSNorm eps, 1e-5 in the reference */
+  float scale;         /* the query scale, dk ** -0.5 */
+  int32_t state_layout; /* PBK_STATE_KV or PBK_STATE_VK */
+  pbk_view qkv;        /* [B, T, (2 hk + hv) 128] the projection's q | k | v channels before the
+                          convolution (stride_h = channel stride) */
+  pbk_view tail;       /* [B, width - 1, channels] the conv inputs before qkv; data NULL: zeros */
+  pbk_view new_tail;   /* [B, width - 1, channels] receives the last width - 1 inputs; may be `tail`
+                          itself (in place: the value heads of a key head then run as one thread-block
+                          cluster, so hv / hk must be at most 8); NULL: not written */
+  const float* conv_weight; /* [channels, width] fp32 contiguous; NULL: SiLU only, no tail */
+  pbk_view decay;      /* [B, T, 2 hv]: a | b, the raw decay and beta gate inputs */
+  const float* a_log;  /* [hv] fp32 */
+  const float* dt_bias; /* [hv] fp32 */
+  pbk_view gate;       /* [B, T, hv 128] the output gate z (stride_h = channel stride) */
+  const void* o_norm;  /* [128] the output RMSNorm weight */
+  int32_t o_norm_dtype;
+  int32_t pad_;
+  pbk_view out;        /* [B, T, hv, 128] the gated, normed output (bf16 or fp32) */
+  float* state;        /* [slots, hv, 128, 128] fp32, updated in place */
+  int64_t state_slot_stride; /* elements between slots */
+  const int32_t* state_indices; /* slot of sequence b (NULL: b); a negative index skips the sequence */
+} pbk_gdn_layer_desc;
+
+/* One kernel for the layer's decode step: short_convolution with the carried tail and SiLU
+ * (:314-338), the q/k L2 norm (:59-70), the gating (:427-429), the recurrence
+ * (delta_rule_sequential, :93-107) on the register-resident state, and the output
+ * o rsqrt(mean(o^2) + eps) o_norm SiLU(z) (:439-440) -- fp32 throughout, so q, k, v, g and
+ * beta never reach memory (pbk_gdn_conv_norm + pbk_gdn_gating + pbk_gdn_decode +
+ * pbk_gdn_out_norm in one launch). Meant for the few tokens per sequence of a decode step;
+ * any seqlen is accepted. */
+PBK_API int pbk_gdn_decode_layer(const pbk_gdn_layer_desc* desc, void* stream);
+
+/* GatedDeltaNetLayer.forward over a prefill (gated_deltanet.py:411-440, the chunked
+ * recurrence of :110-165) from the input projection's output to the gated, normed output, in
+ * three launches: (1) the chunk solve with the producer stages fused in -- each CTA convolves
+ * its chunk's q | k | v channels (short_convolution with the carried tail and SiLU), L2-
+ * normalises q and k and computes g and beta from the raw gate inputs, so the standalone conv
+ * and gating passes never run -- writing q, k, v (bf16) and its chunk records into the
+ * workspace; (2) the tensor-core recurrence from them (desc->state is read as h0 and receives
+ * the final state, slot state_indices[b] or b); (3) the output RMSNorm and SiLU gate. Needs
+ * bf16 qkv with contiguous channels (stride_h 1, even row strides, 4-byte aligned) and gate
+ * channels contiguous; new_tail must not be tail. Workspace:
+ * pbk_gdn_prefill_layer_workspace(desc) bytes, 16-byte aligned, private to the call until it
+ * completes on `stream`. */
+PBK_API size_t pbk_gdn_prefill_layer_workspace(const pbk_gdn_layer_desc* desc);
+PBK_API int pbk_gdn_prefill_layer(const pbk_gdn_layer_desc* desc, void* workspace, size_t workspace_bytes,
+                                  void* stream);
 /* out = o rsqrt(mean(o^2) + eps) weight SiLU(gate) per 128-wide head row
  * (gated_deltanet.py:439-440). */
 PBK_API int pbk_gdn_out_norm(const pbk_out_norm_desc* desc, void* stream);

@@ -13,6 +13,8 @@ from . import build as _build
 
 PBK_ABI_VERSION = 1
 PBK_OK = 0
+PBK_ERR_INVALID, PBK_ERR_SHAPE, PBK_ERR_DTYPE, PBK_ERR_ALIGN = -1, -2, -3, -4
+PBK_ERR_DEVICE, PBK_ERR_LAUNCH, PBK_ERR_WORKSPACE = -5, -6, -8
 PBK_ERR_TIMEOUT = -7
 PBK_ERR_TOO_LARGE = -9
 PBK_QUEST_NOALLOC_MAX_SCORES = 4194304
@@ -51,6 +53,17 @@ class PbkOutNormDesc(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hv", ctypes.c_int32),
                 ("weight_dtype", ctypes.c_int32), ("eps", ctypes.c_float), ("pad_", ctypes.c_int32),
                 ("o", PbkView), ("gate", PbkView), ("out", PbkView), ("weight", ctypes.c_void_p)]
+
+
+class PbkGdnLayerDesc(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("seqlen", ctypes.c_int32), ("hk", ctypes.c_int32), ("hv", ctypes.c_int32),
+                ("width", ctypes.c_int32), ("l2mode", ctypes.c_int32), ("l2_eps", ctypes.c_float),
+                ("norm_eps", ctypes.c_float), ("scale", ctypes.c_float), ("state_layout", ctypes.c_int32),
+                ("qkv", PbkView), ("tail", PbkView), ("new_tail", PbkView), ("conv_weight", ctypes.c_void_p),
+                ("decay", PbkView), ("a_log", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p), ("gate", PbkView),
+                ("o_norm", ctypes.c_void_p), ("o_norm_dtype", ctypes.c_int32), ("pad_", ctypes.c_int32),
+                ("out", PbkView), ("state", ctypes.c_void_p), ("state_slot_stride", ctypes.c_int64),
+                ("state_indices", ctypes.c_void_p)]
 
 
 class PbkTokenDesc(ctypes.Structure):
@@ -149,6 +162,9 @@ SIGNATURES = {
     "pbk_gdn_conv_norm": (ctypes.c_int, [ctypes.POINTER(PbkConvDesc), _VP]),
     "pbk_gdn_gating": (ctypes.c_int, [ctypes.POINTER(PbkGatingDesc), _VP]),
     "pbk_gdn_out_norm": (ctypes.c_int, [ctypes.POINTER(PbkOutNormDesc), _VP]),
+    "pbk_gdn_decode_layer": (ctypes.c_int, [ctypes.POINTER(PbkGdnLayerDesc), _VP]),
+    "pbk_gdn_prefill_layer_workspace": (ctypes.c_size_t, [ctypes.POINTER(PbkGdnLayerDesc)]),
+    "pbk_gdn_prefill_layer": (ctypes.c_int, [ctypes.POINTER(PbkGdnLayerDesc), _VP, ctypes.c_size_t, _VP]),
     "pbk_gdn_prefill_varlen_workspace": (ctypes.c_size_t, [ctypes.POINTER(PbkGdnDesc), _I32]),
     "pbk_gdn_prefill_varlen": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, _I32, _VP, ctypes.c_size_t, _VP]),
     "pbk_gdn_prefill_solved": (ctypes.c_int, [ctypes.POINTER(PbkGdnDesc), _VP, ctypes.c_size_t, _VP]),

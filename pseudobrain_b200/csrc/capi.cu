@@ -20,6 +20,9 @@ size_t gdn_prefill_varlen_workspace(const pbk_gdn_desc& d, int num_seqs);
 cudaError_t launch_gdn_conv_norm(const pbk_conv_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_gating(const pbk_gating_desc& d, cudaStream_t st);
 cudaError_t launch_gdn_out_norm(const pbk_out_norm_desc& d, cudaStream_t st);
+cudaError_t launch_gdn_decode_layer(const pbk_gdn_layer_desc& d, cudaStream_t st);
+size_t gdn_prefill_layer_workspace(const pbk_gdn_layer_desc& d);
+cudaError_t launch_gdn_prefill_layer(const pbk_gdn_layer_desc& d, void* ws, cudaStream_t st);
 cudaError_t launch_gdn_l2norm(const pbk_view& x, const pbk_view& out, int batch, int seqlen, int heads, int mode,
                               float eps, cudaStream_t st);
 bool gdn_conv_width_ok(int width);
@@ -329,6 +332,71 @@ int pbk_gdn_out_norm(const pbk_out_norm_desc* d, void* stream) {
   int st = check_current_device();
   if (st != PBK_OK) return st;
   return launch_status(pbk::launch_gdn_out_norm(*d, static_cast<cudaStream_t>(stream)));
+}
+
+int pbk_gdn_decode_layer(const pbk_gdn_layer_desc* d, void* stream) {
+  if (d == nullptr || d->batch < 0 || d->seqlen < 0 || d->hk < 1 || d->hv < 1) return PBK_ERR_INVALID;
+  if (d->hv % d->hk != 0) return PBK_ERR_SHAPE;
+  if (d->conv_weight != nullptr && !pbk::gdn_conv_width_ok(d->width)) return PBK_ERR_SHAPE;
+  if (d->l2mode < 0 || d->l2mode > 2 || !(d->l2_eps >= 0.f) || !(d->norm_eps >= 0.f)) return PBK_ERR_INVALID;
+  if (d->state_layout != PBK_STATE_KV && d->state_layout != PBK_STATE_VK) return PBK_ERR_INVALID;
+  if ((int64_t)d->batch * d->hv > INT32_MAX) return PBK_ERR_SHAPE;
+  if (d->batch == 0 || d->seqlen == 0) return PBK_OK;
+  if (!view_ok(d->qkv) || !view_ok(d->decay) || !view_ok(d->gate) || !view_ok(d->out)) return PBK_ERR_INVALID;
+  if (!d->a_log || !d->dt_bias || !d->o_norm || !d->state) return PBK_ERR_INVALID;
+  if (!dtype_ok(d->o_norm_dtype)) return PBK_ERR_DTYPE;
+  if (d->tail.data != nullptr && !dtype_ok(d->tail.dtype)) return PBK_ERR_DTYPE;
+  if (d->new_tail.data != nullptr && !dtype_ok(d->new_tail.dtype)) return PBK_ERR_DTYPE;
+  const bool in_place = d->conv_weight != nullptr && d->width > 1 && d->new_tail.data != nullptr &&
+                        d->new_tail.data == d->tail.data;
+  if (in_place && (d->hv / d->hk > 8 || d->new_tail.dtype != d->tail.dtype ||
+                   d->new_tail.stride_b != d->tail.stride_b || d->new_tail.stride_t != d->tail.stride_t ||
+                   d->new_tail.stride_h != d->tail.stride_h))
+    return PBK_ERR_SHAPE;  // in place: one cluster (at most 8 CTAs) per key head, identical views
+  if (d->state_slot_stride < (int64_t)d->hv * 128 * 128) return PBK_ERR_INVALID;
+  if (!aligned16(d->state) || (d->state_slot_stride & 3)) return PBK_ERR_ALIGN;
+  int st = check_current_device();
+  if (st != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_decode_layer(*d, static_cast<cudaStream_t>(stream)));
+}
+
+// The prefill layer: the decode layer's checks plus the producer's (bf16 projection channels,
+// contiguous in pairs; a separate new tail).
+static int check_prefill_layer(const pbk_gdn_layer_desc* d) {
+  if (d == nullptr || d->batch < 0 || d->seqlen < 0 || d->hk < 1 || d->hv < 1) return PBK_ERR_INVALID;
+  if (d->hv % d->hk != 0) return PBK_ERR_SHAPE;
+  if (d->conv_weight != nullptr && !pbk::gdn_conv_width_ok(d->width)) return PBK_ERR_SHAPE;
+  if (d->l2mode < 0 || d->l2mode > 2 || !(d->l2_eps >= 0.f) || !(d->norm_eps >= 0.f)) return PBK_ERR_INVALID;
+  if (d->state_layout != PBK_STATE_KV && d->state_layout != PBK_STATE_VK) return PBK_ERR_INVALID;
+  if (d->batch > 65535 || d->hv > 65535 || (int64_t)d->batch * d->hv > INT32_MAX) return PBK_ERR_SHAPE;
+  if (d->batch == 0 || d->seqlen == 0) return PBK_OK;
+  if (!view_ok(d->qkv) || !view_ok(d->decay) || !view_ok(d->gate) || !view_ok(d->out)) return PBK_ERR_INVALID;
+  if (!d->a_log || !d->dt_bias || !d->o_norm || !d->state) return PBK_ERR_INVALID;
+  if (d->qkv.dtype != PBK_BF16 || !dtype_ok(d->o_norm_dtype)) return PBK_ERR_DTYPE;
+  if (d->qkv.stride_h != 1 || (d->qkv.stride_t & 1) || (d->qkv.stride_b & 1) ||
+      (reinterpret_cast<uintptr_t>(d->qkv.data) & 3) || d->gate.stride_h != 1)
+    return PBK_ERR_ALIGN;
+  if (d->tail.data != nullptr && !dtype_ok(d->tail.dtype)) return PBK_ERR_DTYPE;
+  if (d->new_tail.data != nullptr && (!dtype_ok(d->new_tail.dtype) || d->new_tail.data == d->tail.data))
+    return PBK_ERR_INVALID;  // the prefill's tail is read and written by different CTAs
+  if (d->state_slot_stride < (int64_t)d->hv * 128 * 128) return PBK_ERR_INVALID;
+  if (!aligned16(d->state) || (d->state_slot_stride & 3)) return PBK_ERR_ALIGN;
+  return PBK_OK;
+}
+
+size_t pbk_gdn_prefill_layer_workspace(const pbk_gdn_layer_desc* d) {
+  if (check_prefill_layer(d) != PBK_OK) return 0;
+  return pbk::gdn_prefill_layer_workspace(*d);
+}
+
+int pbk_gdn_prefill_layer(const pbk_gdn_layer_desc* d, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_prefill_layer(d);
+  if (st != PBK_OK) return st;
+  if (d->batch == 0 || d->seqlen == 0) return PBK_OK;
+  if (workspace == nullptr || workspace_bytes < pbk::gdn_prefill_layer_workspace(*d)) return PBK_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return PBK_ERR_ALIGN;
+  if ((st = check_current_device()) != PBK_OK) return st;
+  return launch_status(pbk::launch_gdn_prefill_layer(*d, workspace, static_cast<cudaStream_t>(stream)));
 }
 
 int pbk_l2norm(pbk_view x, pbk_view out, int32_t batch, int32_t seqlen, int32_t heads, int32_t mode, float eps,

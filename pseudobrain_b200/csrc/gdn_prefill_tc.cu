@@ -26,6 +26,7 @@
 // The roles meet on mbarriers; every wait is bounded: on timeout the kernel records an
 // error code, stops issuing, waits (bounded) for its own loads and MMAs, frees its TMEM
 // and returns.
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
@@ -361,6 +362,38 @@ struct SolveArgs {
   int ta_dtype;
 };
 
+// The layer's producer stages fused into the chunk solve (pbk_gdn_prefill_layer, dense
+// sequences only): each CTA makes its own chunk's q, k and v from the input projection's
+// channels -- short_convolution with the carried tail and SiLU (gated_deltanet.py:314-338),
+// the q/k L2 norm (:59-70) -- and its g and beta from the raw gate inputs (:427-429), so the
+// standalone conv and gating passes disappear. k goes straight into the solve's shared K tile;
+// q, k and v are also written (bf16, dense [B, T, H, 128]) for the recurrence kernel.
+struct SolveConvArgs {
+  const bf16* x;              // [B, T, (2 hk + hv) 128] channels contiguous; NULL: the plain solve
+  int64_t x_sb, x_st;
+  const void* tail;           // [B, width - 1, channels] (NULL: zeros)
+  int64_t tl_sb, tl_st, tl_sc;
+  int tl_dtype;
+  void* new_tail;             // [B, width - 1, channels] (NULL: not written); never `tail`
+  int64_t nt_sb, nt_st, nt_sc;
+  int nt_dtype;
+  const float* conv_w;        // [channels, width] (NULL: SiLU only)
+  int width, l2mode;
+  float l2_eps;
+  bf16* qo;                   // [B, T, hk, 128]
+  bf16* ko;                   // [B, T, hk, 128]
+  bf16* vo;                   // [B, T, hv, 128]
+  const void* decay;          // [B, T, 2 hv]: a | b
+  int64_t d_sb, d_st, d_sh;
+  int d_dtype;
+  const float* a_log;
+  const float* dt_bias;
+  const int32_t* state_indices;  // a sequence whose index is negative is skipped (no tail write)
+};
+constexpr int kConvMaxWidth = 8;
+constexpr int kYsStride = D + 4;                      // fp32 row stride of the staged conv rows
+constexpr int kConvSmem = C * 256 + C * kYsStride * 4;  // K tile + staged rows
+
 // Rows [t0, t0 + len) of packed sequence s, clamped into [0, T] (offsets out of order or out of
 // range read nothing outside the tensors; they are caller errors).
 __device__ __forceinline__ void seq_rows(const int32_t* cu_seqlens, int s, int T, int& t0, int& len) {
@@ -448,8 +481,126 @@ __device__ __forceinline__ void group_sync(int g) {
   }
 }
 
+// The conv producer of one CTA (kConv): per 128-channel head of its chunk -- k first (into the
+// shared K tile), q (by the CTA of the key head's first value-head group), then its value
+// heads -- thread (channel pair, row group) convolves its rows from a register window of the
+// width - 1 inputs before them and stages SiLU(y) in fp32; then a warp per row normalises
+// (q, k), rounds to bf16 and stores 8 bytes per lane. The CTA of the sequence's last chunk
+// writes the new tail. Rows past the end are zero in the K tile and not stored.
 template <int G>
-__global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const SolveArgs p) {
+__device__ void solve_conv_produce(const SolveArgs& p, const SolveConvArgs& cv, uint8_t* smem, int b, int m, int hkh,
+                                   int h0) {
+  constexpr int NT = kSolveThreads * G, kWarps = NT / 32;
+  constexpr int kGroups = NT / 64, kRpt = C / kGroups;  // row groups, rows per thread
+  constexpr int KM = kConvMaxWidth;
+  float* ys = reinterpret_cast<float*>(smem + C * 256);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cp = tid & 63, rg = tid >> 6, r0 = rg * kRpt;
+  const int T = p.seqlen;
+  const bool conv = cv.conv_w != nullptr;
+  const int K = conv ? cv.width : 1;
+  const bool qk_writer = (h0 % (p.hv / p.hk)) == 0;
+  const int npass = 1 + (qk_writer ? 1 : 0) + G;
+  // input of step tt (< 0: the carried tail) at channel ch
+  auto xin = [&](int tt, int ch) -> float {
+    if (tt >= 0) return __bfloat162float(cv.x[b * cv.x_sb + (int64_t)tt * cv.x_st + ch]);
+    const int j = K - 1 + tt;
+    if (j < 0 || cv.tail == nullptr) return 0.f;
+    return load_any(cv.tail, b * cv.tl_sb + (int64_t)j * cv.tl_st + (int64_t)ch * cv.tl_sc, cv.tl_dtype);
+  };
+  for (int pass = 0; pass < npass; ++pass) {
+    // pass 0: k; then q (writer only); then value heads h0 .. h0 + G - 1
+    const int kind = pass == 0 ? 1 : (qk_writer && pass == 1 ? 0 : 2);
+    const int vh = h0 + pass - (qk_writer ? 2 : 1);
+    const int head_ch = (kind == 0 ? hkh : (kind == 1 ? p.hk + hkh : 2 * p.hk + vh)) * D;
+    const int ch = head_ch + 2 * cp;
+    {
+      float w0[KM], w1[KM], a0[KM - 1], a1[KM - 1];
+#pragma unroll
+      for (int i = 0; i < KM; ++i) {
+        const int j = i - (KM - K);
+        w0[i] = (conv && j >= 0) ? cv.conv_w[(int64_t)ch * K + j] : 0.f;
+        w1[i] = (conv && j >= 0) ? cv.conv_w[(int64_t)(ch + 1) * K + j] : 0.f;
+      }
+      const int tb = m * C + r0;  // first step of this thread's rows
+#pragma unroll
+      for (int i = 0; i < KM - 1; ++i) {  // slot i: the input KM - 1 - i steps before tb
+        const int tt = tb - (KM - 1 - i);
+        const bool live = conv && i >= KM - K && tt < T;
+        a0[i] = live ? xin(tt, ch) : 0.f;
+        a1[i] = live ? xin(tt, ch + 1) : 0.f;
+      }
+#pragma unroll 4
+      for (int r = 0; r < kRpt; ++r) {
+        const int tt = tb + r;
+        float y0 = 0.f, y1 = 0.f;
+        if (tt < T) {
+          const __nv_bfloat162 xv =
+              *reinterpret_cast<const __nv_bfloat162*>(cv.x + b * cv.x_sb + (int64_t)tt * cv.x_st + ch);
+          const float x0 = __low2float(xv), x1 = __high2float(xv);
+          if (conv) {
+            y0 = w0[KM - 1] * x0;
+            y1 = w1[KM - 1] * x1;
+#pragma unroll
+            for (int i = 0; i < KM - 1; ++i) {
+              y0 = fmaf(w0[i], a0[i], y0);
+              y1 = fmaf(w1[i], a1[i], y1);
+            }
+#pragma unroll
+            for (int i = 0; i + 1 < KM - 1; ++i) {
+              a0[i] = a0[i + 1];
+              a1[i] = a1[i + 1];
+            }
+            a0[KM - 2] = x0;
+            a1[KM - 2] = x1;
+          } else {
+            y0 = x0;
+            y1 = x1;
+          }
+          y0 = y0 / (1.f + expf(-y0));
+          y1 = y1 / (1.f + expf(-y1));
+        }
+        *reinterpret_cast<float2*>(ys + (r0 + r) * kYsStride + 2 * cp) = make_float2(y0, y1);
+      }
+    }
+    __syncthreads();
+    // a warp per row: normalise q / k, round, store (lane: channels 4 lane .. 4 lane + 3)
+    for (int r = warp; r < C; r += kWarps) {
+      const int tt = m * C + r;
+      float4 y = *reinterpret_cast<const float4*>(ys + r * kYsStride + 4 * lane);
+      if (kind != 2 && cv.l2mode != 0) {
+        const float ss = warp_sum(y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w);
+        const float sc = cv.l2mode == 1 ? 1.f / fmaxf(sqrtf(ss), cv.l2_eps) : rsqrtf(ss + cv.l2_eps);
+        y.x *= sc, y.y *= sc, y.z *= sc, y.w *= sc;
+      }
+      uint2 pk = make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
+      if (tt >= T) pk = make_uint2(0u, 0u);
+      if (kind == 1) {  // the K tile: 16-byte chunk c of row r at (c ^ (r & 7))
+        *reinterpret_cast<uint2*>(smem + r * 256 + (((lane >> 1) ^ (r & 7)) << 4) + (lane & 1) * 8) = pk;
+      }
+      if (tt < T && (kind == 2 || qk_writer)) {
+        bf16* dst = kind == 0 ? cv.qo + ((int64_t)b * T + tt) * p.hk * D + hkh * D
+                    : kind == 1 ? cv.ko + ((int64_t)b * T + tt) * p.hk * D + hkh * D
+                                : cv.vo + ((int64_t)b * T + tt) * p.hv * D + (int64_t)vh * D;
+        *reinterpret_cast<uint2*>(dst + 4 * lane) = pk;
+      }
+    }
+    // the new tail (the last width - 1 inputs), by the CTA of the last chunk
+    if (cv.new_tail != nullptr && conv && (m + 1) * C >= T && (kind == 2 || qk_writer)) {
+      for (int e = tid; e < (K - 1) * D; e += NT) {
+        const int j = e / D, c = head_ch + e % D;
+        const float val = xin(T - (K - 1) + j, c);
+        const int64_t o = b * cv.nt_sb + (int64_t)j * cv.nt_st + (int64_t)c * cv.nt_sc;
+        if (cv.nt_dtype == PBK_BF16) static_cast<bf16*>(cv.new_tail)[o] = __float2bfloat16_rn(val);
+        else static_cast<float*>(cv.new_tail)[o] = val;
+      }
+    }
+    __syncthreads();  // ys is rewritten by the next pass
+  }
+}
+
+template <int G, bool kConv>
+__global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const SolveArgs p, const SolveConvArgs cv) {
   extern __shared__ __align__(16) uint8_t solve_raw[];
   SolveSmem<G>& sm = *reinterpret_cast<SolveSmem<G>*>(solve_raw);
   constexpr int NT = kSolveThreads * G, kWarps = NT / 32;
@@ -471,8 +622,12 @@ __global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const Solv
   const int h = blockIdx.y * G + gi;
   const int hkh = (blockIdx.y * G) / (p.hv / p.hk);
   SolveHead& hd = sm.hd[gi];
+  if constexpr (kConv) {
+    if (cv.state_indices != nullptr && cv.state_indices[b] < 0) return;  // the recurrence skips it too
+    solve_conv_produce<G>(p, cv, solve_raw, b, m, hkh, blockIdx.y * G);
+  }
   // K rows (zero past the sequence end, the reference's padding)
-  for (int c = tid; c < C * 16; c += NT) {
+  for (int c = tid; c < C * 16 && !kConv; c += NT) {
     const int r = c >> 4, ch = c & 15, t = m * C + r;
     const uint32_t dst = tc::smem_u32(sm.k) + r * 256 + ((ch ^ (r & 7)) << 4);
     if (t < len) {
@@ -490,13 +645,25 @@ __global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const Solv
     const int t = m * C + 2 * lane;
     const int64_t tg = t0 + t;  // row in the (packed) tensor
     float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
-    if (t < len) {
-      g0 = load_any(p.g, b * p.g_sb + tg * p.g_st + h * p.g_sh, p.g_dtype);
-      b0 = load_any(p.beta, b * p.b_sb + tg * p.b_st + h * p.b_sh, p.b_dtype);
-    }
-    if (t + 1 < len) {
-      g1 = load_any(p.g, b * p.g_sb + (tg + 1) * p.g_st + h * p.g_sh, p.g_dtype);
-      b1 = load_any(p.beta, b * p.b_sb + (tg + 1) * p.b_st + h * p.b_sh, p.b_dtype);
+    if constexpr (kConv) {  // g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
+      const float al = -expf(cv.a_log[h]), db = cv.dt_bias[h];
+      auto gate = [&](int64_t row, float& gv, float& bv) {
+        const int64_t o = b * cv.d_sb + row * cv.d_st;
+        const float xa = load_any(cv.decay, o + h * cv.d_sh, cv.d_dtype) + db;
+        gv = al * (xa > 20.f ? xa : log1pf(expf(xa)));
+        bv = 1.f / (1.f + expf(-load_any(cv.decay, o + (int64_t)(p.hv + h) * cv.d_sh, cv.d_dtype)));
+      };
+      if (t < len) gate(tg, g0, b0);
+      if (t + 1 < len) gate(tg + 1, g1, b1);
+    } else {
+      if (t < len) {
+        g0 = load_any(p.g, b * p.g_sb + tg * p.g_st + h * p.g_sh, p.g_dtype);
+        b0 = load_any(p.beta, b * p.b_sb + tg * p.b_st + h * p.b_sh, p.b_dtype);
+      }
+      if (t + 1 < len) {
+        g1 = load_any(p.g, b * p.g_sb + (tg + 1) * p.g_st + h * p.g_sh, p.g_dtype);
+        b1 = load_any(p.beta, b * p.b_sb + (tg + 1) * p.b_st + h * p.b_sh, p.b_dtype);
+      }
     }
     const float pair = g0 + g1;
     float incl = pair;
@@ -1300,15 +1467,21 @@ void fill_args(PrefillArgs& a, const pbk_gdn_desc& d) {
 
 // The chunk solve over grid (chunks, value-head groups, sequences): two value heads per CTA
 // (sharing K and K K^T) when the heads per key head are even, else one.
-cudaError_t launch_solve(const SolveArgs& sa, unsigned chunks, unsigned seqs, int hv, int hk, cudaStream_t st) {
+cudaError_t launch_solve(const SolveArgs& sa, unsigned chunks, unsigned seqs, int hv, int hk, cudaStream_t st,
+                         const SolveConvArgs* cv = nullptr) {
+  SolveConvArgs none;
+  memset(&none, 0, sizeof(none));
   auto go = [&](auto kern, int g, size_t smem) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    kern<<<dim3(chunks, (unsigned)(hv / g), seqs), kSolveThreads * g, smem, st>>>(sa);
+    kern<<<dim3(chunks, (unsigned)(hv / g), seqs), kSolveThreads * g, smem, st>>>(sa, cv ? *cv : none);
     return cudaGetLastError();
   };
-  if ((hv / hk) % 2 == 0) return go(gdn_solve_kernel<2>, 2, sizeof(SolveSmem<2>));
-  return go(gdn_solve_kernel<1>, 1, sizeof(SolveSmem<1>));
+  const size_t conv2 = std::max(sizeof(SolveSmem<2>), (size_t)kConvSmem);
+  const size_t conv1 = std::max(sizeof(SolveSmem<1>), (size_t)kConvSmem);
+  if ((hv / hk) % 2 == 0)
+    return cv ? go(gdn_solve_kernel<2, true>, 2, conv2) : go(gdn_solve_kernel<2, false>, 2, sizeof(SolveSmem<2>));
+  return cv ? go(gdn_solve_kernel<1, true>, 1, conv1) : go(gdn_solve_kernel<1, false>, 1, sizeof(SolveSmem<1>));
 }
 
 }  // namespace
@@ -1477,6 +1650,127 @@ cudaError_t launch_gdn_prefill_varlen(const pbk_gdn_desc& d, const int32_t* cu_s
     return cudaGetLastError();
   };
   return d.o.dtype == PBK_BF16 ? go(gdn_prefill_tc_kernel<bf16, true>) : go(gdn_prefill_tc_kernel<float, true>);
+}
+
+// ------------------------------------------------------------------ the layer's prefill
+cudaError_t launch_gdn_out_norm(const pbk_out_norm_desc& d, cudaStream_t st);
+
+namespace {
+// Workspace of pbk_gdn_prefill_layer: the chunk records, then q, k, v and o (bf16, dense).
+struct LayerWs {
+  size_t rec, q, k, v, o, total;
+};
+LayerWs layer_ws(const pbk_gdn_layer_desc& d) {
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t rows = (size_t)d.batch * d.seqlen;
+  LayerWs w;
+  w.rec = 0;
+  w.q = up((size_t)d.batch * ((d.seqlen + C - 1) / C) * d.hv * kSolveBytes);
+  w.k = w.q + up(rows * d.hk * D * 2);
+  w.v = w.k + up(rows * d.hk * D * 2);
+  w.o = w.v + up(rows * d.hv * D * 2);
+  w.total = w.o + up(rows * d.hv * D * 2);
+  return w;
+}
+pbk_view dense_view(const void* p, int heads, int seqlen) {
+  pbk_view v;
+  v.data = p;
+  v.stride_h = D;
+  v.stride_t = (int64_t)heads * D;
+  v.stride_b = (int64_t)seqlen * heads * D;
+  v.dtype = PBK_BF16;
+  v.pad_ = 0;
+  return v;
+}
+}  // namespace
+
+size_t gdn_prefill_layer_workspace(const pbk_gdn_layer_desc& d) { return layer_ws(d).total; }
+
+// GatedDeltaNetLayer.forward over a prefill (gated_deltanet.py:411-440): the conv-fused chunk
+// solve (q, k, v, g, beta and the chunk records from the projection's channels), the
+// recurrence from those records, then the gated output norm.
+cudaError_t launch_gdn_prefill_layer(const pbk_gdn_layer_desc& d, void* ws, cudaStream_t st) {
+  const LayerWs w = layer_ws(d);
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  bf16* qb = reinterpret_cast<bf16*>(base + w.q);
+  bf16* kb = reinterpret_cast<bf16*>(base + w.k);
+  bf16* vb = reinterpret_cast<bf16*>(base + w.v);
+  bf16* ob = reinterpret_cast<bf16*>(base + w.o);
+  // the recurrence's problem over the produced tensors (its g / beta are never read: the
+  // records carry the chunk scalars; they point at the gate inputs only to be valid)
+  pbk_gdn_desc g;
+  memset(&g, 0, sizeof(g));
+  g.batch = d.batch;
+  g.seqlen = d.seqlen;
+  g.hk = d.hk;
+  g.hv = d.hv;
+  g.dk = g.dv = D;
+  g.q = dense_view(qb, d.hk, d.seqlen);
+  g.k = dense_view(kb, d.hk, d.seqlen);
+  g.v = dense_view(vb, d.hv, d.seqlen);
+  g.g = d.decay;
+  g.beta = d.decay;
+  g.o = dense_view(ob, d.hv, d.seqlen);
+  g.h0 = d.state;
+  g.state = d.state;
+  g.state_slot_stride = d.state_slot_stride;
+  g.state_layout = d.state_layout;
+  g.state_indices = d.state_indices;
+  g.scale = d.scale;
+
+  SolveArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.k = kb;
+  sa.seqlen = d.seqlen;
+  sa.hk = d.hk;
+  sa.hv = d.hv;
+  sa.ws = base + w.rec;
+  SolveConvArgs cv;
+  memset(&cv, 0, sizeof(cv));
+  cv.x = static_cast<const bf16*>(d.qkv.data);
+  cv.x_sb = d.qkv.stride_b;
+  cv.x_st = d.qkv.stride_t;
+  cv.tail = d.tail.data;
+  cv.tl_sb = d.tail.stride_b;
+  cv.tl_st = d.tail.stride_t;
+  cv.tl_sc = d.tail.stride_h;
+  cv.tl_dtype = d.tail.dtype;
+  cv.new_tail = const_cast<void*>(d.new_tail.data);
+  cv.nt_sb = d.new_tail.stride_b;
+  cv.nt_st = d.new_tail.stride_t;
+  cv.nt_sc = d.new_tail.stride_h;
+  cv.nt_dtype = d.new_tail.dtype;
+  cv.conv_w = d.conv_weight;
+  cv.width = d.conv_weight != nullptr ? d.width : 1;
+  cv.l2mode = d.l2mode;
+  cv.l2_eps = d.l2_eps;
+  cv.qo = qb;
+  cv.ko = kb;
+  cv.vo = vb;
+  cv.decay = d.decay.data;
+  cv.d_sb = d.decay.stride_b;
+  cv.d_st = d.decay.stride_t;
+  cv.d_sh = d.decay.stride_h;
+  cv.d_dtype = d.decay.dtype;
+  cv.a_log = d.a_log;
+  cv.dt_bias = d.dt_bias;
+  cv.state_indices = d.state_indices;
+  cudaError_t e = launch_solve(sa, (unsigned)((d.seqlen + C - 1) / C), (unsigned)d.batch, d.hv, d.hk, st, &cv);
+  if (e != cudaSuccess) return e;
+  if ((e = launch_gdn_prefill_tc(g, base + w.rec, true, st)) != cudaSuccess) return e;
+  pbk_out_norm_desc on;
+  memset(&on, 0, sizeof(on));
+  on.batch = d.batch;
+  on.seqlen = d.seqlen;
+  on.hv = d.hv;
+  on.weight_dtype = d.o_norm_dtype;
+  on.eps = d.norm_eps;
+  on.o = g.o;
+  on.gate = d.gate;
+  on.gate.stride_h = d.gate.stride_h * D;  // [B, T, hv 128] channels -> [B, T, hv, 128]
+  on.out = d.out;
+  on.weight = d.o_norm;
+  return launch_gdn_out_norm(on, st);
 }
 
 }  // namespace pbk

@@ -59,7 +59,8 @@ def test_abi_version_and_status_strings(lib):
                                           ("pbk_quest_levels", "PbkQuestLevels"),
                                           ("pbk_rope_gather_desc", "PbkRopeGatherDesc"),
                                           ("pbk_archive_write_desc", "PbkArchiveWriteDesc"),
-                                          ("pbk_decode_ext", "PbkDecodeExt"), ("pbk_token_desc", "PbkTokenDesc")])
+                                          ("pbk_decode_ext", "PbkDecodeExt"), ("pbk_token_desc", "PbkTokenDesc"),
+                                          ("pbk_gdn_layer_desc", "PbkGdnLayerDesc")])
 def test_descriptor_layout_matches_header(cname, pyname):
     """Offsets of every field of the ctypes mirror equal the C struct's (checked by
     compiling a probe against include/pbk.h)."""
@@ -126,3 +127,62 @@ def test_token_entry_points_validate_on_the_host(lib):
     assert _capi.LIB.pbk_quest_token_rerank(ctypes.byref(d), None) == 0   # nothing to do
     assert _capi.LIB.pbk_quest_row_ranks(None, 20000, 1, 20000, None, 20000, None) == -2
     assert _capi.LIB.pbk_quest_row_ranks(None, 8, 1, 8, None, 8, None) == -1
+
+
+def _layer_desc(hk=2, hv=8, width=4, t=16):
+    """A pbk_gdn_layer_desc with 16-byte aligned fake pointers (never dereferenced: every case
+    below is rejected on the host before any device call)."""
+    from pseudobrain_b200 import _capi
+    fake = 1 << 20
+    c = (2 * hk + hv) * 128
+    v = lambda sb, st, sh, dt=_capi.PBK_BF16: _capi.PbkView(fake, sb, st, sh, dt, 0)  # noqa: E731
+    d = _capi.PbkGdnLayerDesc()
+    d.batch, d.seqlen, d.hk, d.hv, d.width, d.l2mode = 2, t, hk, hv, width, 1
+    d.l2_eps, d.norm_eps, d.scale, d.state_layout = 1e-6, 1e-5, 128 ** -0.5, _capi.PBK_STATE_KV
+    d.qkv = v(t * c, c, 1)
+    d.tail = v((width - 1) * c, c, 1)
+    d.new_tail = v((width - 1) * c, c, 1)
+    d.new_tail.data = fake + (1 << 16)
+    d.conv_weight = d.a_log = d.dt_bias = d.o_norm = fake
+    d.decay = v(t * 2 * hv, 2 * hv, 1)
+    d.gate = v(t * hv * 128, hv * 128, 1)
+    d.out = v(t * hv * 128, hv * 128, 128, _capi.PBK_F32)
+    d.o_norm_dtype = _capi.PBK_F32
+    d.state = fake
+    d.state_slot_stride = hv * 128 * 128
+    return d
+
+
+def test_layer_entry_points_validate_on_the_host(lib):
+    """pbk_gdn_decode_layer / pbk_gdn_prefill_layer reject what they cannot run before any
+    device call: an in-place tail whose key head is shared by more than 8 value heads (one
+    thread-block cluster per key head), an in-place tail in the prefill (read and written by
+    different CTAs), fp32 or strided projection channels in the prefill, conv widths past 8,
+    a missing or short workspace."""
+    from pseudobrain_b200 import _capi
+    L = _capi.LIB
+    d = _layer_desc()
+    assert L.pbk_gdn_prefill_layer_workspace(ctypes.byref(d)) > 0
+    d.width = 9
+    assert L.pbk_gdn_decode_layer(ctypes.byref(d), None) == _capi.PBK_ERR_SHAPE
+    assert L.pbk_gdn_prefill_layer_workspace(ctypes.byref(d)) == 0
+    d = _layer_desc(hk=1, hv=16)
+    d.new_tail = d.tail  # in place, 16 value heads per key head
+    assert L.pbk_gdn_decode_layer(ctypes.byref(d), None) == _capi.PBK_ERR_SHAPE
+    assert L.pbk_gdn_prefill_layer(ctypes.byref(d), 1 << 20, 1 << 40, None) == _capi.PBK_ERR_INVALID
+    d = _layer_desc()
+    d.qkv.dtype = _capi.PBK_F32
+    assert L.pbk_gdn_prefill_layer(ctypes.byref(d), 1 << 20, 1 << 40, None) == _capi.PBK_ERR_DTYPE
+    d = _layer_desc()
+    d.qkv.stride_h = 2
+    assert L.pbk_gdn_prefill_layer(ctypes.byref(d), 1 << 20, 1 << 40, None) == _capi.PBK_ERR_ALIGN
+    d = _layer_desc()
+    need = L.pbk_gdn_prefill_layer_workspace(ctypes.byref(d))
+    assert L.pbk_gdn_prefill_layer(ctypes.byref(d), None, need, None) == _capi.PBK_ERR_WORKSPACE
+    assert L.pbk_gdn_prefill_layer(ctypes.byref(d), 1 << 20, need - 1, None) == _capi.PBK_ERR_WORKSPACE
+    d.hv = 7  # not a multiple of the key heads
+    assert L.pbk_gdn_decode_layer(ctypes.byref(d), None) == _capi.PBK_ERR_SHAPE
+    d = _layer_desc()
+    d.batch = 0  # nothing to do
+    assert L.pbk_gdn_decode_layer(ctypes.byref(d), None) == _capi.PBK_OK
+    assert L.pbk_gdn_prefill_layer(ctypes.byref(d), None, 0, None) == _capi.PBK_OK
