@@ -287,8 +287,8 @@ PBK_API int pbk_gdn_decode_layer(const pbk_gdn_layer_desc* desc, void* stream);
  * and gating passes never run -- writing q, k, v (bf16) and its chunk records into the
  * workspace; (2) the tensor-core recurrence from them (desc->state is read as h0 and receives
  * the final state, slot state_indices[b] or b); (3) the output RMSNorm and SiLU gate. Needs
- * bf16 qkv with contiguous channels (stride_h 1, even row strides, 4-byte aligned) and gate
- * channels contiguous; new_tail must not be tail. Workspace:
+ * bf16 qkv with contiguous channels (stride_h 1, row strides multiples of 8 elements, 16-byte
+ * aligned: its rows arrive by TMA) and gate channels contiguous; new_tail must not be tail. Workspace:
  * pbk_gdn_prefill_layer_workspace(desc) bytes, 16-byte aligned, private to the call until it
  * completes on `stream`. */
 PBK_API size_t pbk_gdn_prefill_layer_workspace(const pbk_gdn_layer_desc* desc);

@@ -361,7 +361,7 @@ int pbk_gdn_decode_layer(const pbk_gdn_layer_desc* d, void* stream) {
 }
 
 // The prefill layer: the decode layer's checks plus the producer's (bf16 projection channels,
-// contiguous in pairs; a separate new tail).
+// contiguous, rows 16-byte aligned for its TMA copies; a separate new tail).
 static int check_prefill_layer(const pbk_gdn_layer_desc* d) {
   if (d == nullptr || d->batch < 0 || d->seqlen < 0 || d->hk < 1 || d->hv < 1) return PBK_ERR_INVALID;
   if (d->hv % d->hk != 0) return PBK_ERR_SHAPE;
@@ -373,9 +373,9 @@ static int check_prefill_layer(const pbk_gdn_layer_desc* d) {
   if (!view_ok(d->qkv) || !view_ok(d->decay) || !view_ok(d->gate) || !view_ok(d->out)) return PBK_ERR_INVALID;
   if (!d->a_log || !d->dt_bias || !d->o_norm || !d->state) return PBK_ERR_INVALID;
   if (d->qkv.dtype != PBK_BF16 || !dtype_ok(d->o_norm_dtype)) return PBK_ERR_DTYPE;
-  if (d->qkv.stride_h != 1 || (d->qkv.stride_t & 1) || (d->qkv.stride_b & 1) ||
-      (reinterpret_cast<uintptr_t>(d->qkv.data) & 3) || d->gate.stride_h != 1)
-    return PBK_ERR_ALIGN;
+  if (d->qkv.stride_h != 1 || (d->qkv.stride_t & 7) || (d->qkv.stride_b & 7) || d->qkv.stride_t <= 0 ||
+      d->qkv.stride_b <= 0 || !aligned16(d->qkv.data) || d->gate.stride_h != 1)
+    return PBK_ERR_ALIGN;  // the producer's TMA copies: 16-byte aligned rows
   if (d->tail.data != nullptr && !dtype_ok(d->tail.dtype)) return PBK_ERR_DTYPE;
   if (d->new_tail.data != nullptr && (!dtype_ok(d->new_tail.dtype) || d->new_tail.data == d->tail.data))
     return PBK_ERR_INVALID;  // the prefill's tail is read and written by different CTAs

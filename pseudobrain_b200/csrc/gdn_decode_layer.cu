@@ -18,9 +18,11 @@
 //
 // The new tail may overwrite the old one in place. Value heads sharing a key head share that
 // key head's q and k tail channels, so those CTAs form one thread-block cluster (Hv / Hk CTAs,
-// at most 8): every CTA reads its tail rows, arrives on the cluster barrier, runs the step,
-// and waits on the barrier before any tail write; the cluster's first CTA writes the q/k
-// channels, every CTA its own v channels.
+// at most 8): every CTA reads its tail rows, runs the step, then arrives on and waits at the
+// cluster barrier before any tail write; the cluster's first CTA writes the q/k channels,
+// every CTA its own v channels. A token's loads (the projection row, the gate inputs, the
+// output gate) are issued one token ahead, token 0's beside the state loads; bf16 tails and
+// rows move through shared memory in 16-byte vectors.
 #include "common.cuh"
 
 namespace pbk {
@@ -39,6 +41,8 @@ struct DecodeLayerArgs {
   int64_t state_slot_stride;
   const int32_t* state_indices;
   int cluster_sync;  // 1: the tail is rewritten in place by a cluster of Hv / Hk CTAs
+  int vec_tail;      // 1: tail and new tail are bf16 rows of contiguous channels, 16-byte aligned
+  int vec_x;         // 1: the projection rows are bf16, contiguous channels, 16-byte aligned
 };
 
 namespace {
@@ -83,9 +87,10 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_layer_kernel(const Dec
   __shared__ float sh_norm[2][4];
   __shared__ float sh_osq[4];
 
-  float4 s[kRows];
-#pragma unroll
-  for (int i = 0; i < kRows; ++i) s[i] = ld_f4_stream(S + (int64_t)(warp + kWarps * i) * kDim + 4 * lane);
+  // the CTA's conv channels: segment 0 its key head's q, 1 its k, 2 its value head's v
+  __shared__ __align__(16) __nv_bfloat16 sh_tail[KMAX - 1][3 * kDim];
+  __shared__ __align__(16) __nv_bfloat16 sh_x[3 * kDim];
+  auto seg_ch = [&](int seg) { return seg == 0 ? hkh * kDim : (seg == 1 ? (a.hk + hkh) * kDim : (2 * a.hk + h) * kDim); };
 
   // conv channels: A = k (low) or q (high), B = v (low only)
   const int ch_a = low ? (a.hk + hkh) * kDim + c : hkh * kDim + c;
@@ -100,27 +105,86 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_layer_kernel(const Dec
     wb[i] = (conv && low && j >= 0) ? a.conv_weight[(int64_t)ch_b * K + j] : 0.f;
   }
   // history slot i holds the input (H - i) steps back; tail row r = i - (KMAX - K) (zero
-  // where the tail has no row or is absent)
+  // where the tail has no row or is absent). The vector path stages the CTA's tail slice in
+  // shared memory with 16-byte loads (scattered 2-byte loads of it cost far more than its bytes).
+  const bool tail_in = conv && K > 1 && a.tail.data != nullptr;
+  if (tail_in && a.vec_tail) {
+    const __nv_bfloat16* tb = reinterpret_cast<const __nv_bfloat16*>(a.tail.data);
+    for (int e = tid; e < (K - 1) * 48; e += kThreads) {
+      const int r = e / 48, rem = e - r * 48, seg = rem >> 4, ck = rem & 15;
+      const uint4 v = *reinterpret_cast<const uint4*>(tb + (int64_t)n * a.tail.stride_b + (int64_t)r * a.tail.stride_t +
+                                                      seg_ch(seg) + 8 * ck);
+      *reinterpret_cast<uint4*>(&sh_tail[r + (KMAX - K)][seg * kDim + 8 * ck]) = v;
+    }
+  }
+  // the state: 16 float4 per thread, in flight from here until the recurrence
+  float4 s[kRows];
+#pragma unroll
+  for (int i = 0; i < kRows; ++i) s[i] = ld_f4_stream(S + (int64_t)(warp + kWarps * i) * kDim + 4 * lane);
+  if (tail_in && a.vec_tail) __syncthreads();
 #pragma unroll
   for (int i = 0; i < H; ++i) {
     const int r = i - (KMAX - K);
     ha[i] = hb[i] = 0.f;
-    if (conv && r >= 0 && a.tail.data != nullptr) {
-      const int64_t base = (int64_t)n * a.tail.stride_b + (int64_t)r * a.tail.stride_t;
-      ha[i] = load_any(a.tail.data, base + (int64_t)ch_a * a.tail.stride_h, a.tail.dtype);
-      if (low) hb[i] = load_any(a.tail.data, base + (int64_t)ch_b * a.tail.stride_h, a.tail.dtype);
+    if (tail_in && r >= 0) {
+      if (a.vec_tail) {
+        ha[i] = __bfloat162float(sh_tail[i][(low ? kDim : 0) + c]);
+        if (low) hb[i] = __bfloat162float(sh_tail[i][2 * kDim + c]);
+      } else {
+        const int64_t base = (int64_t)n * a.tail.stride_b + (int64_t)r * a.tail.stride_t;
+        ha[i] = load_any(a.tail.data, base + (int64_t)ch_a * a.tail.stride_h, a.tail.dtype);
+        if (low) hb[i] = load_any(a.tail.data, base + (int64_t)ch_b * a.tail.stride_h, a.tail.dtype);
+      }
     }
   }
-  if (a.cluster_sync) cluster_arrive();  // this CTA's tail reads are done
-
   const float a_log_h = a.a_log[h], dt_bias_h = a.dt_bias[h];
   const float wo = load_any(a.o_norm, c, a.o_norm_dtype);
+  // token inputs, loaded one token ahead (token 0's here, beside the state and tail loads)
+  auto x_ab = [&](int t, float& xa, float& xb) {
+    const int64_t xrow = (int64_t)n * a.qkv.stride_b + (int64_t)t * a.qkv.stride_t;
+    xa = load_any(a.qkv.data, xrow + (int64_t)ch_a * a.qkv.stride_h, a.qkv.dtype);
+    xb = low ? load_any(a.qkv.data, xrow + (int64_t)ch_b * a.qkv.stride_h, a.qkv.dtype) : 0.f;
+  };
+  // vector path: threads 0..47 load the token's three 256-byte channel segments
+  auto x_vec = [&](int t) -> uint4 {
+    const int seg = tid >> 4, ck = tid & 15;
+    return *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.qkv.data) +
+                                           (int64_t)n * a.qkv.stride_b + (int64_t)t * a.qkv.stride_t + seg_ch(seg) +
+                                           8 * ck);
+  };
+  uint4 nxv = make_uint4(0u, 0u, 0u, 0u);
+  auto gates = [&](int t, float& da, float& db, float& z) {
+    const int64_t drow = (int64_t)n * a.decay.stride_b + (int64_t)t * a.decay.stride_t;
+    da = load_any(a.decay.data, drow + (int64_t)h * a.decay.stride_h, a.decay.dtype);
+    db = load_any(a.decay.data, drow + (int64_t)(a.hv + h) * a.decay.stride_h, a.decay.dtype);
+    z = low ? load_any(a.gate.data, (int64_t)n * a.gate.stride_b + (int64_t)t * a.gate.stride_t +
+                                        (int64_t)(h * kDim + c) * a.gate.stride_h,
+                       a.gate.dtype)
+            : 0.f;
+  };
+  float nxa = 0.f, nxb = 0.f, nda, ndb, nz;
+  if (a.vec_x) {
+    if (tid < 48) nxv = x_vec(0);
+  } else {
+    x_ab(0, nxa, nxb);
+  }
+  gates(0, nda, ndb, nz);
 
   for (int t = 0; t < a.seqlen; ++t) {
     // ---- conv + SiLU of this token's channels
-    const int64_t xrow = (int64_t)n * a.qkv.stride_b + (int64_t)t * a.qkv.stride_t;
-    const float xa = load_any(a.qkv.data, xrow + (int64_t)ch_a * a.qkv.stride_h, a.qkv.dtype);
-    const float xb = low ? load_any(a.qkv.data, xrow + (int64_t)ch_b * a.qkv.stride_h, a.qkv.dtype) : 0.f;
+    float xa = nxa, xb = nxb;
+    const float da = nda, db = ndb, zt = nz;
+    if (a.vec_x) {  // stage the row (every reader of the previous row has passed a barrier since)
+      if (tid < 48) *reinterpret_cast<uint4*>(&sh_x[8 * tid]) = nxv;
+      if (t + 1 < a.seqlen && tid < 48) nxv = x_vec(t + 1);
+      __syncthreads();
+      xa = __bfloat162float(sh_x[(low ? kDim : 0) + c]);
+      xb = low ? __bfloat162float(sh_x[2 * kDim + c]) : 0.f;
+    }
+    if (t + 1 < a.seqlen) {
+      if (!a.vec_x) x_ab(t + 1, nxa, nxb);
+      gates(t + 1, nda, ndb, nz);
+    }
     float ya = xa, yb = xb;
     if (conv) {
       ya = wa[KMAX - 1] * xa;
@@ -157,13 +221,11 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_layer_kernel(const Dec
     } else {
       sh_q[c] = ya * a.scale;
     }
-    // ---- gating (every thread computes the two scalars; two loads from L1)
-    const int64_t drow = (int64_t)n * a.decay.stride_b + (int64_t)t * a.decay.stride_t;
-    const float xg = load_any(a.decay.data, drow + (int64_t)h * a.decay.stride_h, a.decay.dtype) + dt_bias_h;
+    // ---- gating (every thread computes the two scalars)
+    const float xg = da + dt_bias_h;
     const float sp = xg > 20.f ? xg : log1pf(expf(xg));
     const float gam = expf(-expf(a_log_h) * sp);
-    const float bet =
-        1.f / (1.f + expf(-load_any(a.decay.data, drow + (int64_t)(a.hv + h) * a.decay.stride_h, a.decay.dtype)));
+    const float bet = 1.f / (1.f + expf(-db));
     __syncthreads();
     // ---- the recurrence step (gdn_decode.cu's register form); o into sh_o
     if constexpr (LAYOUT == PBK_STATE_KV) {
@@ -234,10 +296,7 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_layer_kernel(const Dec
     __syncthreads();
     if (low) {
       const float ms = (sh_osq[0] + sh_osq[1] + sh_osq[2] + sh_osq[3]) * (1.f / kDim);
-      const float z = load_any(a.gate.data, (int64_t)n * a.gate.stride_b + (int64_t)t * a.gate.stride_t +
-                                                (int64_t)(h * kDim + c) * a.gate.stride_h,
-                               a.gate.dtype);
-      const float y = o * rsqrtf(ms + a.norm_eps) * wo * silu_exact(z);
+      const float y = o * rsqrtf(ms + a.norm_eps) * wo * silu_exact(zt);
       store_any(a.out.data, (int64_t)n * a.out.stride_b + (int64_t)t * a.out.stride_t + (int64_t)h * a.out.stride_h + c,
                 a.out.dtype, y);
     }
@@ -247,24 +306,45 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_layer_kernel(const Dec
 #pragma unroll
   for (int i = 0; i < kRows; ++i) st_f4_stream(S + (int64_t)(warp + kWarps * i) * kDim + 4 * lane, s[i]);
 
-  // ---- the new tail: the last width - 1 inputs (history slots H - (K - 1) .. H - 1)
+  // ---- the new tail: the last width - 1 inputs (history slots H - (K - 1) .. H - 1). The
+  // cluster barrier sits here, after every read of the old tail has been consumed (arriving
+  // earlier would make the release wait on the state loads still in flight).
   if (conv && a.new_tail.data != nullptr) {
-    if (a.cluster_sync) cluster_wait();  // every CTA of the cluster has read the old tail
+    if (a.cluster_sync) {
+      cluster_arrive();
+      cluster_wait();  // every CTA of the cluster has read the old tail
+    }
     uint32_t rank = 0;
     if (a.cluster_sync) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
     // q and k channels: the cluster's first CTA (or, without a cluster, the CTA whose value
     // head is the first of its key head); v channels: every CTA
     const bool lead = a.cluster_sync ? rank == 0 : (h % ratio) == 0;
+    if (a.vec_tail) {  // through shared memory, 16-byte stores (sh_tail's last reads were long ago)
 #pragma unroll
-    for (int i = 0; i < H; ++i) {
-      const int r = i - (KMAX - K);
-      if (r < 0) continue;
-      const int64_t base = (int64_t)n * a.new_tail.stride_b + (int64_t)r * a.new_tail.stride_t;
-      if (lead) store_any(a.new_tail.data, base + (int64_t)ch_a * a.new_tail.stride_h, a.new_tail.dtype, ha[i]);
-      if (low) store_any(a.new_tail.data, base + (int64_t)ch_b * a.new_tail.stride_h, a.new_tail.dtype, hb[i]);
+      for (int i = 0; i < H; ++i) {
+        if (i < KMAX - K) continue;
+        sh_tail[i][(low ? kDim : 0) + c] = __float2bfloat16_rn(ha[i]);
+        if (low) sh_tail[i][2 * kDim + c] = __float2bfloat16_rn(hb[i]);
+      }
+      __syncthreads();
+      __nv_bfloat16* nb = const_cast<__nv_bfloat16*>(reinterpret_cast<const __nv_bfloat16*>(a.new_tail.data));
+      for (int e = tid; e < (K - 1) * 48; e += kThreads) {
+        const int r = e / 48, rem = e - r * 48, seg = rem >> 4, ck = rem & 15;
+        if (seg < 2 && !lead) continue;
+        *reinterpret_cast<uint4*>(nb + (int64_t)n * a.new_tail.stride_b + (int64_t)r * a.new_tail.stride_t +
+                                  seg_ch(seg) + 8 * ck) =
+            *reinterpret_cast<const uint4*>(&sh_tail[r + (KMAX - K)][seg * kDim + 8 * ck]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        const int r = i - (KMAX - K);
+        if (r < 0) continue;
+        const int64_t base = (int64_t)n * a.new_tail.stride_b + (int64_t)r * a.new_tail.stride_t;
+        if (lead) store_any(a.new_tail.data, base + (int64_t)ch_a * a.new_tail.stride_h, a.new_tail.dtype, ha[i]);
+        if (low) store_any(a.new_tail.data, base + (int64_t)ch_b * a.new_tail.stride_h, a.new_tail.dtype, hb[i]);
+      }
     }
-  } else if (a.cluster_sync) {
-    cluster_wait();  // every arrive is matched by a wait before the CTA exits
   }
 }
 
@@ -318,6 +398,12 @@ cudaError_t launch_gdn_decode_layer(const pbk_gdn_layer_desc& d, cudaStream_t st
                     d.new_tail.data == d.tail.data && d.hv / d.hk > 1)
                        ? 1
                        : 0;
+  auto rows16 = [](const pbk_view& v) {  // bf16 rows of contiguous channels, 16-byte aligned
+    return v.data != nullptr && v.dtype == PBK_BF16 && v.stride_h == 1 && v.stride_t % 8 == 0 &&
+           v.stride_b % 8 == 0 && (reinterpret_cast<uintptr_t>(v.data) & 15) == 0;
+  };
+  a.vec_tail = rows16(d.tail) && (d.new_tail.data == nullptr || rows16(d.new_tail)) ? 1 : 0;
+  a.vec_x = rows16(d.qkv) ? 1 : 0;
   const bool narrow = a.width <= 4;
   if (d.state_layout == PBK_STATE_KV)
     return narrow ? launch<PBK_STATE_KV, 4>(a, st) : launch<PBK_STATE_KV, 8>(a, st);

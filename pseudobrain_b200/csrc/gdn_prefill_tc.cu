@@ -389,10 +389,9 @@ struct SolveConvArgs {
   const float* a_log;
   const float* dt_bias;
   const int32_t* state_indices;  // a sequence whose index is negative is skipped (no tail write)
+  int* err;                       // the device error word (a copy that never landed)
 };
 constexpr int kConvMaxWidth = 8;
-constexpr int kYsStride = D + 4;                      // fp32 row stride of the staged conv rows
-constexpr int kConvSmem = C * 256 + C * kYsStride * 4;  // K tile + staged rows
 
 // Rows [t0, t0 + len) of packed sequence s, clamped into [0, T] (offsets out of order or out of
 // range read nothing outside the tensors; they are caller errors).
@@ -481,127 +480,160 @@ __device__ __forceinline__ void group_sync(int g) {
   }
 }
 
-// The conv producer of one CTA (kConv): per 128-channel head of its chunk -- k first (into the
-// shared K tile), q (by the CTA of the key head's first value-head group), then its value
-// heads -- thread (channel pair, row group) convolves its rows from a register window of the
-// width - 1 inputs before them and stages SiLU(y) in fp32; then a warp per row normalises
-// (q, k), rounds to bf16 and stores 8 bytes per lane. The CTA of the sequence's last chunk
-// writes the new tail. Rows past the end are zero in the K tile and not stored.
-template <int G>
-__device__ void solve_conv_produce(const SolveArgs& p, const SolveConvArgs& cv, uint8_t* smem, int b, int m, int hkh,
-                                   int h0) {
-  constexpr int NT = kSolveThreads * G, kWarps = NT / 32;
-  constexpr int kGroups = NT / 64, kRpt = C / kGroups;  // row groups, rows per thread
-  constexpr int KM = kConvMaxWidth;
-  float* ys = reinterpret_cast<float*>(smem + C * 256);
+// The conv producer of one CTA (kConv). Per 128-channel head of its chunk -- k first (into
+// the shared K tile), q (by the CTA of the key head's first value-head group), then its value
+// heads -- one TMA copy brings the head's 64 rows and the 7 before them (zero outside the
+// sequence) into one of two 18 KB buffers, the next head's copy in flight while this one is
+// computed; the first chunk patches the steps before the sequence from the carried tail. A
+// half-warp per row then convolves (lane: 8 channels, its taps' weights in registers), applies
+// SiLU, normalises q and k (one half-warp sum), rounds to bf16 and stores 16 bytes per lane. The CTA
+// of the sequence's last chunk writes the new tail from the same tile. Rows past the end are
+// zero in the K tile and not stored. Returns false (error code recorded) if a copy never lands.
+constexpr int kRawRows = C + kConvMaxWidth - 1;         // the chunk's rows and the 7 before them
+constexpr uint32_t kRawBytes = kRawRows * D * 2;        // 18,176 bytes per head
+static_assert(kRawBytes % 128 == 0, "TMA destinations stay 128-byte aligned");
+// KM: the compiled tap count (4 or 8; the layer's width right-aligned in it).
+template <int G, int KM>
+__device__ bool solve_conv_produce(const SolveArgs& p, const SolveConvArgs& cv, const CUtensorMap* xmap,
+                                   uint8_t* smem, uint64_t* bars, int b, int m, int hkh, int h0) {
+  constexpr int NT = kSolveThreads * G, kWarps = NT / 32, kHalo = kConvMaxWidth - 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int cp = tid & 63, rg = tid >> 6, r0 = rg * kRpt;
   const int T = p.seqlen;
   const bool conv = cv.conv_w != nullptr;
   const int K = conv ? cv.width : 1;
   const bool qk_writer = (h0 % (p.hv / p.hk)) == 0;
   const int npass = 1 + (qk_writer ? 1 : 0) + G;
-  // input of step tt (< 0: the carried tail) at channel ch
-  auto xin = [&](int tt, int ch) -> float {
-    if (tt >= 0) return __bfloat162float(cv.x[b * cv.x_sb + (int64_t)tt * cv.x_st + ch]);
-    const int j = K - 1 + tt;
-    if (j < 0 || cv.tail == nullptr) return 0.f;
-    return load_any(cv.tail, b * cv.tl_sb + (int64_t)j * cv.tl_st + (int64_t)ch * cv.tl_sc, cv.tl_dtype);
+  const int t_first = m * C - kHalo;  // the step of raw row 0
+  // pass 0: k; then q (writer only); then value heads h0 .. h0 + G - 1. kind: 0 q, 1 k, 2 v
+  auto head_of = [&](int pass, int& kind, int& vh) {
+    kind = pass == 0 ? 1 : (qk_writer && pass == 1 ? 0 : 2);
+    vh = h0 + pass - (qk_writer ? 2 : 1);
+    return (kind == 0 ? hkh : (kind == 1 ? p.hk + hkh : 2 * p.hk + vh)) * D;
   };
+  auto buf_of = [&](int pass) { return smem + C * 256 + (pass & 1) * kRawBytes; };
+  auto issue = [&](int pass) {
+    int kind, vh;
+    const int hc = head_of(pass, kind, vh);
+    tc::mbar_expect_tx(&bars[pass & 1], kRawBytes);
+    tc::tma_load_3d(buf_of(pass), xmap, &bars[pass & 1], hc, t_first, b);
+  };
+  if (tid == 0) {
+    issue(0);
+    if (npass > 1) issue(1);
+  }
   for (int pass = 0; pass < npass; ++pass) {
-    // pass 0: k; then q (writer only); then value heads h0 .. h0 + G - 1
-    const int kind = pass == 0 ? 1 : (qk_writer && pass == 1 ? 0 : 2);
-    const int vh = h0 + pass - (qk_writer ? 2 : 1);
-    const int head_ch = (kind == 0 ? hkh : (kind == 1 ? p.hk + hkh : 2 * p.hk + vh)) * D;
-    const int ch = head_ch + 2 * cp;
-    {
-      float w0[KM], w1[KM], a0[KM - 1], a1[KM - 1];
+    int kind, vh;
+    const int hc = head_of(pass, kind, vh);
+    bf16* raw = reinterpret_cast<bf16*>(buf_of(pass));
+    const bool landed = tc::mbar_wait(&bars[pass & 1], (pass >> 1) & 1);
+    if (__syncthreads_or(!landed)) {  // a copy never landed: record it, drain, give up
+      if (tid == 0 && cv.err != nullptr) atomicCAS(cv.err, 0, 280);
+      for (int q = pass; q < min(npass, pass + 2); ++q) tc::mbar_wait(&bars[q & 1], (q >> 1) & 1);
+      return false;
+    }
+    if (conv && t_first < 0) {  // the first chunk: steps before the sequence from the tail
+      for (int e = tid; e < (K - 1) * D; e += NT) {
+        const int jj = e / D, c = e - jj * D;  // tail row jj holds step jj - (K - 1)
+        const float val = cv.tail != nullptr ? load_any(cv.tail, b * cv.tl_sb + (int64_t)jj * cv.tl_st +
+                                                                      (int64_t)(hc + c) * cv.tl_sc,
+                                                        cv.tl_dtype)
+                                             : 0.f;
+        raw[(jj - (K - 1) - t_first) * D + c] = __float2bfloat16_rn(val);
+      }
+      __syncthreads();
+    }
+    // half-warp per row (lane: 8 channels, 16 bytes), two rows per warp and step; the lane's
+    // weights in registers, tap i right-aligned (weight column i - (KM - K))
+    const int l16 = lane & 15, half = lane >> 4;
+    float w[8][KM];
+    if (conv && K == KM && KM == 4) {  // rows of 4 taps: one 16-byte load per channel
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        const float4 w4 = *reinterpret_cast<const float4*>(cv.conv_w + (int64_t)(hc + 8 * l16 + c8) * 4);
+        w[c8][0] = w4.x, w[c8][1] = w4.y, w[c8][2] = w4.z, w[c8][3] = w4.w;
+      }
+    } else {
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+#pragma unroll
+        for (int i = 0; i < KM; ++i) {
+          const int j = i - (KM - K);
+          w[c8][i] = conv ? (j >= 0 ? cv.conv_w[(int64_t)(hc + 8 * l16 + c8) * K + j] : 0.f)
+                          : (i == KM - 1 ? 1.f : 0.f);
+        }
+    }
+    for (int r = 2 * warp + half; r < C; r += 2 * kWarps) {
+      float y[8];
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) y[c8] = 0.f;
 #pragma unroll
       for (int i = 0; i < KM; ++i) {
-        const int j = i - (KM - K);
-        w0[i] = (conv && j >= 0) ? cv.conv_w[(int64_t)ch * K + j] : 0.f;
-        w1[i] = (conv && j >= 0) ? cv.conv_w[(int64_t)(ch + 1) * K + j] : 0.f;
-      }
-      const int tb = m * C + r0;  // first step of this thread's rows
+        if (i < KM - K) continue;  // taps left of the layer's width
+        const uint4 xv =  // raw row of step m C + r - (KM - 1 - i)
+            *reinterpret_cast<const uint4*>(raw + (r + i + kHalo - (KM - 1)) * D + 8 * l16);
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-      for (int i = 0; i < KM - 1; ++i) {  // slot i: the input KM - 1 - i steps before tb
-        const int tt = tb - (KM - 1 - i);
-        const bool live = conv && i >= KM - K && tt < T;
-        a0[i] = live ? xin(tt, ch) : 0.f;
-        a1[i] = live ? xin(tt, ch + 1) : 0.f;
-      }
-#pragma unroll 4
-      for (int r = 0; r < kRpt; ++r) {
-        const int tt = tb + r;
-        float y0 = 0.f, y1 = 0.f;
-        if (tt < T) {
-          const __nv_bfloat162 xv =
-              *reinterpret_cast<const __nv_bfloat162*>(cv.x + b * cv.x_sb + (int64_t)tt * cv.x_st + ch);
-          const float x0 = __low2float(xv), x1 = __high2float(xv);
-          if (conv) {
-            y0 = w0[KM - 1] * x0;
-            y1 = w1[KM - 1] * x1;
-#pragma unroll
-            for (int i = 0; i < KM - 1; ++i) {
-              y0 = fmaf(w0[i], a0[i], y0);
-              y1 = fmaf(w1[i], a1[i], y1);
-            }
-#pragma unroll
-            for (int i = 0; i + 1 < KM - 1; ++i) {
-              a0[i] = a0[i + 1];
-              a1[i] = a1[i + 1];
-            }
-            a0[KM - 2] = x0;
-            a1[KM - 2] = x1;
-          } else {
-            y0 = x0;
-            y1 = x1;
-          }
-          y0 = y0 / (1.f + expf(-y0));
-          y1 = y1 / (1.f + expf(-y1));
+        for (int q2 = 0; q2 < 4; ++q2) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[q2]));
+          y[2 * q2] = fmaf(w[2 * q2][i], f.x, y[2 * q2]);
+          y[2 * q2 + 1] = fmaf(w[2 * q2 + 1][i], f.y, y[2 * q2 + 1]);
         }
-        *reinterpret_cast<float2*>(ys + (r0 + r) * kYsStride + 2 * cp) = make_float2(y0, y1);
       }
-    }
-    __syncthreads();
-    // a warp per row: normalise q / k, round, store (lane: channels 4 lane .. 4 lane + 3)
-    for (int r = warp; r < C; r += kWarps) {
-      const int tt = m * C + r;
-      float4 y = *reinterpret_cast<const float4*>(ys + r * kYsStride + 4 * lane);
-      if (kind != 2 && cv.l2mode != 0) {
-        const float ss = warp_sum(y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w);
+      // SiLU as h (1 + tanh h), h = y / 2, on the hardware tanh (one special-function
+      // instruction; relative error about 2^-11, below the bf16 rounding of q, k and v)
+      float ss = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        const float hh = 0.5f * y[c8];
+        float th;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(th) : "f"(hh));
+        y[c8] = fmaf(hh, th, hh);
+        ss = fmaf(y[c8], y[c8], ss);
+      }
+      if (kind != 2 && cv.l2mode != 0) {  // the row's sum over its half-warp
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float sc = cv.l2mode == 1 ? 1.f / fmaxf(sqrtf(ss), cv.l2_eps) : rsqrtf(ss + cv.l2_eps);
-        y.x *= sc, y.y *= sc, y.z *= sc, y.w *= sc;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) y[c8] *= sc;
       }
-      uint2 pk = make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
-      if (tt >= T) pk = make_uint2(0u, 0u);
-      if (kind == 1) {  // the K tile: 16-byte chunk c of row r at (c ^ (r & 7))
-        *reinterpret_cast<uint2*>(smem + r * 256 + (((lane >> 1) ^ (r & 7)) << 4) + (lane & 1) * 8) = pk;
-      }
+      const int tt = m * C + r;
+      uint4 pk = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                            pack_bf16x2(y[6], y[7]));
+      if (tt >= T) pk = make_uint4(0u, 0u, 0u, 0u);
+      if (kind == 1)  // the K tile: 16-byte chunk c of row r at (c ^ (r & 7))
+        *reinterpret_cast<uint4*>(smem + r * 256 + ((l16 ^ (r & 7)) << 4)) = pk;
       if (tt < T && (kind == 2 || qk_writer)) {
         bf16* dst = kind == 0 ? cv.qo + ((int64_t)b * T + tt) * p.hk * D + hkh * D
                     : kind == 1 ? cv.ko + ((int64_t)b * T + tt) * p.hk * D + hkh * D
                                 : cv.vo + ((int64_t)b * T + tt) * p.hv * D + (int64_t)vh * D;
-        *reinterpret_cast<uint2*>(dst + 4 * lane) = pk;
+        *reinterpret_cast<uint4*>(dst + 8 * l16) = pk;
       }
     }
-    // the new tail (the last width - 1 inputs), by the CTA of the last chunk
+    // the new tail (the last width - 1 inputs), by the CTA of the last chunk, from the tile
     if (cv.new_tail != nullptr && conv && (m + 1) * C >= T && (kind == 2 || qk_writer)) {
       for (int e = tid; e < (K - 1) * D; e += NT) {
-        const int j = e / D, c = head_ch + e % D;
-        const float val = xin(T - (K - 1) + j, c);
-        const int64_t o = b * cv.nt_sb + (int64_t)j * cv.nt_st + (int64_t)c * cv.nt_sc;
+        const int j = e / D, c = e - j * D;
+        const float val = __bfloat162float(raw[(T - (K - 1) + j - t_first) * D + c]);
+        const int64_t o = b * cv.nt_sb + (int64_t)j * cv.nt_st + (int64_t)(hc + c) * cv.nt_sc;
         if (cv.nt_dtype == PBK_BF16) static_cast<bf16*>(cv.new_tail)[o] = __float2bfloat16_rn(val);
         else static_cast<float*>(cv.new_tail)[o] = val;
       }
     }
-    __syncthreads();  // ys is rewritten by the next pass
+    __syncthreads();  // the tile has been read: its buffer takes the pass after next
+    if (tid == 0 && pass + 2 < npass) {
+      tc::fence_proxy_async_smem();
+      issue(pass + 2);
+    }
   }
+  return true;
 }
 
-template <int G, bool kConv>
-__global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const SolveArgs p, const SolveConvArgs cv) {
-  extern __shared__ __align__(16) uint8_t solve_raw[];
+// The solve's body. kConvW: 0 the plain solve (gdn_solve_kernel); 4 or 8 with the conv
+// producer compiled for that many taps (gdn_solve_conv_kernel).
+template <int G, int kConvW>
+__device__ __forceinline__ void solve_body(const SolveArgs& p, const SolveConvArgs& cv, const CUtensorMap* xmap) {
+  extern __shared__ __align__(128) uint8_t solve_raw[];
   SolveSmem<G>& sm = *reinterpret_cast<SolveSmem<G>*>(solve_raw);
   constexpr int NT = kSolveThreads * G, kWarps = NT / 32;
   const int b = blockIdx.z;
@@ -622,9 +654,17 @@ __global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const Solv
   const int h = blockIdx.y * G + gi;
   const int hkh = (blockIdx.y * G) / (p.hv / p.hk);
   SolveHead& hd = sm.hd[gi];
+  constexpr bool kConv = kConvW != 0;
   if constexpr (kConv) {
     if (cv.state_indices != nullptr && cv.state_indices[b] < 0) return;  // the recurrence skips it too
-    solve_conv_produce<G>(p, cv, solve_raw, b, m, hkh, blockIdx.y * G);
+    __shared__ uint64_t conv_bars[2];
+    if (tid == 0) {
+      tc::mbar_init(&conv_bars[0], 1);
+      tc::mbar_init(&conv_bars[1], 1);
+      tc::fence_barrier_init();
+    }
+    __syncthreads();
+    if (!solve_conv_produce<G, kConvW>(p, cv, xmap, solve_raw, conv_bars, b, m, hkh, blockIdx.y * G)) return;
   }
   // K rows (zero past the sequence end, the reference's padding)
   for (int c = tid; c < C * 16 && !kConv; c += NT) {
@@ -882,6 +922,16 @@ __global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const Solv
       }
     }
   }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kSolveThreads * G) gdn_solve_kernel(const SolveArgs p) {
+  solve_body<G, 0>(p, SolveConvArgs{}, nullptr);
+}
+template <int G, int kConvW>
+__global__ void __launch_bounds__(kSolveThreads * G, 8 / G)
+    gdn_solve_conv_kernel(const SolveArgs p, const SolveConvArgs cv, const __grid_constant__ CUtensorMap xmap) {
+  solve_body<G, kConvW>(p, cv, &xmap);
 }
 
 template <typename TOut, bool kOffload>
@@ -1468,20 +1518,30 @@ void fill_args(PrefillArgs& a, const pbk_gdn_desc& d) {
 // The chunk solve over grid (chunks, value-head groups, sequences): two value heads per CTA
 // (sharing K and K K^T) when the heads per key head are even, else one.
 cudaError_t launch_solve(const SolveArgs& sa, unsigned chunks, unsigned seqs, int hv, int hk, cudaStream_t st,
-                         const SolveConvArgs* cv = nullptr) {
-  SolveConvArgs none;
-  memset(&none, 0, sizeof(none));
+                         const SolveConvArgs* cv = nullptr, const CUtensorMap* xmap = nullptr) {
   auto go = [&](auto kern, int g, size_t smem) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    kern<<<dim3(chunks, (unsigned)(hv / g), seqs), kSolveThreads * g, smem, st>>>(sa, cv ? *cv : none);
+    kern<<<dim3(chunks, (unsigned)(hv / g), seqs), kSolveThreads * g, smem, st>>>(sa);
     return cudaGetLastError();
   };
-  const size_t conv2 = std::max(sizeof(SolveSmem<2>), (size_t)kConvSmem);
-  const size_t conv1 = std::max(sizeof(SolveSmem<1>), (size_t)kConvSmem);
-  if ((hv / hk) % 2 == 0)
-    return cv ? go(gdn_solve_kernel<2, true>, 2, conv2) : go(gdn_solve_kernel<2, false>, 2, sizeof(SolveSmem<2>));
-  return cv ? go(gdn_solve_kernel<1, true>, 1, conv1) : go(gdn_solve_kernel<1, false>, 1, sizeof(SolveSmem<1>));
+  auto go_conv = [&](auto kern, int g, size_t smem) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kern<<<dim3(chunks, (unsigned)(hv / g), seqs), kSolveThreads * g, smem, st>>>(sa, *cv, *xmap);
+    return cudaGetLastError();
+  };
+  // the conv producer's smem: the K tile, then two raw tiles over the inverse's scratch
+  constexpr size_t kConvSmem = C * 256 + 2 * kRawBytes;
+  const size_t conv2 = std::max(sizeof(SolveSmem<2>), kConvSmem);
+  const size_t conv1 = std::max(sizeof(SolveSmem<1>), kConvSmem);
+  const bool narrow = cv != nullptr && (cv->conv_w == nullptr || cv->width <= 4);
+  if ((hv / hk) % 2 == 0) {
+    if (cv == nullptr) return go(gdn_solve_kernel<2>, 2, sizeof(SolveSmem<2>));
+    return narrow ? go_conv(gdn_solve_conv_kernel<2, 4>, 2, conv2) : go_conv(gdn_solve_conv_kernel<2, 8>, 2, conv2);
+  }
+  if (cv == nullptr) return go(gdn_solve_kernel<1>, 1, sizeof(SolveSmem<1>));
+  return narrow ? go_conv(gdn_solve_conv_kernel<1, 4>, 1, conv1) : go_conv(gdn_solve_conv_kernel<1, 8>, 1, conv1);
 }
 
 }  // namespace
@@ -1755,7 +1815,15 @@ cudaError_t launch_gdn_prefill_layer(const pbk_gdn_layer_desc& d, void* ws, cuda
   cv.a_log = d.a_log;
   cv.dt_bias = d.dt_bias;
   cv.state_indices = d.state_indices;
-  cudaError_t e = launch_solve(sa, (unsigned)((d.seqlen + C - 1) / C), (unsigned)d.batch, d.hv, d.hk, st, &cv);
+  cv.err = device_error_word();
+  // x as [B, T, channels] bf16; boxes of 128 channels x 71 steps (zero outside the tensor)
+  CUtensorMap xmap;
+  const uint64_t xdims[3] = {(uint64_t)(2 * d.hk + d.hv) * D, (uint64_t)d.seqlen, (uint64_t)d.batch};
+  const uint64_t xstrides[2] = {(uint64_t)d.qkv.stride_t * 2, (uint64_t)d.qkv.stride_b * 2};
+  const uint32_t xbox[3] = {(uint32_t)D, (uint32_t)kRawRows, 1};
+  if (!make_tmap_plain(&xmap, d.qkv.data, true, 3, xdims, xstrides, xbox)) return cudaErrorInvalidValue;
+  cudaError_t e =
+      launch_solve(sa, (unsigned)((d.seqlen + C - 1) / C), (unsigned)d.batch, d.hv, d.hk, st, &cv, &xmap);
   if (e != cudaSuccess) return e;
   if ((e = launch_gdn_prefill_tc(g, base + w.rec, true, st)) != cudaSuccess) return e;
   pbk_out_norm_desc on;

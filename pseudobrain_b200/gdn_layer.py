@@ -11,7 +11,11 @@ pbk_gdn_gating, pbk_gdn_out_norm), with the reference's names and argument meani
   tensor-core kernels, decode on the register kernel), as the vLLM adapter runs it;
 * ``gated_deltanet_decode``: the same for a decode step (the few tokens select_kernel sends
   to the sequential recurrence, :291-294) as ONE kernel (pbk_gdn_decode_layer), the state
-  and the conv tail updated in place.
+  and the conv tail updated in place, fp32 between the stages as in the reference;
+* ``gated_deltanet_prefill``: the same for a prefill (pbk_gdn_prefill_layer), the conv, norm
+  and gating fused into the chunk solve.
+``gated_deltanet_core`` runs the pieces as separate kernels: at config-1 and config-2 shapes
+they measured faster than the two fused entry points.
 """
 from __future__ import annotations
 
@@ -103,23 +107,9 @@ def gated_deltanet_core(qkv: torch.Tensor, gate: torch.Tensor, decay: torch.Tens
     (qkv [B,T,C], gate [B,T,Hv*128], decay [B,T,2Hv]) to the gated, normed output [B,T,Hv,128]
     (fp32), with the conv tail [B,K-1,C] and the fp32 state [B,Hv,128,128] carried.
     Returns (out, new state, new tail)."""
-    from .gated_deltanet import SEQUENTIAL_MAX, gated_delta_rule
+    from .gated_deltanet import gated_delta_rule
     b, t, _ = qkv.shape
     new_tail = torch.empty_like(conv_tail)
-    if t > SEQUENTIAL_MAX and qkv.dtype == torch.bfloat16 and qkv.stride(-1) == 1 and gate.stride(-1) == 1:
-        # the prefill: conv, norm and gating fused into the chunk solve (pbk_gdn_prefill_layer)
-        new_state = state.clone()
-        if conv_weight is None:
-            new_tail.copy_(conv_tail)
-        out = gated_deltanet_prefill(qkv, gate, decay, conv_tail, conv_weight, a_log, dt_bias, o_norm, new_state,
-                                     hk, hv, l2mode, norm_eps, new_tail=new_tail if conv_weight is not None else None)
-        return out, new_state, new_tail
-    if t <= SEQUENTIAL_MAX:  # the decode step: one fused kernel on copies of the carried state
-        new_state = state.clone()
-        new_tail.copy_(conv_tail)
-        out = gated_deltanet_decode(qkv, gate, decay, new_tail, conv_weight, a_log, dt_bias, o_norm, new_state, hk,
-                                    hv, l2mode, norm_eps)
-        return out, new_state, new_tail
     q, k, v = conv_qkv(qkv, conv_tail, conv_weight, hk, hv, l2mode, new_tail)
     g, beta = gdn_gating(decay, a_log, dt_bias, beta_dtype=torch.bfloat16)
     o, new_state = gated_delta_rule(q, k, v, g, beta, 128 ** -0.5, state, "sequential" if t <= 4 else "chunked")
