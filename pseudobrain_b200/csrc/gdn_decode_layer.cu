@@ -59,7 +59,10 @@ __device__ __forceinline__ void store_any(const void* p, int64_t i, int dtype, f
   else const_cast<float*>(reinterpret_cast<const float*>(p))[i] = x;
 }
 
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+// Relaxed arrive: the only ordering the tail needs is the old tail's reads before the cluster
+// leader's writes, and those reads have long returned (their values feed the state stores
+// issued before the arrive). A release arrive would also wait for those 64 KB of stores.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
 // KMAX: the compiled tap count (4 or 8); the layer's `width` taps are right-aligned in it
@@ -307,8 +310,7 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_layer_kernel(const Dec
   for (int i = 0; i < kRows; ++i) st_f4_stream(S + (int64_t)(warp + kWarps * i) * kDim + 4 * lane, s[i]);
 
   // ---- the new tail: the last width - 1 inputs (history slots H - (K - 1) .. H - 1). The
-  // cluster barrier sits here, after every read of the old tail has been consumed (arriving
-  // earlier would make the release wait on the state loads still in flight).
+  // cluster barrier sits here, after every read of the old tail has been consumed.
   if (conv && a.new_tail.data != nullptr) {
     if (a.cluster_sync) {
       cluster_arrive();
