@@ -762,10 +762,11 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
     (16 key / 32 value heads) is split by value head over the ranks, and within a rank along
     T (segments chained by the segment scan) so a few heads still fill the SMs; the
     sliding-window attention branch (32 query / 8 key heads, window 4096) is split by key
-    head. Each branch's output is all-gathered (NCCL) into head-major [N, rows, heads/N * 128]
-    buffers, the hidden-4096 layout the output projection reads: the GDN branch, its gather
-    running under the attention, then the attention in query chunks whose gathers run while
-    the next chunk computes (sharding.hybrid_layer_sharded). Strong scaling: the job is one layer pass
+    head. Each branch's output is gathered into rank-major [N, rows, heads/N * 128] buffers
+    (the hidden-4096 layout the output projection reads): the GDN branch in two parts, each
+    sent as soon as it is written, then the attention in query chunks, each sent while the
+    next chunk computes (sharding.hybrid_layer_sharded): by copy-engine pushes into every
+    rank's mapped buffers up to 4 GPUs, by NCCL's all-gather above. Strong scaling: the job is one layer pass
     whatever N; at N > 1 rank 0 also times the unsharded layer (all heads on one GPU) for
     the strong-scaling efficiency t1 / (N tN)."""
     import torch
@@ -789,6 +790,9 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         return x, qa, ka, va
 
     x, qa, ka, va = shard_inputs(world, 4 + 1000 * rank)
+    from pseudobrain_b200.sharding import default_transport
+    transport = {"p2p": "copy-engine pushes into the peers' mapped buffers (CUDA IPC)",
+                 "nccl": "NCCL all_gather_into_tensor"}[default_transport(world, True)] if world > 1 else "none"
     hv, heads = H["hv"] // world, H["heads"] // world
     scale = H["d"] ** -0.5
 
@@ -823,7 +827,8 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         "metric": "hybrid layer tok/s (config 4)", "value": t / t_step, "unit": "tok/s",
         "per_gpu": t / t_step / world, "scaling": "strong", "ms_per_step": t_step * 1e3,
         "config": {"seqlen": t, "gdn_heads_per_gpu": hv, "gdn_segments": segs, "swa_q_heads_per_gpu": heads,
-                   "window": H["window"], "size": args.size, "swa_query_chunks": 8},
+                   "window": H["window"], "size": args.size, "swa_query_chunks": 8,
+                   "transport": transport},
         "roofline": {"bound": "tensor", "achieved": per_gpu / t_step / 1e12, "peak": pk["tc"],
                      "unit": "TFLOP/s", "frac": per_gpu / t_step / 1e12 / pk["tc"],
                      "traffic": None, "peak_source": f"{pk['src']} bf16 burst (timed regions under a second)"},
@@ -834,8 +839,9 @@ def measure_hybrid(args, timed, dev, rank, world, pk):
         "gpu_launches": steps * (8 + 1 + 4 + 1),  # attention chunks, chunk solve, 4 recurrence runs, scan
     }
     if world > 1:
-        # the gathers timed alone: their share of the step, and what the overlap hid
-        out["all_gather"] = {"ms": t_ag * 1e3, "bytes_received_per_gpu": ag_bytes,
+        # NCCL's all-gather of the same bytes timed alone (the layer moves them overlapped, by
+        # the transport named in its config): its share of the step if it ran serially
+        out["all_gather"] = {"ms": t_ag * 1e3, "bytes_received_per_gpu": ag_bytes, "what": "NCCL, alone",
                              "gbps": ag_bytes / t_ag / 1e9 if t_ag > 0 else None,
                              "share_of_step_if_serial": t_ag / (t_ag + t_gdn + t_swa)}
         # strong scaling: the unsharded layer (all heads) on rank 0 while the others wait

@@ -623,6 +623,21 @@ typedef struct pbk_swa_desc {
 
 PBK_API int pbk_swa_prefill(const pbk_swa_desc* desc, void* stream);
 
+/* Copy-engine exchange between the GPUs of one node (the head-sharded hybrid layer's
+ * all-gather: pseudobrain/transplant.py WindowedHybridLayer's branch outputs gathered to the
+ * hidden layout). The copies run on the copy engines over NVLink and use no SMs, so they
+ * overlap kernels that occupy every SM; NCCL's all-gather kernels need SMs and wait for them.
+ * pbk_ipc_handle exports the allocation holding `ptr` (PBK_IPC_HANDLE_BYTES bytes into
+ * `handle`, ptr's byte offset in it into *offset); another process on the node maps it with
+ * pbk_ipc_open (peer access enabled on first use) and unmaps it with pbk_ipc_close;
+ * pbk_copy_async copies `bytes` between any two device addresses (mapped peer memory
+ * included), stream-ordered. */
+#define PBK_IPC_HANDLE_BYTES 64
+PBK_API int pbk_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+PBK_API int pbk_ipc_open(const void* handle, void** base);
+PBK_API int pbk_ipc_close(void* base);
+PBK_API int pbk_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,6 +16,7 @@ PBK_OK = 0
 PBK_ERR_INVALID, PBK_ERR_SHAPE, PBK_ERR_DTYPE, PBK_ERR_ALIGN = -1, -2, -3, -4
 PBK_ERR_DEVICE, PBK_ERR_LAUNCH, PBK_ERR_WORKSPACE = -5, -6, -8
 PBK_ERR_TIMEOUT = -7
+PBK_IPC_HANDLE_BYTES = 64
 PBK_ERR_TOO_LARGE = -9
 PBK_QUEST_NOALLOC_MAX_SCORES = 4194304
 PBK_F32, PBK_BF16 = 0, 1
@@ -195,6 +196,10 @@ SIGNATURES = {
     "pbk_quest_token_scores": (ctypes.c_int, [ctypes.POINTER(PbkTokenDesc), _VP]),
     "pbk_quest_token_rerank": (ctypes.c_int, [ctypes.POINTER(PbkTokenDesc), _VP]),
     "pbk_quest_row_ranks": (ctypes.c_int, [_VP, _I64, _I32, _I32, _VP, _I64, _VP]),
+    "pbk_ipc_handle": (ctypes.c_int, [_VP, _VP, ctypes.POINTER(ctypes.c_int64)]),
+    "pbk_ipc_open": (ctypes.c_int, [_VP, ctypes.POINTER(ctypes.c_void_p)]),
+    "pbk_ipc_close": (ctypes.c_int, [_VP]),
+    "pbk_copy_async": (ctypes.c_int, [_VP, _VP, ctypes.c_size_t, _VP]),
 }
 
 

@@ -136,8 +136,123 @@ def swa_chunk_plan(t: int, window: int, chunks: int, first: int | None = None) -
     return plan
 
 
+class PeerExchange:
+    """Rank-major gather buffers on every rank of `group`, filled by copy-engine pushes.
+
+    One bf16 buffer holds, for each piece i of shape (rows_i, width_i), a [N, rows_i, width_i]
+    region; rank r's data goes to slot r of every rank's region. The buffer is exported once
+    with CUDA IPC (pbk_ipc_handle) and mapped by every other rank (pbk_ipc_open); ``push``
+    copies a finished piece from this rank's own slot into the same slot of every peer's buffer
+    with one cudaMemcpyAsync per peer, on one stream per peer after an event on the producing
+    stream. The copies run on the copy engines over NVLink and use no SMs, so they overlap
+    kernels that fill every SM (NCCL's all-gather kernels wait for free SMs). ``start`` and
+    ``finish`` are the only collectives: a one-element all-reduce each, so that no rank writes
+    into a peer's buffer before the peer's earlier work is done, and no rank reads its buffer
+    before every peer's pushes into it have landed."""
+
+    def __init__(self, group, pieces: list[tuple[int, int]], device: torch.device):
+        from ._capi import LIB, PBK_IPC_HANDLE_BYTES, check
+        import ctypes
+        self.group, self.device = group, device
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.pieces = list(pieces)
+        self.offsets, total = [], 0
+        for rows, width in self.pieces:
+            self.offsets.append(total)
+            total += self.world * rows * width
+        self.buf = torch.empty(max(total, 1), dtype=torch.bfloat16, device=device)
+        handle = (ctypes.c_uint8 * PBK_IPC_HANDLE_BYTES)()
+        off = ctypes.c_int64()
+        with torch.cuda.device(device):
+            check(LIB.pbk_ipc_handle(self.buf.data_ptr(), handle, ctypes.byref(off)), "pbk_ipc_handle")
+        mine = (bytes(handle), off.value)
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=group)
+        self.bases, self.peer_ptr = {}, {}
+        for p in range(self.world):
+            if p == self.rank:
+                continue
+            base = ctypes.c_void_p()
+            h = (ctypes.c_uint8 * PBK_IPC_HANDLE_BYTES).from_buffer_copy(every[p][0])
+            with torch.cuda.device(device):
+                check(LIB.pbk_ipc_open(h, ctypes.byref(base)), "pbk_ipc_open")
+            self.bases[p] = base.value
+            self.peer_ptr[p] = base.value + every[p][1]
+        self.streams = {p: torch.cuda.Stream(device) for p in self.peer_ptr}
+        self.flag = torch.zeros(1, dtype=torch.float32, device=device)
+        self._lib = LIB
+
+    def view(self, i: int) -> torch.Tensor:
+        """Piece i's region of this rank's buffer, [N, rows, width]."""
+        rows, width = self.pieces[i]
+        o = self.offsets[i]
+        return self.buf[o:o + self.world * rows * width].view(self.world, rows, width)
+
+    def own(self, i: int) -> torch.Tensor:
+        """This rank's slot of piece i, [rows, width] (contiguous)."""
+        return self.view(i)[self.rank]
+
+    def start(self) -> None:
+        dist.all_reduce(self.flag, group=self.group)
+
+    def push(self, i: int) -> None:
+        """Copy this rank's slot of piece i (written on the current stream) to every peer."""
+        from ._capi import check
+        rows, width = self.pieces[i]
+        nbytes = rows * width * 2
+        elem = self.offsets[i] + self.rank * rows * width
+        src = self.buf.data_ptr() + elem * 2
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        for p, st in self.streams.items():
+            st.wait_event(ev)
+            check(self._lib.pbk_copy_async(self.peer_ptr[p] + elem * 2, src, nbytes, st.cuda_stream), "pbk_copy_async")
+
+    def finish(self) -> None:
+        cur = torch.cuda.current_stream(self.device)
+        for st in self.streams.values():
+            cur.wait_stream(st)
+        dist.all_reduce(self.flag, group=self.group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (after every push has completed)."""
+        torch.cuda.synchronize(self.device)
+        for base in self.bases.values():
+            self._lib.pbk_ipc_close(base)
+        self.bases.clear()
+        self.peer_ptr.clear()
+
+
+_EXCHANGES: dict = {}
+
+
+def peer_exchange(group, pieces, device) -> PeerExchange:
+    """The PeerExchange of these piece shapes on `group` (created on first use; every rank
+    must ask for the same shapes in the same order)."""
+    key = (id(group), tuple(pieces), str(device))
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = _EXCHANGES[key] = PeerExchange(group, pieces, device)
+    return ex
+
+
+# Above this many ranks the copy engines' egress (about 330 GB/s per B200 measured, pushing
+# to 7 peers) is slower than NCCL's SM-driven all-gather (about 660 GB/s), even though NCCL's
+# kernels wait for SMs the attention holds.
+P2P_MAX_RANKS = 4
+
+
+def default_transport(world: int, is_cuda: bool, group=None) -> str:
+    """"p2p" (copy-engine pushes) for 2..P2P_MAX_RANKS ranks of an NCCL group on CUDA
+    tensors, else "nccl"."""
+    if world > 1 and world <= P2P_MAX_RANKS and is_cuda and dist.get_backend(group) == "nccl":
+        return "p2p"
+    return "nccl"
+
+
 def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: float, group=None, swa_chunks: int = 8,
-                         gdn=None, attention=None, gather: bool = True, gdn_parts: int | None = None):
+                         gdn=None, attention=None, gather: bool = True, gdn_parts: int | None = None,
+                         transport: str | None = None):
     """One hybrid layer (GDN branch + sliding-window attention branch, pseudobrain/transplant.py
     WindowedHybridLayer, benchmark config 4) on this rank's heads, with every branch output
     all-gathered over `group` into the head-major layout the output projection reads.
@@ -154,7 +269,12 @@ def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: floa
     (v1 - v0)*128]) for each part: the rank-local value heads [v0, v1)], [(s, e, swa_all [N,
     e - s, H/N*128]) for each chunk]); assemble_gdn joins the parts into [N, T, hv/N*128].
     ``gdn(gdn_in, o)`` and ``attention(q, k, v, o, window, scale)`` replace the CUDA kernels (CPU
-    tests); gather=False runs the layer on these heads alone (N = 1 layouts, no exchange)."""
+    tests); gather=False runs the layer on these heads alone (N = 1 layouts, no exchange).
+    transport: "p2p" gathers with copy-engine pushes into every rank's mapped buffers
+    (PeerExchange): each piece goes out as soon as it is written, without SMs, so the pushes
+    overlap the attention kernel; "nccl" uses all_gather_into_tensor on the communicator's
+    stream. The default (default_transport) is "p2p" on NCCL groups of up to P2P_MAX_RANKS. The returned buffers of the p2p
+    transport are reused by the next call of the same shapes."""
     world = dist.get_world_size(group) if (gather and dist.is_initialized()) else 1
     if gdn is None:
         from .gdn_prefill import auto_segments, gdn_prefill_segmented
@@ -176,11 +296,27 @@ def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: floa
     if gdn_parts < 1 or hk % gdn_parts:
         raise ValueError(f"{hk} key heads do not split into {gdn_parts} parts")
     ratio = hv // hk
+    plan = swa_chunk_plan(t, window, swa_chunks)
+    if transport is None:
+        transport = default_transport(world, qa.is_cuda, group)
+    ex = None
+    if world > 1 and transport == "p2p":
+        pieces = [(t, ((p + 1) * hk // gdn_parts - p * hk // gdn_parts) * ratio * dv) for p in range(gdn_parts)]
+        pieces += [(e - s, heads * d) for s, e, _ in plan]
+        ex = peer_exchange(group, pieces, qa.device)
+        ex.start()
+    elif transport not in ("p2p", "nccl"):
+        raise ValueError(f"transport must be 'p2p' or 'nccl', not {transport!r}")
     for part in range(gdn_parts):
         k0, k1 = part * hk // gdn_parts, (part + 1) * hk // gdn_parts
         v0, v1 = k0 * ratio, k1 * ratio
         x = {"q": gdn_in["q"][:, :, k0:k1], "k": gdn_in["k"][:, :, k0:k1], "v": gdn_in["v"][:, :, v0:v1],
              "g": gdn_in["g"][:, :, v0:v1], "beta": gdn_in["beta"][:, :, v0:v1], "scale": gdn_in["scale"]}
+        if ex is not None:  # written straight into this rank's slot, then pushed to the peers
+            gdn(x, ex.own(part).view(1, t, v1 - v0, dv))
+            ex.push(part)
+            gdn_out.append((v0, v1, ex.view(part)))
+            continue
         o_part = torch.empty(1, t, v1 - v0, dv, dtype=torch.bfloat16, device=qa.device)
         gdn(x, o_part)
         if world > 1:
@@ -189,11 +325,16 @@ def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: floa
             gdn_out.append((v0, v1, gathered.view(world, t, -1)))
         else:
             gdn_out.append((v0, v1, o_part.view(1, t, -1)))
-    for s, e, h in swa_chunk_plan(t, window, swa_chunks):
+    for ci, (s, e, h) in enumerate(plan):
         rows = e - s + h
         stage = torch.empty(1, rows, heads, d, dtype=qa.dtype, device=qa.device)
         attention(qa[:, s - h:e], ka[:, s - h:e], va[:, s - h:e], stage, window, attn_scale)
         mine = stage.view(rows, heads * d)[h:]  # this chunk's exact rows (contiguous)
+        if ex is not None:
+            ex.own(gdn_parts + ci).copy_(mine)
+            ex.push(gdn_parts + ci)
+            swa_out.append((s, e, ex.view(gdn_parts + ci)))
+            continue
         if world > 1:
             gathered = torch.empty(world * (e - s), heads * d, dtype=qa.dtype, device=qa.device)
             works.append(dist.all_gather_into_tensor(gathered, mine, group=group, async_op=True))
@@ -202,6 +343,8 @@ def hybrid_layer_sharded(gdn_in: dict, qa, ka, va, window: int, attn_scale: floa
             swa_out.append((s, e, mine.view(1, e - s, heads * d)))
     for w in works:
         w.wait()
+    if ex is not None:
+        ex.finish()
     return gdn_out, swa_out
 
 

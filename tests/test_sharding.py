@@ -189,3 +189,13 @@ def test_hybrid_layer_pipeline_equals_unsharded(tmp_path):
     assert plan[0][0] == 0 and plan[-1][1] == HYB_T
     assert all(a[1] == b[0] for a, b in zip(plan, plan[1:]))
     assert all(h == min(s, 128) for s, _, h in plan)
+
+
+def test_default_transport_by_group_size():
+    """The hybrid layer's exchange: copy engines (p2p) only for NCCL groups of 2..4 CUDA ranks
+    (measured faster there; at 8 ranks NCCL's all-gather is); one rank or host tensors: nccl."""
+    from pseudobrain_b200 import sharding
+    assert sharding.default_transport(1, True) == "nccl"
+    assert sharding.default_transport(2, False) == "nccl"
+    assert sharding.default_transport(8, True) == "nccl"
+    assert sharding.P2P_MAX_RANKS == 4

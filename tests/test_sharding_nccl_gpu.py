@@ -4,7 +4,9 @@ head in halo'd query chunks, every output chunk is all-gathered as it is written
 assembled [T, heads * 128] outputs on every rank equal the unsharded layer (all heads on one
 GPU, the same kernels) to bf16 rounding (2e-2, the bar for bf16 inputs; the segment counts and
 the attention's tile alignment differ between the two, so the sums associate differently).
-Skipped on hosts with fewer than 2 GPUs. The ranks are child processes with a short process-
+Both transports run: NCCL's all-gather, and the copy-engine exchange (CUDA IPC mappings,
+cudaMemcpyAsync pushes) twice in a row, which must move the same bytes. Skipped on hosts with
+fewer than 2 GPUs. The ranks are child processes with a short process-
 group timeout, so a failure ends with an error instead of a wait."""
 from __future__ import annotations
 
@@ -58,9 +60,14 @@ def _worker(rank, world, port, outdir):
         per = ATT_KV // world
         groups = ATT_H // ATT_KV
         a0, a1 = rank * per, (rank + 1) * per
-        gdn_all, pieces = sharding.hybrid_layer_sharded(xs, qa[:, :, a0 * groups:a1 * groups], ka[:, :, a0:a1],
-                                                        va[:, :, a0:a1], WINDOW, 128 ** -0.5, swa_chunks=4)
-        out = {"gdn": sharding.assemble_gdn(gdn_all).cpu(), "swa": sharding.assemble_heads(pieces, T).cpu()}
+        out = {}
+        # NCCL's all-gather, then the copy-engine exchange twice (the second call reuses the
+        # mapped buffers of the first)
+        for name, transport in (("nccl", "nccl"), ("p2p", "p2p"), ("p2p_again", "p2p")):
+            gdn_all, pieces = sharding.hybrid_layer_sharded(xs, qa[:, :, a0 * groups:a1 * groups], ka[:, :, a0:a1],
+                                                            va[:, :, a0:a1], WINDOW, 128 ** -0.5, swa_chunks=4,
+                                                            transport=transport)
+            out[name] = (sharding.assemble_gdn(gdn_all).cpu(), sharding.assemble_heads(pieces, T).cpu())
         if rank == 0:  # the unsharded layer: all heads on this GPU, no exchange
             g1, p1 = sharding.hybrid_layer_sharded(x, qa, ka, va, WINDOW, 128 ** -0.5, swa_chunks=1, gather=False)
             out["gdn_ref"] = sharding.assemble_gdn(g1).cpu()
@@ -91,6 +98,9 @@ def test_hybrid_layer_two_gpus_equals_unsharded(tmp_path):
     for rank in range(world):
         got = torch.load(os.path.join(tmp_path, f"nccl_{rank}.pt"))
         assert got["device_error"] == 0
-        eg, es = _rel(got["gdn"], want_gdn), _rel(got["swa"], want_swa)
+        gdn, swa = got["nccl"]
+        eg, es = _rel(gdn, want_gdn), _rel(swa, want_swa)
         print(f"[2-GPU hybrid layer, rank {rank}] rel err GDN {eg:.2e}, attention {es:.2e}")
         assert eg < 2e-2 and es < 2e-2
+        for name in ("p2p", "p2p_again"):  # the same kernels' outputs, moved by the copy engines
+            assert torch.equal(got[name][0], gdn) and torch.equal(got[name][1], swa), name
