@@ -148,7 +148,9 @@ class PeerExchange:
     kernels that fill every SM (NCCL's all-gather kernels wait for free SMs). ``start`` and
     ``finish`` are the only collectives: a one-element all-reduce each, so that no rank writes
     into a peer's buffer before the peer's earlier work is done, and no rank reads its buffer
-    before every peer's pushes into it have landed."""
+    before every peer's pushes into it have landed. The buffer must come from cudaMalloc (the
+    caching allocator's default segments): CUDA IPC cannot export expandable segments, and
+    pbk_ipc_handle then fails with an error."""
 
     def __init__(self, group, pieces: list[tuple[int, int]], device: torch.device):
         from ._capi import LIB, PBK_IPC_HANDLE_BYTES, check
