@@ -313,7 +313,8 @@ struct SolveTX {       // one value head's inverse blocks
   float x[4][256];     // X_20, X_21, X_30, X_31 (level 1 scratch in x[0], x[1])
 };
 struct SolveHead {     // one value head's A and scalars
-  float at[4][16][16]; // diagonal blocks of A, transposed: at[b][m][r] = A[16b + r][16b + m]
+  float at[4][16][20]; // diagonal blocks of A, transposed: at[b][m][r] = A[16b + r][16b + m]; rows
+                       // padded to 20 so the epilogue's column-group stores hit distinct banks
   float ao[6][256];    // off-diagonal blocks of A
   float c2[C], gam[C], beta[C];
 };
